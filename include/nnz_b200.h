@@ -1,0 +1,211 @@
+/*
+ * nnz_b200.h -- C ABI of the B200-native quantized Qwen3 (Bonsai) hot path.
+ *
+ * This library replaces the Metal backend + dispatch layer of the nnzap
+ * `nnmetal` engine for the decode / prefill hot path.  Every entry point is
+ * plain C: integers, sizes and pointers, no C++ or torch types, no
+ * exceptions.  All functions return 0 (NNZ_OK) or a negative NNZ_E* code;
+ * nnz_last_error() returns a thread-local message for the last failure.
+ *
+ * Citations name files of the nnzap reference tree (path:line).
+ */
+#ifndef NNZ_B200_H_
+#define NNZ_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------- */
+enum {
+  NNZ_OK = 0,
+  NNZ_EINVAL = -1,     /* bad argument / shape (reference: std.debug.assert) */
+  NNZ_ECUDA = -2,      /* CUDA runtime error (MetalNotAvailable & co.)        */
+  NNZ_ENOMEM = -3,     /* device allocation failed (MetalBufferAllocFailed)   */
+  NNZ_ETIMEDOUT = -4,  /* a bounded device or host wait gave up               */
+  NNZ_ENOTFOUND = -5,  /* tensor missing at finalize (TensorNotFound)          */
+  NNZ_ESTATE = -6,     /* call order violated (e.g. decode before finalize)   */
+  NNZ_EDEVICE = -7,    /* a kernel raised a device error flag                 */
+  NNZ_ENCCL = -8       /* NCCL failure (tensor-parallel path)                 */
+};
+
+/* ---- enums ------------------------------------------------------------ */
+/* Quantization format: transformer.zig:35-53 QuantFormat {q1_0, q4_mlx}. */
+enum { NNZ_Q1 = 0, NNZ_Q4 = 1 };
+/* RoPE pairing: engine consecutive pairs (transformer.metal:1535-1549) or
+ * MLX/HF half split (reference/mlx_q4_layer0.py:114-136). */
+enum { NNZ_ROPE_PAIRWISE = 0, NNZ_ROPE_HALF_SPLIT = 1 };
+/* 16-bit scale/bias encoding (Q4): fp16, or raw BF16 (model.zig:1177-1220). */
+enum { NNZ_SCALE_F16 = 0, NNZ_SCALE_BF16 = 1 };
+/* Tensor dtypes accepted by nnz_model_load_tensor (safetensors.zig:46). */
+enum { NNZ_DT_U8 = 0, NNZ_DT_U32 = 1, NNZ_DT_F16 = 2, NNZ_DT_BF16 = 3, NNZ_DT_F32 = 4 };
+/* Output kinds of nnz_qmv. */
+enum { NNZ_OUT_F16 = 0, NNZ_OUT_F32 = 1, NNZ_OUT_F32_ADD = 2 };
+
+/* Model description.  Mirrors TransformerDesc / TransformerConfig
+ * (transformer.zig:62-81, :91-276); runtime instead of comptime. */
+typedef struct nnz_config {
+  uint32_t vocab_size;
+  uint32_t hidden_size;
+  uint32_t intermediate_size;
+  uint32_t num_layers;
+  uint32_t num_query_heads;
+  uint32_t num_kv_heads;
+  uint32_t head_dim;              /* 64 or 128 */
+  uint32_t max_context_length;
+  uint32_t max_prefill_length;
+  uint32_t max_batch;             /* decode rows (1 for the reference engine) */
+  float rope_theta;
+  float eps;                      /* RMSNorm epsilon, 1e-6 in the reference */
+  int32_t quant_format;           /* NNZ_Q1 | NNZ_Q4 */
+  int32_t group_size;             /* 128 (Q1) / 64 (Q4); multiple of 32 */
+  int32_t scale_dtype;            /* Q4: NNZ_SCALE_F16 (spec) | NNZ_SCALE_BF16 (engine) */
+  int32_t bf16_faithful;          /* Q4: truncate outputs to BF16 like the engine */
+  int32_t rope_style;             /* NNZ_ROPE_* */
+  int32_t tie_word_embeddings;
+  int32_t q1_scales_are_mlx;      /* Q1: halve scales at load (model.zig:944-959) */
+  int32_t tp_rank;                /* tensor-parallel rank / size (1 = off) */
+  int32_t tp_size;
+} nnz_config;
+
+typedef struct nnz_model nnz_model;
+
+/* GenerateOpts / GenerateResult (transformer.zig:3663-3690).  Greedy only. */
+typedef struct nnz_generate_opts {
+  const uint32_t* prompt_ids;
+  uint32_t n_prompt;
+  const uint32_t* eos_ids;
+  uint32_t n_eos;
+  uint32_t* output_tokens;       /* capacity max_new */
+  uint32_t max_new;
+  uint64_t* per_token_ns;        /* optional [max_new]: GPU time per decode step */
+} nnz_generate_opts;
+
+typedef struct nnz_generate_result {
+  uint32_t tokens_generated;
+  uint64_t prefill_ns;
+  uint64_t decode_ns;
+} nnz_generate_result;
+
+/* ---- library -------------------------------------------------------- */
+const char* nnz_last_error(void);
+int nnz_version(void);
+/* Device count visible to the CUDA runtime (0 without a GPU). */
+int nnz_device_count(void);
+
+/* ---- model: replaces Model(Config) of model.zig + Device.init -------- */
+/* Device.init + Model.init (metal.zig:959, model.zig:123): allocates
+ * nothing yet; buffers are sized at nnz_model_finalize. */
+int nnz_model_create(int device, const nnz_config* cfg, nnz_model** out);
+/* loadWeights (model.zig:196-242, :571-1026): one tensor by its checkpoint
+ * name ("model.layers.{i}.self_attn.q_proj.weight", ".scales", ".biases",
+ * "model.embed_tokens.*", "model.norm.weight", "lm_head.*", norm weights).
+ * The bytes are copied; conversions follow the reference loader. */
+int nnz_model_load_tensor(nnz_model* m, const char* name, int dtype, const void* data,
+                          size_t bytes);
+/* Packs the loaded tensors into the device layout, allocates the KV cache
+ * and activation buffers, and releases the host copies. */
+int nnz_model_finalize(nnz_model* m);
+int nnz_model_free(nnz_model* m);
+/* Bytes of device memory held by the model (weights + KV + scratch). */
+size_t nnz_model_device_bytes(const nnz_model* m);
+
+/* forwardDecode (transformer.zig:2566) + host argmax (:3694): one token per
+ * row at the given positions, `batch` rows (row r uses KV-cache slot r).
+ * logits (optional, host, [batch][vocab] f32) and argmax_out ([batch]). */
+int nnz_forward_decode(nnz_model* m, const uint32_t* tokens, const uint32_t* positions,
+                       uint32_t batch, float* logits, uint32_t* argmax_out);
+/* Prompt prefill into slot 0 at positions 0..n-1 (replaces chunkedPrefill,
+ * transformer.zig:4032-4068); returns the greedy next token and optionally
+ * the last position's logits. */
+int nnz_prefill(nnz_model* m, const uint32_t* tokens, uint32_t n, uint32_t* next_token,
+                float* last_logits);
+/* generate (transformer.zig:3942-4027), greedy: prefill then one CUDA-graph
+ * replay per token; stops at the first EOS id like the reference. */
+int nnz_generate(nnz_model* m, const nnz_generate_opts* opts, nnz_generate_result* res);
+/* Batched greedy decode of `batch` sequences for `steps` tokens, starting
+ * from tokens[] at positions[] (each row's slot must hold its KV history).
+ * out_tokens [steps][batch]; per_step_ns optional [steps]. */
+int nnz_decode_steps(nnz_model* m, const uint32_t* tokens, const uint32_t* positions,
+                     uint32_t batch, uint32_t steps, uint32_t* out_tokens,
+                     uint64_t* per_step_ns);
+/* Fill KV-cache slot `slot` of layer `layer`, positions [0, len), from host
+ * fp16 arrays laid out [kv_head][len][head_dim]. */
+int nnz_model_write_kv(nnz_model* m, uint32_t layer, uint32_t slot, const uint16_t* k,
+                       const uint16_t* v, uint32_t len);
+/* Read back the same region (tests). */
+int nnz_model_read_kv(nnz_model* m, uint32_t layer, uint32_t slot, uint16_t* k, uint16_t* v,
+                      uint32_t len);
+/* One decoder layer decode step on the model's state:
+ * residual (host f32 [batch][hidden]) is updated in place, `positions` give
+ * each row's position; row r uses KV slot r. */
+int nnz_model_layer_step(nnz_model* m, uint32_t layer, float* residual,
+                         const uint32_t* positions, uint32_t batch);
+/* Average device time of `iters` back-to-back replays of the b=1 decode
+ * graph (no host work between), in microseconds; for benchmarks. */
+int nnz_bench_decode_graph(nnz_model* m, uint32_t batch, uint32_t iters, double* us_per_step);
+
+/* ---- weight packing (host, no GPU needed) --------------------------- */
+/* Bytes of the tile-packed form of an M x K matrix (sub interleaved). */
+size_t nnz_packed_bytes(int fmt, uint32_t M, uint32_t K, uint32_t gs, uint32_t sub);
+/* Reference flat layout -> tile layout (metal.zig:235-469 formats).
+ * weight: Q1 bits (M*K/8 B) or Q4 words (M*K/2 B); scales/biases u16. */
+int nnz_pack_weights(int fmt, const void* weight, const uint16_t* scales, const uint16_t* biases,
+                     uint32_t M, uint32_t K, uint32_t gs, uint32_t sub, uint32_t sub_index,
+                     void* packed_out);
+/* Exact inverse of nnz_pack_weights. */
+int nnz_unpack_weights(int fmt, const void* packed, uint32_t M, uint32_t K, uint32_t gs,
+                       uint32_t sub, uint32_t sub_index, void* weight, uint16_t* scales,
+                       uint16_t* biases);
+
+/* ---- per-kernel entry points on device pointers --------------------- */
+/* All asynchronous on `stream` (a cudaStream_t, NULL = default stream).
+ * They share a per-device workspace allocated on first use. */
+
+/* Dequantize a packed matrix to f32 [M][K] (bit-exact weight check).
+ * Reference dequant: transformer_test.zig:286-321 (Q1), model.zig:969-1026 (Q4). */
+int nnz_dequant(int fmt, int scale_dtype, const void* packed, uint32_t M, uint32_t K, uint32_t gs,
+                uint32_t sub, uint32_t sub_index, float* out, void* stream);
+/* y[b][row] = sum_k x[b][k] W[row][k] for b < batch.  x fp16 [batch][x_stride].
+ * out_kind NNZ_OUT_F16 (fp16 y), NNZ_OUT_F32, NNZ_OUT_F32_ADD (y += into f32).
+ * Replaces qmv_spec_f16io / _f16in / _f16io_resadd
+ * (qmv_specialized.metal:55,217,597; q4mv_bf16_specialized.metal:93,185,394). */
+int nnz_qmv(int fmt, int scale_dtype, int bf16_round, const void* packed, uint32_t M, uint32_t K,
+            uint32_t gs, const void* x, uint32_t x_stride, uint32_t batch, void* out,
+            uint32_t out_stride, int out_kind, void* stream);
+/* Same with the fused RMSNorm prologue over an f32 residual [batch][K]
+ * (qmv_spec_fused_norm_f16io, qmv_specialized.metal:1290). */
+int nnz_qmv_norm(int fmt, int scale_dtype, int bf16_round, const void* packed, uint32_t M,
+                 uint32_t K, uint32_t gs, const float* residual, const float* norm_w, float eps,
+                 uint32_t batch, void* out, uint32_t out_stride, int out_kind, void* stream);
+/* LM head + greedy argmax: optional f32 logits [batch][M], argmax_out
+ * device u32 [batch] (qmv_spec_f16in + transformer.zig:3694-3707). */
+int nnz_lm_head_argmax(int fmt, int scale_dtype, int bf16_round, const void* packed, uint32_t M,
+                       uint32_t K, uint32_t gs, const float* residual, const float* norm_w,
+                       float eps, uint32_t batch, float* logits, uint32_t* argmax_out,
+                       void* stream);
+/* Fused MLP block: out_f32[b] = down(SiLU(gate x) * up x).
+ * gate_up is packed with sub = 2 (gate = sub 0, up = sub 1); x fp16
+ * [batch][K]; h_scratch fp16 [batch][M_inter] may be NULL (workspace).
+ * Replaces qmv_spec_fused_pair_silu_f16io + qmv_spec_mg_f16io_resadd
+ * (qmv_specialized.metal:955,760). */
+int nnz_mlp(int fmt, int scale_dtype, int bf16_round, const void* gate_up, const void* down,
+            uint32_t hidden, uint32_t inter, uint32_t gs, const void* x, uint32_t batch,
+            float* out, void* stream);
+/* GQA decode attention with fused QK-norm + RoPE + KV write
+ * (gqa_attention_fused_f16io_tg, transformer.metal:1467-1695).
+ * qkv fp16 [rows][(n_q + 2 n_kv) hd]; caches fp16 [slots][n_kv][max_ctx][hd];
+ * positions device int32 [rows]; row r uses slot r; out fp16 [rows][n_q hd];
+ * splits = CTAs per (kv head, row), 0 = automatic. */
+int nnz_attn_decode(const void* qkv, const float* q_norm, const float* k_norm, void* k_cache,
+                    void* v_cache, uint32_t max_ctx, const int32_t* positions, uint32_t rows,
+                    uint32_t n_q, uint32_t n_kv, uint32_t head_dim, float eps, float theta,
+                    int rope_style, uint32_t splits, void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NNZ_B200_H_ */

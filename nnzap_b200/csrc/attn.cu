@@ -1,0 +1,361 @@
+// Decode attention kernels (see attn.cuh).
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include "attn.cuh"
+
+namespace nnz {
+
+namespace {
+
+struct AttnSmem {
+  uint32_t bars, kring, vring, q, knew, vnew, s, stat, flag, total;
+};
+
+template <int HD>
+__host__ __device__ inline AttnSmem attn_layout() {
+  AttnSmem L;
+  uint32_t o = 0;
+  L.bars = o; o += kAttnStages * 8;
+  o = (o + 127) & ~127u;
+  L.kring = o; o += kAttnStages * kAttnBlk * HD * 2;
+  L.vring = o; o += kAttnStages * kAttnBlk * HD * 2;
+  L.q = o; o += kAttnMaxG * HD * 4;
+  L.knew = o; o += HD * 4;
+  L.vnew = o; o += HD * 4;
+  L.s = o; o += kAttnMaxG * kAttnBlk * 4;
+  L.stat = o; o += 3 * kAttnMaxG * 4;  // m, l, alpha
+  L.flag = o; o += 16;
+  L.total = o;
+  return L;
+}
+
+// One warp: RMSNorm over the head (f32), scale, RoPE.  Leaves the EPL
+// values this lane owns in v[] (pairwise: contiguous elements; half-split:
+// element i pairs with i + HD/2, which lane + 16 owns).
+template <int HD>
+__device__ __forceinline__ void norm_rope_head(const __half* src, const float* nw, float eps,
+                                               float theta, int style, int pos, int lane,
+                                               float (&v)[HD / 32]) {
+  constexpr int EPL = HD / 32;
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    v[e] = __half2float(src[lane * EPL + e]);
+    ss = fmaf(v[e], v[e], ss);
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)HD + eps);
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) v[e] = v[e] * r * nw[lane * EPL + e];
+  const double l2t = log2((double)theta);
+  if (style == ROPE_PAIRWISE) {
+#pragma unroll
+    for (int e = 0; e < EPL; e += 2) {
+      const int i = (lane * EPL + e) >> 1;
+      const double ang = (double)pos * exp2(-(2.0 * i / HD) * l2t);
+      double sd, cd;
+      sincos(ang, &sd, &cd);
+      const float c = (float)cd, s = (float)sd;
+      const float x0 = v[e], x1 = v[e + 1];
+      v[e] = x0 * c - x1 * s;
+      v[e + 1] = x0 * s + x1 * c;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
+      const int i = (lane & 15) * EPL + e;
+      const double ang = (double)pos * exp2(-(2.0 * i / HD) * l2t);
+      double sd, cd;
+      sincos(ang, &sd, &cd);
+      const float c = (float)cd, s = (float)sd;
+      if (lane < 16) v[e] = v[e] * c - partner * s;   // first half: a*c - b*s
+      else v[e] = partner * s + v[e] * c;             // second half: a*s + b*c
+    }
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs a) {
+  constexpr int EPL = HD / 32;
+  extern __shared__ __align__(128) uint8_t sm[];
+  const AttnSmem L = attn_layout<HD>();
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L.bars);
+  __half* kring = reinterpret_cast<__half*>(sm + L.kring);
+  __half* vring = reinterpret_cast<__half*>(sm + L.vring);
+  float* qs = reinterpret_cast<float*>(sm + L.q);
+  float* knew = reinterpret_cast<float*>(sm + L.knew);
+  float* vnew = reinterpret_cast<float*>(sm + L.vnew);
+  float* ss = reinterpret_cast<float*>(sm + L.s);
+  float* mst = reinterpret_cast<float*>(sm + L.stat);
+  float* lst = mst + kAttnMaxG;
+  float* alp = lst + kAttnMaxG;
+  int* flag = reinterpret_cast<int*>(sm + L.flag);
+
+  const int kvh = blockIdx.x, row = blockIdx.y, split = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = (int)(a.n_q / a.n_kv);
+  // Positions and past K/V were written >= 2 launches earlier: safe pre-wait.
+  int p = a.pos[row];
+  if (p < 0 || p >= (int)a.max_ctx) {
+    if (threadIdx.x == 0) atomicOr(a.err, ERR_BAD_POS);
+    p = p < 0 ? 0 : (int)a.max_ctx - 1;
+  }
+  const int slot = a.slot ? a.slot[row] : row;
+  const int seq = p + 1;
+  const int per = (seq + (int)a.splits - 1) / (int)a.splits;
+  const int t0 = split * per;
+  const int t1 = min(seq, t0 + per);
+  const bool own_new = a.write_kv && t0 <= p && p < t1;
+  const int cend = a.write_kv ? min(t1, p) : t1;
+  const int ncache = cend > t0 ? cend - t0 : 0;
+  const int nblk = (ncache + kAttnBlk - 1) / kAttnBlk;
+  const size_t head_off = ((size_t)slot * a.n_kv + kvh) * a.max_ctx * HD;
+  const __half* kb = a.kc + head_off;
+  const __half* vb = a.vc + head_off;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kAttnStages; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+    for (int b = 0; b < nblk && b < kAttnStages; ++b) {
+      const int n = min(kAttnBlk, ncache - b * kAttnBlk);
+      const uint32_t bytes = (uint32_t)n * HD * 2;
+      mbar_arrive_expect_tx(&bars[b], 2 * bytes);
+      bulk_g2s(kring + (size_t)b * kAttnBlk * HD, kb + (size_t)(t0 + b * kAttnBlk) * HD, bytes, &bars[b]);
+      bulk_g2s(vring + (size_t)b * kAttnBlk * HD, vb + (size_t)(t0 + b * kAttnBlk) * HD, bytes, &bars[b]);
+    }
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_launch();
+
+  // q heads (and the new k/v) -----------------------------------------
+  const __half* qrow = a.qkv + (size_t)row * a.qkv_stride;
+  for (int h = warp; h < G; h += kAttnThreads / 32) {
+    float v[EPL];
+    norm_rope_head<HD>(qrow + (size_t)(kvh * G + h) * HD, a.q_norm, a.eps, a.theta, a.rope_style,
+                       p, lane, v);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) qs[h * HD + lane * EPL + e] = v[e];
+  }
+  if (own_new && warp == (kAttnThreads / 32) - 1) {
+    float v[EPL];
+    norm_rope_head<HD>(qrow + (size_t)a.n_q * HD + (size_t)kvh * HD, a.k_norm, a.eps, a.theta,
+                       a.rope_style, p, lane, v);
+    const __half* vsrc = qrow + (size_t)(a.n_q + a.n_kv) * HD + (size_t)kvh * HD;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const int d = lane * EPL + e;
+      const __half kh = __float2half_rn(v[e]);
+      a.kc[head_off + (size_t)p * HD + d] = kh;
+      a.vc[head_off + (size_t)p * HD + d] = vsrc[d];
+      knew[d] = __half2float(kh);
+      vnew[d] = __half2float(vsrc[d]);
+    }
+  }
+  if (threadIdx.x < kAttnMaxG) {
+    mst[threadIdx.x] = -INFINITY;
+    lst[threadIdx.x] = 0.f;
+  }
+  __syncthreads();
+
+  constexpr int NHS = kAttnThreads / HD;   // thread groups over heads in PV
+  const int d = threadIdx.x % HD, hs = threadIdx.x / HD;
+  float acc[kAttnMaxG];
+#pragma unroll
+  for (int h = 0; h < kAttnMaxG; ++h) acc[h] = 0.f;
+  const float inv = rsqrtf((float)HD);
+  bool failed = false;
+
+  const int total_blocks = nblk + (own_new ? 1 : 0);
+  for (int b = 0; b < total_blocks; ++b) {
+    const bool is_new = b == nblk;
+    const int n = is_new ? 1 : min(kAttnBlk, ncache - b * kAttnBlk);
+    const int stg = b % kAttnStages;
+    const __half* kr = kring + (size_t)stg * kAttnBlk * HD;
+    const __half* vr = vring + (size_t)stg * kAttnBlk * HD;
+    if (!is_new && !failed) failed = !mbar_wait(&bars[stg], (b / kAttnStages) & 1, a.err);
+    // scores
+    for (int t = warp; t < n; t += kAttnThreads / 32) {
+      float kv[EPL];
+      if (is_new) {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) kv[e] = knew[lane * EPL + e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; e += 2) {
+          const __half2 k2 = *reinterpret_cast<const __half2*>(kr + (size_t)t * HD + lane * EPL + e);
+          const float2 f = __half22float2(k2);
+          kv[e] = f.x; kv[e + 1] = f.y;
+        }
+      }
+      for (int h = 0; h < G; ++h) {
+        float dot = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) dot = fmaf(qs[h * HD + lane * EPL + e], kv[e], dot);
+        dot = warp_sum(dot);
+        if (lane == 0) ss[h * kAttnBlk + t] = dot * inv;
+      }
+    }
+    __syncthreads();
+    // online softmax statistics, one warp per head
+    for (int h = warp; h < G; h += kAttnThreads / 32) {
+      const float sv = lane < n ? ss[h * kAttnBlk + lane] : -INFINITY;
+      const float mx = warp_max(sv);
+      const float mo = mst[h];
+      const float mn = fmaxf(mo, mx);
+      const float pe = lane < n ? expf(sv - mn) : 0.f;
+      if (lane < n) ss[h * kAttnBlk + lane] = pe;
+      const float ls = warp_sum(pe);
+      if (lane == 0) {
+        const float al = (mo == -INFINITY) ? 0.f : expf(mo - mn);
+        alp[h] = al;
+        lst[h] = lst[h] * al + ls;
+        mst[h] = mn;
+      }
+    }
+    __syncthreads();
+    // P.V
+    for (int h = hs; h < G; h += NHS) {
+      float o = acc[h] * alp[h];
+      if (is_new) {
+        o = fmaf(ss[h * kAttnBlk], vnew[d], o);
+      } else {
+        for (int t = 0; t < n; ++t) o = fmaf(ss[h * kAttnBlk + t], __half2float(vr[(size_t)t * HD + d]), o);
+      }
+      acc[h] = o;
+    }
+    __syncthreads();
+    if (!is_new && threadIdx.x == 0 && b + kAttnStages < nblk) {
+      const int nb = b + kAttnStages;
+      const int nn = min(kAttnBlk, ncache - nb * kAttnBlk);
+      const uint32_t bytes = (uint32_t)nn * HD * 2;
+      mbar_arrive_expect_tx(&bars[stg], 2 * bytes);
+      bulk_g2s(kring + (size_t)stg * kAttnBlk * HD, kb + (size_t)(t0 + nb * kAttnBlk) * HD, bytes, &bars[stg]);
+      bulk_g2s(vring + (size_t)stg * kAttnBlk * HD, vb + (size_t)(t0 + nb * kAttnBlk) * HD, bytes, &bars[stg]);
+    }
+  }
+
+  __half* orow = a.out + (size_t)row * a.out_stride + (size_t)kvh * G * HD;
+  if (a.splits == 1) {
+    for (int h = hs; h < G; h += NHS) orow[h * HD + d] = __float2half_rn(acc[h] / lst[h]);
+    return;
+  }
+  const uint32_t rec = HD + 2;
+  float* wsp = a.ws + ((size_t)(row * a.n_kv + kvh) * a.splits) * G * rec;
+  for (int h = hs; h < G; h += NHS) wsp[((size_t)split * G + h) * rec + 2 + d] = acc[h];
+  if (threadIdx.x < (unsigned)G) {
+    wsp[((size_t)split * G + threadIdx.x) * rec + 0] = mst[threadIdx.x];
+    wsp[((size_t)split * G + threadIdx.x) * rec + 1] = lst[threadIdx.x];
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t prev = atomicAdd(&a.counters[row * a.n_kv + kvh], 1u);
+    flag[0] = prev == a.splits - 1;
+  }
+  __syncthreads();
+  if (!flag[0]) return;
+  __threadfence();
+  for (int h = hs; h < G; h += NHS) {
+    float M = -INFINITY;
+    for (uint32_t s = 0; s < a.splits; ++s) M = fmaxf(M, __ldcg(&wsp[((size_t)s * G + h) * rec]));
+    float Lsum = 0.f, o = 0.f;
+    for (uint32_t s = 0; s < a.splits; ++s) {
+      const float ms = __ldcg(&wsp[((size_t)s * G + h) * rec]);
+      if (ms == -INFINITY) continue;
+      const float w = expf(ms - M);
+      Lsum = fmaf(__ldcg(&wsp[((size_t)s * G + h) * rec + 1]), w, Lsum);
+      o = fmaf(__ldcg(&wsp[((size_t)s * G + h) * rec + 2 + d]), w, o);
+    }
+    orow[h * HD + d] = __float2half_rn(o / Lsum);
+  }
+  if (threadIdx.x == 0) a.counters[row * a.n_kv + kvh] = 0;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(64) rope_kv_write_kernel(AttnArgs a) {
+  constexpr int EPL = HD / 32;
+  pdl_wait();
+  pdl_launch();
+  const int kvh = blockIdx.x, row = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int p = a.pos[row];
+  if (p < 0 || p >= (int)a.max_ctx) {
+    if (threadIdx.x == 0) atomicOr(a.err, ERR_BAD_POS);
+    return;
+  }
+  const int slot = a.slot ? a.slot[row] : row;
+  const size_t off = (((size_t)slot * a.n_kv + kvh) * a.max_ctx + p) * HD;
+  const __half* qrow = a.qkv + (size_t)row * a.qkv_stride;
+  if (warp == 0) {
+    float v[EPL];
+    norm_rope_head<HD>(qrow + (size_t)a.n_q * HD + (size_t)kvh * HD, a.k_norm, a.eps, a.theta,
+                       a.rope_style, p, lane, v);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) a.kc[off + lane * EPL + e] = __float2half_rn(v[e]);
+  } else {
+    const __half* vsrc = qrow + (size_t)(a.n_q + a.n_kv) * HD + (size_t)kvh * HD;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) a.vc[off + lane * EPL + e] = vsrc[lane * EPL + e];
+  }
+}
+
+cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, uint32_t smem, int pdl, cudaStream_t st,
+                            cudaLaunchAttribute* at) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+template <int HD>
+cudaError_t attn_launch_t(const AttnArgs& a, int pdl, cudaStream_t st) {
+  const AttnSmem L = attn_layout<HD>();
+  cudaLaunchAttribute at[1];
+  cudaLaunchConfig_t cfg = make_cfg(dim3(a.n_kv, a.rows, a.splits), dim3(kAttnThreads), L.total, pdl, st, at);
+  return cudaLaunchKernelEx(&cfg, &attn_decode_kernel<HD>, a);
+}
+
+}  // namespace
+
+cudaError_t attn_prepare() {
+  cudaError_t e = cudaFuncSetAttribute(&attn_decode_kernel<128>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       attn_layout<128>().total);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(&attn_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              attn_layout<64>().total);
+}
+
+size_t attn_ws_floats(uint32_t rows, uint32_t n_q, uint32_t n_kv, uint32_t splits, int head_dim) {
+  if (splits <= 1) return 0;
+  return (size_t)rows * n_kv * splits * (n_q / n_kv) * (head_dim + 2);
+}
+
+cudaError_t attn_decode_launch(const AttnArgs& a, int head_dim, int pdl, cudaStream_t st) {
+  if (a.n_kv == 0 || a.n_q % a.n_kv || a.n_q / a.n_kv > (uint32_t)kAttnMaxG || a.splits == 0 ||
+      a.rows == 0)
+    return cudaErrorInvalidValue;
+  if (head_dim == 128) return attn_launch_t<128>(a, pdl, st);
+  if (head_dim == 64) return attn_launch_t<64>(a, pdl, st);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t rope_kv_write_launch(const AttnArgs& a, int head_dim, int pdl, cudaStream_t st) {
+  if (a.rows == 0 || a.n_kv == 0) return cudaErrorInvalidValue;
+  cudaLaunchAttribute at[1];
+  cudaLaunchConfig_t cfg = make_cfg(dim3(a.n_kv, a.rows), dim3(64), 0, pdl, st, at);
+  if (head_dim == 128) return cudaLaunchKernelEx(&cfg, &rope_kv_write_kernel<128>, a);
+  if (head_dim == 64) return cudaLaunchKernelEx(&cfg, &rope_kv_write_kernel<64>, a);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace nnz

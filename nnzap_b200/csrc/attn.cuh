@@ -1,0 +1,66 @@
+// GQA decode attention over the fp16 KV cache with fused per-head
+// QK-RMSNorm, RoPE and KV-cache write.
+//
+// Replaces nnmetal/src/shaders/transformer.metal:1467-1695
+// (gqa_attention_fused_f16io_tg) and its long-context fallback
+// (:840, :940, :1176): q = RoPE(RMSNorm_hd(q) * qn) kept in f32,
+// k = RoPE(RMSNorm_hd(k) * kn) stored fp16 at `pos`, v stored fp16,
+// scores = q.k / sqrt(hd) in f32, softmax f32, out = sum p v -> fp16.
+//
+// B200 design: flash-decoding.  One CTA per (kv head, query row, split);
+// the CTA serves all G = n_q / n_kv query heads of its kv head, so each K/V
+// byte is read once.  K/V blocks of 32 positions stream into a 4-stage
+// shared-memory ring with 1-D bulk copies issued before griddepcontrol.wait
+// (past positions are constant), an online softmax runs per block, and the
+// splits of one (kv head, row) are merged by the last CTA to arrive.  Any
+// context length up to max_context_length is handled (the reference's fused
+// kernel stops at 1024).  RoPE angles are computed in double precision.
+//
+// Cache layout: [slot][kv_head][max_ctx][hd] for both K and V (the
+// reference's V is transposed [d][t]; the values stored are identical).
+#pragma once
+#include "common.cuh"
+
+namespace nnz {
+
+constexpr int kAttnThreads = 128;
+constexpr int kAttnBlk = 32;     // positions per streamed block
+constexpr int kAttnStages = 4;
+constexpr int kAttnMaxG = 8;     // query heads per kv head
+
+enum RopeStyle : int { ROPE_PAIRWISE = 0, ROPE_HALF_SPLIT = 1 };
+
+struct AttnArgs {
+  const __half* qkv;   // [rows][qkv_stride]: q | k | v
+  uint32_t qkv_stride;
+  const float* q_norm;
+  const float* k_norm;
+  __half* kc;          // layer base of the K cache
+  __half* vc;          // layer base of the V cache
+  uint32_t max_ctx;
+  const int* pos;      // [rows] position of each query row
+  const int* slot;     // [rows] cache slot of each row (nullptr: slot = row)
+  uint32_t rows;
+  uint32_t n_q, n_kv;
+  float eps, theta;
+  int rope_style;
+  int write_kv;        // 1: this launch writes row's k/v at pos and attends to it
+  uint32_t splits;     // CTAs per (kv head, row)
+  __half* out;         // [rows][n_q*hd]
+  uint32_t out_stride;
+  float* ws;
+  uint32_t* counters;  // [rows][n_kv], zero at rest
+  int* err;
+};
+
+// Raise the dynamic shared-memory limit (once per device, before launches).
+cudaError_t attn_prepare();
+cudaError_t attn_decode_launch(const AttnArgs& a, int head_dim, int pdl, cudaStream_t st);
+size_t attn_ws_floats(uint32_t rows, uint32_t n_q, uint32_t n_kv, uint32_t splits, int head_dim);
+
+// Writes normed+roped k and v of `rows` query rows at their positions
+// (used by chunked prefill, where rows of one chunk share a cache slot and
+// must all be written before any row attends).
+cudaError_t rope_kv_write_launch(const AttnArgs& a, int head_dim, int pdl, cudaStream_t st);
+
+}  // namespace nnz

@@ -1,0 +1,1092 @@
+// Engine and C ABI (include/nnz_b200.h).
+//
+// Replaces the reference's Model(Config) buffers + loader (nnmetal/src/
+// model.zig), the encode/dispatch layer (nnmetal/src/transformer.zig:
+// 648-2388, 2452-2930) and the generate loop (:3942-4123).  One decode step
+// is 1 + 5*L + 1 kernels (embed; per layer fused-norm QKV, fused attention,
+// o-proj + residual, fused-norm gate/up + SiLU*mul, down + residual; fused
+// final-norm LM head + argmax) captured once into a CUDA graph with
+// programmatic dependent launch edges.  Token and position live in device
+// memory and the embedding kernel advances them, so generate() replays the
+// graph once per token with no host synchronisation in between.
+#include <cuda_runtime.h>
+#include <string.h>
+
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/nnz_b200.h"
+#include "attn.cuh"
+#include "misc.cuh"
+#include "packing.h"
+#include "qmv.cuh"
+
+using namespace nnz;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+#define NNZ_CK(x)                                                                       \
+  do {                                                                                  \
+    cudaError_t e_ = (x);                                                               \
+    if (e_ != cudaSuccess) return fail(NNZ_ECUDA, std::string(#x) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+constexpr uint32_t kPrefillChunk = 64;
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+float f16_to_f32_host(uint16_t h) {
+  const uint32_t s = (h >> 15) & 1, e = (h >> 10) & 0x1F, m = h & 0x3FF;
+  uint32_t bits;
+  if (e == 0) {
+    if (m == 0) bits = s << 31;
+    else {
+      int ee = -1;
+      uint32_t mm = m;
+      do { ++ee; mm <<= 1; } while (!(mm & 0x400));
+      bits = (s << 31) | ((uint32_t)(127 - 15 - ee) << 23) | ((mm & 0x3FF) << 13);
+    }
+  } else if (e == 31) bits = (s << 31) | 0x7F800000u | (m << 13);
+  else bits = (s << 31) | ((e - 15 + 127) << 23) | (m << 13);
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+
+uint16_t f32_to_f16_host(float f) {  // round to nearest even
+  uint32_t x;
+  memcpy(&x, &f, 4);
+  const uint32_t sign = (x >> 16) & 0x8000u;
+  const int32_t exp = (int32_t)((x >> 23) & 0xFF) - 127 + 15;
+  uint32_t mant = x & 0x7FFFFFu;
+  if (((x >> 23) & 0xFF) == 0xFF) return (uint16_t)(sign | 0x7C00u | (mant ? 0x200u : 0));
+  if (exp >= 31) return (uint16_t)(sign | 0x7C00u);
+  if (exp <= 0) {
+    if (exp < -10) return (uint16_t)sign;
+    mant |= 0x800000u;
+    const uint32_t shift = (uint32_t)(14 - exp);
+    uint32_t hm = mant >> shift;
+    const uint32_t rem = mant & ((1u << shift) - 1), half = 1u << (shift - 1);
+    if (rem > half || (rem == half && (hm & 1))) ++hm;
+    return (uint16_t)(sign | hm);
+  }
+  uint32_t hm = mant >> 13;
+  const uint32_t rem = mant & 0x1FFFu;
+  uint32_t he = (uint32_t)exp;
+  if (rem > 0x1000u || (rem == 0x1000u && (hm & 1))) {
+    ++hm;
+    if (hm == 0x400u) { hm = 0; ++he; if (he >= 31) return (uint16_t)(sign | 0x7C00u); }
+  }
+  return (uint16_t)(sign | (he << 10) | hm);
+}
+
+struct HostTensor {
+  int dtype;
+  std::vector<uint8_t> data;
+};
+
+struct LayerW {
+  uint8_t *qkv, *o, *gu, *down;
+  float *attn_norm, *ffn_norm, *q_norm, *k_norm;
+};
+
+// Per-device workspace for the standalone per-kernel entry points.
+struct DevWs {
+  float* ws = nullptr;
+  size_t ws_floats = 0;
+  uint32_t* counters = nullptr;
+  size_t n_counters = 0;
+  int* err = nullptr;
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  int num_sms = 148;
+};
+std::mutex g_ws_mu;
+std::map<int, DevWs> g_ws;
+std::map<int, bool> g_prepared;
+
+// Kernel attributes, once per device (never inside a stream capture).
+int prepare_device(int dev) {
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  if (g_prepared[dev]) return NNZ_OK;
+  NNZ_CK(qmv_prepare());
+  NNZ_CK(attn_prepare());
+  g_prepared[dev] = true;
+  return NNZ_OK;
+}
+
+int get_ws(DevWs** out) {
+  int dev = 0;
+  NNZ_CK(cudaGetDevice(&dev));
+  int rc = prepare_device(dev);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  DevWs& w = g_ws[dev];
+  if (!w.ws) {
+    NNZ_CK(cudaDeviceGetAttribute(&w.num_sms, cudaDevAttrMultiProcessorCount, dev));
+    w.ws_floats = (size_t)32 << 20;
+    w.n_counters = (size_t)1 << 20;
+    w.scratch_bytes = (size_t)64 << 20;
+    NNZ_CK(cudaMalloc(&w.ws, w.ws_floats * 4));
+    NNZ_CK(cudaMalloc(&w.counters, w.n_counters * 4));
+    NNZ_CK(cudaMalloc(&w.err, 4));
+    NNZ_CK(cudaMalloc(&w.scratch, w.scratch_bytes));
+    NNZ_CK(cudaMemset(w.counters, 0, w.n_counters * 4));
+    NNZ_CK(cudaMemset(w.err, 0, 4));
+  }
+  *out = &w;
+  return NNZ_OK;
+}
+
+std::string err_text(int flags) {
+  std::string s = "device error flags:";
+  if (flags & ERR_MBAR_TIMEOUT) s += " bulk-copy wait timed out;";
+  if (flags & ERR_BAD_TOKEN) s += " token id >= vocab;";
+  if (flags & ERR_BAD_POS) s += " position >= max_context_length;";
+  if (flags & ERR_SPIN_TIMEOUT) s += " spin wait timed out;";
+  return s;
+}
+
+}  // namespace
+
+struct nnz_model {
+  nnz_config c{};
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t st = nullptr;
+  std::map<std::string, HostTensor> host;
+  bool finalized = false;
+  int fmt = 0, bf16s = 0, bf16r = 0;
+  uint32_t qd = 0, kvd = 0, qkv_rows = 0, slots = 0, rows_max = 0;
+  uint8_t* arena = nullptr;
+  size_t arena_bytes = 0;
+  std::vector<LayerW> L;
+  uint8_t* emb_w = nullptr;
+  uint16_t *emb_s = nullptr, *emb_b = nullptr;
+  uint8_t* lm = nullptr;
+  float* fnorm = nullptr;
+  __half *kc = nullptr, *vc = nullptr;
+  size_t kv_layer = 0;  // elements per layer per cache
+  float* residual = nullptr;
+  __half *qkv = nullptr, *attn = nullptr, *h = nullptr;
+  float* logits = nullptr;
+  float* ws = nullptr;
+  size_t ws_floats = 0;
+  uint32_t* counters = nullptr;
+  size_t n_counters = 0;
+  int* err = nullptr;
+  DecodeState* state = nullptr;
+  uint32_t* seq = nullptr;
+  uint32_t* prompt = nullptr;
+  int* iota = nullptr;
+  int* zeros = nullptr;
+  size_t dev_bytes = 0;
+  std::vector<void*> allocs;
+  std::map<std::pair<uint32_t, int>, cudaGraphExec_t> graphs;
+  std::vector<cudaEvent_t> events;
+};
+
+namespace {
+
+int dalloc(nnz_model* m, void** p, size_t bytes) {
+  if (cudaMalloc(p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(NNZ_ENOMEM, "cudaMalloc failed for " + std::to_string(bytes) + " bytes");
+  }
+  m->allocs.push_back(*p);
+  m->dev_bytes += bytes;
+  return NNZ_OK;
+}
+
+const HostTensor* find_t(nnz_model* m, const std::string& name) {
+  auto it = m->host.find(name);
+  return it == m->host.end() ? nullptr : &it->second;
+}
+
+// Fetch a quantized projection in the reference layout, converting scale
+// encodings like the reference loader.  Returns weight bytes and u16 scales
+// (+ biases for Q4) in this model's scale dtype.
+int get_proj(nnz_model* m, const std::string& base, uint32_t M, uint32_t K,
+             std::vector<uint8_t>& w, std::vector<uint16_t>& s, std::vector<uint16_t>& b) {
+  const uint32_t gs = (uint32_t)m->c.group_size;
+  const size_t wbytes = m->fmt == NNZ_Q1 ? (size_t)M * K / 8 : (size_t)M * K / 2;
+  const size_t ng = (size_t)M * K / gs;
+  const HostTensor* tw = find_t(m, base + ".weight");
+  const HostTensor* ts = find_t(m, base + ".scales");
+  if (!tw || !ts) return fail(NNZ_ENOTFOUND, "tensor not found: " + base + (tw ? ".scales" : ".weight"));
+  if (tw->data.size() < wbytes) return fail(NNZ_EINVAL, base + ".weight too small");
+  if (ts->data.size() < ng * 2) return fail(NNZ_EINVAL, base + ".scales too small");
+  w.assign(tw->data.begin(), tw->data.begin() + wbytes);
+  auto conv = [&](const HostTensor* t, std::vector<uint16_t>& out) -> int {
+    out.resize(ng);
+    const uint16_t* src = reinterpret_cast<const uint16_t*>(t->data.data());
+    if (t->dtype != NNZ_DT_F16 && t->dtype != NNZ_DT_BF16)
+      return fail(NNZ_EINVAL, base + ": scales/biases must be f16 or bf16");
+    const bool want_bf16 = m->fmt == NNZ_Q4 && m->bf16s;
+    for (size_t i = 0; i < ng; ++i) {
+      const uint16_t r = src[i];
+      if (t->dtype == NNZ_DT_F16 && want_bf16) {
+        // raw BF16 = high half of the f32 (truncation, model.zig:1191-1205)
+        const float f = f16_to_f32_host(r);
+        uint32_t u;
+        memcpy(&u, &f, 4);
+        out[i] = (uint16_t)(u >> 16);
+      } else if (t->dtype == NNZ_DT_BF16 && !want_bf16) {
+        const uint32_t u = (uint32_t)r << 16;
+        float f;
+        memcpy(&f, &u, 4);
+        out[i] = f32_to_f16_host(f);
+      } else {
+        out[i] = r;
+      }
+    }
+    return NNZ_OK;
+  };
+  int rc = conv(ts, s);
+  if (rc) return rc;
+  if (m->fmt == NNZ_Q1) {
+    if (m->c.q1_scales_are_mlx) {
+      // symmetric scale = mlx_scale / 2 (model.zig:944-959)
+      for (auto& v : s) v = f32_to_f16_host(f16_to_f32_host(v) / 2.0f);
+    }
+    b.clear();
+  } else {
+    const HostTensor* tb = find_t(m, base + ".biases");
+    if (!tb) return fail(NNZ_ENOTFOUND, "tensor not found: " + base + ".biases");
+    if (tb->data.size() < ng * 2) return fail(NNZ_EINVAL, base + ".biases too small");
+    rc = conv(tb, b);
+    if (rc) return rc;
+  }
+  return NNZ_OK;
+}
+
+int get_norm(nnz_model* m, const std::string& name, uint32_t n, std::vector<float>& out) {
+  const HostTensor* t = find_t(m, name);
+  if (!t) return fail(NNZ_ENOTFOUND, "tensor not found: " + name);
+  out.resize(n);
+  if (t->dtype == NNZ_DT_F32) {
+    if (t->data.size() < (size_t)n * 4) return fail(NNZ_EINVAL, name + " too small");
+    memcpy(out.data(), t->data.data(), (size_t)n * 4);
+  } else if (t->dtype == NNZ_DT_F16 || t->dtype == NNZ_DT_BF16) {
+    if (t->data.size() < (size_t)n * 2) return fail(NNZ_EINVAL, name + " too small");
+    const uint16_t* s = reinterpret_cast<const uint16_t*>(t->data.data());
+    for (uint32_t i = 0; i < n; ++i) {
+      if (t->dtype == NNZ_DT_F16) out[i] = f16_to_f32_host(s[i]);
+      else {
+        const uint32_t u = (uint32_t)s[i] << 16;
+        memcpy(&out[i], &u, 4);
+      }
+    }
+  } else {
+    return fail(NNZ_EINVAL, name + ": norm weights must be f32/f16/bf16");
+  }
+  return NNZ_OK;
+}
+
+// ---- launch helpers --------------------------------------------------------
+
+int qmv(nnz_model* m, int sub, int pro, int epi, const uint8_t* w, uint32_t M, uint32_t K,
+        const void* x, uint32_t x_stride, const float* nw, uint32_t batch, void* out,
+        uint32_t out_stride, float* logits, unsigned long long* am, int pdl) {
+  QmvLaunch L{m->fmt, sub, pro, epi, m->bf16s, pdl};
+  QmvArgs a{};
+  a.w = w; a.M = M; a.K = K; a.gs = (uint32_t)m->c.group_size;
+  a.x = x; a.x_stride = x_stride; a.norm_w = nw; a.eps = m->c.eps; a.batch = batch;
+  a.out = out; a.out_stride = out_stride; a.logits = logits; a.logits_stride = M;
+  a.argmax = am; a.ws = m->ws; a.counters = m->counters; a.err = m->err;
+  a.bf16_round = (uint32_t)m->bf16r;
+  NNZ_CK(qmv_launch(L, a, m->num_sms, m->st));
+  return NNZ_OK;
+}
+
+uint32_t attn_splits(nnz_model* m, uint32_t rows) {
+  uint32_t s = (uint32_t)m->num_sms / std::max(1u, m->c.num_kv_heads * rows);
+  return std::min(16u, std::max(1u, s));
+}
+
+int attn(nnz_model* m, uint32_t layer, uint32_t rows, const int* pos, const int* slot, int write,
+         int pdl) {
+  AttnArgs a{};
+  a.qkv = m->qkv; a.qkv_stride = m->qkv_rows;
+  a.q_norm = m->L[layer].q_norm; a.k_norm = m->L[layer].k_norm;
+  a.kc = m->kc + m->kv_layer * layer; a.vc = m->vc + m->kv_layer * layer;
+  a.max_ctx = m->c.max_context_length; a.pos = pos; a.slot = slot; a.rows = rows;
+  a.n_q = m->c.num_query_heads; a.n_kv = m->c.num_kv_heads;
+  a.eps = m->c.eps; a.theta = m->c.rope_theta; a.rope_style = m->c.rope_style;
+  a.write_kv = write; a.splits = attn_splits(m, rows);
+  a.out = m->attn; a.out_stride = m->qd; a.ws = m->ws; a.counters = m->counters; a.err = m->err;
+  NNZ_CK(attn_decode_launch(a, (int)m->c.head_dim, pdl, m->st));
+  return NNZ_OK;
+}
+
+int kv_write(nnz_model* m, uint32_t layer, uint32_t rows, const int* pos, const int* slot, int pdl) {
+  AttnArgs a{};
+  a.qkv = m->qkv; a.qkv_stride = m->qkv_rows;
+  a.q_norm = m->L[layer].q_norm; a.k_norm = m->L[layer].k_norm;
+  a.kc = m->kc + m->kv_layer * layer; a.vc = m->vc + m->kv_layer * layer;
+  a.max_ctx = m->c.max_context_length; a.pos = pos; a.slot = slot; a.rows = rows;
+  a.n_q = m->c.num_query_heads; a.n_kv = m->c.num_kv_heads;
+  a.eps = m->c.eps; a.theta = m->c.rope_theta; a.rope_style = m->c.rope_style;
+  a.err = m->err;
+  NNZ_CK(rope_kv_write_launch(a, (int)m->c.head_dim, pdl, m->st));
+  return NNZ_OK;
+}
+
+// One decoder layer for `rows` rows.  decode: pos/slot per row, fused KV
+// write; prefill chunk: rows share slot 0, K/V written first.
+int enqueue_layer(nnz_model* m, uint32_t l, uint32_t rows, const int* pos, const int* slot,
+                  bool prefill, int pdl) {
+  const nnz_config& c = m->c;
+  const LayerW& W = m->L[l];
+  int rc;
+  if ((rc = qmv(m, 1, PRO_NORM, EPI_F16, W.qkv, m->qkv_rows, c.hidden_size, m->residual,
+                c.hidden_size, W.attn_norm, rows, m->qkv, m->qkv_rows, nullptr, nullptr, pdl)))
+    return rc;
+  if (prefill) {
+    if ((rc = kv_write(m, l, rows, pos, slot, pdl))) return rc;
+    if ((rc = attn(m, l, rows, pos, slot, 0, pdl))) return rc;
+  } else {
+    if ((rc = attn(m, l, rows, pos, slot, 1, pdl))) return rc;
+  }
+  if ((rc = qmv(m, 1, PRO_F16, EPI_RESADD, W.o, c.hidden_size, m->qd, m->attn, m->qd, nullptr,
+                rows, m->residual, c.hidden_size, nullptr, nullptr, pdl)))
+    return rc;
+  if ((rc = qmv(m, 2, PRO_NORM, EPI_SILU, W.gu, c.intermediate_size, c.hidden_size, m->residual,
+                c.hidden_size, W.ffn_norm, rows, m->h, c.intermediate_size, nullptr, nullptr, pdl)))
+    return rc;
+  if ((rc = qmv(m, 1, PRO_F16, EPI_RESADD, W.down, c.hidden_size, c.intermediate_size, m->h,
+                c.intermediate_size, nullptr, rows, m->residual, c.hidden_size, nullptr, nullptr,
+                pdl)))
+    return rc;
+  return NNZ_OK;
+}
+
+int enqueue_embed(nnz_model* m, uint32_t rows, const uint32_t* tokens, int pdl) {
+  EmbedArgs e{};
+  e.wbytes = m->emb_w; e.scales = m->emb_s; e.biases = m->emb_b;
+  e.vocab = m->c.vocab_size; e.H = m->c.hidden_size; e.gs = (uint32_t)m->c.group_size;
+  e.bf16_round = m->bf16r; e.st = m->state; e.tokens = tokens;
+  e.seq = m->seq; e.seq_len = m->c.max_context_length;
+  e.residual = m->residual; e.rows = rows; e.err = m->err;
+  NNZ_CK(embed_launch(e, m->fmt, m->bf16s, pdl, m->st));
+  return NNZ_OK;
+}
+
+int enqueue_decode(nnz_model* m, uint32_t rows, bool want_logits, int pdl) {
+  int rc;
+  if ((rc = enqueue_embed(m, rows, nullptr, pdl))) return rc;
+  for (uint32_t l = 0; l < m->c.num_layers; ++l)
+    if ((rc = enqueue_layer(m, l, rows, m->state->pos, nullptr, false, pdl))) return rc;
+  return qmv(m, 1, PRO_NORM, EPI_LOGITS, m->lm, m->c.vocab_size, m->c.hidden_size, m->residual,
+             m->c.hidden_size, m->fnorm, rows, nullptr, 0, want_logits ? m->logits : nullptr,
+             m->state->argmax, pdl);
+}
+
+int get_graph(nnz_model* m, uint32_t rows, bool want_logits, cudaGraphExec_t* out) {
+  auto key = std::make_pair(rows, want_logits ? 1 : 0);
+  auto it = m->graphs.find(key);
+  if (it != m->graphs.end()) {
+    *out = it->second;
+    return NNZ_OK;
+  }
+  cudaGraph_t g;
+  NNZ_CK(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+  int rc = enqueue_decode(m, rows, want_logits, 1);
+  cudaError_t ce = cudaStreamEndCapture(m->st, &g);
+  if (rc) return rc;
+  if (ce != cudaSuccess) return fail(NNZ_ECUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+  cudaGraphExec_t ex;
+  NNZ_CK(cudaGraphInstantiate(&ex, g, 0));
+  cudaGraphDestroy(g);
+  m->graphs[key] = ex;
+  *out = ex;
+  return NNZ_OK;
+}
+
+int sync_check(nnz_model* m) {
+  NNZ_CK(cudaStreamSynchronize(m->st));
+  int flags = 0;
+  NNZ_CK(cudaMemcpy(&flags, m->err, 4, cudaMemcpyDeviceToHost));
+  if (flags) {
+    cudaMemset(m->err, 0, 4);
+    return fail(flags & (ERR_MBAR_TIMEOUT | ERR_SPIN_TIMEOUT) ? NNZ_ETIMEDOUT : NNZ_EDEVICE,
+                err_text(flags));
+  }
+  return NNZ_OK;
+}
+
+int set_advance(nnz_model* m, int v) {
+  NNZ_CK(cudaMemsetAsync(&m->state->advance, 0, 4, m->st));
+  if (v) NNZ_CK(cudaMemsetAsync(&m->state->advance, 1, 1, m->st));
+  return NNZ_OK;
+}
+
+int enqueue_prefill(nnz_model* m, uint32_t n, bool want_logits) {
+  int rc;
+  for (uint32_t c0 = 0; c0 < n; c0 += kPrefillChunk) {
+    const uint32_t rows = std::min(kPrefillChunk, n - c0);
+    if ((rc = enqueue_embed(m, rows, m->prompt + c0, 0))) return rc;
+    for (uint32_t l = 0; l < m->c.num_layers; ++l)
+      if ((rc = enqueue_layer(m, l, rows, m->iota + c0, m->zeros, true, 0))) return rc;
+    if (c0 + rows == n) {
+      const float* last = m->residual + (size_t)(rows - 1) * m->c.hidden_size;
+      if ((rc = qmv(m, 1, PRO_NORM, EPI_LOGITS, m->lm, m->c.vocab_size, m->c.hidden_size, last,
+                    m->c.hidden_size, m->fnorm, 1, nullptr, 0, want_logits ? m->logits : nullptr,
+                    m->state->argmax, 0)))
+        return rc;
+    }
+  }
+  return NNZ_OK;
+}
+
+}  // namespace
+
+// =========================================================================
+// C ABI
+// =========================================================================
+extern "C" {
+
+const char* nnz_last_error(void) { return g_err.c_str(); }
+int nnz_version(void) { return 1; }
+int nnz_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+size_t nnz_packed_bytes(int fmt, uint32_t M, uint32_t K, uint32_t gs, uint32_t sub) {
+  if ((fmt != NNZ_Q1 && fmt != NNZ_Q4) || gs == 0 || gs % 32 || K % gs || sub == 0) return 0;
+  return packed_bytes(fmt, M, K, gs, sub);
+}
+
+int nnz_pack_weights(int fmt, const void* weight, const uint16_t* scales, const uint16_t* biases,
+                     uint32_t M, uint32_t K, uint32_t gs, uint32_t sub, uint32_t sub_index,
+                     void* packed_out) {
+  if (pack_host(fmt, weight, scales, biases, M, K, gs, sub, sub_index, packed_out, 0))
+    return fail(NNZ_EINVAL, "nnz_pack_weights: invalid arguments");
+  return NNZ_OK;
+}
+
+int nnz_unpack_weights(int fmt, const void* packed, uint32_t M, uint32_t K, uint32_t gs,
+                       uint32_t sub, uint32_t sub_index, void* weight, uint16_t* scales,
+                       uint16_t* biases) {
+  if (unpack_host(fmt, packed, M, K, gs, sub, sub_index, weight, scales, biases))
+    return fail(NNZ_EINVAL, "nnz_unpack_weights: invalid arguments");
+  return NNZ_OK;
+}
+
+int nnz_model_create(int device, const nnz_config* cfg, nnz_model** out) {
+  if (!cfg || !out) return fail(NNZ_EINVAL, "null argument");
+  const nnz_config& c = *cfg;
+  if (c.quant_format != NNZ_Q1 && c.quant_format != NNZ_Q4) return fail(NNZ_EINVAL, "quant_format");
+  if (c.head_dim != 64 && c.head_dim != 128) return fail(NNZ_EINVAL, "head_dim must be 64 or 128");
+  if (!c.num_kv_heads || c.num_query_heads % c.num_kv_heads ||
+      c.num_query_heads / c.num_kv_heads > (uint32_t)kAttnMaxG)
+    return fail(NNZ_EINVAL, "num_query_heads must be a multiple (<= 8x) of num_kv_heads");
+  const uint32_t gs = (uint32_t)c.group_size;
+  const uint32_t qd = c.num_query_heads * c.head_dim;
+  if (gs == 0 || gs % 32 || gs > 256 || c.hidden_size % gs || c.intermediate_size % gs || qd % gs)
+    return fail(NNZ_EINVAL, "group_size must be a multiple of 32 (<= 256) dividing hidden, "
+                            "intermediate and query dims");
+  if (!c.vocab_size || !c.num_layers || !c.max_context_length)
+    return fail(NNZ_EINVAL, "vocab_size, num_layers and max_context_length must be > 0");
+  if (c.max_batch == 0 || c.max_batch > (uint32_t)kMaxRows) return fail(NNZ_EINVAL, "max_batch");
+  if (c.tp_size > 1) return fail(NNZ_EINVAL, "tensor parallelism is driven per rank by the host");
+  int ndev = 0;
+  NNZ_CK(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return fail(NNZ_EINVAL, "bad device index");
+  auto* m = new nnz_model();
+  m->c = c;
+  if (m->c.eps <= 0.f) m->c.eps = 1e-6f;
+  m->device = device;
+  m->fmt = c.quant_format;
+  m->bf16s = (c.quant_format == NNZ_Q4 && c.scale_dtype == NNZ_SCALE_BF16) ? 1 : 0;
+  m->bf16r = (c.quant_format == NNZ_Q4 && c.bf16_faithful) ? 1 : 0;
+  *out = m;
+  return NNZ_OK;
+}
+
+int nnz_model_load_tensor(nnz_model* m, const char* name, int dtype, const void* data, size_t bytes) {
+  if (!m || !name || (!data && bytes)) return fail(NNZ_EINVAL, "null argument");
+  if (m->finalized) return fail(NNZ_ESTATE, "model already finalized");
+  if (dtype < NNZ_DT_U8 || dtype > NNZ_DT_F32) return fail(NNZ_EINVAL, "dtype");
+  HostTensor& t = m->host[name];
+  t.dtype = dtype;
+  t.data.assign(static_cast<const uint8_t*>(data), static_cast<const uint8_t*>(data) + bytes);
+  return NNZ_OK;
+}
+
+int nnz_model_finalize(nnz_model* m) {
+  if (!m) return fail(NNZ_EINVAL, "null model");
+  if (m->finalized) return fail(NNZ_ESTATE, "model already finalized");
+  const nnz_config& c = m->c;
+  NNZ_CK(cudaSetDevice(m->device));
+  NNZ_CK(cudaDeviceGetAttribute(&m->num_sms, cudaDevAttrMultiProcessorCount, m->device));
+  const uint32_t H = c.hidden_size, I = c.intermediate_size, gs = (uint32_t)c.group_size;
+  m->qd = c.num_query_heads * c.head_dim;
+  m->kvd = c.num_kv_heads * c.head_dim;
+  m->qkv_rows = m->qd + 2 * m->kvd;
+  m->slots = c.max_batch;
+  m->rows_max = std::max(c.max_batch, kPrefillChunk);
+  const int fmt = m->fmt;
+
+  // ---- pack weights on the host ----------------------------------------
+  const size_t b_qkv = packed_bytes(fmt, m->qkv_rows, H, gs, 1);
+  const size_t b_o = packed_bytes(fmt, H, m->qd, gs, 1);
+  const size_t b_gu = packed_bytes(fmt, I, H, gs, 2);
+  const size_t b_dn = packed_bytes(fmt, H, I, gs, 1);
+  const size_t b_lm = packed_bytes(fmt, c.vocab_size, H, gs, 1);
+  const size_t emb_w = fmt == NNZ_Q1 ? (size_t)c.vocab_size * H / 8 : (size_t)c.vocab_size * H / 2;
+  const size_t emb_g = (size_t)c.vocab_size * H / gs;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
+  struct LOff { size_t qkv, o, gu, dn, an, fn, qn, kn; };
+  std::vector<LOff> lo(c.num_layers);
+  for (auto& x : lo) {
+    x.qkv = take(b_qkv); x.o = take(b_o); x.gu = take(b_gu); x.dn = take(b_dn);
+    x.an = take(H * 4); x.fn = take(H * 4); x.qn = take(c.head_dim * 4); x.kn = take(c.head_dim * 4);
+  }
+  const size_t o_embw = take(emb_w), o_embs = take(emb_g * 2), o_embb = take(emb_g * 2);
+  const size_t o_lm = take(b_lm), o_fn = take(H * 4);
+  m->arena_bytes = off;
+  int rc;
+  if ((rc = dalloc(m, (void**)&m->arena, m->arena_bytes))) return rc;
+  std::vector<uint8_t> buf;
+  std::vector<uint8_t> w;
+  std::vector<uint16_t> s, b;
+  m->L.resize(c.num_layers);
+  for (uint32_t l = 0; l < c.num_layers; ++l) {
+    const std::string pre = "model.layers." + std::to_string(l) + ".";
+    // fused QKV: q, k, v rows concatenated (flat layouts concatenate exactly)
+    {
+      std::vector<uint8_t> wc;
+      std::vector<uint16_t> sc, bc;
+      const char* names[3] = {"self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"};
+      const uint32_t rows[3] = {m->qd, m->kvd, m->kvd};
+      for (int i = 0; i < 3; ++i) {
+        if ((rc = get_proj(m, pre + names[i], rows[i], H, w, s, b))) return rc;
+        wc.insert(wc.end(), w.begin(), w.end());
+        sc.insert(sc.end(), s.begin(), s.end());
+        bc.insert(bc.end(), b.begin(), b.end());
+      }
+      buf.assign(b_qkv, 0);
+      pack_host(fmt, wc.data(), sc.data(), bc.empty() ? nullptr : bc.data(), m->qkv_rows, H, gs, 1, 0,
+                buf.data(), 0);
+      NNZ_CK(cudaMemcpy(m->arena + lo[l].qkv, buf.data(), b_qkv, cudaMemcpyHostToDevice));
+    }
+    if ((rc = get_proj(m, pre + "self_attn.o_proj", H, m->qd, w, s, b))) return rc;
+    buf.assign(b_o, 0);
+    pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), H, m->qd, gs, 1, 0, buf.data(), 0);
+    NNZ_CK(cudaMemcpy(m->arena + lo[l].o, buf.data(), b_o, cudaMemcpyHostToDevice));
+    buf.assign(b_gu, 0);
+    if ((rc = get_proj(m, pre + "mlp.gate_proj", I, H, w, s, b))) return rc;
+    pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), I, H, gs, 2, 0, buf.data(), 0);
+    if ((rc = get_proj(m, pre + "mlp.up_proj", I, H, w, s, b))) return rc;
+    pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), I, H, gs, 2, 1, buf.data(), 0);
+    NNZ_CK(cudaMemcpy(m->arena + lo[l].gu, buf.data(), b_gu, cudaMemcpyHostToDevice));
+    if ((rc = get_proj(m, pre + "mlp.down_proj", H, I, w, s, b))) return rc;
+    buf.assign(b_dn, 0);
+    pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), H, I, gs, 1, 0, buf.data(), 0);
+    NNZ_CK(cudaMemcpy(m->arena + lo[l].dn, buf.data(), b_dn, cudaMemcpyHostToDevice));
+    std::vector<float> nv;
+    const std::pair<const char*, std::pair<size_t, uint32_t>> norms[4] = {
+        {"input_layernorm.weight", {lo[l].an, H}},
+        {"post_attention_layernorm.weight", {lo[l].fn, H}},
+        {"self_attn.q_norm.weight", {lo[l].qn, c.head_dim}},
+        {"self_attn.k_norm.weight", {lo[l].kn, c.head_dim}}};
+    for (const auto& nm : norms) {
+      if ((rc = get_norm(m, pre + nm.first, nm.second.second, nv))) return rc;
+      NNZ_CK(cudaMemcpy(m->arena + nm.second.first, nv.data(), nv.size() * 4, cudaMemcpyHostToDevice));
+    }
+    LayerW& LW = m->L[l];
+    LW.qkv = m->arena + lo[l].qkv; LW.o = m->arena + lo[l].o;
+    LW.gu = m->arena + lo[l].gu; LW.down = m->arena + lo[l].dn;
+    LW.attn_norm = reinterpret_cast<float*>(m->arena + lo[l].an);
+    LW.ffn_norm = reinterpret_cast<float*>(m->arena + lo[l].fn);
+    LW.q_norm = reinterpret_cast<float*>(m->arena + lo[l].qn);
+    LW.k_norm = reinterpret_cast<float*>(m->arena + lo[l].kn);
+    // release host copies as we go
+    for (const char* nm : {"self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj",
+                           "self_attn.o_proj", "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"})
+      for (const char* suf : {".weight", ".scales", ".biases"}) m->host.erase(pre + nm + suf);
+  }
+  // embedding (reference layout, gathered per token) and LM head (packed)
+  if ((rc = get_proj(m, "model.embed_tokens", c.vocab_size, H, w, s, b))) return rc;
+  NNZ_CK(cudaMemcpy(m->arena + o_embw, w.data(), emb_w, cudaMemcpyHostToDevice));
+  NNZ_CK(cudaMemcpy(m->arena + o_embs, s.data(), emb_g * 2, cudaMemcpyHostToDevice));
+  if (fmt == NNZ_Q4) NNZ_CK(cudaMemcpy(m->arena + o_embb, b.data(), emb_g * 2, cudaMemcpyHostToDevice));
+  if (!c.tie_word_embeddings) {
+    if ((rc = get_proj(m, "lm_head", c.vocab_size, H, w, s, b))) return rc;
+  }
+  buf.assign(b_lm, 0);
+  pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), c.vocab_size, H, gs, 1, 0,
+            buf.data(), 0);
+  NNZ_CK(cudaMemcpy(m->arena + o_lm, buf.data(), b_lm, cudaMemcpyHostToDevice));
+  {
+    std::vector<float> nv;
+    if ((rc = get_norm(m, "model.norm.weight", H, nv))) return rc;
+    NNZ_CK(cudaMemcpy(m->arena + o_fn, nv.data(), H * 4, cudaMemcpyHostToDevice));
+  }
+  m->emb_w = m->arena + o_embw;
+  m->emb_s = reinterpret_cast<uint16_t*>(m->arena + o_embs);
+  m->emb_b = reinterpret_cast<uint16_t*>(m->arena + o_embb);
+  m->lm = m->arena + o_lm;
+  m->fnorm = reinterpret_cast<float*>(m->arena + o_fn);
+  m->host.clear();
+  std::vector<uint8_t>().swap(buf);
+
+  // ---- KV cache, activations, workspace -----------------------------------
+  m->kv_layer = (size_t)m->slots * c.num_kv_heads * c.max_context_length * c.head_dim;
+  const size_t kv_bytes = m->kv_layer * c.num_layers * 2;
+  if ((rc = dalloc(m, (void**)&m->kc, kv_bytes))) return rc;
+  if ((rc = dalloc(m, (void**)&m->vc, kv_bytes))) return rc;
+  NNZ_CK(cudaMemset(m->kc, 0, kv_bytes));
+  NNZ_CK(cudaMemset(m->vc, 0, kv_bytes));
+  const uint32_t R = m->rows_max;
+  if ((rc = dalloc(m, (void**)&m->residual, (size_t)R * H * 4))) return rc;
+  if ((rc = dalloc(m, (void**)&m->qkv, (size_t)R * m->qkv_rows * 2))) return rc;
+  if ((rc = dalloc(m, (void**)&m->attn, (size_t)R * m->qd * 2))) return rc;
+  if ((rc = dalloc(m, (void**)&m->h, (size_t)R * I * 2))) return rc;
+  if ((rc = dalloc(m, (void**)&m->logits, (size_t)c.max_batch * c.vocab_size * 4))) return rc;
+  size_t wsf = 0, nctr = 0;
+  for (uint32_t rows = 1; rows <= R; ++rows) {
+    const uint32_t ych = (rows + kBatchChunk - 1) / kBatchChunk;
+    const uint32_t shapes[4][4] = {{m->qkv_rows, H, 1, 0}, {H, m->qd, 1, 0}, {I, H, 2, 0}, {H, I, 1, 0}};
+    for (const auto& sh : shapes) {
+      wsf = std::max(wsf, qmv_ws_floats(sh[0], sh[1], gs, fmt, (int)sh[2], rows, m->num_sms));
+      nctr = std::max(nctr, (size_t)ych * num_tiles(sh[0]));
+    }
+    wsf = std::max(wsf, attn_ws_floats(rows, c.num_query_heads, c.num_kv_heads, attn_splits(m, rows),
+                                       (int)c.head_dim));
+    nctr = std::max(nctr, (size_t)rows * c.num_kv_heads);
+  }
+  wsf = std::max(wsf, qmv_ws_floats(c.vocab_size, H, gs, fmt, 1, c.max_batch, m->num_sms));
+  m->ws_floats = std::max<size_t>(wsf, 1024);
+  m->n_counters = std::max<size_t>(nctr, 1024);
+  if ((rc = dalloc(m, (void**)&m->ws, m->ws_floats * 4))) return rc;
+  if ((rc = dalloc(m, (void**)&m->counters, m->n_counters * 4))) return rc;
+  if ((rc = dalloc(m, (void**)&m->err, 16))) return rc;
+  if ((rc = dalloc(m, (void**)&m->state, sizeof(DecodeState)))) return rc;
+  if ((rc = dalloc(m, (void**)&m->seq, (size_t)m->slots * c.max_context_length * 4))) return rc;
+  if ((rc = dalloc(m, (void**)&m->prompt, (size_t)c.max_context_length * 4))) return rc;
+  if ((rc = dalloc(m, (void**)&m->iota, (size_t)c.max_context_length * 4))) return rc;
+  if ((rc = dalloc(m, (void**)&m->zeros, (size_t)R * 4))) return rc;
+  NNZ_CK(cudaMemset(m->counters, 0, m->n_counters * 4));
+  NNZ_CK(cudaMemset(m->err, 0, 16));
+  NNZ_CK(cudaMemset(m->state, 0, sizeof(DecodeState)));
+  NNZ_CK(cudaMemset(m->seq, 0, (size_t)m->slots * c.max_context_length * 4));
+  NNZ_CK(cudaMemset(m->zeros, 0, (size_t)R * 4));
+  {
+    std::vector<int> io(c.max_context_length);
+    for (uint32_t i = 0; i < c.max_context_length; ++i) io[i] = (int)i;
+    NNZ_CK(cudaMemcpy(m->iota, io.data(), io.size() * 4, cudaMemcpyHostToDevice));
+  }
+  NNZ_CK(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking));
+  if ((rc = prepare_device(m->device))) return rc;
+  m->finalized = true;
+  return NNZ_OK;
+}
+
+int nnz_model_free(nnz_model* m) {
+  if (!m) return NNZ_OK;
+  if (m->device >= 0) cudaSetDevice(m->device);
+  if (m->st) cudaStreamSynchronize(m->st);
+  for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+  for (auto e : m->events) cudaEventDestroy(e);
+  for (void* p : m->allocs) cudaFree(p);
+  if (m->st) cudaStreamDestroy(m->st);
+  delete m;
+  return NNZ_OK;
+}
+
+size_t nnz_model_device_bytes(const nnz_model* m) { return m ? m->dev_bytes : 0; }
+
+int nnz_forward_decode(nnz_model* m, const uint32_t* tokens, const uint32_t* positions,
+                       uint32_t batch, float* logits, uint32_t* argmax_out) {
+  if (!m || !tokens || !positions || !argmax_out) return fail(NNZ_EINVAL, "null argument");
+  if (!m->finalized) return fail(NNZ_ESTATE, "model not finalized");
+  if (batch == 0 || batch > m->c.max_batch) return fail(NNZ_EINVAL, "batch out of range");
+  for (uint32_t r = 0; r < batch; ++r) {
+    if (tokens[r] >= m->c.vocab_size) return fail(NNZ_EINVAL, "token id >= vocab_size");
+    if (positions[r] >= m->c.max_context_length) return fail(NNZ_EINVAL, "position >= max_context_length");
+  }
+  NNZ_CK(cudaSetDevice(m->device));
+  int rc;
+  NNZ_CK(cudaMemcpyAsync(m->state->token, tokens, batch * 4, cudaMemcpyHostToDevice, m->st));
+  NNZ_CK(cudaMemcpyAsync(m->state->pos, positions, batch * 4, cudaMemcpyHostToDevice, m->st));
+  if ((rc = set_advance(m, 0))) return rc;
+  cudaGraphExec_t g;
+  if ((rc = get_graph(m, batch, logits != nullptr, &g))) return rc;
+  NNZ_CK(cudaGraphLaunch(g, m->st));
+  std::vector<unsigned long long> am(batch);
+  NNZ_CK(cudaMemcpyAsync(am.data(), m->state->argmax, batch * 8, cudaMemcpyDeviceToHost, m->st));
+  if (logits)
+    NNZ_CK(cudaMemcpyAsync(logits, m->logits, (size_t)batch * m->c.vocab_size * 4,
+                           cudaMemcpyDeviceToHost, m->st));
+  if ((rc = sync_check(m))) return rc;
+  for (uint32_t r = 0; r < batch; ++r) argmax_out[r] = argmax_index(am[r]);
+  return NNZ_OK;
+}
+
+int nnz_prefill(nnz_model* m, const uint32_t* tokens, uint32_t n, uint32_t* next_token,
+                float* last_logits) {
+  if (!m || !tokens || !next_token) return fail(NNZ_EINVAL, "null argument");
+  if (!m->finalized) return fail(NNZ_ESTATE, "model not finalized");
+  if (n == 0 || n >= m->c.max_context_length) return fail(NNZ_EINVAL, "prompt length out of range");
+  for (uint32_t i = 0; i < n; ++i)
+    if (tokens[i] >= m->c.vocab_size) return fail(NNZ_EINVAL, "token id >= vocab_size");
+  NNZ_CK(cudaSetDevice(m->device));
+  int rc;
+  NNZ_CK(cudaMemcpyAsync(m->prompt, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, m->st));
+  NNZ_CK(cudaMemcpyAsync(m->seq, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, m->st));
+  if ((rc = enqueue_prefill(m, n, last_logits != nullptr))) return rc;
+  const int p = (int)n - 1;
+  NNZ_CK(cudaMemcpyAsync(m->state->pos, &p, 4, cudaMemcpyHostToDevice, m->st));
+  NNZ_CK(cudaMemcpyAsync(m->state->token, tokens + n - 1, 4, cudaMemcpyHostToDevice, m->st));
+  unsigned long long am = 0;
+  NNZ_CK(cudaMemcpyAsync(&am, m->state->argmax, 8, cudaMemcpyDeviceToHost, m->st));
+  if (last_logits)
+    NNZ_CK(cudaMemcpyAsync(last_logits, m->logits, (size_t)m->c.vocab_size * 4,
+                           cudaMemcpyDeviceToHost, m->st));
+  if ((rc = sync_check(m))) return rc;
+  *next_token = argmax_index(am);
+  return NNZ_OK;
+}
+
+int nnz_generate(nnz_model* m, const nnz_generate_opts* o, nnz_generate_result* res) {
+  if (!m || !o || !res || !o->prompt_ids || !o->output_tokens) return fail(NNZ_EINVAL, "null argument");
+  if (!m->finalized) return fail(NNZ_ESTATE, "model not finalized");
+  if (o->n_prompt == 0 || o->n_prompt >= m->c.max_context_length || o->max_new == 0)
+    return fail(NNZ_EINVAL, "prompt length / max_new out of range");
+  for (uint32_t i = 0; i < o->n_prompt; ++i)
+    if (o->prompt_ids[i] >= m->c.vocab_size) return fail(NNZ_EINVAL, "token id >= vocab_size");
+  NNZ_CK(cudaSetDevice(m->device));
+  const uint32_t n = o->n_prompt;
+  // the reference stops when position reaches max_context_length (transformer.zig:3993)
+  const uint32_t steps = std::min<uint32_t>(o->max_new, m->c.max_context_length - n);
+  int rc;
+  cudaGraphExec_t g;
+  if ((rc = get_graph(m, 1, false, &g))) return rc;
+  while (m->events.size() < (size_t)steps + 2) {
+    cudaEvent_t e;
+    NNZ_CK(cudaEventCreate(&e));
+    m->events.push_back(e);
+  }
+  NNZ_CK(cudaMemsetAsync(m->state, 0, sizeof(DecodeState), m->st));
+  NNZ_CK(cudaMemcpyAsync(m->prompt, o->prompt_ids, (size_t)n * 4, cudaMemcpyHostToDevice, m->st));
+  NNZ_CK(cudaMemcpyAsync(m->seq, o->prompt_ids, (size_t)n * 4, cudaMemcpyHostToDevice, m->st));
+  NNZ_CK(cudaEventRecord(m->events[0], m->st));
+  if ((rc = enqueue_prefill(m, n, false))) return rc;
+  const int p = (int)n - 1;
+  NNZ_CK(cudaMemcpyAsync(m->state->pos, &p, 4, cudaMemcpyHostToDevice, m->st));
+  if ((rc = set_advance(m, 1))) return rc;
+  NNZ_CK(cudaEventRecord(m->events[1], m->st));
+  for (uint32_t i = 0; i < steps; ++i) {
+    NNZ_CK(cudaGraphLaunch(g, m->st));
+    NNZ_CK(cudaEventRecord(m->events[2 + i], m->st));
+  }
+  std::vector<uint32_t> toks(steps);
+  NNZ_CK(cudaMemcpyAsync(toks.data(), m->seq + n, (size_t)steps * 4, cudaMemcpyDeviceToHost, m->st));
+  if ((rc = set_advance(m, 0))) return rc;
+  if ((rc = sync_check(m))) return rc;
+  float ms = 0.f;
+  NNZ_CK(cudaEventElapsedTime(&ms, m->events[0], m->events[1]));
+  res->prefill_ns = (uint64_t)((double)ms * 1e6);
+  uint32_t count = 0;
+  uint64_t decode_ns = 0;
+  for (uint32_t i = 0; i < steps; ++i) {
+    bool eos = false;
+    for (uint32_t k = 0; k < o->n_eos; ++k) eos |= (o->eos_ids && toks[i] == o->eos_ids[k]);
+    if (eos) break;
+    o->output_tokens[count] = toks[i];
+    NNZ_CK(cudaEventElapsedTime(&ms, m->events[1 + i], m->events[2 + i]));
+    const uint64_t ns = (uint64_t)((double)ms * 1e6);
+    if (o->per_token_ns) o->per_token_ns[count] = ns;
+    decode_ns += ns;
+    ++count;
+  }
+  res->tokens_generated = count;
+  res->decode_ns = decode_ns;
+  return NNZ_OK;
+}
+
+int nnz_decode_steps(nnz_model* m, const uint32_t* tokens, const uint32_t* positions,
+                     uint32_t batch, uint32_t steps, uint32_t* out_tokens, uint64_t* per_step_ns) {
+  if (!m || !tokens || !positions || !out_tokens) return fail(NNZ_EINVAL, "null argument");
+  if (!m->finalized) return fail(NNZ_ESTATE, "model not finalized");
+  if (batch == 0 || batch > m->c.max_batch || steps == 0) return fail(NNZ_EINVAL, "batch/steps");
+  for (uint32_t r = 0; r < batch; ++r) {
+    if (tokens[r] >= m->c.vocab_size) return fail(NNZ_EINVAL, "token id >= vocab_size");
+    if (positions[r] + steps > m->c.max_context_length)
+      return fail(NNZ_EINVAL, "positions + steps exceed max_context_length");
+  }
+  NNZ_CK(cudaSetDevice(m->device));
+  int rc;
+  cudaGraphExec_t g;
+  if ((rc = get_graph(m, batch, false, &g))) return rc;
+  while (m->events.size() < (size_t)steps + 2) {
+    cudaEvent_t e;
+    NNZ_CK(cudaEventCreate(&e));
+    m->events.push_back(e);
+  }
+  NNZ_CK(cudaMemcpyAsync(m->state->token, tokens, batch * 4, cudaMemcpyHostToDevice, m->st));
+  NNZ_CK(cudaMemcpyAsync(m->state->pos, positions, batch * 4, cudaMemcpyHostToDevice, m->st));
+  if ((rc = set_advance(m, 0))) return rc;
+  NNZ_CK(cudaEventRecord(m->events[0], m->st));
+  for (uint32_t s = 0; s < steps; ++s) {
+    if (s == 1 && (rc = set_advance(m, 1))) return rc;
+    NNZ_CK(cudaGraphLaunch(g, m->st));
+    NNZ_CK(cudaEventRecord(m->events[1 + s], m->st));
+  }
+  // tokens consumed at steps 1..steps-1 are recorded in seq at pos+1..; the
+  // last step's result is still in the argmax slots.
+  const uint32_t L = m->c.max_context_length;
+  std::vector<uint32_t> seqv((size_t)batch * L);
+  if (steps > 1) NNZ_CK(cudaMemcpyAsync(seqv.data(), m->seq, seqv.size() * 4, cudaMemcpyDeviceToHost, m->st));
+  std::vector<unsigned long long> am(batch);
+  NNZ_CK(cudaMemcpyAsync(am.data(), m->state->argmax, batch * 8, cudaMemcpyDeviceToHost, m->st));
+  if ((rc = set_advance(m, 0))) return rc;
+  if ((rc = sync_check(m))) return rc;
+  for (uint32_t s = 0; s < steps; ++s)
+    for (uint32_t r = 0; r < batch; ++r)
+      out_tokens[(size_t)s * batch + r] =
+          (s + 1 < steps) ? seqv[(size_t)r * L + positions[r] + 1 + s] : argmax_index(am[r]);
+  if (per_step_ns) {
+    for (uint32_t s = 0; s < steps; ++s) {
+      float ms = 0.f;
+      NNZ_CK(cudaEventElapsedTime(&ms, m->events[s], m->events[1 + s]));
+      per_step_ns[s] = (uint64_t)((double)ms * 1e6);
+    }
+  }
+  return NNZ_OK;
+}
+
+int nnz_model_write_kv(nnz_model* m, uint32_t layer, uint32_t slot, const uint16_t* k,
+                       const uint16_t* v, uint32_t len) {
+  if (!m || !k || !v) return fail(NNZ_EINVAL, "null argument");
+  if (!m->finalized) return fail(NNZ_ESTATE, "model not finalized");
+  const nnz_config& c = m->c;
+  if (layer >= c.num_layers || slot >= m->slots || len > c.max_context_length)
+    return fail(NNZ_EINVAL, "layer/slot/len out of range");
+  NNZ_CK(cudaSetDevice(m->device));
+  for (uint32_t h = 0; h < c.num_kv_heads; ++h) {
+    const size_t off = m->kv_layer * layer + ((size_t)slot * c.num_kv_heads + h) * c.max_context_length * c.head_dim;
+    const size_t n = (size_t)len * c.head_dim;
+    NNZ_CK(cudaMemcpyAsync(m->kc + off, k + h * n, n * 2, cudaMemcpyHostToDevice, m->st));
+    NNZ_CK(cudaMemcpyAsync(m->vc + off, v + h * n, n * 2, cudaMemcpyHostToDevice, m->st));
+  }
+  return sync_check(m);
+}
+
+int nnz_model_read_kv(nnz_model* m, uint32_t layer, uint32_t slot, uint16_t* k, uint16_t* v,
+                      uint32_t len) {
+  if (!m || !k || !v) return fail(NNZ_EINVAL, "null argument");
+  if (!m->finalized) return fail(NNZ_ESTATE, "model not finalized");
+  const nnz_config& c = m->c;
+  if (layer >= c.num_layers || slot >= m->slots || len > c.max_context_length)
+    return fail(NNZ_EINVAL, "layer/slot/len out of range");
+  NNZ_CK(cudaSetDevice(m->device));
+  for (uint32_t h = 0; h < c.num_kv_heads; ++h) {
+    const size_t off = m->kv_layer * layer + ((size_t)slot * c.num_kv_heads + h) * c.max_context_length * c.head_dim;
+    const size_t n = (size_t)len * c.head_dim;
+    NNZ_CK(cudaMemcpyAsync(k + h * n, m->kc + off, n * 2, cudaMemcpyDeviceToHost, m->st));
+    NNZ_CK(cudaMemcpyAsync(v + h * n, m->vc + off, n * 2, cudaMemcpyDeviceToHost, m->st));
+  }
+  return sync_check(m);
+}
+
+int nnz_model_layer_step(nnz_model* m, uint32_t layer, float* residual, const uint32_t* positions,
+                         uint32_t batch) {
+  if (!m || !residual || !positions) return fail(NNZ_EINVAL, "null argument");
+  if (!m->finalized) return fail(NNZ_ESTATE, "model not finalized");
+  if (layer >= m->c.num_layers || batch == 0 || batch > m->c.max_batch)
+    return fail(NNZ_EINVAL, "layer/batch out of range");
+  for (uint32_t r = 0; r < batch; ++r)
+    if (positions[r] >= m->c.max_context_length) return fail(NNZ_EINVAL, "position out of range");
+  NNZ_CK(cudaSetDevice(m->device));
+  const size_t bytes = (size_t)batch * m->c.hidden_size * 4;
+  NNZ_CK(cudaMemcpyAsync(m->residual, residual, bytes, cudaMemcpyHostToDevice, m->st));
+  NNZ_CK(cudaMemcpyAsync(m->state->pos, positions, batch * 4, cudaMemcpyHostToDevice, m->st));
+  int rc = enqueue_layer(m, layer, batch, m->state->pos, nullptr, false, 0);
+  if (rc) return rc;
+  NNZ_CK(cudaMemcpyAsync(residual, m->residual, bytes, cudaMemcpyDeviceToHost, m->st));
+  return sync_check(m);
+}
+
+int nnz_bench_decode_graph(nnz_model* m, uint32_t batch, uint32_t iters, double* us_per_step) {
+  if (!m || !us_per_step || iters == 0) return fail(NNZ_EINVAL, "bad argument");
+  if (!m->finalized) return fail(NNZ_ESTATE, "model not finalized");
+  if (batch == 0 || batch > m->c.max_batch) return fail(NNZ_EINVAL, "batch");
+  NNZ_CK(cudaSetDevice(m->device));
+  int rc;
+  cudaGraphExec_t g;
+  if ((rc = get_graph(m, batch, false, &g))) return rc;
+  cudaEvent_t a, b;
+  NNZ_CK(cudaEventCreate(&a));
+  NNZ_CK(cudaEventCreate(&b));
+  if ((rc = set_advance(m, 0))) return rc;
+  NNZ_CK(cudaEventRecord(a, m->st));
+  for (uint32_t i = 0; i < iters; ++i) NNZ_CK(cudaGraphLaunch(g, m->st));
+  NNZ_CK(cudaEventRecord(b, m->st));
+  rc = sync_check(m);
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  if (rc) return rc;
+  *us_per_step = (double)ms * 1000.0 / iters;
+  return NNZ_OK;
+}
+
+// ---- per-kernel entry points ---------------------------------------------
+
+int nnz_dequant(int fmt, int scale_dtype, const void* packed, uint32_t M, uint32_t K, uint32_t gs,
+                uint32_t sub, uint32_t sub_index, float* out, void* stream) {
+  if (!packed || !out || (fmt != NNZ_Q1 && fmt != NNZ_Q4) || gs == 0 || gs % 32 || K % gs ||
+      sub == 0 || sub_index >= sub)
+    return fail(NNZ_EINVAL, "nnz_dequant: invalid arguments");
+  NNZ_CK(dequant_launch(fmt, fmt == NNZ_Q4 && scale_dtype == NNZ_SCALE_BF16, (const uint8_t*)packed,
+                        M, K, gs, sub, sub_index, out, (cudaStream_t)stream));
+  return NNZ_OK;
+}
+
+static int qmv_common(int fmt, int scale_dtype, int bf16_round, const void* packed, uint32_t M,
+                      uint32_t K, uint32_t gs, int pro, const void* x, uint32_t x_stride,
+                      const float* nw, float eps, uint32_t batch, void* out, uint32_t out_stride,
+                      int epi, float* logits, unsigned long long* am, void* stream) {
+  if (!packed || !x || (fmt != NNZ_Q1 && fmt != NNZ_Q4) || batch == 0 || M == 0 || gs == 0 ||
+      gs % 32 || gs > 256 || K % gs)
+    return fail(NNZ_EINVAL, "qmv: invalid arguments");
+  DevWs* w;
+  int rc = get_ws(&w);
+  if (rc) return rc;
+  if (qmv_ws_floats(M, K, gs, fmt, 1, batch, w->num_sms) > w->ws_floats ||
+      (size_t)((batch + 7) / 8) * num_tiles(M) > w->n_counters)
+    return fail(NNZ_EINVAL, "qmv: problem too large for the shared workspace");
+  QmvLaunch L{fmt, 1, pro, epi, fmt == NNZ_Q4 && scale_dtype == NNZ_SCALE_BF16, 0};
+  QmvArgs a{};
+  a.w = (const uint8_t*)packed; a.M = M; a.K = K; a.gs = gs;
+  a.x = x; a.x_stride = x_stride ? x_stride : K; a.norm_w = nw; a.eps = eps; a.batch = batch;
+  a.out = out; a.out_stride = out_stride ? out_stride : M; a.logits = logits; a.logits_stride = M;
+  a.argmax = am; a.ws = w->ws; a.counters = w->counters; a.err = w->err;
+  a.bf16_round = (fmt == NNZ_Q4 && bf16_round) ? 1u : 0u;
+  NNZ_CK(qmv_launch(L, a, w->num_sms, (cudaStream_t)stream));
+  return NNZ_OK;
+}
+
+static int out_epi(int kind) {
+  return kind == NNZ_OUT_F16 ? EPI_F16 : kind == NNZ_OUT_F32 ? EPI_F32 : kind == NNZ_OUT_F32_ADD ? EPI_RESADD : -1;
+}
+
+int nnz_qmv(int fmt, int scale_dtype, int bf16_round, const void* packed, uint32_t M, uint32_t K,
+            uint32_t gs, const void* x, uint32_t x_stride, uint32_t batch, void* out,
+            uint32_t out_stride, int out_kind, void* stream) {
+  const int epi = out_epi(out_kind);
+  if (epi < 0 || !out) return fail(NNZ_EINVAL, "nnz_qmv: bad out_kind/out");
+  return qmv_common(fmt, scale_dtype, bf16_round, packed, M, K, gs, PRO_F16, x, x_stride, nullptr,
+                    0.f, batch, out, out_stride, epi, nullptr, nullptr, stream);
+}
+
+int nnz_qmv_norm(int fmt, int scale_dtype, int bf16_round, const void* packed, uint32_t M,
+                 uint32_t K, uint32_t gs, const float* residual, const float* norm_w, float eps,
+                 uint32_t batch, void* out, uint32_t out_stride, int out_kind, void* stream) {
+  const int epi = out_epi(out_kind);
+  if (epi < 0 || epi == EPI_RESADD || !out || !norm_w)
+    return fail(NNZ_EINVAL, "nnz_qmv_norm: bad out_kind/out/norm_w");
+  return qmv_common(fmt, scale_dtype, bf16_round, packed, M, K, gs, PRO_NORM, residual, K, norm_w,
+                    eps > 0.f ? eps : 1e-6f, batch, out, out_stride, epi, nullptr, nullptr, stream);
+}
+
+namespace {
+__global__ void argmax_unpack_kernel(const unsigned long long* am, uint32_t* out, uint32_t n) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = argmax_index(am[i]);
+}
+}  // namespace
+
+int nnz_lm_head_argmax(int fmt, int scale_dtype, int bf16_round, const void* packed, uint32_t M,
+                       uint32_t K, uint32_t gs, const float* residual, const float* norm_w,
+                       float eps, uint32_t batch, float* logits, uint32_t* argmax_out,
+                       void* stream) {
+  if (!argmax_out || !norm_w || batch == 0) return fail(NNZ_EINVAL, "nnz_lm_head_argmax: bad arguments");
+  DevWs* w;
+  int rc = get_ws(&w);
+  if (rc) return rc;
+  if ((size_t)batch * 8 > w->scratch_bytes) return fail(NNZ_EINVAL, "batch too large");
+  auto* am = reinterpret_cast<unsigned long long*>(w->scratch);
+  NNZ_CK(cudaMemsetAsync(am, 0, (size_t)batch * 8, (cudaStream_t)stream));
+  rc = qmv_common(fmt, scale_dtype, bf16_round, packed, M, K, gs, PRO_NORM, residual, K, norm_w,
+                  eps > 0.f ? eps : 1e-6f, batch, nullptr, 0, EPI_LOGITS, logits, am, stream);
+  if (rc) return rc;
+  argmax_unpack_kernel<<<(batch + 127) / 128, 128, 0, (cudaStream_t)stream>>>(am, argmax_out, batch);
+  NNZ_CK(cudaGetLastError());
+  return NNZ_OK;
+}
+
+int nnz_mlp(int fmt, int scale_dtype, int bf16_round, const void* gate_up, const void* down,
+            uint32_t hidden, uint32_t inter, uint32_t gs, const void* x, uint32_t batch,
+            float* out, void* stream) {
+  if (!gate_up || !down || !x || !out || batch == 0 || (fmt != NNZ_Q1 && fmt != NNZ_Q4) || gs == 0 ||
+      gs % 32 || gs > 256 || hidden % gs || inter % gs)
+    return fail(NNZ_EINVAL, "nnz_mlp: invalid arguments");
+  DevWs* w;
+  int rc = get_ws(&w);
+  if (rc) return rc;
+  if ((size_t)batch * inter * 2 > w->scratch_bytes) return fail(NNZ_EINVAL, "nnz_mlp: batch too large");
+  if (qmv_ws_floats(inter, hidden, gs, fmt, 2, batch, w->num_sms) > w->ws_floats ||
+      qmv_ws_floats(hidden, inter, gs, fmt, 1, batch, w->num_sms) > w->ws_floats)
+    return fail(NNZ_EINVAL, "nnz_mlp: problem too large for the shared workspace");
+  const int bf16s = fmt == NNZ_Q4 && scale_dtype == NNZ_SCALE_BF16;
+  const uint32_t br = (fmt == NNZ_Q4 && bf16_round) ? 1u : 0u;
+  __half* hbuf = reinterpret_cast<__half*>(w->scratch);
+  QmvArgs a{};
+  a.w = (const uint8_t*)gate_up; a.M = inter; a.K = hidden; a.gs = gs;
+  a.x = x; a.x_stride = hidden; a.batch = batch; a.out = hbuf; a.out_stride = inter;
+  a.ws = w->ws; a.counters = w->counters; a.err = w->err; a.bf16_round = br;
+  NNZ_CK(qmv_launch(QmvLaunch{fmt, 2, PRO_F16, EPI_SILU, bf16s, 0}, a, w->num_sms, (cudaStream_t)stream));
+  QmvArgs d{};
+  d.w = (const uint8_t*)down; d.M = hidden; d.K = inter; d.gs = gs;
+  d.x = hbuf; d.x_stride = inter; d.batch = batch; d.out = out; d.out_stride = hidden;
+  d.ws = w->ws; d.counters = w->counters; d.err = w->err; d.bf16_round = br;
+  NNZ_CK(qmv_launch(QmvLaunch{fmt, 1, PRO_F16, EPI_F32, bf16s, 0}, d, w->num_sms, (cudaStream_t)stream));
+  return NNZ_OK;
+}
+
+int nnz_attn_decode(const void* qkv, const float* q_norm, const float* k_norm, void* k_cache,
+                    void* v_cache, uint32_t max_ctx, const int32_t* positions, uint32_t rows,
+                    uint32_t n_q, uint32_t n_kv, uint32_t head_dim, float eps, float theta,
+                    int rope_style, uint32_t splits, void* out, void* stream) {
+  if (!qkv || !q_norm || !k_norm || !k_cache || !v_cache || !positions || !out || rows == 0)
+    return fail(NNZ_EINVAL, "nnz_attn_decode: null argument");
+  DevWs* w;
+  int rc = get_ws(&w);
+  if (rc) return rc;
+  AttnArgs a{};
+  a.qkv = (const __half*)qkv; a.qkv_stride = (n_q + 2 * n_kv) * head_dim;
+  a.q_norm = q_norm; a.k_norm = k_norm; a.kc = (__half*)k_cache; a.vc = (__half*)v_cache;
+  a.max_ctx = max_ctx; a.pos = positions; a.slot = nullptr; a.rows = rows; a.n_q = n_q; a.n_kv = n_kv;
+  a.eps = eps > 0.f ? eps : 1e-6f; a.theta = theta; a.rope_style = rope_style; a.write_kv = 1;
+  a.splits = splits ? splits : std::min(16u, std::max(1u, (uint32_t)w->num_sms / std::max(1u, n_kv * rows)));
+  a.out = (__half*)out; a.out_stride = n_q * head_dim; a.ws = w->ws; a.counters = w->counters; a.err = w->err;
+  if (attn_ws_floats(rows, n_q, n_kv, a.splits, (int)head_dim) > w->ws_floats ||
+      (size_t)rows * n_kv > w->n_counters)
+    return fail(NNZ_EINVAL, "nnz_attn_decode: problem too large for the shared workspace");
+  NNZ_CK(attn_decode_launch(a, (int)head_dim, 0, (cudaStream_t)stream));
+  return NNZ_OK;
+}
+
+}  // extern "C"
