@@ -1,0 +1,340 @@
+#!/usr/bin/env python
+"""Benchmark: Bonsai-1.7B-shaped 1-bit (Q1 g128) greedy decode at batch 1.
+
+Workload: random-init 28-layer Qwen3-1.7B architecture
+with packed 1-bit weights and a tied 1-bit embedding, a 512-token prompt
+(ids uniform from seed 0, tokenizer bypassed) prefilled, then 256 greedy
+tokens.  One "step" = one generate() call = prefill 512 + decode 256.
+
+Prints ONE JSON line (rank 0).  ``value`` is decode tok/s measured on the
+device (CUDA events around every graph replay, max over ranks); ``e2e`` is
+the same job timed on the host around the public generate() call (prompt
+host->device, tokens device->host, prefill included).  Multi-GPU runs are
+independent replicas (batch-1 decode does not shard), so ``value`` sums the
+ranks' tokens over the slowest rank's time.
+
+``--impl reference`` times the CPU oracle's token-at-a-time decode on a
+bounded sample (the reference engine itself needs Apple Metal + Zig).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PROMPT, GEN = 512, 256
+METRIC = "decode_tok_per_sec"
+UNIT = "tok/s"
+
+
+def rank_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid, self.proc, self.lines = uuid, None, []
+
+    def start(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        if self.uuid:
+            cmd[1:1] = ["-i", self.uuid]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        load = [s for s in sm if mx and s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def algorithmic_bytes_per_token(d, ctx):
+    """Weights streamed per decode token (1 bit + fp16 scale per group) plus
+    the K/V history read at context length ctx."""
+    qd, kvd = d.n_q * d.head_dim, d.n_kv * d.head_dim
+    layer_params = d.hidden * (qd + 2 * kvd) + qd * d.hidden + 3 * d.hidden * d.inter
+    per_param = 1 / 8 + 2 / d.gs
+    weights = d.layers * layer_params * per_param + d.vocab * d.hidden * per_param
+    kv = d.layers * 2 * d.n_kv * ctx * d.head_dim * 2
+    return weights + kv
+
+
+def launches_per_step(d, prompt, gen, chunk=64):
+    chunks = -(-prompt // chunk)
+    return chunks * (1 + d.layers * 6) + 1 + gen * (1 + d.layers * 5 + 1)
+
+
+def oracle_cfg(d):
+    from oracle import qwen3_ref as R
+    return R.Cfg(vocab=d.vocab, hidden=d.hidden, inter=d.inter, layers=d.layers, n_q=d.n_q,
+                 n_kv=d.n_kv, head_dim=d.head_dim, gs=d.gs, quant=d.quant)
+
+
+def cpu_decode_sample(d, W, n_prompt=24, n_decode=3):
+    """Token-at-a-time CPU decode with the oracle (all host cores via BLAS)."""
+    from oracle import qwen3_ref as R
+    cfg = oracle_cfg(d)
+    prompt = np.random.default_rng(0).integers(0, d.vocab, n_prompt)
+    kv = []
+    t0 = time.perf_counter()
+    for p, tok in enumerate(prompt):
+        lg = R.decode_one(cfg, W, kv, int(tok), p)
+    t1 = time.perf_counter()
+    tok = int(np.argmax(lg))
+    times = []
+    for i in range(n_decode):
+        a = time.perf_counter()
+        lg = R.decode_one(cfg, W, kv, tok, n_prompt + i)
+        tok = int(np.argmax(lg))
+        times.append(time.perf_counter() - a)
+    return {"decode_tok_per_sec": n_decode / sum(times), "prefill_tok_per_sec": n_prompt / (t1 - t0),
+            "decode_s": sum(times), "prefill_s": t1 - t0, "n_prompt": n_prompt, "n_decode": n_decode}
+
+
+def run_reference(args):
+    rank, world, _ = rank_env()
+    if rank != 0:
+        return
+    from nnzap_b200 import synth
+    from oracle import qwen3_ref as R
+    d = synth.BONSAI_1_7B_Q1
+    W = synth.make_model(d, seed=0)
+    cfg = oracle_cfg(d)
+    n_prompt = 8
+    kv = []
+    for p, tok in enumerate(np.random.default_rng(0).integers(0, d.vocab, n_prompt)):
+        lg = R.decode_one(cfg, W, kv, int(tok), p)
+    tok, pos = int(np.argmax(lg)), n_prompt
+    for _ in range(args.warmup):
+        lg = R.decode_one(cfg, W, kv, tok, pos)
+        tok, pos = int(np.argmax(lg)), pos + 1
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        lg = R.decode_one(cfg, W, kv, tok, pos)
+        tok, pos = int(np.argmax(lg)), pos + 1
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    cores = os.cpu_count()
+    sample = (f"oracle token-at-a-time decode of {args.steps} tokens (after an {n_prompt}-token "
+              f"prompt and {args.warmup} warm-up tokens) on the full config-3 model, numpy/BLAS")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1000 / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "config 3: Bonsai-1.7B-shaped Q1 g128, b=1 greedy decode (bounded CPU sample)",
+                   "model": "Qwen3-1.7B arch, random-init 1-bit", "global_batch": 1,
+                   "seq_len": PROMPT + GEN, "parallelism": "none (CPU)"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference engine needs Apple Metal + Zig (absent); this arm times the CPU "
+                "restatement of its decode (oracle/qwen3_ref.py)"}), flush=True)
+
+
+def qmv_config0(torch, iters=200):
+    """Standalone BASELINE config 0 QMV (Q4 6144x2048 g64, fp16 in/out)
+    rotating through weight copies larger than L2."""
+    from nnzap_b200 import synth
+    from nnzap_b200._capi import check, lib, ptr
+    M, K, gs = 6144, 2048, 64
+    L = lib()
+    t = synth.rand_q4(np.random.default_rng(0), M, K, gs)
+    nb = L.nnz_packed_bytes(1, M, K, gs, 1)
+    packed = np.zeros(nb, dtype=np.uint8)
+    check(L.nnz_pack_weights(1, ptr(t["weight"]), ptr(t["scales"]), ptr(t["biases"]), M, K, gs, 1, 0,
+                             ptr(packed)))
+    copies = 48                                     # 48 x 7.1 MB = 340 MB > L2
+    dev = torch.from_numpy(packed).cuda().repeat(copies)
+    x = torch.randn(K, device="cuda").half()
+    y = torch.empty(M, device="cuda", dtype=torch.float16)
+    stream = torch.cuda.current_stream().cuda_stream
+    for i in range(copies):
+        check(L.nnz_qmv(1, 0, 0, dev.data_ptr() + i * nb, M, K, gs, ptr(x), K, 1, ptr(y), M, 0, stream))
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(iters):
+        c = i % copies
+        check(L.nnz_qmv(1, 0, 0, dev.data_ptr() + c * nb, M, K, gs, ptr(x), K, 1, ptr(y), M, 0, stream))
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1000 / iters
+    alg = M * K / 2 + 2 * 2 * (M * K // gs) + K * 2 + M * 2
+    return us, alg / (us * 1e-6) / 1e9, alg
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    rank, world, local = rank_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    from nnzap_b200 import GenerateOpts, Model, config_from_dims, generate, synth
+
+    d = synth.BONSAI_1_7B_Q1
+    t0 = time.perf_counter()
+    W = synth.make_model(d, seed=0)
+    cfg = config_from_dims(d, max_context_length=PROMPT + GEN + 8, max_batch=1)
+    model = Model(cfg, device=local)
+    model.load_weights(synth.iter_named_tensors(W))
+    load_ms = (time.perf_counter() - t0) * 1000
+    prompt = np.random.default_rng(0).integers(0, d.vocab, PROMPT).tolist()
+    opts = GenerateOpts(prompt_ids=prompt, max_new=GEN)
+
+    for _ in range(args.warmup):
+        generate(model, opts)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+            torch.cuda.synchronize()
+
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(local).uuid)
+        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid)
+    clocks.start()
+    barrier()
+    per_token, prefill_ns, decode_ns, walls, tokens = [], 0, 0, [], None
+    for _ in range(args.steps):
+        w0 = time.perf_counter()
+        res = generate(model, opts)          # host prompt in, host tokens out
+        walls.append(time.perf_counter() - w0)
+        prefill_ns += res.prefill_ns
+        decode_ns += res.decode_ns
+        per_token += res.per_token_ns
+        tokens = res.tokens
+    barrier()
+    clk = clocks.stop()
+
+    stats = torch.tensor([decode_ns / 1e9, prefill_ns / 1e9, sum(walls)], dtype=torch.float64,
+                         device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(stats, op=torch.distributed.ReduceOp.MAX)
+    dec_s, pre_s, wall_s = stats.tolist()
+    value = GEN * args.steps * world / dec_s
+    prefill_tps = PROMPT * args.steps * world / pre_s
+    pt = sorted(per_token)
+    p50 = pt[len(pt) // 2] / 1000
+    p99 = pt[(len(pt) * 99) // 100] / 1000
+
+    if rank != 0:
+        if world > 1:
+            torch.distributed.barrier()
+        return
+    hbm, peak_kind = measured_peaks()
+    mean_ctx = PROMPT + (GEN + 1) / 2
+    bytes_tok = algorithmic_bytes_per_token(d, mean_ctx)
+    us_tok = dec_s / (GEN * args.steps) * 1e6
+    achieved = bytes_tok / (us_tok * 1e-6) / 1e9
+    q0_us, q0_gbs, q0_bytes = qmv_config0(torch)
+    cpu = None
+    if not args.no_cpu_baseline:
+        c = cpu_decode_sample(d, W)
+        cpu = {"value": c["decode_tok_per_sec"], "unit": UNIT, "cores": os.cpu_count(),
+               "kind": "port",
+               "sample": (f"oracle token-at-a-time decode: {c['n_prompt']}-token prompt "
+                          f"({c['prefill_s']:.1f} s) then {c['n_decode']} greedy tokens "
+                          f"({c['decode_s']:.1f} s), full config-3 model, numpy/BLAS on "
+                          f"{os.cpu_count()} host threads")}
+    out = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": wall_s / args.steps * 1000,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "q1 weights, int8 tensor-core MMA, f32 accumulate", "data": "synthetic",
+        "config": {"workload": "config 3: Bonsai-1.7B-shaped 1-bit (Q1 g128) random-init, "
+                               "512-token prompt prefill + 256 greedy tokens, batch 1",
+                   "model": "Qwen3-1.7B architecture (28 layers, vocab 151936)", "global_batch": world,
+                   "seq_len": PROMPT + GEN, "parallelism": f"replicas x{world}",
+                   "l2": "inputs larger than L2: 242 MB of weights streamed per token"},
+        "prefill_tok_per_sec": prefill_tps, "decode_p50_us": p50, "decode_p99_us": p99,
+        "load_ms": load_ms, "prompt_tokens": PROMPT, "measured_tokens": GEN * args.steps,
+        "roofline": {"bound": "hbm", "kernel": "decode step (one CUDA graph replay per token)",
+                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": peak_kind, "traffic": None,
+                     "algorithmic_bytes_per_token": bytes_tok},
+        "qmv_config0": {"us": q0_us, "achieved_gbs": q0_gbs, "frac": q0_gbs / hbm,
+                        "algorithmic_bytes": q0_bytes},
+        "cpu_baseline": cpu,
+        "e2e": {"value": GEN * args.steps * world / wall_s, "unit": "tok/s (generate() wall time, "
+                "512-token prefill included)", "h2d_bytes_per_step": PROMPT * 4,
+                "d2h_bytes_per_step": GEN * 4},
+        "gpu_launches": launches_per_step(d, PROMPT, GEN) * args.steps,
+        "clocks": clk,
+        "sample_tokens": tokens[:8],
+    }
+    print(json.dumps(out), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+
+
+if __name__ == "__main__":
+    main()

@@ -357,3 +357,35 @@ def mlp_block(cfg: Cfg, gate: dict, up: dict, down: dict, x: np.ndarray) -> np.n
     u = qmv(cfg, up, cfg.inter, cfg.hidden, x)
     h = _to_f16(cfg, silu_mul(g, u))
     return qmv(cfg, down, cfg.hidden, cfg.inter, h)
+
+
+def decode_one(cfg: Cfg, W: dict, kv: list, token: int, pos: int) -> np.ndarray:
+    """One token-at-a-time decode step (transformer.zig:4072-4123) with an
+    explicit KV cache: ``kv[layer] = (K [n_kv, L, hd] f16, V [...])`` grown in
+    place.  Returns f32 logits [vocab].  Used as the timed CPU baseline."""
+    hd, nq, nkv = cfg.head_dim, cfg.n_q, cfg.n_kv
+    P = np.array([pos])
+    res = embed(cfg, W["embed"], np.array([token]))
+    for li in range(cfg.layers):
+        L = W["layers"][li]
+        xn = _to_f16(cfg, rmsnorm(res, L["attn_norm"], cfg.eps))
+        q = _to_f16(cfg, qmv(cfg, L["q_proj"], nq * hd, cfg.hidden, xn)).reshape(1, nq, hd)
+        k = _to_f16(cfg, qmv(cfg, L["k_proj"], nkv * hd, cfg.hidden, xn)).reshape(1, nkv, hd)
+        v = _to_f16(cfg, qmv(cfg, L["v_proj"], nkv * hd, cfg.hidden, xn)).reshape(nkv, hd)
+        q = rope(rmsnorm(q, L["q_norm"], cfg.eps), P, cfg.rope_theta, cfg.rope_style)[0]
+        k = rope(rmsnorm(k, L["k_norm"], cfg.eps), P, cfg.rope_theta, cfg.rope_style)[0]
+        if len(kv) <= li:
+            kv.append((np.zeros((nkv, 0, hd), F16), np.zeros((nkv, 0, hd), F16)))
+        K_, V_ = kv[li]
+        K_ = np.concatenate([K_[:, :pos], k.astype(F16)[:, None]], axis=1)
+        V_ = np.concatenate([V_[:, :pos], v.astype(F16)[:, None]], axis=1)
+        kv[li] = (K_, V_)
+        att = attention_decode(q, K_, V_, nkv).astype(F16).astype(F32).reshape(1, -1)
+        res = res + _round_out(cfg, qmv(cfg, L["o_proj"], cfg.hidden, nq * hd, att))
+        xn = _to_f16(cfg, rmsnorm(res, L["ffn_norm"], cfg.eps))
+        g = qmv(cfg, L["gate_proj"], cfg.inter, cfg.hidden, xn)
+        u = qmv(cfg, L["up_proj"], cfg.inter, cfg.hidden, xn)
+        res = res + _round_out(cfg, qmv(cfg, L["down_proj"], cfg.hidden, cfg.inter,
+                                        _to_f16(cfg, silu_mul(g, u))))
+    xn = _to_f16(cfg, rmsnorm(res, W["final_norm"], cfg.eps))
+    return _round_out(cfg, qmv(cfg, W["lm_head"], cfg.vocab, cfg.hidden, xn))[0]

@@ -87,7 +87,8 @@ def test_qmv_residual_add(cuda, built_lib):
     x = np.random.default_rng(2).standard_normal((2, K)).astype(np.float16)
     r0 = np.random.default_rng(3).standard_normal((2, M)).astype(np.float32)
     res = to_dev(torch, r0)
-    check(lib().nnz_qmv(fmt, 0, 0, ptr(w), M, K, gs, ptr(to_dev(torch, x)), K, 2, ptr(res), M, 2, None))
+    xd = to_dev(torch, x)
+    check(lib().nnz_qmv(fmt, 0, 0, ptr(w), M, K, gs, ptr(xd), K, 2, ptr(res), M, 2, None))
     torch.cuda.synchronize()
     want = r0 + R.qmv(cfg_for(fmt, gs, K), t, M, K, x.astype(np.float32))
     close(res.cpu().numpy(), want, 1e-3, 1e-4, "resadd")
@@ -105,8 +106,9 @@ def test_qmv_norm_prologue(cuda, built_lib, fmt, bf16):
     res = (rng.standard_normal((3, K)) * 3).astype(np.float32)
     nw = (1 + 0.1 * rng.standard_normal(K)).astype(np.float32)
     out = torch.empty((3, M), dtype=torch.float16, device="cuda")
-    check(lib().nnz_qmv_norm(fmt, int(bf16), int(bf16), ptr(w), M, K, gs, ptr(to_dev(torch, res)),
-                             ptr(to_dev(torch, nw)), 1e-6, 3, ptr(out), M, 0, None))
+    res_d, nw_d = to_dev(torch, res), to_dev(torch, nw)   # keep alive until the sync
+    check(lib().nnz_qmv_norm(fmt, int(bf16), int(bf16), ptr(w), M, K, gs, ptr(res_d),
+                             ptr(nw_d), 1e-6, 3, ptr(out), M, 0, None))
     torch.cuda.synchronize()
     cfg = cfg_for(fmt, gs, K, sd, bf16)
     xn = R._to_f16(cfg, R.rmsnorm(res, nw))
@@ -126,8 +128,9 @@ def test_lm_head_argmax(cuda, built_lib):
     nw = (1 + 0.1 * rng.standard_normal(K)).astype(np.float32)
     logits = torch.empty((2, V), dtype=torch.float32, device="cuda")
     am = torch.zeros(2, dtype=torch.int32, device="cuda")
-    check(lib().nnz_lm_head_argmax(fmt, 0, 0, ptr(w), V, K, gs, ptr(to_dev(torch, res)),
-                                   ptr(to_dev(torch, nw)), 1e-6, 2, ptr(logits), ptr(am), None))
+    res_d, nw_d = to_dev(torch, res), to_dev(torch, nw)
+    check(lib().nnz_lm_head_argmax(fmt, 0, 0, ptr(w), V, K, gs, ptr(res_d), ptr(nw_d), 1e-6, 2,
+                                   ptr(logits), ptr(am), None))
     torch.cuda.synchronize()
     cfg = cfg_for(fmt, gs, K)
     xn = R._to_f16(cfg, R.rmsnorm(res, nw))
@@ -158,8 +161,8 @@ def test_mlp_block_config1(cuda, built_lib, fmt, batch):
     dn = pack(fmt, d, H, I, gs)
     x = rng.standard_normal((batch, H)).astype(np.float16)
     out = torch.empty((batch, H), dtype=torch.float32, device="cuda")
-    check(lib().nnz_mlp(fmt, 0, 0, ptr(to_dev(torch, gu)), ptr(to_dev(torch, dn)), H, I, gs,
-                        ptr(to_dev(torch, x)), batch, ptr(out), None))
+    gu_d, dn_d, x_d = to_dev(torch, gu), to_dev(torch, dn), to_dev(torch, x)
+    check(lib().nnz_mlp(fmt, 0, 0, ptr(gu_d), ptr(dn_d), H, I, gs, ptr(x_d), batch, ptr(out), None))
     torch.cuda.synchronize()
     cfg = R.Cfg(vocab=8, hidden=H, inter=I, layers=1, n_q=16, n_kv=8, head_dim=128, gs=gs,
                 quant="q1" if fmt == 0 else "q4")
@@ -202,8 +205,9 @@ def test_attention_decode(cuda, built_lib, hd, n_q, n_kv, pos, splits, style):
     positions = np.array([pos, max(0, pos // 2)], dtype=np.int32)
     kd, vd = to_dev(torch, kc), to_dev(torch, vc)
     out = torch.empty((rows, n_q * hd), dtype=torch.float16, device="cuda")
-    check(lib().nnz_attn_decode(ptr(to_dev(torch, qkv)), ptr(to_dev(torch, qn)), ptr(to_dev(torch, kn)),
-                                ptr(kd), ptr(vd), max_ctx, ptr(to_dev(torch, positions)), rows, n_q,
+    keep = [to_dev(torch, a) for a in (qkv, qn, kn, positions)]   # alive until the sync
+    check(lib().nnz_attn_decode(ptr(keep[0]), ptr(keep[1]), ptr(keep[2]),
+                                ptr(kd), ptr(vd), max_ctx, ptr(keep[3]), rows, n_q,
                                 n_kv, hd, 1e-6, theta, 0 if style == "pairwise" else 1, splits,
                                 ptr(out), None))
     torch.cuda.synchronize()
