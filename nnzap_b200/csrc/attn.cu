@@ -258,16 +258,29 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnArgs a) {
   __syncthreads();
   if (!flag[0]) return;
   __threadfence();
+  // merge the splits' (m, l, o) with an online rescale; 8 splits' loads
+  // are issued before any is used
   for (int h = hs; h < G; h += NHS) {
-    float M = -INFINITY;
-    for (uint32_t s = 0; s < a.splits; ++s) M = fmaxf(M, __ldcg(&wsp[((size_t)s * G + h) * rec]));
-    float Lsum = 0.f, o = 0.f;
-    for (uint32_t s = 0; s < a.splits; ++s) {
-      const float ms = __ldcg(&wsp[((size_t)s * G + h) * rec]);
-      if (ms == -INFINITY) continue;
-      const float w = expf(ms - M);
-      Lsum = fmaf(__ldcg(&wsp[((size_t)s * G + h) * rec + 1]), w, Lsum);
-      o = fmaf(__ldcg(&wsp[((size_t)s * G + h) * rec + 2 + d]), w, o);
+    float M = -INFINITY, Lsum = 0.f, o = 0.f;
+    for (uint32_t s0 = 0; s0 < a.splits; s0 += 8) {
+      float mv[8], lv[8], ov[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const bool ok = s0 + j < a.splits;
+        const float* r = wsp + ((size_t)(s0 + j) * G + h) * rec;
+        mv[j] = ok ? __ldcg(r) : -INFINITY;
+        lv[j] = ok ? __ldcg(r + 1) : 0.f;
+        ov[j] = ok ? __ldcg(r + 2 + d) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (mv[j] == -INFINITY) continue;
+        const float nm = fmaxf(M, mv[j]);
+        const float a0 = (M == -INFINITY) ? 0.f : expf(M - nm), a1 = expf(mv[j] - nm);
+        Lsum = Lsum * a0 + lv[j] * a1;
+        o = o * a0 + ov[j] * a1;
+        M = nm;
+      }
     }
     orow[h * HD + d] = __float2half_rn(o / Lsum);
   }

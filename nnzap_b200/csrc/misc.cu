@@ -18,14 +18,21 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedArgs a) {
     uint32_t tok;
     if (a.tokens) {
       tok = a.tokens[r];
-    } else if (a.st->advance) {
-      tok = argmax_index(a.st->argmax[r]);
-      const int p = a.st->pos[r] + 1;
-      a.st->pos[r] = p;
-      a.st->token[r] = tok;
-      if (a.seq && p >= 0 && (uint32_t)p < a.seq_len) a.seq[(size_t)r * a.seq_len + p] = tok;
     } else {
-      tok = a.st->token[r];
+      // issue the three state reads together
+      const int adv = a.st->advance;
+      const unsigned long long am = a.st->argmax[r];
+      const int p0 = a.st->pos[r];
+      const uint32_t t0 = a.st->token[r];
+      if (adv) {
+        tok = argmax_index(am);
+        const int p = p0 + 1;
+        a.st->pos[r] = p;
+        a.st->token[r] = tok;
+        if (a.seq && p >= 0 && (uint32_t)p < a.seq_len) a.seq[(size_t)r * a.seq_len + p] = tok;
+      } else {
+        tok = t0;
+      }
     }
     if (a.st) a.st->argmax[r] = 0ull;
     if (tok >= a.vocab) {
@@ -37,22 +44,29 @@ __global__ void __launch_bounds__(256) embed_kernel(EmbedArgs a) {
   __syncthreads();
   const uint32_t tok = tok_s;
   float* out = a.residual + (size_t)r * a.H;
-  for (uint32_t d = threadIdx.x; d < a.H; d += blockDim.x) {
-    const uint64_t f = (uint64_t)tok * a.H + d;
-    float v;
+  // one thread per 8 consecutive elements: one bits byte / one nibble word
+  // and one scale (gs >= 32) each, all loads independent
+  for (uint32_t d8 = threadIdx.x; d8 < a.H / 8; d8 += blockDim.x) {
+    const uint64_t f = (uint64_t)tok * a.H + 8 * d8;
+    float v[8];
     if constexpr (FMT == FMT_Q1) {
-      const uint32_t bit = (a.wbytes[f >> 3] >> (f & 7)) & 1u;
+      const uint32_t bits = a.wbytes[f >> 3];
       const float s = __half2float(__ushort_as_half(a.scales[f / a.gs]));
-      v = bit ? s : -s;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = ((bits >> i) & 1u) ? s : -s;
     } else {
       const uint32_t word = reinterpret_cast<const uint32_t*>(a.wbytes)[f >> 3];
-      const uint32_t q = (word >> (4 * (f & 7))) & 0xFu;
       const float s = u16_to_f32<BF16S>(a.scales[f / a.gs]);
       const float b = u16_to_f32<BF16S>(a.biases[f / a.gs]);
-      v = __fadd_rn(__fmul_rn(s, (float)q), b);
-      if (a.bf16_round) v = bf16_trunc(v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        v[i] = __fadd_rn(__fmul_rn(s, (float)((word >> (4 * i)) & 0xFu)), b);
+        if (a.bf16_round) v[i] = bf16_trunc(v[i]);
+      }
     }
-    out[d] = v;
+    float4* o4 = reinterpret_cast<float4*>(out + 8 * d8);
+    o4[0] = make_float4(v[0], v[1], v[2], v[3]);
+    o4[1] = make_float4(v[4], v[5], v[6], v[7]);
   }
 }
 

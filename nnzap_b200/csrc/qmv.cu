@@ -7,7 +7,7 @@ namespace nnz {
 
 namespace {
 
-constexpr uint32_t kXfCapBytes = 64 * 1024;   // B-fragment smem cap per CTA
+constexpr uint32_t kXfCapBytes = 96 * 1024;   // x staging + B-fragment smem cap per CTA
 
 // When set, launch_t only raises the instance's dynamic shared memory limit
 // (done once per device, outside any stream capture).
@@ -104,7 +104,8 @@ uint32_t qmv_pick_ksplit(uint32_t M, uint32_t K, uint32_t gs, int fmt, int sub, 
   if (max_ks < 1) max_ks = 1;
   if (ks > max_ks) ks = max_ks;
   // the CTA's x fragments must fit the smem cap
-  while (ks < groups && ((groups + ks - 1) / ks) * gs * 8 * nt > kXfCapBytes) ++ks;
+  const uint32_t rows = batch < (uint32_t)kBatchChunk ? batch : kBatchChunk;
+  while (ks < groups && ((groups + ks - 1) / ks) * gs * (8 * nt + 2 * rows) > kXfCapBytes) ++ks;
   (void)fmt; (void)sub;
   return ks;
 }
@@ -126,10 +127,20 @@ cudaError_t qmv_launch(const QmvLaunch& L, QmvArgs a, int num_sms, cudaStream_t 
   if (a.ksplit > a.groups) return cudaErrorInvalidValue;
   const int nt = a.batch > 4 ? 2 : 1;
   const uint32_t ng_max = (a.groups + a.ksplit - 1) / a.ksplit;
-  const QmvSmem S = qmv_smem_layout(L.fmt, nt, L.sub, a.gs, ng_max);
+  const QmvSmem S = qmv_smem_layout(L.fmt, nt, L.sub, a.gs, ng_max, a.batch < (uint32_t)kBatchChunk ? a.batch : kBatchChunk);
+  // vector loads of x: 16-byte aligned rows
+  const uintptr_t xa = reinterpret_cast<uintptr_t>(a.x);
+  if (xa % 16 || (L.pro == PRO_NORM ? a.x_stride % 4 : a.x_stride % 8) ||
+      (L.pro == PRO_NORM && reinterpret_cast<uintptr_t>(a.norm_w) % 16))
+    return cudaErrorMisalignedAddress;
   if (S.total > 227 * 1024) return cudaErrorInvalidValue;
   const uint32_t ych = (a.batch + kBatchChunk - 1) / kBatchChunk;
-  dim3 grid(a.tiles * a.ksplit, ych);
+  // persistent CTAs: about two resident CTAs per SM over all splits/chunks
+  if (a.P == 0) {
+    const uint32_t want = (2u * (uint32_t)num_sms + a.ksplit * ych - 1) / (a.ksplit * ych);
+    a.P = want < a.tiles ? (want ? want : 1) : a.tiles;
+  }
+  dim3 grid(a.P * a.ksplit, ych);
   if (L.fmt == FMT_Q1) {
     return nt == 1 ? pick_variant<FMT_Q1, 1>(L, a, grid, S.total, st)
                    : pick_variant<FMT_Q1, 2>(L, a, grid, S.total, st);

@@ -52,6 +52,7 @@ struct QmvArgs {
   uint32_t M, K, gs;         // rows (per sub-matrix), cols, group size
   uint32_t tiles, groups;    // ceil(M/128), K/gs
   uint32_t ksplit;           // CTAs along K per tile
+  uint32_t P;                // persistent CTAs per K split (each loops over tiles)
   const void* x;             // fp16 [batch][x_stride] or f32 residual (PRO_NORM)
   uint32_t x_stride;
   const float* norm_w;       // RMSNorm weight [K] (PRO_NORM)
@@ -69,26 +70,28 @@ struct QmvArgs {
 };
 
 struct QmvSmem {
-  uint32_t nslot, bars, ring, red, xf, gsx, gsum, gsq, rms, flag, total;
+  uint32_t nslot, bars, ring, red, xf, xs, gsx, gsum, gsq, rms, flag, total;
 };
 
-// The ring (weight segments) and the reduction buffer alias: the reduction
-// starts only after every warp has consumed every segment it waited for.
+// Shared-memory layout.  The ring keeps streaming the next tile's segments
+// while the current tile is reduced, so the reduction buffer is separate.
 __host__ __device__ inline QmvSmem qmv_smem_layout(int fmt, int nt, int sub, uint32_t gs,
-                                                   uint32_t ngroups_cta) {
+                                                   uint32_t ngroups_cta, uint32_t rows) {
   QmvSmem s;
   uint32_t per_warp = (ngroups_cta + kQmvWarps - 1) / kQmvWarps;
   s.nslot = per_warp < (uint32_t)kQmvRing ? (per_warp ? per_warp : 1) : kQmvRing;
+  // cap the ring at 96 KB so the staging buffers always fit
+  while (s.nslot > 1 && kQmvWarps * s.nslot * sub * seg_bytes(fmt, gs) > 96u * 1024u) --s.nslot;
   uint32_t o = 0;
   s.bars = o; o += kQmvWarps * kQmvRing * 8;
   o = (o + 127) & ~127u;
   s.ring = o;
+  o += kQmvWarps * s.nslot * sub * seg_bytes(fmt, gs);
   s.red = o;
-  const uint32_t ring_b = kQmvWarps * s.nslot * sub * seg_bytes(fmt, gs);
-  const uint32_t red_b = kQmvWarps * kTileRows * sub * kBatchChunk * 4;
-  o += ring_b > red_b ? ring_b : red_b;
+  o += kQmvWarps * kTileRows * sub * kBatchChunk * 4;
   o = (o + 127) & ~127u;
   s.xf = o; o += ngroups_cta * (gs / kChunk) * nt * 256;
+  s.xs = o; o += ((ngroups_cta * gs * rows * 2) + 15) & ~15u;
   s.gsx = o; o += ngroups_cta * kBatchChunk * 4;
   s.gsum = o; o += ngroups_cta * kBatchChunk * 4;
   s.gsq = o; o += ngroups_cta * kBatchChunk * 4;
@@ -103,15 +106,16 @@ __global__ void __launch_bounds__(kQmvThreads) qmv_kernel(QmvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t cpg = a.gs / kChunk;
   const uint32_t seg = seg_bytes(FMT, a.gs);
-  const uint32_t tile = blockIdx.x % a.tiles;
-  const uint32_t split = blockIdx.x / a.tiles;
+  const uint32_t split = blockIdx.x % a.ksplit;
+  const uint32_t pcta = blockIdx.x / a.ksplit;          // tiles pcta, pcta + P, ...
+  const uint32_t ntc = pcta < a.tiles ? (a.tiles - pcta + a.P - 1) / a.P : 0;
   const uint32_t ychunk = blockIdx.y;
   const uint32_t b0 = ychunk * kBatchChunk;
   const uint32_t bc = min(a.batch - b0, (uint32_t)kBatchChunk);
   const uint32_t G0 = (uint32_t)((uint64_t)a.groups * split / a.ksplit);
   const uint32_t G1 = (uint32_t)((uint64_t)a.groups * (split + 1) / a.ksplit);
   const uint32_t ng = G1 - G0;
-  const QmvSmem L = qmv_smem_layout(FMT, NT, SUB, a.gs, ng);
+  const QmvSmem L = qmv_smem_layout(FMT, NT, SUB, a.gs, ng, min(a.batch, (uint32_t)kBatchChunk));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint8_t* ring = smem + L.ring;
   uint8_t* xf = smem + L.xf;
@@ -126,7 +130,13 @@ __global__ void __launch_bounds__(kQmvThreads) qmv_kernel(QmvArgs a) {
   const uint32_t cnt_w = (ng > (uint32_t)warp) ? (ng - warp + kQmvWarps - 1) / kQmvWarps : 0;
   const uint32_t slot_bytes = SUB * seg;
   const uint32_t nslot = L.nslot;
-  const uint8_t* wtile = a.w + (size_t)tile * a.groups * SUB * seg;
+  // per-warp item k -> (tile pcta + (k / cnt_w) * P, group G0 + warp + (k % cnt_w) * 4)
+  auto item_src = [&](uint32_t k) -> const uint8_t* {
+    const uint32_t tl = pcta + (k / cnt_w) * a.P;
+    const uint32_t gi = G0 + warp + (k % cnt_w) * kQmvWarps;
+    return a.w + ((size_t)tl * a.groups + gi) * slot_bytes;
+  };
+  const uint32_t nitems = cnt_w * ntc;
 
   if (lane == 0) {
     for (int s = 0; s < kQmvRing; ++s) mbar_init(&bars[warp * kQmvRing + s], 1);
@@ -135,12 +145,10 @@ __global__ void __launch_bounds__(kQmvThreads) qmv_kernel(QmvArgs a) {
   __syncwarp();
   // Weight prefetch: constant data, safe before the grid dependency wait.
   if (lane == 0) {
-    for (uint32_t k = 0; k < cnt_w && k < nslot; ++k) {
-      const uint32_t gi = G0 + warp + k * kQmvWarps;
+    for (uint32_t k = 0; k < nitems && k < nslot; ++k) {
       uint64_t* bar = &bars[warp * kQmvRing + k];
       mbar_arrive_expect_tx(bar, slot_bytes);
-      bulk_g2s(ring + (size_t)(warp * nslot + k) * slot_bytes, wtile + (size_t)gi * slot_bytes,
-               slot_bytes, bar);
+      bulk_g2s(ring + (size_t)(warp * nslot + k) * slot_bytes, item_src(k), slot_bytes, bar);
     }
   }
 
@@ -148,23 +156,90 @@ __global__ void __launch_bounds__(kQmvThreads) qmv_kernel(QmvArgs a) {
   pdl_launch();
 
   // ---------------- prologue: x -> per-group fixed point B fragments ------
+  // Stage the CTA's slice of x as fp16 in shared memory with wide, fully
+  // parallel loads (every load of a thread is issued before any is used),
+  // then quantize per (row, group) from shared memory.
   const uint32_t xf_words = ng * cpg * NT * 64;  // u32 words
   for (uint32_t i = threadIdx.x; i < xf_words; i += kQmvThreads) reinterpret_cast<uint32_t*>(xf)[i] = 0;
   for (uint32_t i = threadIdx.x; i < ng * kBatchChunk; i += kQmvThreads) {
     gsx[i] = 0.f; gsum[i] = 0.f; gsq[i] = 0;
   }
+  if (threadIdx.x < kBatchChunk) rms[threadIdx.x] = 0.f;
+  const uint32_t K0 = G0 * a.gs, Kr = ng * a.gs;
+  __half* xs = reinterpret_cast<__half*>(smem + L.xs);   // [bc][Kr]
+  __syncthreads();
   if constexpr (PRO == PRO_NORM) {
-    const float* res = static_cast<const float*>(a.x);
-    for (uint32_t b = warp; b < bc; b += kQmvWarps) {
-      const float4* r4 = reinterpret_cast<const float4*>(res + (size_t)(b0 + b) * a.x_stride);
-      float ss = 0.f;
-      for (uint32_t i = lane; i < a.K / 4; i += 32) {
-        const float4 v = r4[i];
-        ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss);
-        ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
+    const float* res = static_cast<const float*>(a.x) + (size_t)b0 * a.x_stride;
+    const uint32_t q4 = a.K / 4, n4 = bc * q4;
+    float ssr[kBatchChunk];
+#pragma unroll
+    for (int bb = 0; bb < kBatchChunk; ++bb) ssr[bb] = 0.f;
+    for (uint32_t j0 = threadIdx.x; j0 < n4; j0 += 4 * kQmvThreads) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t j = j0 + u * kQmvThreads;
+        v[u] = j < n4 ? *reinterpret_cast<const float4*>(res + (size_t)(j / q4) * a.x_stride + 4 * (j % q4))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      ss = warp_sum(ss);
-      if (lane == 0) rms[b] = rsqrtf(ss / (float)a.K + a.eps);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t b = (j0 + u * kQmvThreads) / q4;
+        const float e = v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+#pragma unroll
+        for (int bb = 0; bb < kBatchChunk; ++bb) ssr[bb] += (b == (uint32_t)bb) ? e : 0.f;
+      }
+    }
+#pragma unroll
+    for (int bb = 0; bb < kBatchChunk; ++bb) {
+      if ((uint32_t)bb >= bc) break;
+      const float t = warp_sum(ssr[bb]);
+      if (lane == 0) atomicAdd(&rms[bb], t);
+    }
+    __syncthreads();
+    if (threadIdx.x < bc) rms[threadIdx.x] = rsqrtf(rms[threadIdx.x] / (float)a.K + a.eps);
+    __syncthreads();
+    const uint32_t r4 = Kr / 4, m4 = bc * r4;
+    for (uint32_t j0 = threadIdx.x; j0 < m4; j0 += 4 * kQmvThreads) {
+      float4 v[4], w[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t j = j0 + u * kQmvThreads;
+        if (j < m4) {
+          const uint32_t k = K0 + 4 * (j % r4);
+          v[u] = *reinterpret_cast<const float4*>(res + (size_t)(j / r4) * a.x_stride + k);
+          w[u] = *reinterpret_cast<const float4*>(a.norm_w + k);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t j = j0 + u * kQmvThreads;
+        if (j < m4) {
+          const float rr = rms[j / r4];
+          float o0 = v[u].x * rr * w[u].x, o1 = v[u].y * rr * w[u].y;
+          float o2 = v[u].z * rr * w[u].z, o3 = v[u].w * rr * w[u].w;
+          if (a.bf16_round) { o0 = bf16_trunc(o0); o1 = bf16_trunc(o1); o2 = bf16_trunc(o2); o3 = bf16_trunc(o3); }
+          __half2* dst = reinterpret_cast<__half2*>(xs + (size_t)(j / r4) * Kr + 4 * (j % r4));
+          dst[0] = __floats2half2_rn(o0, o1);
+          dst[1] = __floats2half2_rn(o2, o3);
+        }
+      }
+    }
+  } else {
+    const __half* xh = static_cast<const __half*>(a.x) + (size_t)b0 * a.x_stride;
+    const uint32_t r8 = Kr / 8, m8 = bc * r8;
+    for (uint32_t j0 = threadIdx.x; j0 < m8; j0 += 4 * kQmvThreads) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t j = j0 + u * kQmvThreads;
+        if (j < m8) v[u] = *reinterpret_cast<const uint4*>(xh + (size_t)(j / r8) * a.x_stride + K0 + 8 * (j % r8));
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t j = j0 + u * kQmvThreads;
+        if (j < m8) *reinterpret_cast<uint4*>(xs + (size_t)(j / r8) * Kr + 8 * (j % r8)) = v[u];
+      }
     }
   }
   __syncthreads();
@@ -172,23 +247,12 @@ __global__ void __launch_bounds__(kQmvThreads) qmv_kernel(QmvArgs a) {
     const uint32_t gs = a.gs, per_lane = gs / 32;
     for (uint32_t p = warp; p < bc * ng; p += kQmvWarps) {
       const uint32_t b = p % bc, gl = p / bc;
-      const uint32_t kbase = (G0 + gl) * gs;
       float xv[8];
       float amax = 0.f, sumx = 0.f;
 #pragma unroll
       for (uint32_t m = 0; m < 8; ++m) {
         if (m < per_lane) {
-          const uint32_t k = kbase + m * 32 + lane;
-          float v;
-          if constexpr (PRO == PRO_NORM) {
-            const float* res = static_cast<const float*>(a.x) + (size_t)(b0 + b) * a.x_stride;
-            v = res[k] * rms[b] * a.norm_w[k];
-            if (a.bf16_round) v = bf16_trunc(v);
-            v = __half2float(__float2half_rn(v));
-          } else {
-            const __half* xh = static_cast<const __half*>(a.x) + (size_t)(b0 + b) * a.x_stride;
-            v = __half2float(xh[k]);
-          }
+          const float v = __half2float(xs[(size_t)b * Kr + gl * gs + m * 32 + lane]);
           xv[m] = v;
           amax = fmaxf(amax, fabsf(v));
           sumx += v;
@@ -227,6 +291,9 @@ __global__ void __launch_bounds__(kQmvThreads) qmv_kernel(QmvArgs a) {
 
   // ---------------- main loop --------------------------------------------
   const int g = lane >> 2, t = lane & 3;
+  bool failed = false;
+  for (uint32_t ti = 0; ti < ntc; ++ti) {
+  const uint32_t tile = pcta + ti * a.P;
   float y[SUB][NT][16];
 #pragma unroll
   for (int s = 0; s < SUB; ++s)
@@ -235,12 +302,12 @@ __global__ void __launch_bounds__(kQmvThreads) qmv_kernel(QmvArgs a) {
 #pragma unroll
       for (int v = 0; v < 16; ++v) y[s][n][v] = 0.f;
 
-  bool failed = false;
-  for (uint32_t k = 0; k < cnt_w; ++k) {
+  for (uint32_t kk = 0; kk < cnt_w; ++kk) {
+    const uint32_t k = ti * cnt_w + kk;
     const uint32_t slot = k % nslot;
     uint64_t* bar = &bars[warp * kQmvRing + slot];
     if (!failed) failed = !mbar_wait(bar, (k / nslot) & 1u, a.err);
-    const uint32_t gl = warp + k * kQmvWarps;  // group within CTA range
+    const uint32_t gl = warp + kk * kQmvWarps;  // group within CTA range
     const uint8_t* sb = ring + (size_t)(warp * nslot + slot) * slot_bytes;
 #pragma unroll
     for (int s = 0; s < SUB; ++s) {
@@ -331,16 +398,13 @@ __global__ void __launch_bounds__(kQmvThreads) qmv_kernel(QmvArgs a) {
       }
     }
     __syncwarp();
-    if (lane == 0 && k + nslot < cnt_w) {
-      const uint32_t gi = G0 + warp + (k + nslot) * kQmvWarps;
+    if (lane == 0 && k + nslot < nitems) {
       mbar_arrive_expect_tx(bar, slot_bytes);
-      bulk_g2s(ring + (size_t)(warp * nslot + slot) * slot_bytes,
-               wtile + (size_t)gi * slot_bytes, slot_bytes, bar);
+      bulk_g2s(ring + (size_t)(warp * nslot + slot) * slot_bytes, item_src(k + nslot), slot_bytes, bar);
     }
   }
 
   // ---------------- CTA reduction ----------------------------------------
-  __syncthreads();  // the reduction buffer aliases the segment ring
   {
     float* rw = red + (size_t)warp * kTileRows * SUB * kBatchChunk;
 #pragma unroll
@@ -363,10 +427,17 @@ __global__ void __launch_bounds__(kQmvThreads) qmv_kernel(QmvArgs a) {
     for (int w = 0; w < kQmvWarps; ++w) v += red[(size_t)w * nval + i];
     red[i] = v;
   }
+  bool last = true;
   if (a.ksplit > 1) {
+    // Split-K: partials of the bc live batch columns go to the workspace;
+    // the last CTA of the tile sums them in split order (8 loads in flight
+    // per step) and runs the epilogue.
     __syncthreads();
-    float* wsp = a.ws + ((size_t)(ychunk * a.tiles + tile) * a.ksplit) * nval;
-    for (uint32_t i = threadIdx.x; i < nval; i += kQmvThreads) wsp[(size_t)split * nval + i] = red[i];
+    const uint32_t bcm = min(a.batch, (uint32_t)kBatchChunk);
+    const uint32_t nvc = kTileRows * SUB * bcm;
+    float* wsp = a.ws + ((size_t)(ychunk * a.tiles + tile) * a.ksplit) * nvc;
+    for (uint32_t i = threadIdx.x; i < nvc; i += kQmvThreads)
+      wsp[(size_t)split * nvc + i] = red[(i / bcm) * kBatchChunk + (i % bcm)];
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -374,16 +445,36 @@ __global__ void __launch_bounds__(kQmvThreads) qmv_kernel(QmvArgs a) {
       flag[0] = (prev == a.ksplit - 1);
     }
     __syncthreads();
-    if (!flag[0]) return;
+    last = flag[0] != 0;
+    if (last) {
     __threadfence();
-    for (uint32_t i = threadIdx.x; i < nval; i += kQmvThreads) {
-      float v = 0.f;
-      for (uint32_t s = 0; s < a.ksplit; ++s) v += __ldcg(&wsp[(size_t)s * nval + i]);
-      red[i] = v;
+    for (uint32_t i0 = threadIdx.x; i0 < nvc; i0 += 2 * kQmvThreads) {
+      float acc[2] = {0.f, 0.f};
+      for (uint32_t s0 = 0; s0 < a.ksplit; s0 += 8) {
+        float t[2][8];
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t i = i0 + u * kQmvThreads;
+            t[u][j] = (i < nvc && s0 + j < a.ksplit) ? __ldcg(&wsp[(size_t)(s0 + j) * nvc + i]) : 0.f;
+          }
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[u] += t[u][j];
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const uint32_t i = i0 + u * kQmvThreads;
+        if (i < nvc) red[(i / bcm) * kBatchChunk + (i % bcm)] = acc[u];
+      }
     }
     if (threadIdx.x == 0) a.counters[ychunk * a.tiles + tile] = 0;
+    }
   }
   __syncthreads();
+  if (last) {
 
   // ---------------- epilogue ---------------------------------------------
   const bool rb = a.bf16_round != 0;
@@ -414,25 +505,41 @@ __global__ void __launch_bounds__(kQmvThreads) qmv_kernel(QmvArgs a) {
       if (lane == 0 && (uint32_t)b < bc && v) atomicMax(&a.argmax[b0 + b], v);
     }
   } else {
-    for (uint32_t i = threadIdx.x; i < kTileRows * kBatchChunk; i += kQmvThreads) {
-      const uint32_t r = i / kBatchChunk, b = i % kBatchChunk;
-      const uint32_t row = tile * kTileRows + r;
-      if (row >= a.M || b >= bc) continue;
-      const size_t o = (size_t)(b0 + b) * a.out_stride + row;
-      float v = red[i];
-      if constexpr (EPI == EPI_SILU) {
-        const float gv = v, uv = red[kTileRows * kBatchChunk + i];
-        v = gv / (1.0f + expf(-gv)) * uv;
-        if (rb) v = bf16_trunc(v);
-        static_cast<__half*>(a.out)[o] = __float2half_rn(v);
-      } else {
-        if (rb) v = bf16_trunc(v);
-        if constexpr (EPI == EPI_F16) static_cast<__half*>(a.out)[o] = __float2half_rn(v);
-        else if constexpr (EPI == EPI_F32) static_cast<float*>(a.out)[o] = v;
-        else static_cast<float*>(a.out)[o] += v;
+    // compact (row, live column) index; residual-add reads of up to 4 items
+    // per thread are issued before their stores
+    const uint32_t n = kTileRows * bc;
+    for (uint32_t i0 = threadIdx.x; i0 < n; i0 += 4 * kQmvThreads) {
+      float v[4], old[4];
+      size_t o[4];
+      bool ok[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t i = i0 + u * kQmvThreads;
+        const uint32_t r = i / bc, b = i % bc;
+        const uint32_t row = tile * kTileRows + r;
+        ok[u] = i < n && row < a.M;
+        o[u] = (size_t)(b0 + b) * a.out_stride + row;
+        v[u] = ok[u] ? red[r * kBatchChunk + b] : 0.f;
+        if constexpr (EPI == EPI_SILU) {
+          const float gv = v[u], uv = ok[u] ? red[kTileRows * kBatchChunk + r * kBatchChunk + b] : 0.f;
+          v[u] = gv / (1.0f + expf(-gv)) * uv;
+        }
+        if constexpr (EPI == EPI_RESADD) old[u] = ok[u] ? static_cast<float*>(a.out)[o[u]] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (!ok[u]) continue;
+        float x = v[u];
+        if (rb) x = bf16_trunc(x);
+        if constexpr (EPI == EPI_F16 || EPI == EPI_SILU) static_cast<__half*>(a.out)[o[u]] = __float2half_rn(x);
+        else if constexpr (EPI == EPI_F32) static_cast<float*>(a.out)[o[u]] = x;
+        else static_cast<float*>(a.out)[o[u]] = old[u] + x;
       }
     }
   }
+  }   // if (last)
+  __syncthreads();   // red is rewritten by the next tile
+  }   // tile loop
 }
 
 // Host launcher (qmv.cu).  Picks ksplit and the template instance.
