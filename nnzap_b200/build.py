@@ -22,7 +22,7 @@ LIB = OUT_DIR / "libnnz_b200.so"
 BUILD = ROOT / "_build"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3",
+NVCC_FLAGS = ["-O3", "-std=c++20", "-lineinfo", "-Xcompiler", "-fPIC,-O3",
               "--expt-relaxed-constexpr", "-I", str(ROOT / "include"), "-I", str(CSRC)]
 
 
@@ -54,7 +54,7 @@ def build(verbose: bool = False, force: bool = False) -> Path:
         objs.append(obj)
         if force or _stale(obj, src):
             if src.suffix == ".cpp":
-                cmd = ["g++", "-O3", "-std=c++17", "-fPIC", "-pthread", "-I", str(CSRC),
+                cmd = ["g++", "-O3", "-std=c++20", "-fPIC", "-pthread", "-I", str(CSRC),
                        "-I", str(ROOT / "include"), "-c", str(src), "-o", str(obj)]
             else:
                 cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]

@@ -3,6 +3,7 @@
 #include <math.h>
 
 #include "attn.cuh"
+#include "rope_dev.cuh"
 
 namespace nnz {
 
@@ -28,52 +29,6 @@ __host__ __device__ inline AttnSmem attn_layout() {
   L.flag = o; o += 16;
   L.total = o;
   return L;
-}
-
-// One warp: RMSNorm over the head (f32), scale, RoPE.  Leaves the EPL
-// values this lane owns in v[] (pairwise: contiguous elements; half-split:
-// element i pairs with i + HD/2, which lane + 16 owns).
-template <int HD>
-__device__ __forceinline__ void norm_rope_head(const __half* src, const float* nw, float eps,
-                                               float theta, int style, int pos, int lane,
-                                               float (&v)[HD / 32]) {
-  constexpr int EPL = HD / 32;
-  float ss = 0.f;
-#pragma unroll
-  for (int e = 0; e < EPL; ++e) {
-    v[e] = __half2float(src[lane * EPL + e]);
-    ss = fmaf(v[e], v[e], ss);
-  }
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / (float)HD + eps);
-#pragma unroll
-  for (int e = 0; e < EPL; ++e) v[e] = v[e] * r * nw[lane * EPL + e];
-  const double l2t = log2((double)theta);
-  if (style == ROPE_PAIRWISE) {
-#pragma unroll
-    for (int e = 0; e < EPL; e += 2) {
-      const int i = (lane * EPL + e) >> 1;
-      const double ang = (double)pos * exp2(-(2.0 * i / HD) * l2t);
-      double sd, cd;
-      sincos(ang, &sd, &cd);
-      const float c = (float)cd, s = (float)sd;
-      const float x0 = v[e], x1 = v[e + 1];
-      v[e] = x0 * c - x1 * s;
-      v[e + 1] = x0 * s + x1 * c;
-    }
-  } else {
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) {
-      const float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
-      const int i = (lane & 15) * EPL + e;
-      const double ang = (double)pos * exp2(-(2.0 * i / HD) * l2t);
-      double sd, cd;
-      sincos(ang, &sd, &cd);
-      const float c = (float)cd, s = (float)sd;
-      if (lane < 16) v[e] = v[e] * c - partner * s;   // first half: a*c - b*s
-      else v[e] = partner * s + v[e] * c;             // second half: a*s + b*c
-    }
-  }
 }
 
 template <int HD>

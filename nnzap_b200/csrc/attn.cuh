@@ -20,6 +20,7 @@
 // reference's V is transposed [d][t]; the values stored are identical).
 #pragma once
 #include "common.cuh"
+#include "rope_dev.cuh"
 
 namespace nnz {
 
@@ -28,7 +29,6 @@ constexpr int kAttnBlk = 32;     // positions per streamed block
 constexpr int kAttnStages = 4;
 constexpr int kAttnMaxG = 8;     // query heads per kv head
 
-enum RopeStyle : int { ROPE_PAIRWISE = 0, ROPE_HALF_SPLIT = 1 };
 
 struct AttnArgs {
   const __half* qkv;   // [rows][qkv_stride]: q | k | v

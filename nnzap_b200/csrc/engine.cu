@@ -20,6 +20,7 @@
 
 #include "../../include/nnz_b200.h"
 #include "attn.cuh"
+#include "mega.cuh"
 #include "misc.cuh"
 #include "packing.h"
 #include "qmv.cuh"
@@ -194,6 +195,13 @@ struct nnz_model {
   size_t dev_bytes = 0;
   std::vector<void*> allocs;
   std::map<std::pair<uint32_t, int>, cudaGraphExec_t> graphs;
+  // persistent decode kernel
+  bool mega_ok = false;
+  MegaLayer* mlayers = nullptr;
+  float *mR = nullptr, *mqkv = nullptr, *mgu = nullptr, *matt = nullptr;
+  unsigned int* mbar = nullptr;
+  struct MegaPlan { MegaArgs a; uint32_t grid, smem; bool ok; };
+  std::map<uint32_t, MegaPlan> mplans;
   std::vector<cudaEvent_t> events;
 };
 
@@ -432,6 +440,42 @@ int set_advance(nnz_model* m, int v) {
   return NNZ_OK;
 }
 
+const nnz_model::MegaPlan* mega_plan_for(nnz_model* m, uint32_t rows) {
+  if (!m->mega_ok || rows > (uint32_t)kBatchChunk) return nullptr;
+  auto it = m->mplans.find(rows);
+  if (it != m->mplans.end()) return it->second.ok ? &it->second : nullptr;
+  nnz_model::MegaPlan P{};
+  MegaArgs& a = P.a;
+  const nnz_config& c = m->c;
+  a.H = c.hidden_size; a.I = c.intermediate_size; a.n_q = c.num_query_heads; a.n_kv = c.num_kv_heads;
+  a.hd = c.head_dim; a.L = c.num_layers; a.vocab = c.vocab_size; a.gs = (uint32_t)c.group_size;
+  a.max_ctx = c.max_context_length; a.batch = rows; a.eps = c.eps; a.theta = c.rope_theta;
+  a.rope_style = c.rope_style; a.bf16r = m->bf16r; a.layers = m->mlayers; a.lm = m->lm; a.fnorm = m->fnorm;
+  a.emb_w = m->emb_w; a.emb_s = m->emb_s; a.emb_b = m->emb_b; a.kc = m->kc; a.vc = m->vc;
+  a.kv_layer = m->kv_layer; a.R = m->mR; a.qkv_acc = m->mqkv; a.gu_acc = m->mgu; a.att_ws = m->matt;
+  a.st = m->state; a.seq = m->seq; a.seq_len = c.max_context_length; a.logits = nullptr;
+  a.bar = m->mbar; a.err = m->err;
+  P.ok = mega_plan(a, m->fmt, m->bf16s, m->device, &P.grid, &P.smem);
+  m->mplans[rows] = P;
+  return P.ok ? &m->mplans[rows] : nullptr;
+}
+
+// One decode step for `rows` rows from the device decode state: the
+// persistent kernel when it applies, else the captured multi-kernel graph.
+int run_step(nnz_model* m, uint32_t rows, bool want_logits) {
+  if (const nnz_model::MegaPlan* P = mega_plan_for(m, rows)) {
+    MegaArgs a = P->a;
+    a.logits = want_logits ? m->logits : nullptr;
+    NNZ_CK(mega_launch(a, m->fmt, m->bf16s, P->grid, P->smem, m->st));
+    return NNZ_OK;
+  }
+  cudaGraphExec_t g;
+  int rc = get_graph(m, rows, want_logits, &g);
+  if (rc) return rc;
+  NNZ_CK(cudaGraphLaunch(g, m->st));
+  return NNZ_OK;
+}
+
 int enqueue_prefill(nnz_model* m, uint32_t n, bool want_logits) {
   int rc;
   for (uint32_t c0 = 0; c0 < n; c0 += kPrefillChunk) {
@@ -449,6 +493,8 @@ int enqueue_prefill(nnz_model* m, uint32_t n, bool want_logits) {
   }
   return NNZ_OK;
 }
+
+// Persistent-kernel plan for `rows` decode rows (cached).
 
 }  // namespace
 
@@ -695,6 +741,28 @@ int nnz_model_finalize(nnz_model* m) {
     for (uint32_t i = 0; i < c.max_context_length; ++i) io[i] = (int)i;
     NNZ_CK(cudaMemcpy(m->iota, io.data(), io.size() * 4, cudaMemcpyHostToDevice));
   }
+  {
+    // persistent decode kernel buffers (NNZ_DECODE_PATH=graph disables it)
+    const char* path = getenv("NNZ_DECODE_PATH");
+    m->mega_ok = !(path && strcmp(path, "graph") == 0) && !m->bf16r;
+    if (m->mega_ok) {
+      const uint32_t bmax = std::min<uint32_t>(c.max_batch, kBatchChunk);
+      const size_t G = c.num_query_heads / c.num_kv_heads;
+      if ((rc = dalloc(m, (void**)&m->mR, (size_t)3 * bmax * H * 4))) return rc;
+      if ((rc = dalloc(m, (void**)&m->mqkv, (size_t)bmax * m->qkv_rows * 4))) return rc;
+      if ((rc = dalloc(m, (void**)&m->mgu, (size_t)bmax * 2 * I * 4))) return rc;
+      if ((rc = dalloc(m, (void**)&m->matt, (size_t)bmax * c.num_kv_heads * 32 * G * (c.head_dim + 2) * 4))) return rc;
+      if ((rc = dalloc(m, (void**)&m->mbar, 64))) return rc;
+      if ((rc = dalloc(m, (void**)&m->mlayers, sizeof(MegaLayer) * c.num_layers))) return rc;
+      NNZ_CK(cudaMemset(m->mbar, 0, 64));
+      std::vector<MegaLayer> ml(c.num_layers);
+      for (uint32_t l = 0; l < c.num_layers; ++l) {
+        const LayerW& W = m->L[l];
+        ml[l] = MegaLayer{W.qkv, W.o, W.gu, W.down, W.attn_norm, W.ffn_norm, W.q_norm, W.k_norm};
+      }
+      NNZ_CK(cudaMemcpy(m->mlayers, ml.data(), sizeof(MegaLayer) * ml.size(), cudaMemcpyHostToDevice));
+    }
+  }
   NNZ_CK(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking));
   if ((rc = prepare_device(m->device))) return rc;
   m->finalized = true;
@@ -729,9 +797,7 @@ int nnz_forward_decode(nnz_model* m, const uint32_t* tokens, const uint32_t* pos
   NNZ_CK(cudaMemcpyAsync(m->state->token, tokens, batch * 4, cudaMemcpyHostToDevice, m->st));
   NNZ_CK(cudaMemcpyAsync(m->state->pos, positions, batch * 4, cudaMemcpyHostToDevice, m->st));
   if ((rc = set_advance(m, 0))) return rc;
-  cudaGraphExec_t g;
-  if ((rc = get_graph(m, batch, logits != nullptr, &g))) return rc;
-  NNZ_CK(cudaGraphLaunch(g, m->st));
+  if ((rc = run_step(m, batch, logits != nullptr))) return rc;
   std::vector<unsigned long long> am(batch);
   NNZ_CK(cudaMemcpyAsync(am.data(), m->state->argmax, batch * 8, cudaMemcpyDeviceToHost, m->st));
   if (logits)
@@ -779,8 +845,6 @@ int nnz_generate(nnz_model* m, const nnz_generate_opts* o, nnz_generate_result* 
   // the reference stops when position reaches max_context_length (transformer.zig:3993)
   const uint32_t steps = std::min<uint32_t>(o->max_new, m->c.max_context_length - n);
   int rc;
-  cudaGraphExec_t g;
-  if ((rc = get_graph(m, 1, false, &g))) return rc;
   while (m->events.size() < (size_t)steps + 2) {
     cudaEvent_t e;
     NNZ_CK(cudaEventCreate(&e));
@@ -796,7 +860,7 @@ int nnz_generate(nnz_model* m, const nnz_generate_opts* o, nnz_generate_result* 
   if ((rc = set_advance(m, 1))) return rc;
   NNZ_CK(cudaEventRecord(m->events[1], m->st));
   for (uint32_t i = 0; i < steps; ++i) {
-    NNZ_CK(cudaGraphLaunch(g, m->st));
+    if ((rc = run_step(m, 1, false))) return rc;
     NNZ_CK(cudaEventRecord(m->events[2 + i], m->st));
   }
   std::vector<uint32_t> toks(steps);
@@ -836,8 +900,6 @@ int nnz_decode_steps(nnz_model* m, const uint32_t* tokens, const uint32_t* posit
   }
   NNZ_CK(cudaSetDevice(m->device));
   int rc;
-  cudaGraphExec_t g;
-  if ((rc = get_graph(m, batch, false, &g))) return rc;
   while (m->events.size() < (size_t)steps + 2) {
     cudaEvent_t e;
     NNZ_CK(cudaEventCreate(&e));
@@ -849,7 +911,7 @@ int nnz_decode_steps(nnz_model* m, const uint32_t* tokens, const uint32_t* posit
   NNZ_CK(cudaEventRecord(m->events[0], m->st));
   for (uint32_t s = 0; s < steps; ++s) {
     if (s == 1 && (rc = set_advance(m, 1))) return rc;
-    NNZ_CK(cudaGraphLaunch(g, m->st));
+    if ((rc = run_step(m, batch, false))) return rc;
     NNZ_CK(cudaEventRecord(m->events[1 + s], m->st));
   }
   // tokens consumed at steps 1..steps-1 are recorded in seq at pos+1..; the
@@ -933,14 +995,13 @@ int nnz_bench_decode_graph(nnz_model* m, uint32_t batch, uint32_t iters, double*
   if (batch == 0 || batch > m->c.max_batch) return fail(NNZ_EINVAL, "batch");
   NNZ_CK(cudaSetDevice(m->device));
   int rc;
-  cudaGraphExec_t g;
-  if ((rc = get_graph(m, batch, false, &g))) return rc;
   cudaEvent_t a, b;
   NNZ_CK(cudaEventCreate(&a));
   NNZ_CK(cudaEventCreate(&b));
   if ((rc = set_advance(m, 0))) return rc;
   NNZ_CK(cudaEventRecord(a, m->st));
-  for (uint32_t i = 0; i < iters; ++i) NNZ_CK(cudaGraphLaunch(g, m->st));
+  for (uint32_t i = 0; i < iters; ++i)
+    if ((rc = run_step(m, batch, false))) return rc;
   NNZ_CK(cudaEventRecord(b, m->st));
   rc = sync_check(m);
   float ms = 0.f;

@@ -1,0 +1,759 @@
+// Persistent cooperative decode kernel (see mega.cuh).
+//
+// Phases, each ended by a grid barrier:
+//   EMBED   CTA 0 advances the device decode state (token <- previous
+//           argmax, position += 1) and writes residual version 0; the other
+//           CTAs clear the accumulators;
+//   per layer l:
+//   QKV     fused-norm QKV matvec, split-K partials -> qkv_acc (red.add);
+//   ATT     flash-decoding over the fp16 KV cache per (kv head, row, split)
+//           with QK-norm + RoPE + KV write, partial (m, l, o) -> att_ws;
+//   O       merges the splits into the fp16 attention output, o-proj,
+//           partials -> next residual version (red.add), plus the previous
+//           residual added once by the split-0 units;
+//   GU      fused-norm gate/up matvec, partials -> gu_acc (red.add);
+//   DN      fp16(SiLU(g) * u) from gu_acc, down-proj -> next residual;
+//   LM      fused final-norm LM head, f32 logits (optional) and argmax.
+// The residual rotates over three buffers: the phase producing version v+1
+// accumulates into a buffer cleared during the phase that produced v, and
+// no phase reads the buffer it writes.  Every read of data produced in this
+// launch bypasses L1 (__ldcg).
+//
+// Weight streaming: each warp owns a ring of `nslot` segment buffers fed by
+// 1-D bulk copies.  Its lane 0 walks the warp's static sequence of weight
+// segments across ALL phases, keeping nslot copies in flight, so while a CTA
+// waits at a grid barrier the next phases' weights are already landing in
+// shared memory.  Every wait (mbarrier, grid barrier) is bounded.
+#include <cuda_runtime.h>
+
+#include "mega.cuh"
+#include "rope_dev.cuh"
+
+namespace nnz {
+
+namespace {
+
+enum PhaseType : int { PH_EMBED = 0, PH_QKV, PH_ATT, PH_O, PH_GU, PH_DN, PH_LM, PH_END };
+
+constexpr int kMaxSlots = 4;
+constexpr int kAttBlk = 32;
+constexpr int kAttStages = 2;
+constexpr int kAttMaxG = 8;
+
+struct PhaseInfo {
+  int type;
+  uint32_t layer, M, K, tiles, ks, groups, sub, units;
+  const uint8_t* w;
+};
+
+__host__ __device__ inline PhaseInfo phase_info(const MegaArgs& a, const MegaLayer* layers,
+                                                uint32_t ph) {
+  PhaseInfo p{};
+  const uint32_t last = 1 + 5 * a.L;
+  if (ph == 0) { p.type = PH_EMBED; return p; }
+  if (ph > last) { p.type = PH_END; return p; }
+  p.sub = 1;
+  if (ph == last) {
+    p.type = PH_LM; p.w = a.lm; p.M = a.vocab; p.K = a.H; p.ks = 1;
+  } else {
+    const uint32_t l = (ph - 1) / 5, r = (ph - 1) % 5;
+    p.layer = l;
+    const uint32_t qd = a.n_q * a.hd, kvd = a.n_kv * a.hd;
+    switch (r) {
+      case 0: p.type = PH_QKV; p.w = layers ? layers[l].qkv : nullptr; p.M = qd + 2 * kvd; p.K = a.H; p.ks = a.ks_qkv; break;
+      case 1: p.type = PH_ATT; p.units = a.n_kv * a.batch * a.att_splits; return p;
+      case 2: p.type = PH_O; p.w = layers ? layers[l].o : nullptr; p.M = a.H; p.K = qd; p.ks = a.ks_o; break;
+      case 3: p.type = PH_GU; p.w = layers ? layers[l].gu : nullptr; p.M = a.I; p.K = a.H; p.ks = a.ks_gu; p.sub = 2; break;
+      default: p.type = PH_DN; p.w = layers ? layers[l].down : nullptr; p.M = a.H; p.K = a.I; p.ks = a.ks_dn; break;
+    }
+  }
+  p.tiles = num_tiles(p.M);
+  p.groups = p.K / a.gs;
+  p.units = p.tiles * p.ks;
+  return p;
+}
+
+__host__ __device__ inline void unit_range(const PhaseInfo& p, uint32_t u, uint32_t* tile, uint32_t* split,
+                                           uint32_t* G0, uint32_t* ng) {
+  *tile = u / p.ks;
+  *split = u % p.ks;
+  const uint32_t g0 = (uint32_t)((uint64_t)p.groups * (*split) / p.ks);
+  const uint32_t g1 = (uint32_t)((uint64_t)p.groups * (*split + 1) / p.ks);
+  *G0 = g0;
+  *ng = g1 - g0;
+}
+
+struct MegaSmem {
+  uint32_t bars, abars, ring, slot_bytes, u, xs, xf, gsx, gsum, gsq, red, rms, flag,
+      kring, vring, qs, knew, vnew, ss, stat, tok, total, kr_max, ng_max, bcm, nt;
+};
+
+__host__ __device__ inline MegaSmem mega_layout(const MegaArgs& a, int fmt) {
+  MegaSmem s{};
+  s.bcm = a.batch < (uint32_t)kBatchChunk ? a.batch : kBatchChunk;
+  s.nt = s.bcm > 4 ? 2 : 1;
+  // widest K range any CTA quantizes
+  uint32_t krm = a.H;  // LM head runs unsplit
+  const uint32_t gs = a.gs;
+  const uint32_t ks[4] = {a.ks_qkv, a.ks_o, a.ks_gu, a.ks_dn};
+  const uint32_t Ks[4] = {a.H, a.n_q * a.hd, a.H, a.I};
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t g = Ks[i] / gs, r = ((g + ks[i] - 1) / ks[i]) * gs;
+    krm = r > krm ? r : krm;
+  }
+  s.kr_max = krm;
+  s.ng_max = krm / gs;
+  s.slot_bytes = 2 * seg_bytes(fmt, gs);
+  uint32_t o = 0;
+  s.bars = o; o += kQmvWarps * kMaxSlots * 8;
+  s.abars = o; o += kAttStages * 8;
+  o = (o + 127) & ~127u;
+  s.ring = o; o += kQmvWarps * a.nslot * s.slot_bytes;
+  o = (o + 127) & ~127u;
+  s.u = o;
+  // matvec view of the union
+  uint32_t q = o;
+  s.xs = q; q += ((krm * s.bcm * 2) + 15) & ~15u;
+  s.xf = q; q += (krm / kChunk) * s.nt * 256;
+  s.gsx = q; q += s.ng_max * kBatchChunk * 4;
+  s.gsum = q; q += s.ng_max * kBatchChunk * 4;
+  s.gsq = q; q += s.ng_max * kBatchChunk * 4;
+  s.red = q; q += kQmvWarps * 2 * kTileRows * s.bcm * 4;
+  s.rms = q; q += kBatchChunk * 4;
+  s.flag = q; q += 16;
+  s.tok = q; q += kBatchChunk * 4;
+  // attention view of the union
+  uint32_t t = o;
+  s.kring = t; t += kAttStages * kAttBlk * a.hd * 2;
+  s.vring = t; t += kAttStages * kAttBlk * a.hd * 2;
+  s.qs = t; t += kAttMaxG * a.hd * 4;
+  s.knew = t; t += a.hd * 4;
+  s.vnew = t; t += a.hd * 4;
+  s.ss = t; t += kAttMaxG * kAttBlk * 4;
+  s.stat = t; t += 3 * kAttMaxG * 4;
+  s.total = q > t ? q : t;
+  return s;
+}
+
+// Grid barrier over all CTAs (co-resident by cooperative launch).  Bounded:
+// after kSpinLimit polls it records ERR_SPIN_TIMEOUT and lets the CTA run
+// on (results are then garbage, but every CTA terminates).
+__device__ __forceinline__ void grid_sync(unsigned int* bar, unsigned int nblocks, unsigned int& gen,
+                                          int* err) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned int prev = atomicAdd(&bar[0], 1u);
+    if (prev == nblocks - 1) {
+      bar[0] = 0;
+      __threadfence();
+      atomicAdd(&bar[1], 1u);
+    } else {
+      uint32_t i = 0;
+      while (true) {
+        unsigned int g;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(&bar[1]) : "memory");
+        if (g != gen) break;
+        if (++i > kSpinLimit) { atomicOr(err, ERR_SPIN_TIMEOUT); break; }
+      }
+    }
+    __threadfence();
+  }
+  gen += 1;
+  __syncthreads();
+}
+
+struct Ctx {
+  const MegaArgs* a;
+  const MegaLayer* layers;
+  uint8_t* smem;
+  MegaSmem S;
+  uint32_t cta, G, seg;
+  int warp, lane;
+  // consumer item counter and producer cursor (lane 0 of each warp)
+  uint32_t k;
+  uint32_t pph, pu, pgl;
+  bool failed;
+};
+
+// Advance the producer cursor to the next weight segment of this warp.
+__device__ __forceinline__ void prod_normalize(Ctx& c) {
+  const uint32_t last = 1 + 5 * c.a->L;
+  while (c.pph <= last) {
+    const PhaseInfo p = phase_info(*c.a, c.layers, c.pph);
+    if (p.type == PH_EMBED || p.type == PH_ATT || c.pu >= p.units) {
+      ++c.pph; c.pu = c.cta; c.pgl = c.warp;
+      continue;
+    }
+    uint32_t tile, split, G0, ng;
+    unit_range(p, c.pu, &tile, &split, &G0, &ng);
+    if (c.pgl >= ng) { c.pu += c.G; c.pgl = c.warp; continue; }
+    return;
+  }
+}
+
+// Issue the producer's current segment into slot `slot` and advance.
+__device__ __forceinline__ void prod_issue(Ctx& c, uint32_t slot) {
+  if (c.pph > 1 + 5 * c.a->L) return;
+  const PhaseInfo p = phase_info(*c.a, c.layers, c.pph);
+  uint32_t tile, split, G0, ng;
+  unit_range(p, c.pu, &tile, &split, &G0, &ng);
+  const uint32_t bytes = p.sub * c.seg;
+  const uint8_t* src = p.w + ((size_t)tile * p.groups + G0 + c.pgl) * bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(c.smem + c.S.bars);
+  uint64_t* bar = &bars[c.warp * kMaxSlots + slot];
+  mbar_arrive_expect_tx(bar, bytes);
+  bulk_g2s(c.smem + c.S.ring + (size_t)(c.warp * c.a->nslot + slot) * c.S.slot_bytes, src, bytes, bar);
+  c.pgl += kQmvWarps;
+  prod_normalize(c);
+}
+
+__device__ __forceinline__ float* resv(const MegaArgs& a, uint32_t v) {
+  return a.R + (size_t)(v % 3) * a.batch * a.H;
+}
+
+// Zero n floats of `p`, spread over the whole grid.
+__device__ __forceinline__ void grid_zero(float* p, size_t n, const Ctx& c) {
+  for (size_t i = (size_t)c.cta * blockDim.x + threadIdx.x; i < n; i += (size_t)c.G * blockDim.x) p[i] = 0.f;
+}
+
+// ---- prologues -------------------------------------------------------------
+
+// O phase: merge the attention splits of the heads in [K0, K0+Kr) into fp16.
+__device__ void stage_attn(const Ctx& c, uint32_t K0, uint32_t Kr, uint32_t bc, __half* xs) {
+  const MegaArgs& a = *c.a;
+  const uint32_t G = a.n_q / a.n_kv, S = a.att_splits, rec = a.hd + 2;
+  for (uint32_t j = threadIdx.x; j < bc * Kr; j += blockDim.x) {
+    const uint32_t b = j / Kr, k = K0 + j % Kr;
+    const uint32_t h = k / a.hd, d = k % a.hd;
+    const uint32_t kvh = h / G, hg = h % G;
+    const float* base = a.att_ws + ((size_t)(b * a.n_kv + kvh) * S) * G * rec + (size_t)hg * rec;
+    float M = -INFINITY, Ls = 0.f, o = 0.f;
+    for (uint32_t s0 = 0; s0 < S; s0 += 8) {
+      float mv[8], lv[8], ov[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const bool ok = s0 + q < S;
+        const float* r = base + (size_t)(s0 + q) * G * rec;
+        mv[q] = ok ? __ldcg(r) : -INFINITY;
+        lv[q] = ok ? __ldcg(r + 1) : 0.f;
+        ov[q] = ok ? __ldcg(r + 2 + d) : 0.f;
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (mv[q] == -INFINITY) continue;
+        const float nm = fmaxf(M, mv[q]);
+        const float a0 = (M == -INFINITY) ? 0.f : expf(M - nm), a1 = expf(mv[q] - nm);
+        Ls = Ls * a0 + lv[q] * a1;
+        o = o * a0 + ov[q] * a1;
+        M = nm;
+      }
+    }
+    xs[(size_t)b * Kr + (k - K0)] = __float2half_rn(o / Ls);
+  }
+}
+
+// DN phase: fp16(SiLU(g) * u) for k in [K0, K0+Kr).
+__device__ void stage_silu(const Ctx& c, uint32_t K0, uint32_t Kr, uint32_t bc, __half* xs) {
+  const MegaArgs& a = *c.a;
+  for (uint32_t j0 = threadIdx.x; j0 < bc * Kr; j0 += 4 * blockDim.x) {
+    float g[4], u[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t j = j0 + q * blockDim.x;
+      if (j < bc * Kr) {
+        const uint32_t b = j / Kr, k = K0 + j % Kr;
+        g[q] = __ldcg(&a.gu_acc[((size_t)b * 2) * a.I + k]);
+        u[q] = __ldcg(&a.gu_acc[((size_t)b * 2 + 1) * a.I + k]);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t j = j0 + q * blockDim.x;
+      if (j < bc * Kr) {
+        float v = g[q] / (1.0f + expf(-g[q])) * u[q];
+        if (a.bf16r) v = bf16_trunc(v);
+        xs[(size_t)(j / Kr) * Kr + (j % Kr)] = __float2half_rn(v);
+      }
+    }
+  }
+}
+
+// ---- one matvec work unit ------------------------------------------------------
+template <int FMT, int NT, int SUB, bool BF16S>
+__device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u) {
+  const MegaArgs& a = *c.a;
+  uint32_t tile, split, G0, ng;
+  unit_range(p, u, &tile, &split, &G0, &ng);
+  const uint32_t gs = a.gs, cpg = gs / kChunk, K0 = G0 * gs, Kr = ng * gs;
+  const uint32_t bc = c.S.bcm;
+  uint8_t* sm = c.smem;
+  __half* xs = reinterpret_cast<__half*>(sm + c.S.xs);
+  uint8_t* xf = sm + c.S.xf;
+  float* gsx = reinterpret_cast<float*>(sm + c.S.gsx);
+  float* gsum = reinterpret_cast<float*>(sm + c.S.gsum);
+  int* gsq = reinterpret_cast<int*>(sm + c.S.gsq);
+  float* red = reinterpret_cast<float*>(sm + c.S.red);
+  float* rms = reinterpret_cast<float*>(sm + c.S.rms);
+
+  // prologue: this unit's slice of x
+  if (p.type == PH_QKV || p.type == PH_GU || p.type == PH_LM) {
+    const uint32_t v = p.type == PH_QKV ? 2 * p.layer : p.type == PH_GU ? 2 * p.layer + 1 : 2 * a.L;
+    const float* nw = p.type == PH_QKV ? c.layers[p.layer].attn_norm
+                    : p.type == PH_GU ? c.layers[p.layer].ffn_norm : a.fnorm;
+    const float* res = resv(a, v);
+    block_rms(res, a.H, a.H, bc, a.eps, rms);
+    stage_norm(res, a.H, nw, rms, K0, Kr, bc, a.bf16r != 0, xs);
+  } else if (p.type == PH_O) {
+    stage_attn(c, K0, Kr, bc, xs);
+  } else {
+    stage_silu(c, K0, Kr, bc, xs);
+  }
+  quantize_xs<NT>(xs, Kr, bc, ng, gs, xf, gsx, gsum, gsq);
+
+  float y[SUB][NT][16];
+#pragma unroll
+  for (int s = 0; s < SUB; ++s)
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int v = 0; v < 16; ++v) y[s][n][v] = 0.f;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + c.S.bars);
+  for (uint32_t gl = c.warp; gl < ng; gl += kQmvWarps) {
+    const uint32_t slot = c.k % a.nslot;
+    if (!c.failed) c.failed = !mbar_wait(&bars[c.warp * kMaxSlots + slot], (c.k / a.nslot) & 1u, a.err);
+    const uint8_t* sb = sm + c.S.ring + (size_t)(c.warp * a.nslot + slot) * c.S.slot_bytes;
+    qmv_group<FMT, NT, SUB, BF16S>(sb, c.seg, xf, gl, cpg, gsx, gsum, gsq, y);
+    __syncwarp();
+    if (c.lane == 0) prod_issue(c, slot);
+    ++c.k;
+  }
+
+  // CTA reduction: red[warp][sub*128 + row][b]
+  const int g = c.lane >> 2, t = c.lane & 3;
+  const uint32_t nrow = kTileRows * SUB;
+  float* rw = red + (size_t)c.warp * nrow * bc;
+#pragma unroll
+  for (int s = 0; s < SUB; ++s)
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int v = 0; v < 16; ++v) {
+        const uint32_t b = n * 4 + t;
+        if (b < bc) rw[(s * kTileRows + y_row<FMT>(v, g)) * bc + b] = y[s][n][v];
+      }
+  __syncthreads();
+  const uint32_t nv = nrow * bc;
+  const uint32_t qd = a.n_q * a.hd, qkv_rows = qd + 2 * a.n_kv * a.hd;
+  if (p.type == PH_LM) {
+    // unsplit: final logits of this tile, argmax per row
+    float* lg = a.logits;
+    for (uint32_t b = 0; b < bc; ++b) {
+      unsigned long long best = 0ull;
+      for (uint32_t r = threadIdx.x; r < kTileRows; r += blockDim.x) {
+        const uint32_t row = tile * kTileRows + r;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kQmvWarps; ++w) v += red[(size_t)w * nv + r * bc + b];
+        if (row < p.M) {
+          if (a.bf16r) v = bf16_trunc(v);
+          if (lg) lg[(size_t)b * a.vocab + row] = v;
+          const unsigned long long pk = argmax_pack(v, row);
+          best = pk > best ? pk : best;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long q = __shfl_xor_sync(0xffffffffu, best, o);
+        best = q > best ? q : best;
+      }
+      if (c.lane == 0 && best) atomicMax(&a.st->argmax[b], best);
+    }
+  } else {
+    for (uint32_t i = threadIdx.x; i < nv; i += blockDim.x) {
+      const uint32_t rl = i / bc, b = i % bc;
+      const uint32_t s = rl / kTileRows, row = tile * kTileRows + (rl % kTileRows);
+      if (row >= p.M) continue;
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < kQmvWarps; ++w) v += red[(size_t)w * nv + i];
+      switch (p.type) {
+        case PH_QKV: atomicAdd(&a.qkv_acc[(size_t)b * qkv_rows + row], v); break;
+        case PH_GU: atomicAdd(&a.gu_acc[((size_t)b * 2 + s) * a.I + row], v); break;
+        default: {   // O / DN: residual versions
+          const uint32_t vin = p.type == PH_O ? 2 * p.layer : 2 * p.layer + 1;
+          if (split == 0) v += __ldcg(&resv(a, vin)[(size_t)b * a.H + row]);
+          atomicAdd(&resv(a, vin + 1)[(size_t)b * a.H + row], v);
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// ---- attention work unit -----------------------------------------------------
+// One (kv head, row, split): QK-norm + RoPE of the G query heads (and of the
+// new key when this split owns the current position, which it then writes to
+// the cache), online softmax over the split's cached positions streamed in
+// 32-position blocks, partial (m, l, o) to att_ws.
+template <int HD>
+__device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause)[kAttStages]) {
+  constexpr int EPL = HD / 32;
+  const MegaArgs& a = *c.a;
+  const uint32_t S = a.att_splits, G = a.n_q / a.n_kv;
+  const uint32_t kvh = u % a.n_kv, b = (u / a.n_kv) % a.batch, split = u / (a.n_kv * a.batch);
+  uint8_t* sm = c.smem;
+  uint64_t* abars = reinterpret_cast<uint64_t*>(sm + c.S.abars);
+  __half* kring = reinterpret_cast<__half*>(sm + c.S.kring);
+  __half* vring = reinterpret_cast<__half*>(sm + c.S.vring);
+  float* qs = reinterpret_cast<float*>(sm + c.S.qs);
+  float* knew = reinterpret_cast<float*>(sm + c.S.knew);
+  float* vnew = reinterpret_cast<float*>(sm + c.S.vnew);
+  float* ss = reinterpret_cast<float*>(sm + c.S.ss);
+  float* mst = reinterpret_cast<float*>(sm + c.S.stat);
+  float* lst = mst + kAttMaxG;
+  float* alp = lst + kAttMaxG;
+  const int warp = c.warp, lane = c.lane;
+
+  int pos = __ldcg(&a.st->pos[b]);
+  if (pos < 0 || pos >= (int)a.max_ctx) {
+    if (threadIdx.x == 0) atomicOr(a.err, ERR_BAD_POS);
+    pos = pos < 0 ? 0 : (int)a.max_ctx - 1;
+  }
+  const int seq = pos + 1;
+  const int per = (seq + (int)S - 1) / (int)S;
+  const int t0 = (int)split * per;
+  const int t1 = min(seq, t0 + per);
+  const bool own_new = t0 <= pos && pos < t1;
+  const int cend = min(t1, pos);
+  const int ncache = cend > t0 ? cend - t0 : 0;
+  const int nblk = (ncache + kAttBlk - 1) / kAttBlk;
+  const size_t head_off = a.kv_layer * p.layer + ((size_t)b * a.n_kv + kvh) * a.max_ctx * HD;
+  const __half* kb = a.kc + head_off;
+  const __half* vb = a.vc + head_off;
+  auto issue = [&](int blk) {
+    const int stg = blk % kAttStages;
+    const int n = min(kAttBlk, ncache - blk * kAttBlk);
+    const uint32_t bytes = (uint32_t)n * HD * 2;
+    mbar_arrive_expect_tx(&abars[stg], 2 * bytes);
+    bulk_g2s(kring + (size_t)stg * kAttBlk * HD, kb + (size_t)(t0 + blk * kAttBlk) * HD, bytes, &abars[stg]);
+    bulk_g2s(vring + (size_t)stg * kAttBlk * HD, vb + (size_t)(t0 + blk * kAttBlk) * HD, bytes, &abars[stg]);
+  };
+  if (threadIdx.x == 0)
+    for (int blk = 0; blk < nblk && blk < kAttStages; ++blk) issue(blk);
+
+  const uint32_t qkv_rows = (a.n_q + 2 * a.n_kv) * HD;
+  const float* qrow = a.qkv_acc + (size_t)b * qkv_rows;
+  const float* qn = c.layers[p.layer].q_norm;
+  const float* kn = c.layers[p.layer].k_norm;
+  for (uint32_t h = warp; h < G; h += kQmvWarps) {
+    float v[EPL];
+    norm_rope_head<HD>(qrow + (size_t)(kvh * G + h) * HD, qn, a.eps, a.theta, a.rope_style, pos, lane, v);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) qs[h * HD + lane * EPL + e] = v[e];
+  }
+  if (own_new && warp == kQmvWarps - 1) {
+    float v[EPL];
+    norm_rope_head<HD>(qrow + (size_t)a.n_q * HD + (size_t)kvh * HD, kn, a.eps, a.theta, a.rope_style,
+                       pos, lane, v);
+    const float* vsrc = qrow + (size_t)(a.n_q + a.n_kv) * HD + (size_t)kvh * HD;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const int d = lane * EPL + e;
+      const __half kh = __float2half_rn(v[e]);
+      const __half vh = __float2half_rn(__ldcg(vsrc + d));
+      a.kc[head_off + (size_t)pos * HD + d] = kh;
+      a.vc[head_off + (size_t)pos * HD + d] = vh;
+      knew[d] = __half2float(kh);
+      vnew[d] = __half2float(vh);
+    }
+  }
+  if (threadIdx.x < kAttMaxG) {
+    mst[threadIdx.x] = -INFINITY;
+    lst[threadIdx.x] = 0.f;
+  }
+  __syncthreads();
+
+  constexpr int NHS = kQmvThreads / HD;
+  const int d = threadIdx.x % HD, hs = threadIdx.x / HD;
+  float acc[kAttMaxG];
+#pragma unroll
+  for (int h = 0; h < kAttMaxG; ++h) acc[h] = 0.f;
+  const float inv = rsqrtf((float)HD);
+  const int total = nblk + (own_new ? 1 : 0);
+  for (int blk = 0; blk < total; ++blk) {
+    const bool is_new = blk == nblk;
+    const int n = is_new ? 1 : min(kAttBlk, ncache - blk * kAttBlk);
+    const int stg = blk % kAttStages;
+    const __half* kr = kring + (size_t)stg * kAttBlk * HD;
+    const __half* vr = vring + (size_t)stg * kAttBlk * HD;
+    if (!is_new) {
+      if (!c.failed) c.failed = !mbar_wait(&abars[stg], ause[stg] & 1u, a.err);
+      ause[stg] += 1;
+    }
+    for (int t = warp; t < n; t += kQmvWarps) {
+      float kv[EPL];
+      if (is_new) {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) kv[e] = knew[lane * EPL + e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; e += 2) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(kr + (size_t)t * HD + lane * EPL + e));
+          kv[e] = f.x; kv[e + 1] = f.y;
+        }
+      }
+      for (uint32_t h = 0; h < G; ++h) {
+        float dot = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) dot = fmaf(qs[h * HD + lane * EPL + e], kv[e], dot);
+        dot = warp_sum(dot);
+        if (lane == 0) ss[h * kAttBlk + t] = dot * inv;
+      }
+    }
+    __syncthreads();
+    for (uint32_t h = warp; h < G; h += kQmvWarps) {
+      const float sv = lane < n ? ss[h * kAttBlk + lane] : -INFINITY;
+      const float mx = warp_max(sv);
+      const float mo = mst[h], mn = fmaxf(mo, mx);
+      const float pe = lane < n ? expf(sv - mn) : 0.f;
+      if (lane < n) ss[h * kAttBlk + lane] = pe;
+      const float ls = warp_sum(pe);
+      if (lane == 0) {
+        const float al = (mo == -INFINITY) ? 0.f : expf(mo - mn);
+        alp[h] = al;
+        lst[h] = lst[h] * al + ls;
+        mst[h] = mn;
+      }
+    }
+    __syncthreads();
+    for (uint32_t h = hs; h < G; h += NHS) {
+      float o = acc[h] * alp[h];
+      if (is_new) o = fmaf(ss[h * kAttBlk], vnew[d], o);
+      else
+        for (int t = 0; t < n; ++t) o = fmaf(ss[h * kAttBlk + t], __half2float(vr[(size_t)t * HD + d]), o);
+      acc[h] = o;
+    }
+    __syncthreads();
+    if (!is_new && threadIdx.x == 0 && blk + kAttStages < nblk) issue(blk + kAttStages);
+  }
+  const uint32_t rec = HD + 2;
+  float* wsp = a.att_ws + (((size_t)(b * a.n_kv + kvh) * S + split) * G) * rec;
+  for (uint32_t h = hs; h < G; h += NHS) wsp[(size_t)h * rec + 2 + d] = acc[h];
+  if (threadIdx.x < G) {
+    wsp[(size_t)threadIdx.x * rec + 0] = mst[threadIdx.x];
+    wsp[(size_t)threadIdx.x * rec + 1] = lst[threadIdx.x];
+  }
+  __syncthreads();
+}
+
+// ---- embedding phase -------------------------------------------------------------
+template <int FMT, bool BF16S>
+__device__ void embed_phase(Ctx& c) {
+  const MegaArgs& a = *c.a;
+  uint32_t* tok_s = reinterpret_cast<uint32_t*>(c.smem + c.S.tok);
+  if (c.cta == 0) {
+    if (threadIdx.x < a.batch) {
+      const uint32_t r = threadIdx.x;
+      const int adv = a.st->advance;
+      const unsigned long long am = a.st->argmax[r];
+      const int p0 = a.st->pos[r];
+      const uint32_t t0 = a.st->token[r];
+      uint32_t tok = t0;
+      if (adv) {
+        tok = argmax_index(am);
+        const int pp = p0 + 1;
+        a.st->pos[r] = pp;
+        a.st->token[r] = tok;
+        if (a.seq && pp >= 0 && (uint32_t)pp < a.seq_len) a.seq[(size_t)r * a.seq_len + pp] = tok;
+      }
+      a.st->argmax[r] = 0ull;
+      if (tok >= a.vocab) {
+        atomicOr(a.err, ERR_BAD_TOKEN);
+        tok = 0;
+      }
+      tok_s[r] = tok;
+    }
+    __syncthreads();
+    float* out0 = resv(a, 0);
+    for (uint32_t i = threadIdx.x; i < a.batch * (a.H / 8); i += blockDim.x) {
+      const uint32_t r = i / (a.H / 8), d8 = i % (a.H / 8);
+      const uint64_t f = (uint64_t)tok_s[r] * a.H + 8 * d8;
+      float v[8];
+      if constexpr (FMT == FMT_Q1) {
+        const uint32_t bits = a.emb_w[f >> 3];
+        const float s = __half2float(__ushort_as_half(a.emb_s[f / a.gs]));
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[q] = ((bits >> q) & 1u) ? s : -s;
+      } else {
+        const uint32_t word = reinterpret_cast<const uint32_t*>(a.emb_w)[f >> 3];
+        const float s = u16_to_f32<BF16S>(a.emb_s[f / a.gs]);
+        const float bb = u16_to_f32<BF16S>(a.emb_b[f / a.gs]);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          v[q] = __fadd_rn(__fmul_rn(s, (float)((word >> (4 * q)) & 0xFu)), bb);
+          if (a.bf16r) v[q] = bf16_trunc(v[q]);
+        }
+      }
+      float4* o4 = reinterpret_cast<float4*>(out0 + (size_t)r * a.H + 8 * d8);
+      o4[0] = make_float4(v[0], v[1], v[2], v[3]);
+      o4[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+  }
+  grid_zero(resv(a, 1), (size_t)a.batch * a.H, c);
+  grid_zero(a.qkv_acc, (size_t)a.batch * (a.n_q + 2 * a.n_kv) * a.hd, c);
+  grid_zero(a.gu_acc, (size_t)a.batch * 2 * a.I, c);
+}
+
+template <int FMT, int NT, bool BF16S, int HD>
+__global__ void __launch_bounds__(kQmvThreads) mega_kernel(MegaArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  Ctx c;
+  c.a = &a;
+  c.layers = a.layers;
+  c.smem = smem;
+  c.S = mega_layout(a, FMT);
+  c.cta = blockIdx.x;
+  c.G = gridDim.x;
+  c.seg = seg_bytes(FMT, a.gs);
+  c.warp = threadIdx.x >> 5;
+  c.lane = threadIdx.x & 31;
+  c.k = 0;
+  c.failed = false;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + c.S.bars);
+  uint64_t* abars = reinterpret_cast<uint64_t*>(smem + c.S.abars);
+  if (c.lane == 0) {
+    for (int s = 0; s < kMaxSlots; ++s) mbar_init(&bars[c.warp * kMaxSlots + s], 1);
+    if (threadIdx.x == 0)
+      for (int s = 0; s < kAttStages; ++s) mbar_init(&abars[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  unsigned int gen;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(gen) : "l"(&a.bar[1]) : "memory");
+  // start this warp's weight stream
+  if (c.lane == 0) {
+    c.pph = 0; c.pu = c.cta; c.pgl = c.warp;
+    prod_normalize(c);
+    for (uint32_t s = 0; s < a.nslot; ++s) prod_issue(c, s);
+  }
+  uint32_t ause[kAttStages] = {0, 0};
+  const uint32_t last = 1 + 5 * a.L;
+  for (uint32_t ph = 0; ph <= last; ++ph) {
+    const PhaseInfo p = phase_info(a, c.layers, ph);
+    switch (p.type) {
+      case PH_EMBED:
+        embed_phase<FMT, BF16S>(c);
+        break;
+      case PH_ATT:
+        for (uint32_t u = c.cta; u < p.units; u += c.G) att_unit<HD>(c, p, u, ause);
+        break;
+      case PH_GU:
+        grid_zero(a.qkv_acc, (size_t)a.batch * (a.n_q + 2 * a.n_kv) * a.hd, c);
+        for (uint32_t u = c.cta; u < p.units; u += c.G) qmv_unit<FMT, NT, 2, BF16S>(c, p, u);
+        break;
+      default:
+        if (p.type == PH_QKV) grid_zero(a.gu_acc, (size_t)a.batch * 2 * a.I, c);
+        if (p.type == PH_O) grid_zero(resv(a, 2 * p.layer + 2), (size_t)a.batch * a.H, c);
+        if (p.type == PH_DN) grid_zero(resv(a, 2 * p.layer + 3), (size_t)a.batch * a.H, c);
+        for (uint32_t u = c.cta; u < p.units; u += c.G) qmv_unit<FMT, NT, 1, BF16S>(c, p, u);
+        break;
+    }
+    if (ph < last) grid_sync(a.bar, c.G, gen, a.err);
+  }
+}
+
+template <int FMT, int NT, bool BF16S, int HD>
+cudaError_t launch_t(const MegaArgs& a, uint32_t grid, uint32_t smem, cudaStream_t st, bool prepare) {
+  auto* fn = &mega_kernel<FMT, NT, BF16S, HD>;
+  if (prepare) return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kQmvThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fn, a);
+}
+
+template <int FMT, int NT, bool BF16S, int HD>
+int occupancy_t(uint32_t smem) {
+  int n = 0;
+  if (cudaFuncSetAttribute(&mega_kernel<FMT, NT, BF16S, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           smem) != cudaSuccess)
+    return 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, &mega_kernel<FMT, NT, BF16S, HD>, kQmvThreads,
+                                                    smem) != cudaSuccess)
+    return 0;
+  return n;
+}
+
+// Calls f.operator()<FMT, NT, BF16S, HD>() for a supported combination and
+// returns true, else returns false.
+template <typename F>
+bool dispatch(int fmt, int nt, int bf16s, uint32_t hd, F&& f) {
+#define NNZ_MEGA_CASE(FM, N, B, H) \
+  if (fmt == FM && nt == N && bf16s == B && hd == H) { f.template operator()<FM, N, (bool)B, H>(); return true; }
+  NNZ_MEGA_CASE(FMT_Q1, 1, 0, 128) NNZ_MEGA_CASE(FMT_Q1, 2, 0, 128)
+  NNZ_MEGA_CASE(FMT_Q1, 1, 0, 64) NNZ_MEGA_CASE(FMT_Q1, 2, 0, 64)
+  NNZ_MEGA_CASE(FMT_Q4, 1, 0, 128) NNZ_MEGA_CASE(FMT_Q4, 2, 0, 128)
+  NNZ_MEGA_CASE(FMT_Q4, 1, 1, 128) NNZ_MEGA_CASE(FMT_Q4, 2, 1, 128)
+  NNZ_MEGA_CASE(FMT_Q4, 1, 0, 64) NNZ_MEGA_CASE(FMT_Q4, 2, 0, 64)
+  NNZ_MEGA_CASE(FMT_Q4, 1, 1, 64) NNZ_MEGA_CASE(FMT_Q4, 2, 1, 64)
+#undef NNZ_MEGA_CASE
+  return false;
+}
+
+}  // namespace
+
+bool mega_plan(MegaArgs& a, int fmt, int bf16s, int device, uint32_t* grid, uint32_t* smem) {
+  if (a.batch == 0 || a.batch > (uint32_t)kBatchChunk || a.bf16r || (a.hd != 64 && a.hd != 128) ||
+      a.n_q / a.n_kv > (uint32_t)kAttMaxG)
+    return false;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return false;
+  const int nt = a.batch > 4 ? 2 : 1;
+  const uint32_t qd = a.n_q * a.hd;
+  for (int occ_try = 2; occ_try >= 1; --occ_try) {
+    const uint32_t G = (uint32_t)(sms * occ_try);
+    auto pick = [&](uint32_t M, uint32_t K) {
+      const uint32_t tiles = num_tiles(M), groups = K / a.gs;
+      uint32_t ks = (G + tiles - 1) / tiles;
+      const uint32_t mx = groups / kQmvWarps ? groups / kQmvWarps : 1;
+      return ks < 1 ? 1u : ks > mx ? mx : ks;
+    };
+    a.ks_qkv = pick(qd + 2 * a.n_kv * a.hd, a.H);
+    a.ks_o = pick(a.H, qd);
+    a.ks_gu = pick(a.I, a.H);
+    a.ks_dn = pick(a.H, a.I);
+    uint32_t sp = G / (a.n_kv * a.batch);
+    a.att_splits = sp < 1 ? 1 : sp > 32 ? 32 : sp;
+    for (uint32_t ns = kMaxSlots; ns >= 2; --ns) {
+      a.nslot = ns;
+      const MegaSmem S = mega_layout(a, fmt);
+      const uint32_t budget = occ_try == 2 ? 112u * 1024u : 220u * 1024u;
+      if (S.total > budget) continue;
+      int occ = 0;
+      dispatch(fmt, nt, bf16s, a.hd, [&]<int F, int N, bool B, int H>() { occ = occupancy_t<F, N, B, H>(S.total); });
+      if (occ >= occ_try) {
+        *grid = G;
+        *smem = S.total;
+        return true;
+      }
+    }
+  }
+  return false;
+}
+
+cudaError_t mega_launch(const MegaArgs& a, int fmt, int bf16s, uint32_t grid, uint32_t smem, cudaStream_t st) {
+  const int nt = a.batch > 4 ? 2 : 1;
+  cudaError_t e = cudaErrorInvalidValue;
+  dispatch(fmt, nt, bf16s, a.hd, [&]<int F, int N, bool B, int H>() { e = launch_t<F, N, B, H>(a, grid, smem, st, false); });
+  return e;
+}
+
+}  // namespace nnz

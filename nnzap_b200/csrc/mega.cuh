@@ -1,0 +1,51 @@
+// Persistent decode kernel: one cooperative launch runs a whole decode step
+// (embedding, every decoder layer, final norm + LM head + argmax) for up to
+// 8 rows.  Replaces the reference's per-token command buffer of ~172
+// dispatches (nnmetal/src/transformer.zig:2566-2930, 4072-4123).
+#pragma once
+#include "misc.cuh"
+#include "qmv_dev.cuh"
+
+namespace nnz {
+
+struct MegaLayer {
+  const uint8_t *qkv, *o, *gu, *down;
+  const float *attn_norm, *ffn_norm, *q_norm, *k_norm;
+};
+
+struct MegaArgs {
+  uint32_t H, I, n_q, n_kv, hd, L, vocab, gs, max_ctx, batch;
+  float eps, theta;
+  int rope_style, bf16r;
+  const MegaLayer* layers;      // device array [L]
+  const uint8_t* lm;            // packed LM head
+  const float* fnorm;
+  const uint8_t* emb_w;         // embedding, reference layout
+  const uint16_t* emb_s;
+  const uint16_t* emb_b;
+  __half* kc;                   // K cache base [L][slots][n_kv][max_ctx][hd]
+  __half* vc;
+  size_t kv_layer;              // elements per layer per cache
+  float* R;                     // 3 rotating residual buffers [3][batch][H]
+  float* qkv_acc;               // [batch][(n_q + 2 n_kv) hd]
+  float* gu_acc;                // [batch][2][I]
+  float* att_ws;                // attention split partials
+  uint32_t att_splits;
+  uint32_t ks_qkv, ks_o, ks_gu, ks_dn;   // K splits per phase
+  DecodeState* st;
+  uint32_t* seq;
+  uint32_t seq_len;
+  float* logits;                // optional [batch][vocab]
+  unsigned int* bar;            // [0] arrival count, [1] generation
+  int* err;
+  uint32_t nslot;               // weight-ring slots per warp
+};
+
+// Launch (cooperative) with the grid / shared memory chosen by mega_plan.
+cudaError_t mega_launch(const MegaArgs& a, int fmt, int bf16s, uint32_t grid, uint32_t smem,
+                        cudaStream_t st);
+// Host-side plan: grid size, smem size, splits.  Returns false if the
+// kernel cannot be co-resident on this device.
+bool mega_plan(MegaArgs& a, int fmt, int bf16s, int device, uint32_t* grid, uint32_t* smem);
+
+}  // namespace nnz

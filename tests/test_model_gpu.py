@@ -31,10 +31,21 @@ def oracle_cfg(d):
                  scale_dtype=d.scale_dtype, bf16_faithful=d.bf16_faithful)
 
 
-def build(d, seed=0, max_ctx=256, max_batch=4):
+def build(d, seed=0, max_ctx=256, max_batch=4, path="persistent"):
+    """path: "persistent" (one cooperative kernel per decode step, the default)
+    or "graph" (the captured multi-kernel CUDA graph)."""
+    import os
     W = synth.make_model(d, seed=seed)
-    m = Model(config_from_dims(d, max_context_length=max_ctx, max_batch=max_batch))
-    m.load_weights(synth.iter_named_tensors(W))
+    old = os.environ.get("NNZ_DECODE_PATH")
+    os.environ["NNZ_DECODE_PATH"] = path
+    try:
+        m = Model(config_from_dims(d, max_context_length=max_ctx, max_batch=max_batch))
+        m.load_weights(synth.iter_named_tensors(W))
+    finally:
+        if old is None:
+            os.environ.pop("NNZ_DECODE_PATH")
+        else:
+            os.environ["NNZ_DECODE_PATH"] = old
     return m, W
 
 
@@ -48,10 +59,11 @@ def greedy_ok(cfg, W, prompt, toks, tol=2e-2):
     return exact
 
 
+@pytest.mark.parametrize("path", ["persistent", "graph"])
 @pytest.mark.parametrize("d", [SMALL_Q1, SMALL_Q4, SMALL_Q4_ENGINE, SMALL_HALF],
                          ids=["q1", "q4", "q4_engine_bf16", "q1_half_split_hd64"])
-def test_forward_decode_logits(cuda, built_lib, d):
-    m, W = build(d)
+def test_forward_decode_logits(cuda, built_lib, d, path):
+    m, W = build(d, path=path)
     cfg = oracle_cfg(d)
     rng = np.random.default_rng(1)
     seq = rng.integers(0, d.vocab, 12)
@@ -84,9 +96,10 @@ def test_prefill_matches_decode_and_oracle(cuda, built_lib, d):
     m.free()
 
 
+@pytest.mark.parametrize("path", ["persistent", "graph"])
 @pytest.mark.parametrize("d", [SMALL_Q1, SMALL_Q4], ids=["q1", "q4"])
-def test_generate_greedy(cuda, built_lib, d):
-    m, W = build(d)
+def test_generate_greedy(cuda, built_lib, d, path):
+    m, W = build(d, path=path)
     cfg = oracle_cfg(d)
     prompt = list(np.random.default_rng(3).integers(0, d.vocab, 20))
     res = generate(m, GenerateOpts(prompt_ids=prompt, max_new=24))
@@ -100,9 +113,10 @@ def test_generate_greedy(cuda, built_lib, d):
     m.free()
 
 
-def test_batched_decode_rows_independent(cuda, built_lib):
+@pytest.mark.parametrize("path", ["persistent", "graph"])
+def test_batched_decode_rows_independent(cuda, built_lib, path):
     d = SMALL_Q1
-    m, W = build(d, max_batch=6)
+    m, W = build(d, max_batch=6, path=path)
     rng = np.random.default_rng(4)
     toks = rng.integers(0, d.vocab, 6)
     pos = np.array([0, 0, 0, 0, 0, 0])
@@ -150,10 +164,11 @@ def test_layer_step_config2_q4(cuda, built_lib):
     m.free()
 
 
-def test_full_bonsai_q1_generate(cuda, built_lib):
+@pytest.mark.parametrize("path", ["persistent", "graph"])
+def test_full_bonsai_q1_generate(cuda, built_lib, path):
     """BASELINE config 3 shape (28 layers, vocab 151936), short run."""
     d = synth.BONSAI_1_7B_Q1
-    m, W = build(d, max_ctx=1024, max_batch=1)
+    m, W = build(d, max_ctx=1024, max_batch=1, path=path)
     cfg = oracle_cfg(d)
     prompt = list(np.random.default_rng(0).integers(0, d.vocab, 64))
     res = generate(m, GenerateOpts(prompt_ids=prompt, max_new=8))
