@@ -428,6 +428,7 @@ int sync_check(nnz_model* m) {
   NNZ_CK(cudaMemcpy(&flags, m->err, 4, cudaMemcpyDeviceToHost));
   if (flags) {
     cudaMemset(m->err, 0, 4);
+    if (m->mbar) cudaMemset(m->mbar, 0, 64);   // clear a persistent-kernel abort
     return fail(flags & (ERR_MBAR_TIMEOUT | ERR_SPIN_TIMEOUT) ? NNZ_ETIMEDOUT : NNZ_EDEVICE,
                 err_text(flags));
   }

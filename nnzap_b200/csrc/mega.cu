@@ -138,6 +138,16 @@ __host__ __device__ inline MegaSmem mega_layout(const MegaArgs& a, int fmt) {
 // Grid barrier over all CTAs (co-resident by cooperative launch).  Bounded:
 // after kSpinLimit polls it records ERR_SPIN_TIMEOUT and lets the CTA run
 // on (results are then garbage, but every CTA terminates).
+constexpr uint32_t kGridSpinLimit = 1u << 20;
+
+__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// bar[0] arrivals, bar[1] generation, bar[2] sticky abort flag: once any
+// wait of the launch times out, every other wait gives up immediately.
 __device__ __forceinline__ void grid_sync(unsigned int* bar, unsigned int nblocks, unsigned int& gen,
                                           int* err) {
   __syncthreads();
@@ -150,17 +160,30 @@ __device__ __forceinline__ void grid_sync(unsigned int* bar, unsigned int nblock
       atomicAdd(&bar[1], 1u);
     } else {
       uint32_t i = 0;
-      while (true) {
-        unsigned int g;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(&bar[1]) : "memory");
-        if (g != gen) break;
-        if (++i > kSpinLimit) { atomicOr(err, ERR_SPIN_TIMEOUT); break; }
+      while (ld_acquire(&bar[1]) == gen) {
+        if (ld_acquire(&bar[2])) break;
+        if (++i > kGridSpinLimit) {
+          atomicOr(err, ERR_SPIN_TIMEOUT);
+          atomicExch(&bar[2], 1u);
+          break;
+        }
       }
     }
     __threadfence();
   }
   gen += 1;
   __syncthreads();
+}
+
+// Bounded mbarrier wait that also gives up once the launch has aborted.
+__device__ __forceinline__ bool mbar_wait_abort(uint64_t* bar, uint32_t parity, int* err,
+                                                const unsigned int* abort_flag) {
+  for (uint32_t i = 0; i < kGridSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && ld_acquire(abort_flag)) return false;
+  }
+  atomicOr(err, ERR_MBAR_TIMEOUT);
+  return false;
 }
 
 struct Ctx {
@@ -321,7 +344,7 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u) {
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + c.S.bars);
   for (uint32_t gl = c.warp; gl < ng; gl += kQmvWarps) {
     const uint32_t slot = c.k % a.nslot;
-    if (!c.failed) c.failed = !mbar_wait(&bars[c.warp * kMaxSlots + slot], (c.k / a.nslot) & 1u, a.err);
+    if (!c.failed) c.failed = !mbar_wait_abort(&bars[c.warp * kMaxSlots + slot], (c.k / a.nslot) & 1u, a.err, &a.bar[2]);
     const uint8_t* sb = sm + c.S.ring + (size_t)(c.warp * a.nslot + slot) * c.S.slot_bytes;
     qmv_group<FMT, NT, SUB, BF16S>(sb, c.seg, xf, gl, cpg, gsx, gsum, gsq, y);
     __syncwarp();
@@ -488,7 +511,7 @@ __device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause
     const __half* kr = kring + (size_t)stg * kAttBlk * HD;
     const __half* vr = vring + (size_t)stg * kAttBlk * HD;
     if (!is_new) {
-      if (!c.failed) c.failed = !mbar_wait(&abars[stg], ause[stg] & 1u, a.err);
+      if (!c.failed) c.failed = !mbar_wait_abort(&abars[stg], ause[stg] & 1u, a.err, &a.bar[2]);
       ause[stg] += 1;
     }
     for (int t = warp; t < n; t += kQmvWarps) {
