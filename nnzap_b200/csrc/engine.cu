@@ -200,6 +200,7 @@ struct nnz_model {
   MegaLayer* mlayers = nullptr;
   float *mR = nullptr, *mqkv = nullptr, *mgu = nullptr, *matt = nullptr;
   unsigned int* mbar = nullptr;
+  unsigned long long* mprof = nullptr;    // NNZ_MEGA_PROFILE=1: per-phase timestamps
   struct MegaPlan { MegaArgs a; uint32_t grid, smem; bool ok; };
   std::map<uint32_t, MegaPlan> mplans;
   std::vector<cudaEvent_t> events;
@@ -455,7 +456,25 @@ const nnz_model::MegaPlan* mega_plan_for(nnz_model* m, uint32_t rows) {
   a.emb_w = m->emb_w; a.emb_s = m->emb_s; a.emb_b = m->emb_b; a.kc = m->kc; a.vc = m->vc;
   a.kv_layer = m->kv_layer; a.R = m->mR; a.qkv_acc = m->mqkv; a.gu_acc = m->mgu; a.att_ws = m->matt;
   a.st = m->state; a.seq = m->seq; a.seq_len = c.max_context_length; a.logits = nullptr;
-  a.bar = m->mbar; a.err = m->err;
+  a.bar = m->mbar; a.err = m->err; a.prof = m->mprof;
+  {
+    const LayerW& W0 = m->L[0];
+    a.l0 = MegaLayer{W0.qkv, W0.o, W0.gu, W0.down, W0.attn_norm, W0.ffn_norm, W0.q_norm, W0.k_norm};
+    a.lstride = c.num_layers > 1 ? (size_t)(m->L[1].qkv - W0.qkv) : 0;
+    for (uint32_t l = 0; l < c.num_layers; ++l) {   // layers must be equally spaced
+      const LayerW& W = m->L[l];
+      const size_t d = (size_t)l * a.lstride;
+      auto same = [&](const void* x, const void* x0) {
+        return reinterpret_cast<const uint8_t*>(x) == reinterpret_cast<const uint8_t*>(x0) + d;
+      };
+      if (!same(W.qkv, W0.qkv) || !same(W.o, W0.o) || !same(W.gu, W0.gu) || !same(W.down, W0.down) ||
+          !same(W.attn_norm, W0.attn_norm) || !same(W.ffn_norm, W0.ffn_norm) ||
+          !same(W.q_norm, W0.q_norm) || !same(W.k_norm, W0.k_norm)) {
+        m->mplans[rows] = P;   // ok = false
+        return nullptr;
+      }
+    }
+  }
   P.ok = mega_plan(a, m->fmt, m->bf16s, m->device, &P.grid, &P.smem);
   m->mplans[rows] = P;
   return P.ok ? &m->mplans[rows] : nullptr;
@@ -754,6 +773,10 @@ int nnz_model_finalize(nnz_model* m) {
       if ((rc = dalloc(m, (void**)&m->mgu, (size_t)bmax * 2 * I * 4))) return rc;
       if ((rc = dalloc(m, (void**)&m->matt, (size_t)bmax * c.num_kv_heads * 32 * G * (c.head_dim + 2) * 4))) return rc;
       if ((rc = dalloc(m, (void**)&m->mbar, 64))) return rc;
+      const char* prof = getenv("NNZ_MEGA_PROFILE");
+      if (prof && prof[0] == '1') {
+        if ((rc = dalloc(m, (void**)&m->mprof, 8 * (2 * (2 + 5 * c.num_layers) + 64)))) return rc;
+      }
       if ((rc = dalloc(m, (void**)&m->mlayers, sizeof(MegaLayer) * c.num_layers))) return rc;
       NNZ_CK(cudaMemset(m->mbar, 0, 64));
       std::vector<MegaLayer> ml(c.num_layers);
@@ -1148,6 +1171,21 @@ int nnz_attn_decode(const void* qkv, const float* q_norm, const float* k_norm, v
       (size_t)rows * n_kv > w->n_counters)
     return fail(NNZ_EINVAL, "nnz_attn_decode: problem too large for the shared workspace");
   NNZ_CK(attn_decode_launch(a, (int)head_dim, 0, (cudaStream_t)stream));
+  return NNZ_OK;
+}
+
+// Development aid (not part of the documented ABI): per-phase timestamps of
+// the last persistent-kernel launch when the model was finalized with
+// NNZ_MEGA_PROFILE=1; out receives 2 * n entries (phase end, barrier exit).
+int nnz_debug_mega_profile(nnz_model* m, uint64_t* out, uint32_t n, uint32_t* grid) {
+  if (!m || !out || !m->mprof) return fail(NNZ_ESTATE, "profiling not enabled");
+  NNZ_CK(cudaStreamSynchronize(m->st));
+  const uint32_t nph = 2 + 5 * m->c.num_layers;
+  NNZ_CK(cudaMemcpy(out, m->mprof, 8 * (2 * std::min(n, nph) + (n > nph ? 64 : 0)), cudaMemcpyDeviceToHost));
+  if (grid) {
+    auto it = m->mplans.find(1);
+    *grid = it != m->mplans.end() ? it->second.grid : 0;
+  }
   return NNZ_OK;
 }
 

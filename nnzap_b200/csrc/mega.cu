@@ -39,12 +39,19 @@ constexpr int kMaxSlots = 4;
 constexpr int kAttBlk = 32;
 constexpr int kAttStages = 2;
 constexpr int kAttMaxG = 8;
+constexpr int kMaxAttSplits = 16;
+constexpr int kMaxHeadsPerUnit = 32;
 
 struct PhaseInfo {
   int type;
   uint32_t layer, M, K, tiles, ks, groups, sub, units;
   const uint8_t* w;
 };
+
+template <typename T>
+__host__ __device__ __forceinline__ const T* lptr(const MegaArgs& a, const T* p0, uint32_t l) {
+  return reinterpret_cast<const T*>(reinterpret_cast<const uint8_t*>(p0) + (size_t)l * a.lstride);
+}
 
 __host__ __device__ inline PhaseInfo phase_info(const MegaArgs& a, const MegaLayer* layers,
                                                 uint32_t ph) {
@@ -60,11 +67,11 @@ __host__ __device__ inline PhaseInfo phase_info(const MegaArgs& a, const MegaLay
     p.layer = l;
     const uint32_t qd = a.n_q * a.hd, kvd = a.n_kv * a.hd;
     switch (r) {
-      case 0: p.type = PH_QKV; p.w = layers ? layers[l].qkv : nullptr; p.M = qd + 2 * kvd; p.K = a.H; p.ks = a.ks_qkv; break;
+      case 0: p.type = PH_QKV; p.w = lptr(a, a.l0.qkv, l); p.M = qd + 2 * kvd; p.K = a.H; p.ks = a.ks_qkv; break;
       case 1: p.type = PH_ATT; p.units = a.n_kv * a.batch * a.att_splits; return p;
-      case 2: p.type = PH_O; p.w = layers ? layers[l].o : nullptr; p.M = a.H; p.K = qd; p.ks = a.ks_o; break;
-      case 3: p.type = PH_GU; p.w = layers ? layers[l].gu : nullptr; p.M = a.I; p.K = a.H; p.ks = a.ks_gu; p.sub = 2; break;
-      default: p.type = PH_DN; p.w = layers ? layers[l].down : nullptr; p.M = a.H; p.K = a.I; p.ks = a.ks_dn; break;
+      case 2: p.type = PH_O; p.w = lptr(a, a.l0.o, l); p.M = a.H; p.K = qd; p.ks = a.ks_o; break;
+      case 3: p.type = PH_GU; p.w = lptr(a, a.l0.gu, l); p.M = a.I; p.K = a.H; p.ks = a.ks_gu; p.sub = 2; break;
+      default: p.type = PH_DN; p.w = lptr(a, a.l0.down, l); p.M = a.H; p.K = a.I; p.ks = a.ks_dn; break;
     }
   }
   p.tiles = num_tiles(p.M);
@@ -77,14 +84,14 @@ __host__ __device__ inline void unit_range(const PhaseInfo& p, uint32_t u, uint3
                                            uint32_t* G0, uint32_t* ng) {
   *tile = u / p.ks;
   *split = u % p.ks;
-  const uint32_t g0 = (uint32_t)((uint64_t)p.groups * (*split) / p.ks);
-  const uint32_t g1 = (uint32_t)((uint64_t)p.groups * (*split + 1) / p.ks);
+  const uint32_t g0 = p.groups * (*split) / p.ks;     // groups * ks < 2^32
+  const uint32_t g1 = p.groups * (*split + 1) / p.ks;
   *G0 = g0;
   *ng = g1 - g0;
 }
 
 struct MegaSmem {
-  uint32_t bars, abars, ring, slot_bytes, u, xs, xf, gsx, gsum, gsq, red, rms, flag,
+  uint32_t tmpl, bars, abars, ring, slot_bytes, u, xs, xf, gsx, gsum, gsq, red, rms, flag, mw,
       kring, vring, qs, knew, vnew, ss, stat, tok, total, kr_max, ng_max, bcm, nt;
 };
 
@@ -105,23 +112,30 @@ __host__ __device__ inline MegaSmem mega_layout(const MegaArgs& a, int fmt) {
   s.ng_max = krm / gs;
   s.slot_bytes = 2 * seg_bytes(fmt, gs);
   uint32_t o = 0;
+  s.tmpl = o; o += 6 * sizeof(PhaseInfo);
+  o = (o + 15) & ~15u;
   s.bars = o; o += kQmvWarps * kMaxSlots * 8;
   s.abars = o; o += kAttStages * 8;
   o = (o + 127) & ~127u;
   s.ring = o; o += kQmvWarps * a.nslot * s.slot_bytes;
   o = (o + 127) & ~127u;
+  // quantized-x fragments persist across phases (zeroed once per launch)
+  s.xf = o; o += (krm / kChunk) * s.nt * 256;
+  s.gsx = o; o += s.ng_max * kBatchChunk * 4;
+  s.gsum = o; o += s.ng_max * kBatchChunk * 4;
+  s.gsq = o; o += s.ng_max * kBatchChunk * 4;
+  o = (o + 127) & ~127u;
   s.u = o;
   // matvec view of the union
   uint32_t q = o;
   s.xs = q; q += ((krm * s.bcm * 2) + 15) & ~15u;
-  s.xf = q; q += (krm / kChunk) * s.nt * 256;
-  s.gsx = q; q += s.ng_max * kBatchChunk * 4;
-  s.gsum = q; q += s.ng_max * kBatchChunk * 4;
-  s.gsq = q; q += s.ng_max * kBatchChunk * 4;
   s.red = q; q += kQmvWarps * 2 * kTileRows * s.bcm * 4;
   s.rms = q; q += kBatchChunk * 4;
   s.flag = q; q += 16;
   s.tok = q; q += kBatchChunk * 4;
+  // full residual rows for the one-round-trip RMSNorm (small batches only)
+  // attention merge weights [b][head in range][split] (m, l -> weight)
+  s.mw = q; q += s.bcm * kMaxHeadsPerUnit * kMaxAttSplits * 2 * 4;
   // attention view of the union
   uint32_t t = o;
   s.kring = t; t += kAttStages * kAttBlk * a.hd * 2;
@@ -146,6 +160,12 @@ __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
   return v;
 }
 
+__device__ __forceinline__ unsigned int ld_relaxed(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // bar[0] arrivals, bar[1] generation, bar[2] sticky abort flag: once any
 // wait of the launch times out, every other wait gives up immediately.
 __device__ __forceinline__ void grid_sync(unsigned int* bar, unsigned int nblocks, unsigned int& gen,
@@ -159,14 +179,17 @@ __device__ __forceinline__ void grid_sync(unsigned int* bar, unsigned int nblock
       __threadfence();
       atomicAdd(&bar[1], 1u);
     } else {
+      // poll with relaxed loads and a short sleep (spinning CTAs must not
+      // flood the barrier's L2 slice); one fence after release
       uint32_t i = 0;
-      while (ld_acquire(&bar[1]) == gen) {
-        if (ld_acquire(&bar[2])) break;
+      while (ld_relaxed(&bar[1]) == gen) {
+        if (ld_relaxed(&bar[2])) break;
         if (++i > kGridSpinLimit) {
           atomicOr(err, ERR_SPIN_TIMEOUT);
           atomicExch(&bar[2], 1u);
           break;
         }
+        __nanosleep(40);
       }
     }
     __threadfence();
@@ -180,7 +203,7 @@ __device__ __forceinline__ bool mbar_wait_abort(uint64_t* bar, uint32_t parity, 
                                                 const unsigned int* abort_flag) {
   for (uint32_t i = 0; i < kGridSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 255u && ld_acquire(abort_flag)) return false;
+    if ((i & 255u) == 255u && ld_relaxed(abort_flag)) return false;
   }
   atomicOr(err, ERR_MBAR_TIMEOUT);
   return false;
@@ -188,9 +211,10 @@ __device__ __forceinline__ bool mbar_wait_abort(uint64_t* bar, uint32_t parity, 
 
 struct Ctx {
   const MegaArgs* a;
+  const PhaseInfo* tmpl;   // smem: layer-0 templates of QKV, ATT, O, GU, DN, and LM
   const MegaLayer* layers;
   uint8_t* smem;
-  MegaSmem S;
+  const MegaSmem* S;       // smem copy of the layout
   uint32_t cta, G, seg;
   int warp, lane;
   // consumer item counter and producer cursor (lane 0 of each warp)
@@ -199,11 +223,25 @@ struct Ctx {
   bool failed;
 };
 
+// Phase geometry from the shared-memory templates: no divisions by runtime
+// values beyond the layer index, no global loads.
+__device__ __forceinline__ PhaseInfo phase_at(const Ctx& c, uint32_t ph) {
+  const uint32_t last = 1 + 5 * c.a->L;
+  if (ph == 0) { PhaseInfo p{}; p.type = PH_EMBED; return p; }
+  if (ph > last) { PhaseInfo p{}; p.type = PH_END; return p; }
+  if (ph == last) return c.tmpl[5];
+  const uint32_t l = (ph - 1) / 5;
+  PhaseInfo p = c.tmpl[(ph - 1) - 5 * l];
+  p.layer = l;
+  if (p.w) p.w += (size_t)l * c.a->lstride;
+  return p;
+}
+
 // Advance the producer cursor to the next weight segment of this warp.
 __device__ __forceinline__ void prod_normalize(Ctx& c) {
   const uint32_t last = 1 + 5 * c.a->L;
   while (c.pph <= last) {
-    const PhaseInfo p = phase_info(*c.a, c.layers, c.pph);
+    const PhaseInfo p = phase_at(c, c.pph);
     if (p.type == PH_EMBED || p.type == PH_ATT || c.pu >= p.units) {
       ++c.pph; c.pu = c.cta; c.pgl = c.warp;
       continue;
@@ -218,15 +256,15 @@ __device__ __forceinline__ void prod_normalize(Ctx& c) {
 // Issue the producer's current segment into slot `slot` and advance.
 __device__ __forceinline__ void prod_issue(Ctx& c, uint32_t slot) {
   if (c.pph > 1 + 5 * c.a->L) return;
-  const PhaseInfo p = phase_info(*c.a, c.layers, c.pph);
+  const PhaseInfo p = phase_at(c, c.pph);
   uint32_t tile, split, G0, ng;
   unit_range(p, c.pu, &tile, &split, &G0, &ng);
   const uint32_t bytes = p.sub * c.seg;
   const uint8_t* src = p.w + ((size_t)tile * p.groups + G0 + c.pgl) * bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(c.smem + c.S.bars);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(c.smem + c.S->bars);
   uint64_t* bar = &bars[c.warp * kMaxSlots + slot];
   mbar_arrive_expect_tx(bar, bytes);
-  bulk_g2s(c.smem + c.S.ring + (size_t)(c.warp * c.a->nslot + slot) * c.S.slot_bytes, src, bytes, bar);
+  bulk_g2s(c.smem + c.S->ring + (size_t)(c.warp * c.a->nslot + slot) * c.S->slot_bytes, src, bytes, bar);
   c.pgl += kQmvWarps;
   prod_normalize(c);
 }
@@ -243,36 +281,37 @@ __device__ __forceinline__ void grid_zero(float* p, size_t n, const Ctx& c) {
 // ---- prologues -------------------------------------------------------------
 
 // O phase: merge the attention splits of the heads in [K0, K0+Kr) into fp16.
-__device__ void stage_attn(const Ctx& c, uint32_t K0, uint32_t Kr, uint32_t bc, __half* xs) {
+// Each thread owns (row, element) pairs and issues every load it needs --
+// the S (m, l) pairs of the element's head and its S partial outputs --
+// before using any, so the merge costs one round trip per pass.
+__device__ __forceinline__ void stage_attn(const Ctx& c, uint32_t K0, uint32_t Kr, uint32_t bc, __half* xs) {
   const MegaArgs& a = *c.a;
   const uint32_t G = a.n_q / a.n_kv, S = a.att_splits, rec = a.hd + 2;
   for (uint32_t j = threadIdx.x; j < bc * Kr; j += blockDim.x) {
     const uint32_t b = j / Kr, k = K0 + j % Kr;
-    const uint32_t h = k / a.hd, d = k % a.hd;
-    const uint32_t kvh = h / G, hg = h % G;
-    const float* base = a.att_ws + ((size_t)(b * a.n_kv + kvh) * S) * G * rec + (size_t)hg * rec;
-    float M = -INFINITY, Ls = 0.f, o = 0.f;
-    for (uint32_t s0 = 0; s0 < S; s0 += 8) {
-      float mv[8], lv[8], ov[8];
+    const uint32_t h = k / a.hd, d = k % a.hd, kvh = h / G, hg = h % G;
+    const float* base = a.att_ws + (((size_t)(b * a.n_kv + kvh) * S) * G + hg) * rec;
+    const size_t sstride = (size_t)G * rec;
+    float mv[kMaxAttSplits], lv[kMaxAttSplits], ov[kMaxAttSplits];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const bool ok = s0 + q < S;
-        const float* r = base + (size_t)(s0 + q) * G * rec;
-        mv[q] = ok ? __ldcg(r) : -INFINITY;
-        lv[q] = ok ? __ldcg(r + 1) : 0.f;
-        ov[q] = ok ? __ldcg(r + 2 + d) : 0.f;
-      }
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        if (mv[q] == -INFINITY) continue;
-        const float nm = fmaxf(M, mv[q]);
-        const float a0 = (M == -INFINITY) ? 0.f : expf(M - nm), a1 = expf(mv[q] - nm);
-        Ls = Ls * a0 + lv[q] * a1;
-        o = o * a0 + ov[q] * a1;
-        M = nm;
-      }
+    for (int q = 0; q < kMaxAttSplits; ++q) {
+      const bool ok = (uint32_t)q < S;
+      const float* r = base + q * sstride;
+      mv[q] = ok ? __ldcg(r) : -INFINITY;
+      lv[q] = ok ? __ldcg(r + 1) : 0.f;
+      ov[q] = ok ? __ldcg(r + 2 + d) : 0.f;
     }
-    xs[(size_t)b * Kr + (k - K0)] = __float2half_rn(o / Ls);
+    float M = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < kMaxAttSplits; ++q) M = fmaxf(M, mv[q]);
+    float L = 0.f, o = 0.f;
+#pragma unroll
+    for (int q = 0; q < kMaxAttSplits; ++q) {
+      const float w = mv[q] == -INFINITY ? 0.f : expf(mv[q] - M);
+      L = fmaf(w, lv[q], L);
+      o = fmaf(w, ov[q], o);
+    }
+    xs[j] = __float2half_rn(o / L);
   }
 }
 
@@ -303,36 +342,53 @@ __device__ void stage_silu(const Ctx& c, uint32_t K0, uint32_t Kr, uint32_t bc, 
 }
 
 // ---- one matvec work unit ------------------------------------------------------
-template <int FMT, int NT, int SUB, bool BF16S>
-__device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u) {
+__device__ __forceinline__ void stamp(const Ctx& c, const PhaseInfo& p, uint32_t u, int i) {
   const MegaArgs& a = *c.a;
+  if (!a.prof || c.cta != 0 || threadIdx.x != 0 || u != 0 || p.layer != 1) return;
+  const int which = p.type == PH_QKV ? 0 : p.type == PH_O ? 1 : p.type == PH_GU ? 2 : p.type == PH_DN ? 3 : -1;
+  if (which < 0) return;
+  a.prof[2 * (2 + 5 * a.L) + 8 * which + i] = clock64();
+}
+
+template <int FMT, int NT, int SUB, bool BF16S>
+__device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue = true) {
+  const MegaArgs& a = *c.a;
+  stamp(c, p, u, 0);
   uint32_t tile, split, G0, ng;
   unit_range(p, u, &tile, &split, &G0, &ng);
   const uint32_t gs = a.gs, cpg = gs / kChunk, K0 = G0 * gs, Kr = ng * gs;
-  const uint32_t bc = c.S.bcm;
+  const uint32_t bc = c.S->bcm;
   uint8_t* sm = c.smem;
-  __half* xs = reinterpret_cast<__half*>(sm + c.S.xs);
-  uint8_t* xf = sm + c.S.xf;
-  float* gsx = reinterpret_cast<float*>(sm + c.S.gsx);
-  float* gsum = reinterpret_cast<float*>(sm + c.S.gsum);
-  int* gsq = reinterpret_cast<int*>(sm + c.S.gsq);
-  float* red = reinterpret_cast<float*>(sm + c.S.red);
-  float* rms = reinterpret_cast<float*>(sm + c.S.rms);
+  __half* xs = reinterpret_cast<__half*>(sm + c.S->xs);
+  uint8_t* xf = sm + c.S->xf;
+  float* gsx = reinterpret_cast<float*>(sm + c.S->gsx);
+  float* gsum = reinterpret_cast<float*>(sm + c.S->gsum);
+  int* gsq = reinterpret_cast<int*>(sm + c.S->gsq);
+  float* red = reinterpret_cast<float*>(sm + c.S->red);
+  float* rms = reinterpret_cast<float*>(sm + c.S->rms);
 
-  // prologue: this unit's slice of x
-  if (p.type == PH_QKV || p.type == PH_GU || p.type == PH_LM) {
+  // prologue: this unit's slice of x (the LM head's x is the same for all
+  // of a CTA's units, so the caller runs it once)
+  if (!prologue) {
+  } else if (p.type == PH_QKV || p.type == PH_GU || p.type == PH_LM) {
     const uint32_t v = p.type == PH_QKV ? 2 * p.layer : p.type == PH_GU ? 2 * p.layer + 1 : 2 * a.L;
-    const float* nw = p.type == PH_QKV ? c.layers[p.layer].attn_norm
-                    : p.type == PH_GU ? c.layers[p.layer].ffn_norm : a.fnorm;
+    const float* nw = p.type == PH_QKV ? lptr(a, a.l0.attn_norm, p.layer)
+                    : p.type == PH_GU ? lptr(a, a.l0.ffn_norm, p.layer) : a.fnorm;
     const float* res = resv(a, v);
-    block_rms(res, a.H, a.H, bc, a.eps, rms);
-    stage_norm(res, a.H, nw, rms, K0, Kr, bc, a.bf16r != 0, xs);
+    if (bc * a.H <= 2048u) {
+      stage_norm_fast(res, a.H, a.H, nw, a.eps, K0, Kr, bc, a.bf16r != 0, rms, xs);
+    } else {
+      block_rms(res, a.H, a.H, bc, a.eps, rms);
+      stage_norm(res, a.H, nw, rms, K0, Kr, bc, a.bf16r != 0, xs);
+    }
   } else if (p.type == PH_O) {
     stage_attn(c, K0, Kr, bc, xs);
   } else {
     stage_silu(c, K0, Kr, bc, xs);
   }
-  quantize_xs<NT>(xs, Kr, bc, ng, gs, xf, gsx, gsum, gsq);
+  stamp(c, p, u, 1);
+  if (prologue) quantize_xs<NT>(xs, Kr, bc, ng, gs, xf, gsx, gsum, gsq, false);
+  stamp(c, p, u, 2);
 
   float y[SUB][NT][16];
 #pragma unroll
@@ -341,17 +397,19 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u) {
     for (int n = 0; n < NT; ++n)
 #pragma unroll
       for (int v = 0; v < 16; ++v) y[s][n][v] = 0.f;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + c.S.bars);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + c.S->bars);
   for (uint32_t gl = c.warp; gl < ng; gl += kQmvWarps) {
     const uint32_t slot = c.k % a.nslot;
     if (!c.failed) c.failed = !mbar_wait_abort(&bars[c.warp * kMaxSlots + slot], (c.k / a.nslot) & 1u, a.err, &a.bar[2]);
-    const uint8_t* sb = sm + c.S.ring + (size_t)(c.warp * a.nslot + slot) * c.S.slot_bytes;
+    if (gl == (uint32_t)c.warp) stamp(c, p, u, 6);
+    const uint8_t* sb = sm + c.S->ring + (size_t)(c.warp * a.nslot + slot) * c.S->slot_bytes;
     qmv_group<FMT, NT, SUB, BF16S>(sb, c.seg, xf, gl, cpg, gsx, gsum, gsq, y);
     __syncwarp();
     if (c.lane == 0) prod_issue(c, slot);
     ++c.k;
   }
 
+  stamp(c, p, u, 3);
   // CTA reduction: red[warp][sub*128 + row][b]
   const int g = c.lane >> 2, t = c.lane & 3;
   const uint32_t nrow = kTileRows * SUB;
@@ -366,6 +424,7 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u) {
         if (b < bc) rw[(s * kTileRows + y_row<FMT>(v, g)) * bc + b] = y[s][n][v];
       }
   __syncthreads();
+  stamp(c, p, u, 4);
   const uint32_t nv = nrow * bc;
   const uint32_t qd = a.n_q * a.hd, qkv_rows = qd + 2 * a.n_kv * a.hd;
   if (p.type == PH_LM) {
@@ -412,6 +471,7 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u) {
     }
   }
   __syncthreads();
+  stamp(c, p, u, 5);
 }
 
 // ---- attention work unit -----------------------------------------------------
@@ -426,14 +486,14 @@ __device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause
   const uint32_t S = a.att_splits, G = a.n_q / a.n_kv;
   const uint32_t kvh = u % a.n_kv, b = (u / a.n_kv) % a.batch, split = u / (a.n_kv * a.batch);
   uint8_t* sm = c.smem;
-  uint64_t* abars = reinterpret_cast<uint64_t*>(sm + c.S.abars);
-  __half* kring = reinterpret_cast<__half*>(sm + c.S.kring);
-  __half* vring = reinterpret_cast<__half*>(sm + c.S.vring);
-  float* qs = reinterpret_cast<float*>(sm + c.S.qs);
-  float* knew = reinterpret_cast<float*>(sm + c.S.knew);
-  float* vnew = reinterpret_cast<float*>(sm + c.S.vnew);
-  float* ss = reinterpret_cast<float*>(sm + c.S.ss);
-  float* mst = reinterpret_cast<float*>(sm + c.S.stat);
+  uint64_t* abars = reinterpret_cast<uint64_t*>(sm + c.S->abars);
+  __half* kring = reinterpret_cast<__half*>(sm + c.S->kring);
+  __half* vring = reinterpret_cast<__half*>(sm + c.S->vring);
+  float* qs = reinterpret_cast<float*>(sm + c.S->qs);
+  float* knew = reinterpret_cast<float*>(sm + c.S->knew);
+  float* vnew = reinterpret_cast<float*>(sm + c.S->vnew);
+  float* ss = reinterpret_cast<float*>(sm + c.S->ss);
+  float* mst = reinterpret_cast<float*>(sm + c.S->stat);
   float* lst = mst + kAttMaxG;
   float* alp = lst + kAttMaxG;
   const int warp = c.warp, lane = c.lane;
@@ -467,8 +527,8 @@ __device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause
 
   const uint32_t qkv_rows = (a.n_q + 2 * a.n_kv) * HD;
   const float* qrow = a.qkv_acc + (size_t)b * qkv_rows;
-  const float* qn = c.layers[p.layer].q_norm;
-  const float* kn = c.layers[p.layer].k_norm;
+  const float* qn = lptr(a, a.l0.q_norm, p.layer);
+  const float* kn = lptr(a, a.l0.k_norm, p.layer);
   for (uint32_t h = warp; h < G; h += kQmvWarps) {
     float v[EPL];
     norm_rope_head<HD>(qrow + (size_t)(kvh * G + h) * HD, qn, a.eps, a.theta, a.rope_style, pos, lane, v);
@@ -574,7 +634,7 @@ __device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause
 template <int FMT, bool BF16S>
 __device__ void embed_phase(Ctx& c) {
   const MegaArgs& a = *c.a;
-  uint32_t* tok_s = reinterpret_cast<uint32_t*>(c.smem + c.S.tok);
+  uint32_t* tok_s = reinterpret_cast<uint32_t*>(c.smem + c.S->tok);
   if (c.cta == 0) {
     if (threadIdx.x < a.batch) {
       const uint32_t r = threadIdx.x;
@@ -629,13 +689,16 @@ __device__ void embed_phase(Ctx& c) {
 }
 
 template <int FMT, int NT, bool BF16S, int HD>
-__global__ void __launch_bounds__(kQmvThreads) mega_kernel(MegaArgs a) {
+__global__ void __launch_bounds__(kQmvThreads) mega_kernel(const __grid_constant__ MegaArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   Ctx c;
   c.a = &a;
   c.layers = a.layers;
   c.smem = smem;
-  c.S = mega_layout(a, FMT);
+  __shared__ MegaSmem s_layout;
+  if (threadIdx.x == 0) s_layout = mega_layout(a, FMT);
+  __syncthreads();
+  c.S = &s_layout;
   c.cta = blockIdx.x;
   c.G = gridDim.x;
   c.seg = seg_bytes(FMT, a.gs);
@@ -643,8 +706,13 @@ __global__ void __launch_bounds__(kQmvThreads) mega_kernel(MegaArgs a) {
   c.lane = threadIdx.x & 31;
   c.k = 0;
   c.failed = false;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + c.S.bars);
-  uint64_t* abars = reinterpret_cast<uint64_t*>(smem + c.S.abars);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + c.S->bars);
+  uint64_t* abars = reinterpret_cast<uint64_t*>(smem + c.S->abars);
+  PhaseInfo* tm = reinterpret_cast<PhaseInfo*>(smem + c.S->tmpl);
+  c.tmpl = tm;
+  if (threadIdx.x < 6) tm[threadIdx.x] = phase_info(a, nullptr, threadIdx.x < 5 ? 1 + threadIdx.x : 1 + 5 * a.L);
+  for (uint32_t i = threadIdx.x; i < (c.S->u - c.S->xf) / 4; i += blockDim.x)
+    reinterpret_cast<uint32_t*>(smem + c.S->xf)[i] = 0;
   if (c.lane == 0) {
     for (int s = 0; s < kMaxSlots; ++s) mbar_init(&bars[c.warp * kMaxSlots + s], 1);
     if (threadIdx.x == 0)
@@ -663,7 +731,7 @@ __global__ void __launch_bounds__(kQmvThreads) mega_kernel(MegaArgs a) {
   uint32_t ause[kAttStages] = {0, 0};
   const uint32_t last = 1 + 5 * a.L;
   for (uint32_t ph = 0; ph <= last; ++ph) {
-    const PhaseInfo p = phase_info(a, c.layers, ph);
+    const PhaseInfo p = phase_at(c, ph);
     switch (p.type) {
       case PH_EMBED:
         embed_phase<FMT, BF16S>(c);
@@ -675,6 +743,14 @@ __global__ void __launch_bounds__(kQmvThreads) mega_kernel(MegaArgs a) {
         grid_zero(a.qkv_acc, (size_t)a.batch * (a.n_q + 2 * a.n_kv) * a.hd, c);
         for (uint32_t u = c.cta; u < p.units; u += c.G) qmv_unit<FMT, NT, 2, BF16S>(c, p, u);
         break;
+      case PH_LM: {
+        bool first = true;
+        for (uint32_t u = c.cta; u < p.units; u += c.G) {
+          qmv_unit<FMT, NT, 1, BF16S>(c, p, u, first);
+          first = false;
+        }
+        break;
+      }
       default:
         if (p.type == PH_QKV) grid_zero(a.gu_acc, (size_t)a.batch * 2 * a.I, c);
         if (p.type == PH_O) grid_zero(resv(a, 2 * p.layer + 2), (size_t)a.batch * a.H, c);
@@ -682,7 +758,18 @@ __global__ void __launch_bounds__(kQmvThreads) mega_kernel(MegaArgs a) {
         for (uint32_t u = c.cta; u < p.units; u += c.G) qmv_unit<FMT, NT, 1, BF16S>(c, p, u);
         break;
     }
+    if (a.prof && c.cta == 0 && threadIdx.x == 0) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      a.prof[2 * ph] = t;
+      if (ph == 0 || ph == last) a.prof[2 * (2 + 5 * a.L) + 40 + (ph == 0 ? 0 : 1)] = clock64();
+    }
     if (ph < last) grid_sync(a.bar, c.G, gen, a.err);
+    if (a.prof && c.cta == 0 && threadIdx.x == 0) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      a.prof[2 * ph + 1] = t;
+    }
   }
 }
 
@@ -735,6 +822,7 @@ bool dispatch(int fmt, int nt, int bf16s, uint32_t hd, F&& f) {
 
 bool mega_plan(MegaArgs& a, int fmt, int bf16s, int device, uint32_t* grid, uint32_t* smem) {
   if (a.batch == 0 || a.batch > (uint32_t)kBatchChunk || a.bf16r || (a.hd != 64 && a.hd != 128) ||
+      a.n_q > (uint32_t)kMaxHeadsPerUnit ||
       a.n_q / a.n_kv > (uint32_t)kAttMaxG)
     return false;
   int sms = 0;
@@ -743,18 +831,20 @@ bool mega_plan(MegaArgs& a, int fmt, int bf16s, int device, uint32_t* grid, uint
   const uint32_t qd = a.n_q * a.hd;
   for (int occ_try = 2; occ_try >= 1; --occ_try) {
     const uint32_t G = (uint32_t)(sms * occ_try);
+    // as many units as CTAs, down to one scale group per unit: the phase
+    // latency is the per-unit latency
     auto pick = [&](uint32_t M, uint32_t K) {
       const uint32_t tiles = num_tiles(M), groups = K / a.gs;
-      uint32_t ks = (G + tiles - 1) / tiles;
-      const uint32_t mx = groups / kQmvWarps ? groups / kQmvWarps : 1;
-      return ks < 1 ? 1u : ks > mx ? mx : ks;
+      const uint32_t ks = G / tiles;               // units <= CTAs
+      return ks < 1 ? 1u : ks > groups ? groups : ks;
     };
     a.ks_qkv = pick(qd + 2 * a.n_kv * a.hd, a.H);
     a.ks_o = pick(a.H, qd);
     a.ks_gu = pick(a.I, a.H);
     a.ks_dn = pick(a.H, a.I);
-    uint32_t sp = G / (a.n_kv * a.batch);
-    a.att_splits = sp < 1 ? 1 : sp > 32 ? 32 : sp;
+    // splits of at most 64 positions (two streamed blocks), up to 16
+    const uint32_t sp = (a.max_ctx + 63) / 64;
+    a.att_splits = sp < 1 ? 1 : sp > (uint32_t)kMaxAttSplits ? (uint32_t)kMaxAttSplits : sp;
     for (uint32_t ns = kMaxSlots; ns >= 2; --ns) {
       a.nslot = ns;
       const MegaSmem S = mega_layout(a, fmt);

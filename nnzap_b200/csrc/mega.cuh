@@ -17,7 +17,9 @@ struct MegaArgs {
   uint32_t H, I, n_q, n_kv, hd, L, vocab, gs, max_ctx, batch;
   float eps, theta;
   int rope_style, bf16r;
-  const MegaLayer* layers;      // device array [L]
+  const MegaLayer* layers;      // device array [L] (unused on the hot path)
+  MegaLayer l0;                 // layer 0 pointers; layer l = l0 + l * lstride bytes
+  size_t lstride;
   const uint8_t* lm;            // packed LM head
   const float* fnorm;
   const uint8_t* emb_w;         // embedding, reference layout
@@ -39,6 +41,7 @@ struct MegaArgs {
   unsigned int* bar;            // [0] arrival count, [1] generation
   int* err;
   uint32_t nslot;               // weight-ring slots per warp
+  unsigned long long* prof;     // optional: CTA 0 records %globaltimer after each phase
 };
 
 // Launch (cooperative) with the grid / shared memory chosen by mega_plan.

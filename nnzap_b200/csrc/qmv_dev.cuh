@@ -83,6 +83,61 @@ __device__ __forceinline__ void stage_norm(const float* res, uint32_t stride, co
   }
 }
 
+// Small batches (bc * K <= 2048 floats): one round trip.  Every thread
+// loads its float4s of the full rows plus the matching norm weights of the
+// slice [K0, K0 + Kr), reduces the sum of squares through registers and a
+// shared-memory atomic per warp and row, then normalises its own slice
+// elements in registers.  rms holds kBatchChunk floats.
+__device__ __forceinline__ void stage_norm_fast(const float* res, uint32_t stride, uint32_t K,
+                                                const float* norm_w, float eps, uint32_t K0, uint32_t Kr,
+                                                uint32_t bc, bool bf16r, float* rms, __half* xs) {
+  constexpr int kItems = 4;
+  const int lane = threadIdx.x & 31;
+  const uint32_t q4 = K / 4, n4 = bc * q4;
+  if (threadIdx.x < kBatchChunk) rms[threadIdx.x] = 0.f;
+  float4 v[kItems], w[kItems];
+#pragma unroll
+  for (int u = 0; u < kItems; ++u) {
+    const uint32_t j = threadIdx.x + u * kQmvThreads;
+    const uint32_t k = 4 * (j % q4);
+    v[u] = j < n4 ? __ldcg(reinterpret_cast<const float4*>(res + (size_t)(j / q4) * stride + k))
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (j < n4 && k >= K0 && k < K0 + Kr) w[u] = *reinterpret_cast<const float4*>(norm_w + k);
+  }
+  float ssr[kBatchChunk];
+#pragma unroll
+  for (int bb = 0; bb < kBatchChunk; ++bb) ssr[bb] = 0.f;
+#pragma unroll
+  for (int u = 0; u < kItems; ++u) {
+    const uint32_t b = (threadIdx.x + u * kQmvThreads) / q4;
+    const float e = v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+#pragma unroll
+    for (int bb = 0; bb < kBatchChunk; ++bb) ssr[bb] += (b == (uint32_t)bb) ? e : 0.f;
+  }
+  __syncthreads();   // rms zeroed
+#pragma unroll
+  for (int bb = 0; bb < kBatchChunk; ++bb) {
+    if ((uint32_t)bb >= bc) break;
+    const float t = warp_sum(ssr[bb]);
+    if (lane == 0) atomicAdd(&rms[bb], t);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int u = 0; u < kItems; ++u) {
+    const uint32_t j = threadIdx.x + u * kQmvThreads;
+    const uint32_t b = j / q4, k = 4 * (j % q4);
+    if (j < n4 && k >= K0 && k < K0 + Kr) {
+      const float rr = rsqrtf(rms[b] / (float)K + eps);
+      float o0 = v[u].x * rr * w[u].x, o1 = v[u].y * rr * w[u].y;
+      float o2 = v[u].z * rr * w[u].z, o3 = v[u].w * rr * w[u].w;
+      if (bf16r) { o0 = bf16_trunc(o0); o1 = bf16_trunc(o1); o2 = bf16_trunc(o2); o3 = bf16_trunc(o3); }
+      __half2* dst = reinterpret_cast<__half2*>(xs + (size_t)b * Kr + (k - K0));
+      dst[0] = __floats2half2_rn(o0, o1);
+      dst[1] = __floats2half2_rn(o2, o3);
+    }
+  }
+}
+
 // xs[b][k - K0] = x_b[k] (fp16 input, 16-byte aligned rows).  No trailing sync.
 __device__ __forceinline__ void stage_f16(const __half* xh, uint32_t stride, uint32_t K0, uint32_t Kr,
                                           uint32_t bc, __half* xs) {
@@ -105,16 +160,20 @@ __device__ __forceinline__ void stage_f16(const __half* xh, uint32_t stride, uin
 // Per (row, group): exact fixed-point split of the staged fp16 x into int8
 // hi/lo B fragments (xf), the group scale 2^(E-14) (gsx), sum(x) (gsum) and
 // sum(q) (gsq).  Zeroes xf/gsx/gsum/gsq itself.  Syncs at start and end.
+// With zero = false the caller guarantees xf/gsx/gsum/gsq were zeroed once
+// and only ever rewritten at the same (row < bc) positions.
 template <int NT>
 __device__ __forceinline__ void quantize_xs(const __half* xs, uint32_t Kr, uint32_t bc, uint32_t ng,
                                             uint32_t gs, uint8_t* xf, float* gsx, float* gsum,
-                                            int* gsq) {
+                                            int* gsq, bool zero = true) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t cpg = gs / kChunk;
-  const uint32_t xf_words = ng * cpg * NT * 64;
-  for (uint32_t i = threadIdx.x; i < xf_words; i += kQmvThreads) reinterpret_cast<uint32_t*>(xf)[i] = 0;
-  for (uint32_t i = threadIdx.x; i < ng * kBatchChunk; i += kQmvThreads) {
-    gsx[i] = 0.f; gsum[i] = 0.f; gsq[i] = 0;
+  if (zero) {
+    const uint32_t xf_words = ng * cpg * NT * 64;
+    for (uint32_t i = threadIdx.x; i < xf_words; i += kQmvThreads) reinterpret_cast<uint32_t*>(xf)[i] = 0;
+    for (uint32_t i = threadIdx.x; i < ng * kBatchChunk; i += kQmvThreads) {
+      gsx[i] = 0.f; gsum[i] = 0.f; gsq[i] = 0;
+    }
   }
   __syncthreads();
   {
@@ -134,14 +193,16 @@ __device__ __forceinline__ void quantize_xs(const __half* xs, uint32_t Kr, uint3
       }
       amax = warp_max(amax);
       sumx = warp_sum(sumx);
-      int E = 0;
-      if (amax > 0.f) frexpf(amax, &E);
+      // amax = m * 2^E, m in [0.5, 1): E from the exponent field (amax is a
+      // normal fp16 value or 0); scale 2^(14-E) built from its bits (exact).
+      const int E = (amax > 0.f) ? (int)((__float_as_uint(amax) >> 23) & 0xFFu) - 126 : 0;
+      const float up = __uint_as_float((uint32_t)(127 + 14 - E) << 23);
       int qsum = 0;
       const uint32_t nt = b >> 2, ncol = 2 * (b & 3);
 #pragma unroll
       for (uint32_t m = 0; m < 8; ++m) {
         if (m < per_lane) {
-          const int q = (amax > 0.f) ? __float2int_rn(ldexpf(xv[m], 14 - E)) : 0;
+          const int q = (amax > 0.f) ? __float2int_rn(xv[m] * up) : 0;
           qsum += q;
           const int lo = ((q + 128) & 255) - 128;
           const int hi = (q - lo) >> 8;
@@ -155,7 +216,7 @@ __device__ __forceinline__ void quantize_xs(const __half* xs, uint32_t Kr, uint3
       }
       for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
       if (lane == 0) {
-        gsx[gl * kBatchChunk + b] = (amax > 0.f) ? ldexpf(1.f, E - 14) : 0.f;
+        gsx[gl * kBatchChunk + b] = (amax > 0.f) ? __uint_as_float((uint32_t)(127 + E - 14) << 23) : 0.f;
         gsum[gl * kBatchChunk + b] = sumx;
         gsq[gl * kBatchChunk + b] = qsum;
       }

@@ -91,7 +91,9 @@ def test_prefill_matches_decode_and_oracle(cuda, built_lib, d):
     for p, tok in enumerate(prompt):
         m.forward_decode([tok], [p])
     k_dec, v_dec = m.read_kv(0, 0, len(prompt))
-    np.testing.assert_array_equal(v_pre, v_dec)
+    # same fp16 values up to one rounding step: prefill and the persistent decode
+    # kernel sum the projection's split-K partials in different orders
+    np.testing.assert_allclose(v_pre.astype(np.float32), v_dec.astype(np.float32), atol=2e-3, rtol=2e-3)
     np.testing.assert_allclose(k_pre.astype(np.float32), k_dec.astype(np.float32), atol=2e-3, rtol=2e-3)
     m.free()
 
