@@ -165,6 +165,22 @@ int nnz_unpack_weights(int fmt, const void* packed, uint32_t M, uint32_t K, uint
 /* All asynchronous on `stream` (a cudaStream_t, NULL = default stream).
  * They share a per-device workspace allocated on first use. */
 
+/* nnz_qmv without any device allocation, for callers that cannot allocate
+ * device memory once running (a host that gave the whole device memory
+ * budget to its own pool at start-up, or work issued while another thread
+ * captures a CUDA graph).  No counterpart in the reference: it exists only
+ * for such callers.  Same arguments, results and tolerance as nnz_qmv, but
+ * the split-K scratch is a fixed array compiled into the library (8 MiB of
+ * partial sums + 64 KiB of counters, held on every GPU that loads the
+ * library until exit); problems that need more return NNZ_EINVAL.  All calls
+ * share that array: calls that overlap on the GPU race, so issue them on one
+ * stream.  The first call on a device does one-time set-up (device
+ * addresses of the array, kernel attributes); make it before any stream
+ * capture starts on that device. */
+int nnz_qmv_noalloc(int fmt, int scale_dtype, int bf16_round, const void* packed, uint32_t M,
+                    uint32_t K, uint32_t gs, const void* x, uint32_t x_stride, uint32_t batch,
+                    void* out, uint32_t out_stride, int out_kind, void* stream);
+
 /* Dequantize a packed matrix to f32 [M][K] (bit-exact weight check).
  * Reference dequant: transformer_test.zig:286-321 (Q1), model.zig:969-1026 (Q4). */
 int nnz_dequant(int fmt, int scale_dtype, const void* packed, uint32_t M, uint32_t K, uint32_t gs,

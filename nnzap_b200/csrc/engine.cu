@@ -161,6 +161,11 @@ std::string err_text(int flags) {
 
 }  // namespace
 
+namespace nnz {
+// Lets other translation units of the library set nnz_last_error()'s text.
+void set_last_error(const std::string& msg) { g_err = msg; }
+}  // namespace nnz
+
 struct nnz_model {
   nnz_config c{};
   int device = 0;
