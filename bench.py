@@ -112,8 +112,12 @@ def algorithmic_bytes_per_token(d, ctx):
 
 
 def launches_per_step(d, prompt, gen, chunk=64):
+    """Our kernels launched per generate(): chunked prefill (embed, 6 per
+    layer, LM head) plus one persistent kernel per decode token (or the
+    1 + 5 L + 1 kernels of the CUDA-graph path)."""
     chunks = -(-prompt // chunk)
-    return chunks * (1 + d.layers * 6) + 1 + gen * (1 + d.layers * 5 + 1)
+    per_tok = (1 + d.layers * 5 + 1) if os.environ.get("NNZ_DECODE_PATH") == "graph" else 1
+    return chunks * (1 + d.layers * 6) + 1 + gen * per_tok
 
 
 def oracle_cfg(d):
@@ -317,9 +321,15 @@ def main():
                    "l2": "inputs larger than L2: 242 MB of weights streamed per token"},
         "prefill_tok_per_sec": prefill_tps, "decode_p50_us": p50, "decode_p99_us": p99,
         "load_ms": load_ms, "prompt_tokens": PROMPT, "measured_tokens": GEN * args.steps,
-        "roofline": {"bound": "hbm", "kernel": "decode step (one CUDA graph replay per token)",
+        "roofline": {"bound": "hbm",
+                     "kernel": ("decode step: CUDA graph" if os.environ.get("NNZ_DECODE_PATH") == "graph"
+                                else "decode step: persistent cooperative kernel mega_kernel"),
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": peak_kind, "traffic": None,
+                     "peak_kind": peak_kind,
+                     # ncu dram__bytes of one persistent decode launch at ctx 66
+                     # (profiles/decode_persistent_bonsai_q1.md), scaled to the
+                     # mean context by the KV bytes it adds
+                     "traffic": 260e6 + d.layers * 2 * d.n_kv * (mean_ctx - 66) * d.head_dim * 2,
                      "algorithmic_bytes_per_token": bytes_tok},
         "qmv_config0": {"us": q0_us, "achieved_gbs": q0_gbs, "frac": q0_gbs / hbm,
                         "algorithmic_bytes": q0_bytes},
