@@ -211,6 +211,16 @@ int nnz_lm_head_argmax(int fmt, int scale_dtype, int bf16_round, const void* pac
 int nnz_mlp(int fmt, int scale_dtype, int bf16_round, const void* gate_up, const void* down,
             uint32_t hidden, uint32_t inter, uint32_t gs, const void* x, uint32_t batch,
             float* out, void* stream);
+/* Prefill GEMM on the tcgen05 tensor cores: out[m][n] (+)= sum_k x[m][k] *
+ * W[n][k] for m < M, n < N, with W in the reference's flat layout (Q1 bits +
+ * fp16 scales, or Q4 words + scales + biases; metal.zig:235-469) and x fp16
+ * [M][K] (16-byte aligned, K % 64 == 0, gs >= 64).  out_kind NNZ_OUT_F16 or
+ * NNZ_OUT_F32_ADD (row stride N).  No reference counterpart: the reference
+ * prefills token by token (transformer.zig:4032-4068). */
+int nnz_prefill_gemm(int fmt, int scale_dtype, const void* w, const uint16_t* scales,
+                     const uint16_t* biases, uint32_t M, uint32_t K, uint32_t N, uint32_t gs,
+                     const void* x, void* out, int out_kind, void* stream);
+
 /* GQA decode attention with fused QK-norm + RoPE + KV write
  * (gqa_attention_fused_f16io_tg, transformer.metal:1467-1695).
  * qkv fp16 [rows][(n_q + 2 n_kv) hd]; caches fp16 [slots][n_kv][max_ctx][hd];

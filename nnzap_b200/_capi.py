@@ -78,6 +78,7 @@ SIGNATURES = [
     ("nnz_qmv_norm", I32, [I32, I32, I32, P, U32, U32, U32, P, P, F32, U32, P, U32, I32, P]),
     ("nnz_lm_head_argmax", I32, [I32, I32, I32, P, U32, U32, U32, P, P, F32, U32, P, P, P]),
     ("nnz_mlp", I32, [I32, I32, I32, P, P, U32, U32, U32, P, U32, P, P]),
+    ("nnz_prefill_gemm", I32, [I32, I32, P, P, P, U32, U32, U32, U32, P, P, I32, P]),
     ("nnz_attn_decode", I32, [P, P, P, P, P, U32, P, U32, U32, U32, U32, F32, F32, I32, U32, P, P]),
 ]
 

@@ -20,6 +20,7 @@
 
 #include "../../include/nnz_b200.h"
 #include "attn.cuh"
+#include "gemm.cuh"
 #include "mega.cuh"
 #include "misc.cuh"
 #include "packing.h"
@@ -42,7 +43,8 @@ int fail(int code, const std::string& msg) {
     if (e_ != cudaSuccess) return fail(NNZ_ECUDA, std::string(#x) + ": " + cudaGetErrorString(e_)); \
   } while (0)
 
-constexpr uint32_t kPrefillChunk = 64;
+constexpr uint32_t kPrefillChunk = 64;        // chunked-matvec prefill
+constexpr uint32_t kGemmPrefillChunk = 512;    // tcgen05 GEMM prefill
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -96,7 +98,15 @@ struct HostTensor {
   std::vector<uint8_t> data;
 };
 
+// Weights of one matrix in the reference's flat layout (prefill GEMM operand).
+struct FlatW {
+  const uint8_t* w = nullptr;
+  const uint16_t* s = nullptr;
+  const uint16_t* b = nullptr;
+};
+
 struct LayerW {
+  FlatW fqkv, fo, fgate, fup, fdown;
   uint8_t *qkv, *o, *gu, *down;
   float *attn_norm, *ffn_norm, *q_norm, *k_norm;
 };
@@ -185,6 +195,9 @@ struct nnz_model {
   __half *kc = nullptr, *vc = nullptr;
   size_t kv_layer = 0;  // elements per layer per cache
   float* residual = nullptr;
+  __half* xn = nullptr;          // fp16 RMSNorm output [rows_max][max(H, ...)] (GEMM prefill)
+  bool gemm_prefill = false;
+  uint8_t* flat = nullptr;       // flat weight copies for the GEMM prefill
   __half *qkv = nullptr, *attn = nullptr, *h = nullptr;
   float* logits = nullptr;
   float* ws = nullptr;
@@ -305,6 +318,22 @@ int get_norm(nnz_model* m, const std::string& name, uint32_t n, std::vector<floa
   } else {
     return fail(NNZ_EINVAL, name + ": norm weights must be f32/f16/bf16");
   }
+  return NNZ_OK;
+}
+
+// Device copy of a matrix in the reference's flat layout (prefill GEMM).
+int upload_flat(nnz_model* m, const std::vector<uint8_t>& w, const std::vector<uint16_t>& s,
+                const std::vector<uint16_t>& b, FlatW* out) {
+  const size_t wb = align_up(w.size(), 256), sb = align_up(s.size() * 2, 256), bb = b.size() * 2;
+  uint8_t* p = nullptr;
+  int rc = dalloc(m, (void**)&p, wb + sb + std::max<size_t>(bb, 16));
+  if (rc) return rc;
+  NNZ_CK(cudaMemcpy(p, w.data(), w.size(), cudaMemcpyHostToDevice));
+  NNZ_CK(cudaMemcpy(p + wb, s.data(), s.size() * 2, cudaMemcpyHostToDevice));
+  if (bb) NNZ_CK(cudaMemcpy(p + wb + sb, b.data(), bb, cudaMemcpyHostToDevice));
+  out->w = p;
+  out->s = reinterpret_cast<const uint16_t*>(p + wb);
+  out->b = bb ? reinterpret_cast<const uint16_t*>(p + wb + sb) : nullptr;
   return NNZ_OK;
 }
 
@@ -501,8 +530,54 @@ int run_step(nnz_model* m, uint32_t rows, bool want_logits) {
   return NNZ_OK;
 }
 
+int gemm(nnz_model* m, const FlatW& W, const FlatW* W2, uint32_t N, uint32_t K, const __half* x,
+         uint32_t rows, int epi, void* out, uint32_t ldo) {
+  GemmArgs g{};
+  g.M = rows; g.K = K; g.N = N; g.fmt = m->fmt; g.gs = m->c.group_size; g.bf16s = m->bf16s;
+  g.bf16r = m->bf16r; g.w = W.w; g.s = W.s; g.b = W.b;
+  if (W2) { g.w2 = W2->w; g.s2 = W2->s; g.b2 = W2->b; }
+  g.epi = epi; g.out = out; g.ldo = ldo; g.err = m->err;
+  NNZ_CK(gemm_launch(g, x, m->st));
+  return NNZ_OK;
+}
+
+// Prefill of prompt rows [c0, c0 + rows) on the tensor cores: per layer
+// RMSNorm -> QKV GEMM -> K/V write + causal attention -> O GEMM (+residual)
+// -> RMSNorm -> gate/up GEMM (SiLU*up) -> down GEMM (+residual).
+int enqueue_layer_gemm(nnz_model* m, uint32_t l, uint32_t rows, const int* pos) {
+  const nnz_config& c = m->c;
+  const LayerW& W = m->L[l];
+  const uint32_t H = c.hidden_size, I = c.intermediate_size;
+  int rc;
+  NNZ_CK(rmsnorm_f16_launch(m->residual, W.attn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st));
+  if ((rc = gemm(m, W.fqkv, nullptr, m->qkv_rows, H, m->xn, rows, GEPI_F16, m->qkv, m->qkv_rows))) return rc;
+  if ((rc = kv_write(m, l, rows, pos, m->zeros, 0))) return rc;
+  if ((rc = attn(m, l, rows, pos, m->zeros, 0, 0))) return rc;
+  if ((rc = gemm(m, W.fo, nullptr, H, m->qd, m->attn, rows, GEPI_RESADD, m->residual, H))) return rc;
+  NNZ_CK(rmsnorm_f16_launch(m->residual, W.ffn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st));
+  if ((rc = gemm(m, W.fgate, &W.fup, I, H, m->xn, rows, GEPI_SILU, m->h, I))) return rc;
+  if ((rc = gemm(m, W.fdown, nullptr, H, I, m->h, rows, GEPI_RESADD, m->residual, H))) return rc;
+  return NNZ_OK;
+}
+
 int enqueue_prefill(nnz_model* m, uint32_t n, bool want_logits) {
   int rc;
+  if (m->gemm_prefill) {
+    for (uint32_t c0 = 0; c0 < n; c0 += kGemmPrefillChunk) {
+      const uint32_t rows = std::min(kGemmPrefillChunk, n - c0);
+      if ((rc = enqueue_embed(m, rows, m->prompt + c0, 0))) return rc;
+      for (uint32_t l = 0; l < m->c.num_layers; ++l)
+        if ((rc = enqueue_layer_gemm(m, l, rows, m->iota + c0))) return rc;
+      if (c0 + rows == n) {
+        const float* last = m->residual + (size_t)(rows - 1) * m->c.hidden_size;
+        if ((rc = qmv(m, 1, PRO_NORM, EPI_LOGITS, m->lm, m->c.vocab_size, m->c.hidden_size, last,
+                      m->c.hidden_size, m->fnorm, 1, nullptr, 0, want_logits ? m->logits : nullptr,
+                      m->state->argmax, 0)))
+          return rc;
+      }
+    }
+    return NNZ_OK;
+  }
   for (uint32_t c0 = 0; c0 < n; c0 += kPrefillChunk) {
     const uint32_t rows = std::min(kPrefillChunk, n - c0);
     if ((rc = enqueue_embed(m, rows, m->prompt + c0, 0))) return rc;
@@ -612,7 +687,12 @@ int nnz_model_finalize(nnz_model* m) {
   m->kvd = c.num_kv_heads * c.head_dim;
   m->qkv_rows = m->qd + 2 * m->kvd;
   m->slots = c.max_batch;
-  m->rows_max = std::max(c.max_batch, kPrefillChunk);
+  {
+    const char* pp = getenv("NNZ_PREFILL_PATH");
+    m->gemm_prefill = !(pp && strcmp(pp, "qmv") == 0) && gs >= 64 && H % 64 == 0 &&
+                      I % 64 == 0 && (c.num_query_heads * c.head_dim) % 64 == 0;
+  }
+  m->rows_max = std::max(c.max_batch, m->gemm_prefill ? kGemmPrefillChunk : kPrefillChunk);
   const int fmt = m->fmt;
 
   // ---- pack weights on the host ----------------------------------------
@@ -654,22 +734,27 @@ int nnz_model_finalize(nnz_model* m) {
         sc.insert(sc.end(), s.begin(), s.end());
         bc.insert(bc.end(), b.begin(), b.end());
       }
+      if (m->gemm_prefill && (rc = upload_flat(m, wc, sc, bc, &m->L[l].fqkv))) return rc;
       buf.assign(b_qkv, 0);
       pack_host(fmt, wc.data(), sc.data(), bc.empty() ? nullptr : bc.data(), m->qkv_rows, H, gs, 1, 0,
                 buf.data(), 0);
       NNZ_CK(cudaMemcpy(m->arena + lo[l].qkv, buf.data(), b_qkv, cudaMemcpyHostToDevice));
     }
     if ((rc = get_proj(m, pre + "self_attn.o_proj", H, m->qd, w, s, b))) return rc;
+    if (m->gemm_prefill && (rc = upload_flat(m, w, s, b, &m->L[l].fo))) return rc;
     buf.assign(b_o, 0);
     pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), H, m->qd, gs, 1, 0, buf.data(), 0);
     NNZ_CK(cudaMemcpy(m->arena + lo[l].o, buf.data(), b_o, cudaMemcpyHostToDevice));
     buf.assign(b_gu, 0);
     if ((rc = get_proj(m, pre + "mlp.gate_proj", I, H, w, s, b))) return rc;
+    if (m->gemm_prefill && (rc = upload_flat(m, w, s, b, &m->L[l].fgate))) return rc;
     pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), I, H, gs, 2, 0, buf.data(), 0);
     if ((rc = get_proj(m, pre + "mlp.up_proj", I, H, w, s, b))) return rc;
+    if (m->gemm_prefill && (rc = upload_flat(m, w, s, b, &m->L[l].fup))) return rc;
     pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), I, H, gs, 2, 1, buf.data(), 0);
     NNZ_CK(cudaMemcpy(m->arena + lo[l].gu, buf.data(), b_gu, cudaMemcpyHostToDevice));
     if ((rc = get_proj(m, pre + "mlp.down_proj", H, I, w, s, b))) return rc;
+    if (m->gemm_prefill && (rc = upload_flat(m, w, s, b, &m->L[l].fdown))) return rc;
     buf.assign(b_dn, 0);
     pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), H, I, gs, 1, 0, buf.data(), 0);
     NNZ_CK(cudaMemcpy(m->arena + lo[l].dn, buf.data(), b_dn, cudaMemcpyHostToDevice));
@@ -732,6 +817,7 @@ int nnz_model_finalize(nnz_model* m) {
   if ((rc = dalloc(m, (void**)&m->qkv, (size_t)R * m->qkv_rows * 2))) return rc;
   if ((rc = dalloc(m, (void**)&m->attn, (size_t)R * m->qd * 2))) return rc;
   if ((rc = dalloc(m, (void**)&m->h, (size_t)R * I * 2))) return rc;
+  if (m->gemm_prefill && (rc = dalloc(m, (void**)&m->xn, (size_t)R * H * 2))) return rc;
   if ((rc = dalloc(m, (void**)&m->logits, (size_t)c.max_batch * c.vocab_size * 4))) return rc;
   size_t wsf = 0, nctr = 0;
   for (uint32_t rows = 1; rows <= R; ++rows) {
@@ -1153,6 +1239,28 @@ int nnz_mlp(int fmt, int scale_dtype, int bf16_round, const void* gate_up, const
   d.x = hbuf; d.x_stride = inter; d.batch = batch; d.out = out; d.out_stride = hidden;
   d.ws = w->ws; d.counters = w->counters; d.err = w->err; d.bf16_round = br;
   NNZ_CK(qmv_launch(QmvLaunch{fmt, 1, PRO_F16, EPI_F32, bf16s, 0}, d, w->num_sms, (cudaStream_t)stream));
+  return NNZ_OK;
+}
+
+int nnz_prefill_gemm(int fmt, int scale_dtype, const void* w, const uint16_t* scales,
+                     const uint16_t* biases, uint32_t M, uint32_t K, uint32_t N, uint32_t gs,
+                     const void* x, void* out, int out_kind, void* stream) {
+  if (!w || !scales || !x || !out || (fmt == NNZ_Q4 && !biases) ||
+      (out_kind != NNZ_OUT_F16 && out_kind != NNZ_OUT_F32_ADD))
+    return fail(NNZ_EINVAL, "nnz_prefill_gemm: bad arguments");
+  int dev = 0;
+  NNZ_CK(cudaGetDevice(&dev));
+  GemmArgs g{};
+  g.M = M; g.K = K; g.N = N; g.fmt = fmt; g.gs = (int)gs;
+  g.bf16s = fmt == NNZ_Q4 && scale_dtype == NNZ_SCALE_BF16; g.bf16r = 0;
+  g.w = (const uint8_t*)w; g.s = scales; g.b = biases;
+  g.epi = out_kind == NNZ_OUT_F16 ? GEPI_F16 : GEPI_RESADD;
+  g.out = out; g.ldo = N; g.err = nullptr;
+  DevWs* ws;
+  int rc = get_ws(&ws);
+  if (rc) return rc;
+  g.err = ws->err;
+  NNZ_CK(gemm_launch(g, (const __half*)x, (cudaStream_t)stream));
   return NNZ_OK;
 }
 

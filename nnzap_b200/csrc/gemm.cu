@@ -1,0 +1,353 @@
+// tcgen05 prefill GEMM (see gemm.cuh).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "gemm.cuh"
+
+namespace nnz {
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kBK = 64, kStages = 4;
+constexpr uint32_t kTileBytes = kBM * kBK * 2;          // 16 KB per operand per stage
+constexpr uint32_t kTmemCols = 128;
+constexpr int kThreads = 128;
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Canonical K-major, 128B-swizzled shared-memory matrix descriptor.
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
+  const uint64_t addr = smem_u32(p);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;                 // start address
+  d |= (uint64_t)(16 >> 4) << 16;               // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;             // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;                       // descriptor version (sm100)
+  d |= (uint64_t)2 << 61;                       // SWIZZLE_128B
+  return d;
+}
+
+// kind::f16 instruction descriptor: f32 accumulate, f16 A/B, K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+        "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+        "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Raw weights of one row for one 64-wide K step.
+struct Raw {
+  uint4 q0, q1;    // Q1: q0.x/y = 64 sign bits; Q4: 32 bytes of nibbles
+  uint16_t s, b;
+};
+
+template <int FMT>
+__device__ __forceinline__ Raw load_raw(const GemmArgs& a, const uint8_t* w, const uint16_t* s, const uint16_t* b,
+                                        uint32_t row, bool ok, uint32_t step) {
+  Raw r{};
+  if (!ok) return r;
+  const uint32_t k0 = step * kBK;
+  const size_t g = (size_t)row * (a.K / a.gs) + k0 / a.gs;
+  if constexpr (FMT == FMT_Q1) {
+    const uint2 v = *reinterpret_cast<const uint2*>(w + ((size_t)row * a.K + k0) / 8);
+    r.q0.x = v.x; r.q0.y = v.y;
+  } else {
+    const uint4* p = reinterpret_cast<const uint4*>(w + ((size_t)row * a.K + k0) / 2);
+    r.q0 = p[0]; r.q1 = p[1];
+    r.b = b[g];
+  }
+  r.s = s[g];
+  return r;
+}
+
+__device__ __forceinline__ float u16f(uint16_t v, int bf16s) {
+  return bf16s ? __uint_as_float((uint32_t)v << 16) : __half2float(__ushort_as_half(v));
+}
+
+// Dequantize one row's 64 weights into the 128B-swizzled K-major stage.
+template <int FMT>
+__device__ __forceinline__ void write_row(uint8_t* stage, uint32_t r, const Raw& raw, int bf16s) {
+  uint8_t* rowp = stage + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+  for (uint32_t c = 0; c < 8; ++c) {
+    uint32_t h[4];
+    if constexpr (FMT == FMT_Q1) {
+      const uint32_t bits = ((c < 4 ? raw.q0.x : raw.q0.y) >> (8 * (c & 3))) & 0xFFu;
+      const uint32_t sp = raw.s, sn = raw.s ^ 0x8000u;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t lo = ((bits >> (2 * j)) & 1u) ? sp : sn;
+        const uint32_t hi = ((bits >> (2 * j + 1)) & 1u) ? sp : sn;
+        h[j] = lo | (hi << 16);
+      }
+    } else {
+      const uint32_t word = c < 4 ? (&raw.q0.x)[c] : (&raw.q1.x)[c - 4];
+      const float sc = u16f(raw.s, bf16s), bi = u16f(raw.b, bf16s);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float f0 = __fadd_rn(__fmul_rn(sc, (float)((word >> (8 * j)) & 0xFu)), bi);
+        const float f1 = __fadd_rn(__fmul_rn(sc, (float)((word >> (8 * j + 4)) & 0xFu)), bi);
+        const __half2 v = __floats2half2_rn(f0, f1);
+        h[j] = *reinterpret_cast<const uint32_t*>(&v);
+      }
+    }
+    *reinterpret_cast<uint4*>(rowp + ((c ^ (r & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+  }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmX, GemmArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* As = sm;
+  uint8_t* Bs = sm + kStages * kTileBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + 2 * kStages * kTileBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* done = empty + kStages;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t m0 = blockIdx.y * kBM;
+  const bool silu = a.epi == GEPI_SILU;
+  const uint32_t ncols = silu ? kBN / 2 : kBN;           // output columns per tile
+  const uint32_t n0 = blockIdx.x * ncols;
+  const uint32_t nk = a.K / kBK;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], kThreads + 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tslot;
+
+  // this thread's weight row
+  const uint32_t r = tid;
+  const uint8_t* w = a.w;
+  const uint16_t* sc = a.s;
+  const uint16_t* bi = a.b;
+  uint32_t row = n0 + r;
+  if (silu && r >= kBN / 2) { w = a.w2; sc = a.s2; bi = a.b2; row = n0 + r - kBN / 2; }
+  const bool rok = row < a.N && (silu ? (n0 + (r & 63)) < a.N : true);
+
+  pdl_wait();
+  pdl_launch();
+
+  // raw-weight prefetch three steps ahead (register rotation)
+  Raw r0 = load_raw<FMT>(a, w, sc, bi, row, rok && 0 < nk, 0);
+  Raw r1 = load_raw<FMT>(a, w, sc, bi, row, rok && 1 < nk, 1);
+  Raw r2 = load_raw<FMT>(a, w, sc, bi, row, rok && 2 < nk, 2);
+  const uint32_t idesc = idesc_f16(kBM, kBN);
+  bool failed = false;
+  for (uint32_t i = 0; i < nk; ++i) {
+    const uint32_t s = i % kStages;
+    const Raw r3 = load_raw<FMT>(a, w, sc, bi, row, rok && i + 3 < nk, i + 3);
+    if (i >= (uint32_t)kStages && !failed) failed = !mbar_wait(&empty[s], ((i / kStages) - 1) & 1u, a.err);
+    if (tid == 0) {
+      mbar_arrive_expect_tx(&full[s], kTileBytes);
+      tma_load_2d(As + s * kTileBytes, &tmX, (int)(i * kBK), (int)m0, &full[s]);
+    }
+    write_row<FMT>(Bs + s * kTileBytes, r, r0, a.bf16s);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_arrive(&full[s]);
+    if (tid == 0) {
+      if (!failed) failed = !mbar_wait(&full[s], (i / kStages) & 1u, a.err);
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint64_t da = smem_desc_sw128(As + s * kTileBytes);
+      const uint64_t db = smem_desc_sw128(Bs + s * kTileBytes);
+#pragma unroll
+      for (int kk = 0; kk < kBK / 16; ++kk)   // +32 B per 16-element K step inside the swizzle atom
+        umma_f16(tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (i | kk) != 0);
+      umma_commit(&empty[s]);
+    }
+    r0 = r1; r1 = r2; r2 = r3;
+  }
+  if (tid == 0) umma_commit(done);
+  if (!failed) failed = !mbar_wait(done, 0, a.err);
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+
+  // ---- epilogue: TMEM lanes 32w..32w+31 = rows m0 + 32w + lane ----
+  const uint32_t m = m0 + 32 * warp + lane;
+  const uint32_t tbase = tmem + ((uint32_t)(32 * warp) << 16);
+  const bool rb = a.bf16r != 0;
+  if (silu) {
+    for (int cc = 0; cc < 2; ++cc) {
+      uint32_t g[32], u[32];
+      tmem_ld32(tbase + cc * 32, g);
+      tmem_ld32(tbase + 64 + cc * 32, u);
+      if (m < a.M) {
+        __half* o = static_cast<__half*>(a.out) + (size_t)m * a.ldo + n0 + cc * 32;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const uint32_t n = n0 + cc * 32 + j;
+          const float gv = __uint_as_float(g[j]), uv = __uint_as_float(u[j]);
+          float h = gv / (1.0f + expf(-gv)) * uv;
+          if (rb) h = bf16_trunc(h);
+          if (n < a.N) o[j] = __float2half_rn(h);
+        }
+      }
+    }
+  } else {
+    for (int cc = 0; cc < kBN / 32; ++cc) {
+      uint32_t v[32];
+      tmem_ld32(tbase + cc * 32, v);
+      if (m >= a.M) continue;
+      const uint32_t nb = n0 + cc * 32;
+      if (a.epi == GEPI_F16) {
+        __half* o = static_cast<__half*>(a.out) + (size_t)m * a.ldo + nb;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float x = __uint_as_float(v[j]);
+          if (rb) x = bf16_trunc(x);
+          if (nb + j < a.N) o[j] = __float2half_rn(x);
+        }
+      } else {
+        float* o = static_cast<float*>(a.out) + (size_t)m * a.ldo + nb;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float x = __uint_as_float(v[j]);
+          if (rb) x = bf16_trunc(x);
+          if (nb + j < a.N) o[j] += x;
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+}
+
+__global__ void rmsnorm_f16_kernel(const float* res, const float* w, float eps, uint32_t K, int bf16r,
+                                   __half* out) {
+  __shared__ float red[32];
+  const uint32_t row = blockIdx.x;
+  const float* x = res + (size_t)row * K;
+  float ss = 0.f;
+  for (uint32_t k = threadIdx.x; k < K; k += blockDim.x) ss = fmaf(x[k], x[k], ss);
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = rsqrtf(t / (float)K + eps);
+  }
+  __syncthreads();
+  const float r = red[0];
+  for (uint32_t k = threadIdx.x; k < K; k += blockDim.x) {
+    float v = x[k] * r * w[k];
+    if (bf16r) v = bf16_trunc(v);
+    out[(size_t)row * K + k] = __float2half_rn(v);
+  }
+}
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn get_encode() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  }
+  return fn;
+}
+
+constexpr uint32_t kSmemBytes = 2 * kStages * kTileBytes + 1024 + 256;
+
+}  // namespace
+
+cudaError_t gemm_launch(const GemmArgs& a, const __half* x, cudaStream_t st) {
+  if (a.K % kBK || a.gs < 64 || a.K % a.gs || a.M == 0 || a.N == 0 ||
+      (a.fmt != FMT_Q1 && a.fmt != FMT_Q4) || (reinterpret_cast<uintptr_t>(x) & 15))
+    return cudaErrorInvalidValue;
+  EncodeFn enc = get_encode();
+  if (!enc) return cudaErrorNotSupported;
+  CUtensorMap tm;
+  const cuuint64_t dims[2] = {a.K, a.M};
+  const cuuint64_t strides[1] = {(cuuint64_t)a.K * 2};
+  const cuuint32_t box[2] = {kBK, kBM};
+  const cuuint32_t estr[2] = {1, 1};
+  if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  const uint32_t ncols = a.epi == GEPI_SILU ? kBN / 2 : kBN;
+  dim3 grid((a.N + ncols - 1) / ncols, (a.M + kBM - 1) / kBM);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = st;
+  cfg.numAttrs = 0;
+  if (a.fmt == FMT_Q1) {
+    static bool attr = false;
+    if (!attr) {
+      cudaError_t e = cudaFuncSetAttribute(&gemm_kernel<FMT_Q1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      if (e != cudaSuccess) return e;
+      attr = true;
+    }
+    return cudaLaunchKernelEx(&cfg, &gemm_kernel<FMT_Q1>, tm, a);
+  }
+  static bool attr4 = false;
+  if (!attr4) {
+    cudaError_t e = cudaFuncSetAttribute(&gemm_kernel<FMT_Q4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr4 = true;
+  }
+  return cudaLaunchKernelEx(&cfg, &gemm_kernel<FMT_Q4>, tm, a);
+}
+
+cudaError_t rmsnorm_f16_launch(const float* res, const float* w, float eps, uint32_t rows, uint32_t K, int bf16r,
+                               __half* out, cudaStream_t st) {
+  rmsnorm_f16_kernel<<<rows, 256, 0, st>>>(res, w, eps, K, bf16r, out);
+  return cudaGetLastError();
+}
+
+}  // namespace nnz
