@@ -327,3 +327,168 @@ cudaError_t rope_kv_write_launch(const AttnArgs& a, int head_dim, int pdl, cudaS
 }
 
 }  // namespace nnz
+
+// ===========================================================================
+// Causal prefill attention.  One CTA per (kv head, block of query rows);
+// threads own (row, query head of the group, quarter of head_dim), so a
+// score needs two shuffles and the online softmax stays per thread.  K/V
+// tiles of 64 positions are staged in shared memory and shared by all rows
+// of the block.  Same f32 math as the decode kernel: q = RoPE(RMSNorm(q))
+// kept f32, scores q.k / sqrt(hd), online softmax, fp16 output.  The chunk's
+// own K/V must already be in the cache (rope_kv_write_launch).
+// ===========================================================================
+namespace nnz {
+namespace {
+
+constexpr int kPfThreads = 256;
+constexpr int kPfKeys = 64;
+
+template <int HD>
+__global__ void __launch_bounds__(kPfThreads) attn_prefill_kernel(AttnArgs a) {
+  constexpr int Q4 = HD / 4;            // dims per thread
+  __shared__ __align__(16) __half ks[kPfKeys][HD];
+  __shared__ __align__(16) __half vs[kPfKeys][HD];
+  pdl_wait();
+  pdl_launch();
+  const int G = (int)(a.n_q / a.n_kv);
+  const int rows_per_cta = kPfThreads / (4 * G);
+  const int tid = threadIdx.x, c = tid & 3, g = (tid >> 2) % G, rl = tid / (4 * G);
+  const int kvh = blockIdx.x;
+  const uint32_t r = blockIdx.y * rows_per_cta + rl;
+  const bool live = r < a.rows;
+  const int pos = live ? a.pos[r] : -1;
+  const int slot = (live && a.slot) ? a.slot[r] : 0;
+  // keys to visit: up to the largest position of the block's rows
+  int maxpos = pos;
+  for (int o = 16; o > 0; o >>= 1) maxpos = max(maxpos, __shfl_xor_sync(0xffffffffu, maxpos, o));
+  __shared__ int s_max[kPfThreads / 32];
+  __shared__ int s_slot;
+  if ((tid & 31) == 0) s_max[tid >> 5] = maxpos;
+  if (tid == 0) s_slot = slot;
+  __syncthreads();
+  int kmax = -1;
+  for (int w = 0; w < kPfThreads / 32; ++w) kmax = max(kmax, s_max[w]);
+  const size_t head_off = ((size_t)s_slot * a.n_kv + kvh) * a.max_ctx * HD;
+
+  // q: RMSNorm over the head (4 threads) + RoPE, f32
+  float q[Q4], o[Q4];
+  const int h = kvh * G + g;
+  {
+    const __half* src = a.qkv + (size_t)(live ? r : 0) * a.qkv_stride + (size_t)h * HD + c * Q4;
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < Q4; ++i) { q[i] = __half2float(src[i]); ss = fmaf(q[i], q[i], ss); }
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    const float rr = rsqrtf(ss / (float)HD + a.eps);
+#pragma unroll
+    for (int i = 0; i < Q4; ++i) q[i] = q[i] * rr * a.q_norm[c * Q4 + i];
+    const double l2t = log2((double)a.theta);
+    if (a.rope_style == ROPE_PAIRWISE) {
+#pragma unroll
+      for (int i = 0; i < Q4; i += 2) {
+        const int p = (c * Q4 + i) >> 1;
+        double sd, cd;
+        sincos((double)max(pos, 0) * exp2(-(2.0 * p / HD) * l2t), &sd, &cd);
+        const float cs = (float)cd, sn = (float)sd, x0 = q[i], x1 = q[i + 1];
+        q[i] = x0 * cs - x1 * sn;
+        q[i + 1] = x0 * sn + x1 * cs;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < Q4; ++i) {
+        const float partner = __shfl_xor_sync(0xffffffffu, q[i], 2);   // quarter c <-> c^2
+        const int p = (c & 1) * Q4 + i;
+        double sd, cd;
+        sincos((double)max(pos, 0) * exp2(-(2.0 * p / HD) * l2t), &sd, &cd);
+        const float cs = (float)cd, sn = (float)sd;
+        q[i] = (c < 2) ? q[i] * cs - partner * sn : partner * sn + q[i] * cs;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < Q4; ++i) o[i] = 0.f;
+  }
+  const float inv = rsqrtf((float)HD);
+  float m = -INFINITY, l = 0.f;
+  for (int t0 = 0; t0 <= kmax; t0 += kPfKeys) {
+    const int n = min(kPfKeys, kmax + 1 - t0);
+    __syncthreads();
+    for (int i = tid; i < n * HD / 8; i += kPfThreads) {
+      const int t = i / (HD / 8), d8 = i % (HD / 8);
+      reinterpret_cast<uint4*>(&ks[t][0])[d8] =
+          *reinterpret_cast<const uint4*>(a.kc + head_off + (size_t)(t0 + t) * HD + 8 * d8);
+      reinterpret_cast<uint4*>(&vs[t][0])[d8] =
+          *reinterpret_cast<const uint4*>(a.vc + head_off + (size_t)(t0 + t) * HD + 8 * d8);
+    }
+    __syncthreads();
+    for (int t = 0; t < n; t += 4) {
+      float s4[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int tt = min(t + u, n - 1);
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < Q4; i += 4) {
+          const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&ks[tt][c * Q4 + i]));
+          const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&ks[tt][c * Q4 + i + 2]));
+          a0 = fmaf(q[i], k0.x, a0); a1 = fmaf(q[i + 1], k0.y, a1);
+          a0 = fmaf(q[i + 2], k1.x, a0); a1 = fmaf(q[i + 3], k1.y, a1);
+        }
+        s4[u] = a0 + a1;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        s4[u] += __shfl_xor_sync(0xffffffffu, s4[u], 1);
+        s4[u] += __shfl_xor_sync(0xffffffffu, s4[u], 2);
+      }
+      float p4[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const bool ok = (t + u < n) && (t0 + t + u <= pos);
+        const float sc = ok ? s4[u] * inv : -INFINITY;
+        if (sc > m) {
+          const float al = (m == -INFINITY) ? 0.f : expf(m - sc);
+          l *= al;
+#pragma unroll
+          for (int i = 0; i < Q4; ++i) o[i] *= al;
+#pragma unroll
+          for (int v = 0; v < u; ++v) p4[v] *= al;
+          m = sc;
+        }
+        p4[u] = ok ? expf(sc - m) : 0.f;
+        l += p4[u];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int tt = min(t + u, n - 1);
+#pragma unroll
+        for (int i = 0; i < Q4; i += 2) {
+          const float2 v2 = __half22float2(*reinterpret_cast<const __half2*>(&vs[tt][c * Q4 + i]));
+          o[i] = fmaf(p4[u], v2.x, o[i]);
+          o[i + 1] = fmaf(p4[u], v2.y, o[i + 1]);
+        }
+      }
+    }
+  }
+  if (live) {
+    __half* dst = a.out + (size_t)r * a.out_stride + (size_t)h * HD + c * Q4;
+    const float il = 1.f / l;
+#pragma unroll
+    for (int i = 0; i < Q4; i += 2) *reinterpret_cast<__half2*>(&dst[i]) = __floats2half2_rn(o[i] * il, o[i + 1] * il);
+  }
+}
+
+}  // namespace
+
+cudaError_t attn_prefill_launch(const AttnArgs& a, int head_dim, int pdl, cudaStream_t st) {
+  const uint32_t G = a.n_q / a.n_kv;
+  if (a.rows == 0 || a.n_kv == 0 || a.n_q % a.n_kv || 4 * G > (uint32_t)kPfThreads) return cudaErrorInvalidValue;
+  const uint32_t rpc = kPfThreads / (4 * G);
+  cudaLaunchAttribute at[1];
+  cudaLaunchConfig_t cfg = make_cfg(dim3(a.n_kv, (a.rows + rpc - 1) / rpc), dim3(kPfThreads), 0, pdl, st, at);
+  if (head_dim == 128) return cudaLaunchKernelEx(&cfg, &attn_prefill_kernel<128>, a);
+  if (head_dim == 64) return cudaLaunchKernelEx(&cfg, &attn_prefill_kernel<64>, a);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace nnz

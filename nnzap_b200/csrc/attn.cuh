@@ -62,5 +62,8 @@ size_t attn_ws_floats(uint32_t rows, uint32_t n_q, uint32_t n_kv, uint32_t split
 // (used by chunked prefill, where rows of one chunk share a cache slot and
 // must all be written before any row attends).
 cudaError_t rope_kv_write_launch(const AttnArgs& a, int head_dim, int pdl, cudaStream_t st);
+// Causal attention of a prefill chunk (rows attend to positions <= their own;
+// K/V of the chunk already written).  Writes `out` like attn_decode_launch.
+cudaError_t attn_prefill_launch(const AttnArgs& a, int head_dim, int pdl, cudaStream_t st);
 
 }  // namespace nnz

@@ -552,7 +552,15 @@ int enqueue_layer_gemm(nnz_model* m, uint32_t l, uint32_t rows, const int* pos) 
   NNZ_CK(rmsnorm_f16_launch(m->residual, W.attn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st));
   if ((rc = gemm(m, W.fqkv, nullptr, m->qkv_rows, H, m->xn, rows, GEPI_F16, m->qkv, m->qkv_rows))) return rc;
   if ((rc = kv_write(m, l, rows, pos, m->zeros, 0))) return rc;
-  if ((rc = attn(m, l, rows, pos, m->zeros, 0, 0))) return rc;
+  {
+    AttnArgs aa{};
+    aa.qkv = m->qkv; aa.qkv_stride = m->qkv_rows; aa.q_norm = W.q_norm; aa.k_norm = W.k_norm;
+    aa.kc = m->kc + m->kv_layer * l; aa.vc = m->vc + m->kv_layer * l; aa.max_ctx = c.max_context_length;
+    aa.pos = pos; aa.slot = m->zeros; aa.rows = rows; aa.n_q = c.num_query_heads; aa.n_kv = c.num_kv_heads;
+    aa.eps = c.eps; aa.theta = c.rope_theta; aa.rope_style = c.rope_style; aa.out = m->attn;
+    aa.out_stride = m->qd; aa.err = m->err;
+    NNZ_CK(attn_prefill_launch(aa, (int)c.head_dim, 0, m->st));
+  }
   if ((rc = gemm(m, W.fo, nullptr, H, m->qd, m->attn, rows, GEPI_RESADD, m->residual, H))) return rc;
   NNZ_CK(rmsnorm_f16_launch(m->residual, W.ffn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st));
   if ((rc = gemm(m, W.fgate, &W.fup, I, H, m->xn, rows, GEPI_SILU, m->h, I))) return rc;

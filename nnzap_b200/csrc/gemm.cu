@@ -10,7 +10,9 @@ namespace {
 constexpr int kBM = 128, kBN = 128, kBK = 64, kStages = 4;
 constexpr uint32_t kTileBytes = kBM * kBK * 2;          // 16 KB per operand per stage
 constexpr uint32_t kTmemCols = 128;
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;
+constexpr int kProducers = 128;   // dequantizing threads (warps 4-7)
+constexpr int kPf = 4;            // raw-weight prefetch depth (steps)
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -125,6 +127,12 @@ __device__ __forceinline__ void write_row(uint8_t* stage, uint32_t r, const Raw&
   }
 }
 
+// Warp roles (256 threads): warp 0 lane 0 streams X tiles with TMA up to
+// kStages ahead; warp 1 lane 0 issues the MMAs; warps 4-7 dequantize one
+// weight row each into the B stages (raw weights prefetched kPf steps ahead
+// in registers) and run the epilogue (TMEM lane quarter = warp % 4).
+// Split-K over gridDim.z is allowed only for the residual-add epilogue,
+// whose partial sums are accumulated with atomicAdd.
 template <int FMT>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmX, GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -141,17 +149,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   const bool silu = a.epi == GEPI_SILU;
   const uint32_t ncols = silu ? kBN / 2 : kBN;           // output columns per tile
   const uint32_t n0 = blockIdx.x * ncols;
-  const uint32_t nk = a.K / kBK;
+  const uint32_t nk_all = a.K / kBK;
+  const uint32_t ks0 = nk_all * blockIdx.z / gridDim.z, ks1 = nk_all * (blockIdx.z + 1) / gridDim.z;
+  const uint32_t nk = ks1 - ks0;
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], kThreads + 1);
+      mbar_init(&full[s], kProducers + 1);
       mbar_init(&empty[s], 1);
     }
     mbar_init(done, 1);
     fence_barrier_init();
   }
-  if (warp == 0) {
+  if (warp == 2) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
                  "r"(kTmemCols)
                  : "memory");
@@ -161,101 +171,118 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tslot;
-
-  // this thread's weight row
-  const uint32_t r = tid;
-  const uint8_t* w = a.w;
-  const uint16_t* sc = a.s;
-  const uint16_t* bi = a.b;
-  uint32_t row = n0 + r;
-  if (silu && r >= kBN / 2) { w = a.w2; sc = a.s2; bi = a.b2; row = n0 + r - kBN / 2; }
-  const bool rok = row < a.N && (silu ? (n0 + (r & 63)) < a.N : true);
-
   pdl_wait();
   pdl_launch();
-
-  // raw-weight prefetch three steps ahead (register rotation)
-  Raw r0 = load_raw<FMT>(a, w, sc, bi, row, rok && 0 < nk, 0);
-  Raw r1 = load_raw<FMT>(a, w, sc, bi, row, rok && 1 < nk, 1);
-  Raw r2 = load_raw<FMT>(a, w, sc, bi, row, rok && 2 < nk, 2);
-  const uint32_t idesc = idesc_f16(kBM, kBN);
   bool failed = false;
-  for (uint32_t i = 0; i < nk; ++i) {
-    const uint32_t s = i % kStages;
-    const Raw r3 = load_raw<FMT>(a, w, sc, bi, row, rok && i + 3 < nk, i + 3);
-    if (i >= (uint32_t)kStages && !failed) failed = !mbar_wait(&empty[s], ((i / kStages) - 1) & 1u, a.err);
-    if (tid == 0) {
-      mbar_arrive_expect_tx(&full[s], kTileBytes);
-      tma_load_2d(As + s * kTileBytes, &tmX, (int)(i * kBK), (int)m0, &full[s]);
-    }
-    write_row<FMT>(Bs + s * kTileBytes, r, r0, a.bf16s);
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_arrive(&full[s]);
-    if (tid == 0) {
-      if (!failed) failed = !mbar_wait(&full[s], (i / kStages) & 1u, a.err);
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint64_t da = smem_desc_sw128(As + s * kTileBytes);
-      const uint64_t db = smem_desc_sw128(Bs + s * kTileBytes);
-#pragma unroll
-      for (int kk = 0; kk < kBK / 16; ++kk)   // +32 B per 16-element K step inside the swizzle atom
-        umma_f16(tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (i | kk) != 0);
-      umma_commit(&empty[s]);
-    }
-    r0 = r1; r1 = r2; r2 = r3;
-  }
-  if (tid == 0) umma_commit(done);
-  if (!failed) failed = !mbar_wait(done, 0, a.err);
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 
-  // ---- epilogue: TMEM lanes 32w..32w+31 = rows m0 + 32w + lane ----
-  const uint32_t m = m0 + 32 * warp + lane;
-  const uint32_t tbase = tmem + ((uint32_t)(32 * warp) << 16);
-  const bool rb = a.bf16r != 0;
-  if (silu) {
-    for (int cc = 0; cc < 2; ++cc) {
-      uint32_t g[32], u[32];
-      tmem_ld32(tbase + cc * 32, g);
-      tmem_ld32(tbase + 64 + cc * 32, u);
-      if (m < a.M) {
-        __half* o = static_cast<__half*>(a.out) + (size_t)m * a.ldo + n0 + cc * 32;
+  if (warp == 0) {
+    if (lane == 0) {
+      for (uint32_t i = 0; i < nk; ++i) {
+        const uint32_t s = i % kStages;
+        if (i >= (uint32_t)kStages && !failed) failed = !mbar_wait(&empty[s], ((i / kStages) - 1) & 1u, a.err);
+        mbar_arrive_expect_tx(&full[s], kTileBytes);
+        tma_load_2d(As + s * kTileBytes, &tmX, (int)((ks0 + i) * kBK), (int)m0, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(kBM, kBN);
+      for (uint32_t i = 0; i < nk; ++i) {
+        const uint32_t s = i % kStages;
+        if (!failed) failed = !mbar_wait(&full[s], (i / kStages) & 1u, a.err);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint64_t da = smem_desc_sw128(As + s * kTileBytes);
+        const uint64_t db = smem_desc_sw128(Bs + s * kTileBytes);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const uint32_t n = n0 + cc * 32 + j;
-          const float gv = __uint_as_float(g[j]), uv = __uint_as_float(u[j]);
-          float h = gv / (1.0f + expf(-gv)) * uv;
-          if (rb) h = bf16_trunc(h);
-          if (n < a.N) o[j] = __float2half_rn(h);
+        for (int kk = 0; kk < kBK / 16; ++kk)   // +32 B per 16-element K step inside the swizzle atom
+          umma_f16(tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (i | kk) != 0);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(done);
+    }
+  } else if (warp >= 4) {
+    const uint32_t r = tid - 128;              // weight row of the tile
+    const uint8_t* w = a.w;
+    const uint16_t* sc = a.s;
+    const uint16_t* bi = a.b;
+    uint32_t row = n0 + r;
+    if (silu && r >= kBN / 2) { w = a.w2; sc = a.s2; bi = a.b2; row = n0 + r - kBN / 2; }
+    const bool rok = row < a.N;
+    Raw raw[kPf];
+#pragma unroll
+    for (int d = 0; d < kPf; ++d) raw[d] = load_raw<FMT>(a, w, sc, bi, row, rok && (uint32_t)d < nk, ks0 + d);
+    for (uint32_t i0 = 0; i0 < nk; i0 += kPf) {
+#pragma unroll
+      for (int d = 0; d < kPf; ++d) {
+        const uint32_t i = i0 + d;
+        if (i < nk) {
+          const uint32_t s = i % kStages;
+          if (i >= (uint32_t)kStages && !failed) failed = !mbar_wait(&empty[s], ((i / kStages) - 1) & 1u, a.err);
+          write_row<FMT>(Bs + s * kTileBytes, r, raw[d], a.bf16s);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          mbar_arrive(&full[s]);
+          raw[d] = load_raw<FMT>(a, w, sc, bi, row, rok && i + kPf < nk, ks0 + i + kPf);
         }
       }
     }
-  } else {
-    for (int cc = 0; cc < kBN / 32; ++cc) {
-      uint32_t v[32];
-      tmem_ld32(tbase + cc * 32, v);
-      if (m >= a.M) continue;
-      const uint32_t nb = n0 + cc * 32;
-      if (a.epi == GEPI_F16) {
-        __half* o = static_cast<__half*>(a.out) + (size_t)m * a.ldo + nb;
+  }
+  // ---- epilogue (warps 4-7): TMEM lanes 32q..32q+31 = rows m0 + 32q + lane ----
+  if (warp >= 4) {
+    if (!failed) failed = !mbar_wait(done, 0, a.err);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int q = warp - 4;
+    const uint32_t m = m0 + 32 * q + lane;
+    const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16);
+    const bool rb = a.bf16r != 0;
+    if (silu) {
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t g[32], u[32];
+        tmem_ld32(tbase + cc * 32, g);
+        tmem_ld32(tbase + 64 + cc * 32, u);
+        if (m < a.M) {
+          __half* o = static_cast<__half*>(a.out) + (size_t)m * a.ldo + n0 + cc * 32;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float x = __uint_as_float(v[j]);
-          if (rb) x = bf16_trunc(x);
-          if (nb + j < a.N) o[j] = __float2half_rn(x);
+          for (int j = 0; j < 32; ++j) {
+            const uint32_t n = n0 + cc * 32 + j;
+            const float gv = __uint_as_float(g[j]), uv = __uint_as_float(u[j]);
+            float h = gv / (1.0f + expf(-gv)) * uv;
+            if (rb) h = bf16_trunc(h);
+            if (n < a.N) o[j] = __float2half_rn(h);
+          }
         }
-      } else {
-        float* o = static_cast<float*>(a.out) + (size_t)m * a.ldo + nb;
+      }
+    } else {
+      for (int cc = 0; cc < kBN / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld32(tbase + cc * 32, v);
+        if (m >= a.M) continue;
+        const uint32_t nb = n0 + cc * 32;
+        if (a.epi == GEPI_F16) {
+          __half* o = static_cast<__half*>(a.out) + (size_t)m * a.ldo + nb;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float x = __uint_as_float(v[j]);
-          if (rb) x = bf16_trunc(x);
-          if (nb + j < a.N) o[j] += x;
+          for (int j = 0; j < 32; ++j) {
+            float x = __uint_as_float(v[j]);
+            if (rb) x = bf16_trunc(x);
+            if (nb + j < a.N) o[j] = __float2half_rn(x);
+          }
+        } else {
+          float* o = static_cast<float*>(a.out) + (size_t)m * a.ldo + nb;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float x = __uint_as_float(v[j]);
+            if (rb) x = bf16_trunc(x);
+            if (nb + j < a.N) {
+              if (gridDim.z > 1) atomicAdd(&o[j], x);
+              else o[j] += x;
+            }
+          }
         }
       }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 0)
+  if (warp == 2)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
 }
 
@@ -320,6 +347,16 @@ cudaError_t gemm_launch(const GemmArgs& a, const __half* x, cudaStream_t st) {
     return cudaErrorInvalidValue;
   const uint32_t ncols = a.epi == GEPI_SILU ? kBN / 2 : kBN;
   dim3 grid((a.N + ncols - 1) / ncols, (a.M + kBM - 1) / kBM);
+  // residual-add GEMMs with few tiles split K (partials added atomically)
+  if (a.epi == GEPI_RESADD && a.bf16r == 0) {
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    uint32_t ks = (uint32_t)sms / (grid.x * grid.y);
+    const uint32_t nk = a.K / kBK;
+    if (ks > nk / 8) ks = nk / 8;            // >= 8 K steps per CTA
+    grid.z = ks < 1 ? 1 : ks;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);
