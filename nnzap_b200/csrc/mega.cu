@@ -172,27 +172,25 @@ __device__ __forceinline__ void grid_sync(unsigned int* bar, unsigned int nblock
                                           int* err) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned int prev = atomicAdd(&bar[0], 1u);
+    // release: this CTA's writes (ordered before by bar.sync) become visible
+    // to whoever acquires the generation bump
+    unsigned int prev;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&bar[0]) : "memory");
     if (prev == nblocks - 1) {
-      bar[0] = 0;
-      __threadfence();
-      atomicAdd(&bar[1], 1u);
+      asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(&bar[0]) : "memory");
+      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&bar[1]) : "memory");
     } else {
-      // poll with relaxed loads and a short sleep (spinning CTAs must not
-      // flood the barrier's L2 slice); one fence after release
       uint32_t i = 0;
-      while (ld_relaxed(&bar[1]) == gen) {
+      while (ld_acquire(&bar[1]) == gen) {
         if (ld_relaxed(&bar[2])) break;
         if (++i > kGridSpinLimit) {
           atomicOr(err, ERR_SPIN_TIMEOUT);
           atomicExch(&bar[2], 1u);
           break;
         }
-        __nanosleep(40);
+        __nanosleep(32);
       }
     }
-    __threadfence();
   }
   gen += 1;
   __syncthreads();
@@ -474,6 +472,51 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
   stamp(c, p, u, 5);
 }
 
+// Scores of one 32-position block: warp w takes positions 8w..8w+7.  Each
+// lane owns HD/32 dims, forms the 8 * G partial dots, and a recursive-halving
+// butterfly leaves each (position, head) sum on a lane pair.
+template <int HD, int G>
+__device__ __forceinline__ void att_scores(const __half* kr, const float* qs, float* ss, int warp, int lane,
+                                           float inv) {
+  constexpr int EPL = HD / 32, NV = 8 * G;
+  float v[NV];
+#pragma unroll
+  for (int p = 0; p < 8; ++p) {
+    float kv[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; e += 2) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(kr + (size_t)(8 * warp + p) * HD + lane * EPL + e));
+      kv[e] = f.x; kv[e + 1] = f.y;
+    }
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      float d = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) d = fmaf(qs[h * HD + lane * EPL + e], kv[e], d);
+      v[p * G + h] = d;
+    }
+  }
+  int idx = 0;
+  int o = 16;
+#pragma unroll
+  for (int n = NV; n > 1; n >>= 1, o >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) {
+      const float send = up ? v[i] : v[i + n / 2];
+      const float keep = up ? v[i + n / 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+    if (up) idx += n / 2;
+  }
+  for (; o >= 1; o >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+  // lanes sharing idx hold the same sum; the lowest of them writes it
+  if ((lane & ((32 / NV) - 1)) == 0) {
+    const int p = idx / G, h = idx % G;
+    ss[h * kAttBlk + 8 * warp + p] = v[0] * inv;
+  }
+}
+
 // ---- attention work unit -----------------------------------------------------
 // One (kv head, row, split): QK-norm + RoPE of the G query heads (and of the
 // new key when this split owns the current position, which it then writes to
@@ -574,6 +617,14 @@ __device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause
       if (!c.failed) c.failed = !mbar_wait_abort(&abars[stg], ause[stg] & 1u, a.err, &a.bar[2]);
       ause[stg] += 1;
     }
+    if (!is_new && (G == 1 || G == 2 || G == 4)) {
+      // 8 positions per warp; every lane forms the partial dots of its dims
+      // for all (position, head) pairs, then one transposed butterfly sums
+      // all of them (8 G values over 32 lanes)
+      if (G == 1) att_scores<HD, 1>(kr, qs, ss, warp, lane, inv);
+      else if (G == 2) att_scores<HD, 2>(kr, qs, ss, warp, lane, inv);
+      else att_scores<HD, 4>(kr, qs, ss, warp, lane, inv);
+    } else {
     for (int t = warp; t < n; t += kQmvWarps) {
       float kv[EPL];
       if (is_new) {
@@ -593,6 +644,7 @@ __device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause
         dot = warp_sum(dot);
         if (lane == 0) ss[h * kAttBlk + t] = dot * inv;
       }
+    }
     }
     __syncthreads();
     for (uint32_t h = warp; h < G; h += kQmvWarps) {
