@@ -218,6 +218,7 @@ struct nnz_model {
   MegaLayer* mlayers = nullptr;
   float *mR = nullptr, *mqkv = nullptr, *mgu = nullptr, *matt = nullptr;
   unsigned int* mbar = nullptr;
+  unsigned long long mbar_count = 0;   // grid-barrier arrivals so far (device counter's value)
   unsigned long long* mprof = nullptr;    // NNZ_MEGA_PROFILE=1: per-phase timestamps
   struct MegaPlan { MegaArgs a; uint32_t grid, smem; bool ok; };
   std::map<uint32_t, MegaPlan> mplans;
@@ -464,6 +465,7 @@ int sync_check(nnz_model* m) {
   if (flags) {
     cudaMemset(m->err, 0, 4);
     if (m->mbar) cudaMemset(m->mbar, 0, 64);   // clear a persistent-kernel abort
+    m->mbar_count = 0;
     return fail(flags & (ERR_MBAR_TIMEOUT | ERR_SPIN_TIMEOUT) ? NNZ_ETIMEDOUT : NNZ_EDEVICE,
                 err_text(flags));
   }
@@ -510,6 +512,19 @@ const nnz_model::MegaPlan* mega_plan_for(nnz_model* m, uint32_t rows) {
     }
   }
   P.ok = mega_plan(a, m->fmt, m->bf16s, m->device, &P.grid, &P.smem);
+  if (P.ok) {
+    std::vector<uint32_t> off;
+    const std::vector<unsigned long long> wl = mega_weight_stream(a, m->fmt, P.grid, &off);
+    void *dl = nullptr, *doff = nullptr;
+    if (dalloc(m, &dl, wl.size() * 8) || dalloc(m, &doff, off.size() * 4) ||
+        cudaMemcpy(dl, wl.data(), wl.size() * 8, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(doff, off.data(), off.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+      P.ok = false;
+    } else {
+      a.wlist = static_cast<const unsigned long long*>(dl);
+      a.woff = static_cast<const uint32_t*>(doff);
+    }
+  }
   m->mplans[rows] = P;
   return P.ok ? &m->mplans[rows] : nullptr;
 }
@@ -520,7 +535,9 @@ int run_step(nnz_model* m, uint32_t rows, bool want_logits) {
   if (const nnz_model::MegaPlan* P = mega_plan_for(m, rows)) {
     MegaArgs a = P->a;
     a.logits = want_logits ? m->logits : nullptr;
+    a.bar_base = m->mbar_count;
     NNZ_CK(mega_launch(a, m->fmt, m->bf16s, P->grid, P->smem, m->st));
+    m->mbar_count += (unsigned long long)P->grid * (1 + 5 * a.L);   // one arrival per CTA per barrier
     return NNZ_OK;
   }
   cudaGraphExec_t g;
@@ -874,7 +891,7 @@ int nnz_model_finalize(nnz_model* m) {
       if ((rc = dalloc(m, (void**)&m->mbar, 64))) return rc;
       const char* prof = getenv("NNZ_MEGA_PROFILE");
       if (prof && prof[0] == '1') {
-        if ((rc = dalloc(m, (void**)&m->mprof, 8 * (2 * (2 + 5 * c.num_layers) + 64)))) return rc;
+        if ((rc = dalloc(m, (void**)&m->mprof, 8 * (2 * (2 + 5 * c.num_layers) + 64 + 5 * 1024)))) return rc;
       }
       if ((rc = dalloc(m, (void**)&m->mlayers, sizeof(MegaLayer) * c.num_layers))) return rc;
       NNZ_CK(cudaMemset(m->mbar, 0, 64));
@@ -1302,7 +1319,7 @@ int nnz_debug_mega_profile(nnz_model* m, uint64_t* out, uint32_t n, uint32_t* gr
   if (!m || !out || !m->mprof) return fail(NNZ_ESTATE, "profiling not enabled");
   NNZ_CK(cudaStreamSynchronize(m->st));
   const uint32_t nph = 2 + 5 * m->c.num_layers;
-  NNZ_CK(cudaMemcpy(out, m->mprof, 8 * (2 * std::min(n, nph) + (n > nph ? 64 : 0)), cudaMemcpyDeviceToHost));
+  NNZ_CK(cudaMemcpy(out, m->mprof, 8 * (2 * std::min(n, nph) + (n > nph ? 64 + 5 * 1024 : 0)), cudaMemcpyDeviceToHost));
   if (grid) {
     auto it = m->mplans.find(1);
     *grid = it != m->mplans.end() ? it->second.grid : 0;

@@ -166,33 +166,38 @@ __device__ __forceinline__ unsigned int ld_relaxed(const unsigned int* p) {
   return v;
 }
 
-// bar[0] arrivals, bar[1] generation, bar[2] sticky abort flag: once any
-// wait of the launch times out, every other wait gives up immediately.
-__device__ __forceinline__ void grid_sync(unsigned int* bar, unsigned int nblocks, unsigned int& gen,
+__device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// bar[2] is the sticky abort flag (once any wait of the launch times out,
+// every other wait gives up immediately); bar[4..5] a 64-bit arrival counter
+// that only grows: barrier i of a launch completes when it reaches
+// bar_base + (i + 1) * nblocks.  One release-add per CTA and acquire polls,
+// so the barrier costs a single one-way trip after the last arrival.
+__device__ __forceinline__ void grid_sync(unsigned int* bar, unsigned int nblocks, unsigned long long& target,
                                           int* err) {
   __syncthreads();
   if (threadIdx.x == 0) {
+    unsigned long long* cnt = reinterpret_cast<unsigned long long*>(bar + 4);
+    target += nblocks;
     // release: this CTA's writes (ordered before by bar.sync) become visible
-    // to whoever acquires the generation bump
-    unsigned int prev;
-    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&bar[0]) : "memory");
-    if (prev == nblocks - 1) {
-      asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(&bar[0]) : "memory");
-      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&bar[1]) : "memory");
-    } else {
-      uint32_t i = 0;
-      while (ld_acquire(&bar[1]) == gen) {
+    // to every CTA that acquires a count including this arrival
+    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(cnt) : "memory");
+    uint32_t i = 0;
+    while (ld_acquire64(cnt) < target) {
+      if ((++i & 63u) == 0) {
         if (ld_relaxed(&bar[2])) break;
-        if (++i > kGridSpinLimit) {
+        if (i > kGridSpinLimit) {
           atomicOr(err, ERR_SPIN_TIMEOUT);
           atomicExch(&bar[2], 1u);
           break;
         }
-        __nanosleep(32);
       }
     }
   }
-  gen += 1;
   __syncthreads();
 }
 
@@ -217,7 +222,8 @@ struct Ctx {
   int warp, lane;
   // consumer item counter and producer cursor (lane 0 of each warp)
   uint32_t k;
-  uint32_t pph, pu, pgl;
+  const unsigned long long* wl;   // producer: current weight-stream entry
+  unsigned long long wnext;
   bool failed;
 };
 
@@ -235,36 +241,18 @@ __device__ __forceinline__ PhaseInfo phase_at(const Ctx& c, uint32_t ph) {
   return p;
 }
 
-// Advance the producer cursor to the next weight segment of this warp.
-__device__ __forceinline__ void prod_normalize(Ctx& c) {
-  const uint32_t last = 1 + 5 * c.a->L;
-  while (c.pph <= last) {
-    const PhaseInfo p = phase_at(c, c.pph);
-    if (p.type == PH_EMBED || p.type == PH_ATT || c.pu >= p.units) {
-      ++c.pph; c.pu = c.cta; c.pgl = c.warp;
-      continue;
-    }
-    uint32_t tile, split, G0, ng;
-    unit_range(p, c.pu, &tile, &split, &G0, &ng);
-    if (c.pgl >= ng) { c.pu += c.G; c.pgl = c.warp; continue; }
-    return;
-  }
-}
-
-// Issue the producer's current segment into slot `slot` and advance.
+// Issue the warp's next weight segment into slot `slot` (lane 0).  The
+// entry after it is loaded now and used by the next call.
 __device__ __forceinline__ void prod_issue(Ctx& c, uint32_t slot) {
-  if (c.pph > 1 + 5 * c.a->L) return;
-  const PhaseInfo p = phase_at(c, c.pph);
-  uint32_t tile, split, G0, ng;
-  unit_range(p, c.pu, &tile, &split, &G0, &ng);
-  const uint32_t bytes = p.sub * c.seg;
-  const uint8_t* src = p.w + ((size_t)tile * p.groups + G0 + c.pgl) * bytes;
+  const unsigned long long e = c.wnext;
+  if (!e) return;
+  c.wnext = __ldg(++c.wl);
+  const uint32_t bytes = (e & 1ull) ? 2 * c.seg : c.seg;
+  const uint8_t* src = reinterpret_cast<const uint8_t*>(e & ~1ull);
   uint64_t* bars = reinterpret_cast<uint64_t*>(c.smem + c.S->bars);
   uint64_t* bar = &bars[c.warp * kMaxSlots + slot];
   mbar_arrive_expect_tx(bar, bytes);
   bulk_g2s(c.smem + c.S->ring + (size_t)(c.warp * c.a->nslot + slot) * c.S->slot_bytes, src, bytes, bar);
-  c.pgl += kQmvWarps;
-  prod_normalize(c);
 }
 
 __device__ __forceinline__ float* resv(const MegaArgs& a, uint32_t v) {
@@ -342,8 +330,9 @@ __device__ void stage_silu(const Ctx& c, uint32_t K0, uint32_t Kr, uint32_t bc, 
 // ---- one matvec work unit ------------------------------------------------------
 __device__ __forceinline__ void stamp(const Ctx& c, const PhaseInfo& p, uint32_t u, int i) {
   const MegaArgs& a = *c.a;
-  if (!a.prof || c.cta != 0 || threadIdx.x != 0 || u != 0 || p.layer != 1) return;
-  const int which = p.type == PH_QKV ? 0 : p.type == PH_O ? 1 : p.type == PH_GU ? 2 : p.type == PH_DN ? 3 : -1;
+  if (!a.prof || c.cta != 0 || threadIdx.x != 0 || u != 0 || (p.layer != 1 && p.type != PH_LM)) return;
+  const int which = p.type == PH_QKV ? 0 : p.type == PH_O ? 1 : p.type == PH_GU ? 2 : p.type == PH_DN ? 3
+                  : p.type == PH_LM ? 4 : -1;
   if (which < 0) return;
   a.prof[2 * (2 + 5 * a.L) + 8 * which + i] = clock64();
 }
@@ -402,6 +391,7 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
     if (gl == (uint32_t)c.warp) stamp(c, p, u, 6);
     const uint8_t* sb = sm + c.S->ring + (size_t)(c.warp * a.nslot + slot) * c.S->slot_bytes;
     qmv_group<FMT, NT, SUB, BF16S>(sb, c.seg, xf, gl, cpg, gsx, gsum, gsq, y);
+    if (gl == (uint32_t)c.warp) stamp(c, p, u, 7);
     __syncwarp();
     if (c.lane == 0) prod_issue(c, slot);
     ++c.k;
@@ -772,12 +762,11 @@ __global__ void __launch_bounds__(kQmvThreads) mega_kernel(const __grid_constant
     fence_barrier_init();
   }
   __syncthreads();
-  unsigned int gen;
-  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(gen) : "l"(&a.bar[1]) : "memory");
+  unsigned long long gen = a.bar_base;
   // start this warp's weight stream
   if (c.lane == 0) {
-    c.pph = 0; c.pu = c.cta; c.pgl = c.warp;
-    prod_normalize(c);
+    c.wl = a.wlist + a.woff[c.cta * kQmvWarps + c.warp];
+    c.wnext = __ldg(c.wl);
     for (uint32_t s = 0; s < a.nslot; ++s) prod_issue(c, s);
   }
   uint32_t ause[kAttStages] = {0, 0};
@@ -815,6 +804,11 @@ __global__ void __launch_bounds__(kQmvThreads) mega_kernel(const __grid_constant
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
       a.prof[2 * ph] = t;
       if (ph == 0 || ph == last) a.prof[2 * (2 + 5 * a.L) + 40 + (ph == 0 ? 0 : 1)] = clock64();
+    }
+    if (a.prof && threadIdx.x == 0 && ph >= 6 && ph < 11 && c.cta < 1024) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      a.prof[2 * (2 + 5 * a.L) + 64 + (ph - 6) * 1024 + c.cta] = t;
     }
     if (ph < last) grid_sync(a.bar, c.G, gen, a.err);
     if (a.prof && c.cta == 0 && threadIdx.x == 0) {
@@ -919,6 +913,32 @@ cudaError_t mega_launch(const MegaArgs& a, int fmt, int bf16s, uint32_t grid, ui
   cudaError_t e = cudaErrorInvalidValue;
   dispatch(fmt, nt, bf16s, a.hd, [&]<int F, int N, bool B, int H>() { e = launch_t<F, N, B, H>(a, grid, smem, st, false); });
   return e;
+}
+
+std::vector<unsigned long long> mega_weight_stream(const MegaArgs& a, int fmt, uint32_t grid,
+                                                   std::vector<uint32_t>* off) {
+  std::vector<unsigned long long> list;
+  off->assign((size_t)grid * kQmvWarps + 1, 0);
+  const uint32_t seg = seg_bytes(fmt, a.gs), last = 1 + 5 * a.L;
+  for (uint32_t cta = 0; cta < grid; ++cta)
+    for (uint32_t w = 0; w < (uint32_t)kQmvWarps; ++w) {
+      (*off)[cta * kQmvWarps + w] = (uint32_t)list.size();
+      for (uint32_t ph = 1; ph <= last; ++ph) {
+        const PhaseInfo p = phase_info(a, nullptr, ph);
+        if (p.type != PH_QKV && p.type != PH_O && p.type != PH_GU && p.type != PH_DN && p.type != PH_LM) continue;
+        for (uint32_t u = cta; u < p.units; u += grid) {
+          uint32_t tile, split, G0, ng;
+          unit_range(p, u, &tile, &split, &G0, &ng);
+          for (uint32_t gl = w; gl < ng; gl += kQmvWarps) {
+            const uint8_t* src = p.w + ((size_t)tile * p.groups + G0 + gl) * (p.sub * seg);
+            list.push_back(reinterpret_cast<unsigned long long>(src) | (p.sub == 2 ? 1ull : 0ull));
+          }
+        }
+      }
+      list.push_back(0ull);
+    }
+  (*off)[(size_t)grid * kQmvWarps] = (uint32_t)list.size();
+  return list;
 }
 
 }  // namespace nnz

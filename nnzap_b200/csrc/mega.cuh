@@ -5,6 +5,7 @@
 #pragma once
 #include "misc.cuh"
 #include "qmv_dev.cuh"
+#include <vector>
 
 namespace nnz {
 
@@ -38,10 +39,15 @@ struct MegaArgs {
   uint32_t* seq;
   uint32_t seq_len;
   float* logits;                // optional [batch][vocab]
-  unsigned int* bar;            // [0] arrival count, [1] generation
+  unsigned int* bar;            // [2] abort flag, [4..5] u64 arrival counter
+  unsigned long long bar_base;  // arrival count before this launch
   int* err;
   uint32_t nslot;               // weight-ring slots per warp
   unsigned long long* prof;     // optional: CTA 0 records %globaltimer after each phase
+  // Weight stream: warp w of CTA c copies the segments wlist[woff[4c+w]..]
+  // in order (address | 1 for a two-matrix segment), up to a 0 entry.
+  const unsigned long long* wlist;
+  const uint32_t* woff;
 };
 
 // Launch (cooperative) with the grid / shared memory chosen by mega_plan.
@@ -50,5 +56,9 @@ cudaError_t mega_launch(const MegaArgs& a, int fmt, int bf16s, uint32_t grid, ui
 // Host-side plan: grid size, smem size, splits.  Returns false if the
 // kernel cannot be co-resident on this device.
 bool mega_plan(MegaArgs& a, int fmt, int bf16s, int device, uint32_t* grid, uint32_t* smem);
+// Host-side weight stream of a plan: every warp's segment sequence, in the
+// order its consumer loop visits them.  `off` gets grid * 4 + 1 offsets.
+std::vector<unsigned long long> mega_weight_stream(const MegaArgs& a, int fmt, uint32_t grid,
+                                                   std::vector<uint32_t>* off);
 
 }  // namespace nnz

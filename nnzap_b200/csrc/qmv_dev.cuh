@@ -242,25 +242,43 @@ __device__ __forceinline__ void qmv_group(const uint8_t* sb, uint32_t seg, const
         const uint32_t bcol = n * 4 + t;
         const float sx = gsx[gl * kBatchChunk + bcol];
         if constexpr (FMT == FMT_Q1) {
+          const uint4 s0 = *reinterpret_cast<const uint4*>(segp + cpg * 512 + g * 32);
+          const uint4 s1 = *reinterpret_cast<const uint4*>(segp + cpg * 512 + g * 32 + 16);
+          const int sq = gsq[gl * kBatchChunk + bcol];
           int D[8][4];
 #pragma unroll
           for (int j = 0; j < 8; ++j) D[j][0] = D[j][1] = D[j][2] = D[j][3] = 0;
-#pragma unroll 1
-          for (uint32_t cc = 0; cc < cpg; ++cc) {
-            const uint4 A = *reinterpret_cast<const uint4*>(segp + cc * 512 + lane * 16);
-            const uint2 B = *reinterpret_cast<const uint2*>(
-                xf + ((size_t)((gl * cpg + cc) * NT + n) * 32 + lane) * 8);
+          const uint8_t* xb = xf + ((size_t)(gl * cpg * NT + n) * 32 + lane) * 8;
+          if (cpg == 4) {
+            // common case (group 128): every operand load issued up front
+            uint4 A[4];
+            uint2 B[4];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const uint32_t msk = 0x01010101u << j;
-              mma_u8s8(D[j], A.x & msk, A.y & msk, A.z & msk, A.w & msk, B.x, B.y);
+            for (int cc = 0; cc < 4; ++cc) {
+              A[cc] = *reinterpret_cast<const uint4*>(segp + cc * 512 + lane * 16);
+              B[cc] = *reinterpret_cast<const uint2*>(xb + (size_t)cc * NT * 256);
+            }
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const uint32_t msk = 0x01010101u << j;
+                mma_u8s8(D[j], A[cc].x & msk, A[cc].y & msk, A[cc].z & msk, A[cc].w & msk, B[cc].x, B[cc].y);
+              }
+          } else {
+#pragma unroll 1
+            for (uint32_t cc = 0; cc < cpg; ++cc) {
+              const uint4 A = *reinterpret_cast<const uint4*>(segp + cc * 512 + lane * 16);
+              const uint2 B = *reinterpret_cast<const uint2*>(xb + (size_t)cc * NT * 256);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const uint32_t msk = 0x01010101u << j;
+                mma_u8s8(D[j], A.x & msk, A.y & msk, A.z & msk, A.w & msk, B.x, B.y);
+              }
             }
           }
-          const uint4 s0 = *reinterpret_cast<const uint4*>(segp + cpg * 512 + g * 32);
-          const uint4 s1 = *reinterpret_cast<const uint4*>(segp + cpg * 512 + g * 32 + 16);
           const uint16_t* sc0 = reinterpret_cast<const uint16_t*>(&s0);
           const uint16_t* sc1 = reinterpret_cast<const uint16_t*>(&s1);
-          const int sq = gsq[gl * kBatchChunk + bcol];
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
 #pragma unroll
