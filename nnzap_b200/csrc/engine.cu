@@ -13,6 +13,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <cmath>
 #include <map>
 #include <mutex>
 #include <string>
@@ -218,7 +219,8 @@ struct nnz_model {
   MegaLayer* mlayers = nullptr;
   float *mR = nullptr, *mqkv = nullptr, *mgu = nullptr, *matt = nullptr;
   unsigned int* mbar = nullptr;
-  unsigned long long mbar_count = 0;   // grid-barrier arrivals so far (device counter's value)
+  unsigned long long mbar_count = 0;
+  float2* rope_tab = nullptr;          // [max_ctx][head_dim / 2] (cos, sin)   // grid-barrier arrivals so far (device counter's value)
   unsigned long long* mprof = nullptr;    // NNZ_MEGA_PROFILE=1: per-phase timestamps
   struct MegaPlan { MegaArgs a; uint32_t grid, smem; bool ok; };
   std::map<uint32_t, MegaPlan> mplans;
@@ -488,7 +490,7 @@ const nnz_model::MegaPlan* mega_plan_for(nnz_model* m, uint32_t rows) {
   a.H = c.hidden_size; a.I = c.intermediate_size; a.n_q = c.num_query_heads; a.n_kv = c.num_kv_heads;
   a.hd = c.head_dim; a.L = c.num_layers; a.vocab = c.vocab_size; a.gs = (uint32_t)c.group_size;
   a.max_ctx = c.max_context_length; a.batch = rows; a.eps = c.eps; a.theta = c.rope_theta;
-  a.rope_style = c.rope_style; a.bf16r = m->bf16r; a.layers = m->mlayers; a.lm = m->lm; a.fnorm = m->fnorm;
+  a.rope_style = c.rope_style; a.bf16r = m->bf16r; a.layers = m->mlayers; a.rope_tab = m->rope_tab; a.lm = m->lm; a.fnorm = m->fnorm;
   a.emb_w = m->emb_w; a.emb_s = m->emb_s; a.emb_b = m->emb_b; a.kc = m->kc; a.vc = m->vc;
   a.kv_layer = m->kv_layer; a.R = m->mR; a.qkv_acc = m->mqkv; a.gu_acc = m->mgu; a.att_ws = m->matt;
   a.st = m->state; a.seq = m->seq; a.seq_len = c.max_context_length; a.logits = nullptr;
@@ -895,6 +897,20 @@ int nnz_model_finalize(nnz_model* m) {
       }
       if ((rc = dalloc(m, (void**)&m->mlayers, sizeof(MegaLayer) * c.num_layers))) return rc;
       NNZ_CK(cudaMemset(m->mbar, 0, 64));
+      {
+        // rotary (cos, sin) per position and pair, in double like the
+        // kernels' own evaluation, rounded to f32
+        const uint32_t half = c.head_dim / 2;
+        std::vector<float2> tab((size_t)c.max_context_length * half);
+        const double l2t = std::log2((double)c.rope_theta);
+        for (uint32_t p = 0; p < c.max_context_length; ++p)
+          for (uint32_t i = 0; i < half; ++i) {
+            const double ang = (double)p * std::exp2(-(2.0 * i / c.head_dim) * l2t);
+            tab[(size_t)p * half + i] = make_float2((float)std::cos(ang), (float)std::sin(ang));
+          }
+        if ((rc = dalloc(m, (void**)&m->rope_tab, tab.size() * sizeof(float2)))) return rc;
+        NNZ_CK(cudaMemcpy(m->rope_tab, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+      }
       std::vector<MegaLayer> ml(c.num_layers);
       for (uint32_t l = 0; l < c.num_layers; ++l) {
         const LayerW& W = m->L[l];

@@ -332,7 +332,7 @@ __device__ __forceinline__ void stamp(const Ctx& c, const PhaseInfo& p, uint32_t
   const MegaArgs& a = *c.a;
   if (!a.prof || c.cta != 0 || threadIdx.x != 0 || u != 0 || (p.layer != 1 && p.type != PH_LM)) return;
   const int which = p.type == PH_QKV ? 0 : p.type == PH_O ? 1 : p.type == PH_GU ? 2 : p.type == PH_DN ? 3
-                  : p.type == PH_LM ? 4 : -1;
+                  : p.type == PH_LM ? 4 : p.type == PH_ATT ? 5 : -1;
   if (which < 0) return;
   a.prof[2 * (2 + 5 * a.L) + 8 * which + i] = clock64();
 }
@@ -507,17 +507,64 @@ __device__ __forceinline__ void att_scores(const __half* kr, const float* qs, fl
   }
 }
 
+// Cache range of one attention unit (kv head, row, split).
+struct AttGeom {
+  int pos, t0, ncache, nblk;
+  bool own_new;
+  size_t head_off;
+};
+
+__device__ __forceinline__ AttGeom att_geom(const MegaArgs& a, const PhaseInfo& p, uint32_t u, bool report) {
+  const uint32_t S = a.att_splits;
+  const uint32_t kvh = u % a.n_kv, b = (u / a.n_kv) % a.batch, split = u / (a.n_kv * a.batch);
+  AttGeom g;
+  int pos = __ldcg(&a.st->pos[b]);
+  if (pos < 0 || pos >= (int)a.max_ctx) {
+    if (report && threadIdx.x == 0) atomicOr(a.err, ERR_BAD_POS);
+    pos = pos < 0 ? 0 : (int)a.max_ctx - 1;
+  }
+  const int seq = pos + 1;
+  const int per = (seq + (int)S - 1) / (int)S;
+  g.pos = pos;
+  g.t0 = (int)split * per;
+  const int t1 = min(seq, g.t0 + per);
+  g.own_new = g.t0 <= pos && pos < t1;
+  const int cend = min(t1, pos);
+  g.ncache = cend > g.t0 ? cend - g.t0 : 0;
+  g.nblk = (g.ncache + kAttBlk - 1) / kAttBlk;
+  g.head_off = a.kv_layer * p.layer + ((size_t)b * a.n_kv + kvh) * a.max_ctx * a.hd;
+  return g;
+}
+
+// Start the K and V copies of cached block `blk` of a unit (one thread).
+template <int HD>
+__device__ __forceinline__ void att_issue(const Ctx& c, const AttGeom& g, int blk) {
+  const MegaArgs& a = *c.a;
+  uint64_t* abars = reinterpret_cast<uint64_t*>(c.smem + c.S->abars);
+  __half* kring = reinterpret_cast<__half*>(c.smem + c.S->kring);
+  __half* vring = reinterpret_cast<__half*>(c.smem + c.S->vring);
+  const int stg = blk % kAttStages;
+  const int n = min(kAttBlk, g.ncache - blk * kAttBlk);
+  const uint32_t bytes = (uint32_t)n * HD * 2;
+  // the ring overlays shared memory last written through the generic proxy
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  mbar_arrive_expect_tx(&abars[stg], 2 * bytes);
+  bulk_g2s(kring + (size_t)stg * kAttBlk * HD, a.kc + g.head_off + (size_t)(g.t0 + blk * kAttBlk) * HD, bytes, &abars[stg]);
+  bulk_g2s(vring + (size_t)stg * kAttBlk * HD, a.vc + g.head_off + (size_t)(g.t0 + blk * kAttBlk) * HD, bytes, &abars[stg]);
+}
+
 // ---- attention work unit -----------------------------------------------------
 // One (kv head, row, split): QK-norm + RoPE of the G query heads (and of the
 // new key when this split owns the current position, which it then writes to
 // the cache), online softmax over the split's cached positions streamed in
 // 32-position blocks, partial (m, l, o) to att_ws.
 template <int HD>
-__device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause)[kAttStages]) {
+__device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause)[kAttStages], bool prefetched) {
   constexpr int EPL = HD / 32;
   const MegaArgs& a = *c.a;
   const uint32_t S = a.att_splits, G = a.n_q / a.n_kv;
   const uint32_t kvh = u % a.n_kv, b = (u / a.n_kv) % a.batch, split = u / (a.n_kv * a.batch);
+  (void)split;
   uint8_t* sm = c.smem;
   uint64_t* abars = reinterpret_cast<uint64_t*>(sm + c.S->abars);
   __half* kring = reinterpret_cast<__half*>(sm + c.S->kring);
@@ -531,31 +578,13 @@ __device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause
   float* alp = lst + kAttMaxG;
   const int warp = c.warp, lane = c.lane;
 
-  int pos = __ldcg(&a.st->pos[b]);
-  if (pos < 0 || pos >= (int)a.max_ctx) {
-    if (threadIdx.x == 0) atomicOr(a.err, ERR_BAD_POS);
-    pos = pos < 0 ? 0 : (int)a.max_ctx - 1;
-  }
-  const int seq = pos + 1;
-  const int per = (seq + (int)S - 1) / (int)S;
-  const int t0 = (int)split * per;
-  const int t1 = min(seq, t0 + per);
-  const bool own_new = t0 <= pos && pos < t1;
-  const int cend = min(t1, pos);
-  const int ncache = cend > t0 ? cend - t0 : 0;
-  const int nblk = (ncache + kAttBlk - 1) / kAttBlk;
-  const size_t head_off = a.kv_layer * p.layer + ((size_t)b * a.n_kv + kvh) * a.max_ctx * HD;
-  const __half* kb = a.kc + head_off;
-  const __half* vb = a.vc + head_off;
-  auto issue = [&](int blk) {
-    const int stg = blk % kAttStages;
-    const int n = min(kAttBlk, ncache - blk * kAttBlk);
-    const uint32_t bytes = (uint32_t)n * HD * 2;
-    mbar_arrive_expect_tx(&abars[stg], 2 * bytes);
-    bulk_g2s(kring + (size_t)stg * kAttBlk * HD, kb + (size_t)(t0 + blk * kAttBlk) * HD, bytes, &abars[stg]);
-    bulk_g2s(vring + (size_t)stg * kAttBlk * HD, vb + (size_t)(t0 + blk * kAttBlk) * HD, bytes, &abars[stg]);
-  };
-  if (threadIdx.x == 0)
+  stamp(c, p, u, 0);
+  const AttGeom ag = att_geom(a, p, u, true);
+  const int pos = ag.pos, t0 = ag.t0, ncache = ag.ncache, nblk = ag.nblk;
+  const bool own_new = ag.own_new;
+  const size_t head_off = ag.head_off;
+  auto issue = [&](int blk) { att_issue<HD>(c, ag, blk); };
+  if (threadIdx.x == 0 && !prefetched)
     for (int blk = 0; blk < nblk && blk < kAttStages; ++blk) issue(blk);
 
   const uint32_t qkv_rows = (a.n_q + 2 * a.n_kv) * HD;
@@ -564,14 +593,15 @@ __device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause
   const float* kn = lptr(a, a.l0.k_norm, p.layer);
   for (uint32_t h = warp; h < G; h += kQmvWarps) {
     float v[EPL];
-    norm_rope_head<HD>(qrow + (size_t)(kvh * G + h) * HD, qn, a.eps, a.theta, a.rope_style, pos, lane, v);
+    norm_rope_head<HD>(qrow + (size_t)(kvh * G + h) * HD, qn, a.eps, a.theta, a.rope_style, pos, lane, v,
+                       a.rope_tab + (size_t)pos * (HD / 2));
 #pragma unroll
     for (int e = 0; e < EPL; ++e) qs[h * HD + lane * EPL + e] = v[e];
   }
   if (own_new && warp == kQmvWarps - 1) {
     float v[EPL];
     norm_rope_head<HD>(qrow + (size_t)a.n_q * HD + (size_t)kvh * HD, kn, a.eps, a.theta, a.rope_style,
-                       pos, lane, v);
+                       pos, lane, v, a.rope_tab + (size_t)pos * (HD / 2));
     const float* vsrc = qrow + (size_t)(a.n_q + a.n_kv) * HD + (size_t)kvh * HD;
 #pragma unroll
     for (int e = 0; e < EPL; ++e) {
@@ -589,6 +619,7 @@ __device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause
     lst[threadIdx.x] = 0.f;
   }
   __syncthreads();
+  stamp(c, p, u, 1);
 
   constexpr int NHS = kQmvThreads / HD;
   const int d = threadIdx.x % HD, hs = threadIdx.x / HD;
@@ -606,6 +637,7 @@ __device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause
     if (!is_new) {
       if (!c.failed) c.failed = !mbar_wait_abort(&abars[stg], ause[stg] & 1u, a.err, &a.bar[2]);
       ause[stg] += 1;
+      if (blk == 0) stamp(c, p, u, 2);
     }
     if (!is_new && (G == 1 || G == 2 || G == 4)) {
       // 8 positions per warp; every lane forms the partial dots of its dims
@@ -660,8 +692,10 @@ __device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause
       acc[h] = o;
     }
     __syncthreads();
+    if (blk == 0) stamp(c, p, u, 3);
     if (!is_new && threadIdx.x == 0 && blk + kAttStages < nblk) issue(blk + kAttStages);
   }
+  stamp(c, p, u, 4);
   const uint32_t rec = HD + 2;
   float* wsp = a.att_ws + (((size_t)(b * a.n_kv + kvh) * S + split) * G) * rec;
   for (uint32_t h = hs; h < G; h += NHS) wsp[(size_t)h * rec + 2 + d] = acc[h];
@@ -670,6 +704,7 @@ __device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause
     wsp[(size_t)threadIdx.x * rec + 1] = lst[threadIdx.x];
   }
   __syncthreads();
+  stamp(c, p, u, 5);
 }
 
 // ---- embedding phase -------------------------------------------------------------
@@ -778,7 +813,7 @@ __global__ void __launch_bounds__(kQmvThreads) mega_kernel(const __grid_constant
         embed_phase<FMT, BF16S>(c);
         break;
       case PH_ATT:
-        for (uint32_t u = c.cta; u < p.units; u += c.G) att_unit<HD>(c, p, u, ause);
+        for (uint32_t u = c.cta; u < p.units; u += c.G) att_unit<HD>(c, p, u, ause, u == c.cta);
         break;
       case PH_GU:
         grid_zero(a.qkv_acc, (size_t)a.batch * (a.n_q + 2 * a.n_kv) * a.hd, c);
@@ -797,13 +832,23 @@ __global__ void __launch_bounds__(kQmvThreads) mega_kernel(const __grid_constant
         if (p.type == PH_O) grid_zero(resv(a, 2 * p.layer + 2), (size_t)a.batch * a.H, c);
         if (p.type == PH_DN) grid_zero(resv(a, 2 * p.layer + 3), (size_t)a.batch * a.H, c);
         for (uint32_t u = c.cta; u < p.units; u += c.G) qmv_unit<FMT, NT, 1, BF16S>(c, p, u);
+        if (p.type == PH_QKV) {
+          // the cached K/V blocks of this CTA's first attention unit do not
+          // depend on the barrier: start their copies now (the matvec's
+          // shared-memory view is dead after its last unit's final sync)
+          const PhaseInfo pa = phase_at(c, ph + 1);
+          if (c.cta < pa.units && threadIdx.x == 0) {
+            const AttGeom ag = att_geom(a, pa, c.cta, false);
+            for (int blk = 0; blk < ag.nblk && blk < kAttStages; ++blk) att_issue<HD>(c, ag, blk);
+          }
+        }
         break;
     }
     if (a.prof && c.cta == 0 && threadIdx.x == 0) {
       unsigned long long t;
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
       a.prof[2 * ph] = t;
-      if (ph == 0 || ph == last) a.prof[2 * (2 + 5 * a.L) + 40 + (ph == 0 ? 0 : 1)] = clock64();
+      if (ph == 0 || ph == last) a.prof[2 * (2 + 5 * a.L) + 62 + (ph == 0 ? 0 : 1)] = clock64();
     }
     if (a.prof && threadIdx.x == 0 && ph >= 6 && ph < 11 && c.cta < 1024) {
       unsigned long long t;

@@ -18,6 +18,7 @@ struct MegaArgs {
   uint32_t H, I, n_q, n_kv, hd, L, vocab, gs, max_ctx, batch;
   float eps, theta;
   int rope_style, bf16r;
+  const float2* rope_tab;       // [max_ctx][hd / 2] (cos, sin) of every position
   const MegaLayer* layers;      // device array [L] (unused on the hot path)
   MegaLayer l0;                 // layer 0 pointers; layer l = l0 + l * lstride bytes
   size_t lstride;
