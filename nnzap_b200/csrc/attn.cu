@@ -1,6 +1,8 @@
 // Decode attention kernels (see attn.cuh).
 #include <cuda_runtime.h>
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "attn.cuh"
 #include "rope_dev.cuh"
@@ -295,7 +297,9 @@ cudaError_t attn_launch_t(const AttnArgs& a, int pdl, cudaStream_t st) {
 }  // namespace
 
 cudaError_t attn_prepare() {
-  cudaError_t e = cudaFuncSetAttribute(&attn_decode_kernel<128>,
+  cudaError_t e = attn_tc_prepare();
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(&attn_decode_kernel<128>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        attn_layout<128>().total);
   if (e != cudaSuccess) return e;
@@ -303,15 +307,28 @@ cudaError_t attn_prepare() {
                               attn_layout<64>().total);
 }
 
-size_t attn_ws_floats(uint32_t rows, uint32_t n_q, uint32_t n_kv, uint32_t splits, int head_dim) {
-  if (splits <= 1) return 0;
-  return (size_t)rows * n_kv * splits * (n_q / n_kv) * (head_dim + 2);
+size_t attn_ws_floats(uint32_t rows, uint32_t n_q, uint32_t n_kv, uint32_t splits, int head_dim,
+                      uint32_t max_ctx) {
+  const size_t legacy = splits <= 1 ? 0 : (size_t)rows * n_kv * splits * (n_q / n_kv) * (head_dim + 2);
+  const size_t tc = attn_tc_applies(n_q, n_kv, head_dim) ? attn_tc_ws_floats(rows, n_q, n_kv, max_ctx) : 0;
+  return legacy > tc ? legacy : tc;
 }
+
+namespace {
+bool use_legacy_attn() {
+  static const int v = [] {
+    const char* e = getenv("NNZ_ATTN");
+    return (e && strcmp(e, "legacy") == 0) ? 1 : 0;
+  }();
+  return v != 0;
+}
+}  // namespace
 
 cudaError_t attn_decode_launch(const AttnArgs& a, int head_dim, int pdl, cudaStream_t st) {
   if (a.n_kv == 0 || a.n_q % a.n_kv || a.n_q / a.n_kv > (uint32_t)kAttnMaxG || a.splits == 0 ||
       a.rows == 0)
     return cudaErrorInvalidValue;
+  if (attn_tc_applies(a.n_q, a.n_kv, head_dim) && a.ws && !use_legacy_attn()) return attn_tc_launch(a, pdl, st);
   if (head_dim == 128) return attn_launch_t<128>(a, pdl, st);
   if (head_dim == 64) return attn_launch_t<64>(a, pdl, st);
   return cudaErrorInvalidValue;

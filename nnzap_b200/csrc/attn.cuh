@@ -28,6 +28,7 @@ constexpr int kAttnThreads = 128;
 constexpr int kAttnBlk = 32;     // positions per streamed block
 constexpr int kAttnStages = 4;
 constexpr int kAttnMaxG = 8;     // query heads per kv head
+constexpr int kTcChunk = 256;    // positions per task of the tensor-core kernel
 
 
 struct AttnArgs {
@@ -51,12 +52,23 @@ struct AttnArgs {
   float* ws;
   uint32_t* counters;  // [rows][n_kv], zero at rest
   int* err;
+  const float2* rope_tab;   // optional [max_ctx][hd / 2] (cos, sin) table
 };
 
 // Raise the dynamic shared-memory limit (once per device, before launches).
 cudaError_t attn_prepare();
+// Picks the tensor-core kernel (attn_tc.cu) when it applies (head_dim 128,
+// G in {1, 2, 4}; NNZ_ATTN=legacy forces the other), else the CUDA-core one.
 cudaError_t attn_decode_launch(const AttnArgs& a, int head_dim, int pdl, cudaStream_t st);
-size_t attn_ws_floats(uint32_t rows, uint32_t n_q, uint32_t n_kv, uint32_t splits, int head_dim);
+// Workspace (floats) either kernel may need.
+size_t attn_ws_floats(uint32_t rows, uint32_t n_q, uint32_t n_kv, uint32_t splits, int head_dim,
+                      uint32_t max_ctx);
+
+// Tensor-core decode attention (attn_tc.cu).
+bool attn_tc_applies(uint32_t n_q, uint32_t n_kv, int head_dim);
+size_t attn_tc_ws_floats(uint32_t rows, uint32_t n_q, uint32_t n_kv, uint32_t max_ctx);
+cudaError_t attn_tc_prepare();
+cudaError_t attn_tc_launch(const AttnArgs& a, int pdl, cudaStream_t st);
 
 // Writes normed+roped k and v of `rows` query rows at their positions
 // (used by chunked prefill, where rows of one chunk share a cache slot and

@@ -1,0 +1,423 @@
+// Decode attention on the tensor cores (head_dim 128, GQA group 1, 2 or 4).
+//
+// Same result as attn_decode_kernel (q = RoPE(RMSNorm_hd(q) * qn) in f32,
+// scores q.k / sqrt(hd) in f32, f32 softmax, fp16 output; reference
+// nnmetal/src/shaders/transformer.metal:1467-1695), reorganised so that a
+// batch of long sequences streams the KV cache at HBM speed:
+//
+//  1. attn_tc_prep_kernel, one CTA per (kv head, row): QK-norm + RoPE of the
+//     G query heads, stored as fp16 hi/lo pairs (q = hi + lo to ~22 bits),
+//     and (decode) the new K/V written into the cache at `pos`.
+//  2. attn_tc_kernel, persistent: every warp owns a stream of tasks
+//     (row, kv head, 256-position chunk) and a private 3-stage shared-memory
+//     ring of 16-position K/V blocks filled by 1-D bulk copies, one 256-byte
+//     row per copy into rows padded to 272 bytes (conflict-free ldmatrix).
+//     S = Q.K^T and O += P.V run as mma.m16n8k16 (f16 in, f32 accumulate)
+//     with A rows [q_hi(G) | q_lo(G)] and [p_hi(G) | p_lo(G)], so each f32
+//     operand enters the tensor core as an exact-to-2^-22 pair; the online
+//     softmax keeps its statistics in the score fragments' lanes.  The ring
+//     runs ahead across task boundaries, so a warp never drains it.
+//  3. attn_tc_combine_kernel, one CTA per (kv head, row): merges the
+//     chunks' (m, l, o) and writes the fp16 output.
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include "attn.cuh"
+#include "rope_dev.cuh"
+
+namespace nnz {
+
+namespace {
+
+constexpr int kHD = 128;
+constexpr int kTcWarps = 4;
+constexpr int kTcBlk = 16;              // positions per streamed block
+constexpr int kTcStages = 3;
+constexpr int kTcRowB = kHD * 2 + 16;   // padded shared-memory row (bytes)
+constexpr int kTcSlotB = 2 * kTcBlk * kTcRowB;   // K rows then V rows
+constexpr int kTcWarpB = kTcStages * kTcSlotB + 64;
+constexpr int kTcSmem = kTcWarps * kTcWarpB;
+constexpr int kTcQRows = 8;             // hi/lo query rows per (row, kv head)
+
+__host__ __device__ inline uint32_t tc_chunks(uint32_t max_ctx) { return (max_ctx + kTcChunk - 1) / kTcChunk; }
+
+struct TcArgs {
+  AttnArgs a;
+  uint32_t nch;        // chunks per (row, kv head) at max_ctx
+  uint32_t ntasks;
+  float* part;         // [rows][n_kv][nch][G][hd + 2]
+  __half* q16;         // [rows][n_kv][8][hd]
+};
+
+__device__ __forceinline__ int clamp_pos(const AttnArgs& a, uint32_t row, bool report) {
+  int p = a.pos[row];
+  if (p < 0 || p >= (int)a.max_ctx) {
+    if (report) atomicOr(a.err, ERR_BAD_POS);
+    p = p < 0 ? 0 : (int)a.max_ctx - 1;
+  }
+  return p;
+}
+
+// ---------------------------------------------------------------------------
+// 1. query prep (+ KV write)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(160) attn_tc_prep_kernel(TcArgs t) {
+  constexpr int EPL = kHD / 32;
+  const AttnArgs& a = t.a;
+  pdl_wait();
+  pdl_launch();
+  const int kvh = blockIdx.x, row = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = (int)(a.n_q / a.n_kv);
+  const int p = clamp_pos(a, row, threadIdx.x == 0);
+  const __half* qrow = a.qkv + (size_t)row * a.qkv_stride;
+  __half* q16 = t.q16 + ((size_t)row * a.n_kv + kvh) * kTcQRows * kHD;
+  if (warp < G) {
+    float v[EPL];
+    norm_rope_head<kHD>(qrow + (size_t)(kvh * G + warp) * kHD, a.q_norm, a.eps, a.theta, a.rope_style, p,
+                        lane, v, a.rope_tab ? a.rope_tab + (size_t)p * (kHD / 2) : nullptr);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const __half hi = __float2half_rn(v[e]);
+      const __half lo = __float2half_rn(v[e] - __half2float(hi));
+      q16[(size_t)warp * kHD + lane * EPL + e] = hi;
+      q16[(size_t)(G + warp) * kHD + lane * EPL + e] = lo;
+    }
+  } else if (warp == 4 && a.write_kv) {
+    const int slot = a.slot ? a.slot[row] : row;
+    const size_t off = (((size_t)slot * a.n_kv + kvh) * a.max_ctx + p) * kHD;
+    float v[EPL];
+    norm_rope_head<kHD>(qrow + (size_t)a.n_q * kHD + (size_t)kvh * kHD, a.k_norm, a.eps, a.theta,
+                        a.rope_style, p, lane, v,
+                        a.rope_tab ? a.rope_tab + (size_t)p * (kHD / 2) : nullptr);
+    const __half* vsrc = qrow + (size_t)(a.n_q + a.n_kv) * kHD + (size_t)kvh * kHD;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      a.kc[off + lane * EPL + e] = __float2half_rn(v[e]);
+      a.vc[off + lane * EPL + e] = vsrc[lane * EPL + e];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 2. streaming attention
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float x, float y) {
+  const __half2 h = __floats2half2_rn(x, y);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// One task's cache range; false when the chunk lies past the row's position.
+struct TcTask {
+  uint32_t row, kvh, c;
+  int npos, nblk;
+  size_t off;   // element offset of the chunk's first position in the layer's K/V
+};
+
+__device__ __forceinline__ bool tc_task(const TcArgs& t, uint32_t task, TcTask& k) {
+  const AttnArgs& a = t.a;
+  k.c = task % t.nch;
+  const uint32_t rk = task / t.nch;
+  k.kvh = rk % a.n_kv;
+  k.row = rk / a.n_kv;
+  const int seq = clamp_pos(a, k.row, false) + 1;
+  const int t0 = (int)k.c * kTcChunk;
+  if (t0 >= seq) return false;
+  k.npos = min(kTcChunk, seq - t0);
+  k.nblk = (k.npos + kTcBlk - 1) / kTcBlk;
+  const int slot = a.slot ? a.slot[k.row] : (int)k.row;
+  k.off = (((size_t)slot * a.n_kv + k.kvh) * a.max_ctx + t0) * kHD;
+  return true;
+}
+
+template <int G>
+__global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(const __grid_constant__ TcArgs t) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const AttnArgs& a = t.a;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q4 = lane & 3;
+  uint8_t* ring = smem + warp * kTcWarpB;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + kTcStages * kTcSlotB);
+  if (lane == 0) {
+    for (int s = 0; s < kTcStages; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+  pdl_wait();
+  pdl_launch();
+  const uint32_t stride = gridDim.x * kTcWarps;
+  const uint32_t first = blockIdx.x * kTcWarps + warp;
+  bool failed = false;
+
+  // producer cursor: next block to copy
+  uint32_t ptask = first;
+  TcTask pk;
+  bool pvalid = false;
+  while (ptask < t.ntasks && !(pvalid = tc_task(t, ptask, pk))) ptask += stride;
+  int pblk = 0;
+  auto issue = [&](int stg) {
+    uint8_t* slot = ring + stg * kTcSlotB;
+    const int n = min(kTcBlk, pk.npos - pblk * kTcBlk);
+    // the slot was last read through the generic proxy (ldmatrix)
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (lane == 0) mbar_arrive_expect_tx(&bars[stg], (uint32_t)(2 * n * kHD * 2));
+    __syncwarp();
+    const size_t src = pk.off + (size_t)(pblk * kTcBlk) * kHD;
+    const int r = lane & 15;
+    const bool isv = lane >= 16;
+    uint8_t* dst = slot + (isv ? kTcBlk * kTcRowB : 0) + r * kTcRowB;
+    if (r < n) {
+      bulk_g2s(dst, (isv ? a.vc : a.kc) + src + (size_t)r * kHD, kHD * 2, &bars[stg]);
+    } else if (isv) {
+      // rows past the chunk: zero V so that 0-probability * V stays 0
+      for (int i = 0; i < kHD * 2 / 16; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
+    }
+    if (++pblk == pk.nblk) {
+      pblk = 0;
+      pvalid = false;
+      ptask += stride;
+      while (ptask < t.ntasks && !(pvalid = tc_task(t, ptask, pk))) ptask += stride;
+    }
+  };
+  int pstg = 0;
+  for (int s = 0; s < kTcStages && pvalid; ++s) {
+    issue(pstg);
+    pstg = pstg + 1 == kTcStages ? 0 : pstg + 1;
+  }
+
+  uint32_t ctask = first;
+  int cstg = 0;
+  uint32_t cphase = 0;   // bit s: parity of stage s
+  const float inv = rsqrtf((float)kHD);
+  for (;;) {
+    TcTask ck;
+    bool cvalid = false;
+    while (ctask < t.ntasks && !(cvalid = tc_task(t, ctask, ck))) ctask += stride;
+    if (!cvalid) break;
+    // query fragments: rows g < 2G (hi then lo), zero above
+    uint32_t qa[8][2];
+    {
+      const __half* qp = t.q16 + ((size_t)ck.row * a.n_kv + ck.kvh) * kTcQRows * kHD + (size_t)g * kHD;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        qa[ks][0] = g < 2 * G ? __ldcg(reinterpret_cast<const unsigned int*>(qp + 16 * ks + 2 * q4)) : 0u;
+        qa[ks][1] = g < 2 * G ? __ldcg(reinterpret_cast<const unsigned int*>(qp + 16 * ks + 8 + 2 * q4)) : 0u;
+      }
+    }
+    float o[16][4];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m = -INFINITY, l = 0.f;
+    for (int blk = 0; blk < ck.nblk; ++blk) {
+      if (!failed) failed = !mbar_wait(&bars[cstg], (cphase >> cstg) & 1u, a.err);
+      cphase ^= 1u << cstg;
+      const uint32_t kbase = smem_u32(ring + cstg * kTcSlotB);
+      const uint32_t vbase = kbase + kTcBlk * kTcRowB;
+      // S = Q K^T for 16 positions (two n-tiles of 8)
+      float s[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+        for (int kq = 0; kq < 4; ++kq) {
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4(kbase + (nt * 8 + (lane & 7)) * kTcRowB + (4 * kq + (lane >> 3)) * 16, r0, r1, r2, r3);
+          mma_f16(s[nt], qa[2 * kq][0], 0u, qa[2 * kq][1], 0u, r0, r1);
+          mma_f16(s[nt], qa[2 * kq + 1][0], 0u, qa[2 * kq + 1][1], 0u, r2, r3);
+        }
+      }
+      // hi + lo rows, scale, mask
+      const int nvalid = ck.npos - blk * kTcBlk;
+      float sv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float x = s[i >> 1][i & 1];
+        const float y = __shfl_xor_sync(0xffffffffu, x, 4 * G);
+        const int pl = (i >> 1) * 8 + 2 * q4 + (i & 1);
+        sv[i] = pl < nvalid ? (x + y) * inv : -INFINITY;
+      }
+      float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn = fmaxf(m, mx);
+      const float al = m == -INFINITY ? 0.f : expf(m - mn);
+      m = mn;
+      float pv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pv[i] = expf(sv[i] - mn);
+      l = l * al + (pv[0] + pv[1] + pv[2] + pv[3]);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) { o[j][0] *= al; o[j][1] *= al; }
+      // P fragments: rows g < G carry fp16(p), rows G..2G-1 the residual
+      uint32_t pa0, pa2;
+      if (g < G) {
+        pa0 = pack_h2(pv[0], pv[1]);
+        pa2 = pack_h2(pv[2], pv[3]);
+      } else if (g < 2 * G) {
+        pa0 = pack_h2(pv[0] - __half2float(__float2half_rn(pv[0])), pv[1] - __half2float(__float2half_rn(pv[1])));
+        pa2 = pack_h2(pv[2] - __half2float(__float2half_rn(pv[2])), pv[3] - __half2float(__float2half_rn(pv[3])));
+      } else {
+        pa0 = pa2 = 0u;
+      }
+      // O += P V
+#pragma unroll
+      for (int jp = 0; jp < 8; ++jp) {
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4_t(vbase + ((lane & 7) + 8 * ((lane >> 3) & 1)) * kTcRowB + (2 * jp + (lane >> 4)) * 16, r0, r1,
+                  r2, r3);
+        mma_f16(o[2 * jp], pa0, 0u, pa2, 0u, r0, r1);
+        mma_f16(o[2 * jp + 1], pa0, 0u, pa2, 0u, r2, r3);
+      }
+      __syncwarp();
+      if (pvalid) issue(cstg);   // refill the slot just consumed
+      cstg = cstg + 1 == kTcStages ? 0 : cstg + 1;
+    }
+    // task epilogue: full row sums, hi + lo output rows, partial record
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] += __shfl_xor_sync(0xffffffffu, o[j][0], 4 * G);
+      o[j][1] += __shfl_xor_sync(0xffffffffu, o[j][1], 4 * G);
+    }
+    if (g < G) {
+      float* rec = t.part + ((((size_t)ck.row * a.n_kv + ck.kvh) * t.nch + ck.c) * G + g) * (kHD + 2);
+      if (q4 == 0) { rec[0] = m; rec[1] = l; }
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        *reinterpret_cast<float2*>(rec + 2 + 8 * j + 2 * q4) = make_float2(o[j][0], o[j][1]);
+    }
+    ctask += stride;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 3. merge the chunks
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kHD) attn_tc_combine_kernel(TcArgs t) {
+  const AttnArgs& a = t.a;
+  pdl_wait();
+  pdl_launch();
+  const int kvh = blockIdx.x, row = blockIdx.y, d = threadIdx.x;
+  const uint32_t G = a.n_q / a.n_kv;
+  const int seq = clamp_pos(a, row, false) + 1;
+  const uint32_t nc = (uint32_t)(seq + kTcChunk - 1) / kTcChunk;
+  __half* orow = a.out + (size_t)row * a.out_stride + (size_t)kvh * G * kHD;
+  for (uint32_t h = 0; h < G; ++h) {
+    const float* base = t.part + (((size_t)row * a.n_kv + kvh) * t.nch * G + h) * (kHD + 2);
+    const size_t cs = (size_t)G * (kHD + 2);
+    float M = -INFINITY, L = 0.f, o = 0.f;
+    for (uint32_t c0 = 0; c0 < nc; c0 += 8) {
+      float mv[8], lv[8], ov[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const bool ok = c0 + j < nc;
+        const float* r = base + (c0 + j) * cs;
+        mv[j] = ok ? __ldcg(r) : -INFINITY;
+        lv[j] = ok ? __ldcg(r + 1) : 0.f;
+        ov[j] = ok ? __ldcg(r + 2 + d) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (mv[j] == -INFINITY) continue;
+        const float nm = fmaxf(M, mv[j]);
+        const float a0 = M == -INFINITY ? 0.f : expf(M - nm), a1 = expf(mv[j] - nm);
+        L = L * a0 + lv[j] * a1;
+        o = o * a0 + ov[j] * a1;
+        M = nm;
+      }
+    }
+    orow[h * kHD + d] = __float2half_rn(o / L);
+  }
+}
+
+cudaLaunchConfig_t tc_cfg(dim3 grid, dim3 block, uint32_t smem, int pdl, cudaStream_t st, cudaLaunchAttribute* at) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+int g_tc_sms[64];
+
+}  // namespace
+
+bool attn_tc_applies(uint32_t n_q, uint32_t n_kv, int head_dim) {
+  if (head_dim != kHD || n_kv == 0 || n_q % n_kv) return false;
+  const uint32_t G = n_q / n_kv;
+  return G == 1 || G == 2 || G == 4;
+}
+
+size_t attn_tc_ws_floats(uint32_t rows, uint32_t n_q, uint32_t n_kv, uint32_t max_ctx) {
+  const size_t G = n_q / n_kv;
+  return (size_t)rows * n_kv * tc_chunks(max_ctx) * G * (kHD + 2) + (size_t)rows * n_kv * kTcQRows * kHD / 2;
+}
+
+cudaError_t attn_tc_prepare() {
+  cudaError_t e = cudaFuncSetAttribute(&attn_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(&attn_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(&attn_tc_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+  return e;
+}
+
+cudaError_t attn_tc_launch(const AttnArgs& a, int pdl, cudaStream_t st) {
+  if (!attn_tc_applies(a.n_q, a.n_kv, kHD) || a.rows == 0 || !a.ws) return cudaErrorInvalidValue;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!g_tc_sms[dev]) {
+    int sms = 0;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    g_tc_sms[dev] = sms;
+  }
+  TcArgs t{};
+  t.a = a;
+  t.nch = tc_chunks(a.max_ctx);
+  t.ntasks = a.rows * a.n_kv * t.nch;
+  const uint32_t G = a.n_q / a.n_kv;
+  t.part = a.ws;
+  t.q16 = reinterpret_cast<__half*>(a.ws + (size_t)a.rows * a.n_kv * t.nch * G * (kHD + 2));
+  cudaLaunchAttribute at[1];
+  cudaLaunchConfig_t c1 = tc_cfg(dim3(a.n_kv, a.rows), dim3(160), 0, pdl, st, at);
+  if ((e = cudaLaunchKernelEx(&c1, &attn_tc_prep_kernel, t)) != cudaSuccess) return e;
+  // two CTAs per SM; no more warps than tasks
+  const uint32_t want = (t.ntasks + kTcWarps - 1) / kTcWarps;
+  const uint32_t grid = want < 2u * g_tc_sms[dev] ? want : 2u * g_tc_sms[dev];
+  cudaLaunchConfig_t c2 = tc_cfg(dim3(grid), dim3(kTcWarps * 32), kTcSmem, 1, st, at);
+  if (G == 1) e = cudaLaunchKernelEx(&c2, &attn_tc_kernel<1>, t);
+  else if (G == 2) e = cudaLaunchKernelEx(&c2, &attn_tc_kernel<2>, t);
+  else e = cudaLaunchKernelEx(&c2, &attn_tc_kernel<4>, t);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t c3 = tc_cfg(dim3(a.n_kv, a.rows), dim3(kHD), 0, 1, st, at);
+  return cudaLaunchKernelEx(&c3, &attn_tc_combine_kernel, t);
+}
+
+}  // namespace nnz

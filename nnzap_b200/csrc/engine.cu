@@ -370,7 +370,7 @@ int attn(nnz_model* m, uint32_t layer, uint32_t rows, const int* pos, const int*
   a.max_ctx = m->c.max_context_length; a.pos = pos; a.slot = slot; a.rows = rows;
   a.n_q = m->c.num_query_heads; a.n_kv = m->c.num_kv_heads;
   a.eps = m->c.eps; a.theta = m->c.rope_theta; a.rope_style = m->c.rope_style;
-  a.write_kv = write; a.splits = attn_splits(m, rows);
+  a.write_kv = write; a.splits = attn_splits(m, rows); a.rope_tab = m->rope_tab;
   a.out = m->attn; a.out_stride = m->qd; a.ws = m->ws; a.counters = m->counters; a.err = m->err;
   NNZ_CK(attn_decode_launch(a, (int)m->c.head_dim, pdl, m->st));
   return NNZ_OK;
@@ -855,7 +855,7 @@ int nnz_model_finalize(nnz_model* m) {
       nctr = std::max(nctr, (size_t)ych * num_tiles(sh[0]));
     }
     wsf = std::max(wsf, attn_ws_floats(rows, c.num_query_heads, c.num_kv_heads, attn_splits(m, rows),
-                                       (int)c.head_dim));
+                                       (int)c.head_dim, c.max_context_length));
     nctr = std::max(nctr, (size_t)rows * c.num_kv_heads);
   }
   wsf = std::max(wsf, qmv_ws_floats(c.vocab_size, H, gs, fmt, 1, c.max_batch, m->num_sms));
@@ -880,6 +880,20 @@ int nnz_model_finalize(nnz_model* m) {
     NNZ_CK(cudaMemcpy(m->iota, io.data(), io.size() * 4, cudaMemcpyHostToDevice));
   }
   {
+    // rotary (cos, sin) per position and pair, in double like the
+    // kernels' own evaluation, rounded to f32
+    const uint32_t half = c.head_dim / 2;
+    std::vector<float2> tab((size_t)c.max_context_length * half);
+    const double l2t = std::log2((double)c.rope_theta);
+    for (uint32_t p = 0; p < c.max_context_length; ++p)
+      for (uint32_t i = 0; i < half; ++i) {
+        const double ang = (double)p * std::exp2(-(2.0 * i / c.head_dim) * l2t);
+        tab[(size_t)p * half + i] = make_float2((float)std::cos(ang), (float)std::sin(ang));
+      }
+    if ((rc = dalloc(m, (void**)&m->rope_tab, tab.size() * sizeof(float2)))) return rc;
+    NNZ_CK(cudaMemcpy(m->rope_tab, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  }
+  {
     // persistent decode kernel buffers (NNZ_DECODE_PATH=graph disables it)
     const char* path = getenv("NNZ_DECODE_PATH");
     m->mega_ok = !(path && strcmp(path, "graph") == 0) && !m->bf16r;
@@ -897,20 +911,7 @@ int nnz_model_finalize(nnz_model* m) {
       }
       if ((rc = dalloc(m, (void**)&m->mlayers, sizeof(MegaLayer) * c.num_layers))) return rc;
       NNZ_CK(cudaMemset(m->mbar, 0, 64));
-      {
-        // rotary (cos, sin) per position and pair, in double like the
-        // kernels' own evaluation, rounded to f32
-        const uint32_t half = c.head_dim / 2;
-        std::vector<float2> tab((size_t)c.max_context_length * half);
-        const double l2t = std::log2((double)c.rope_theta);
-        for (uint32_t p = 0; p < c.max_context_length; ++p)
-          for (uint32_t i = 0; i < half; ++i) {
-            const double ang = (double)p * std::exp2(-(2.0 * i / c.head_dim) * l2t);
-            tab[(size_t)p * half + i] = make_float2((float)std::cos(ang), (float)std::sin(ang));
-          }
-        if ((rc = dalloc(m, (void**)&m->rope_tab, tab.size() * sizeof(float2)))) return rc;
-        NNZ_CK(cudaMemcpy(m->rope_tab, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
-      }
+
       std::vector<MegaLayer> ml(c.num_layers);
       for (uint32_t l = 0; l < c.num_layers; ++l) {
         const LayerW& W = m->L[l];
@@ -1321,7 +1322,7 @@ int nnz_attn_decode(const void* qkv, const float* q_norm, const float* k_norm, v
   a.eps = eps > 0.f ? eps : 1e-6f; a.theta = theta; a.rope_style = rope_style; a.write_kv = 1;
   a.splits = splits ? splits : std::min(16u, std::max(1u, (uint32_t)w->num_sms / std::max(1u, n_kv * rows)));
   a.out = (__half*)out; a.out_stride = n_q * head_dim; a.ws = w->ws; a.counters = w->counters; a.err = w->err;
-  if (attn_ws_floats(rows, n_q, n_kv, a.splits, (int)head_dim) > w->ws_floats ||
+  if (attn_ws_floats(rows, n_q, n_kv, a.splits, (int)head_dim, max_ctx) > w->ws_floats ||
       (size_t)rows * n_kv > w->n_counters)
     return fail(NNZ_EINVAL, "nnz_attn_decode: problem too large for the shared workspace");
   NNZ_CK(attn_decode_launch(a, (int)head_dim, 0, (cudaStream_t)stream));

@@ -194,15 +194,27 @@ def _attn_oracle(qkv, qn, kn, kc, vc, pos, n_q, n_kv, hd, theta, style):
     (128, 16, 8, 300, 0, "half_split"), (64, 2, 2, 5, 0, "pairwise"), (64, 8, 2, 130, 3, "half_split"),
     (128, 32, 8, 4095, 0, "pairwise")])
 def test_attention_decode(cuda, built_lib, hd, n_q, n_kv, pos, splits, style):
+    _attention_case(cuda, hd, n_q, n_kv, [pos, max(0, pos // 2)], splits, style, pos + hd)
+
+
+@pytest.mark.parametrize("n_q,n_kv,positions", [
+    (8, 8, [0, 15, 16, 257, 4095]), (16, 8, [255, 256, 511, 4000, 17, 1, 2048]),
+    (32, 8, [3, 1000, 4094])])
+def test_attention_decode_batch(cuda, built_lib, n_q, n_kv, positions):
+    """Rows at chunk and block edges (16-position blocks, 256-position chunks)."""
+    _attention_case(cuda, 128, n_q, n_kv, positions, 0, "pairwise", len(positions))
+
+
+def _attention_case(cuda, hd, n_q, n_kv, pos_list, splits, style, seed):
     torch = cuda
-    rng = np.random.default_rng(pos + hd)
-    rows, max_ctx, theta = 2, 4096, 1e6
+    rng = np.random.default_rng(seed)
+    rows, max_ctx, theta = len(pos_list), 4096, 1e6
     qkv = rng.standard_normal((rows, (n_q + 2 * n_kv) * hd)).astype(np.float16)
     qn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
     kn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
     kc = rng.standard_normal((rows, n_kv, max_ctx, hd)).astype(np.float16)
     vc = rng.standard_normal((rows, n_kv, max_ctx, hd)).astype(np.float16)
-    positions = np.array([pos, max(0, pos // 2)], dtype=np.int32)
+    positions = np.array(pos_list, dtype=np.int32)
     kd, vd = to_dev(torch, kc), to_dev(torch, vc)
     out = torch.empty((rows, n_q * hd), dtype=torch.float16, device="cuda")
     keep = [to_dev(torch, a) for a in (qkv, qn, kn, positions)]   # alive until the sync
