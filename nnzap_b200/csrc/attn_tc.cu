@@ -313,41 +313,45 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(const __grid_con
 // ---------------------------------------------------------------------------
 // 3. merge the chunks
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kHD) attn_tc_combine_kernel(TcArgs t) {
+// Thread (head h, dim d) of a (kv head, row); up to 16 chunks' loads are
+// in flight before any is used.
+__global__ void __launch_bounds__(4 * kHD) attn_tc_combine_kernel(TcArgs t) {
+  constexpr int kB = 16;
   const AttnArgs& a = t.a;
   pdl_wait();
   pdl_launch();
-  const int kvh = blockIdx.x, row = blockIdx.y, d = threadIdx.x;
+  const int kvh = blockIdx.x, row = blockIdx.y, d = threadIdx.x % kHD, h = threadIdx.x / kHD;
   const uint32_t G = a.n_q / a.n_kv;
   const int seq = clamp_pos(a, row, false) + 1;
   const uint32_t nc = (uint32_t)(seq + kTcChunk - 1) / kTcChunk;
-  __half* orow = a.out + (size_t)row * a.out_stride + (size_t)kvh * G * kHD;
-  for (uint32_t h = 0; h < G; ++h) {
-    const float* base = t.part + (((size_t)row * a.n_kv + kvh) * t.nch * G + h) * (kHD + 2);
-    const size_t cs = (size_t)G * (kHD + 2);
-    float M = -INFINITY, L = 0.f, o = 0.f;
-    for (uint32_t c0 = 0; c0 < nc; c0 += 8) {
-      float mv[8], lv[8], ov[8];
+  const float* base = t.part + (((size_t)row * a.n_kv + kvh) * t.nch * G + h) * (kHD + 2);
+  const size_t cs = (size_t)G * (kHD + 2);
+  float M = -INFINITY, L = 0.f, o = 0.f;
+  for (uint32_t c0 = 0; c0 < nc; c0 += kB) {
+    float mv[kB], lv[kB], ov[kB];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const bool ok = c0 + j < nc;
-        const float* r = base + (c0 + j) * cs;
-        mv[j] = ok ? __ldcg(r) : -INFINITY;
-        lv[j] = ok ? __ldcg(r + 1) : 0.f;
-        ov[j] = ok ? __ldcg(r + 2 + d) : 0.f;
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (mv[j] == -INFINITY) continue;
-        const float nm = fmaxf(M, mv[j]);
-        const float a0 = M == -INFINITY ? 0.f : expf(M - nm), a1 = expf(mv[j] - nm);
-        L = L * a0 + lv[j] * a1;
-        o = o * a0 + ov[j] * a1;
-        M = nm;
-      }
+    for (int j = 0; j < kB; ++j) {
+      const bool ok = c0 + j < nc;
+      const float* r = base + (c0 + j) * cs;
+      mv[j] = ok ? __ldcg(r) : -INFINITY;
+      lv[j] = ok ? __ldcg(r + 1) : 0.f;
+      ov[j] = ok ? __ldcg(r + 2 + d) : 0.f;
     }
-    orow[h * kHD + d] = __float2half_rn(o / L);
+    float nm = M;
+#pragma unroll
+    for (int j = 0; j < kB; ++j) nm = fmaxf(nm, mv[j]);
+    const float a0 = M == -INFINITY ? 0.f : expf(M - nm);
+    L *= a0;
+    o *= a0;
+#pragma unroll
+    for (int j = 0; j < kB; ++j) {
+      const float w = mv[j] == -INFINITY ? 0.f : expf(mv[j] - nm);
+      L = fmaf(lv[j], w, L);
+      o = fmaf(ov[j], w, o);
+    }
+    M = nm;
   }
+  a.out[(size_t)row * a.out_stride + ((size_t)kvh * G + h) * kHD + d] = __float2half_rn(o / L);
 }
 
 cudaLaunchConfig_t tc_cfg(dim3 grid, dim3 block, uint32_t smem, int pdl, cudaStream_t st, cudaLaunchAttribute* at) {
@@ -416,7 +420,7 @@ cudaError_t attn_tc_launch(const AttnArgs& a, int pdl, cudaStream_t st) {
   else if (G == 2) e = cudaLaunchKernelEx(&c2, &attn_tc_kernel<2>, t);
   else e = cudaLaunchKernelEx(&c2, &attn_tc_kernel<4>, t);
   if (e != cudaSuccess) return e;
-  cudaLaunchConfig_t c3 = tc_cfg(dim3(a.n_kv, a.rows), dim3(kHD), 0, 1, st, at);
+  cudaLaunchConfig_t c3 = tc_cfg(dim3(a.n_kv, a.rows), dim3(kHD * G), 0, 1, st, at);
   return cudaLaunchKernelEx(&c3, &attn_tc_combine_kernel, t);
 }
 

@@ -46,6 +46,7 @@ int fail(int code, const std::string& msg) {
 
 constexpr uint32_t kPrefillChunk = 64;        // chunked-matvec prefill
 constexpr uint32_t kGemmPrefillChunk = 512;    // tcgen05 GEMM prefill
+constexpr uint32_t kGemmDecodeRows = 16;       // decode batches from here on use the GEMM
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -198,6 +199,7 @@ struct nnz_model {
   float* residual = nullptr;
   __half* xn = nullptr;          // fp16 RMSNorm output [rows_max][max(H, ...)] (GEMM prefill)
   bool gemm_prefill = false;
+  FlatW flm;                           // LM head in the reference layout (GEMM decode of large batches)
   uint8_t* flat = nullptr;       // flat weight copies for the GEMM prefill
   __half *qkv = nullptr, *attn = nullptr, *h = nullptr;
   float* logits = nullptr;
@@ -391,11 +393,25 @@ int kv_write(nnz_model* m, uint32_t layer, uint32_t rows, const int* pos, const 
 
 // One decoder layer for `rows` rows.  decode: pos/slot per row, fused KV
 // write; prefill chunk: rows share slot 0, K/V written first.
+int gemm(nnz_model* m, const FlatW& W, const FlatW* W2, uint32_t N, uint32_t K, const __half* x,
+         uint32_t rows, int epi, void* out, uint32_t ldo);
+
 int enqueue_layer(nnz_model* m, uint32_t l, uint32_t rows, const int* pos, const int* slot,
                   bool prefill, int pdl) {
   const nnz_config& c = m->c;
   const LayerW& W = m->L[l];
   int rc;
+  if (!prefill && m->gemm_prefill && rows >= kGemmDecodeRows) {
+    // large decode batches: the projections as tcgen05 GEMMs over the rows
+    const uint32_t H = c.hidden_size, I = c.intermediate_size;
+    NNZ_CK(rmsnorm_f16_launch(m->residual, W.attn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st));
+    if ((rc = gemm(m, W.fqkv, nullptr, m->qkv_rows, H, m->xn, rows, GEPI_F16, m->qkv, m->qkv_rows))) return rc;
+    if ((rc = attn(m, l, rows, pos, slot, 1, 0))) return rc;
+    if ((rc = gemm(m, W.fo, nullptr, H, m->qd, m->attn, rows, GEPI_RESADD, m->residual, H))) return rc;
+    NNZ_CK(rmsnorm_f16_launch(m->residual, W.ffn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st));
+    if ((rc = gemm(m, W.fgate, &W.fup, I, H, m->xn, rows, GEPI_SILU, m->h, I))) return rc;
+    return gemm(m, W.fdown, nullptr, H, I, m->h, rows, GEPI_RESADD, m->residual, H);
+  }
   if ((rc = qmv(m, 1, PRO_NORM, EPI_F16, W.qkv, m->qkv_rows, c.hidden_size, m->residual,
                 c.hidden_size, W.attn_norm, rows, m->qkv, m->qkv_rows, nullptr, nullptr, pdl)))
     return rc;
@@ -434,6 +450,16 @@ int enqueue_decode(nnz_model* m, uint32_t rows, bool want_logits, int pdl) {
   if ((rc = enqueue_embed(m, rows, nullptr, pdl))) return rc;
   for (uint32_t l = 0; l < m->c.num_layers; ++l)
     if ((rc = enqueue_layer(m, l, rows, m->state->pos, nullptr, false, pdl))) return rc;
+  if (m->gemm_prefill && rows >= kGemmDecodeRows) {
+    // final norm -> LM-head GEMM into the logits buffer -> argmax per row
+    const nnz_config& c = m->c;
+    NNZ_CK(rmsnorm_f16_launch(m->residual, m->fnorm, c.eps, rows, c.hidden_size, m->bf16r, m->xn, m->st));
+    if ((rc = gemm(m, m->flm, nullptr, c.vocab_size, c.hidden_size, m->xn, rows, GEPI_F32, m->logits,
+                   c.vocab_size)))
+      return rc;
+    NNZ_CK(logits_argmax_launch(m->logits, rows, c.vocab_size, c.vocab_size, m->state->argmax, m->st));
+    return NNZ_OK;
+  }
   return qmv(m, 1, PRO_NORM, EPI_LOGITS, m->lm, m->c.vocab_size, m->c.hidden_size, m->residual,
              m->c.hidden_size, m->fnorm, rows, nullptr, 0, want_logits ? m->logits : nullptr,
              m->state->argmax, pdl);
@@ -814,6 +840,11 @@ int nnz_model_finalize(nnz_model* m) {
   if (fmt == NNZ_Q4) NNZ_CK(cudaMemcpy(m->arena + o_embb, b.data(), emb_g * 2, cudaMemcpyHostToDevice));
   if (!c.tie_word_embeddings) {
     if ((rc = get_proj(m, "lm_head", c.vocab_size, H, w, s, b))) return rc;
+    if (m->gemm_prefill && (rc = upload_flat(m, w, s, b, &m->flm))) return rc;
+  } else if (m->gemm_prefill) {
+    m->flm.w = m->arena + o_embw;
+    m->flm.s = reinterpret_cast<const uint16_t*>(m->arena + o_embs);
+    m->flm.b = fmt == NNZ_Q4 ? reinterpret_cast<const uint16_t*>(m->arena + o_embb) : nullptr;
   }
   buf.assign(b_lm, 0);
   pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), c.vocab_size, H, gs, 1, 0,

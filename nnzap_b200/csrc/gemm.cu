@@ -272,7 +272,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             float x = __uint_as_float(v[j]);
             if (rb) x = bf16_trunc(x);
             if (nb + j < a.N) {
-              if (gridDim.z > 1) atomicAdd(&o[j], x);
+              if (a.epi == GEPI_F32) o[j] = x;
+              else if (gridDim.z > 1) atomicAdd(&o[j], x);
               else o[j] += x;
             }
           }
@@ -286,13 +287,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
 }
 
-__global__ void rmsnorm_f16_kernel(const float* res, const float* w, float eps, uint32_t K, int bf16r,
-                                   __half* out) {
+// One CTA per row; K % 4 == 0.  Every thread's float4 loads of a pass are
+// issued before any is used (one round trip per 4 * 1024 columns).
+__global__ void __launch_bounds__(256) rmsnorm_f16_kernel(const float* res, const float* w, float eps, uint32_t K,
+                                                          int bf16r, __half* out) {
+  constexpr int kU = 4;
   __shared__ float red[32];
-  const uint32_t row = blockIdx.x;
-  const float* x = res + (size_t)row * K;
+  const uint32_t row = blockIdx.x, K4 = K / 4;
+  const float4* x = reinterpret_cast<const float4*>(res + (size_t)row * K);
   float ss = 0.f;
-  for (uint32_t k = threadIdx.x; k < K; k += blockDim.x) ss = fmaf(x[k], x[k], ss);
+  for (uint32_t k0 = threadIdx.x; k0 < K4; k0 += kU * blockDim.x) {
+    float4 v[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const uint32_t k = k0 + u * blockDim.x;
+      v[u] = k < K4 ? x[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+  }
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
@@ -303,10 +316,25 @@ __global__ void rmsnorm_f16_kernel(const float* res, const float* w, float eps, 
   }
   __syncthreads();
   const float r = red[0];
-  for (uint32_t k = threadIdx.x; k < K; k += blockDim.x) {
-    float v = x[k] * r * w[k];
-    if (bf16r) v = bf16_trunc(v);
-    out[(size_t)row * K + k] = __float2half_rn(v);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  for (uint32_t k0 = threadIdx.x; k0 < K4; k0 += kU * blockDim.x) {
+    float4 v[kU], g[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const uint32_t k = k0 + u * blockDim.x;
+      if (k < K4) { v[u] = x[k]; g[u] = w4[k]; }
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const uint32_t k = k0 + u * blockDim.x;
+      if (k >= K4) continue;
+      float o[4] = {v[u].x * r * g[u].x, v[u].y * r * g[u].y, v[u].z * r * g[u].z, v[u].w * r * g[u].w};
+      if (bf16r)
+        for (int i = 0; i < 4; ++i) o[i] = bf16_trunc(o[i]);
+      __half2* dst = reinterpret_cast<__half2*>(out + (size_t)row * K + 4 * k);
+      dst[0] = __floats2half2_rn(o[0], o[1]);
+      dst[1] = __floats2half2_rn(o[2], o[3]);
+    }
   }
 }
 
@@ -383,6 +411,7 @@ cudaError_t gemm_launch(const GemmArgs& a, const __half* x, cudaStream_t st) {
 
 cudaError_t rmsnorm_f16_launch(const float* res, const float* w, float eps, uint32_t rows, uint32_t K, int bf16r,
                                __half* out, cudaStream_t st) {
+  if (K % 4) return cudaErrorInvalidValue;
   rmsnorm_f16_kernel<<<rows, 256, 0, st>>>(res, w, eps, K, bf16r, out);
   return cudaGetLastError();
 }

@@ -22,7 +22,7 @@
 
 namespace nnz {
 
-enum GemmEpi : int { GEPI_F16 = 0, GEPI_RESADD = 1, GEPI_SILU = 2 };
+enum GemmEpi : int { GEPI_F16 = 0, GEPI_RESADD = 1, GEPI_SILU = 2, GEPI_F32 = 3 };
 
 struct GemmArgs {
   uint32_t M, K, N;              // tokens, reduction dim, weight rows (per matrix)
@@ -34,7 +34,7 @@ struct GemmArgs {
   const uint16_t* s2;
   const uint16_t* b2;
   int epi;
-  void* out;                     // f16 [M][ldo] or f32 residual [M][ldo]
+  void* out;                     // f16 [M][ldo], f32 residual [M][ldo] (+=), or f32 [M][ldo] (GEPI_F32)
   uint32_t ldo;
   int* err;
 };

@@ -130,4 +130,43 @@ cudaError_t dequant_launch(int fmt, int bf16s, const uint8_t* w, uint32_t M, uin
   return cudaGetLastError();
 }
 
+namespace {
+constexpr uint32_t kArgThreads = 256, kArgItems = 8;
+__global__ void __launch_bounds__(kArgThreads) logits_argmax_kernel(const float* logits, uint32_t n, uint32_t stride,
+                                                                    unsigned long long* argmax) {
+  const uint32_t r = blockIdx.y;
+  const float* x = logits + (size_t)r * stride;
+  const uint32_t i0 = blockIdx.x * kArgThreads * kArgItems + threadIdx.x;
+  float v[kArgItems];
+#pragma unroll
+  for (int u = 0; u < (int)kArgItems; ++u) {
+    const uint32_t i = i0 + u * kArgThreads;
+    v[u] = i < n ? __ldcg(x + i) : 0.f;
+  }
+  unsigned long long best = 0ull;
+#pragma unroll
+  for (int u = 0; u < (int)kArgItems; ++u) {
+    const uint32_t i = i0 + u * kArgThreads;
+    if (i < n) {
+      const unsigned long long pk = argmax_pack(v[u], i);
+      best = pk > best ? pk : best;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long q = __shfl_xor_sync(0xffffffffu, best, o);
+    best = q > best ? q : best;
+  }
+  if ((threadIdx.x & 31) == 0 && best) atomicMax(&argmax[r], best);
+}
+}  // namespace
+
+cudaError_t logits_argmax_launch(const float* logits, uint32_t rows, uint32_t n, uint32_t stride,
+                                 unsigned long long* argmax, cudaStream_t st) {
+  if (rows == 0 || n == 0) return cudaErrorInvalidValue;
+  const dim3 grid((n + kArgThreads * kArgItems - 1) / (kArgThreads * kArgItems), rows);
+  logits_argmax_kernel<<<grid, kArgThreads, 0, st>>>(logits, n, stride, argmax);
+  return cudaGetLastError();
+}
+
 }  // namespace nnz

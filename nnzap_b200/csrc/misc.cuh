@@ -34,6 +34,10 @@ struct EmbedArgs {
 };
 
 cudaError_t embed_launch(const EmbedArgs& a, int fmt, int bf16s, int pdl, cudaStream_t st);
+// argmax[r] = max(argmax[r], packed first-max of logits[r][0..n)) for r < rows
+// (the packed slot the decode state consumes; see argmax_pack).
+cudaError_t logits_argmax_launch(const float* logits, uint32_t rows, uint32_t n, uint32_t stride,
+                                 unsigned long long* argmax, cudaStream_t st);
 cudaError_t dequant_launch(int fmt, int bf16s, const uint8_t* w, uint32_t M, uint32_t K, uint32_t gs,
                            uint32_t sub, uint32_t si, float* out, cudaStream_t st);
 
