@@ -67,8 +67,14 @@ typedef struct nnz_config {
   int32_t rope_style;             /* NNZ_ROPE_* */
   int32_t tie_word_embeddings;
   int32_t q1_scales_are_mlx;      /* Q1: halve scales at load (model.zig:944-959) */
-  int32_t tp_rank;                /* tensor-parallel rank / size (1 = off) */
-  int32_t tp_size;
+  /* Tensor parallelism (batched decode, one process per GPU): with
+   * tp_size > 1 this model holds rank tp_rank's shard -- query/kv heads,
+   * gate/up rows and the LM head's vocabulary rows split tp_size ways,
+   * o/down split along their input columns -- and the full-size tensors
+   * passed to nnz_model_load_tensor are sliced at finalize.  The dims
+   * above stay the full model's.  Call nnz_tp_init before finalize. */
+  int32_t tp_rank;
+  int32_t tp_size;                /* 0 or 1 = off */
 } nnz_config;
 
 typedef struct nnz_model nnz_model;
@@ -112,10 +118,14 @@ int nnz_model_finalize(nnz_model* m);
 int nnz_model_free(nnz_model* m);
 /* Bytes of device memory held by the model (weights + KV + scratch). */
 size_t nnz_model_device_bytes(const nnz_model* m);
+/* Vocabulary rows of this rank's LM-head shard (vocab_size without TP). */
+uint32_t nnz_model_vocab_shard(const nnz_model* m);
 
 /* forwardDecode (transformer.zig:2566) + host argmax (:3694): one token per
  * row at the given positions, `batch` rows (row r uses KV-cache slot r).
- * logits (optional, host, [batch][vocab] f32) and argmax_out ([batch]). */
+ * logits (optional, host, [batch][vocab] f32; with tensor parallelism
+ * [batch][nnz_model_vocab_shard] of this rank's rows) and argmax_out
+ * ([batch], global token ids on every rank). */
 int nnz_forward_decode(nnz_model* m, const uint32_t* tokens, const uint32_t* positions,
                        uint32_t batch, float* logits, uint32_t* argmax_out);
 /* Prompt prefill into slot 0 at positions 0..n-1 (replaces chunkedPrefill,
@@ -160,6 +170,24 @@ int nnz_pack_weights(int fmt, const void* weight, const uint16_t* scales, const 
 int nnz_unpack_weights(int fmt, const void* packed, uint32_t M, uint32_t K, uint32_t gs,
                        uint32_t sub, uint32_t sub_index, void* weight, uint16_t* scales,
                        uint16_t* biases);
+
+/* Tensor-parallel shard of a flat [M][K] weight (reference layout): rows
+ * [lo, hi) (axis 0) or columns [lo, hi) (axis 1; multiples of gs).  Host
+ * memory only; outputs are flat in the shard's shape.  Q1: biases NULL. */
+int nnz_shard_weights(int fmt, int axis, const void* weight, const uint16_t* scales,
+                      const uint16_t* biases, uint32_t M, uint32_t K, uint32_t gs, uint32_t lo,
+                      uint32_t hi, void* weight_out, uint16_t* scales_out, uint16_t* biases_out);
+
+/* ---- tensor parallelism (NCCL over NVLink; replaces nothing in the
+ * reference, which is single-device) ------------------------------------ */
+/* Rank 0 creates the group id (NCCL unique id, copied into out[0..cap));
+ * returns its size in bytes (> 0) or a negative error. */
+int nnz_tp_unique_id(void* out, size_t cap);
+/* Joins the group (blocking until all tp_size ranks joined); the model
+ * must have been created with tp_size > 1 and not be finalized.  Decode
+ * then all-reduces the residual after o_proj and down_proj (sum) and the
+ * argmax slots after the LM head (max), inside the same CUDA graph. */
+int nnz_tp_init(nnz_model* m, const void* unique_id, size_t len);
 
 /* ---- per-kernel entry points on device pointers --------------------- */
 /* All asynchronous on `stream` (a cudaStream_t, NULL = default stream).

@@ -6,7 +6,9 @@ nnmetal engine interface (``engine``), the library binding (``_capi``), the
 in-tree build (``build``) and seeded synthetic weights (``synth``).
 """
 from .engine import (Bonsai1_7B, Bonsai1_7B_Q4, GenerateOpts, GenerateResult, Model,
-                     SamplingParams, TinyBlock, TransformerConfig, config_from_dims, generate)
+                     SamplingParams, TinyBlock, TransformerConfig, config_from_dims, generate,
+                     shard_weights, tp_unique_id)
 
 __all__ = ["Bonsai1_7B", "Bonsai1_7B_Q4", "GenerateOpts", "GenerateResult", "Model",
-           "SamplingParams", "TinyBlock", "TransformerConfig", "config_from_dims", "generate"]
+           "SamplingParams", "TinyBlock", "TransformerConfig", "config_from_dims", "generate",
+           "shard_weights", "tp_unique_id"]

@@ -61,6 +61,10 @@ SIGNATURES = [
     ("nnz_model_finalize", I32, [P]),
     ("nnz_model_free", I32, [P]),
     ("nnz_model_device_bytes", SZ, [P]),
+    ("nnz_model_vocab_shard", U32, [P]),
+    ("nnz_shard_weights", I32, [I32, I32, P, P, P, U32, U32, U32, U32, U32, P, P, P]),
+    ("nnz_tp_unique_id", I32, [P, SZ]),
+    ("nnz_tp_init", I32, [P, P, SZ]),
     ("nnz_forward_decode", I32, [P, P, P, U32, P, P]),
     ("nnz_prefill", I32, [P, P, U32, P, P]),
     ("nnz_generate", I32, [P, C.POINTER(NnzGenerateOpts), C.POINTER(NnzGenerateResult)]),

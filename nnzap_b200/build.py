@@ -26,6 +26,18 @@ NVCC_FLAGS = ["-O3", "-std=c++20", "-lineinfo", "-Xcompiler", "-fPIC,-O3",
               "--expt-relaxed-constexpr", "-I", str(ROOT / "include"), "-I", str(CSRC)]
 
 
+def _nccl_include() -> list[str]:
+    """nccl.h for the run-time-loaded NCCL (types only; the library is dlopen()ed)."""
+    try:
+        import nvidia.nccl as nn  # the NCCL wheel torch ships with
+        inc = Path(list(nn.__path__)[0]) / "include"
+        if (inc / "nccl.h").exists():
+            return ["-I", str(inc)]
+    except ImportError:
+        pass
+    return []
+
+
 def _nvcc() -> str:
     for cand in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", shutil.which("nvcc")):
         if cand and Path(cand).exists():
@@ -57,7 +69,7 @@ def build(verbose: bool = False, force: bool = False) -> Path:
                 cmd = ["g++", "-O3", "-std=c++20", "-fPIC", "-pthread", "-I", str(CSRC),
                        "-I", str(ROOT / "include"), "-c", str(src), "-o", str(obj)]
             else:
-                cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
+                cmd = [nvcc, *ARCH, *NVCC_FLAGS, *_nccl_include(), "-c", str(src), "-o", str(obj)]
             jobs.append(cmd)
     with cf.ThreadPoolExecutor(max_workers=max(1, os.cpu_count() or 1)) as ex:
         for cmd, res in zip(jobs, ex.map(lambda c: subprocess.run(c, capture_output=True, text=True), jobs)):
@@ -67,7 +79,7 @@ def build(verbose: bool = False, force: bool = False) -> Path:
                 raise RuntimeError(f"compile failed: {cmd[-3]}")
     if force or jobs or not LIB.exists():
         link = [nvcc, *ARCH, "-shared", "-Xcompiler", "-fPIC", "-cudart", "static",
-                "-o", str(LIB), *map(str, objs), "-lpthread"]
+                "-o", str(LIB), *map(str, objs), "-lpthread", "-ldl"]
         res = subprocess.run(link, capture_output=True, text=True)
         if res.returncode:
             sys.stderr.write(res.stdout + res.stderr)

@@ -26,6 +26,7 @@
 #include "misc.cuh"
 #include "packing.h"
 #include "qmv.cuh"
+#include "tp.cuh"
 
 using namespace nnz;
 
@@ -179,7 +180,11 @@ void set_last_error(const std::string& msg) { g_err = msg; }
 }  // namespace nnz
 
 struct nnz_model {
-  nnz_config c{};
+  nnz_config c{};          // this rank's dims (heads / intermediate divided by tp)
+  nnz_config full{};       // the model's dims as given
+  int tp = 1, tp_rank = 0;
+  ncclComm_t comm = nullptr;
+  uint32_t lm_rows = 0, lm_off = 0;   // this rank's LM-head vocabulary rows
   int device = 0;
   int num_sms = 148;
   cudaStream_t st = nullptr;
@@ -303,6 +308,35 @@ int get_proj(nnz_model* m, const std::string& base, uint32_t M, uint32_t K,
   return NNZ_OK;
 }
 
+// Replace a flat [M][K] matrix by its rows / columns [lo, hi) (axis 0 / 1).
+int shard_vec(nnz_model* m, int axis, uint32_t M, uint32_t K, uint32_t lo, uint32_t hi,
+              std::vector<uint8_t>& w, std::vector<uint16_t>& s, std::vector<uint16_t>& b) {
+  const uint32_t gs = (uint32_t)m->c.group_size;
+  const uint32_t Mo = axis == 0 ? hi - lo : M, Ko = axis == 0 ? K : hi - lo;
+  std::vector<uint8_t> wo(m->fmt == NNZ_Q1 ? (size_t)Mo * Ko / 8 : (size_t)Mo * Ko / 2);
+  std::vector<uint16_t> so((size_t)Mo * Ko / gs), bo(b.empty() ? 0 : so.size());
+  if (shard_host(m->fmt, axis, w.data(), s.data(), b.empty() ? nullptr : b.data(), M, K, gs, lo, hi, wo.data(),
+                 so.data(), bo.empty() ? nullptr : bo.data()))
+    return fail(NNZ_EINVAL, "tensor-parallel shard: bad range");
+  w.swap(wo);
+  s.swap(so);
+  b.swap(bo);
+  return NNZ_OK;
+}
+
+// get_proj of this rank's shard: (Mloc x Kloc) taken at rank * Mloc rows
+// (axis 0) or rank * Kloc columns (axis 1) of the full tensor.
+int get_proj_tp(nnz_model* m, const std::string& base, uint32_t Mloc, uint32_t Kloc, int axis,
+                std::vector<uint8_t>& w, std::vector<uint16_t>& s, std::vector<uint16_t>& b) {
+  if (m->tp == 1) return get_proj(m, base, Mloc, Kloc, w, s, b);
+  const uint32_t T = (uint32_t)m->tp, r = (uint32_t)m->tp_rank;
+  const uint32_t M = axis == 0 ? Mloc * T : Mloc, K = axis == 1 ? Kloc * T : Kloc;
+  int rc = get_proj(m, base, M, K, w, s, b);
+  if (rc) return rc;
+  const uint32_t n = axis == 0 ? Mloc : Kloc;
+  return shard_vec(m, axis, M, K, r * n, (r + 1) * n, w, s, b);
+}
+
 int get_norm(nnz_model* m, const std::string& name, uint32_t n, std::vector<float>& out) {
   const HostTensor* t = find_t(m, name);
   if (!t) return fail(NNZ_ENOTFOUND, "tensor not found: " + name);
@@ -396,6 +430,40 @@ int kv_write(nnz_model* m, uint32_t layer, uint32_t rows, const int* pos, const 
 int gemm(nnz_model* m, const FlatW& W, const FlatW* W2, uint32_t N, uint32_t K, const __half* x,
          uint32_t rows, int epi, void* out, uint32_t ldo);
 
+// Tensor parallelism around a row-split projection (o, down): every rank
+// holds the same residual R; rank 0 accumulates R + P_0, the others start
+// from zero and accumulate P_r, and a sum all-reduce leaves R + sum P_r.
+int tp_pre_add(nnz_model* m, uint32_t rows) {
+  if (m->tp > 1 && m->tp_rank != 0)
+    NNZ_CK(cudaMemsetAsync(m->residual, 0, (size_t)rows * m->c.hidden_size * 4, m->st));
+  return NNZ_OK;
+}
+
+int nccl_fail(ncclResult_t r) {
+  std::string e;
+  const NcclApi* api = nccl_api(&e);
+  return fail(NNZ_ENCCL, std::string("NCCL: ") + (api ? api->error_string(r) : e.c_str()));
+}
+
+int tp_post_add(nnz_model* m, uint32_t rows) {
+  if (m->tp == 1) return NNZ_OK;
+  const NcclApi* api = nccl_api(nullptr);
+  const ncclResult_t r = api->all_reduce(m->residual, m->residual, (size_t)rows * m->c.hidden_size, ncclFloat32,
+                                         ncclSum, m->comm, m->st);
+  return r == ncclSuccess ? NNZ_OK : nccl_fail(r);
+}
+
+// After a vocabulary-sharded LM head: local indices -> global, then the
+// packed (value, index) slots reduced with max (first maximum wins).
+int tp_argmax(nnz_model* m, uint32_t rows) {
+  if (m->tp == 1) return NNZ_OK;
+  NNZ_CK(argmax_shift_launch(m->state->argmax, rows, m->lm_off, m->st));
+  const NcclApi* api = nccl_api(nullptr);
+  const ncclResult_t r = api->all_reduce(m->state->argmax, m->state->argmax, rows, ncclUint64, ncclMax, m->comm, m->st);
+  return r == ncclSuccess ? NNZ_OK : nccl_fail(r);
+}
+
+
 int enqueue_layer(nnz_model* m, uint32_t l, uint32_t rows, const int* pos, const int* slot,
                   bool prefill, int pdl) {
   const nnz_config& c = m->c;
@@ -407,10 +475,14 @@ int enqueue_layer(nnz_model* m, uint32_t l, uint32_t rows, const int* pos, const
     NNZ_CK(rmsnorm_f16_launch(m->residual, W.attn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st));
     if ((rc = gemm(m, W.fqkv, nullptr, m->qkv_rows, H, m->xn, rows, GEPI_F16, m->qkv, m->qkv_rows))) return rc;
     if ((rc = attn(m, l, rows, pos, slot, 1, 0))) return rc;
+    if ((rc = tp_pre_add(m, rows))) return rc;
     if ((rc = gemm(m, W.fo, nullptr, H, m->qd, m->attn, rows, GEPI_RESADD, m->residual, H))) return rc;
+    if ((rc = tp_post_add(m, rows))) return rc;
     NNZ_CK(rmsnorm_f16_launch(m->residual, W.ffn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st));
     if ((rc = gemm(m, W.fgate, &W.fup, I, H, m->xn, rows, GEPI_SILU, m->h, I))) return rc;
-    return gemm(m, W.fdown, nullptr, H, I, m->h, rows, GEPI_RESADD, m->residual, H);
+    if ((rc = tp_pre_add(m, rows))) return rc;
+    if ((rc = gemm(m, W.fdown, nullptr, H, I, m->h, rows, GEPI_RESADD, m->residual, H))) return rc;
+    return tp_post_add(m, rows);
   }
   if ((rc = qmv(m, 1, PRO_NORM, EPI_F16, W.qkv, m->qkv_rows, c.hidden_size, m->residual,
                 c.hidden_size, W.attn_norm, rows, m->qkv, m->qkv_rows, nullptr, nullptr, pdl)))
@@ -421,17 +493,20 @@ int enqueue_layer(nnz_model* m, uint32_t l, uint32_t rows, const int* pos, const
   } else {
     if ((rc = attn(m, l, rows, pos, slot, 1, pdl))) return rc;
   }
+  if ((rc = tp_pre_add(m, rows))) return rc;
   if ((rc = qmv(m, 1, PRO_F16, EPI_RESADD, W.o, c.hidden_size, m->qd, m->attn, m->qd, nullptr,
                 rows, m->residual, c.hidden_size, nullptr, nullptr, pdl)))
     return rc;
+  if ((rc = tp_post_add(m, rows))) return rc;
   if ((rc = qmv(m, 2, PRO_NORM, EPI_SILU, W.gu, c.intermediate_size, c.hidden_size, m->residual,
                 c.hidden_size, W.ffn_norm, rows, m->h, c.intermediate_size, nullptr, nullptr, pdl)))
     return rc;
+  if ((rc = tp_pre_add(m, rows))) return rc;
   if ((rc = qmv(m, 1, PRO_F16, EPI_RESADD, W.down, c.hidden_size, c.intermediate_size, m->h,
                 c.intermediate_size, nullptr, rows, m->residual, c.hidden_size, nullptr, nullptr,
                 pdl)))
     return rc;
-  return NNZ_OK;
+  return tp_post_add(m, rows);
 }
 
 int enqueue_embed(nnz_model* m, uint32_t rows, const uint32_t* tokens, int pdl) {
@@ -454,15 +529,17 @@ int enqueue_decode(nnz_model* m, uint32_t rows, bool want_logits, int pdl) {
     // final norm -> LM-head GEMM into the logits buffer -> argmax per row
     const nnz_config& c = m->c;
     NNZ_CK(rmsnorm_f16_launch(m->residual, m->fnorm, c.eps, rows, c.hidden_size, m->bf16r, m->xn, m->st));
-    if ((rc = gemm(m, m->flm, nullptr, c.vocab_size, c.hidden_size, m->xn, rows, GEPI_F32, m->logits,
-                   c.vocab_size)))
+    if ((rc = gemm(m, m->flm, nullptr, m->lm_rows, c.hidden_size, m->xn, rows, GEPI_F32, m->logits,
+                   m->lm_rows)))
       return rc;
-    NNZ_CK(logits_argmax_launch(m->logits, rows, c.vocab_size, c.vocab_size, m->state->argmax, m->st));
-    return NNZ_OK;
+    NNZ_CK(logits_argmax_launch(m->logits, rows, m->lm_rows, m->lm_rows, m->state->argmax, m->st));
+    return tp_argmax(m, rows);
   }
-  return qmv(m, 1, PRO_NORM, EPI_LOGITS, m->lm, m->c.vocab_size, m->c.hidden_size, m->residual,
-             m->c.hidden_size, m->fnorm, rows, nullptr, 0, want_logits ? m->logits : nullptr,
-             m->state->argmax, pdl);
+  if ((rc = qmv(m, 1, PRO_NORM, EPI_LOGITS, m->lm, m->lm_rows, m->c.hidden_size, m->residual,
+                m->c.hidden_size, m->fnorm, rows, nullptr, 0, want_logits ? m->logits : nullptr,
+                m->state->argmax, pdl)))
+    return rc;
+  return tp_argmax(m, rows);
 }
 
 int get_graph(nnz_model* m, uint32_t rows, bool want_logits, cudaGraphExec_t* out) {
@@ -514,7 +591,7 @@ const nnz_model::MegaPlan* mega_plan_for(nnz_model* m, uint32_t rows) {
   MegaArgs& a = P.a;
   const nnz_config& c = m->c;
   a.H = c.hidden_size; a.I = c.intermediate_size; a.n_q = c.num_query_heads; a.n_kv = c.num_kv_heads;
-  a.hd = c.head_dim; a.L = c.num_layers; a.vocab = c.vocab_size; a.gs = (uint32_t)c.group_size;
+  a.hd = c.head_dim; a.L = c.num_layers; a.vocab = m->lm_rows; a.gs = (uint32_t)c.group_size;
   a.max_ctx = c.max_context_length; a.batch = rows; a.eps = c.eps; a.theta = c.rope_theta;
   a.rope_style = c.rope_style; a.bf16r = m->bf16r; a.layers = m->mlayers; a.rope_tab = m->rope_tab; a.lm = m->lm; a.fnorm = m->fnorm;
   a.emb_w = m->emb_w; a.emb_s = m->emb_s; a.emb_b = m->emb_b; a.kc = m->kc; a.vc = m->vc;
@@ -606,11 +683,14 @@ int enqueue_layer_gemm(nnz_model* m, uint32_t l, uint32_t rows, const int* pos) 
     aa.out_stride = m->qd; aa.err = m->err;
     NNZ_CK(attn_prefill_launch(aa, (int)c.head_dim, 0, m->st));
   }
+  if ((rc = tp_pre_add(m, rows))) return rc;
   if ((rc = gemm(m, W.fo, nullptr, H, m->qd, m->attn, rows, GEPI_RESADD, m->residual, H))) return rc;
+  if ((rc = tp_post_add(m, rows))) return rc;
   NNZ_CK(rmsnorm_f16_launch(m->residual, W.ffn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st));
   if ((rc = gemm(m, W.fgate, &W.fup, I, H, m->xn, rows, GEPI_SILU, m->h, I))) return rc;
+  if ((rc = tp_pre_add(m, rows))) return rc;
   if ((rc = gemm(m, W.fdown, nullptr, H, I, m->h, rows, GEPI_RESADD, m->residual, H))) return rc;
-  return NNZ_OK;
+  return tp_post_add(m, rows);
 }
 
 int enqueue_prefill(nnz_model* m, uint32_t n, bool want_logits) {
@@ -623,10 +703,11 @@ int enqueue_prefill(nnz_model* m, uint32_t n, bool want_logits) {
         if ((rc = enqueue_layer_gemm(m, l, rows, m->iota + c0))) return rc;
       if (c0 + rows == n) {
         const float* last = m->residual + (size_t)(rows - 1) * m->c.hidden_size;
-        if ((rc = qmv(m, 1, PRO_NORM, EPI_LOGITS, m->lm, m->c.vocab_size, m->c.hidden_size, last,
+        if ((rc = qmv(m, 1, PRO_NORM, EPI_LOGITS, m->lm, m->lm_rows, m->c.hidden_size, last,
                       m->c.hidden_size, m->fnorm, 1, nullptr, 0, want_logits ? m->logits : nullptr,
                       m->state->argmax, 0)))
           return rc;
+        if ((rc = tp_argmax(m, 1))) return rc;
       }
     }
     return NNZ_OK;
@@ -638,10 +719,11 @@ int enqueue_prefill(nnz_model* m, uint32_t n, bool want_logits) {
       if ((rc = enqueue_layer(m, l, rows, m->iota + c0, m->zeros, true, 0))) return rc;
     if (c0 + rows == n) {
       const float* last = m->residual + (size_t)(rows - 1) * m->c.hidden_size;
-      if ((rc = qmv(m, 1, PRO_NORM, EPI_LOGITS, m->lm, m->c.vocab_size, m->c.hidden_size, last,
+      if ((rc = qmv(m, 1, PRO_NORM, EPI_LOGITS, m->lm, m->lm_rows, m->c.hidden_size, last,
                     m->c.hidden_size, m->fnorm, 1, nullptr, 0, want_logits ? m->logits : nullptr,
                     m->state->argmax, 0)))
         return rc;
+      if ((rc = tp_argmax(m, 1))) return rc;
     }
   }
   return NNZ_OK;
@@ -704,13 +786,37 @@ int nnz_model_create(int device, const nnz_config* cfg, nnz_model** out) {
   if (!c.vocab_size || !c.num_layers || !c.max_context_length)
     return fail(NNZ_EINVAL, "vocab_size, num_layers and max_context_length must be > 0");
   if (c.max_batch == 0 || c.max_batch > (uint32_t)kMaxRows) return fail(NNZ_EINVAL, "max_batch");
-  if (c.tp_size > 1) return fail(NNZ_EINVAL, "tensor parallelism is driven per rank by the host");
+  const int tp = c.tp_size > 1 ? c.tp_size : 1;
+  if (tp > 1) {
+    if (tp > 64 || c.tp_rank < 0 || c.tp_rank >= tp) return fail(NNZ_EINVAL, "tp_rank / tp_size");
+    if (c.num_kv_heads % tp || c.intermediate_size % ((uint32_t)tp * gs) ||
+        (qd / tp) % gs)
+      return fail(NNZ_EINVAL, "tensor parallelism needs num_kv_heads, intermediate_size / group_size "
+                              "and query dim / group_size divisible by tp_size");
+  }
   int ndev = 0;
   NNZ_CK(cudaGetDeviceCount(&ndev));
   if (device < 0 || device >= ndev) return fail(NNZ_EINVAL, "bad device index");
   auto* m = new nnz_model();
   m->c = c;
   if (m->c.eps <= 0.f) m->c.eps = 1e-6f;
+  m->full = m->c;
+  m->tp = tp;
+  m->tp_rank = tp > 1 ? c.tp_rank : 0;
+  if (tp > 1) {
+    m->c.num_query_heads /= tp;
+    m->c.num_kv_heads /= tp;
+    m->c.intermediate_size /= tp;
+  }
+  {
+    const uint32_t per = (c.vocab_size + tp - 1) / tp;
+    m->lm_off = std::min(c.vocab_size, per * (uint32_t)m->tp_rank);
+    m->lm_rows = std::min(c.vocab_size - m->lm_off, per);
+    if (m->lm_rows == 0) {
+      delete m;
+      return fail(NNZ_EINVAL, "vocab_size smaller than tp_size");
+    }
+  }
   m->device = device;
   m->fmt = c.quant_format;
   m->bf16s = (c.quant_format == NNZ_Q4 && c.scale_dtype == NNZ_SCALE_BF16) ? 1 : 0;
@@ -732,6 +838,7 @@ int nnz_model_load_tensor(nnz_model* m, const char* name, int dtype, const void*
 int nnz_model_finalize(nnz_model* m) {
   if (!m) return fail(NNZ_EINVAL, "null model");
   if (m->finalized) return fail(NNZ_ESTATE, "model already finalized");
+  if (m->tp > 1 && !m->comm) return fail(NNZ_ESTATE, "tensor-parallel model: call nnz_tp_init first");
   const nnz_config& c = m->c;
   NNZ_CK(cudaSetDevice(m->device));
   NNZ_CK(cudaDeviceGetAttribute(&m->num_sms, cudaDevAttrMultiProcessorCount, m->device));
@@ -753,7 +860,7 @@ int nnz_model_finalize(nnz_model* m) {
   const size_t b_o = packed_bytes(fmt, H, m->qd, gs, 1);
   const size_t b_gu = packed_bytes(fmt, I, H, gs, 2);
   const size_t b_dn = packed_bytes(fmt, H, I, gs, 1);
-  const size_t b_lm = packed_bytes(fmt, c.vocab_size, H, gs, 1);
+  const size_t b_lm = packed_bytes(fmt, m->lm_rows, H, gs, 1);
   const size_t emb_w = fmt == NNZ_Q1 ? (size_t)c.vocab_size * H / 8 : (size_t)c.vocab_size * H / 2;
   const size_t emb_g = (size_t)c.vocab_size * H / gs;
   size_t off = 0;
@@ -782,7 +889,7 @@ int nnz_model_finalize(nnz_model* m) {
       const char* names[3] = {"self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"};
       const uint32_t rows[3] = {m->qd, m->kvd, m->kvd};
       for (int i = 0; i < 3; ++i) {
-        if ((rc = get_proj(m, pre + names[i], rows[i], H, w, s, b))) return rc;
+        if ((rc = get_proj_tp(m, pre + names[i], rows[i], H, 0, w, s, b))) return rc;
         wc.insert(wc.end(), w.begin(), w.end());
         sc.insert(sc.end(), s.begin(), s.end());
         bc.insert(bc.end(), b.begin(), b.end());
@@ -793,20 +900,20 @@ int nnz_model_finalize(nnz_model* m) {
                 buf.data(), 0);
       NNZ_CK(cudaMemcpy(m->arena + lo[l].qkv, buf.data(), b_qkv, cudaMemcpyHostToDevice));
     }
-    if ((rc = get_proj(m, pre + "self_attn.o_proj", H, m->qd, w, s, b))) return rc;
+    if ((rc = get_proj_tp(m, pre + "self_attn.o_proj", H, m->qd, 1, w, s, b))) return rc;
     if (m->gemm_prefill && (rc = upload_flat(m, w, s, b, &m->L[l].fo))) return rc;
     buf.assign(b_o, 0);
     pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), H, m->qd, gs, 1, 0, buf.data(), 0);
     NNZ_CK(cudaMemcpy(m->arena + lo[l].o, buf.data(), b_o, cudaMemcpyHostToDevice));
     buf.assign(b_gu, 0);
-    if ((rc = get_proj(m, pre + "mlp.gate_proj", I, H, w, s, b))) return rc;
+    if ((rc = get_proj_tp(m, pre + "mlp.gate_proj", I, H, 0, w, s, b))) return rc;
     if (m->gemm_prefill && (rc = upload_flat(m, w, s, b, &m->L[l].fgate))) return rc;
     pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), I, H, gs, 2, 0, buf.data(), 0);
-    if ((rc = get_proj(m, pre + "mlp.up_proj", I, H, w, s, b))) return rc;
+    if ((rc = get_proj_tp(m, pre + "mlp.up_proj", I, H, 0, w, s, b))) return rc;
     if (m->gemm_prefill && (rc = upload_flat(m, w, s, b, &m->L[l].fup))) return rc;
     pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), I, H, gs, 2, 1, buf.data(), 0);
     NNZ_CK(cudaMemcpy(m->arena + lo[l].gu, buf.data(), b_gu, cudaMemcpyHostToDevice));
-    if ((rc = get_proj(m, pre + "mlp.down_proj", H, I, w, s, b))) return rc;
+    if ((rc = get_proj_tp(m, pre + "mlp.down_proj", H, I, 1, w, s, b))) return rc;
     if (m->gemm_prefill && (rc = upload_flat(m, w, s, b, &m->L[l].fdown))) return rc;
     buf.assign(b_dn, 0);
     pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), H, I, gs, 1, 0, buf.data(), 0);
@@ -840,6 +947,9 @@ int nnz_model_finalize(nnz_model* m) {
   if (fmt == NNZ_Q4) NNZ_CK(cudaMemcpy(m->arena + o_embb, b.data(), emb_g * 2, cudaMemcpyHostToDevice));
   if (!c.tie_word_embeddings) {
     if ((rc = get_proj(m, "lm_head", c.vocab_size, H, w, s, b))) return rc;
+  }
+  if (m->tp > 1 && (rc = shard_vec(m, 0, c.vocab_size, H, m->lm_off, m->lm_off + m->lm_rows, w, s, b))) return rc;
+  if (!c.tie_word_embeddings || m->tp > 1) {
     if (m->gemm_prefill && (rc = upload_flat(m, w, s, b, &m->flm))) return rc;
   } else if (m->gemm_prefill) {
     m->flm.w = m->arena + o_embw;
@@ -847,7 +957,7 @@ int nnz_model_finalize(nnz_model* m) {
     m->flm.b = fmt == NNZ_Q4 ? reinterpret_cast<const uint16_t*>(m->arena + o_embb) : nullptr;
   }
   buf.assign(b_lm, 0);
-  pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), c.vocab_size, H, gs, 1, 0,
+  pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), m->lm_rows, H, gs, 1, 0,
             buf.data(), 0);
   NNZ_CK(cudaMemcpy(m->arena + o_lm, buf.data(), b_lm, cudaMemcpyHostToDevice));
   {
@@ -876,7 +986,7 @@ int nnz_model_finalize(nnz_model* m) {
   if ((rc = dalloc(m, (void**)&m->attn, (size_t)R * m->qd * 2))) return rc;
   if ((rc = dalloc(m, (void**)&m->h, (size_t)R * I * 2))) return rc;
   if (m->gemm_prefill && (rc = dalloc(m, (void**)&m->xn, (size_t)R * H * 2))) return rc;
-  if ((rc = dalloc(m, (void**)&m->logits, (size_t)c.max_batch * c.vocab_size * 4))) return rc;
+  if ((rc = dalloc(m, (void**)&m->logits, (size_t)c.max_batch * m->lm_rows * 4))) return rc;
   size_t wsf = 0, nctr = 0;
   for (uint32_t rows = 1; rows <= R; ++rows) {
     const uint32_t ych = (rows + kBatchChunk - 1) / kBatchChunk;
@@ -889,7 +999,7 @@ int nnz_model_finalize(nnz_model* m) {
                                        (int)c.head_dim, c.max_context_length));
     nctr = std::max(nctr, (size_t)rows * c.num_kv_heads);
   }
-  wsf = std::max(wsf, qmv_ws_floats(c.vocab_size, H, gs, fmt, 1, c.max_batch, m->num_sms));
+  wsf = std::max(wsf, qmv_ws_floats(m->lm_rows, H, gs, fmt, 1, c.max_batch, m->num_sms));
   m->ws_floats = std::max<size_t>(wsf, 1024);
   m->n_counters = std::max<size_t>(nctr, 1024);
   if ((rc = dalloc(m, (void**)&m->ws, m->ws_floats * 4))) return rc;
@@ -927,7 +1037,7 @@ int nnz_model_finalize(nnz_model* m) {
   {
     // persistent decode kernel buffers (NNZ_DECODE_PATH=graph disables it)
     const char* path = getenv("NNZ_DECODE_PATH");
-    m->mega_ok = !(path && strcmp(path, "graph") == 0) && !m->bf16r;
+    m->mega_ok = !(path && strcmp(path, "graph") == 0) && !m->bf16r && m->tp == 1;
     if (m->mega_ok) {
       const uint32_t bmax = std::min<uint32_t>(c.max_batch, kBatchChunk);
       const size_t G = c.num_query_heads / c.num_kv_heads;
@@ -965,11 +1075,52 @@ int nnz_model_free(nnz_model* m) {
   for (auto e : m->events) cudaEventDestroy(e);
   for (void* p : m->allocs) cudaFree(p);
   if (m->st) cudaStreamDestroy(m->st);
+  if (m->comm)
+    if (const NcclApi* api = nccl_api(nullptr)) api->comm_destroy(m->comm);
   delete m;
   return NNZ_OK;
 }
 
 size_t nnz_model_device_bytes(const nnz_model* m) { return m ? m->dev_bytes : 0; }
+uint32_t nnz_model_vocab_shard(const nnz_model* m) { return m ? m->lm_rows : 0; }
+
+int nnz_shard_weights(int fmt, int axis, const void* weight, const uint16_t* scales, const uint16_t* biases,
+                      uint32_t M, uint32_t K, uint32_t gs, uint32_t lo, uint32_t hi, void* weight_out,
+                      uint16_t* scales_out, uint16_t* biases_out) {
+  if (shard_host(fmt, axis, weight, scales, biases, M, K, gs, lo, hi, weight_out, scales_out, biases_out))
+    return fail(NNZ_EINVAL, "nnz_shard_weights: invalid arguments");
+  return NNZ_OK;
+}
+
+int nnz_tp_unique_id(void* out, size_t cap) {
+  if (!out || cap < sizeof(ncclUniqueId)) return fail(NNZ_EINVAL, "nnz_tp_unique_id: buffer too small");
+  std::string e;
+  const NcclApi* api = nccl_api(&e);
+  if (!api) return fail(NNZ_ENCCL, e);
+  ncclUniqueId id;
+  const ncclResult_t r = api->get_unique_id(&id);
+  if (r != ncclSuccess) return nccl_fail(r);
+  memcpy(out, &id, sizeof(id));
+  return (int)sizeof(id);
+}
+
+int nnz_tp_init(nnz_model* m, const void* unique_id, size_t len) {
+  if (!m || !unique_id || len != sizeof(ncclUniqueId)) return fail(NNZ_EINVAL, "nnz_tp_init: bad arguments");
+  if (m->tp == 1) return fail(NNZ_ESTATE, "nnz_tp_init: model was not created with tp_size > 1");
+  if (m->finalized || m->comm) return fail(NNZ_ESTATE, "nnz_tp_init: call once, before finalize");
+  std::string e;
+  const NcclApi* api = nccl_api(&e);
+  if (!api) return fail(NNZ_ENCCL, e);
+  NNZ_CK(cudaSetDevice(m->device));
+  ncclUniqueId id;
+  memcpy(&id, unique_id, sizeof(id));
+  const ncclResult_t r = api->comm_init_rank(&m->comm, m->tp, id, m->tp_rank);
+  if (r != ncclSuccess) {
+    m->comm = nullptr;
+    return nccl_fail(r);
+  }
+  return NNZ_OK;
+}
 
 int nnz_forward_decode(nnz_model* m, const uint32_t* tokens, const uint32_t* positions,
                        uint32_t batch, float* logits, uint32_t* argmax_out) {
@@ -989,7 +1140,7 @@ int nnz_forward_decode(nnz_model* m, const uint32_t* tokens, const uint32_t* pos
   std::vector<unsigned long long> am(batch);
   NNZ_CK(cudaMemcpyAsync(am.data(), m->state->argmax, batch * 8, cudaMemcpyDeviceToHost, m->st));
   if (logits)
-    NNZ_CK(cudaMemcpyAsync(logits, m->logits, (size_t)batch * m->c.vocab_size * 4,
+    NNZ_CK(cudaMemcpyAsync(logits, m->logits, (size_t)batch * m->lm_rows * 4,
                            cudaMemcpyDeviceToHost, m->st));
   if ((rc = sync_check(m))) return rc;
   for (uint32_t r = 0; r < batch; ++r) argmax_out[r] = argmax_index(am[r]);
@@ -1014,7 +1165,7 @@ int nnz_prefill(nnz_model* m, const uint32_t* tokens, uint32_t n, uint32_t* next
   unsigned long long am = 0;
   NNZ_CK(cudaMemcpyAsync(&am, m->state->argmax, 8, cudaMemcpyDeviceToHost, m->st));
   if (last_logits)
-    NNZ_CK(cudaMemcpyAsync(last_logits, m->logits, (size_t)m->c.vocab_size * 4,
+    NNZ_CK(cudaMemcpyAsync(last_logits, m->logits, (size_t)m->lm_rows * 4,
                            cudaMemcpyDeviceToHost, m->st));
   if ((rc = sync_check(m))) return rc;
   *next_token = argmax_index(am);

@@ -186,4 +186,33 @@ int unpack_host(int fmt, const void* packed, uint32_t M, uint32_t K, uint32_t gs
   return 0;
 }
 
+int shard_host(int fmt, int axis, const void* weight, const uint16_t* scales, const uint16_t* biases,
+               uint32_t M, uint32_t K, uint32_t gs, uint32_t lo, uint32_t hi, void* w_out,
+               uint16_t* s_out, uint16_t* b_out) {
+  if ((fmt != FMT_Q1 && fmt != FMT_Q4) || gs == 0 || K % gs || lo >= hi || !weight || !scales || !w_out ||
+      !s_out || (fmt == FMT_Q4 && (!biases || !b_out)))
+    return -1;
+  const uint8_t* w = static_cast<const uint8_t*>(weight);
+  uint8_t* wo = static_cast<uint8_t*>(w_out);
+  const size_t row_bytes = fmt == FMT_Q1 ? K / 8 : K / 2;   // 1 or 4 bits per weight
+  const uint32_t ng = K / gs;
+  if (axis == 0) {
+    if (hi > M) return -1;
+    const size_t n = hi - lo;
+    memcpy(wo, w + lo * row_bytes, n * row_bytes);
+    memcpy(s_out, scales + (size_t)lo * ng, n * ng * 2);
+    if (fmt == FMT_Q4) memcpy(b_out, biases + (size_t)lo * ng, n * ng * 2);
+    return 0;
+  }
+  if (axis != 1 || hi > K || lo % gs || hi % gs) return -1;
+  const uint32_t kc = hi - lo, g0 = lo / gs, gn = kc / gs;
+  const size_t b0 = fmt == FMT_Q1 ? lo / 8 : lo / 2, bn = fmt == FMT_Q1 ? kc / 8 : kc / 2;
+  for (uint32_t r = 0; r < M; ++r) {
+    memcpy(wo + (size_t)r * bn, w + (size_t)r * row_bytes + b0, bn);
+    memcpy(s_out + (size_t)r * gn, scales + (size_t)r * ng + g0, (size_t)gn * 2);
+    if (fmt == FMT_Q4) memcpy(b_out + (size_t)r * gn, biases + (size_t)r * ng + g0, (size_t)gn * 2);
+  }
+  return 0;
+}
+
 }  // namespace nnz

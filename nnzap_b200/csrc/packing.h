@@ -65,5 +65,11 @@ int pack_host(int fmt, const void* weight, const uint16_t* scales, const uint16_
               int nthreads);
 int unpack_host(int fmt, const void* packed, uint32_t M, uint32_t K, uint32_t gs, uint32_t sub,
                 uint32_t sub_index, void* weight, uint16_t* scales, uint16_t* biases);
+// Tensor-parallel shard of a flat [M][K] matrix: rows [lo, hi) (axis 0) or
+// columns [lo, hi) (axis 1, lo and hi multiples of gs) into flat outputs of
+// the shard's own shape.  biases may be null (Q1).
+int shard_host(int fmt, int axis, const void* weight, const uint16_t* scales, const uint16_t* biases,
+               uint32_t M, uint32_t K, uint32_t gs, uint32_t lo, uint32_t hi, void* w_out,
+               uint16_t* s_out, uint16_t* b_out);
 
 }  // namespace nnz

@@ -45,6 +45,8 @@ class TransformerConfig:
     bf16_faithful: bool = False         # q4: truncate outputs to BF16
     rope_style: str = "pairwise"        # "pairwise" (engine) | "half_split" (MLX/HF)
     q1_scales_are_mlx: bool = False     # halve Q1 scales at load (model.zig:944-959)
+    tp_rank: int = 0                    # tensor-parallel rank / size (batched decode)
+    tp_size: int = 1
 
     @property
     def query_dim(self) -> int:
@@ -77,7 +79,7 @@ class TransformerConfig:
                         "half_split": capi.NNZ_ROPE_HALF_SPLIT}[self.rope_style]
         c.tie_word_embeddings = int(self.tie_word_embeddings)
         c.q1_scales_are_mlx = int(self.q1_scales_are_mlx)
-        c.tp_rank, c.tp_size = 0, 1
+        c.tp_rank, c.tp_size = int(self.tp_rank), int(self.tp_size)
         return c
 
 
@@ -135,12 +137,26 @@ def _dtype_code(a: np.ndarray) -> int:
 class Model:
     """Model(Config) of model.zig: owns every device buffer of one model."""
 
-    def __init__(self, config: TransformerConfig, device: int = 0):
+    def __init__(self, config: TransformerConfig, device: int = 0, tp_unique_id: bytes | None = None):
+        """With config.tp_size > 1 this process holds rank config.tp_rank's
+        shard; every rank passes the same ``tp_unique_id`` (from
+        :func:`tp_unique_id` on one rank, shared by the caller) and the
+        constructor joins the NCCL group."""
         self.config = config
         self.device = device
         self._h = C.c_void_p()
         check(lib().nnz_model_create(device, C.byref(config.to_c()), C.byref(self._h)))
         self._finalized = False
+        if config.tp_size > 1:
+            if tp_unique_id is None:
+                raise ValueError("tensor-parallel model needs tp_unique_id")
+            uid = (C.c_uint8 * len(tp_unique_id)).from_buffer_copy(tp_unique_id)
+            check(lib().nnz_tp_init(self._h, uid, len(tp_unique_id)))
+
+    @property
+    def vocab_shard(self) -> int:
+        """LM-head rows this rank computes (vocab_size without TP)."""
+        return int(lib().nnz_model_vocab_shard(self._h))
 
     # -- model.zig:196 loadWeights ---------------------------------------
     def load_tensor(self, name: str, arr: np.ndarray, dtype: int | None = None) -> None:
@@ -166,14 +182,14 @@ class Model:
         p = np.ascontiguousarray(np.atleast_1d(positions), dtype=np.uint32)
         b = len(t)
         am = np.zeros(b, dtype=np.uint32)
-        lg = np.empty((b, self.config.vocab_size), dtype=np.float32) if want_logits else None
+        lg = np.empty((b, self.vocab_shard), dtype=np.float32) if want_logits else None
         check(lib().nnz_forward_decode(self._h, ptr(t), ptr(p), b, ptr(lg), ptr(am)))
         return am, lg
 
     def prefill(self, tokens, want_logits: bool = False):
         t = np.ascontiguousarray(tokens, dtype=np.uint32)
         nxt = np.zeros(1, dtype=np.uint32)
-        lg = np.empty(self.config.vocab_size, dtype=np.float32) if want_logits else None
+        lg = np.empty(self.vocab_shard, dtype=np.float32) if want_logits else None
         check(lib().nnz_prefill(self._h, ptr(t), len(t), ptr(nxt), ptr(lg)))
         return int(nxt[0]), lg
 
@@ -218,6 +234,33 @@ class Model:
             self.free()
         except Exception:
             pass
+
+
+def tp_unique_id() -> bytes:
+    """A new NCCL group id (create on one rank, hand to all)."""
+    buf = (C.c_uint8 * 256)()
+    n = lib().nnz_tp_unique_id(buf, 256)
+    if n < 0:
+        check(n)
+    return bytes(buf[:n])
+
+
+def shard_weights(fmt: str, axis: int, weight: np.ndarray, scales: np.ndarray, biases, M: int, K: int,
+                  gs: int, lo: int, hi: int):
+    """Host-side tensor-parallel slice of a flat reference-layout matrix:
+    rows [lo, hi) (axis 0) or columns [lo, hi) (axis 1)."""
+    code = {"q1_0": capi.NNZ_Q1, "q4_mlx": capi.NNZ_Q4}[fmt]
+    Mo, Ko = (hi - lo, K) if axis == 0 else (M, hi - lo)
+    wbytes = Mo * Ko // 8 if code == capi.NNZ_Q1 else Mo * Ko // 2
+    w = np.zeros(wbytes, np.uint8)
+    s = np.zeros(Mo * Ko // gs, np.uint16)
+    b = np.zeros_like(s) if biases is not None else None
+    weight = np.ascontiguousarray(weight)
+    scales = np.ascontiguousarray(scales, dtype=np.uint16)
+    bi = None if biases is None else np.ascontiguousarray(biases, dtype=np.uint16)
+    check(lib().nnz_shard_weights(code, axis, ptr(weight), ptr(scales), ptr(bi), M, K, gs, lo, hi,
+                                  ptr(w), ptr(s), ptr(b)))
+    return w, s, b
 
 
 def generate(model: Model, opts: GenerateOpts) -> GenerateResult:
