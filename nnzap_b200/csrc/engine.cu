@@ -205,6 +205,8 @@ struct nnz_model {
   __half* xn = nullptr;          // fp16 RMSNorm output [rows_max][max(H, ...)] (GEMM prefill)
   bool gemm_prefill = false;
   FlatW flm;                           // LM head in the reference layout (GEMM decode of large batches)
+  float* gacc = nullptr;               // split-K accumulator of decode GEMMs (zero at rest)
+  size_t gacc_floats = 0;
   uint8_t* flat = nullptr;       // flat weight copies for the GEMM prefill
   __half *qkv = nullptr, *attn = nullptr, *h = nullptr;
   float* logits = nullptr;
@@ -659,6 +661,7 @@ int gemm(nnz_model* m, const FlatW& W, const FlatW* W2, uint32_t N, uint32_t K, 
   g.bf16r = m->bf16r; g.w = W.w; g.s = W.s; g.b = W.b;
   if (W2) { g.w2 = W2->w; g.s2 = W2->s; g.b2 = W2->b; }
   g.epi = epi; g.out = out; g.ldo = ldo; g.err = m->err;
+  g.acc = m->gacc; g.acc_floats = m->gacc_floats;
   NNZ_CK(gemm_launch(g, x, m->st));
   return NNZ_OK;
 }
@@ -986,6 +989,12 @@ int nnz_model_finalize(nnz_model* m) {
   if ((rc = dalloc(m, (void**)&m->attn, (size_t)R * m->qd * 2))) return rc;
   if ((rc = dalloc(m, (void**)&m->h, (size_t)R * I * 2))) return rc;
   if (m->gemm_prefill && (rc = dalloc(m, (void**)&m->xn, (size_t)R * H * 2))) return rc;
+  if (m->gemm_prefill && c.max_batch >= kGemmDecodeRows) {
+    const size_t n = (size_t)c.max_batch * std::max<size_t>(std::max<size_t>(m->qkv_rows, 2 * I), H);
+    if ((rc = dalloc(m, (void**)&m->gacc, n * 4))) return rc;
+    NNZ_CK(cudaMemset(m->gacc, 0, n * 4));
+    m->gacc_floats = n;
+  }
   if ((rc = dalloc(m, (void**)&m->logits, (size_t)c.max_batch * m->lm_rows * 4))) return rc;
   size_t wsf = 0, nctr = 0;
   for (uint32_t rows = 1; rows <= R; ++rows) {
@@ -1508,6 +1517,14 @@ int nnz_attn_decode(const void* qkv, const float* q_norm, const float* k_norm, v
       (size_t)rows * n_kv > w->n_counters)
     return fail(NNZ_EINVAL, "nnz_attn_decode: problem too large for the shared workspace");
   NNZ_CK(attn_decode_launch(a, (int)head_dim, 0, (cudaStream_t)stream));
+  return NNZ_OK;
+}
+
+// Development aid (not part of the documented ABI): clock64() stamps of CTA
+// (0,0,0) of the last GEMM launched with NNZ_GEMM_PROFILE=1.
+int nnz_debug_gemm_profile(uint64_t* out) {
+  if (!out) return fail(NNZ_EINVAL, "null");
+  NNZ_CK(gemm_debug_profile(reinterpret_cast<unsigned long long*>(out)));
   return NNZ_OK;
 }
 

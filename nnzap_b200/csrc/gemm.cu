@@ -4,15 +4,18 @@
 
 #include "gemm.cuh"
 
+#include <stdlib.h>
+
 namespace nnz {
 namespace {
 
 constexpr int kBM = 128, kBN = 128, kBK = 64, kStages = 4;
 constexpr uint32_t kTileBytes = kBM * kBK * 2;          // 16 KB per operand per stage
 constexpr uint32_t kTmemCols = 128;
-constexpr int kThreads = 256;
-constexpr int kProducers = 128;   // dequantizing threads (warps 4-7)
-constexpr int kPf = 4;            // raw-weight prefetch depth (steps)
+constexpr int kGroups = 2;        // dequantizing groups of 4 warps, K steps dealt round robin
+constexpr int kThreads = 128 + 128 * kGroups;
+constexpr int kProducerWarps = 4;   // full-barrier arrivals per stage: one per warp of the filling group
+constexpr int kPf = 4;            // raw-weight prefetch depth (steps of a producer group)
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -97,42 +100,64 @@ __device__ __forceinline__ float u16f(uint16_t v, int bf16s) {
 }
 
 // Dequantize one row's 64 weights into the 128B-swizzled K-major stage.
+// Dequantize one row's 64 weights into the 128B-swizzled K-major stage
+// (.shared addresses).
 template <int FMT>
-__device__ __forceinline__ void write_row(uint8_t* stage, uint32_t r, const Raw& raw, int bf16s) {
-  uint8_t* rowp = stage + (r >> 3) * 1024 + (r & 7) * 128;
+__device__ __forceinline__ void write_row(uint32_t stage, uint32_t r, const Raw& raw, int bf16s) {
+  const uint32_t rowp = stage + (r >> 3) * 1024 + (r & 7) * 128;
+  uint32_t h[8][4];
+  if constexpr (FMT == FMT_Q1) {
+    // bit 2j / 2j+1 of byte c -> sign of half 0 / 1 of word j: +s for 1, -s for 0
+    const uint32_t sp = raw.s, sn = raw.s ^ 0x8000u;
 #pragma unroll
-  for (uint32_t c = 0; c < 8; ++c) {
-    uint32_t h[4];
-    if constexpr (FMT == FMT_Q1) {
-      const uint32_t bits = ((c < 4 ? raw.q0.x : raw.q0.y) >> (8 * (c & 3))) & 0xFFu;
-      const uint32_t sp = raw.s, sn = raw.s ^ 0x8000u;
+    for (uint32_t c = 0; c < 8; ++c) {
+      const uint32_t bits = (c < 4 ? raw.q0.x : raw.q0.y) >> (8 * (c & 3));
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t lo = ((bits >> (2 * j)) & 1u) ? sp : sn;
         const uint32_t hi = ((bits >> (2 * j + 1)) & 1u) ? sp : sn;
-        h[j] = lo | (hi << 16);
+        h[c][j] = lo | (hi << 16);
       }
-    } else {
+    }
+  } else {
+    const float sc = u16f(raw.s, bf16s), bi = u16f(raw.b, bf16s);
+#pragma unroll
+    for (uint32_t c = 0; c < 8; ++c) {
       const uint32_t word = c < 4 ? (&raw.q0.x)[c] : (&raw.q1.x)[c - 4];
-      const float sc = u16f(raw.s, bf16s), bi = u16f(raw.b, bf16s);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float f0 = __fadd_rn(__fmul_rn(sc, (float)((word >> (8 * j)) & 0xFu)), bi);
         const float f1 = __fadd_rn(__fmul_rn(sc, (float)((word >> (8 * j + 4)) & 0xFu)), bi);
         const __half2 v = __floats2half2_rn(f0, f1);
-        h[j] = *reinterpret_cast<const uint32_t*>(&v);
+        h[c][j] = *reinterpret_cast<const uint32_t*>(&v);
       }
     }
-    *reinterpret_cast<uint4*>(rowp + ((c ^ (r & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
   }
+#pragma unroll
+  for (uint32_t c = 0; c < 8; ++c)
+    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(rowp + ((c ^ (r & 7)) << 4)), "r"(h[c][0]),
+                 "r"(h[c][1]), "r"(h[c][2]), "r"(h[c][3])
+                 : "memory");
 }
 
-// Warp roles (256 threads): warp 0 lane 0 streams X tiles with TMA up to
-// kStages ahead; warp 1 lane 0 issues the MMAs; warps 4-7 dequantize one
-// weight row each into the B stages (raw weights prefetched kPf steps ahead
-// in registers) and run the epilogue (TMEM lane quarter = warp % 4).
+// Warp roles (128 + 128 kGroups threads): warp 0 lane 0 streams X tiles
+// with TMA up to kStages ahead; warp 1 lane 0 issues the MMAs; the warps
+// from 4 on dequantize the weights into the B stages in kGroups groups of
+// four -- group g takes K steps g, g + kGroups, ..., one weight row per
+// thread, raw weights prefetched kPf of the group's steps ahead in
+// registers -- so one group's proxy fence and barrier arrival overlap the
+// others' dequantization.  Groups 0 and 1 (warps 4-11) run the epilogue
+// (TMEM lane quarter = warp % 4, the two groups taking alternate column
+// halves).
 // Split-K over gridDim.z is allowed only for the residual-add epilogue,
 // whose partial sums are accumulated with atomicAdd.
+// Development aid: NNZ_GEMM_PROFILE=1 makes CTA (0,0,0) record clock64()
+// stamps of its pipeline (read back with nnz_debug_gemm_profile).
+__device__ unsigned long long g_gemm_prof[128];
+__device__ __forceinline__ void gstamp(const GemmArgs& a, int i) {
+  if (a.prof && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && i < 128) g_gemm_prof[i] = clock64();
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmX, GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -145,6 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) gstamp(a, 0);
   const uint32_t m0 = blockIdx.y * kBM;
   const bool silu = a.epi == GEPI_SILU;
   const uint32_t ncols = silu ? kBN / 2 : kBN;           // output columns per tile
@@ -155,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], kProducers + 1);
+      mbar_init(&full[s], kProducerWarps + 1);
       mbar_init(&empty[s], 1);
     }
     mbar_init(done, 1);
@@ -173,6 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   const uint32_t tmem = *tslot;
   pdl_wait();
   pdl_launch();
+  if (tid == 0) gstamp(a, 1);
   bool failed = false;
 
   if (warp == 0) {
@@ -190,6 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       for (uint32_t i = 0; i < nk; ++i) {
         const uint32_t s = i % kStages;
         if (!failed) failed = !mbar_wait(&full[s], (i / kStages) & 1u, a.err);
+        if (i < 32) gstamp(a, 66 + (int)i);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint64_t da = smem_desc_sw128(As + s * kTileBytes);
         const uint64_t db = smem_desc_sw128(Bs + s * kTileBytes);
@@ -201,7 +229,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       umma_commit(done);
     }
   } else if (warp >= 4) {
-    const uint32_t r = tid - 128;              // weight row of the tile
+    const uint32_t r = (tid - 128) & (kBN - 1);   // weight row of the tile
+    const uint32_t grp = (tid - 128) / kBN;       // K steps grp, grp + kGroups, ...
     const uint8_t* w = a.w;
     const uint16_t* sc = a.s;
     const uint16_t* bi = a.b;
@@ -210,32 +239,51 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     const bool rok = row < a.N;
     Raw raw[kPf];
 #pragma unroll
-    for (int d = 0; d < kPf; ++d) raw[d] = load_raw<FMT>(a, w, sc, bi, row, rok && (uint32_t)d < nk, ks0 + d);
-    for (uint32_t i0 = 0; i0 < nk; i0 += kPf) {
+    for (int d = 0; d < kPf; ++d)
+      raw[d] = load_raw<FMT>(a, w, sc, bi, row, rok && grp + kGroups * d < nk, ks0 + grp + kGroups * d);
+    for (uint32_t i0 = grp; i0 < nk; i0 += kGroups * kPf) {
 #pragma unroll
       for (int d = 0; d < kPf; ++d) {
-        const uint32_t i = i0 + d;
+        const uint32_t i = i0 + kGroups * d;
         if (i < nk) {
           const uint32_t s = i % kStages;
           if (i >= (uint32_t)kStages && !failed) failed = !mbar_wait(&empty[s], ((i / kStages) - 1) & 1u, a.err);
-          write_row<FMT>(Bs + s * kTileBytes, r, raw[d], a.bf16s);
+          if (tid == 128 && i < 32) gstamp(a, 2 + (int)i);
+          write_row<FMT>(smem_u32(Bs + s * kTileBytes), r, raw[d], a.bf16s);
+          if (tid == 128 && i < 32) gstamp(a, 34 + (int)i);
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          mbar_arrive(&full[s]);
-          raw[d] = load_raw<FMT>(a, w, sc, bi, row, rok && i + kPf < nk, ks0 + i + kPf);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full[s]);
+          raw[d] = load_raw<FMT>(a, w, sc, bi, row, rok && i + kGroups * kPf < nk, ks0 + i + kGroups * kPf);
         }
       }
     }
   }
-  // ---- epilogue (warps 4-7): TMEM lanes 32q..32q+31 = rows m0 + 32q + lane ----
-  if (warp >= 4) {
+  // ---- epilogue (warps 4-11): TMEM lanes 32q..32q+31 = rows m0 + 32q + lane;
+  // warps 4-7 take column chunks 0-1, warps 8-11 chunks 2-3 ----
+  if (warp >= 4 && warp < 12) {
     if (!failed) failed = !mbar_wait(done, 0, a.err);
+    if (tid == 128) gstamp(a, 98);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int q = warp - 4;
+    const int q = warp & 3, part = (warp - 4) >> 2;
     const uint32_t m = m0 + 32 * q + lane;
     const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16);
     const bool rb = a.bf16r != 0;
-    if (silu) {
-      for (int cc = 0; cc < 2; ++cc) {
+    if (gridDim.z > 1 && a.epi != GEPI_RESADD) {
+      // split K: f32 partials into the accumulator (gate | up halves for SILU)
+      for (int cc = 2 * part; cc < 2 * part + 2; ++cc) {
+        uint32_t v[32];
+        tmem_ld32(tbase + cc * 32, v);
+        if (m >= a.M) continue;
+        const uint32_t half = silu ? (uint32_t)(cc * 32) / (kBN / 2) : 0;
+        const uint32_t nb = n0 + (silu ? (uint32_t)(cc * 32) % (kBN / 2) : (uint32_t)(cc * 32));
+        float* o = a.acc + (size_t)m * (silu ? 2 * a.N : a.N) + half * a.N + nb;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (nb + j < a.N) atomicAdd(&o[j], __uint_as_float(v[j]));
+      }
+    } else if (silu) {
+      for (int cc = part; cc < part + 1; ++cc) {
         uint32_t g[32], u[32];
         tmem_ld32(tbase + cc * 32, g);
         tmem_ld32(tbase + 64 + cc * 32, u);
@@ -252,18 +300,34 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         }
       }
     } else {
-      for (int cc = 0; cc < kBN / 32; ++cc) {
+      for (int cc = 2 * part; cc < 2 * part + 2; ++cc) {
         uint32_t v[32];
         tmem_ld32(tbase + cc * 32, v);
         if (m >= a.M) continue;
         const uint32_t nb = n0 + cc * 32;
         if (a.epi == GEPI_F16) {
           __half* o = static_cast<__half*>(a.out) + (size_t)m * a.ldo + nb;
+          if (nb + 32 <= a.N && (a.ldo & 7) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0) {
+            // 16-byte stores
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float x = __uint_as_float(v[j]);
-            if (rb) x = bf16_trunc(x);
-            if (nb + j < a.N) o[j] = __float2half_rn(x);
+            for (int j = 0; j < 32; j += 8) {
+              uint32_t pk[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                float x0 = __uint_as_float(v[j + 2 * e]), x1 = __uint_as_float(v[j + 2 * e + 1]);
+                if (rb) { x0 = bf16_trunc(x0); x1 = bf16_trunc(x1); }
+                const __half2 h2 = __floats2half2_rn(x0, x1);
+                pk[e] = *reinterpret_cast<const uint32_t*>(&h2);
+              }
+              *reinterpret_cast<uint4*>(o + j) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float x = __uint_as_float(v[j]);
+              if (rb) x = bf16_trunc(x);
+              if (nb + j < a.N) o[j] = __float2half_rn(x);
+            }
           }
         } else {
           float* o = static_cast<float*>(a.out) + (size_t)m * a.ldo + nb;
@@ -282,6 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  if (tid == 128) gstamp(a, 99);
   __syncthreads();
   if (warp == 2)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
@@ -338,6 +403,31 @@ __global__ void __launch_bounds__(256) rmsnorm_f16_kernel(const float* res, cons
   }
 }
 
+// Split-K finalize: the accumulated f32 tile -> the epilogue's output, and
+// the accumulator back to zero for its next use.
+__global__ void __launch_bounds__(256) gemm_finalize_kernel(GemmArgs a) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)a.M * a.N) return;
+  const uint32_t m = (uint32_t)(i / a.N), n = (uint32_t)(i % a.N);
+  const bool rb = a.bf16r != 0;
+  if (a.epi == GEPI_SILU) {
+    float* g = a.acc + (size_t)m * 2 * a.N + n;
+    const float gv = *g, uv = g[a.N];
+    *g = 0.f;
+    g[a.N] = 0.f;
+    float h = gv / (1.0f + expf(-gv)) * uv;
+    if (rb) h = bf16_trunc(h);
+    static_cast<__half*>(a.out)[(size_t)m * a.ldo + n] = __float2half_rn(h);
+    return;
+  }
+  float* p = a.acc + i;
+  float x = *p;
+  *p = 0.f;
+  if (rb) x = bf16_trunc(x);
+  if (a.epi == GEPI_F16) static_cast<__half*>(a.out)[(size_t)m * a.ldo + n] = __float2half_rn(x);
+  else static_cast<float*>(a.out)[(size_t)m * a.ldo + n] = x;
+}
+
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -358,7 +448,17 @@ constexpr uint32_t kSmemBytes = 2 * kStages * kTileBytes + 1024 + 256;
 
 }  // namespace
 
-cudaError_t gemm_launch(const GemmArgs& a, const __half* x, cudaStream_t st) {
+cudaError_t gemm_debug_profile(unsigned long long* out) {
+  return cudaMemcpyFromSymbol(out, g_gemm_prof, sizeof(g_gemm_prof));
+}
+
+cudaError_t gemm_launch(const GemmArgs& a_in, const __half* x, cudaStream_t st) {
+  GemmArgs a = a_in;
+  static const int prof = [] {
+    const char* e = getenv("NNZ_GEMM_PROFILE");
+    return (e && e[0] == '1') ? 1 : 0;
+  }();
+  a.prof = prof;
   if (a.K % kBK || a.gs < 64 || a.K % a.gs || a.M == 0 || a.N == 0 ||
       (a.fmt != FMT_Q1 && a.fmt != FMT_Q4) || (reinterpret_cast<uintptr_t>(x) & 15))
     return cudaErrorInvalidValue;
@@ -375,14 +475,18 @@ cudaError_t gemm_launch(const GemmArgs& a, const __half* x, cudaStream_t st) {
     return cudaErrorInvalidValue;
   const uint32_t ncols = a.epi == GEPI_SILU ? kBN / 2 : kBN;
   dim3 grid((a.N + ncols - 1) / ncols, (a.M + kBM - 1) / kBM);
-  // residual-add GEMMs with few tiles split K (partials added atomically)
-  if (a.epi == GEPI_RESADD && a.bf16r == 0) {
+  // GEMMs with fewer tiles than SMs split K: residual adds accumulate their
+  // partials atomically in place, the other epilogues in the f32
+  // accumulator (when given one that fits), finished by gemm_finalize_kernel
+  const size_t acc_need = (size_t)a.M * a.N * (a.epi == GEPI_SILU ? 2 : 1);
+  const bool can_split = a.epi == GEPI_RESADD ? a.bf16r == 0 : (a.acc && acc_need <= a.acc_floats);
+  if (can_split) {
     int sms = 148, dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     uint32_t ks = (uint32_t)sms / (grid.x * grid.y);
     const uint32_t nk = a.K / kBK;
-    if (ks > nk / 8) ks = nk / 8;            // >= 8 K steps per CTA
+    if (ks > nk / 4) ks = nk / 4;            // >= 4 K steps per CTA
     grid.z = ks < 1 ? 1 : ks;
   }
   cudaLaunchConfig_t cfg = {};
@@ -398,15 +502,21 @@ cudaError_t gemm_launch(const GemmArgs& a, const __half* x, cudaStream_t st) {
       if (e != cudaSuccess) return e;
       attr = true;
     }
-    return cudaLaunchKernelEx(&cfg, &gemm_kernel<FMT_Q1>, tm, a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, &gemm_kernel<FMT_Q1>, tm, a);
+    if (e != cudaSuccess || grid.z == 1 || a.epi == GEPI_RESADD) return e;
+  } else {
+    static bool attr4 = false;
+    if (!attr4) {
+      cudaError_t e = cudaFuncSetAttribute(&gemm_kernel<FMT_Q4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      if (e != cudaSuccess) return e;
+      attr4 = true;
+    }
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, &gemm_kernel<FMT_Q4>, tm, a);
+    if (e != cudaSuccess || grid.z == 1 || a.epi == GEPI_RESADD) return e;
   }
-  static bool attr4 = false;
-  if (!attr4) {
-    cudaError_t e = cudaFuncSetAttribute(&gemm_kernel<FMT_Q4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr4 = true;
-  }
-  return cudaLaunchKernelEx(&cfg, &gemm_kernel<FMT_Q4>, tm, a);
+  const size_t n = (size_t)a.M * a.N;
+  gemm_finalize_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a);
+  return cudaGetLastError();
 }
 
 cudaError_t rmsnorm_f16_launch(const float* res, const float* w, float eps, uint32_t rows, uint32_t K, int bf16r,

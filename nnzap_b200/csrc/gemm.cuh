@@ -34,13 +34,21 @@ struct GemmArgs {
   const uint16_t* s2;
   const uint16_t* b2;
   int epi;
+  // split-K accumulator for the F16 / F32 / SILU epilogues (f32, zero at
+  // rest, [M][N] or [M][2][N] for SILU; the finalize kernel re-zeroes it);
+  // null: those epilogues never split K
+  float* acc;
+  size_t acc_floats;
   void* out;                     // f16 [M][ldo], f32 residual [M][ldo] (+=), or f32 [M][ldo] (GEPI_F32)
   uint32_t ldo;
   int* err;
+  int prof;                      // set by gemm_launch from NNZ_GEMM_PROFILE
 };
 
 // Builds the TMA descriptor for X [M][K] fp16 (row stride K) and launches.
 cudaError_t gemm_launch(const GemmArgs& a, const __half* x, cudaStream_t st);
+// Development aid: the 128 clock64() stamps of the last profiled launch.
+cudaError_t gemm_debug_profile(unsigned long long* out);
 // RMSNorm rows of an f32 residual into fp16 (the prefill GEMM's X operand).
 cudaError_t rmsnorm_f16_launch(const float* res, const float* w, float eps, uint32_t rows, uint32_t K,
                                int bf16r, __half* out, cudaStream_t st);
