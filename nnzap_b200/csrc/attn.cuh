@@ -69,6 +69,9 @@ bool attn_tc_applies(uint32_t n_q, uint32_t n_kv, int head_dim);
 size_t attn_tc_ws_floats(uint32_t rows, uint32_t n_q, uint32_t n_kv, uint32_t max_ctx);
 cudaError_t attn_tc_prepare();
 cudaError_t attn_tc_launch(const AttnArgs& a, int pdl, cudaStream_t st);
+// Causal prefill attention on the tensor cores (same contract as
+// attn_prefill_launch; head_dim 128, G in {1, 2, 4}).
+cudaError_t attn_prefill_tc_launch(const AttnArgs& a, int pdl, cudaStream_t st);
 
 // Writes normed+roped k and v of `rows` query rows at their positions
 // (used by chunked prefill, where rows of one chunk share a cache slot and

@@ -354,6 +354,264 @@ __global__ void __launch_bounds__(4 * kHD) attn_tc_combine_kernel(TcArgs t) {
   a.out[(size_t)row * a.out_stride + ((size_t)kvh * G + h) * kHD + d] = __float2half_rn(o / L);
 }
 
+// ---------------------------------------------------------------------------
+// 4. causal prefill attention on the tensor cores
+// ---------------------------------------------------------------------------
+// One CTA per (kv head, block of query rows): warp w serves query head
+// w % G of the group and 16 consecutive rows (block = 16 * 4 / G rows), so
+// every K/V tile in shared memory feeds all G heads.  Each warp normalises
+// and rotates its rows' queries (f32) and keeps them as fp16 hi/lo A
+// fragments; S = Q_hi K^T + Q_lo K^T and O += P_hi V + P_lo V accumulate in
+// f32, with the causal mask and the online softmax in registers (FA2
+// layout: the score accumulators are the P operand).  64-position K/V tiles
+// are double-buffered with cp.async into rows padded to 272 bytes.
+constexpr int kPfTcKeys = 64;
+constexpr int kPfTcQB = 2 * 16 * kTcRowB;                 // per warp: hi + lo, 16 rows
+constexpr int kPfTcTile = kPfTcKeys * kTcRowB;            // one K or V tile
+constexpr int kPfTcSmem = 4 * kPfTcQB + 2 * 2 * kPfTcTile;
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+template <int G>
+__global__ void __launch_bounds__(128) attn_prefill_tc_kernel(AttnArgs a) {
+  constexpr int RG = 4 / G;                 // 16-row groups per CTA
+  constexpr int QR = 16 * RG;               // query rows per CTA
+  extern __shared__ __align__(128) uint8_t smem[];
+  pdl_wait();
+  pdl_launch();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q4 = lane & 3;
+  const int kvh = blockIdx.x;
+  const int hl = warp % G, rg = warp / G;
+  const int h = kvh * G + hl;
+  const uint32_t rbase = blockIdx.y * QR;
+  uint8_t* qsm = smem + warp * kPfTcQB;
+  uint8_t* kv = smem + 4 * kPfTcQB;
+
+  // CTA key range: up to the largest position of its rows; rows share a slot
+  __shared__ int s_kmax, s_slot;
+  if (threadIdx.x == 0) {
+    int mx = 0;
+    for (int r = 0; r < QR; ++r)
+      if (rbase + r < a.rows) mx = max(mx, min(max(a.pos[rbase + r], 0), (int)a.max_ctx - 1));
+    s_kmax = mx;
+    s_slot = a.slot ? a.slot[rbase] : (int)rbase;
+  }
+  __syncthreads();
+  const int kmax = s_kmax;
+  const size_t head_off = ((size_t)s_slot * a.n_kv + kvh) * a.max_ctx * kHD;
+  auto load_tile = [&](int kb, int stg) {
+    const uint32_t kt = smem_u32(kv + stg * 2 * kPfTcTile), vt = kt + kPfTcTile;
+    for (int c = threadIdx.x; c < kPfTcKeys * 16; c += 128) {
+      const int r = c >> 4, ch = c & 15, t = kb * kPfTcKeys + r;
+      const uint32_t off = r * kTcRowB + ch * 16;
+      if (t <= kmax) {
+        cp_async16(kt + off, a.kc + head_off + (size_t)t * kHD + ch * 8);
+        cp_async16(vt + off, a.vc + head_off + (size_t)t * kHD + ch * 8);
+      } else {
+        // past the last query position: zero, so 0-probability * V stays 0
+        asm volatile("st.shared.v4.b32 [%0], {%1,%1,%1,%1};" ::"r"(kt + off), "r"(0u) : "memory");
+        asm volatile("st.shared.v4.b32 [%0], {%1,%1,%1,%1};" ::"r"(vt + off), "r"(0u) : "memory");
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  load_tile(0, 0);
+
+  // queries: RMSNorm over the head, q_norm, RoPE (f32), then fp16 hi/lo rows
+  {
+    const int EPL = 4;
+    int prow[16];
+    float v[16][4];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t r = rbase + rg * 16 + i;
+      const bool ok = r < a.rows;
+      prow[i] = ok ? min(max(a.pos[r], 0), (int)a.max_ctx - 1) : 0;
+      const __half* src = a.qkv + (size_t)(ok ? r : 0) * a.qkv_stride + (size_t)h * kHD + lane * EPL;
+      const uint2 raw = ok ? *reinterpret_cast<const uint2*>(src) : make_uint2(0, 0);
+      const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+      const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+      v[i][0] = f0.x; v[i][1] = f0.y; v[i][2] = f1.x; v[i][3] = f1.y;
+    }
+    float nw[4];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) nw[e] = a.q_norm[lane * EPL + e];
+    const double l2t = a.rope_tab ? 0.0 : log2((double)a.theta);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float ss = v[i][0] * v[i][0] + v[i][1] * v[i][1] + v[i][2] * v[i][2] + v[i][3] * v[i][3];
+      ss = warp_sum(ss);
+      const float rr = rsqrtf(ss / (float)kHD + a.eps);
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) v[i][e] = v[i][e] * rr * nw[e];
+      const float2* tab = a.rope_tab ? a.rope_tab + (size_t)prow[i] * (kHD / 2) : nullptr;
+      if (a.rope_style == ROPE_PAIRWISE) {
+#pragma unroll
+        for (int e = 0; e < EPL; e += 2) {
+          const float2 cs = rope_cs<kHD>(tab, l2t, prow[i], (lane * EPL + e) >> 1);
+          const float x0 = v[i][e], x1 = v[i][e + 1];
+          v[i][e] = x0 * cs.x - x1 * cs.y;
+          v[i][e + 1] = x0 * cs.y + x1 * cs.x;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          const float partner = __shfl_xor_sync(0xffffffffu, v[i][e], 16);
+          const float2 cs = rope_cs<kHD>(tab, l2t, prow[i], (lane & 15) * EPL + e);
+          v[i][e] = lane < 16 ? v[i][e] * cs.x - partner * cs.y : partner * cs.y + v[i][e] * cs.x;
+        }
+      }
+      uint32_t hi[2], lo[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const __half h0 = __float2half_rn(v[i][2 * e]), h1 = __float2half_rn(v[i][2 * e + 1]);
+        const __half2 hh = __halves2half2(h0, h1);
+        const __half2 ll = __floats2half2_rn(v[i][2 * e] - __half2float(h0), v[i][2 * e + 1] - __half2float(h1));
+        hi[e] = *reinterpret_cast<const uint32_t*>(&hh);
+        lo[e] = *reinterpret_cast<const uint32_t*>(&ll);
+      }
+      const uint32_t qa = smem_u32(qsm) + i * kTcRowB + lane * 8;
+      asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(qa), "r"(hi[0]), "r"(hi[1]) : "memory");
+      asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(qa + 16 * kTcRowB), "r"(lo[0]), "r"(lo[1]) : "memory");
+    }
+  }
+  __syncwarp();
+  // A fragments (row-major 16 x 16 per k-step) of q_hi and q_lo
+  uint32_t qh[8][4], ql[8][4];
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const uint32_t ad = smem_u32(qsm) + (lane & 15) * kTcRowB + (2 * ks + (lane >> 4)) * 16;
+    ldsm_x4(ad, qh[ks][0], qh[ks][1], qh[ks][2], qh[ks][3]);
+    ldsm_x4(ad + 16 * kTcRowB, ql[ks][0], ql[ks][1], ql[ks][2], ql[ks][3]);
+  }
+  int posg = -1, posg8 = -1;   // positions of this lane's rows g and g + 8
+  {
+    const uint32_t r0 = rbase + rg * 16 + g, r1 = r0 + 8;
+    if (r0 < a.rows) posg = min(max(a.pos[r0], 0), (int)a.max_ctx - 1);
+    if (r1 < a.rows) posg8 = min(max(a.pos[r1], 0), (int)a.max_ctx - 1);
+  }
+  int wmax = max(posg, posg8);
+  wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, 4));
+  wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, 8));
+  wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, 16));
+
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const float inv = rsqrtf((float)kHD);
+  const int nkb = kmax / kPfTcKeys + 1;
+  for (int kb = 0; kb < nkb; ++kb) {
+    if (kb + 1 < nkb) load_tile(kb + 1, (kb + 1) & 1);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncthreads();
+    if (kb * kPfTcKeys <= wmax) {
+      const uint32_t kt = smem_u32(kv + (kb & 1) * 2 * kPfTcTile), vt = kt + kPfTcTile;
+      float sc[8][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+        for (int kq = 0; kq < 4; ++kq) {
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4(kt + (nt * 8 + (lane & 7)) * kTcRowB + (4 * kq + (lane >> 3)) * 16, r0, r1, r2, r3);
+          mma_f16(sc[nt], qh[2 * kq][0], qh[2 * kq][1], qh[2 * kq][2], qh[2 * kq][3], r0, r1);
+          mma_f16(sc[nt], ql[2 * kq][0], ql[2 * kq][1], ql[2 * kq][2], ql[2 * kq][3], r0, r1);
+          mma_f16(sc[nt], qh[2 * kq + 1][0], qh[2 * kq + 1][1], qh[2 * kq + 1][2], qh[2 * kq + 1][3], r2, r3);
+          mma_f16(sc[nt], ql[2 * kq + 1][0], ql[2 * kq + 1][1], ql[2 * kq + 1][2], ql[2 * kq + 1][3], r2, r3);
+        }
+      }
+      // scale + causal mask, online softmax for rows g (c0, c1) and g + 8 (c2, c3)
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const int t = kb * kPfTcKeys + nt * 8 + 2 * q4;
+        sc[nt][0] = t <= posg ? sc[nt][0] * inv : -INFINITY;
+        sc[nt][1] = t + 1 <= posg ? sc[nt][1] * inv : -INFINITY;
+        sc[nt][2] = t <= posg8 ? sc[nt][2] * inv : -INFINITY;
+        sc[nt][3] = t + 1 <= posg8 ? sc[nt][3] * inv : -INFINITY;
+        mx0 = fmaxf(mx0, fmaxf(sc[nt][0], sc[nt][1]));
+        mx1 = fmaxf(mx1, fmaxf(sc[nt][2], sc[nt][3]));
+      }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+      const float al0 = n0 == -INFINITY ? 1.f : (m0 == -INFINITY ? 0.f : expf(m0 - n0));
+      const float al1 = n1 == -INFINITY ? 1.f : (m1 == -INFINITY ? 0.f : expf(m1 - n1));
+      m0 = n0;
+      m1 = n1;
+      float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        sc[nt][0] = n0 == -INFINITY ? 0.f : expf(sc[nt][0] - n0);
+        sc[nt][1] = n0 == -INFINITY ? 0.f : expf(sc[nt][1] - n0);
+        sc[nt][2] = n1 == -INFINITY ? 0.f : expf(sc[nt][2] - n1);
+        sc[nt][3] = n1 == -INFINITY ? 0.f : expf(sc[nt][3] - n1);
+        ps0 += sc[nt][0] + sc[nt][1];
+        ps1 += sc[nt][2] + sc[nt][3];
+      }
+      l0 = l0 * al0 + ps0;
+      l1 = l1 * al1 + ps1;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        o[j][0] *= al0; o[j][1] *= al0;
+        o[j][2] *= al1; o[j][3] *= al1;
+      }
+      // O += P V, P as fp16 hi + lo
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t ph[4], pl[4];
+        const float* p0 = sc[2 * kk];
+        const float* p1 = sc[2 * kk + 1];
+        const float pv[8] = {p0[0], p0[1], p0[2], p0[3], p1[0], p1[1], p1[2], p1[3]};
+        // a0: row g keys 2t..; a1: row g+8; a2: row g keys 8+2t..; a3: row g+8
+        const int ord[4][2] = {{0, 1}, {2, 3}, {4, 5}, {6, 7}};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float x = pv[ord[e][0]], y = pv[ord[e][1]];
+          const __half hx = __float2half_rn(x), hy = __float2half_rn(y);
+          const __half2 hh = __halves2half2(hx, hy);
+          const __half2 ll = __floats2half2_rn(x - __half2float(hx), y - __half2float(hy));
+          ph[e] = *reinterpret_cast<const uint32_t*>(&hh);
+          pl[e] = *reinterpret_cast<const uint32_t*>(&ll);
+        }
+#pragma unroll
+        for (int jp = 0; jp < 8; ++jp) {
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4_t(vt + (kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * kTcRowB + (2 * jp + (lane >> 4)) * 16,
+                    r0, r1, r2, r3);
+          mma_f16(o[2 * jp], ph[0], ph[1], ph[2], ph[3], r0, r1);
+          mma_f16(o[2 * jp], pl[0], pl[1], pl[2], pl[3], r0, r1);
+          mma_f16(o[2 * jp + 1], ph[0], ph[1], ph[2], ph[3], r2, r3);
+          mma_f16(o[2 * jp + 1], pl[0], pl[1], pl[2], pl[3], r2, r3);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const uint32_t r0 = rbase + rg * 16 + g, r1 = r0 + 8;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int d = 8 * j + 2 * q4;
+    if (r0 < a.rows)
+      *reinterpret_cast<__half2*>(a.out + (size_t)r0 * a.out_stride + (size_t)h * kHD + d) =
+          __floats2half2_rn(o[j][0] / l0, o[j][1] / l0);
+    if (r1 < a.rows)
+      *reinterpret_cast<__half2*>(a.out + (size_t)r1 * a.out_stride + (size_t)h * kHD + d) =
+          __floats2half2_rn(o[j][2] / l1, o[j][3] / l1);
+  }
+}
+
 cudaLaunchConfig_t tc_cfg(dim3 grid, dim3 block, uint32_t smem, int pdl, cudaStream_t st, cudaLaunchAttribute* at) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -384,6 +642,12 @@ size_t attn_tc_ws_floats(uint32_t rows, uint32_t n_q, uint32_t n_kv, uint32_t ma
 
 cudaError_t attn_tc_prepare() {
   cudaError_t e = cudaFuncSetAttribute(&attn_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(&attn_prefill_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfTcSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(&attn_prefill_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfTcSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(&attn_prefill_tc_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfTcSmem);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(&attn_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
   if (e == cudaSuccess)
@@ -422,6 +686,16 @@ cudaError_t attn_tc_launch(const AttnArgs& a, int pdl, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t c3 = tc_cfg(dim3(a.n_kv, a.rows), dim3(kHD * G), 0, 1, st, at);
   return cudaLaunchKernelEx(&c3, &attn_tc_combine_kernel, t);
+}
+
+cudaError_t attn_prefill_tc_launch(const AttnArgs& a, int pdl, cudaStream_t st) {
+  if (!attn_tc_applies(a.n_q, a.n_kv, kHD) || a.rows == 0) return cudaErrorInvalidValue;
+  const uint32_t G = a.n_q / a.n_kv, qr = 16 * (4 / G);
+  cudaLaunchAttribute at[1];
+  cudaLaunchConfig_t c = tc_cfg(dim3(a.n_kv, (a.rows + qr - 1) / qr), dim3(128), kPfTcSmem, pdl, st, at);
+  if (G == 1) return cudaLaunchKernelEx(&c, &attn_prefill_tc_kernel<1>, a);
+  if (G == 2) return cudaLaunchKernelEx(&c, &attn_prefill_tc_kernel<2>, a);
+  return cudaLaunchKernelEx(&c, &attn_prefill_tc_kernel<4>, a);
 }
 
 }  // namespace nnz
