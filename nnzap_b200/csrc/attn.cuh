@@ -71,7 +71,9 @@ cudaError_t attn_tc_prepare();
 cudaError_t attn_tc_launch(const AttnArgs& a, int pdl, cudaStream_t st);
 // Causal prefill attention on the tensor cores (same contract as
 // attn_prefill_launch; head_dim 128, G in {1, 2, 4}).
+// Uses a.ws (attn_prefill_tc_ws_floats) for the key splits' partials.
 cudaError_t attn_prefill_tc_launch(const AttnArgs& a, int pdl, cudaStream_t st);
+size_t attn_prefill_tc_ws_floats(uint32_t rows, uint32_t n_q);
 
 // Writes normed+roped k and v of `rows` query rows at their positions
 // (used by chunked prefill, where rows of one chunk share a cache slot and

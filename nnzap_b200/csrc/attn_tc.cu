@@ -134,10 +134,14 @@ struct TcTask {
   size_t off;   // element offset of the chunk's first position in the layer's K/V
 };
 
+// Tasks are numbered chunk-major (all rows' chunk 0, then chunk 1, ...), so
+// the chunks that exist at the current positions are spread evenly over the
+// warps' grid-stride sequences.
 __device__ __forceinline__ bool tc_task(const TcArgs& t, uint32_t task, TcTask& k) {
   const AttnArgs& a = t.a;
-  k.c = task % t.nch;
-  const uint32_t rk = task / t.nch;
+  const uint32_t nrk = a.rows * a.n_kv;
+  k.c = task / nrk;
+  const uint32_t rk = task % nrk;
   k.kvh = rk % a.n_kv;
   k.row = rk / a.n_kv;
   const int seq = clamp_pos(a, k.row, false) + 1;
@@ -357,9 +361,12 @@ __global__ void __launch_bounds__(4 * kHD) attn_tc_combine_kernel(TcArgs t) {
 // ---------------------------------------------------------------------------
 // 4. causal prefill attention on the tensor cores
 // ---------------------------------------------------------------------------
-// One CTA per (kv head, block of query rows): warp w serves query head
-// w % G of the group and 16 consecutive rows (block = 16 * 4 / G rows), so
-// every K/V tile in shared memory feeds all G heads.  Each warp normalises
+// One CTA per (kv head, block of query rows, key split): warp w serves
+// query head w % G of the group and 16 consecutive rows (block = 16 * 4 / G
+// rows), so every K/V tile in shared memory feeds all G heads; the block's
+// causal key range is cut into up to kPfSplits splits of whole 64-key tiles
+// (balancing the long rows against the short ones), each writing partial
+// (m, l, o) records that attn_prefill_combine_kernel merges.  Each warp normalises
 // and rotates its rows' queries (f32) and keeps them as fp16 hi/lo A
 // fragments; S = Q_hi K^T + Q_lo K^T and O += P_hi V + P_lo V accumulate in
 // f32, with the causal mask and the online softmax in registers (FA2
@@ -369,6 +376,7 @@ constexpr int kPfTcKeys = 64;
 constexpr int kPfTcQB = 2 * 16 * kTcRowB;                 // per warp: hi + lo, 16 rows
 constexpr int kPfTcTile = kPfTcKeys * kTcRowB;            // one K or V tile
 constexpr int kPfTcSmem = 4 * kPfTcQB + 2 * 2 * kPfTcTile;
+constexpr int kPfSplits = 4;
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
@@ -401,6 +409,19 @@ __global__ void __launch_bounds__(128) attn_prefill_tc_kernel(AttnArgs a) {
   __syncthreads();
   const int kmax = s_kmax;
   const size_t head_off = ((size_t)s_slot * a.n_kv + kvh) * a.max_ctx * kHD;
+  // this split's key tiles [kb0, kb1)
+  const int ntile = kmax / kPfTcKeys + 1;
+  const int per = (ntile + kPfSplits - 1) / kPfSplits;
+  const int kb0 = blockIdx.z * per, kb1 = min(ntile, kb0 + per);
+  const uint32_t rec = kHD + 2;
+  if (kb0 >= kb1) {
+    // empty split: mark its records so the merge skips them
+    if (lane < 16) {
+      const uint32_t r = rbase + rg * 16 + lane;
+      if (r < a.rows) a.ws[(((size_t)r * a.n_q + h) * kPfSplits + blockIdx.z) * rec] = -INFINITY;
+    }
+    return;
+  }
   auto load_tile = [&](int kb, int stg) {
     const uint32_t kt = smem_u32(kv + stg * 2 * kPfTcTile), vt = kt + kPfTcTile;
     for (int c = threadIdx.x; c < kPfTcKeys * 16; c += 128) {
@@ -417,7 +438,7 @@ __global__ void __launch_bounds__(128) attn_prefill_tc_kernel(AttnArgs a) {
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  load_tile(0, 0);
+  load_tile(kb0, 0);
 
   // queries: RMSNorm over the head, q_norm, RoPE (f32), then fp16 hi/lo rows
   {
@@ -502,14 +523,14 @@ __global__ void __launch_bounds__(128) attn_prefill_tc_kernel(AttnArgs a) {
   for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   const float inv = rsqrtf((float)kHD);
-  const int nkb = kmax / kPfTcKeys + 1;
-  for (int kb = 0; kb < nkb; ++kb) {
-    if (kb + 1 < nkb) load_tile(kb + 1, (kb + 1) & 1);
+  for (int kb = kb0; kb < kb1; ++kb) {
+    const int stg = (kb - kb0) & 1;
+    if (kb + 1 < kb1) load_tile(kb + 1, stg ^ 1);
     else asm volatile("cp.async.commit_group;" ::: "memory");
     asm volatile("cp.async.wait_group 1;" ::: "memory");
     __syncthreads();
     if (kb * kPfTcKeys <= wmax) {
-      const uint32_t kt = smem_u32(kv + (kb & 1) * 2 * kPfTcTile), vt = kt + kPfTcTile;
+      const uint32_t kt = smem_u32(kv + stg * 2 * kPfTcTile), vt = kt + kPfTcTile;
       float sc[8][4];
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
@@ -599,17 +620,47 @@ __global__ void __launch_bounds__(128) attn_prefill_tc_kernel(AttnArgs a) {
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  // partial records [row][head][split]: m, l, unnormalised o
   const uint32_t r0 = rbase + rg * 16 + g, r1 = r0 + 8;
+  float* w0 = a.ws + (((size_t)r0 * a.n_q + h) * kPfSplits + blockIdx.z) * rec;
+  float* w1 = a.ws + (((size_t)r1 * a.n_q + h) * kPfSplits + blockIdx.z) * rec;
+  if (q4 == 0) {
+    if (r0 < a.rows) { w0[0] = m0; w0[1] = l0; }
+    if (r1 < a.rows) { w1[0] = m1; w1[1] = l1; }
+  }
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     const int d = 8 * j + 2 * q4;
-    if (r0 < a.rows)
-      *reinterpret_cast<__half2*>(a.out + (size_t)r0 * a.out_stride + (size_t)h * kHD + d) =
-          __floats2half2_rn(o[j][0] / l0, o[j][1] / l0);
-    if (r1 < a.rows)
-      *reinterpret_cast<__half2*>(a.out + (size_t)r1 * a.out_stride + (size_t)h * kHD + d) =
-          __floats2half2_rn(o[j][2] / l1, o[j][3] / l1);
+    if (r0 < a.rows) *reinterpret_cast<float2*>(w0 + 2 + d) = make_float2(o[j][0], o[j][1]);
+    if (r1 < a.rows) *reinterpret_cast<float2*>(w1 + 2 + d) = make_float2(o[j][2], o[j][3]);
   }
+}
+
+// Merges the kPfSplits partial records of one (row, query head) into the
+// fp16 output; one CTA per (row, head), a thread per element.
+__global__ void __launch_bounds__(kHD) attn_prefill_combine_kernel(AttnArgs a) {
+  pdl_wait();
+  pdl_launch();
+  const uint32_t r = blockIdx.x, h = blockIdx.y, d = threadIdx.x, rec = kHD + 2;
+  const float* base = a.ws + ((size_t)r * a.n_q + h) * kPfSplits * rec;
+  float mv[kPfSplits], lv[kPfSplits], ov[kPfSplits];
+#pragma unroll
+  for (int q = 0; q < kPfSplits; ++q) {
+    mv[q] = __ldcg(base + q * rec);
+    lv[q] = __ldcg(base + q * rec + 1);
+    ov[q] = __ldcg(base + q * rec + 2 + d);
+  }
+  float M = -INFINITY;
+#pragma unroll
+  for (int q = 0; q < kPfSplits; ++q) M = fmaxf(M, mv[q]);
+  float L = 0.f, o = 0.f;
+#pragma unroll
+  for (int q = 0; q < kPfSplits; ++q) {
+    const float w = mv[q] == -INFINITY ? 0.f : expf(mv[q] - M);
+    L = fmaf(w, lv[q], L);
+    o = fmaf(w, ov[q], o);
+  }
+  a.out[(size_t)r * a.out_stride + (size_t)h * kHD + d] = __float2half_rn(o / L);
 }
 
 cudaLaunchConfig_t tc_cfg(dim3 grid, dim3 block, uint32_t smem, int pdl, cudaStream_t st, cudaLaunchAttribute* at) {
@@ -688,14 +739,22 @@ cudaError_t attn_tc_launch(const AttnArgs& a, int pdl, cudaStream_t st) {
   return cudaLaunchKernelEx(&c3, &attn_tc_combine_kernel, t);
 }
 
+size_t attn_prefill_tc_ws_floats(uint32_t rows, uint32_t n_q) {
+  return (size_t)rows * n_q * kPfSplits * (kHD + 2);
+}
+
 cudaError_t attn_prefill_tc_launch(const AttnArgs& a, int pdl, cudaStream_t st) {
-  if (!attn_tc_applies(a.n_q, a.n_kv, kHD) || a.rows == 0) return cudaErrorInvalidValue;
+  if (!attn_tc_applies(a.n_q, a.n_kv, kHD) || a.rows == 0 || !a.ws) return cudaErrorInvalidValue;
   const uint32_t G = a.n_q / a.n_kv, qr = 16 * (4 / G);
   cudaLaunchAttribute at[1];
-  cudaLaunchConfig_t c = tc_cfg(dim3(a.n_kv, (a.rows + qr - 1) / qr), dim3(128), kPfTcSmem, pdl, st, at);
-  if (G == 1) return cudaLaunchKernelEx(&c, &attn_prefill_tc_kernel<1>, a);
-  if (G == 2) return cudaLaunchKernelEx(&c, &attn_prefill_tc_kernel<2>, a);
-  return cudaLaunchKernelEx(&c, &attn_prefill_tc_kernel<4>, a);
+  cudaLaunchConfig_t c = tc_cfg(dim3(a.n_kv, (a.rows + qr - 1) / qr, kPfSplits), dim3(128), kPfTcSmem, pdl, st, at);
+  cudaError_t e;
+  if (G == 1) e = cudaLaunchKernelEx(&c, &attn_prefill_tc_kernel<1>, a);
+  else if (G == 2) e = cudaLaunchKernelEx(&c, &attn_prefill_tc_kernel<2>, a);
+  else e = cudaLaunchKernelEx(&c, &attn_prefill_tc_kernel<4>, a);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t c2 = tc_cfg(dim3(a.rows, a.n_q), dim3(kHD), 0, 1, st, at);
+  return cudaLaunchKernelEx(&c2, &attn_prefill_combine_kernel, a);
 }
 
 }  // namespace nnz

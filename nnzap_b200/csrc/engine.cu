@@ -683,7 +683,7 @@ int enqueue_layer_gemm(nnz_model* m, uint32_t l, uint32_t rows, const int* pos) 
     aa.kc = m->kc + m->kv_layer * l; aa.vc = m->vc + m->kv_layer * l; aa.max_ctx = c.max_context_length;
     aa.pos = pos; aa.slot = m->zeros; aa.rows = rows; aa.n_q = c.num_query_heads; aa.n_kv = c.num_kv_heads;
     aa.eps = c.eps; aa.theta = c.rope_theta; aa.rope_style = c.rope_style; aa.out = m->attn;
-    aa.out_stride = m->qd; aa.err = m->err;
+    aa.out_stride = m->qd; aa.err = m->err; aa.rope_tab = m->rope_tab; aa.ws = m->ws;
     NNZ_CK(attn_prefill_launch(aa, (int)c.head_dim, 0, m->st));
   }
   if ((rc = tp_pre_add(m, rows))) return rc;
@@ -1009,6 +1009,8 @@ int nnz_model_finalize(nnz_model* m) {
     nctr = std::max(nctr, (size_t)rows * c.num_kv_heads);
   }
   wsf = std::max(wsf, qmv_ws_floats(m->lm_rows, H, gs, fmt, 1, c.max_batch, m->num_sms));
+  if (attn_tc_applies(c.num_query_heads, c.num_kv_heads, (int)c.head_dim))
+    wsf = std::max(wsf, attn_prefill_tc_ws_floats(R, c.num_query_heads));
   m->ws_floats = std::max<size_t>(wsf, 1024);
   m->n_counters = std::max<size_t>(nctr, 1024);
   if ((rc = dalloc(m, (void**)&m->ws, m->ws_floats * 4))) return rc;

@@ -222,6 +222,7 @@ struct Ctx {
   int warp, lane;
   // consumer item counter and producer cursor (lane 0 of each warp)
   uint32_t k;
+  const int* spos;                // smem: each row's position this step (read once after EMBED)
   const unsigned long long* wl;   // producer: current weight-stream entry
   unsigned long long wnext;
   bool failed;
@@ -514,15 +515,12 @@ struct AttGeom {
   size_t head_off;
 };
 
-__device__ __forceinline__ AttGeom att_geom(const MegaArgs& a, const PhaseInfo& p, uint32_t u, bool report) {
+__device__ __forceinline__ AttGeom att_geom(const Ctx& c, const PhaseInfo& p, uint32_t u) {
+  const MegaArgs& a = *c.a;
   const uint32_t S = a.att_splits;
   const uint32_t kvh = u % a.n_kv, b = (u / a.n_kv) % a.batch, split = u / (a.n_kv * a.batch);
   AttGeom g;
-  int pos = __ldcg(&a.st->pos[b]);
-  if (pos < 0 || pos >= (int)a.max_ctx) {
-    if (report && threadIdx.x == 0) atomicOr(a.err, ERR_BAD_POS);
-    pos = pos < 0 ? 0 : (int)a.max_ctx - 1;
-  }
+  const int pos = c.spos[b];   // range-checked when read
   const int seq = pos + 1;
   const int per = (seq + (int)S - 1) / (int)S;
   g.pos = pos;
@@ -579,7 +577,7 @@ __device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause
   const int warp = c.warp, lane = c.lane;
 
   stamp(c, p, u, 0);
-  const AttGeom ag = att_geom(a, p, u, true);
+  const AttGeom ag = att_geom(c, p, u);
   const int pos = ag.pos, t0 = ag.t0, ncache = ag.ncache, nblk = ag.nblk;
   const bool own_new = ag.own_new;
   const size_t head_off = ag.head_off;
@@ -805,6 +803,8 @@ __global__ void __launch_bounds__(kQmvThreads) mega_kernel(const __grid_constant
     for (uint32_t s = 0; s < a.nslot; ++s) prod_issue(c, s);
   }
   uint32_t ause[kAttStages] = {0, 0};
+  __shared__ int s_pos[kBatchChunk];
+  c.spos = s_pos;
   const uint32_t last = 1 + 5 * a.L;
   for (uint32_t ph = 0; ph <= last; ++ph) {
     const PhaseInfo p = phase_at(c, ph);
@@ -838,7 +838,7 @@ __global__ void __launch_bounds__(kQmvThreads) mega_kernel(const __grid_constant
           // shared-memory view is dead after its last unit's final sync)
           const PhaseInfo pa = phase_at(c, ph + 1);
           if (c.cta < pa.units && threadIdx.x == 0) {
-            const AttGeom ag = att_geom(a, pa, c.cta, false);
+            const AttGeom ag = att_geom(c, pa, c.cta);
             for (int blk = 0; blk < ag.nblk && blk < kAttStages; ++blk) att_issue<HD>(c, ag, blk);
           }
         }
@@ -856,6 +856,18 @@ __global__ void __launch_bounds__(kQmvThreads) mega_kernel(const __grid_constant
       a.prof[2 * (2 + 5 * a.L) + 64 + (ph - 6) * 1024 + c.cta] = t;
     }
     if (ph < last) grid_sync(a.bar, c.G, gen, a.err);
+    if (ph == 0) {
+      // positions were advanced by the embedding phase; constant from here on
+      if (threadIdx.x < a.batch) {
+        int pos = __ldcg(&a.st->pos[threadIdx.x]);
+        if (pos < 0 || pos >= (int)a.max_ctx) {
+          if (c.cta == 0) atomicOr(a.err, ERR_BAD_POS);
+          pos = pos < 0 ? 0 : (int)a.max_ctx - 1;
+        }
+        s_pos[threadIdx.x] = pos;
+      }
+      __syncthreads();
+    }
     if (a.prof && c.cta == 0 && threadIdx.x == 0) {
       unsigned long long t;
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
