@@ -8,7 +8,10 @@ from __future__ import annotations
 import ctypes as C
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libnnz_b200.so"
+import os
+
+# NNZ_LIB_PATH selects another build of the same library (A/B timing of variants)
+LIB_PATH = Path(os.environ.get("NNZ_LIB_PATH") or Path(__file__).resolve().parent / "_lib" / "libnnz_b200.so")
 
 NNZ_OK, NNZ_EINVAL, NNZ_ECUDA, NNZ_ENOMEM, NNZ_ETIMEDOUT = 0, -1, -2, -3, -4
 NNZ_ENOTFOUND, NNZ_ESTATE, NNZ_EDEVICE, NNZ_ENCCL = -5, -6, -7, -8

@@ -27,6 +27,8 @@
 #include <cuda_runtime.h>
 
 #include "mega.cuh"
+
+#include <stdlib.h>
 #include "rope_dev.cuh"
 
 namespace nnz {
@@ -279,25 +281,32 @@ __device__ __forceinline__ void stage_attn(const Ctx& c, uint32_t K0, uint32_t K
     const uint32_t h = k / a.hd, d = k % a.hd, kvh = h / G, hg = h % G;
     const float* base = a.att_ws + (((size_t)(b * a.n_kv + kvh) * S) * G + hg) * rec;
     const size_t sstride = (size_t)G * rec;
-    float mv[kMaxAttSplits], lv[kMaxAttSplits], ov[kMaxAttSplits];
+    // every load issued before any is used; the (m, l) pairs and the
+    // element's partial outputs of all S splits
+    float w[kMaxAttSplits], ov[kMaxAttSplits];
+    float L = 0.f;
+    {
+      float lv[kMaxAttSplits];
 #pragma unroll
-    for (int q = 0; q < kMaxAttSplits; ++q) {
-      const bool ok = (uint32_t)q < S;
-      const float* r = base + q * sstride;
-      mv[q] = ok ? __ldcg(r) : -INFINITY;
-      lv[q] = ok ? __ldcg(r + 1) : 0.f;
-      ov[q] = ok ? __ldcg(r + 2 + d) : 0.f;
+      for (int q = 0; q < kMaxAttSplits; ++q) {
+        const bool ok = (uint32_t)q < S;
+        const float* r = base + q * sstride;
+        w[q] = ok ? __ldcg(r) : -INFINITY;
+        lv[q] = ok ? __ldcg(r + 1) : 0.f;
+        ov[q] = ok ? __ldcg(r + 2 + d) : 0.f;
+      }
+      float M = -INFINITY;
+#pragma unroll
+      for (int q = 0; q < kMaxAttSplits; ++q) M = fmaxf(M, w[q]);
+#pragma unroll
+      for (int q = 0; q < kMaxAttSplits; ++q) {
+        w[q] = w[q] == -INFINITY ? 0.f : expf(w[q] - M);
+        L = fmaf(w[q], lv[q], L);
+      }
     }
-    float M = -INFINITY;
+    float o = 0.f;
 #pragma unroll
-    for (int q = 0; q < kMaxAttSplits; ++q) M = fmaxf(M, mv[q]);
-    float L = 0.f, o = 0.f;
-#pragma unroll
-    for (int q = 0; q < kMaxAttSplits; ++q) {
-      const float w = mv[q] == -INFINITY ? 0.f : expf(mv[q] - M);
-      L = fmaf(w, lv[q], L);
-      o = fmaf(w, ov[q], o);
-    }
+    for (int q = 0; q < kMaxAttSplits; ++q) o = fmaf(w[q], ov[q], o);
     xs[j] = __float2half_rn(o / L);
   }
 }
@@ -946,7 +955,8 @@ bool mega_plan(MegaArgs& a, int fmt, int bf16s, int device, uint32_t* grid, uint
     a.ks_gu = pick(a.I, a.H);
     a.ks_dn = pick(a.H, a.I);
     // splits of at most 64 positions (two streamed blocks), up to 16
-    const uint32_t sp = (a.max_ctx + 63) / 64;
+    uint32_t sp = (a.max_ctx + 63) / 64;
+    if (const char* e = getenv("NNZ_ATT_SPLITS")) sp = (uint32_t)atoi(e);   // tuning override
     a.att_splits = sp < 1 ? 1 : sp > (uint32_t)kMaxAttSplits ? (uint32_t)kMaxAttSplits : sp;
     for (uint32_t ns = kMaxSlots; ns >= 2; --ns) {
       a.nslot = ns;
