@@ -366,13 +366,18 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
 
   // prologue: this unit's slice of x (the LM head's x is the same for all
   // of a CTA's units, so the caller runs it once)
+  bool fused = false;
   if (!prologue) {
   } else if (p.type == PH_QKV || p.type == PH_GU || p.type == PH_LM) {
     const uint32_t v = p.type == PH_QKV ? 2 * p.layer : p.type == PH_GU ? 2 * p.layer + 1 : 2 * a.L;
     const float* nw = p.type == PH_QKV ? lptr(a, a.l0.attn_norm, p.layer)
                     : p.type == PH_GU ? lptr(a, a.l0.ffn_norm, p.layer) : a.fnorm;
     const float* res = resv(a, v);
-    if (bc * a.H <= 2048u) {
+    if (bc == 1 && gs == 128 && a.H <= 2048u && a.H % 128 == 0) {
+      // one row, 128-wide groups: normalise and quantise from registers
+      norm_quant_row128<NT>(res, a.H, nw, a.eps, G0, ng, a.bf16r != 0, rms, xf, gsx, gsum, gsq);
+      fused = true;
+    } else if (bc * a.H <= 2048u) {
       stage_norm_fast(res, a.H, a.H, nw, a.eps, K0, Kr, bc, a.bf16r != 0, rms, xs);
     } else {
       block_rms(res, a.H, a.H, bc, a.eps, rms);
@@ -384,7 +389,7 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
     stage_silu(c, K0, Kr, bc, xs);
   }
   stamp(c, p, u, 1);
-  if (prologue) quantize_xs<NT>(xs, Kr, bc, ng, gs, xf, gsx, gsum, gsq, false);
+  if (prologue && !fused) quantize_xs<NT>(xs, Kr, bc, ng, gs, xf, gsx, gsum, gsq, false);
   stamp(c, p, u, 2);
 
   float y[SUB][NT][16];
