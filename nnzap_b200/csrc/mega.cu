@@ -337,6 +337,98 @@ __device__ void stage_silu(const Ctx& c, uint32_t K0, uint32_t Kr, uint32_t bc, 
   }
 }
 
+// One row, 128-wide groups: the DN / O prologues with the quantisation done
+// from registers (warp gl takes group gl of the unit, lane l its columns
+// 4l..4l+3), the same values stage_silu / stage_attn + quantize_xs produce.
+template <int NT>
+__device__ __forceinline__ void silu_quant_row128(const Ctx& c, uint32_t K0, uint32_t ng, uint8_t* xf, float* gsx,
+                                                  float* gsum, int* gsq) {
+  const MegaArgs& a = *c.a;
+  for (uint32_t gl = c.warp; gl < ng; gl += kQmvWarps) {
+    const uint32_t k = K0 + gl * 128 + c.lane * 4;
+    const float4 g4 = __ldcg(reinterpret_cast<const float4*>(a.gu_acc + k));
+    const float4 u4 = __ldcg(reinterpret_cast<const float4*>(a.gu_acc + a.I + k));
+    const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
+    float x[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float v = gv[i] / (1.0f + expf(-gv[i])) * uv[i];
+      if (a.bf16r) v = bf16_trunc(v);
+      x[i] = __half2float(__float2half_rn(v));
+    }
+    quant_group_row0<NT>(x, gl, c.lane, xf, gsx, gsum, gsq);
+  }
+  __syncthreads();
+}
+
+// O prologue for one row, 128-wide groups = heads (head_dim 128): group gl
+// of the unit is head K0 / 128 + gl.  The four warps share each group's
+// splits (warp w merges splits w, w + 4, ...; more loads in flight per CTA),
+// combine their partial (max, sum, output) through shared memory, and the
+// group's owner warp quantises.
+template <int NT>
+__device__ __forceinline__ void attn_quant_row128(const Ctx& c, uint32_t K0, uint32_t ng, uint8_t* xf, float* gsx,
+                                                  float* gsum, int* gsq, float* scratch) {
+  const MegaArgs& a = *c.a;
+  const uint32_t G = a.n_q / a.n_kv, S = a.att_splits, rec = a.hd + 2;
+  constexpr int kPer = (kMaxAttSplits + kQmvWarps - 1) / kQmvWarps;
+  for (uint32_t gl = 0; gl < ng; ++gl) {
+    const uint32_t h = K0 / 128 + gl, kvh = h / G, hg = h % G;
+    const float* base = a.att_ws + ((size_t)kvh * S * G + hg) * rec;
+    float mv[kPer], lv[kPer];
+    float2 o0[kPer], o1[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const uint32_t q = c.warp + kQmvWarps * j;
+      const bool ok = q < S;
+      const float* r = base + (size_t)q * G * rec;
+      mv[j] = ok ? __ldcg(r) : -INFINITY;
+      lv[j] = ok ? __ldcg(r + 1) : 0.f;
+      o0[j] = ok ? __ldcg(reinterpret_cast<const float2*>(r + 2 + c.lane * 4)) : make_float2(0.f, 0.f);
+      o1[j] = ok ? __ldcg(reinterpret_cast<const float2*>(r + 4 + c.lane * 4)) : make_float2(0.f, 0.f);
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) M = fmaxf(M, mv[j]);
+    float L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const float w = mv[j] == -INFINITY ? 0.f : expf(mv[j] - M);
+      L = fmaf(w, lv[j], L);
+      o[0] = fmaf(w, o0[j].x, o[0]); o[1] = fmaf(w, o0[j].y, o[1]);
+      o[2] = fmaf(w, o1[j].x, o[2]); o[3] = fmaf(w, o1[j].y, o[3]);
+    }
+    // scratch: [warp][lane][4] outputs, then [warp][2] (max, sum)
+    float* so = scratch + (c.warp * 32 + c.lane) * 4;
+    so[0] = o[0]; so[1] = o[1]; so[2] = o[2]; so[3] = o[3];
+    if (c.lane == 0) {
+      scratch[kQmvWarps * 128 + 2 * c.warp] = M;
+      scratch[kQmvWarps * 128 + 2 * c.warp + 1] = L;
+    }
+    __syncthreads();
+    if ((uint32_t)c.warp == gl % kQmvWarps) {
+      float Mt = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kQmvWarps; ++w) Mt = fmaxf(Mt, scratch[kQmvWarps * 128 + 2 * w]);
+      float Lt = 0.f, ot[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int w = 0; w < kQmvWarps; ++w) {
+        const float mw = scratch[kQmvWarps * 128 + 2 * w];
+        const float f = mw == -INFINITY ? 0.f : expf(mw - Mt);
+        Lt = fmaf(f, scratch[kQmvWarps * 128 + 2 * w + 1], Lt);
+        const float* sw = scratch + (w * 32 + c.lane) * 4;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ot[i] = fmaf(f, sw[i], ot[i]);
+      }
+      float x[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x[i] = __half2float(__float2half_rn(ot[i] / Lt));
+      quant_group_row0<NT>(x, gl, c.lane, xf, gsx, gsum, gsq);
+    }
+    __syncthreads();
+  }
+}
+
 // ---- one matvec work unit ------------------------------------------------------
 __device__ __forceinline__ void stamp(const Ctx& c, const PhaseInfo& p, uint32_t u, int i) {
   const MegaArgs& a = *c.a;
@@ -384,9 +476,19 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
       stage_norm(res, a.H, nw, rms, K0, Kr, bc, a.bf16r != 0, xs);
     }
   } else if (p.type == PH_O) {
-    stage_attn(c, K0, Kr, bc, xs);
+    if (bc == 1 && gs == 128 && a.hd == 128) {
+      attn_quant_row128<NT>(c, K0, ng, xf, gsx, gsum, gsq, red);
+      fused = true;
+    } else {
+      stage_attn(c, K0, Kr, bc, xs);
+    }
   } else {
-    stage_silu(c, K0, Kr, bc, xs);
+    if (bc == 1 && gs == 128) {
+      silu_quant_row128<NT>(c, K0, ng, xf, gsx, gsum, gsq);
+      fused = true;
+    } else {
+      stage_silu(c, K0, Kr, bc, xs);
+    }
   }
   stamp(c, p, u, 1);
   if (prologue && !fused) quantize_xs<NT>(xs, Kr, bc, ng, gs, xf, gsx, gsum, gsq, false);

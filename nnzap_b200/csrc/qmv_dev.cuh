@@ -138,6 +138,48 @@ __device__ __forceinline__ void stage_norm_fast(const float* res, uint32_t strid
   }
 }
 
+// Quantise one 128-wide scale group of row 0 held by a warp, 4 consecutive
+// fp16-representable values per lane (lane l: group columns 4l..4l+3), into
+// the int8 hi/lo B fragments and the group's gsx / gsum / gsq -- the same
+// arithmetic as quantize_xs.  Writes only batch-column-0 words of xf.
+template <int NT>
+__device__ __forceinline__ void quant_group_row0(const float (&x)[4], uint32_t gl, int lane, uint8_t* xf,
+                                                 float* gsx, float* gsum, int* gsq) {
+  float amax = 0.f, sumx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    amax = fmaxf(amax, fabsf(x[i]));
+    sumx += x[i];
+  }
+  amax = warp_max(amax);
+  sumx = warp_sum(sumx);
+  const int E = (amax > 0.f) ? (int)((__float_as_uint(amax) >> 23) & 0xFFu) - 126 : 0;
+  const float up = __uint_as_float((uint32_t)(127 + 14 - E) << 23);
+  uint32_t hiw = 0, low = 0;
+  int qsum = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int q = (amax > 0.f) ? __float2int_rn(x[i] * up) : 0;
+    qsum += q;
+    const int lo = ((q + 128) & 255) - 128;
+    const int hi = (q - lo) >> 8;
+    hiw |= ((uint32_t)hi & 0xFFu) << (8 * i);
+    low |= ((uint32_t)lo & 0xFFu) << (8 * i);
+  }
+  qsum = warp_sum_int(qsum);
+  // lane's 4 columns = bytes 0-3 of one fragment word: chunk lane / 8,
+  // k-register (lane >> 2) & 1, fragment lane (lane & 3) (hi) / 4 + (lane & 3) (lo)
+  const uint32_t c = gl * (128 / kChunk) + lane / 8;
+  uint8_t* base = xf + ((size_t)(c * NT) * 32) * 8 + ((lane >> 2) & 1) * 4;
+  *reinterpret_cast<uint32_t*>(base + (size_t)(lane & 3) * 8) = hiw;
+  *reinterpret_cast<uint32_t*>(base + (size_t)(4 + (lane & 3)) * 8) = low;
+  if (lane == 0) {
+    gsx[gl * kBatchChunk] = (amax > 0.f) ? __uint_as_float((uint32_t)(127 + E - 14) << 23) : 0.f;
+    gsum[gl * kBatchChunk] = sumx;
+    gsq[gl * kBatchChunk] = qsum;
+  }
+}
+
 // Fused RMSNorm + activation quantisation for one row (bc = 1), group size
 // 128 and K <= 2048: thread t holds columns 4 (t + 128 u), so warp w's item
 // u is the whole scale group w + 4 u.  Each warp quantises, straight from
@@ -175,41 +217,12 @@ __device__ __forceinline__ void norm_quant_row128(const float* res, uint32_t K, 
     const uint32_t g = warp + 4 * u;
     if (g < G0 || g >= G0 + ng || threadIdx.x + u * kQmvThreads >= q4) continue;   // warp-uniform
     float x[4] = {v[u].x * rr * w[u].x, v[u].y * rr * w[u].y, v[u].z * rr * w[u].z, v[u].w * rr * w[u].w};
-    float amax = 0.f, sumx = 0.f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       if (bf16r) x[i] = bf16_trunc(x[i]);
       x[i] = __half2float(__float2half_rn(x[i]));
-      amax = fmaxf(amax, fabsf(x[i]));
-      sumx += x[i];
     }
-    amax = warp_max(amax);
-    sumx = warp_sum(sumx);
-    const int E = (amax > 0.f) ? (int)((__float_as_uint(amax) >> 23) & 0xFFu) - 126 : 0;
-    const float up = __uint_as_float((uint32_t)(127 + 14 - E) << 23);
-    uint32_t hiw = 0, low = 0;
-    int qsum = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int q = (amax > 0.f) ? __float2int_rn(x[i] * up) : 0;
-      qsum += q;
-      const int lo = ((q + 128) & 255) - 128;
-      const int hi = (q - lo) >> 8;
-      hiw |= ((uint32_t)hi & 0xFFu) << (8 * i);
-      low |= ((uint32_t)lo & 0xFFu) << (8 * i);
-    }
-    qsum = warp_sum_int(qsum);
-    // lane's 4 columns = bytes 0-3 of one fragment word: chunk c = lane / 8,
-    // k-register (lane >> 2) & 1, fragment lane (lane & 3) (hi) / 4 + (lane & 3) (lo)
-    const uint32_t gl = g - G0, c = gl * (128 / kChunk) + lane / 8;
-    uint8_t* base = xf + ((size_t)(c * NT) * 32) * 8 + ((lane >> 2) & 1) * 4;
-    *reinterpret_cast<uint32_t*>(base + (size_t)(lane & 3) * 8) = hiw;
-    *reinterpret_cast<uint32_t*>(base + (size_t)(4 + (lane & 3)) * 8) = low;
-    if (lane == 0) {
-      gsx[gl * kBatchChunk] = (amax > 0.f) ? __uint_as_float((uint32_t)(127 + E - 14) << 23) : 0.f;
-      gsum[gl * kBatchChunk] = sumx;
-      gsq[gl * kBatchChunk] = qsum;
-    }
+    quant_group_row0<NT>(x, g - G0, lane, xf, gsx, gsum, gsq);
   }
   __syncthreads();
 }
