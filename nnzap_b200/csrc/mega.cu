@@ -492,6 +492,17 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
   }
   stamp(c, p, u, 1);
   if (prologue && !fused) quantize_xs<NT>(xs, Kr, bc, ng, gs, xf, gsx, gsum, gsq, false);
+  // the split-0 O / down unit adds the previous residual once: fetch it now
+  // (into the dead staging area) so the load overlaps the MMAs
+  float* rpre = reinterpret_cast<float*>(xs);
+  const bool add_res = (p.type == PH_O || p.type == PH_DN) && split == 0;
+  if (add_res) {
+    const uint32_t vin = p.type == PH_O ? 2 * p.layer : 2 * p.layer + 1;
+    for (uint32_t i = threadIdx.x; i < kTileRows * bc; i += blockDim.x) {
+      const uint32_t rl = i / bc, b = i % bc, row = tile * kTileRows + rl;
+      rpre[i] = row < p.M ? __ldcg(&resv(a, vin)[(size_t)b * a.H + row]) : 0.f;
+    }
+  }
   stamp(c, p, u, 2);
 
   float y[SUB][NT][16];
@@ -569,7 +580,7 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
         case PH_GU: atomicAdd(&a.gu_acc[((size_t)b * 2 + s) * a.I + row], v); break;
         default: {   // O / DN: residual versions
           const uint32_t vin = p.type == PH_O ? 2 * p.layer : 2 * p.layer + 1;
-          if (split == 0) v += __ldcg(&resv(a, vin)[(size_t)b * a.H + row]);
+          if (add_res) v += rpre[i];
           atomicAdd(&resv(a, vin + 1)[(size_t)b * a.H + row], v);
         }
       }
