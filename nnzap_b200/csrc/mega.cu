@@ -41,7 +41,7 @@ constexpr int kMaxSlots = 4;
 constexpr int kAttBlk = 32;
 constexpr int kAttStages = 2;
 constexpr int kAttMaxG = 8;
-constexpr int kMaxAttSplits = 16;
+constexpr int kMaxAttSplits = 32;
 constexpr int kMaxHeadsPerUnit = 32;
 
 struct PhaseInfo {
@@ -93,7 +93,7 @@ __host__ __device__ inline void unit_range(const PhaseInfo& p, uint32_t u, uint3
 }
 
 struct MegaSmem {
-  uint32_t tmpl, bars, abars, ring, slot_bytes, u, xs, xf, gsx, gsum, gsq, red, rms, flag, mw,
+  uint32_t tmpl, bars, abars, ring, slot_bytes, u, xs, xf, gsx, gsum, gsq, red, rms, flag,
       kring, vring, qs, knew, vnew, ss, stat, tok, total, kr_max, ng_max, bcm, nt;
 };
 
@@ -136,8 +136,6 @@ __host__ __device__ inline MegaSmem mega_layout(const MegaArgs& a, int fmt) {
   s.flag = q; q += 16;
   s.tok = q; q += kBatchChunk * 4;
   // full residual rows for the one-round-trip RMSNorm (small batches only)
-  // attention merge weights [b][head in range][split] (m, l -> weight)
-  s.mw = q; q += s.bcm * kMaxHeadsPerUnit * kMaxAttSplits * 2 * 4;
   // attention view of the union
   uint32_t t = o;
   s.kring = t; t += kAttStages * kAttBlk * a.hd * 2;
@@ -274,6 +272,7 @@ __device__ __forceinline__ void grid_zero(float* p, size_t n, const Ctx& c) {
 // the S (m, l) pairs of the element's head and its S partial outputs --
 // before using any, so the merge costs one round trip per pass.
 __device__ __forceinline__ void stage_attn(const Ctx& c, uint32_t K0, uint32_t Kr, uint32_t bc, __half* xs) {
+  constexpr int kB = 8;   // splits per batch of loads
   const MegaArgs& a = *c.a;
   const uint32_t G = a.n_q / a.n_kv, S = a.att_splits, rec = a.hd + 2;
   for (uint32_t j = threadIdx.x; j < bc * Kr; j += blockDim.x) {
@@ -281,32 +280,31 @@ __device__ __forceinline__ void stage_attn(const Ctx& c, uint32_t K0, uint32_t K
     const uint32_t h = k / a.hd, d = k % a.hd, kvh = h / G, hg = h % G;
     const float* base = a.att_ws + (((size_t)(b * a.n_kv + kvh) * S) * G + hg) * rec;
     const size_t sstride = (size_t)G * rec;
-    // every load issued before any is used; the (m, l) pairs and the
-    // element's partial outputs of all S splits
-    float w[kMaxAttSplits], ov[kMaxAttSplits];
-    float L = 0.f;
-    {
-      float lv[kMaxAttSplits];
+    float M = -INFINITY, L = 0.f, o = 0.f;
+    for (uint32_t q0 = 0; q0 < S; q0 += kB) {
+      float mv[kB], lv[kB], ov[kB];
 #pragma unroll
-      for (int q = 0; q < kMaxAttSplits; ++q) {
-        const bool ok = (uint32_t)q < S;
-        const float* r = base + q * sstride;
-        w[q] = ok ? __ldcg(r) : -INFINITY;
+      for (int q = 0; q < kB; ++q) {
+        const bool ok = q0 + q < S;
+        const float* r = base + (q0 + q) * sstride;
+        mv[q] = ok ? __ldcg(r) : -INFINITY;
         lv[q] = ok ? __ldcg(r + 1) : 0.f;
         ov[q] = ok ? __ldcg(r + 2 + d) : 0.f;
       }
-      float M = -INFINITY;
+      float nm = M;
 #pragma unroll
-      for (int q = 0; q < kMaxAttSplits; ++q) M = fmaxf(M, w[q]);
+      for (int q = 0; q < kB; ++q) nm = fmaxf(nm, mv[q]);
+      const float al = M == -INFINITY ? 0.f : expf(M - nm);
+      L *= al;
+      o *= al;
 #pragma unroll
-      for (int q = 0; q < kMaxAttSplits; ++q) {
-        w[q] = w[q] == -INFINITY ? 0.f : expf(w[q] - M);
-        L = fmaf(w[q], lv[q], L);
+      for (int q = 0; q < kB; ++q) {
+        const float w = mv[q] == -INFINITY ? 0.f : expf(mv[q] - nm);
+        L = fmaf(w, lv[q], L);
+        o = fmaf(w, ov[q], o);
       }
+      M = nm;
     }
-    float o = 0.f;
-#pragma unroll
-    for (int q = 0; q < kMaxAttSplits; ++q) o = fmaf(w[q], ov[q], o);
     xs[j] = __float2half_rn(o / L);
   }
 }
@@ -1072,7 +1070,9 @@ bool mega_plan(MegaArgs& a, int fmt, int bf16s, int device, uint32_t* grid, uint
     a.ks_o = pick(a.H, qd);
     a.ks_gu = pick(a.I, a.H);
     a.ks_dn = pick(a.H, a.I);
-    // splits of at most 64 positions (two streamed blocks), up to 16
+    // attention splits
+    // splits of up to 64 positions (two streamed blocks), at most 32: one
+    // block per split moves the cost into the O phase's merge
     uint32_t sp = (a.max_ctx + 63) / 64;
     if (const char* e = getenv("NNZ_ATT_SPLITS")) sp = (uint32_t)atoi(e);   // tuning override
     a.att_splits = sp < 1 ? 1 : sp > (uint32_t)kMaxAttSplits ? (uint32_t)kMaxAttSplits : sp;
