@@ -170,6 +170,14 @@ class Model:
     def load_weights(self, tensors: Iterable) -> None:
         for name, arr in tensors:
             self.load_tensor(name, arr)
+        self.finalize()
+
+    def load_safetensors(self, paths) -> None:
+        """loadWeights from safetensors shard files (model.zig:196-242)."""
+        from .safetensors import load_safetensors
+        load_safetensors(self, [paths] if isinstance(paths, (str, bytes)) or hasattr(paths, "open") else paths)
+
+    def finalize(self) -> None:
         check(lib().nnz_model_finalize(self._h))
         self._finalized = True
 
