@@ -88,6 +88,15 @@ typedef struct nnz_generate_opts {
   uint32_t* output_tokens;       /* capacity max_new */
   uint32_t max_new;
   uint64_t* per_token_ns;        /* optional [max_new]: GPU time per decode step */
+  /* SamplingParams (transformer.zig:3655-3660): temperature 0 = greedy.
+   * With temperature > 0 every generated token is drawn on the device
+   * (sampleToken, transformer.zig:3833-3869: temperature, top-k, top-p,
+   * inverse CDF) with uniforms[i] in [0, 1) for the i-th token, drawn by
+   * the host's generator (the reference's DefaultPrng(seed)). */
+  float temperature;
+  uint32_t top_k;                /* 0 = off */
+  float top_p;                   /* 1 = off */
+  const float* uniforms;         /* [max_new], required when temperature > 0 */
 } nnz_generate_opts;
 
 typedef struct nnz_generate_result {
@@ -177,6 +186,13 @@ int nnz_unpack_weights(int fmt, const void* packed, uint32_t M, uint32_t K, uint
 int nnz_shard_weights(int fmt, int axis, const void* weight, const uint16_t* scales,
                       const uint16_t* biases, uint32_t M, uint32_t K, uint32_t gs, uint32_t lo,
                       uint32_t hi, void* weight_out, uint16_t* scales_out, uint16_t* biases_out);
+
+/* sampleToken (transformer.zig:3833-3869) on device logits: rows x n f32
+ * (row stride `stride`, modified in place like the reference), one uniform
+ * draw per row (device pointer); tokens_out (device, [rows]).  temperature
+ * > 0, 0 < top_p <= 1, top_k 0 = off. */
+int nnz_sample(float* logits, uint32_t rows, uint32_t n, uint32_t stride, float temperature, uint32_t top_k,
+               float top_p, const float* uniforms, uint32_t* tokens_out, void* stream);
 
 /* ---- tensor parallelism (NCCL over NVLink; replaces nothing in the
  * reference, which is single-device) ------------------------------------ */

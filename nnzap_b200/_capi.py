@@ -45,7 +45,8 @@ class NnzGenerateOpts(C.Structure):
     _fields_ = [("prompt_ids", C.POINTER(C.c_uint32)), ("n_prompt", C.c_uint32),
                 ("eos_ids", C.POINTER(C.c_uint32)), ("n_eos", C.c_uint32),
                 ("output_tokens", C.POINTER(C.c_uint32)), ("max_new", C.c_uint32),
-                ("per_token_ns", C.POINTER(C.c_uint64))]
+                ("per_token_ns", C.POINTER(C.c_uint64)), ("temperature", C.c_float),
+                ("top_k", C.c_uint32), ("top_p", C.c_float), ("uniforms", C.POINTER(C.c_float))]
 
 
 class NnzGenerateResult(C.Structure):
@@ -68,6 +69,7 @@ SIGNATURES = [
     ("nnz_model_vocab_shard", U32, [P]),
     ("nnz_shard_weights", I32, [I32, I32, P, P, P, U32, U32, U32, U32, U32, P, P, P]),
     ("nnz_tp_unique_id", I32, [P, SZ]),
+    ("nnz_sample", I32, [P, U32, U32, U32, F32, U32, F32, P, P, P]),
     ("nnz_tp_init", I32, [P, P, SZ]),
     ("nnz_forward_decode", I32, [P, P, P, U32, P, P]),
     ("nnz_prefill", I32, [P, P, U32, P, P]),

@@ -218,6 +218,7 @@ struct nnz_model {
   DecodeState* state = nullptr;
   uint32_t* seq = nullptr;
   uint32_t* prompt = nullptr;
+  float* uniforms = nullptr;           // [max_context] sampling draws of one generate call
   int* iota = nullptr;
   int* zeros = nullptr;
   size_t dev_bytes = 0;
@@ -1019,6 +1020,7 @@ int nnz_model_finalize(nnz_model* m) {
   if ((rc = dalloc(m, (void**)&m->state, sizeof(DecodeState)))) return rc;
   if ((rc = dalloc(m, (void**)&m->seq, (size_t)m->slots * c.max_context_length * 4))) return rc;
   if ((rc = dalloc(m, (void**)&m->prompt, (size_t)c.max_context_length * 4))) return rc;
+  if ((rc = dalloc(m, (void**)&m->uniforms, (size_t)c.max_context_length * 4))) return rc;
   if ((rc = dalloc(m, (void**)&m->iota, (size_t)c.max_context_length * 4))) return rc;
   if ((rc = dalloc(m, (void**)&m->zeros, (size_t)R * 4))) return rc;
   NNZ_CK(cudaMemset(m->counters, 0, m->n_counters * 4));
@@ -1100,6 +1102,20 @@ int nnz_shard_weights(int fmt, int axis, const void* weight, const uint16_t* sca
                       uint16_t* scales_out, uint16_t* biases_out) {
   if (shard_host(fmt, axis, weight, scales, biases, M, K, gs, lo, hi, weight_out, scales_out, biases_out))
     return fail(NNZ_EINVAL, "nnz_shard_weights: invalid arguments");
+  return NNZ_OK;
+}
+
+int nnz_sample(float* logits, uint32_t rows, uint32_t n, uint32_t stride, float temperature, uint32_t top_k,
+               float top_p, const float* uniforms, uint32_t* tokens_out, void* stream) {
+  if (!logits || !uniforms || !tokens_out || rows == 0 || n == 0 || stride < n)
+    return fail(NNZ_EINVAL, "nnz_sample: bad arguments");
+  DevWs* w;
+  int rc = get_ws(&w);
+  if (rc) return rc;
+  // the argmax slots the kernel also writes land in the shared scratch
+  if ((size_t)rows * 2 > w->ws_floats) return fail(NNZ_EINVAL, "nnz_sample: too many rows");
+  NNZ_CK(sample_launch(logits, rows, n, stride, temperature, top_k, top_p, uniforms,
+                       reinterpret_cast<unsigned long long*>(w->ws), tokens_out, (cudaStream_t)stream));
   return NNZ_OK;
 }
 
@@ -1190,6 +1206,10 @@ int nnz_generate(nnz_model* m, const nnz_generate_opts* o, nnz_generate_result* 
     return fail(NNZ_EINVAL, "prompt length / max_new out of range");
   for (uint32_t i = 0; i < o->n_prompt; ++i)
     if (o->prompt_ids[i] >= m->c.vocab_size) return fail(NNZ_EINVAL, "token id >= vocab_size");
+  const bool sample = o->temperature > 0.f;
+  if (sample && (!o->uniforms || !(o->top_p > 0.f) || o->top_p > 1.f))
+    return fail(NNZ_EINVAL, "sampling needs uniforms[max_new] and 0 < top_p <= 1");
+  if (sample && m->tp > 1) return fail(NNZ_EINVAL, "sampling with tensor parallelism is not supported");
   NNZ_CK(cudaSetDevice(m->device));
   const uint32_t n = o->n_prompt;
   // the reference stops when position reaches max_context_length (transformer.zig:3993)
@@ -1203,14 +1223,23 @@ int nnz_generate(nnz_model* m, const nnz_generate_opts* o, nnz_generate_result* 
   NNZ_CK(cudaMemsetAsync(m->state, 0, sizeof(DecodeState), m->st));
   NNZ_CK(cudaMemcpyAsync(m->prompt, o->prompt_ids, (size_t)n * 4, cudaMemcpyHostToDevice, m->st));
   NNZ_CK(cudaMemcpyAsync(m->seq, o->prompt_ids, (size_t)n * 4, cudaMemcpyHostToDevice, m->st));
+  if (sample)
+    NNZ_CK(cudaMemcpyAsync(m->uniforms, o->uniforms, (size_t)std::min<uint32_t>(o->max_new, m->c.max_context_length) * 4,
+                           cudaMemcpyHostToDevice, m->st));
   NNZ_CK(cudaEventRecord(m->events[0], m->st));
-  if ((rc = enqueue_prefill(m, n, false))) return rc;
+  if ((rc = enqueue_prefill(m, n, sample))) return rc;
+  if (sample)   // the first generated token comes from the prompt's last logits
+    NNZ_CK(sample_launch(m->logits, 1, m->lm_rows, m->lm_rows, o->temperature, o->top_k, o->top_p, m->uniforms,
+                         m->state->argmax, nullptr, m->st));
   const int p = (int)n - 1;
   NNZ_CK(cudaMemcpyAsync(m->state->pos, &p, 4, cudaMemcpyHostToDevice, m->st));
   if ((rc = set_advance(m, 1))) return rc;
   NNZ_CK(cudaEventRecord(m->events[1], m->st));
   for (uint32_t i = 0; i < steps; ++i) {
-    if ((rc = run_step(m, 1, false))) return rc;
+    if ((rc = run_step(m, 1, sample))) return rc;
+    if (sample && i + 1 < steps)
+      NNZ_CK(sample_launch(m->logits, 1, m->lm_rows, m->lm_rows, o->temperature, o->top_k, o->top_p,
+                           m->uniforms + i + 1, m->state->argmax, nullptr, m->st));
     NNZ_CK(cudaEventRecord(m->events[2 + i], m->st));
   }
   std::vector<uint32_t> toks(steps);

@@ -36,6 +36,12 @@ struct EmbedArgs {
 cudaError_t embed_launch(const EmbedArgs& a, int fmt, int bf16s, int pdl, cudaStream_t st);
 // argmax[r] = max(argmax[r], packed first-max of logits[r][0..n)) for r < rows
 // (the packed slot the decode state consumes; see argmax_pack).
+// Sampling (sample.cu): rows x n logits (row stride `stride`, modified in
+// place), one uniform draw per row; the token goes to the argmax slot and,
+// when `tokens` is given, to tokens[row].
+cudaError_t sample_launch(float* logits, uint32_t rows, uint32_t n, uint32_t stride, float temperature,
+                          uint32_t top_k, float top_p, const float* uniforms, unsigned long long* argmax,
+                          uint32_t* tokens, cudaStream_t st);
 cudaError_t logits_argmax_launch(const float* logits, uint32_t rows, uint32_t n, uint32_t stride,
                                  unsigned long long* argmax, cudaStream_t st);
 cudaError_t dequant_launch(int fmt, int bf16s, const uint8_t* w, uint32_t M, uint32_t K, uint32_t gs,

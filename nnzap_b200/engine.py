@@ -272,10 +272,9 @@ def shard_weights(fmt: str, axis: int, weight: np.ndarray, scales: np.ndarray, b
 
 
 def generate(model: Model, opts: GenerateOpts) -> GenerateResult:
-    """Greedy generate (transformer.zig:3942-4027): device prefill, then one
-    CUDA-graph replay per token; stops at the first EOS like the reference."""
-    if opts.params.temperature > 0.0:
-        raise ValueError("only greedy decoding (temperature 0) runs on the B200 path")
+    """generate (transformer.zig:3942-4027): device prefill, then one decode
+    launch per token; greedy, or sampled on the device when
+    opts.params.temperature > 0; stops at the first EOS like the reference."""
     prompt = np.ascontiguousarray(opts.prompt_ids, dtype=np.uint32)
     eos = np.ascontiguousarray(opts.eos_ids, dtype=np.uint32) if len(opts.eos_ids) else None
     out = np.zeros(opts.max_new, dtype=np.uint32)
@@ -288,6 +287,16 @@ def generate(model: Model, opts: GenerateOpts) -> GenerateResult:
     o.output_tokens = out.ctypes.data_as(C.POINTER(C.c_uint32))
     o.max_new = opts.max_new
     o.per_token_ns = ns.ctypes.data_as(C.POINTER(C.c_uint64)) if opts.per_token_ns else None
+    sp = opts.params
+    uni = None
+    if sp.temperature > 0.0:
+        # the host draws the per-token uniforms (seeded; the reference uses
+        # Zig's DefaultPrng(seed), which this generator does not reproduce)
+        uni = np.random.default_rng(sp.seed).random(opts.max_new, dtype=np.float32)
+        o.temperature, o.top_k, o.top_p = float(sp.temperature), int(sp.top_k), float(sp.top_p)
+        o.uniforms = uni.ctypes.data_as(C.POINTER(C.c_float))
+    else:
+        o.temperature, o.top_k, o.top_p = 0.0, 0, 1.0
     r = capi.NnzGenerateResult()
     check(lib().nnz_generate(model._h, C.byref(o), C.byref(r)))
     n = r.tokens_generated

@@ -29,7 +29,8 @@ What it restates (all citations are paths inside the nnzap reference tree):
   after norm+RoPE, f32 softmax, f32 logits
   (nnmetal/src/shaders/qmv_specialized.metal:1096-1279,
   nnmetal/src/shaders/transformer.metal:1467-1695, :561-608).
-* Greedy argmax, first maximum wins (nnmetal/src/transformer.zig:3694-3707).
+* Greedy argmax, first maximum wins (nnmetal/src/transformer.zig:3694-3707);
+  sampling with temperature / top-k / top-p (:3709-3880) given the draw.
 
 Parity status: UNPINNED against the reference's own outputs.  The engine
 needs Zig + Apple Metal and the MLX scripts need Apple's MLX, none of which
@@ -200,6 +201,45 @@ def attention_decode(q: np.ndarray, kc: np.ndarray, vc: np.ndarray, n_kv: int) -
 def argmax_first(logits: np.ndarray) -> int:
     """First maximum wins (transformer.zig:3694-3707)."""
     return int(np.argmax(logits))
+
+
+def softmax_f32(x: np.ndarray) -> np.ndarray:
+    """softmaxInPlace (transformer.zig:3724-3744), f32."""
+    x = x.astype(np.float32)
+    e = np.exp(x - np.max(x)).astype(np.float32)
+    return (e * np.float32(1.0 / e.sum(dtype=np.float32))).astype(np.float32)
+
+
+def sample_cdf(logits: np.ndarray, temperature: float, top_k: int, top_p: float) -> np.ndarray:
+    """The running sum (vocabulary order) of the probabilities sampleToken
+    draws from (transformer.zig:3833-3869): temperature scaling
+    (applyTemperature :3709), top-k (applyTopK :3748: keep values >= the
+    k-th largest), top-p (applyTopP :3779: walk the probabilities in
+    descending order, keep tokens until the cumulative mass reaches p),
+    softmax."""
+    x = logits.astype(np.float32) * np.float32(1.0 / np.float32(temperature))
+    if 0 < top_k < len(x):
+        thr = np.sort(x)[::-1][top_k - 1]
+        x = np.where(x < thr, np.float32(-np.inf), x)
+    if top_p < 1.0:
+        pr = softmax_f32(x)
+        order = np.argsort(-pr, kind="stable")
+        cum = np.cumsum(pr[order], dtype=np.float32)
+        keep = np.searchsorted(cum, np.float32(top_p)) + 1   # through the first crossing
+        x = x.copy()
+        x[order[keep:]] = np.float32(-np.inf)
+    return np.cumsum(softmax_f32(x), dtype=np.float32)
+
+
+def sample_token(logits: np.ndarray, temperature: float, top_k: int, top_p: float, r: float) -> int:
+    """sampleToken with the uniform draw r given; greedy at temperature 0.
+    sampleFromDistribution (:3873): first index whose running sum exceeds r,
+    else the last index."""
+    if temperature == 0.0:
+        return argmax_first(logits)
+    cum = sample_cdf(logits, temperature, top_k, top_p)
+    idx = np.nonzero(cum > np.float32(r))[0]
+    return int(idx[0]) if len(idx) else len(cum) - 1
 
 
 # --------------------------------------------------------------------------

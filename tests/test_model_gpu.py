@@ -200,3 +200,25 @@ def test_batched_decode_gemm_rows(cuda, built_lib, d):
         want = R.forward_tokens(cfg, W, [int(toks[r]), int(nxt[r])])[-1]
         np.testing.assert_allclose(lg2[r], want, atol=2e-2, rtol=0)
     m.free()
+
+
+def test_generate_sampled_matches_oracle(cuda, built_lib):
+    """Sampled generate(): each token is the oracle's sampleToken of the
+    teacher-forced logits with the same uniform draw (a draw within rounding
+    of a CDF boundary may take the neighbour)."""
+    from nnzap_b200 import SamplingParams
+    d = SMALL_Q1
+    m, W = build(d, max_ctx=64, max_batch=1)
+    prompt = [7, 300, 41, 999, 5]
+    sp = SamplingParams(temperature=0.8, top_k=40, top_p=0.9, seed=11)
+    res = generate(m, GenerateOpts(prompt_ids=prompt, max_new=10, params=sp))
+    assert res.tokens_generated == 10
+    u = np.random.default_rng(sp.seed).random(10, dtype=np.float32)
+    lg = R.forward_tokens(oracle_cfg(d), W, prompt + res.tokens[:-1])[len(prompt) - 1:]
+    for i, t in enumerate(res.tokens):
+        want = R.sample_token(lg[i], sp.temperature, sp.top_k, sp.top_p, float(u[i]))
+        if t != want:
+            cum = R.sample_cdf(lg[i], sp.temperature, sp.top_k, sp.top_p)
+            # logits differ from the oracle by < 2e-2, so the CDF may shift a little
+            assert abs(float(cum[min(t, want)]) - float(u[i])) < 2e-2, (i, t, want)
+    m.free()
