@@ -184,6 +184,15 @@ struct nnz_model {
   nnz_config full{};       // the model's dims as given
   int tp = 1, tp_rank = 0;
   ncclComm_t comm = nullptr;
+  // fused GEMM + peer-memory all-reduce (decode / prefill GEMM path)
+  bool tp_fused = false;
+  float* tp_racc = nullptr;            // [2][rows_max][H] f32 local partials, zero at rest
+  float* tp_slots = nullptr;           // [2][tp][rows_max * H] f32 peers' partials
+  int tp_parity = 0;                   // which half the next reduction uses
+  uint32_t* tp_flags = nullptr;        // per-slice arrival counts (tp_allreduce_flag_words)
+  float** d_peer_slots = nullptr;      // device [2][tp]: every GPU's slot arrays, mapped here
+  uint32_t** d_peer_flags = nullptr;   // device [tp]: every GPU's flags, mapped here
+  std::vector<void*> ipc_opened;
   uint32_t lm_rows = 0, lm_off = 0;   // this rank's LM-head vocabulary rows
   int device = 0;
   int num_sms = 148;
@@ -448,6 +457,31 @@ int nccl_fail(ncclResult_t r) {
   return fail(NNZ_ENCCL, std::string("NCCL: ") + (api ? api->error_string(r) : e.c_str()));
 }
 
+// A row-split projection (o / down) added into the residual of the whole
+// group.  With peer memory: the GEMM accumulates this GPU's partial in a
+// local buffer, then tp_allreduce_kernel pushes it into every peer's slot
+// array over NVLink, exchanges per-slice flags and adds all partials into
+// the residual.  The buffers alternate between two halves, so a GPU that
+// runs ahead writes into the half its slower peers are not reading.
+// Otherwise: zero-start + NCCL all-reduce.
+int tp_post_add(nnz_model* m, uint32_t rows);
+int gemm_resadd_tp(nnz_model* m, const FlatW& W, uint32_t K, const __half* x, uint32_t rows) {
+  const uint32_t H = m->c.hidden_size;
+  int rc;
+  if (m->tp_fused) {
+    const int par = m->tp_parity;
+    m->tp_parity ^= 1;
+    float* racc = m->tp_racc + (size_t)par * m->rows_max * H;
+    if ((rc = gemm(m, W, nullptr, H, K, x, rows, GEPI_RESADD, racc, H))) return rc;
+    NNZ_CK(tp_allreduce_launch(m->residual, racc, m->d_peer_slots + (size_t)par * m->tp, m->tp_flags,
+                               m->d_peer_flags, (size_t)rows * H, m->tp_rank, m->tp, m->err, m->st));
+    return NNZ_OK;
+  }
+  if ((rc = tp_pre_add(m, rows))) return rc;
+  if ((rc = gemm(m, W, nullptr, H, K, x, rows, GEPI_RESADD, m->residual, H))) return rc;
+  return tp_post_add(m, rows);
+}
+
 int tp_post_add(nnz_model* m, uint32_t rows) {
   if (m->tp == 1) return NNZ_OK;
   const NcclApi* api = nccl_api(nullptr);
@@ -478,14 +512,10 @@ int enqueue_layer(nnz_model* m, uint32_t l, uint32_t rows, const int* pos, const
     NNZ_CK(rmsnorm_f16_launch(m->residual, W.attn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st));
     if ((rc = gemm(m, W.fqkv, nullptr, m->qkv_rows, H, m->xn, rows, GEPI_F16, m->qkv, m->qkv_rows))) return rc;
     if ((rc = attn(m, l, rows, pos, slot, 1, 0))) return rc;
-    if ((rc = tp_pre_add(m, rows))) return rc;
-    if ((rc = gemm(m, W.fo, nullptr, H, m->qd, m->attn, rows, GEPI_RESADD, m->residual, H))) return rc;
-    if ((rc = tp_post_add(m, rows))) return rc;
+    if ((rc = gemm_resadd_tp(m, W.fo, m->qd, m->attn, rows))) return rc;
     NNZ_CK(rmsnorm_f16_launch(m->residual, W.ffn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st));
     if ((rc = gemm(m, W.fgate, &W.fup, I, H, m->xn, rows, GEPI_SILU, m->h, I))) return rc;
-    if ((rc = tp_pre_add(m, rows))) return rc;
-    if ((rc = gemm(m, W.fdown, nullptr, H, I, m->h, rows, GEPI_RESADD, m->residual, H))) return rc;
-    return tp_post_add(m, rows);
+    return gemm_resadd_tp(m, W.fdown, I, m->h, rows);
   }
   if ((rc = qmv(m, 1, PRO_NORM, EPI_F16, W.qkv, m->qkv_rows, c.hidden_size, m->residual,
                 c.hidden_size, W.attn_norm, rows, m->qkv, m->qkv_rows, nullptr, nullptr, pdl)))
@@ -687,14 +717,10 @@ int enqueue_layer_gemm(nnz_model* m, uint32_t l, uint32_t rows, const int* pos) 
     aa.out_stride = m->qd; aa.err = m->err; aa.rope_tab = m->rope_tab; aa.ws = m->ws;
     NNZ_CK(attn_prefill_launch(aa, (int)c.head_dim, 0, m->st));
   }
-  if ((rc = tp_pre_add(m, rows))) return rc;
-  if ((rc = gemm(m, W.fo, nullptr, H, m->qd, m->attn, rows, GEPI_RESADD, m->residual, H))) return rc;
-  if ((rc = tp_post_add(m, rows))) return rc;
+  if ((rc = gemm_resadd_tp(m, W.fo, m->qd, m->attn, rows))) return rc;
   NNZ_CK(rmsnorm_f16_launch(m->residual, W.ffn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st));
   if ((rc = gemm(m, W.fgate, &W.fup, I, H, m->xn, rows, GEPI_SILU, m->h, I))) return rc;
-  if ((rc = tp_pre_add(m, rows))) return rc;
-  if ((rc = gemm(m, W.fdown, nullptr, H, I, m->h, rows, GEPI_RESADD, m->residual, H))) return rc;
-  return tp_post_add(m, rows);
+  return gemm_resadd_tp(m, W.fdown, I, m->h, rows);
 }
 
 int enqueue_prefill(nnz_model* m, uint32_t n, bool want_logits) {
@@ -736,6 +762,61 @@ int enqueue_prefill(nnz_model* m, uint32_t n, bool want_logits) {
 // Persistent-kernel plan for `rows` decode rows (cached).
 
 }  // namespace
+
+// Map every group member's reduction buffers and barrier flags into this process
+// (CUDA IPC handles exchanged with an NCCL all-gather) for the fused
+// GEMM + peer-memory reduction.  Collective: every rank calls it at
+// finalize.
+int tp_setup_peers(nnz_model* m) {
+  const int T = m->tp, r = m->tp_rank;
+  int rc;
+  const size_t nmax = (size_t)m->rows_max * m->c.hidden_size;
+  const size_t nflag = tp_allreduce_flag_words(nmax, T);
+  if ((rc = dalloc(m, (void**)&m->tp_racc, 2 * nmax * 4))) return rc;
+  NNZ_CK(cudaMemset(m->tp_racc, 0, 2 * nmax * 4));
+  if ((rc = dalloc(m, (void**)&m->tp_slots, 2 * (size_t)T * nmax * 4))) return rc;
+  if ((rc = dalloc(m, (void**)&m->tp_flags, nflag * 4))) return rc;
+  NNZ_CK(cudaMemset(m->tp_flags, 0, nflag * 4));
+  struct Handles { cudaIpcMemHandle_t slots, flags; };
+  Handles mine;
+  NNZ_CK(cudaIpcGetMemHandle(&mine.slots, m->tp_slots));
+  NNZ_CK(cudaIpcGetMemHandle(&mine.flags, m->tp_flags));
+  void* dbuf = nullptr;
+  if ((rc = dalloc(m, &dbuf, sizeof(Handles) * (T + 1)))) return rc;
+  NNZ_CK(cudaMemcpy(dbuf, &mine, sizeof(Handles), cudaMemcpyHostToDevice));
+  const NcclApi* api = nccl_api(nullptr);
+  const ncclResult_t nr = api->all_gather(dbuf, static_cast<uint8_t*>(dbuf) + sizeof(Handles), sizeof(Handles),
+                                          ncclUint8, m->comm, m->st);
+  if (nr != ncclSuccess) return nccl_fail(nr);
+  std::vector<Handles> all(T);
+  NNZ_CK(cudaMemcpyAsync(all.data(), static_cast<uint8_t*>(dbuf) + sizeof(Handles), sizeof(Handles) * T,
+                         cudaMemcpyDeviceToHost, m->st));
+  NNZ_CK(cudaStreamSynchronize(m->st));
+  std::vector<float*> slots(2 * T);
+  std::vector<uint32_t*> flags(T);
+  for (int j = 0; j < T; ++j) {
+    float* sb = m->tp_slots;
+    uint32_t* fb = m->tp_flags;
+    if (j != r) {
+      void *ps = nullptr, *pf = nullptr;
+      NNZ_CK(cudaIpcOpenMemHandle(&ps, all[j].slots, cudaIpcMemLazyEnablePeerAccess));
+      m->ipc_opened.push_back(ps);
+      NNZ_CK(cudaIpcOpenMemHandle(&pf, all[j].flags, cudaIpcMemLazyEnablePeerAccess));
+      m->ipc_opened.push_back(pf);
+      sb = static_cast<float*>(ps);
+      fb = static_cast<uint32_t*>(pf);
+    }
+    slots[j] = sb;                                // parity 0 half
+    slots[T + j] = sb + (size_t)T * nmax;         // parity 1 half
+    flags[j] = fb;
+  }
+  if ((rc = dalloc(m, (void**)&m->d_peer_slots, sizeof(float*) * 2 * T))) return rc;
+  NNZ_CK(cudaMemcpy(m->d_peer_slots, slots.data(), sizeof(float*) * 2 * T, cudaMemcpyHostToDevice));
+  if ((rc = dalloc(m, (void**)&m->d_peer_flags, sizeof(uint32_t*) * T))) return rc;
+  NNZ_CK(cudaMemcpy(m->d_peer_flags, flags.data(), sizeof(uint32_t*) * T, cudaMemcpyHostToDevice));
+  m->tp_fused = true;
+  return NNZ_OK;
+}
 
 // =========================================================================
 // C ABI
@@ -1076,6 +1157,10 @@ int nnz_model_finalize(nnz_model* m) {
   }
   NNZ_CK(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking));
   if ((rc = prepare_device(m->device))) return rc;
+  if (m->tp > 1) {
+    const char* col = getenv("NNZ_TP_COLLECTIVE");
+    if (!(col && strcmp(col, "nccl") == 0) && (rc = tp_setup_peers(m))) return rc;
+  }
   m->finalized = true;
   return NNZ_OK;
 }
@@ -1086,6 +1171,7 @@ int nnz_model_free(nnz_model* m) {
   if (m->st) cudaStreamSynchronize(m->st);
   for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
   for (auto e : m->events) cudaEventDestroy(e);
+  for (void* p : m->ipc_opened) cudaIpcCloseMemHandle(p);
   for (void* p : m->allocs) cudaFree(p);
   if (m->st) cudaStreamDestroy(m->st);
   if (m->comm)

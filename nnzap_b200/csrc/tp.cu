@@ -5,6 +5,7 @@
 #include <mutex>
 
 #include "tp.cuh"
+#include "common.cuh"
 
 namespace nnz {
 
@@ -32,12 +33,85 @@ void load() {
   g_api.all_reduce = reinterpret_cast<decltype(g_api.all_reduce)>(dlsym(h, "ncclAllReduce"));
   g_api.comm_destroy = reinterpret_cast<decltype(g_api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
   g_api.error_string = reinterpret_cast<decltype(g_api.error_string)>(dlsym(h, "ncclGetErrorString"));
+  g_api.all_gather = reinterpret_cast<decltype(g_api.all_gather)>(dlsym(h, "ncclAllGather"));
   if (!g_api.get_unique_id || !g_api.comm_init_rank || !g_api.all_reduce || !g_api.comm_destroy ||
-      !g_api.error_string) {
+      !g_api.error_string || !g_api.all_gather) {
     g_err = "NCCL library lacks an entry point";
     return;
   }
   g_ok = true;
+}
+
+constexpr uint32_t kTpSpinLimit = 1u << 24;
+constexpr int kArThreads = 256;
+constexpr size_t kArSlice = kArThreads * 8;   // floats per CTA (two float4 per thread)
+
+__global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(float* residual, float* part,
+                                                                  float* const* peer_slots, uint32_t* flags,
+                                                                  uint32_t* const* peer_flags, size_t n, int rank,
+                                                                  int T, int* err) {
+  const size_t c = blockIdx.x, base = c * kArSlice;
+  const size_t stride = (size_t)(T + 1);
+  float4 v[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const size_t i = base + (size_t)(threadIdx.x + u * kArThreads) * 4;
+    v[u] = i < n ? *reinterpret_cast<const float4*>(part + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  // 1. this GPU's partial into slot `rank` of every peer
+  for (int j = 0; j < T; ++j) {
+    if (j == rank) continue;
+    float* dst = peer_slots[j] + (size_t)rank * n;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const size_t i = base + (size_t)(threadIdx.x + u * kArThreads) * 4;
+      if (i < n) *reinterpret_cast<float4*>(dst + i) = v[u];
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  // 2. raise this slice's flag on every peer, 3. wait for theirs
+  __shared__ uint32_t s_c;
+  if (threadIdx.x == 0) {
+    const uint32_t cnt = flags[c * stride + T] + 1;
+    flags[c * stride + T] = cnt;
+    s_c = cnt;
+    for (int j = 0; j < T; ++j)
+      if (j != rank)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peer_flags[j] + c * stride + rank), "r"(cnt)
+                     : "memory");
+    for (int j = 0; j < T; ++j) {
+      if (j == rank) continue;
+      uint32_t f, it = 0;
+      for (;;) {
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(flags + c * stride + j) : "memory");
+        if ((int)(f - cnt) >= 0) break;
+        if (++it > kTpSpinLimit) {
+          atomicOr(err, ERR_SPIN_TIMEOUT);
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+  }
+  __syncthreads();
+  // 4. fold: residual += own partial + peers' partials; re-zero the partial
+  float* slots = peer_slots[rank];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const size_t i = base + (size_t)(threadIdx.x + u * kArThreads) * 4;
+    if (i >= n) continue;
+    float4 acc = v[u];
+    for (int j = 0; j < T; ++j) {
+      if (j == rank) continue;
+      const float4 w = __ldcg(reinterpret_cast<const float4*>(slots + (size_t)j * n + i));
+      acc.x += w.x; acc.y += w.y; acc.z += w.z; acc.w += w.w;
+    }
+    float4 r = *reinterpret_cast<float4*>(residual + i);
+    r.x += acc.x; r.y += acc.y; r.z += acc.z; r.w += acc.w;
+    *reinterpret_cast<float4*>(residual + i) = r;
+    *reinterpret_cast<float4*>(part + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
 }
 
 __global__ void argmax_shift_kernel(unsigned long long* am, uint32_t rows, uint32_t off) {
@@ -45,6 +119,19 @@ __global__ void argmax_shift_kernel(unsigned long long* am, uint32_t rows, uint3
   if (r < rows && am[r]) am[r] -= off;
 }
 }  // namespace
+
+size_t tp_allreduce_flag_words(size_t n_max, int T) {
+  return ((n_max + kArSlice - 1) / kArSlice) * (size_t)(T + 1);
+}
+
+cudaError_t tp_allreduce_launch(float* residual, float* part, float* const* peer_slots, uint32_t* flags,
+                                uint32_t* const* peer_flags, size_t n, int rank, int T, int* err,
+                                cudaStream_t st) {
+  if (n % 4) return cudaErrorInvalidValue;
+  const unsigned grid = (unsigned)((n + kArSlice - 1) / kArSlice);
+  tp_allreduce_kernel<<<grid, kArThreads, 0, st>>>(residual, part, peer_slots, flags, peer_flags, n, rank, T, err);
+  return cudaGetLastError();
+}
 
 const NcclApi* nccl_api(std::string* err) {
   std::call_once(g_once, load);
