@@ -39,6 +39,7 @@ struct AttnArgs {
   __half* kc;          // layer base of the K cache
   __half* vc;          // layer base of the V cache
   uint32_t max_ctx;
+  uint32_t slots;      // cache slots behind kc / vc (0: rows)
   const int* pos;      // [rows] position of each query row
   const int* slot;     // [rows] cache slot of each row (nullptr: slot = row)
   uint32_t rows;

@@ -10,8 +10,9 @@
 //     and (decode) the new K/V written into the cache at `pos`.
 //  2. attn_tc_kernel, persistent: every warp owns a stream of tasks
 //     (row, kv head, 256-position chunk) and a private 3-stage shared-memory
-//     ring of 16-position K/V blocks filled by 1-D bulk copies, one 256-byte
-//     row per copy into rows padded to 272 bytes (conflict-free ldmatrix).
+//     ring of 16-position K/V blocks, each loaded by four 2-D TMA copies
+//     (K and V, head dims 0-63 and 64-127) with the 128-byte swizzle, so
+//     ldmatrix reads are conflict-free.
 //     S = Q.K^T and O += P.V run as mma.m16n8k16 (f16 in, f32 accumulate)
 //     with A rows [q_hi(G) | q_lo(G)] and [p_hi(G) | p_lo(G)], so each f32
 //     operand enters the tensor core as an exact-to-2^-22 pair; the online
@@ -19,10 +20,12 @@
 //     runs ahead across task boundaries, so a warp never drains it.
 //  3. attn_tc_combine_kernel, one CTA per (kv head, row): merges the
 //     chunks' (m, l, o) and writes the fp16 output.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <math.h>
 
 #include "attn.cuh"
+#include "gemm.cuh"
 #include "rope_dev.cuh"
 
 namespace nnz {
@@ -34,14 +37,16 @@ constexpr int kTcWarps = 4;
 constexpr int kTcBlk = 16;              // positions per streamed block
 constexpr int kTcStages = 3;
 constexpr int kTcRowB = kHD * 2 + 16;   // padded shared-memory row (bytes)
-constexpr int kTcSlotB = 2 * kTcBlk * kTcRowB;   // K rows then V rows
-constexpr int kTcWarpB = kTcStages * kTcSlotB + 64;
-constexpr int kTcSmem = kTcWarps * kTcWarpB;
+constexpr int kTcBoxB = kTcBlk * 128;            // one TMA box: 16 rows x 64 dims (fp16)
+constexpr int kTcSlotB = 4 * kTcBoxB;             // K dims 0-63, K 64-127, V 0-63, V 64-127
+constexpr int kTcWarpB = kTcStages * kTcSlotB + 1024;   // + barriers, padded to the 1 KB swizzle atom
+constexpr int kTcSmem = kTcWarps * kTcWarpB + 1024;     // + alignment slack
 constexpr int kTcQRows = 8;             // hi/lo query rows per (row, kv head)
 
 __host__ __device__ inline uint32_t tc_chunks(uint32_t max_ctx) { return (max_ctx + kTcChunk - 1) / kTcChunk; }
 
 struct TcArgs {
+  CUtensorMap tmK, tmV;   // the layer's K / V cache as [slots * n_kv * max_ctx][hd] fp16 rows
   AttnArgs a;
   uint32_t nch;        // chunks per (row, kv head) at max_ctx
   uint32_t ntasks;
@@ -127,11 +132,25 @@ __device__ __forceinline__ uint32_t pack_h2(float x, float y) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared address of 16-byte chunk `ch` (0-15: head dims 8ch..8ch+7) of row
+// r of a 16-row K or V tile stored as two 128B-swizzled TMA boxes.
+__device__ __forceinline__ uint32_t swz(uint32_t tile, int r, int ch) {
+  return tile + (ch >> 3) * kTcBoxB + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
+}
+
 // One task's cache range; false when the chunk lies past the row's position.
 struct TcTask {
   uint32_t row, kvh, c;
   int npos, nblk;
-  size_t off;   // element offset of the chunk's first position in the layer's K/V
+  uint32_t row0;   // cache row (of the 2-D view) of the chunk's first position
 };
 
 // Tasks are numbered chunk-major (all rows' chunk 0, then chunk 1, ...), so
@@ -150,13 +169,14 @@ __device__ __forceinline__ bool tc_task(const TcArgs& t, uint32_t task, TcTask& 
   k.npos = min(kTcChunk, seq - t0);
   k.nblk = (k.npos + kTcBlk - 1) / kTcBlk;
   const int slot = a.slot ? a.slot[k.row] : (int)k.row;
-  k.off = (((size_t)slot * a.n_kv + k.kvh) * a.max_ctx + t0) * kHD;
+  k.row0 = ((uint32_t)slot * a.n_kv + k.kvh) * a.max_ctx + (uint32_t)t0;
   return true;
 }
 
 template <int G>
 __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(const __grid_constant__ TcArgs t) {
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const AttnArgs& a = t.a;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q4 = lane & 3;
   uint8_t* ring = smem + warp * kTcWarpB;
@@ -180,21 +200,18 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(const __grid_con
   int pblk = 0;
   auto issue = [&](int stg) {
     uint8_t* slot = ring + stg * kTcSlotB;
-    const int n = min(kTcBlk, pk.npos - pblk * kTcBlk);
-    // the slot was last read through the generic proxy (ldmatrix)
+    // the slot was last read (and possibly zeroed) through the generic proxy
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    if (lane == 0) mbar_arrive_expect_tx(&bars[stg], (uint32_t)(2 * n * kHD * 2));
     __syncwarp();
-    const size_t src = pk.off + (size_t)(pblk * kTcBlk) * kHD;
-    const int r = lane & 15;
-    const bool isv = lane >= 16;
-    uint8_t* dst = slot + (isv ? kTcBlk * kTcRowB : 0) + r * kTcRowB;
-    if (r < n) {
-      bulk_g2s(dst, (isv ? a.vc : a.kc) + src + (size_t)r * kHD, kHD * 2, &bars[stg]);
-    } else if (isv) {
-      // rows past the chunk: zero V so that 0-probability * V stays 0
-      for (int i = 0; i < kHD * 2 / 16; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bars[stg], (uint32_t)kTcSlotB);
+      const int y = (int)(pk.row0 + (uint32_t)(pblk * kTcBlk));
+      tma_load_2d(slot, &t.tmK, 0, y, &bars[stg]);
+      tma_load_2d(slot + kTcBoxB, &t.tmK, 64, y, &bars[stg]);
+      tma_load_2d(slot + 2 * kTcBoxB, &t.tmV, 0, y, &bars[stg]);
+      tma_load_2d(slot + 3 * kTcBoxB, &t.tmV, 64, y, &bars[stg]);
     }
+    __syncwarp();
     if (++pblk == pk.nblk) {
       pblk = 0;
       pvalid = false;
@@ -235,7 +252,18 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(const __grid_con
       if (!failed) failed = !mbar_wait(&bars[cstg], (cphase >> cstg) & 1u, a.err);
       cphase ^= 1u << cstg;
       const uint32_t kbase = smem_u32(ring + cstg * kTcSlotB);
-      const uint32_t vbase = kbase + kTcBlk * kTcRowB;
+      const uint32_t vbase = kbase + 2 * kTcBoxB;
+      const int nvalid = ck.npos - blk * kTcBlk;
+      if (nvalid < kTcBlk) {
+        // rows past the chunk hold other positions (or zero fill): zero V so
+        // that 0-probability * V stays 0 whatever they contain
+        for (int i = lane; i < (kTcBlk - nvalid) * 16; i += 32) {
+          const int r = nvalid + i / 16, part = i % 16;   // 16 x 16 bytes per row (two boxes)
+          const uint32_t ad = vbase + (part / 8) * kTcBoxB + r * 128 + (part % 8) * 16;
+          asm volatile("st.shared.v4.b32 [%0], {%1,%1,%1,%1};" ::"r"(ad), "r"(0u) : "memory");
+        }
+        __syncwarp();
+      }
       // S = Q K^T for 16 positions (two n-tiles of 8)
       float s[2][4];
 #pragma unroll
@@ -244,13 +272,12 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(const __grid_con
 #pragma unroll
         for (int kq = 0; kq < 4; ++kq) {
           uint32_t r0, r1, r2, r3;
-          ldsm_x4(kbase + (nt * 8 + (lane & 7)) * kTcRowB + (4 * kq + (lane >> 3)) * 16, r0, r1, r2, r3);
+          ldsm_x4(swz(kbase, nt * 8 + (lane & 7), 4 * kq + (lane >> 3)), r0, r1, r2, r3);
           mma_f16(s[nt], qa[2 * kq][0], 0u, qa[2 * kq][1], 0u, r0, r1);
           mma_f16(s[nt], qa[2 * kq + 1][0], 0u, qa[2 * kq + 1][1], 0u, r2, r3);
         }
       }
       // hi + lo rows, scale, mask
-      const int nvalid = ck.npos - blk * kTcBlk;
       float sv[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -286,8 +313,7 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(const __grid_con
 #pragma unroll
       for (int jp = 0; jp < 8; ++jp) {
         uint32_t r0, r1, r2, r3;
-        ldsm_x4_t(vbase + ((lane & 7) + 8 * ((lane >> 3) & 1)) * kTcRowB + (2 * jp + (lane >> 4)) * 16, r0, r1,
-                  r2, r3);
+        ldsm_x4_t(swz(vbase, (lane & 7) + 8 * ((lane >> 3) & 1), 2 * jp + (lane >> 4)), r0, r1, r2, r3);
         mma_f16(o[2 * jp], pa0, 0u, pa2, 0u, r0, r1);
         mma_f16(o[2 * jp + 1], pa0, 0u, pa2, 0u, r2, r3);
       }
@@ -719,6 +745,12 @@ cudaError_t attn_tc_launch(const AttnArgs& a, int pdl, cudaStream_t st) {
   }
   TcArgs t{};
   t.a = a;
+  {
+    const uint64_t rows = (uint64_t)(a.slots ? a.slots : a.rows) * a.n_kv * a.max_ctx;
+    if (!tensor_map_f16_2d(&t.tmK, a.kc, kHD, rows, kHD * 2, 64, kTcBlk) ||
+        !tensor_map_f16_2d(&t.tmV, a.vc, kHD, rows, kHD * 2, 64, kTcBlk))
+      return cudaErrorInvalidValue;
+  }
   t.nch = tc_chunks(a.max_ctx);
   t.ntasks = a.rows * a.n_kv * t.nch;
   const uint32_t G = a.n_q / a.n_kv;

@@ -418,7 +418,7 @@ int attn(nnz_model* m, uint32_t layer, uint32_t rows, const int* pos, const int*
   a.max_ctx = m->c.max_context_length; a.pos = pos; a.slot = slot; a.rows = rows;
   a.n_q = m->c.num_query_heads; a.n_kv = m->c.num_kv_heads;
   a.eps = m->c.eps; a.theta = m->c.rope_theta; a.rope_style = m->c.rope_style;
-  a.write_kv = write; a.splits = attn_splits(m, rows); a.rope_tab = m->rope_tab;
+  a.write_kv = write; a.splits = attn_splits(m, rows); a.rope_tab = m->rope_tab; a.slots = m->slots;
   a.out = m->attn; a.out_stride = m->qd; a.ws = m->ws; a.counters = m->counters; a.err = m->err;
   NNZ_CK(attn_decode_launch(a, (int)m->c.head_dim, pdl, m->st));
   return NNZ_OK;

@@ -448,6 +448,19 @@ constexpr uint32_t kSmemBytes = 2 * kStages * kTileBytes + 1024 + 256;
 
 }  // namespace
 
+bool tensor_map_f16_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                       uint32_t box_inner, uint32_t box_outer) {
+  EncodeFn enc = get_encode();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 cudaError_t gemm_debug_profile(unsigned long long* out) {
   return cudaMemcpyFromSymbol(out, g_gemm_prof, sizeof(g_gemm_prof));
 }

@@ -47,6 +47,11 @@ struct GemmArgs {
 
 // Builds the TMA descriptor for X [M][K] fp16 (row stride K) and launches.
 cudaError_t gemm_launch(const GemmArgs& a, const __half* x, cudaStream_t st);
+// 2-D fp16 tensor map with 128-byte swizzle: `outer` rows of `inner`
+// elements, row pitch row_bytes, boxes of box_outer x box_inner (box_inner
+// * 2 = 128 bytes).  False if the driver entry point or the encode fails.
+bool tensor_map_f16_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                       uint32_t box_inner, uint32_t box_outer);
 // Development aid: the 128 clock64() stamps of the last profiled launch.
 cudaError_t gemm_debug_profile(unsigned long long* out);
 // RMSNorm rows of an f32 residual into fp16 (the prefill GEMM's X operand).
