@@ -239,6 +239,7 @@ struct nnz_model {
   float *mR = nullptr, *mqkv = nullptr, *mgu = nullptr, *matt = nullptr;
   unsigned int* mbar = nullptr;
   unsigned long long mbar_count = 0;
+  unsigned int* mdep = nullptr;        // persistent kernel dataflow counters
   float2* rope_tab = nullptr;          // [max_ctx][head_dim / 2] (cos, sin)   // grid-barrier arrivals so far (device counter's value)
   unsigned long long* mprof = nullptr;    // NNZ_MEGA_PROFILE=1: per-phase timestamps
   struct MegaPlan { MegaArgs a; uint32_t grid, smem; bool ok; };
@@ -630,7 +631,7 @@ const nnz_model::MegaPlan* mega_plan_for(nnz_model* m, uint32_t rows) {
   a.emb_w = m->emb_w; a.emb_s = m->emb_s; a.emb_b = m->emb_b; a.kc = m->kc; a.vc = m->vc;
   a.kv_layer = m->kv_layer; a.R = m->mR; a.qkv_acc = m->mqkv; a.gu_acc = m->mgu; a.att_ws = m->matt;
   a.st = m->state; a.seq = m->seq; a.seq_len = c.max_context_length; a.logits = nullptr;
-  a.bar = m->mbar; a.err = m->err; a.prof = m->mprof;
+  a.bar = m->mbar; a.err = m->err; a.prof = m->mprof; a.dep = m->mdep;
   {
     const LayerW& W0 = m->L[0];
     a.l0 = MegaLayer{W0.qkv, W0.o, W0.gu, W0.down, W0.attn_norm, W0.ffn_norm, W0.q_norm, W0.k_norm};
@@ -675,7 +676,7 @@ int run_step(nnz_model* m, uint32_t rows, bool want_logits) {
     a.logits = want_logits ? m->logits : nullptr;
     a.bar_base = m->mbar_count;
     NNZ_CK(mega_launch(a, m->fmt, m->bf16s, P->grid, P->smem, m->st));
-    m->mbar_count += (unsigned long long)P->grid * (1 + 5 * a.L);   // one arrival per CTA per barrier
+    m->mbar_count += (unsigned long long)P->grid * (1 + 3 * a.L);   // one arrival per CTA per barrier
     return NNZ_OK;
   }
   cudaGraphExec_t g;
@@ -1140,6 +1141,8 @@ int nnz_model_finalize(nnz_model* m) {
       if ((rc = dalloc(m, (void**)&m->mgu, (size_t)bmax * 2 * I * 4))) return rc;
       if ((rc = dalloc(m, (void**)&m->matt, (size_t)bmax * c.num_kv_heads * 32 * G * (c.head_dim + 2) * 4))) return rc;
       if ((rc = dalloc(m, (void**)&m->mbar, 64))) return rc;
+      if ((rc = dalloc(m, (void**)&m->mdep, (size_t)(num_tiles(m->qkv_rows) + bmax * c.num_kv_heads) * 4))) return rc;
+      NNZ_CK(cudaMemset(m->mdep, 0, (size_t)(num_tiles(m->qkv_rows) + bmax * c.num_kv_heads) * 4));
       const char* prof = getenv("NNZ_MEGA_PROFILE");
       if (prof && prof[0] == '1') {
         if ((rc = dalloc(m, (void**)&m->mprof, 8 * (2 * (2 + 5 * c.num_layers) + 64 + 5 * 1024)))) return rc;

@@ -1,6 +1,7 @@
 // Persistent cooperative decode kernel (see mega.cuh).
 //
-// Phases, each ended by a grid barrier:
+// Phases (grid barriers between them, except QKV -> ATT and ATT -> O, which
+// are per-unit dataflow counters):
 //   EMBED   CTA 0 advances the device decode state (token <- previous
 //           argmax, position += 1) and writes residual version 0; the other
 //           CTAs clear the accumulators;
@@ -199,6 +200,33 @@ __device__ __forceinline__ void grid_sync(unsigned int* bar, unsigned int nblock
     }
   }
   __syncthreads();
+}
+
+// Dataflow edges (QKV -> attention, attention -> O): the producer unit adds
+// one to its counter after its results are written (release: the CTA's
+// writes, ordered by bar.sync, become visible to whoever acquires the
+// count); the consumer waits, bounded, until every counter it reads has
+// reached its target.
+__device__ __forceinline__ void dep_signal(unsigned int* ctr) {
+  __syncthreads();
+  if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
+}
+
+__device__ __forceinline__ void dep_wait(const unsigned int* ctr, unsigned int target, unsigned int* bar, int* err) {
+  uint32_t i = 0;
+  for (;;) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+    if (v >= target) return;
+    if ((++i & 63u) == 0) {
+      if (ld_relaxed(&bar[2])) return;
+      if (i > kGridSpinLimit) {
+        atomicOr(err, ERR_SPIN_TIMEOUT);
+        atomicExch(&bar[2], 1u);
+        return;
+      }
+    }
+  }
 }
 
 // Bounded mbarrier wait that also gives up once the launch has aborted.
@@ -474,6 +502,15 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
       stage_norm(res, a.H, nw, rms, K0, Kr, bc, a.bf16r != 0, xs);
     }
   } else if (p.type == PH_O) {
+    // the attention splits of the kv heads whose outputs this unit reads
+    if (threadIdx.x == 0) {
+      const uint32_t G = a.n_q / a.n_kv, ntile = num_tiles((a.n_q + 2 * a.n_kv) * a.hd);
+      const uint32_t h0 = K0 / a.hd, h1 = (K0 + Kr - 1) / a.hd;
+      for (uint32_t b = 0; b < a.batch; ++b)
+        for (uint32_t kvh = h0 / G; kvh <= h1 / G; ++kvh)
+          dep_wait(&a.dep[ntile + b * a.n_kv + kvh], a.att_splits * (p.layer + 1), a.bar, a.err);
+    }
+    __syncthreads();
     if (bc == 1 && gs == 128 && a.hd == 128) {
       attn_quant_row128<NT>(c, K0, ng, xf, gsx, gsum, gsq, red);
       fused = true;
@@ -585,6 +622,7 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
     }
   }
   __syncthreads();
+  if (p.type == PH_QKV) dep_signal(&a.dep[tile]);
   stamp(c, p, u, 5);
 }
 
@@ -710,6 +748,15 @@ __device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause
   if (threadIdx.x == 0 && !prefetched)
     for (int blk = 0; blk < nblk && blk < kAttStages; ++blk) issue(blk);
 
+  // the QKV row tiles holding this kv head's q heads, k and v
+  if (threadIdx.x == 0) {
+    const uint32_t qd = a.n_q * HD, kvd = a.n_kv * HD, tgt = a.ks_qkv * (p.layer + 1);
+    for (uint32_t t = (kvh * G * HD) / kTileRows; t <= ((kvh + 1) * G * HD - 1) / kTileRows; ++t)
+      dep_wait(&a.dep[t], tgt, a.bar, a.err);
+    dep_wait(&a.dep[(qd + kvh * HD) / kTileRows], tgt, a.bar, a.err);
+    dep_wait(&a.dep[(qd + kvd + kvh * HD) / kTileRows], tgt, a.bar, a.err);
+  }
+  __syncthreads();
   const uint32_t qkv_rows = (a.n_q + 2 * a.n_kv) * HD;
   const float* qrow = a.qkv_acc + (size_t)b * qkv_rows;
   const float* qn = lptr(a, a.l0.q_norm, p.layer);
@@ -826,7 +873,7 @@ __device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause
     wsp[(size_t)threadIdx.x * rec + 0] = mst[threadIdx.x];
     wsp[(size_t)threadIdx.x * rec + 1] = lst[threadIdx.x];
   }
-  __syncthreads();
+  dep_signal(&a.dep[num_tiles((a.n_q + 2 * a.n_kv) * HD) + b * a.n_kv + kvh]);
   stamp(c, p, u, 5);
 }
 
@@ -886,6 +933,8 @@ __device__ void embed_phase(Ctx& c) {
   grid_zero(resv(a, 1), (size_t)a.batch * a.H, c);
   grid_zero(a.qkv_acc, (size_t)a.batch * (a.n_q + 2 * a.n_kv) * a.hd, c);
   grid_zero(a.gu_acc, (size_t)a.batch * 2 * a.I, c);
+  const uint32_t ndep = num_tiles((a.n_q + 2 * a.n_kv) * a.hd) + a.batch * a.n_kv;
+  for (uint32_t i = c.cta * blockDim.x + threadIdx.x; i < ndep; i += c.G * blockDim.x) a.dep[i] = 0u;
 }
 
 template <int FMT, int NT, bool BF16S, int HD>
@@ -980,7 +1029,8 @@ __global__ void __launch_bounds__(kQmvThreads) mega_kernel(const __grid_constant
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
       a.prof[2 * (2 + 5 * a.L) + 64 + (ph - 6) * 1024 + c.cta] = t;
     }
-    if (ph < last) grid_sync(a.bar, c.G, gen, a.err);
+    // the QKV -> attention and attention -> O edges are per-unit counters
+    if (ph < last && p.type != PH_QKV && p.type != PH_ATT) grid_sync(a.bar, c.G, gen, a.err);
     if (ph == 0) {
       // positions were advanced by the embedding phase; constant from here on
       if (threadIdx.x < a.batch) {

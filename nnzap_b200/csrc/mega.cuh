@@ -42,6 +42,10 @@ struct MegaArgs {
   float* logits;                // optional [batch][vocab]
   unsigned int* bar;            // [2] abort flag, [4..5] u64 arrival counter
   unsigned long long bar_base;  // arrival count before this launch
+  // dataflow counters replacing the grid barriers after the QKV and the
+  // attention phases: [qkv tiles] QKV units done per row tile, then
+  // [batch][n_kv] attention splits done; zeroed by the embedding phase
+  unsigned int* dep;
   int* err;
   uint32_t nslot;               // weight-ring slots per warp
   unsigned long long* prof;     // optional: CTA 0 records %globaltimer after each phase
