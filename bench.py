@@ -113,13 +113,14 @@ def algorithmic_bytes_per_token(d, ctx):
 
 def launches_per_step(d, prompt, gen, chunk=512):
     """Our kernels launched per generate(): GEMM prefill per 512-row chunk
-    (embed, 8 per layer: norm, QKV GEMM, K/V write, attention, O GEMM,
-    norm, gate/up GEMM, down GEMM; LM head on the last chunk) plus one
-    persistent kernel per decode token (or, on the CUDA-graph path, embed +
-    7 per layer: QKV, 3 attention kernels, O, gate/up, down + LM head)."""
+    (embed, 9 per layer: norm, QKV GEMM, K/V write, attention + split
+    combine, O GEMM, norm, gate/up GEMM, down GEMM; LM head on the last
+    chunk) plus one persistent kernel per decode token (or, on the CUDA-graph
+    path, embed + 7 per layer: QKV, 3 attention kernels, O, gate/up, down +
+    LM head)."""
     chunks = -(-prompt // chunk)
     per_tok = (1 + d.layers * 7 + 1) if os.environ.get("NNZ_DECODE_PATH") == "graph" else 1
-    return chunks * (1 + d.layers * 8) + 1 + gen * per_tok
+    return chunks * (1 + d.layers * 9) + 1 + gen * per_tok
 
 
 def oracle_cfg(d):

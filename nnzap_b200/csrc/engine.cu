@@ -676,7 +676,7 @@ int run_step(nnz_model* m, uint32_t rows, bool want_logits) {
     a.logits = want_logits ? m->logits : nullptr;
     a.bar_base = m->mbar_count;
     NNZ_CK(mega_launch(a, m->fmt, m->bf16s, P->grid, P->smem, m->st));
-    m->mbar_count += (unsigned long long)P->grid * (1 + 3 * a.L);   // one arrival per CTA per barrier
+    m->mbar_count += (unsigned long long)P->grid * (1 + 2 * a.L);   // one arrival per CTA per barrier
     return NNZ_OK;
   }
   cudaGraphExec_t g;
@@ -1141,8 +1141,9 @@ int nnz_model_finalize(nnz_model* m) {
       if ((rc = dalloc(m, (void**)&m->mgu, (size_t)bmax * 2 * I * 4))) return rc;
       if ((rc = dalloc(m, (void**)&m->matt, (size_t)bmax * c.num_kv_heads * 32 * G * (c.head_dim + 2) * 4))) return rc;
       if ((rc = dalloc(m, (void**)&m->mbar, 64))) return rc;
-      if ((rc = dalloc(m, (void**)&m->mdep, (size_t)(num_tiles(m->qkv_rows) + bmax * c.num_kv_heads) * 4))) return rc;
-      NNZ_CK(cudaMemset(m->mdep, 0, (size_t)(num_tiles(m->qkv_rows) + bmax * c.num_kv_heads) * 4));
+      const size_t ndep = num_tiles(m->qkv_rows) + bmax * c.num_kv_heads + num_tiles(I);
+      if ((rc = dalloc(m, (void**)&m->mdep, ndep * 4))) return rc;
+      NNZ_CK(cudaMemset(m->mdep, 0, ndep * 4));
       const char* prof = getenv("NNZ_MEGA_PROFILE");
       if (prof && prof[0] == '1') {
         if ((rc = dalloc(m, (void**)&m->mprof, 8 * (2 * (2 + 5 * c.num_layers) + 64 + 5 * 1024)))) return rc;

@@ -1,7 +1,7 @@
 // Persistent cooperative decode kernel (see mega.cuh).
 //
-// Phases (grid barriers between them, except QKV -> ATT and ATT -> O, which
-// are per-unit dataflow counters):
+// Phases (grid barriers between them, except QKV -> ATT, ATT -> O and
+// GU -> DN, which are per-unit dataflow counters):
 //   EMBED   CTA 0 advances the device decode state (token <- previous
 //           argmax, position += 1) and writes residual version 0; the other
 //           CTAs clear the accumulators;
@@ -518,6 +518,13 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
       stage_attn(c, K0, Kr, bc, xs);
     }
   } else {
+    // the gate/up row tiles this unit's K range reads
+    if (threadIdx.x == 0) {
+      const uint32_t base = num_tiles((a.n_q + 2 * a.n_kv) * a.hd) + a.batch * a.n_kv;
+      for (uint32_t t = K0 / kTileRows; t <= (K0 + Kr - 1) / kTileRows; ++t)
+        dep_wait(&a.dep[base + t], a.ks_gu * (p.layer + 1), a.bar, a.err);
+    }
+    __syncthreads();
     if (bc == 1 && gs == 128) {
       silu_quant_row128<NT>(c, K0, ng, xf, gsx, gsum, gsq);
       fused = true;
@@ -623,6 +630,7 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
   }
   __syncthreads();
   if (p.type == PH_QKV) dep_signal(&a.dep[tile]);
+  if (p.type == PH_GU) dep_signal(&a.dep[num_tiles((a.n_q + 2 * a.n_kv) * a.hd) + a.batch * a.n_kv + tile]);
   stamp(c, p, u, 5);
 }
 
@@ -933,7 +941,7 @@ __device__ void embed_phase(Ctx& c) {
   grid_zero(resv(a, 1), (size_t)a.batch * a.H, c);
   grid_zero(a.qkv_acc, (size_t)a.batch * (a.n_q + 2 * a.n_kv) * a.hd, c);
   grid_zero(a.gu_acc, (size_t)a.batch * 2 * a.I, c);
-  const uint32_t ndep = num_tiles((a.n_q + 2 * a.n_kv) * a.hd) + a.batch * a.n_kv;
+  const uint32_t ndep = num_tiles((a.n_q + 2 * a.n_kv) * a.hd) + a.batch * a.n_kv + num_tiles(a.I);
   for (uint32_t i = c.cta * blockDim.x + threadIdx.x; i < ndep; i += c.G * blockDim.x) a.dep[i] = 0u;
 }
 
@@ -1029,8 +1037,9 @@ __global__ void __launch_bounds__(kQmvThreads) mega_kernel(const __grid_constant
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
       a.prof[2 * (2 + 5 * a.L) + 64 + (ph - 6) * 1024 + c.cta] = t;
     }
-    // the QKV -> attention and attention -> O edges are per-unit counters
-    if (ph < last && p.type != PH_QKV && p.type != PH_ATT) grid_sync(a.bar, c.G, gen, a.err);
+    // the QKV -> attention, attention -> O and gate/up -> down edges are
+    // per-unit counters
+    if (ph < last && p.type != PH_QKV && p.type != PH_ATT && p.type != PH_GU) grid_sync(a.bar, c.G, gen, a.err);
     if (ph == 0) {
       // positions were advanced by the embedding phase; constant from here on
       if (threadIdx.x < a.batch) {

@@ -42,9 +42,10 @@ struct MegaArgs {
   float* logits;                // optional [batch][vocab]
   unsigned int* bar;            // [2] abort flag, [4..5] u64 arrival counter
   unsigned long long bar_base;  // arrival count before this launch
-  // dataflow counters replacing the grid barriers after the QKV and the
-  // attention phases: [qkv tiles] QKV units done per row tile, then
-  // [batch][n_kv] attention splits done; zeroed by the embedding phase
+  // dataflow counters replacing the grid barriers after the QKV, attention
+  // and gate/up phases: [qkv tiles] QKV units done per row tile,
+  // [batch][n_kv] attention splits done, [I tiles] gate/up units done per
+  // row tile; zeroed by the embedding phase
   unsigned int* dep;
   int* err;
   uint32_t nslot;               // weight-ring slots per warp
