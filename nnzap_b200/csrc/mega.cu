@@ -1001,19 +1001,16 @@ __global__ void __launch_bounds__(kQmvThreads) mega_kernel(const __grid_constant
         grid_zero(a.qkv_acc, (size_t)a.batch * (a.n_q + 2 * a.n_kv) * a.hd, c);
         for (uint32_t u = c.cta; u < p.units; u += c.G) qmv_unit<FMT, NT, 2, BF16S>(c, p, u);
         break;
-      case PH_LM: {
-        bool first = true;
-        for (uint32_t u = c.cta; u < p.units; u += c.G) {
-          qmv_unit<FMT, NT, 1, BF16S>(c, p, u, first);
-          first = false;
-        }
-        break;
-      }
       default:
+        // QKV, O, down and the LM head share this one call site, so the
+        // LM head runs the instructions the layers already brought into the
+        // instruction cache (the LM head's x is the same for all of a CTA's
+        // units: only its first unit runs the prologue)
         if (p.type == PH_QKV) grid_zero(a.gu_acc, (size_t)a.batch * 2 * a.I, c);
         if (p.type == PH_O) grid_zero(resv(a, 2 * p.layer + 2), (size_t)a.batch * a.H, c);
         if (p.type == PH_DN) grid_zero(resv(a, 2 * p.layer + 3), (size_t)a.batch * a.H, c);
-        for (uint32_t u = c.cta; u < p.units; u += c.G) qmv_unit<FMT, NT, 1, BF16S>(c, p, u);
+        for (uint32_t u = c.cta; u < p.units; u += c.G)
+          qmv_unit<FMT, NT, 1, BF16S>(c, p, u, p.type != PH_LM || u == c.cta);
         if (p.type == PH_QKV) {
           // the cached K/V blocks of this CTA's first attention unit do not
           // depend on the barrier: start their copies now (the matvec's
