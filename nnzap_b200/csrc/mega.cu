@@ -465,6 +465,38 @@ __device__ __forceinline__ void stamp(const Ctx& c, const PhaseInfo& p, uint32_t
   a.prof[2 * (2 + 5 * a.L) + 8 * which + i] = clock64();
 }
 
+// Prologue of the layouts the register-fused paths above do not cover
+// (batch > 1, other group sizes or widths): stage the unit's slice of x in
+// fp16 shared memory, then quantise it.  Out of line, so the single-row path
+// carries neither its instructions nor its registers.
+template <int NT>
+__device__ __noinline__ void staged_prologue(const Ctx c, const PhaseInfo p, uint32_t K0, uint32_t Kr,
+                                             uint32_t ng) {
+  const MegaArgs& a = *c.a;
+  const uint32_t bc = c.S->bcm;
+  uint8_t* sm = c.smem;
+  __half* xs = reinterpret_cast<__half*>(sm + c.S->xs);
+  float* rms = reinterpret_cast<float*>(sm + c.S->rms);
+  if (p.type == PH_QKV || p.type == PH_GU || p.type == PH_LM) {
+    const uint32_t v = p.type == PH_QKV ? 2 * p.layer : p.type == PH_GU ? 2 * p.layer + 1 : 2 * a.L;
+    const float* nw = p.type == PH_QKV ? lptr(a, a.l0.attn_norm, p.layer)
+                    : p.type == PH_GU ? lptr(a, a.l0.ffn_norm, p.layer) : a.fnorm;
+    const float* res = resv(a, v);
+    if (bc * a.H <= 2048u) {
+      stage_norm_fast(res, a.H, a.H, nw, a.eps, K0, Kr, bc, a.bf16r != 0, rms, xs);
+    } else {
+      block_rms(res, a.H, a.H, bc, a.eps, rms);
+      stage_norm(res, a.H, nw, rms, K0, Kr, bc, a.bf16r != 0, xs);
+    }
+  } else if (p.type == PH_O) {
+    stage_attn(c, K0, Kr, bc, xs);
+  } else {
+    stage_silu(c, K0, Kr, bc, xs);
+  }
+  quantize_xs<NT>(xs, Kr, bc, ng, a.gs, sm + c.S->xf, reinterpret_cast<float*>(sm + c.S->gsx),
+                  reinterpret_cast<float*>(sm + c.S->gsum), reinterpret_cast<int*>(sm + c.S->gsq), false);
+}
+
 template <int FMT, int NT, int SUB, bool BF16S>
 __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue = true) {
   const MegaArgs& a = *c.a;
@@ -495,11 +527,6 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
       // one row, 128-wide groups: normalise and quantise from registers
       norm_quant_row128<NT>(res, a.H, nw, a.eps, G0, ng, a.bf16r != 0, rms, xf, gsx, gsum, gsq);
       fused = true;
-    } else if (bc * a.H <= 2048u) {
-      stage_norm_fast(res, a.H, a.H, nw, a.eps, K0, Kr, bc, a.bf16r != 0, rms, xs);
-    } else {
-      block_rms(res, a.H, a.H, bc, a.eps, rms);
-      stage_norm(res, a.H, nw, rms, K0, Kr, bc, a.bf16r != 0, xs);
     }
   } else if (p.type == PH_O) {
     // the attention splits of the kv heads whose outputs this unit reads
@@ -514,8 +541,6 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
     if (bc == 1 && gs == 128 && a.hd == 128) {
       attn_quant_row128<NT>(c, K0, ng, xf, gsx, gsum, gsq, red);
       fused = true;
-    } else {
-      stage_attn(c, K0, Kr, bc, xs);
     }
   } else {
     // the gate/up row tiles this unit's K range reads
@@ -528,12 +553,10 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
     if (bc == 1 && gs == 128) {
       silu_quant_row128<NT>(c, K0, ng, xf, gsx, gsum, gsq);
       fused = true;
-    } else {
-      stage_silu(c, K0, Kr, bc, xs);
     }
   }
   stamp(c, p, u, 1);
-  if (prologue && !fused) quantize_xs<NT>(xs, Kr, bc, ng, gs, xf, gsx, gsum, gsq, false);
+  if (prologue && !fused) staged_prologue<NT>(c, p, K0, Kr, ng);
   // the split-0 O / down unit adds the previous residual once: fetch it now
   // (into the dead staging area) so the load overlaps the MMAs
   float* rpre = reinterpret_cast<float*>(xs);
