@@ -93,6 +93,13 @@ __host__ __device__ inline void unit_range(const PhaseInfo& p, uint32_t u, uint3
   *ng = g1 - g0;
 }
 
+// Scale groups per weight-ring item.  A ring slot holds a gate/up pair's two
+// segments; the LM head (a single matrix with many groups per unit) fills it
+// with two adjacent groups of its tile, contiguous in the tile-packed layout.
+__host__ __device__ inline uint32_t groups_per_item(int type, uint32_t ng) {
+  return type == PH_LM && ng % 2 == 0 ? 2u : 1u;
+}
+
 struct MegaSmem {
   uint32_t tmpl, bars, abars, ring, slot_bytes, u, xs, xf, gsx, gsum, gsq, red, rms, flag,
       kring, vring, qs, knew, vnew, ss, stat, tok, total, kr_max, ng_max, bcm, nt;
@@ -499,6 +506,9 @@ __device__ __noinline__ void staged_prologue(const Ctx c, const PhaseInfo p, uin
 
 template <int FMT, int NT, int SUB, bool BF16S>
 __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue = true) {
+  // the gate/up pair (SUB == 2) is always PH_GU: let the compiler drop the rest
+  const int ptype = SUB == 2 ? (int)PH_GU : p.type;
+  if constexpr (SUB == 1) __builtin_assume(ptype != PH_GU);
   const MegaArgs& a = *c.a;
   stamp(c, p, u, 0);
   uint32_t tile, split, G0, ng;
@@ -518,17 +528,17 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
   // of a CTA's units, so the caller runs it once)
   bool fused = false;
   if (!prologue) {
-  } else if (p.type == PH_QKV || p.type == PH_GU || p.type == PH_LM) {
-    const uint32_t v = p.type == PH_QKV ? 2 * p.layer : p.type == PH_GU ? 2 * p.layer + 1 : 2 * a.L;
-    const float* nw = p.type == PH_QKV ? lptr(a, a.l0.attn_norm, p.layer)
-                    : p.type == PH_GU ? lptr(a, a.l0.ffn_norm, p.layer) : a.fnorm;
+  } else if (ptype == PH_QKV || ptype == PH_GU || ptype == PH_LM) {
+    const uint32_t v = ptype == PH_QKV ? 2 * p.layer : ptype == PH_GU ? 2 * p.layer + 1 : 2 * a.L;
+    const float* nw = ptype == PH_QKV ? lptr(a, a.l0.attn_norm, p.layer)
+                    : ptype == PH_GU ? lptr(a, a.l0.ffn_norm, p.layer) : a.fnorm;
     const float* res = resv(a, v);
     if (bc == 1 && gs == 128 && a.H <= 2048u && a.H % 128 == 0) {
       // one row, 128-wide groups: normalise and quantise from registers
       norm_quant_row128<NT>(res, a.H, nw, a.eps, G0, ng, a.bf16r != 0, rms, xf, gsx, gsum, gsq);
       fused = true;
     }
-  } else if (p.type == PH_O) {
+  } else if (ptype == PH_O) {
     // the attention splits of the kv heads whose outputs this unit reads
     if (threadIdx.x == 0) {
       const uint32_t G = a.n_q / a.n_kv, ntile = num_tiles((a.n_q + 2 * a.n_kv) * a.hd);
@@ -560,9 +570,9 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
   // the split-0 O / down unit adds the previous residual once: fetch it now
   // (into the dead staging area) so the load overlaps the MMAs
   float* rpre = reinterpret_cast<float*>(xs);
-  const bool add_res = (p.type == PH_O || p.type == PH_DN) && split == 0;
+  const bool add_res = (ptype == PH_O || ptype == PH_DN) && split == 0;
   if (add_res) {
-    const uint32_t vin = p.type == PH_O ? 2 * p.layer : 2 * p.layer + 1;
+    const uint32_t vin = ptype == PH_O ? 2 * p.layer : 2 * p.layer + 1;
     for (uint32_t i = threadIdx.x; i < kTileRows * bc; i += blockDim.x) {
       const uint32_t rl = i / bc, b = i % bc, row = tile * kTileRows + rl;
       rpre[i] = row < p.M ? __ldcg(&resv(a, vin)[(size_t)b * a.H + row]) : 0.f;
@@ -578,13 +588,17 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
 #pragma unroll
       for (int v = 0; v < 16; ++v) y[s][n][v] = 0.f;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + c.S->bars);
-  for (uint32_t gl = c.warp; gl < ng; gl += kQmvWarps) {
+  // ring items: one scale group (of each matrix of the pair), or two
+  // adjacent groups of the LM head (one copy fills the whole slot)
+  const uint32_t gpi = groups_per_item(ptype, ng), items = ng / gpi;
+  for (uint32_t it = c.warp; it < items; it += kQmvWarps) {
     const uint32_t slot = c.k % a.nslot;
     if (!c.failed) c.failed = !mbar_wait_abort(&bars[c.warp * kMaxSlots + slot], (c.k / a.nslot) & 1u, a.err, &a.bar[2]);
-    if (gl == (uint32_t)c.warp) stamp(c, p, u, 6);
+    if (it == (uint32_t)c.warp) stamp(c, p, u, 6);
     const uint8_t* sb = sm + c.S->ring + (size_t)(c.warp * a.nslot + slot) * c.S->slot_bytes;
-    qmv_group<FMT, NT, SUB, BF16S>(sb, c.seg, xf, gl, cpg, gsx, gsum, gsq, y);
-    if (gl == (uint32_t)c.warp) stamp(c, p, u, 7);
+    for (uint32_t j = 0; j < gpi; ++j)
+      qmv_group<FMT, NT, SUB, BF16S>(sb + j * c.seg, c.seg, xf, it * gpi + j, cpg, gsx, gsum, gsq, y);
+    if (it == (uint32_t)c.warp) stamp(c, p, u, 7);
     __syncwarp();
     if (c.lane == 0) prod_issue(c, slot);
     ++c.k;
@@ -608,7 +622,7 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
   stamp(c, p, u, 4);
   const uint32_t nv = nrow * bc;
   const uint32_t qd = a.n_q * a.hd, qkv_rows = qd + 2 * a.n_kv * a.hd;
-  if (p.type == PH_LM) {
+  if (ptype == PH_LM) {
     // unsplit: final logits of this tile, argmax per row
     float* lg = a.logits;
     for (uint32_t b = 0; b < bc; ++b) {
@@ -640,11 +654,11 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
       float v = 0.f;
 #pragma unroll
       for (int w = 0; w < kQmvWarps; ++w) v += red[(size_t)w * nv + i];
-      switch (p.type) {
+      switch (ptype) {
         case PH_QKV: atomicAdd(&a.qkv_acc[(size_t)b * qkv_rows + row], v); break;
         case PH_GU: atomicAdd(&a.gu_acc[((size_t)b * 2 + s) * a.I + row], v); break;
         default: {   // O / DN: residual versions
-          const uint32_t vin = p.type == PH_O ? 2 * p.layer : 2 * p.layer + 1;
+          const uint32_t vin = ptype == PH_O ? 2 * p.layer : 2 * p.layer + 1;
           if (add_res) v += rpre[i];
           atomicAdd(&resv(a, vin + 1)[(size_t)b * a.H + row], v);
         }
@@ -652,8 +666,8 @@ __device__ void qmv_unit(Ctx& c, const PhaseInfo& p, uint32_t u, bool prologue =
     }
   }
   __syncthreads();
-  if (p.type == PH_QKV) dep_signal(&a.dep[tile]);
-  if (p.type == PH_GU) dep_signal(&a.dep[num_tiles((a.n_q + 2 * a.n_kv) * a.hd) + a.batch * a.n_kv + tile]);
+  if (ptype == PH_QKV) dep_signal(&a.dep[tile]);
+  if (ptype == PH_GU) dep_signal(&a.dep[num_tiles((a.n_q + 2 * a.n_kv) * a.hd) + a.batch * a.n_kv + tile]);
   stamp(c, p, u, 5);
 }
 
@@ -1193,9 +1207,10 @@ std::vector<unsigned long long> mega_weight_stream(const MegaArgs& a, int fmt, u
         for (uint32_t u = cta; u < p.units; u += grid) {
           uint32_t tile, split, G0, ng;
           unit_range(p, u, &tile, &split, &G0, &ng);
-          for (uint32_t gl = w; gl < ng; gl += kQmvWarps) {
-            const uint8_t* src = p.w + ((size_t)tile * p.groups + G0 + gl) * (p.sub * seg);
-            list.push_back(reinterpret_cast<unsigned long long>(src) | (p.sub == 2 ? 1ull : 0ull));
+          const uint32_t gpi = groups_per_item(p.type, ng);
+          for (uint32_t it = w; it < ng / gpi; it += kQmvWarps) {
+            const uint8_t* src = p.w + ((size_t)tile * p.groups + G0 + it * gpi) * (p.sub * seg);
+            list.push_back(reinterpret_cast<unsigned long long>(src) | (p.sub * gpi == 2 ? 1ull : 0ull));
           }
         }
       }
