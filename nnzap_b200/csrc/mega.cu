@@ -1164,9 +1164,11 @@ bool mega_plan(MegaArgs& a, int fmt, int bf16s, int device, uint32_t* grid, uint
     a.ks_gu = pick(a.I, a.H);
     a.ks_dn = pick(a.H, a.I);
     // attention splits
-    // splits of up to 64 positions (two streamed blocks), at most 32: one
-    // block per split moves the cost into the O phase's merge
-    uint32_t sp = (a.max_ctx + 63) / 64;
+    // one split per 40 positions of the maximum context, at most 32: with
+    // 512-768 cached positions of a 776-position cache that is ~1.3 streamed
+    // blocks per split (13 splits of two blocks cost ~45 us per token more;
+    // 20-32 splits measure alike, the merge in the O phase growing with them)
+    uint32_t sp = (a.max_ctx + 39) / 40;
     if (const char* e = getenv("NNZ_ATT_SPLITS")) sp = (uint32_t)atoi(e);   // tuning override
     a.att_splits = sp < 1 ? 1 : sp > (uint32_t)kMaxAttSplits ? (uint32_t)kMaxAttSplits : sp;
     for (uint32_t ns = kMaxSlots; ns >= 2; --ns) {
