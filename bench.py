@@ -321,6 +321,105 @@ def run_config4(args):
         torch.distributed.barrier()
 
 
+def tokenizer_text(seed: int, nbytes: int) -> bytes:
+    """Seeded synthetic prompt text: syllable words, numbers, punctuation,
+    contractions, accented / CJK / emoji runs, tabs, newlines and the chat
+    special tokens (the reference's bench prompt text is replaced by this)."""
+    import random
+    rng = random.Random(seed)
+    syl = [a + b for a in "bcdfghjklmnprstvwz" for b in "aeiou"]
+    words = ["".join(rng.choice(syl) for _ in range(rng.randint(1, 4))) for _ in range(2000)]
+    extra = ["é", "日本", "中文", "😀", "—", "…", "don't", "it's", "(x)", "!?", "\n", "\t",
+             "<|im_start|>", "<|im_end|>", "  "]
+    out, n = [], 0
+    while n < nbytes:
+        r = rng.random()
+        w = rng.choice(words) if r < 0.8 else str(rng.randint(0, 99999)) if r < 0.88 else rng.choice(extra)
+        piece = (" " + w).encode()
+        out.append(piece)
+        n += len(piece)
+    return b"".join(out)[:nbytes]
+
+
+def run_tokenizer(args):
+    """Host workload: BPE encode throughput of the library's C++ tokenizer
+    (value) and through the Python mirror (e2e) on ~1 MiB of text, with the
+    oracle (the literal restatement of the reference's tokenizer) timed on a
+    bounded sample beside it."""
+    rank, world, _ = rank_env()
+    if rank != 0:
+        return
+    from oracle import tokenizer_ref as R
+    js = (ROOT / "tests" / "golden" / "tokenizer_synth.json").read_bytes()
+    text = tokenizer_text(0, 1 << 20)
+    mb = len(text) / 1e6
+    sample = text[: 64 << 10]
+    ref = R.Tokenizer(js)
+
+    def time_ref():
+        t0 = time.perf_counter()
+        ref.encode(sample)
+        return len(sample) / 1e6 / (time.perf_counter() - t0)
+
+    cfg = {"workload": "BPE encode (tokenizer.zig encode): 1 MiB of seeded synthetic text incl. "
+                       "UTF-8 and chat special tokens", "tokenizer": "synthetic byte-level BPE, "
+                       "3000 entries, 2740 merges (tests/golden/tokenizer_synth.json)",
+           "global_batch": 1, "parallelism": "host, 1 thread"}
+    ref_note = (f"oracle/tokenizer_ref.py (pure Python, the reference's algorithm and data "
+                f"structures) encoding the first {len(sample)} bytes")
+    if args.impl == "reference":
+        for _ in range(args.warmup):
+            time_ref()
+        vals = [time_ref() for _ in range(args.steps)]
+        v = statistics.median(vals)
+        print(json.dumps({
+            "impl": "reference", "metric": "tokenizer_encode_mb_per_sec", "value": v, "unit": "MB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": len(sample) / 1e6 / v * 1000, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u8", "data": "synthetic", "config": cfg,
+            "cpu_baseline": {"value": v, "unit": "MB/s", "cores": 1, "kind": "port", "sample": ref_note},
+            "e2e": {"value": v, "unit": "MB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return
+    import ctypes as C
+    from nnzap_b200 import _capi
+    from nnzap_b200.tokenizer import Tokenizer
+    tok = Tokenizer.from_json(js)
+    L = _capi.lib()
+    out = np.empty(len(text) + 1, np.uint32)
+    n = C.c_uint32()
+
+    def step_lib():
+        t0 = time.perf_counter()
+        _capi.check(L.nnz_tokenizer_encode(tok._h, text, len(text), out.ctypes.data, len(out), C.byref(n)))
+        return time.perf_counter() - t0
+
+    def step_py():
+        t0 = time.perf_counter()
+        tok.encode(text)
+        return time.perf_counter() - t0
+
+    for _ in range(args.warmup):
+        step_lib()
+        step_py()
+    lib_t = [step_lib() for _ in range(args.steps)]
+    py_t = [step_py() for _ in range(args.steps)]
+    assert out[: n.value].tolist() == ref.encode(text[:0]) + tok.encode(text)   # same ids both ways
+    ms = statistics.median(lib_t) * 1000
+    cpu = None if args.no_cpu_baseline else {
+        "value": time_ref(), "unit": "MB/s", "cores": 1, "kind": "port", "sample": ref_note}
+    print(json.dumps({
+        "metric": "tokenizer_encode_mb_per_sec", "value": mb / (ms / 1000), "unit": "MB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic", "config": cfg, "tokens_per_step": int(n.value),
+        "cpu_baseline": cpu,
+        "e2e": {"value": mb / statistics.median(py_t), "unit": "MB/s (Tokenizer.encode -> list)",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0, "note": "host-only row: the tokenizer runs on the CPU in the reference "
+                                   "and here (C++ in libnnz_b200.so)"}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -328,11 +427,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="config3", choices=["config3", "config4"],
+    ap.add_argument("--workload", default="config3", choices=["config3", "config4", "tokenizer"],
                     help="config3: b=1 generate (default, replicas for N>1); config4: batch-64 "
-                         "decode at KV 4096, tensor-parallel over the N GPUs")
+                         "decode at KV 4096, tensor-parallel over the N GPUs; tokenizer: host BPE "
+                         "encode throughput")
     ap.add_argument("--quant", default="q1", choices=["q1", "q4"], help="config4 weights")
     args = ap.parse_args()
+    if args.workload == "tokenizer":
+        run_tokenizer(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

@@ -29,7 +29,8 @@ enum {
   NNZ_ENOTFOUND = -5,  /* tensor missing at finalize (TensorNotFound)          */
   NNZ_ESTATE = -6,     /* call order violated (e.g. decode before finalize)   */
   NNZ_EDEVICE = -7,    /* a kernel raised a device error flag                 */
-  NNZ_ENCCL = -8       /* NCCL failure (tensor-parallel path)                 */
+  NNZ_ENCCL = -8,      /* NCCL failure (tensor-parallel path)                 */
+  NNZ_ERANGE = -9      /* caller's output buffer too small (OutputBufferTooSmall) */
 };
 
 /* ---- enums ------------------------------------------------------------ */
@@ -274,6 +275,64 @@ int nnz_attn_decode(const void* qkv, const float* q_norm, const float* k_norm, v
                     void* v_cache, uint32_t max_ctx, const int32_t* positions, uint32_t rows,
                     uint32_t n_q, uint32_t n_kv, uint32_t head_dim, float eps, float theta,
                     int rope_style, uint32_t splits, void* out, void* stream);
+
+/* ---- tokenizer: replaces Tokenizer of nnmetal/src/tokenizer.zig ------ */
+/* Byte-level BPE over a HuggingFace tokenizer.json (Qwen3 format).  Host
+ * code only (no device calls).  A tokenizer is immutable after creation:
+ * encode / decode / chat-template calls may run concurrently on one handle.
+ * Errors return NNZ_EINVAL (or NNZ_ERANGE / NNZ_ENOTFOUND where stated) and
+ * nnz_last_error() starts with the reference's error name (InvalidJson,
+ * MissingField, InvalidVocabEntry, VocabTooLarge, InvalidMergeEntry,
+ * InputTooLong, ChunkTooLong, UnknownByte, UnknownTokenId, ...).
+ * Limits as in the reference (tokenizer.zig:28-46): token ids < 200000,
+ * <= 200000 merges, <= 256 special tokens (later ones are ignored), encode
+ * input <= 1 MiB, pre-tokenized chunks <= 512 bytes, files <= 32 MiB. */
+typedef struct nnz_tokenizer nnz_tokenizer;
+
+typedef struct nnz_tokenizer_info {
+  uint32_t vocab_size;          /* one past the highest id seen */
+  uint32_t special_token_count;
+  uint32_t eos_token_id;        /* "<|endoftext|>", 0 if absent */
+  uint32_t im_start_token_id;   /* "<|im_start|>", 0 if absent  */
+  uint32_t im_end_token_id;     /* "<|im_end|>", 0 if absent    */
+  uint32_t merge_count;         /* entries of model.merges      */
+} nnz_tokenizer_info;
+
+/* Tokenizer.initFromJson (tokenizer.zig:195-229): parse an in-memory
+ * tokenizer.json (model.vocab, model.merges in "a b" or ["a", "b"] form,
+ * added_tokens). */
+int nnz_tokenizer_from_json(const char* json, size_t len, nnz_tokenizer** out);
+/* Tokenizer.init (tokenizer.zig:164-193): read and parse a file
+ * (NNZ_ENOTFOUND if it cannot be opened). */
+int nnz_tokenizer_from_file(const char* path, nnz_tokenizer** out);
+/* Tokenizer.deinit (tokenizer.zig:232-242). */
+int nnz_tokenizer_free(nnz_tokenizer* tok);
+/* The fields Tokenizer exposes (vocab_size, special_token_count,
+ * eos/im_start/im_end ids; tokenizer.zig:124-156). */
+int nnz_tokenizer_get_info(const nnz_tokenizer* tok, nnz_tokenizer_info* info);
+/* Tokenizer.encode (tokenizer.zig:247-289): special tokens matched longest
+ * first, other text pre-tokenized and BPE-merged per chunk.  Writes at most
+ * cap ids (NNZ_ERANGE when they do not fit; len + 1 always suffices). */
+int nnz_tokenizer_encode(const nnz_tokenizer* tok, const char* text, size_t len, uint32_t* ids,
+                         uint32_t cap, uint32_t* n_out);
+/* Tokenizer.decode (tokenizer.zig:293-324): raw bytes of the ids (NNZ_ERANGE
+ * when the next token's vocabulary string is longer than the room left). */
+int nnz_tokenizer_decode(const nnz_tokenizer* tok, const uint32_t* ids, uint32_t n, char* out,
+                         size_t cap, size_t* n_out);
+/* Tokenizer.applyChatTemplate (tokenizer.zig:330-370):
+ * <|im_start|>user\n{prompt}<|im_end|>\n<|im_start|>assistant\n
+ * (len + 32 ids always suffice). */
+int nnz_tokenizer_chat_template(const nnz_tokenizer* tok, const char* prompt, size_t len,
+                                uint32_t* ids, uint32_t cap, uint32_t* n_out);
+/* Tokenizer.bpeMerge (tokenizer.zig:761-800): greedy lowest-rank merging of
+ * ids[0..n) in place; *n_out = the merged length. */
+int nnz_tokenizer_bpe_merge(const nnz_tokenizer* tok, uint32_t* ids, uint32_t n, uint32_t* n_out);
+/* id_to_vocab[id] (the token's vocabulary string, byte-level form);
+ * NNZ_ERANGE if longer than cap, UnknownTokenId if unused. */
+int nnz_tokenizer_token(const nnz_tokenizer* tok, uint32_t id, char* out, size_t cap, size_t* n_out);
+/* nextPretokenChunk (tokenizer.zig:936-994): byte length of the first
+ * pre-tokenizer chunk of text[0..len) (0 when len == 0). */
+uint32_t nnz_pretoken_chunk(const char* text, size_t len);
 
 #ifdef __cplusplus
 }

@@ -14,7 +14,7 @@ import os
 LIB_PATH = Path(os.environ.get("NNZ_LIB_PATH") or Path(__file__).resolve().parent / "_lib" / "libnnz_b200.so")
 
 NNZ_OK, NNZ_EINVAL, NNZ_ECUDA, NNZ_ENOMEM, NNZ_ETIMEDOUT = 0, -1, -2, -3, -4
-NNZ_ENOTFOUND, NNZ_ESTATE, NNZ_EDEVICE, NNZ_ENCCL = -5, -6, -7, -8
+NNZ_ENOTFOUND, NNZ_ESTATE, NNZ_EDEVICE, NNZ_ENCCL, NNZ_ERANGE = -5, -6, -7, -8, -9
 NNZ_Q1, NNZ_Q4 = 0, 1
 NNZ_ROPE_PAIRWISE, NNZ_ROPE_HALF_SPLIT = 0, 1
 NNZ_SCALE_F16, NNZ_SCALE_BF16 = 0, 1
@@ -23,7 +23,8 @@ NNZ_OUT_F16, NNZ_OUT_F32, NNZ_OUT_F32_ADD = 0, 1, 2
 
 _ERRNAMES = {NNZ_EINVAL: "EINVAL", NNZ_ECUDA: "ECUDA", NNZ_ENOMEM: "ENOMEM",
              NNZ_ETIMEDOUT: "ETIMEDOUT", NNZ_ENOTFOUND: "ENOTFOUND", NNZ_ESTATE: "ESTATE",
-             NNZ_EDEVICE: "EDEVICE", NNZ_ENCCL: "ENCCL"}
+             NNZ_EDEVICE: "EDEVICE", NNZ_ENCCL: "ENCCL",
+             NNZ_ERANGE: "ERANGE"}
 
 
 class NnzError(RuntimeError):
@@ -47,6 +48,12 @@ class NnzGenerateOpts(C.Structure):
                 ("output_tokens", C.POINTER(C.c_uint32)), ("max_new", C.c_uint32),
                 ("per_token_ns", C.POINTER(C.c_uint64)), ("temperature", C.c_float),
                 ("top_k", C.c_uint32), ("top_p", C.c_float), ("uniforms", C.POINTER(C.c_float))]
+
+
+class NnzTokenizerInfo(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in (
+        "vocab_size", "special_token_count", "eos_token_id", "im_start_token_id",
+        "im_end_token_id", "merge_count")]
 
 
 class NnzGenerateResult(C.Structure):
@@ -90,6 +97,16 @@ SIGNATURES = [
     ("nnz_mlp", I32, [I32, I32, I32, P, P, U32, U32, U32, P, U32, P, P]),
     ("nnz_prefill_gemm", I32, [I32, I32, P, P, P, U32, U32, U32, U32, P, P, I32, P]),
     ("nnz_attn_decode", I32, [P, P, P, P, P, U32, P, U32, U32, U32, U32, F32, F32, I32, U32, P, P]),
+    ("nnz_tokenizer_from_json", I32, [C.c_char_p, SZ, P]),
+    ("nnz_tokenizer_from_file", I32, [C.c_char_p, P]),
+    ("nnz_tokenizer_free", I32, [P]),
+    ("nnz_tokenizer_get_info", I32, [P, P]),
+    ("nnz_tokenizer_encode", I32, [P, C.c_char_p, SZ, P, U32, P]),
+    ("nnz_tokenizer_decode", I32, [P, P, U32, P, SZ, P]),
+    ("nnz_tokenizer_chat_template", I32, [P, C.c_char_p, SZ, P, U32, P]),
+    ("nnz_tokenizer_bpe_merge", I32, [P, P, U32, P]),
+    ("nnz_tokenizer_token", I32, [P, U32, P, SZ, P]),
+    ("nnz_pretoken_chunk", U32, [C.c_char_p, SZ]),
 ]
 
 _lib = None
