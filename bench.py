@@ -354,9 +354,9 @@ def run_tokenizer(args):
     text = tokenizer_text(0, 1 << 20)
     mb = len(text) / 1e6
     sample = text[: 64 << 10]
-    ref = R.Tokenizer(js)
 
     def time_ref():
+        ref = R.Tokenizer(js)
         t0 = time.perf_counter()
         ref.encode(sample)
         return len(sample) / 1e6 / (time.perf_counter() - t0)
@@ -404,7 +404,7 @@ def run_tokenizer(args):
         step_py()
     lib_t = [step_lib() for _ in range(args.steps)]
     py_t = [step_py() for _ in range(args.steps)]
-    assert out[: n.value].tolist() == ref.encode(text[:0]) + tok.encode(text)   # same ids both ways
+    assert out[: n.value].tolist() == tok.encode(text)   # same ids through both entry points
     ms = statistics.median(lib_t) * 1000
     cpu = None if args.no_cpu_baseline else {
         "value": time_ref(), "unit": "MB/s", "cores": 1, "kind": "port", "sample": ref_note}
