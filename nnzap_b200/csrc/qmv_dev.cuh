@@ -212,11 +212,15 @@ __device__ __forceinline__ void norm_quant_row128(const float* res, uint32_t K, 
   if (lane == 0) atomicAdd(&rms[0], ss);
   __syncthreads();
   const float rr = rsqrtf(rms[0] / (float)K + eps);
-#pragma unroll
+  // one copy of the quantiser, run for each of this warp's groups in the
+  // unit (the group's registers picked by selects, not by indexing)
+#pragma unroll 1
   for (int u = 0; u < kItems; ++u) {
     const uint32_t g = warp + 4 * u;
     if (g < G0 || g >= G0 + ng || threadIdx.x + u * kQmvThreads >= q4) continue;   // warp-uniform
-    float x[4] = {v[u].x * rr * w[u].x, v[u].y * rr * w[u].y, v[u].z * rr * w[u].z, v[u].w * rr * w[u].w};
+    const float4 vu = u == 0 ? v[0] : u == 1 ? v[1] : u == 2 ? v[2] : v[3];
+    const float4 wu = u == 0 ? w[0] : u == 1 ? w[1] : u == 2 ? w[2] : w[3];
+    float x[4] = {vu.x * rr * wu.x, vu.y * rr * wu.y, vu.z * rr * wu.z, vu.w * rr * wu.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       if (bf16r) x[i] = bf16_trunc(x[i]);
