@@ -162,12 +162,6 @@ __host__ __device__ inline MegaSmem mega_layout(const MegaArgs& a, int fmt) {
 // on (results are then garbage, but every CTA terminates).
 constexpr uint32_t kGridSpinLimit = 1u << 20;
 
-__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
-  unsigned int v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 __device__ __forceinline__ unsigned int ld_relaxed(const unsigned int* p) {
   unsigned int v;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -786,7 +780,7 @@ __device__ void att_unit(Ctx& c, const PhaseInfo& p, uint32_t u, uint32_t (&ause
 
   stamp(c, p, u, 0);
   const AttGeom ag = att_geom(c, p, u);
-  const int pos = ag.pos, t0 = ag.t0, ncache = ag.ncache, nblk = ag.nblk;
+  const int pos = ag.pos, ncache = ag.ncache, nblk = ag.nblk;
   const bool own_new = ag.own_new;
   const size_t head_off = ag.head_off;
   auto issue = [&](int blk) { att_issue<HD>(c, ag, blk); };

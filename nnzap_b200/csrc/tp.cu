@@ -71,11 +71,9 @@ __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(float* residua
   __threadfence_system();
   __syncthreads();
   // 2. raise this slice's flag on every peer, 3. wait for theirs
-  __shared__ uint32_t s_c;
   if (threadIdx.x == 0) {
     const uint32_t cnt = flags[c * stride + T] + 1;
     flags[c * stride + T] = cnt;
-    s_c = cnt;
     for (int j = 0; j < T; ++j)
       if (j != rank)
         asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peer_flags[j] + c * stride + rank), "r"(cnt)
