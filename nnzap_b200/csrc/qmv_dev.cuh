@@ -342,9 +342,8 @@ __device__ __forceinline__ void qmv_group(const uint8_t* sb, uint32_t seg, const
 #pragma unroll
           for (int j = 0; j < 8; ++j) D[j][0] = D[j][1] = D[j][2] = D[j][3] = 0;
           const uint8_t* xb = xf + ((size_t)(gl * cpg * NT + n) * 32 + lane) * 8;
-          if (SUB == 1 && cpg == 4) {
+          if (cpg == 4) {
             // common case (group 128): every operand load issued up front
-            // (single-matrix units only: the gate/up pair would spill)
             uint4 A[4];
             uint2 B[4];
 #pragma unroll
