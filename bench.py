@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark: Bonsai-1.7B-shaped 1-bit (Q1 g128) greedy decode at batch 1.
 
-Workload: random-init 28-layer Qwen3-1.7B architecture
+Workload (benchmark configuration 3, the full model): random-init 28-layer Qwen3-1.7B architecture
 with packed 1-bit weights and a tied 1-bit embedding, a 512-token prompt
 (ids uniform from seed 0, tokenizer bypassed) prefilled, then 256 greedy
 tokens.  One "step" = one generate() call = prefill 512 + decode 256.
@@ -191,7 +191,7 @@ def run_reference(args):
 
 
 def qmv_config0(torch, iters=200):
-    """Standalone BASELINE config 0 QMV (Q4 6144x2048 g64, fp16 in/out)
+    """Standalone benchmark configuration 0: one QMV (Q4 6144x2048 g64, fp16 in/out)
     rotating through weight copies larger than L2."""
     from nnzap_b200 import synth
     from nnzap_b200._capi import check, lib, ptr
@@ -226,7 +226,7 @@ C4_BATCH, C4_CTX = 64, 4096
 
 
 def run_config4(args):
-    """64 sequences decoded together with a 4096-position
+    """Benchmark configuration 4: 64 sequences decoded together with a 4096-position
     KV cache, tensor-parallel over the job's GPUs (tp = N: heads, gate/up
     rows and vocabulary split, NCCL all-reduce after o/down inside the decode
     graph).  A step = one decode step of all 64 rows; positions start at

@@ -159,7 +159,7 @@ int nnz_model_write_kv(nnz_model* m, uint32_t layer, uint32_t slot, const uint16
 /* Read back the same region (tests). */
 int nnz_model_read_kv(nnz_model* m, uint32_t layer, uint32_t slot, uint16_t* k, uint16_t* v,
                       uint32_t len);
-/* One decoder layer decode step on the model's state:
+/* One decoder layer decode step on the model's state (benchmark configuration 2):
  * residual (host f32 [batch][hidden]) is updated in place, `positions` give
  * each row's position; row r uses KV slot r. */
 int nnz_model_layer_step(nnz_model* m, uint32_t layer, float* residual,
@@ -248,7 +248,7 @@ int nnz_lm_head_argmax(int fmt, int scale_dtype, int bf16_round, const void* pac
                        uint32_t K, uint32_t gs, const float* residual, const float* norm_w,
                        float eps, uint32_t batch, float* logits, uint32_t* argmax_out,
                        void* stream);
-/* Fused MLP block: out_f32[b] = down(SiLU(gate x) * up x).
+/* Fused MLP block (benchmark configuration 1): out_f32[b] = down(SiLU(gate x) * up x).
  * gate_up is packed with sub = 2 (gate = sub 0, up = sub 1); x fp16
  * [batch][K]; h_scratch fp16 [batch][M_inter] may be NULL (workspace).
  * Replaces qmv_spec_fused_pair_silu_f16io + qmv_spec_mg_f16io_resadd

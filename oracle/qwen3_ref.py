@@ -391,7 +391,7 @@ def greedy_check(cfg: Cfg, W: dict, prompt, generated, tol: float = 2e-2):
 
 
 def mlp_block(cfg: Cfg, gate: dict, up: dict, down: dict, x: np.ndarray) -> np.ndarray:
-    """BASELINE config 1 block: down(SiLU(gate x) * up x) with the engine's
+    """Benchmark configuration 1 block: down(SiLU(gate x) * up x) with the engine's
     fp16 rounding of the SiLU*mul output (qmv_specialized.metal:1268-1276)."""
     g = qmv(cfg, gate, cfg.inter, cfg.hidden, x)
     u = qmv(cfg, up, cfg.inter, cfg.hidden, x)

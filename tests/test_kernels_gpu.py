@@ -145,7 +145,7 @@ def test_lm_head_argmax(cuda, built_lib):
 
 @pytest.mark.parametrize("fmt,batch", [(0, 1), (0, 8), (1, 1), (1, 8)])
 def test_mlp_block_config1(cuda, built_lib, fmt, batch):
-    """BASELINE config 1 (Q1) and its 4-bit twin: down(SiLU(gate x) * up x)."""
+    """Benchmark configuration 1 (Q1) and its 4-bit twin: down(SiLU(gate x) * up x)."""
     torch = cuda
     H, I = 2048, 6144
     gs = 128 if fmt == 0 else 64

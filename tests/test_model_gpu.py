@@ -132,7 +132,7 @@ def test_batched_decode_rows_independent(cuda, built_lib, path):
 
 
 def test_layer_step_config2_q4(cuda, built_lib):
-    """one 4-bit g64 decoder layer, KV 2048 filled N(0,1)."""
+    """Benchmark configuration 2: one 4-bit g64 decoder layer, KV 2048 filled N(0,1)."""
     d = synth.ModelDims(vocab=256, layers=1, quant="q4", gs=64)
     m, W = build(d, max_ctx=2049, max_batch=1)
     cfg = oracle_cfg(d)
@@ -168,7 +168,7 @@ def test_layer_step_config2_q4(cuda, built_lib):
 
 @pytest.mark.parametrize("path", ["persistent", "graph"])
 def test_full_bonsai_q1_generate(cuda, built_lib, path):
-    """BASELINE config 3 shape (28 layers, vocab 151936), short run."""
+    """Benchmark configuration 3 shape (28 layers, vocab 151936), short run."""
     d = synth.BONSAI_1_7B_Q1
     m, W = build(d, max_ctx=1024, max_batch=1, path=path)
     cfg = oracle_cfg(d)
