@@ -420,3 +420,26 @@ def test_memo_does_not_leak_between_tokenizers(built_lib):
     a.t.close()
     c = Lib(b_js)
     assert c.encode(b"abab") == [0, 1, 0, 1]
+
+
+def test_large_random_vocabulary_matches_oracle(built_lib):
+    # ~40k random merges over the 256 byte tokens (deep merge chains, many
+    # competing ranks): library == oracle on random text, and the round trip
+    rng = random.Random(11)
+    base = [chr(R.BYTE_FWD[b]) for b in range(256)]
+    vocab = {s: i for i, s in enumerate(base)}
+    merges, toks = [], list(base)
+    while len(vocab) < 40000:
+        a, b = rng.choice(toks), rng.choice(toks)
+        if len(a) + len(b) > 12 or (a + b) in vocab:
+            continue
+        vocab[a + b] = len(vocab)
+        toks.append(a + b)
+        merges.append([a, b])
+    js = tok_json(vocab, merges, [{"id": 40000, "content": "<|im_end|>", "special": True}])
+    lib, ref = Lib(js), R.Tokenizer(js)
+    assert lib.vocab_size == ref.vocab_size == 40001
+    for text in random_texts(7, 60):
+        ids = lib.encode(text)
+        assert ids == ref.encode(text)
+        assert lib.decode(ids) == text
