@@ -330,6 +330,9 @@ int nnz_tokenizer_bpe_merge(const nnz_tokenizer* tok, uint32_t* ids, uint32_t n,
 /* id_to_vocab[id] (the token's vocabulary string, byte-level form);
  * NNZ_ERANGE if longer than cap, UnknownTokenId if unused. */
 int nnz_tokenizer_token(const nnz_tokenizer* tok, uint32_t id, char* out, size_t cap, size_t* n_out);
+/* decodeTokenToBytes (tokenizer.zig:1066-1108): raw bytes of one token
+ * string in byte-level form (len bytes; cap >= len always suffices). */
+int nnz_token_to_bytes(const char* token, size_t len, char* out, size_t cap, size_t* n_out);
 /* nextPretokenChunk (tokenizer.zig:936-994): byte length of the first
  * pre-tokenizer chunk of text[0..len) (0 when len == 0). */
 uint32_t nnz_pretoken_chunk(const char* text, size_t len);

@@ -106,6 +106,7 @@ SIGNATURES = [
     ("nnz_tokenizer_chat_template", I32, [P, C.c_char_p, SZ, P, U32, P]),
     ("nnz_tokenizer_bpe_merge", I32, [P, P, U32, P]),
     ("nnz_tokenizer_token", I32, [P, U32, P, SZ, P]),
+    ("nnz_token_to_bytes", I32, [C.c_char_p, SZ, P, SZ, P]),
     ("nnz_pretoken_chunk", U32, [C.c_char_p, SZ]),
 ]
 

@@ -811,6 +811,14 @@ int nnz_tokenizer_token(const nnz_tokenizer* tok, uint32_t id, char* out, size_t
   return NNZ_OK;
 }
 
+int nnz_token_to_bytes(const char* token, size_t len, char* out, size_t cap, size_t* n_out) {
+  if (!n_out || (!token && len) || (!out && cap)) return fail(NNZ_EINVAL, "nnz_token_to_bytes: null argument");
+  *n_out = 0;
+  if (cap < len) return fail(NNZ_ERANGE, "OutputBufferTooSmall");
+  if (len) *n_out = token_to_bytes(std::string(token, len), out);
+  return NNZ_OK;
+}
+
 uint32_t nnz_pretoken_chunk(const char* text, size_t len) {
   if (!text || len == 0) return 0;
   const uint32_t n = len > kMaxInput ? (uint32_t)kMaxInput : (uint32_t)len;

@@ -51,6 +51,16 @@ def next_pretoken_chunk(text: str | bytes) -> int:
     return int(capi.lib().nnz_pretoken_chunk(b, len(b)))
 
 
+def decode_token_to_bytes(token: str | bytes) -> bytes:
+    """Raw bytes of one byte-level token string (decodeTokenToBytes,
+    tokenizer.zig:1066)."""
+    b = _as_bytes(token)
+    buf = C.create_string_buffer(max(1, len(b)))
+    n = C.c_size_t()
+    _check(capi.lib().nnz_token_to_bytes(b, len(b), buf, len(buf), C.byref(n)))
+    return buf.raw[: n.value]
+
+
 class Tokenizer:
     """A loaded tokenizer.json (immutable; safe to share between threads)."""
 

@@ -213,6 +213,20 @@ def test_decode_token_bytes(built_lib, impl):
     assert t.decode([2, 0]) == b" hellohello"
 
 
+def test_decode_token_to_bytes_function(built_lib):
+    # tokenizer_test.zig:392-408, literally: "hello" -> "hello"; U+0120 -> " "
+    from nnzap_b200.tokenizer import decode_token_to_bytes
+    for f in (decode_token_to_bytes, R.decode_token_to_bytes):
+        assert f(b"hello") == b"hello"
+        assert f(bytes([0xC4, 0xA0])) == b" "
+        assert f(bytes([0xE2, 0x82, 0xAC])) == "€".encode()       # not in the byte map: passes through
+        assert f(bytes([0xC4])) == bytes([0xC4])                 # cut-short sequence: raw byte
+    rng = random.Random(9)
+    for _ in range(500):
+        t = bytes(rng.randrange(256) for _ in range(rng.randint(1, 10)))
+        assert decode_token_to_bytes(t) == R.decode_token_to_bytes(t)
+
+
 @pytest.mark.parametrize("impl", IMPLS)
 def test_merge_priority_lowest_rank(built_lib, impl):
     # tokenizer_test.zig:410-443
