@@ -23,6 +23,7 @@
 #include <string>
 #include <string_view>
 #include <unordered_map>
+#include <unordered_set>
 #include <utility>
 #include <vector>
 
@@ -87,8 +88,8 @@ void utf8_append(std::string& s, uint32_t cp) {
 
 // ---- minimal JSON reader ----------------------------------------------------
 // Objects keep their member order (the vocabulary is read in file order, as
-// the reference's std.json ObjectMap iterates it); a repeated key keeps its
-// last value.  Strings are validated UTF-8 with \u escapes (surrogate pairs
+// the reference's std.json ObjectMap iterates it); a repeated member name is
+// an error (InvalidJson).  Strings are validated UTF-8 with \u escapes (surrogate pairs
 // joined); numbers are integers when written without fraction or exponent
 // and within int64, else doubles.
 struct JVal {
@@ -162,7 +163,6 @@ class JsonReader {
     ++p_;
     ws();
     if (p_ < end_ && *p_ == '}') { ++p_; return true; }
-    std::unordered_map<std::string, size_t> seen;
     for (;;) {
       ws();
       if (p_ >= end_ || *p_ != '"') return bad("expected a member name");
@@ -172,20 +172,29 @@ class JsonReader {
       if (p_ >= end_ || *p_ != ':') return bad("expected ':'");
       ++p_;
       ws();
-      JVal mv;
-      if (!value(mv, depth + 1)) return false;
-      auto it = seen.find(key);
-      if (it != seen.end()) {
-        v.obj[it->second].second = std::move(mv);
-      } else {
-        seen.emplace(key, v.obj.size());
-        v.obj.emplace_back(std::move(key), std::move(mv));
-      }
+      v.obj.emplace_back(std::move(key), JVal{});
+      if (!value(v.obj.back().second, depth + 1)) return false;
       ws();
       if (p_ < end_ && *p_ == ',') { ++p_; continue; }
-      if (p_ < end_ && *p_ == '}') { ++p_; return true; }
+      if (p_ < end_ && *p_ == '}') { ++p_; return unique_members(v); }
       return bad("expected ',' or '}'");
     }
+  }
+  // A repeated member name is an error, as in the reference's JSON parser
+  // (its default duplicate-field behaviour).
+  bool unique_members(const JVal& v) {
+    const size_t n = v.obj.size();
+    if (n < 16) {
+      for (size_t i = 1; i < n; ++i)
+        for (size_t j = 0; j < i; ++j)
+          if (v.obj[i].first == v.obj[j].first) return bad("duplicate member name");
+      return true;
+    }
+    std::unordered_set<std::string_view> seen;
+    seen.reserve(2 * n);
+    for (const auto& kv : v.obj)
+      if (!seen.insert(kv.first).second) return bad("duplicate member name");
+    return true;
   }
   bool array(JVal& v, int depth) {
     v.kind = JVal::ARR;
@@ -405,19 +414,25 @@ inline uint64_t pair_key(uint32_t a, uint32_t b) { return ((uint64_t)a << 32) | 
 // full, multiplicative hash, linear probing.  Built once; read-only after.
 class PairTable {
  public:
-  void build(const std::unordered_map<uint64_t, Merge>& m) {
+  // room for up to n entries at most half full
+  void reserve(size_t n) {
     size_t cap = 16;
-    while (cap < 2 * m.size()) cap <<= 1;
+    while (cap < 2 * n) cap <<= 1;
     bits_ = 0;
     while ((size_t(1) << bits_) < cap) ++bits_;
     keys_.assign(cap, kEmpty);
     vals_.assign(cap, Merge{kNone, kNone});
-    for (const auto& kv : m) {
-      size_t i = slot(kv.first);
-      while (keys_[i] != kEmpty) i = (i + 1) & (cap - 1);
-      keys_[i] = kv.first;
-      vals_[i] = kv.second;
-    }
+    count_ = 0;
+  }
+  // insert or overwrite (a later merge entry for the same pair wins)
+  void put(uint64_t key, Merge m) {
+    if (2 * (count_ + 1) > keys_.size()) grow();
+    const size_t mask = keys_.size() - 1;
+    size_t i = slot(key);
+    while (keys_[i] != kEmpty && keys_[i] != key) i = (i + 1) & mask;
+    if (keys_[i] == kEmpty) ++count_;
+    keys_[i] = key;
+    vals_[i] = m;
   }
   const Merge* find(uint64_t key) const {
     const size_t mask = keys_.size() - 1;
@@ -430,8 +445,16 @@ class PairTable {
  private:
   static constexpr uint64_t kEmpty = ~0ull;   // ids are < 2^18: never a real key
   size_t slot(uint64_t k) const { return (size_t)((k * 0x9E3779B97F4A7C15ull) >> (64 - bits_)); }
-  std::vector<uint64_t> keys_;
-  std::vector<Merge> vals_;
+  void grow() {
+    std::vector<uint64_t> k = std::move(keys_);
+    std::vector<Merge> v = std::move(vals_);
+    reserve(k.size());   // twice the slots
+    for (size_t i = 0; i < k.size(); ++i)
+      if (k[i] != kEmpty) put(k[i], v[i]);
+  }
+  std::vector<uint64_t> keys_{std::vector<uint64_t>(16, kEmpty)};
+  std::vector<Merge> vals_{std::vector<Merge>(16, Merge{kNone, kNone})};
+  size_t count_ = 0;
   unsigned bits_ = 4;
 };
 
@@ -481,6 +504,7 @@ struct nnz_tokenizer {
     const JVal* vocab = model->get("vocab");
     if (!vocab) return fail(NNZ_EINVAL, "MissingField: 'model.vocab'");
     if (vocab->kind != JVal::OBJ) return fail(NNZ_EINVAL, "InvalidJson: 'model.vocab' is not an object");
+    vocab_to_id.reserve(vocab->obj.size() + 64);
     for (const auto& kv : vocab->obj) {
       if (kv.second.kind != JVal::INT || kv.second.i < 0 || kv.second.i > 0xFFFFFFFFll)
         return fail(NNZ_EINVAL, "InvalidVocabEntry: '" + kv.first + "'");
@@ -551,25 +575,40 @@ struct nnz_tokenizer {
     // A key "A B" ranks every id pair whose vocabulary strings are A and B,
     // for every split at a space (the reference compares joined strings);
     // pairs whose joined key exceeds its 1025-byte buffer never match there.
-    std::unordered_map<uint64_t, Merge> pairs;
-    std::unordered_map<std::string_view, std::vector<uint32_t>> ids_of;
-    for (uint32_t id = 0; id < vocab_size; ++id)
-      if (!id_to_vocab[id].empty()) ids_of[id_to_vocab[id]].push_back(id);
+    // ids by vocabulary string: one id almost always; strings shared by
+    // several ids (possible through added_tokens) keep the rest aside
+    std::unordered_map<std::string_view, uint32_t> id_of;
+    std::unordered_map<std::string_view, std::vector<uint32_t>> more_ids;
+    id_of.reserve(vocab_size);
+    for (uint32_t id = 0; id < vocab_size; ++id) {
+      if (id_to_vocab[id].empty()) continue;
+      auto [it, fresh] = id_of.emplace(id_to_vocab[id], id);
+      if (!fresh) more_ids[it->first].push_back(id);
+    }
+    auto for_ids = [&](std::string_view s, auto&& f) {
+      auto it = id_of.find(s);
+      if (it == id_of.end()) return;
+      f(it->second);
+      if (!more_ids.empty()) {
+        auto m = more_ids.find(s);
+        if (m != more_ids.end())
+          for (uint32_t id : m->second) f(id);
+      }
+    };
+    merges.reserve(keys.size());
+    std::string joined;
     for (const auto& [key, rank] : keys) {
       if (key.size() > 2 * kMaxTokenLength + 1) continue;
       for (size_t sp = key.find(' '); sp != std::string::npos; sp = key.find(' ', sp + 1)) {
         const std::string_view A(key.data(), sp), B(key.data() + sp + 1, key.size() - sp - 1);
-        auto ia = ids_of.find(A), ib = ids_of.find(B);
-        if (ia == ids_of.end() || ib == ids_of.end()) continue;
-        std::string joined(A);
+        if (!id_of.count(A) || !id_of.count(B)) continue;
+        joined.assign(A);
         joined.append(B);
         auto jm = vocab_to_id.find(joined);
         const Merge mg{rank, jm == vocab_to_id.end() ? kNone : jm->second};
-        for (uint32_t a : ia->second)
-          for (uint32_t b : ib->second) pairs[pair_key(a, b)] = mg;
+        for_ids(A, [&](uint32_t a) { for_ids(B, [&](uint32_t b) { merges.put(pair_key(a, b), mg); }); });
       }
     }
-    merges.build(pairs);
     return NNZ_OK;
   }
 

@@ -11,9 +11,11 @@ reference tree):
 
 * GPT-2 byte <-> unicode table: bytes 33-126, 161-172, 174-255 map to
   themselves, the other 68 to 256.. in byte order (tokenizer.zig:76-108).
-* tokenizer.json reading: model.vocab (ids must be integers in u32 and
-  < 200000), model.merges as "a b" strings or ["a", "b"] pairs keyed by the
-  joined string, rank = array index, a repeated key keeps the later rank;
+* tokenizer.json reading (a repeated member name is invalid JSON, the
+  default of the reference's std.json parser): model.vocab (ids must be
+  integers in u32 and < 200000), model.merges as "a b" strings or
+  ["a", "b"] pairs keyed by the joined string, rank = array index, a
+  repeated key keeps the later rank;
   added_tokens go into the vocabulary (id_to_vocab only where unused) and,
   when "special", into the special list (at most 256); eos / im_start /
   im_end resolved by content (tokenizer.zig:375-656); the byte -> base token
@@ -196,8 +198,17 @@ class Tokenizer:
     def __init__(self, json_bytes: bytes | str):
         if isinstance(json_bytes, str):
             json_bytes = json_bytes.encode()
+        def no_duplicates(pairs):
+            # the reference's std.json rejects a repeated member name
+            d = {}
+            for k, v in pairs:
+                if k in d:
+                    raise TokError("InvalidJson")
+                d[k] = v
+            return d
+
         try:
-            root = json.loads(json_bytes.decode("utf-8"))
+            root = json.loads(json_bytes.decode("utf-8"), object_pairs_hook=no_duplicates)
         except (UnicodeDecodeError, json.JSONDecodeError):
             raise TokError("InvalidJson") from None
         if not isinstance(root, dict):

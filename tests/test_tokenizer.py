@@ -361,6 +361,8 @@ def test_concurrent_encode_is_consistent(built_lib):
     ('{"model": {"vocab": {"a": 0}, "merges": [["a"]]}}', "InvalidMergeEntry"),
     ('{"model": {"vocab": {"a": 0}, "merges": [3]}}', "InvalidMergeEntry"),
     ('{"model": {"vocab": {"a": 0}}, "added_tokens": {}}', "InvalidJson"),
+    ('{"model": {"vocab": {"a": 0, "b": 1, "a": 2}}}', "InvalidJson"),
+    ('{"model": {"vocab": {"a": 0}}, "model": {"vocab": {"a": 0}}}', "InvalidJson"),
 ])
 def test_load_errors(built_lib, js, name):
     from nnzap_b200.tokenizer import Tokenizer
