@@ -337,6 +337,45 @@ int nnz_token_to_bytes(const char* token, size_t len, char* out, size_t cap, siz
  * pre-tokenizer chunk of text[0..len) (0 when len == 0). */
 uint32_t nnz_pretoken_chunk(const char* text, size_t len);
 
+/* ---- safetensors: replaces SafetensorsFile of nnmetal/src/safetensors.zig */
+/* Host code only.  A reader memory-maps one file and describes its tensors;
+ * the descriptors' data pointers stay valid until nnz_safetensors_close.
+ * Model.loadWeights (model.zig:196-242) is then, per file:
+ *   for i < nnz_safetensors_count(f): nnz_safetensors_tensor(f, i, &d);
+ *                                     nnz_model_load_tensor(m, d.name, d.dtype, d.data, d.nbytes);
+ * and nnz_model_finalize(m) once all files are read (load_tensor copies).
+ * Same format, limits and error names as the reference (InvalidHeader,
+ * InvalidJson, TooManyTensors, InvalidTensorEntry, MissingDtype,
+ * InvalidDtype, UnsupportedDtype, MissingShape, InvalidShape,
+ * TooManyDimensions, MissingDataOffsets, InvalidDataOffsets,
+ * DataOffsetOutOfBounds; NNZ_EINVAL) plus one check it leaves to its loader:
+ * a tensor's byte range equals element count x dtype size. */
+typedef struct nnz_safetensors nnz_safetensors;
+
+typedef struct nnz_tensor_desc {
+  const char* name;      /* NUL-terminated, owned by the reader */
+  int dtype;             /* NNZ_DT_* */
+  uint32_t rank;         /* 0..4 */
+  uint32_t dims[4];      /* dims[0..rank) */
+  const void* data;      /* into the mapping */
+  size_t nbytes;
+} nnz_tensor_desc;
+
+/* SafetensorsFile.init (safetensors.zig:134-161): open + mmap + parse
+ * (NNZ_ENOTFOUND if the file cannot be opened). */
+int nnz_safetensors_open(const char* path, nnz_safetensors** out);
+/* SafetensorsFile.initFromBytes (safetensors.zig:167-181): parse a buffer
+ * the caller keeps alive while the reader is open. */
+int nnz_safetensors_from_bytes(const void* bytes, size_t len, nnz_safetensors** out);
+/* SafetensorsFile.deinit (safetensors.zig:183-193). */
+int nnz_safetensors_close(nnz_safetensors* f);
+/* Number of tensors (SafetensorsFile.count), in header order. */
+uint32_t nnz_safetensors_count(const nnz_safetensors* f);
+/* tensors[index]. */
+int nnz_safetensors_tensor(const nnz_safetensors* f, uint32_t index, nnz_tensor_desc* desc);
+/* SafetensorsFile.getTensor (safetensors.zig:196-209); NNZ_ENOTFOUND if absent. */
+int nnz_safetensors_find(const nnz_safetensors* f, const char* name, nnz_tensor_desc* desc);
+
 #ifdef __cplusplus
 }
 #endif

@@ -56,6 +56,11 @@ class NnzTokenizerInfo(C.Structure):
         "im_end_token_id", "merge_count")]
 
 
+class NnzTensorDesc(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("dtype", C.c_int), ("rank", C.c_uint32),
+                ("dims", C.c_uint32 * 4), ("data", C.c_void_p), ("nbytes", C.c_size_t)]
+
+
 class NnzGenerateResult(C.Structure):
     _fields_ = [("tokens_generated", C.c_uint32), ("prefill_ns", C.c_uint64),
                 ("decode_ns", C.c_uint64)]
@@ -107,6 +112,12 @@ SIGNATURES = [
     ("nnz_tokenizer_bpe_merge", I32, [P, P, U32, P]),
     ("nnz_tokenizer_token", I32, [P, U32, P, SZ, P]),
     ("nnz_token_to_bytes", I32, [C.c_char_p, SZ, P, SZ, P]),
+    ("nnz_safetensors_open", I32, [C.c_char_p, P]),
+    ("nnz_safetensors_from_bytes", I32, [P, SZ, P]),
+    ("nnz_safetensors_close", I32, [P]),
+    ("nnz_safetensors_count", U32, [P]),
+    ("nnz_safetensors_tensor", I32, [P, U32, P]),
+    ("nnz_safetensors_find", I32, [P, C.c_char_p, P]),
     ("nnz_pretoken_chunk", U32, [C.c_char_p, SZ]),
 ]
 

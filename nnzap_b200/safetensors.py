@@ -4,9 +4,12 @@ Restates the reference's parser (nnmetal/src/safetensors.zig:1-582) for
 the Python host: an 8-byte little-endian header length, a JSON header of
 tensor descriptors ({"dtype", "shape", "data_offsets"}; "__metadata__"
 skipped), then the contiguous tensor data, memory-mapped.  Same limits and
-checks: header <= 16 MiB and inside the file, <= 1024 tensors, <= 4
-dimensions, dtypes U8 / U32 / F16 / F32 / BF16, offsets ordered and inside
-the data region.
+checks: header <= 16 MiB and inside the file, <= 1024 tensors, names <=
+256 bytes, <= 4 dimensions, dtypes U8 / U32 / F16 / F32 / BF16, offsets
+ordered and inside the data region, a repeated JSON member name invalid.
+One check beyond the reference (which leaves it to its loader): a tensor's
+byte range equals its element count times the dtype size.  The library's
+C++ reader (nnz_safetensors_*) applies the same rules.
 
 `load_safetensors(model, paths)` is Model.loadWeights
 (nnmetal/src/model.zig:196-242): every tensor of every shard file is handed
@@ -27,6 +30,12 @@ import numpy as np
 MAX_TENSORS = 1024
 MAX_DIMS = 4
 MAX_HEADER_BYTES = 16 * 1024 * 1024
+MAX_NAME_LENGTH = 256
+
+
+def _is_uint(v, top: int) -> bool:
+    """A JSON integer (not a boolean) in [0, top]."""
+    return isinstance(v, int) and not isinstance(v, bool) and 0 <= v <= top
 
 # safetensors dtype string -> (numpy dtype, bytes per element)
 DTYPES = {"U8": (np.uint8, 1), "U32": (np.uint32, 4), "F16": (np.float16, 2), "F32": (np.float32, 4),
@@ -74,8 +83,17 @@ class SafetensorsFile:
         start = 8 + hlen
         if start > len(buf):
             raise SafetensorsError(f"InvalidHeader: header length ({hlen}) exceeds file size ({len(buf)})")
+        def no_duplicates(pairs):
+            # a repeated member name is invalid, as in the reference's std.json
+            d = {}
+            for k, v in pairs:
+                if k in d:
+                    raise SafetensorsError(f"InvalidJson: duplicate member '{k}'")
+                d[k] = v
+            return d
+
         try:
-            header = json.loads(bytes(buf[8:start]).decode("utf-8"))
+            header = json.loads(bytes(buf[8:start]).decode("utf-8"), object_pairs_hook=no_duplicates)
         except (UnicodeDecodeError, json.JSONDecodeError) as e:
             raise SafetensorsError(f"InvalidJson: {e}") from None
         if not isinstance(header, dict):
@@ -86,6 +104,8 @@ class SafetensorsFile:
                 continue
             if len(self.tensors) >= MAX_TENSORS:
                 raise SafetensorsError(f"TooManyTensors: more than {MAX_TENSORS}")
+            if not name or len(name.encode()) > MAX_NAME_LENGTH:
+                raise SafetensorsError("InvalidTensorEntry: tensor name empty or longer than 256 bytes")
             if not isinstance(desc, dict):
                 raise SafetensorsError(f"InvalidTensorEntry: '{name}'")
             if "dtype" not in desc:
@@ -98,14 +118,14 @@ class SafetensorsFile:
             if "shape" not in desc:
                 raise SafetensorsError(f"MissingShape: '{name}'")
             shape = desc["shape"]
-            if not isinstance(shape, list) or not all(isinstance(d, int) and d >= 0 for d in shape):
+            if not isinstance(shape, list) or not all(_is_uint(d, 0xFFFFFFFF) for d in shape):
                 raise SafetensorsError(f"InvalidShape: '{name}'")
             if len(shape) > MAX_DIMS:
                 raise SafetensorsError(f"TooManyDimensions: '{name}' has {len(shape)}")
             if "data_offsets" not in desc:
                 raise SafetensorsError(f"MissingDataOffsets: '{name}'")
             off = desc["data_offsets"]
-            if (not isinstance(off, list) or len(off) != 2 or not all(isinstance(o, int) for o in off)
+            if (not isinstance(off, list) or len(off) != 2 or not all(_is_uint(o, 2 ** 63 - 1) for o in off)
                     or off[0] > off[1]):
                 raise SafetensorsError(f"InvalidDataOffsets: '{name}'")
             if off[1] > len(data):
