@@ -14,8 +14,10 @@
 
 #include <algorithm>
 #include <cmath>
+#include <exception>
 #include <map>
 #include <mutex>
+#include <new>
 #include <string>
 #include <vector>
 
@@ -822,6 +824,20 @@ int tp_setup_peers(nnz_model* m) {
 // =========================================================================
 // C ABI
 // =========================================================================
+// No C++ exception crosses the C ABI: the entry points that allocate host
+// memory (weight packing, tensor copies, finalize) turn a failed allocation
+// into NNZ_ENOMEM.
+template <typename F>
+static int host_guard(F&& f) {
+  try {
+    return f();
+  } catch (const std::bad_alloc&) {
+    return fail(NNZ_ENOMEM, "host memory allocation failed");
+  } catch (const std::exception& e) {
+    return fail(NNZ_EINVAL, std::string("host error: ") + e.what());
+  }
+}
+
 extern "C" {
 
 const char* nnz_last_error(void) { return g_err.c_str(); }
@@ -840,7 +856,7 @@ size_t nnz_packed_bytes(int fmt, uint32_t M, uint32_t K, uint32_t gs, uint32_t s
   return packed_bytes(fmt, M, K, gs, sub);
 }
 
-int nnz_pack_weights(int fmt, const void* weight, const uint16_t* scales, const uint16_t* biases,
+static int pack_weights_impl(int fmt, const void* weight, const uint16_t* scales, const uint16_t* biases,
                      uint32_t M, uint32_t K, uint32_t gs, uint32_t sub, uint32_t sub_index,
                      void* packed_out) {
   if (pack_host(fmt, weight, scales, biases, M, K, gs, sub, sub_index, packed_out, 0))
@@ -848,7 +864,14 @@ int nnz_pack_weights(int fmt, const void* weight, const uint16_t* scales, const 
   return NNZ_OK;
 }
 
-int nnz_unpack_weights(int fmt, const void* packed, uint32_t M, uint32_t K, uint32_t gs,
+int nnz_pack_weights(int fmt, const void* weight, const uint16_t* scales, const uint16_t* biases,
+                     uint32_t M, uint32_t K, uint32_t gs, uint32_t sub, uint32_t sub_index,
+                     void* packed_out) {
+  return host_guard(
+      [&] { return pack_weights_impl(fmt, weight, scales, biases, M, K, gs, sub, sub_index, packed_out); });
+}
+
+static int unpack_weights_impl(int fmt, const void* packed, uint32_t M, uint32_t K, uint32_t gs,
                        uint32_t sub, uint32_t sub_index, void* weight, uint16_t* scales,
                        uint16_t* biases) {
   if (unpack_host(fmt, packed, M, K, gs, sub, sub_index, weight, scales, biases))
@@ -856,7 +879,14 @@ int nnz_unpack_weights(int fmt, const void* packed, uint32_t M, uint32_t K, uint
   return NNZ_OK;
 }
 
-int nnz_model_create(int device, const nnz_config* cfg, nnz_model** out) {
+int nnz_unpack_weights(int fmt, const void* packed, uint32_t M, uint32_t K, uint32_t gs,
+                       uint32_t sub, uint32_t sub_index, void* weight, uint16_t* scales,
+                       uint16_t* biases) {
+  return host_guard(
+      [&] { return unpack_weights_impl(fmt, packed, M, K, gs, sub, sub_index, weight, scales, biases); });
+}
+
+static int model_create_impl(int device, const nnz_config* cfg, nnz_model** out) {
   if (!cfg || !out) return fail(NNZ_EINVAL, "null argument");
   const nnz_config& c = *cfg;
   if (c.quant_format != NNZ_Q1 && c.quant_format != NNZ_Q4) return fail(NNZ_EINVAL, "quant_format");
@@ -911,7 +941,11 @@ int nnz_model_create(int device, const nnz_config* cfg, nnz_model** out) {
   return NNZ_OK;
 }
 
-int nnz_model_load_tensor(nnz_model* m, const char* name, int dtype, const void* data, size_t bytes) {
+int nnz_model_create(int device, const nnz_config* cfg, nnz_model** out) {
+  return host_guard([&] { return model_create_impl(device, cfg, out); });
+}
+
+static int model_load_tensor_impl(nnz_model* m, const char* name, int dtype, const void* data, size_t bytes) {
   if (!m || !name || (!data && bytes)) return fail(NNZ_EINVAL, "null argument");
   if (m->finalized) return fail(NNZ_ESTATE, "model already finalized");
   if (dtype < NNZ_DT_U8 || dtype > NNZ_DT_F32) return fail(NNZ_EINVAL, "dtype");
@@ -921,7 +955,11 @@ int nnz_model_load_tensor(nnz_model* m, const char* name, int dtype, const void*
   return NNZ_OK;
 }
 
-int nnz_model_finalize(nnz_model* m) {
+int nnz_model_load_tensor(nnz_model* m, const char* name, int dtype, const void* data, size_t bytes) {
+  return host_guard([&] { return model_load_tensor_impl(m, name, dtype, data, bytes); });
+}
+
+static int model_finalize_impl(nnz_model* m) {
   if (!m) return fail(NNZ_EINVAL, "null model");
   if (m->finalized) return fail(NNZ_ESTATE, "model already finalized");
   if (m->tp > 1 && !m->comm) return fail(NNZ_ESTATE, "tensor-parallel model: call nnz_tp_init first");
@@ -1169,6 +1207,10 @@ int nnz_model_finalize(nnz_model* m) {
   return NNZ_OK;
 }
 
+int nnz_model_finalize(nnz_model* m) {
+  return host_guard([&] { return model_finalize_impl(m); });
+}
+
 int nnz_model_free(nnz_model* m) {
   if (!m) return NNZ_OK;
   if (m->device >= 0) cudaSetDevice(m->device);
@@ -1187,12 +1229,21 @@ int nnz_model_free(nnz_model* m) {
 size_t nnz_model_device_bytes(const nnz_model* m) { return m ? m->dev_bytes : 0; }
 uint32_t nnz_model_vocab_shard(const nnz_model* m) { return m ? m->lm_rows : 0; }
 
-int nnz_shard_weights(int fmt, int axis, const void* weight, const uint16_t* scales, const uint16_t* biases,
+static int shard_weights_impl(int fmt, int axis, const void* weight, const uint16_t* scales, const uint16_t* biases,
                       uint32_t M, uint32_t K, uint32_t gs, uint32_t lo, uint32_t hi, void* weight_out,
                       uint16_t* scales_out, uint16_t* biases_out) {
   if (shard_host(fmt, axis, weight, scales, biases, M, K, gs, lo, hi, weight_out, scales_out, biases_out))
     return fail(NNZ_EINVAL, "nnz_shard_weights: invalid arguments");
   return NNZ_OK;
+}
+
+int nnz_shard_weights(int fmt, int axis, const void* weight, const uint16_t* scales, const uint16_t* biases,
+                      uint32_t M, uint32_t K, uint32_t gs, uint32_t lo, uint32_t hi, void* weight_out,
+                      uint16_t* scales_out, uint16_t* biases_out) {
+  return host_guard([&] {
+    return shard_weights_impl(fmt, axis, weight, scales, biases, M, K, gs, lo, hi, weight_out, scales_out,
+                              biases_out);
+  });
 }
 
 int nnz_sample(float* logits, uint32_t rows, uint32_t n, uint32_t stride, float temperature, uint32_t top_k,

@@ -16,7 +16,9 @@
 
 #include <cstdint>
 #include <cstring>
+#include <exception>
 #include <memory>
+#include <new>
 #include <string>
 #include <vector>
 
@@ -41,6 +43,19 @@ constexpr size_t kMaxNameLength = 256;
 int fail(int code, const std::string& msg) {
   nnz::set_last_error(msg);
   return code;
+}
+
+// No C++ exception crosses the C ABI: a failed host allocation becomes
+// NNZ_ENOMEM.
+template <typename F>
+int host_guard(F&& f) {
+  try {
+    return f();
+  } catch (const std::bad_alloc&) {
+    return fail(NNZ_ENOMEM, "OutOfMemory: host allocation failed");
+  } catch (const std::exception& e) {
+    return fail(NNZ_EINVAL, std::string("host error: ") + e.what());
+  }
 }
 
 // Dtype.fromString / sizeBytes (safetensors.zig:45-78).
@@ -153,7 +168,7 @@ struct nnz_safetensors {
 
 extern "C" {
 
-int nnz_safetensors_open(const char* path, nnz_safetensors** out) {
+static int safetensors_open_impl(const char* path, nnz_safetensors** out) {
   if (!path || !*path || !out) return fail(NNZ_EINVAL, "nnz_safetensors_open: null or empty path");
   *out = nullptr;
   const int fd = open(path, O_RDONLY | O_CLOEXEC);
@@ -181,7 +196,11 @@ int nnz_safetensors_open(const char* path, nnz_safetensors** out) {
   return NNZ_OK;
 }
 
-int nnz_safetensors_from_bytes(const void* bytes, size_t len, nnz_safetensors** out) {
+int nnz_safetensors_open(const char* path, nnz_safetensors** out) {
+  return host_guard([&] { return safetensors_open_impl(path, out); });
+}
+
+static int safetensors_from_bytes_impl(const void* bytes, size_t len, nnz_safetensors** out) {
   if (!out || (!bytes && len)) return fail(NNZ_EINVAL, "nnz_safetensors_from_bytes: null argument");
   *out = nullptr;
   auto f = std::make_unique<nnz_safetensors>();
@@ -193,21 +212,33 @@ int nnz_safetensors_from_bytes(const void* bytes, size_t len, nnz_safetensors** 
   return NNZ_OK;
 }
 
-int nnz_safetensors_close(nnz_safetensors* f) {
+int nnz_safetensors_from_bytes(const void* bytes, size_t len, nnz_safetensors** out) {
+  return host_guard([&] { return safetensors_from_bytes_impl(bytes, len, out); });
+}
+
+static int safetensors_close_impl(nnz_safetensors* f) {
   delete f;
   return NNZ_OK;
 }
 
+int nnz_safetensors_close(nnz_safetensors* f) {
+  return host_guard([&] { return safetensors_close_impl(f); });
+}
+
 uint32_t nnz_safetensors_count(const nnz_safetensors* f) { return f ? (uint32_t)f->tensors.size() : 0; }
 
-int nnz_safetensors_tensor(const nnz_safetensors* f, uint32_t index, nnz_tensor_desc* desc) {
+static int safetensors_tensor_impl(const nnz_safetensors* f, uint32_t index, nnz_tensor_desc* desc) {
   if (!f || !desc) return fail(NNZ_EINVAL, "nnz_safetensors_tensor: null argument");
   if (index >= f->tensors.size()) return fail(NNZ_EINVAL, "nnz_safetensors_tensor: index out of range");
   f->describe(f->tensors[index], desc);
   return NNZ_OK;
 }
 
-int nnz_safetensors_find(const nnz_safetensors* f, const char* name, nnz_tensor_desc* desc) {
+int nnz_safetensors_tensor(const nnz_safetensors* f, uint32_t index, nnz_tensor_desc* desc) {
+  return host_guard([&] { return safetensors_tensor_impl(f, index, desc); });
+}
+
+static int safetensors_find_impl(const nnz_safetensors* f, const char* name, nnz_tensor_desc* desc) {
   if (!f || !name || !desc) return fail(NNZ_EINVAL, "nnz_safetensors_find: null argument");
   for (const Tensor& t : f->tensors)
     if (t.name == name) {
@@ -215,6 +246,10 @@ int nnz_safetensors_find(const nnz_safetensors* f, const char* name, nnz_tensor_
       return NNZ_OK;
     }
   return fail(NNZ_ENOTFOUND, std::string("TensorNotFound: ") + name);
+}
+
+int nnz_safetensors_find(const nnz_safetensors* f, const char* name, nnz_tensor_desc* desc) {
+  return host_guard([&] { return safetensors_find_impl(f, name, desc); });
 }
 
 }  // extern "C"

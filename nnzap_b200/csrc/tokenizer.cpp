@@ -19,7 +19,9 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <exception>
 #include <memory>
+#include <new>
 #include <string>
 #include <string_view>
 #include <unordered_map>
@@ -52,6 +54,19 @@ constexpr uint32_t kNone = 0xFFFFFFFFu;
 int fail(int code, const std::string& msg) {
   nnz::set_last_error(msg);
   return code;
+}
+
+// No C++ exception crosses the C ABI: a failed host allocation becomes
+// NNZ_ENOMEM.
+template <typename F>
+int host_guard(F&& f) {
+  try {
+    return f();
+  } catch (const std::bad_alloc&) {
+    return fail(NNZ_ENOMEM, "OutOfMemory: host allocation failed");
+  } catch (const std::exception& e) {
+    return fail(NNZ_EINVAL, std::string("host error: ") + e.what());
+  }
 }
 
 // ---- GPT-2 byte <-> unicode table (tokenizer.zig:52-108) -----------------
@@ -496,7 +511,7 @@ struct nnz_tokenizer {
 
 extern "C" {
 
-int nnz_tokenizer_from_json(const char* json, size_t len, nnz_tokenizer** out) {
+static int tokenizer_from_json_impl(const char* json, size_t len, nnz_tokenizer** out) {
   if (!out || (!json && len)) return fail(NNZ_EINVAL, "nnz_tokenizer_from_json: null argument");
   *out = nullptr;
   try {
@@ -510,7 +525,11 @@ int nnz_tokenizer_from_json(const char* json, size_t len, nnz_tokenizer** out) {
   }
 }
 
-int nnz_tokenizer_from_file(const char* path, nnz_tokenizer** out) {
+int nnz_tokenizer_from_json(const char* json, size_t len, nnz_tokenizer** out) {
+  return host_guard([&] { return tokenizer_from_json_impl(json, len, out); });
+}
+
+static int tokenizer_from_file_impl(const char* path, nnz_tokenizer** out) {
   if (!path || !out || !*path) return fail(NNZ_EINVAL, "nnz_tokenizer_from_file: null or empty path");
   *out = nullptr;
   FILE* f = fopen(path, "rb");
@@ -529,12 +548,20 @@ int nnz_tokenizer_from_file(const char* path, nnz_tokenizer** out) {
   return nnz_tokenizer_from_json(buf.data(), buf.size(), out);
 }
 
-int nnz_tokenizer_free(nnz_tokenizer* tok) {
+int nnz_tokenizer_from_file(const char* path, nnz_tokenizer** out) {
+  return host_guard([&] { return tokenizer_from_file_impl(path, out); });
+}
+
+static int tokenizer_free_impl(nnz_tokenizer* tok) {
   delete tok;
   return NNZ_OK;
 }
 
-int nnz_tokenizer_get_info(const nnz_tokenizer* tok, nnz_tokenizer_info* info) {
+int nnz_tokenizer_free(nnz_tokenizer* tok) {
+  return host_guard([&] { return tokenizer_free_impl(tok); });
+}
+
+static int tokenizer_get_info_impl(const nnz_tokenizer* tok, nnz_tokenizer_info* info) {
   if (!tok || !info) return fail(NNZ_EINVAL, "nnz_tokenizer_get_info: null argument");
   info->vocab_size = tok->vocab_size;
   info->special_token_count = (uint32_t)tok->specials.size();
@@ -545,19 +572,33 @@ int nnz_tokenizer_get_info(const nnz_tokenizer* tok, nnz_tokenizer_info* info) {
   return NNZ_OK;
 }
 
-int nnz_tokenizer_encode(const nnz_tokenizer* tok, const char* text, size_t len, uint32_t* ids,
+int nnz_tokenizer_get_info(const nnz_tokenizer* tok, nnz_tokenizer_info* info) {
+  return host_guard([&] { return tokenizer_get_info_impl(tok, info); });
+}
+
+static int tokenizer_encode_impl(const nnz_tokenizer* tok, const char* text, size_t len, uint32_t* ids,
                          uint32_t cap, uint32_t* n_out) {
   if (!tok || !n_out || (!text && len) || (!ids && cap)) return fail(NNZ_EINVAL, "nnz_tokenizer_encode: null argument");
   return tok->encode(reinterpret_cast<const uint8_t*>(text), len, ids, cap, n_out);
 }
 
-int nnz_tokenizer_decode(const nnz_tokenizer* tok, const uint32_t* ids, uint32_t n, char* out, size_t cap,
+int nnz_tokenizer_encode(const nnz_tokenizer* tok, const char* text, size_t len, uint32_t* ids,
+                         uint32_t cap, uint32_t* n_out) {
+  return host_guard([&] { return tokenizer_encode_impl(tok, text, len, ids, cap, n_out); });
+}
+
+static int tokenizer_decode_impl(const nnz_tokenizer* tok, const uint32_t* ids, uint32_t n, char* out, size_t cap,
                          size_t* n_out) {
   if (!tok || !n_out || (!ids && n) || (!out && cap)) return fail(NNZ_EINVAL, "nnz_tokenizer_decode: null argument");
   return tok->decode(ids, n, out, cap, n_out);
 }
 
-int nnz_tokenizer_chat_template(const nnz_tokenizer* tok, const char* prompt, size_t len, uint32_t* ids,
+int nnz_tokenizer_decode(const nnz_tokenizer* tok, const uint32_t* ids, uint32_t n, char* out, size_t cap,
+                         size_t* n_out) {
+  return host_guard([&] { return tokenizer_decode_impl(tok, ids, n, out, cap, n_out); });
+}
+
+static int tokenizer_chat_template_impl(const nnz_tokenizer* tok, const char* prompt, size_t len, uint32_t* ids,
                                 uint32_t cap, uint32_t* n_out) {
   if (!tok || !n_out || !prompt || len == 0 || (!ids && cap))
     return fail(NNZ_EINVAL, "nnz_tokenizer_chat_template: null argument or empty prompt");
@@ -582,7 +623,12 @@ int nnz_tokenizer_chat_template(const nnz_tokenizer* tok, const char* prompt, si
   return NNZ_OK;
 }
 
-int nnz_tokenizer_bpe_merge(const nnz_tokenizer* tok, uint32_t* ids, uint32_t n, uint32_t* n_out) {
+int nnz_tokenizer_chat_template(const nnz_tokenizer* tok, const char* prompt, size_t len, uint32_t* ids,
+                                uint32_t cap, uint32_t* n_out) {
+  return host_guard([&] { return tokenizer_chat_template_impl(tok, prompt, len, ids, cap, n_out); });
+}
+
+static int tokenizer_bpe_merge_impl(const nnz_tokenizer* tok, uint32_t* ids, uint32_t n, uint32_t* n_out) {
   if (!tok || !n_out || (!ids && n)) return fail(NNZ_EINVAL, "nnz_tokenizer_bpe_merge: null argument");
   if (n > kMaxTokenLength) return fail(NNZ_EINVAL, "ChunkTooLong: more than 512 tokens");
   for (uint32_t i = 0; i < n; ++i)
@@ -591,7 +637,11 @@ int nnz_tokenizer_bpe_merge(const nnz_tokenizer* tok, uint32_t* ids, uint32_t n,
   return NNZ_OK;
 }
 
-int nnz_tokenizer_token(const nnz_tokenizer* tok, uint32_t id, char* out, size_t cap, size_t* n_out) {
+int nnz_tokenizer_bpe_merge(const nnz_tokenizer* tok, uint32_t* ids, uint32_t n, uint32_t* n_out) {
+  return host_guard([&] { return tokenizer_bpe_merge_impl(tok, ids, n, n_out); });
+}
+
+static int tokenizer_token_impl(const nnz_tokenizer* tok, uint32_t id, char* out, size_t cap, size_t* n_out) {
   if (!tok || !n_out || (!out && cap)) return fail(NNZ_EINVAL, "nnz_tokenizer_token: null argument");
   *n_out = 0;
   if (id >= tok->vocab_size || tok->id_to_vocab[id].empty())
@@ -603,12 +653,20 @@ int nnz_tokenizer_token(const nnz_tokenizer* tok, uint32_t id, char* out, size_t
   return NNZ_OK;
 }
 
-int nnz_token_to_bytes(const char* token, size_t len, char* out, size_t cap, size_t* n_out) {
+int nnz_tokenizer_token(const nnz_tokenizer* tok, uint32_t id, char* out, size_t cap, size_t* n_out) {
+  return host_guard([&] { return tokenizer_token_impl(tok, id, out, cap, n_out); });
+}
+
+static int token_to_bytes_impl(const char* token, size_t len, char* out, size_t cap, size_t* n_out) {
   if (!n_out || (!token && len) || (!out && cap)) return fail(NNZ_EINVAL, "nnz_token_to_bytes: null argument");
   *n_out = 0;
   if (cap < len) return fail(NNZ_ERANGE, "OutputBufferTooSmall");
   if (len) *n_out = token_to_bytes(std::string(token, len), out);
   return NNZ_OK;
+}
+
+int nnz_token_to_bytes(const char* token, size_t len, char* out, size_t cap, size_t* n_out) {
+  return host_guard([&] { return token_to_bytes_impl(token, len, out, cap, n_out); });
 }
 
 uint32_t nnz_pretoken_chunk(const char* text, size_t len) {
