@@ -1,0 +1,1236 @@
+// Single-row Q1 decode kernel (see decode1.cuh for the design summary).
+//
+// Per token, every CTA runs the same program:
+//   token start  read the decode state (token <- previous argmax, position+1);
+//                the layer-0 residual is the embedding row, which every CTA
+//                dequantizes for itself (no barrier);
+//   per layer l:
+//     QKV   fused RMSNorm (attn_norm) + q/k/v rows of this CTA (whole K),
+//           fp16 out; one release-add per row block on the kv head's counter;
+//           the CTA also clears its slice of the next residual and of the
+//           next O accumulator;
+//     ATT   CTAs [0, nkv*S): one (kv head, position split) each: QK-norm +
+//           RoPE of q/k (k and v of the new position go to the fp16 cache),
+//           flash-decoding partial (max, sum, output) over the split's K/V
+//           blocks (prefetched with bulk copies while QKV runs);
+//     O     CTAs [0, nq*nrr): one (head, row range) each: merge the head's
+//           splits, o_proj rows of that range over the head's 128 columns,
+//           red.add into the O accumulator Z;
+//     --- grid barrier ---
+//     GU    fused RMSNorm (ffn_norm) of residual + Z, gate and up rows of
+//           this CTA's intermediate slice, h = fp16(SiLU(g) * u);
+//     DN    down_proj columns of that slice for all H rows, red.add into the
+//           next residual (plus this CTA's slice of residual + Z);
+//     --- grid barrier ---
+//   LM      fused final RMSNorm + this CTA's LM-head rows, f32 logits
+//           (optional) and a packed first-max argmax (atomicMax);
+//   --- grid barrier ---
+//
+// Memory ordering: data produced inside the launch is read with ld.global.cg
+// (L2) after an acquire (counter or barrier); producers publish with a
+// release-add after a CTA barrier.  Every wait is bounded: on a timeout the
+// kernel records ERR_SPIN_TIMEOUT / ERR_MBAR_TIMEOUT, raises the sticky abort
+// flag that releases every other waiter, stops issuing copies, drains the
+// bulk copies it has in flight and returns; the host then reports
+// NNZ_ETIMEDOUT.  The red.add accumulations make the f32 sums' order (and so
+// their last bits) vary from run to run.
+#include <cuda_runtime.h>
+#include <string.h>
+
+#include "decode1.cuh"
+
+namespace nnz {
+
+namespace {
+
+constexpr uint32_t kD1Spin = 1u << 22;
+constexpr unsigned kFull = 0xffffffffu;
+
+// ---- shared-memory layout ----------------------------------------------------
+constexpr uint32_t al16(uint32_t v) { return (v + 15u) & ~15u; }
+constexpr uint32_t KV_BLKB = kD1KvBlk * 128 * 2;                       // one K (or V) block, bytes
+constexpr uint32_t OFF_RING = 0;
+constexpr uint32_t OFF_KV = OFF_RING + kD1Slots * kD1Chunk;            // [2 stages][K, V]
+constexpr uint32_t OFF_XB = OFF_KV + 4 * KV_BLKB;                      // [group][4 k32 chunks][12 lanes] uint2
+constexpr uint32_t OFF_GEF = OFF_XB + kD1MaxGroups * 4 * 12 * 8;       // [group] 2^(E-22)
+constexpr uint32_t OFF_GSQ = OFF_GEF + kD1MaxGroups * 4;               // [group] sum of q
+constexpr uint32_t OFF_XB16 = OFF_GSQ + kD1MaxGroups * 4;              // [k16 chunk][12 lanes] u32
+constexpr uint32_t OFF_EF16 = al16(OFF_XB16 + kD1MaxNb * 12 * 4);
+constexpr uint32_t OFF_SQ16 = OFF_EF16 + kD1MaxNb * 4;
+constexpr uint32_t OFF_PART = al16(OFF_SQ16 + kD1MaxNb * 4);           // [warp][rb][16] f32
+constexpr uint32_t OFF_ROWS = OFF_PART + kD1Warps * kD1MaxRb * 16 * 4; // [rb * 16] f32
+constexpr uint32_t OFF_RED = OFF_ROWS + kD1MaxRb * 16 * 4;             // [16] f32
+constexpr uint32_t OFF_AMAX = OFF_RED + 16 * 4;                        // [16] u64
+constexpr uint32_t OFF_QS = OFF_AMAX + 16 * 8;                         // [G][128] f32
+constexpr uint32_t OFF_SC = OFF_QS + kD1MaxG * 128 * 4;                // [G][32] f32
+constexpr uint32_t OFF_KNEW = OFF_SC + kD1MaxG * kD1KvBlk * 4;         // [128] fp16
+constexpr uint32_t OFF_VNEW = OFF_KNEW + 256;                          // [128] fp16
+constexpr uint32_t OFF_STAT = OFF_VNEW + 256;                          // m[4], l[4], alpha[4]
+constexpr uint32_t OFF_COMB = al16(OFF_STAT + 3 * kD1MaxG * 4);        // [4][128] f32
+constexpr uint32_t OFF_MER = OFF_COMB + 4 * 128 * 4;                   // [4][132] f32
+constexpr uint32_t OFF_XO = OFF_MER + 4 * kD1AttRec * 4;               // [128] f32
+constexpr uint32_t OFF_TOK = OFF_XO + 128 * 4;                         // tok, pos, adv
+constexpr uint32_t OFF_BAR = al16(OFF_TOK + 16);                       // full[S], empty[S], kv[2]
+constexpr uint32_t SMEM_TOTAL = OFF_BAR + (2 * kD1Slots + 2) * 8;
+static_assert(SMEM_TOTAL <= 227 * 1024, "decode1 shared memory");
+static_assert(OFF_KV % 128 == 0 && OFF_XB % 16 == 0, "alignment");
+
+// ---- small PTX helpers ---------------------------------------------------------
+__device__ __forceinline__ void named_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kD1Warps * 32) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_relaxed_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_u32(unsigned int* p, unsigned int v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive1(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async;" ::: "memory"); }
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// D(16x8 s32) += A(16x16 u8) * B(16x8 s8)
+__device__ __forceinline__ void mma_u8s8_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(b0));
+}
+// four bits -> four bytes in {0, 1}
+__device__ __forceinline__ uint32_t spread4(uint32_t nib) { return (nib * 0x00204081u) & 0x01010101u; }
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+// ---- per-warp state --------------------------------------------------------------
+struct Ctx {
+  const D1Args* a;
+  uint8_t* sm;
+  uint32_t c;
+  int warp, lane;
+  uint32_t rel;                  // next ring chunk this warp has not released
+  bool failed;                   // a wait of this thread gave up
+  unsigned long long bar_target; // thread 0: grid-barrier arrival target
+  uint32_t kvseq;                // K/V blocks consumed by this CTA so far
+  uint32_t kv_hi;                // thread 0: K/V block sequence numbers issued so far
+};
+
+__device__ __forceinline__ uint64_t* fullb(uint8_t* sm, uint32_t s) { return reinterpret_cast<uint64_t*>(sm + OFF_BAR) + s; }
+__device__ __forceinline__ uint64_t* emptyb(uint8_t* sm, uint32_t s) {
+  return reinterpret_cast<uint64_t*>(sm + OFF_BAR) + kD1Slots + s;
+}
+__device__ __forceinline__ uint64_t* kvbar(uint8_t* sm, uint32_t s) {
+  return reinterpret_cast<uint64_t*>(sm + OFF_BAR) + 2 * kD1Slots + s;
+}
+
+__device__ __noinline__ void raise_abort(const D1Args& a, int code) {
+  atomicOr(a.err, code);
+  atomicExch(&a.bar[2], 1u);
+}
+
+// Bounded mbarrier wait that also gives up once the launch has aborted.
+__device__ __forceinline__ bool wait_mbar(uint64_t* b, uint32_t parity, const D1Args& a) {
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(b, parity)) return true;
+    if ((i & 127u) == 127u) {
+      if (ld_relaxed_u32(&a.bar[2])) return false;
+      if (i > kD1Spin) {
+        raise_abort(a, ERR_MBAR_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+// Bounded wait used only while draining: no abort check, no error.
+__device__ __forceinline__ void drain_mbar(uint64_t* b, uint32_t parity) {
+  for (uint32_t i = 0; i < kD1Spin; ++i)
+    if (mbar_try_wait(b, parity)) return;
+}
+
+// Bounded spin until *ctr >= target (acquire).
+__device__ __forceinline__ void wait_count(const unsigned int* ctr, unsigned int target, const D1Args& a) {
+  for (uint32_t i = 0;; ++i) {
+    if ((int)(ld_acquire_u32(ctr) - target) >= 0) return;
+    if ((i & 63u) == 63u) {
+      if (ld_relaxed_u32(&a.bar[2])) return;
+      if (i > kD1Spin) {
+        raise_abort(a, ERR_SPIN_TIMEOUT);
+        return;
+      }
+    }
+  }
+}
+
+// Grid barrier over the compute warps of every CTA (co-resident by
+// cooperative launch): one release-add per CTA on a 64-bit counter that only
+// grows, acquire polls until it reaches this barrier's target.
+__device__ __forceinline__ void grid_bar(Ctx& c) {
+  named_sync();
+  if (threadIdx.x == 0) {
+    const D1Args& a = *c.a;
+    unsigned long long* cnt = reinterpret_cast<unsigned long long*>(a.bar + 4);
+    c.bar_target += a.g.P;
+    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(cnt) : "memory");
+    for (uint32_t i = 0;; ++i) {
+      if (ld_acquire_u64(cnt) >= c.bar_target) break;
+      if ((i & 63u) == 63u) {
+        if (ld_relaxed_u32(&a.bar[2])) break;
+        if (i > kD1Spin) {
+          raise_abort(a, ERR_SPIN_TIMEOUT);
+          break;
+        }
+      }
+    }
+  }
+  named_sync();
+}
+
+// ---- weight ring (consumer side) ----------------------------------------------------
+// A warp may arrive on a chunk's `empty` barrier only after that chunk's
+// `full` barrier completed (otherwise the arrival could count toward the
+// slot's previous use), so releasing a chunk waits for it first.
+__device__ __forceinline__ void ring_release_one(Ctx& c) {
+  const uint32_t K = c.rel;
+  if (!c.failed) c.failed = !wait_mbar(fullb(c.sm, K % kD1Slots), (K / kD1Slots) & 1u, *c.a);
+  __syncwarp();
+  if (c.lane == 0) mbar_arrive1(emptyb(c.sm, K % kD1Slots));
+  ++c.rel;
+}
+__device__ __forceinline__ void ring_release_upto(Ctx& c, uint32_t K) {
+  while (c.rel < K) ring_release_one(c);
+}
+__device__ __forceinline__ const uint8_t* ring_get(Ctx& c, uint32_t K) {
+  ring_release_upto(c, K);
+  if (!c.failed) c.failed = !wait_mbar(fullb(c.sm, K % kD1Slots), (K / kD1Slots) & 1u, *c.a);
+  return c.sm + OFF_RING + (K % kD1Slots) * kD1Chunk;
+}
+
+// ---- activation quantisation ----------------------------------------------------------
+// One warp, one 128-wide group; lane holds elements 4 lane .. 4 lane + 3.
+// q = x * 2^(22-E) (2^E > max |x|), exact for every element within 2^-11 of
+// the maximum; q = hi * 65536 + mid * 256 + lo with balanced signed bytes.
+// B fragment of m16n8k32 (.s8): lane n*4 + t holds column n, k = 4t..4t+3
+// (reg 0) and 16 + 4t.. (reg 1); columns 0, 1, 2 = hi, mid, lo.
+__device__ __forceinline__ void digits(int q, uint32_t& hi, uint32_t& mid, uint32_t& lo) {
+  const int l = ((q + 128) & 255) - 128;
+  const int r1 = (q - l) >> 8;
+  const int m = ((r1 + 128) & 255) - 128;
+  const int h = (r1 - m) >> 8;
+  hi = (uint32_t)(h & 255);
+  mid = (uint32_t)(m & 255);
+  lo = (uint32_t)(l & 255);
+}
+
+__device__ __forceinline__ void quant_group(const float (&x)[4], uint32_t gg, int lane, uint8_t* sm) {
+  float am = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+  am = warp_max(am);
+  int E = 0;
+  if (am > 0.f) frexpf(am, &E);
+  const float up = ldexpf(1.f, 22 - E);
+  uint32_t w0 = 0, w1 = 0, w2 = 0;
+  int sum = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int q = __float2int_rn(x[i] * up);
+    sum += q;
+    uint32_t h, m, l;
+    digits(q, h, m, l);
+    w0 |= h << (8 * i);
+    w1 |= m << (8 * i);
+    w2 |= l << (8 * i);
+  }
+  sum = warp_sum_int(sum);
+  uint32_t* xb = reinterpret_cast<uint32_t*>(sm + OFF_XB) + ((size_t)gg * 4 + (lane >> 3)) * 24;
+  const int t = lane & 3, reg = (lane >> 2) & 1;
+  xb[(0 * 4 + t) * 2 + reg] = w0;
+  xb[(1 * 4 + t) * 2 + reg] = w1;
+  xb[(2 * 4 + t) * 2 + reg] = w2;
+  if (lane == 0) {
+    reinterpret_cast<float*>(sm + OFF_GEF)[gg] = ldexpf(1.f, E - 22);
+    reinterpret_cast<int*>(sm + OFF_GSQ)[gg] = sum;
+  }
+}
+
+// k16 chunk p of the SiLU*up slice: lanes 4p .. 4p+3 of warp 0, lane holds
+// elements 4t .. 4t+3 of the chunk (t = lane & 3).
+__device__ __forceinline__ void quant_chunk16(const float (&x)[4], uint32_t p, int lane, bool active, uint8_t* sm) {
+  float am = active ? fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3]))) : 0.f;
+  am = fmaxf(am, __shfl_xor_sync(kFull, am, 1));
+  am = fmaxf(am, __shfl_xor_sync(kFull, am, 2));
+  int E = 0;
+  if (am > 0.f) frexpf(am, &E);
+  const float up = ldexpf(1.f, 22 - E);
+  uint32_t w0 = 0, w1 = 0, w2 = 0;
+  int sum = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int q = active ? __float2int_rn(x[i] * up) : 0;
+    sum += q;
+    uint32_t h, m, l;
+    digits(q, h, m, l);
+    w0 |= h << (8 * i);
+    w1 |= m << (8 * i);
+    w2 |= l << (8 * i);
+  }
+  sum += __shfl_xor_sync(kFull, sum, 1);
+  sum += __shfl_xor_sync(kFull, sum, 2);
+  if (active) {
+    uint32_t* xb = reinterpret_cast<uint32_t*>(sm + OFF_XB16) + p * 12;
+    const int t = lane & 3;
+    xb[0 * 4 + t] = w0;
+    xb[1 * 4 + t] = w1;
+    xb[2 * 4 + t] = w2;
+    if (t == 0) {
+      reinterpret_cast<float*>(sm + OFF_EF16)[p] = ldexpf(1.f, E - 22);
+      reinterpret_cast<int*>(sm + OFF_SQ16)[p] = sum;
+    }
+  }
+}
+
+// ---- matvec core ----------------------------------------------------------------------
+// One 16-row x 128-k unit: 4 int8 MMAs.  Lane's 8 bytes: word w covers MMAs
+// 2w, 2w+1; bit (s + 8i) of a word, s = 4 j' + r, is byte i of A register r
+// of MMA 2w + j'.
+__device__ __forceinline__ void unit_mma(const uint8_t* unit, const uint2* xbg, int lane, int (&acc)[4]) {
+  const uint2 wb = *reinterpret_cast<const uint2*>(unit + lane * 8);
+  acc[0] = acc[1] = acc[2] = acc[3] = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t W = (j < 2) ? wb.x : wb.y;
+    const int s = (j & 1) * 4;
+    const uint2 b = lane < 12 ? xbg[j * 12 + lane] : make_uint2(0u, 0u);
+    mma_u8s8(acc, (W >> s) & 0x01010101u, (W >> (s + 1)) & 0x01010101u, (W >> (s + 2)) & 0x01010101u,
+             (W >> (s + 3)) & 0x01010101u, b.x, b.y);
+  }
+}
+
+// Accumulator digits -> scaled f32 row sums (lanes with lane % 4 == 0 hold rows
+// lane / 4 and lane / 4 + 8).  sum(sign * q) = 2 sum(bit * q) - sum(q), exact.
+__device__ __forceinline__ void unit_epi(const int (&acc)[4], float s0, float s1, int sq, float& y0, float& y1,
+                                         int lane) {
+  const int lo0 = __shfl_down_sync(kFull, acc[0], 1);
+  const int lo1 = __shfl_down_sync(kFull, acc[2], 1);
+  if ((lane & 3) == 0) {
+    const int v0 = acc[0] * 65536 + acc[1] * 256 + lo0;
+    const int v1 = acc[2] * 65536 + acc[3] * 256 + lo1;
+    y0 = fmaf(s0, (float)(2 * v0 - sq), y0);
+    y1 = fmaf(s1, (float)(2 * v1 - sq), y1);
+  }
+}
+
+// Row sums of 16 rows (lanes 4r hold rows r and r + 8) into lanes 0..3 as
+// float4 of rows 4q..4q+3, then one vector red.add per lane.
+__device__ __forceinline__ void red_rows16(float* dst, float y0, float y1, int lane) {
+  const int q = lane & 3;
+  float v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int src = ((4 * q + i) & 7) * 4;
+    const float a = __shfl_sync(kFull, y0, src), b = __shfl_sync(kFull, y1, src);
+    v[i] = q < 2 ? a : b;
+  }
+  if (lane < 4) red_add_v4(dst + 4 * lane, v[0], v[1], v[2], v[3]);
+}
+
+// Units [0, U) of a phase starting at ring chunk Kb, unit u = (row block
+// u / GH, group u % GH); warp w takes u = w, w + 16, ...  Per row block the
+// warp's partial sums go to part[warp][rb] (zeroed by the prologue).
+__device__ __forceinline__ void mv_group_split(Ctx& c, uint32_t Kb, uint32_t U) {
+  const uint32_t GH = c.a->g.GH;
+  const int lane = c.lane, r0 = lane >> 2;
+  const uint2* xb = reinterpret_cast<const uint2*>(c.sm + OFF_XB);
+  const float* gef = reinterpret_cast<const float*>(c.sm + OFF_GEF);
+  const int* gsq = reinterpret_cast<const int*>(c.sm + OFF_GSQ);
+  float* part = reinterpret_cast<float*>(c.sm + OFF_PART) + c.warp * kD1MaxRb * 16;
+  float y0 = 0.f, y1 = 0.f;
+  uint32_t cur = 0xffffffffu, curk = 0xffffffffu;
+  const uint8_t* ch = nullptr;
+  for (uint32_t u = c.warp; u < U; u += kD1Warps) {
+    const uint32_t rbl = u / GH, gg = u % GH;
+    if (rbl != cur) {
+      if (cur != 0xffffffffu && (lane & 3) == 0) {
+        part[cur * 16 + r0] = y0;
+        part[cur * 16 + r0 + 8] = y1;
+      }
+      cur = rbl;
+      y0 = y1 = 0.f;
+    }
+    if (Kb + u / 32 != curk) {
+      curk = Kb + u / 32;
+      ch = ring_get(c, curk);
+    }
+    const uint8_t* unit = ch + (u % 32) * kD1Unit;
+    int acc[4];
+    unit_mma(unit, xb + gg * 48, lane, acc);
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(unit + 256);
+    const float ef = gef[gg];
+    unit_epi(acc, h2f(sc[r0]) * ef, h2f(sc[r0 + 8]) * ef, gsq[gg], y0, y1, lane);
+  }
+  if (cur != 0xffffffffu && (lane & 3) == 0) {
+    part[cur * 16 + r0] = y0;
+    part[cur * 16 + r0 + 8] = y1;
+  }
+}
+
+// ---- residual sources --------------------------------------------------------------
+// Four consecutive elements [k, k+4) of the layer input: the embedding row of
+// `tok` (layer 0, dequantized here) or residual buffer l & 1.
+__device__ __forceinline__ void emb4(const D1Args& a, uint32_t tok, uint32_t k, float (&v)[4]) {
+  const uint64_t f = (uint64_t)tok * a.g.H + k;
+  const uint32_t bits = (__ldg(a.emb_w + (f >> 3)) >> (f & 7)) & 0xFu;
+  const float s = h2f(__ldg(a.emb_s + f / 128));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = ((bits >> i) & 1u) ? s : -s;
+}
+__device__ __forceinline__ void layer_in4(const D1Args& a, uint32_t l, uint32_t tok, uint32_t k, float (&v)[4]) {
+  if (l == 0) {
+    emb4(a, tok, k, v);
+  } else {
+    const float4 r = __ldcg(reinterpret_cast<const float4*>(a.R + (size_t)(l & 1) * a.g.H + k));
+    v[0] = r.x; v[1] = r.y; v[2] = r.z; v[3] = r.w;
+  }
+}
+
+// RMSNorm of the input vector (H elements; warp w owns groups w and w + 16,
+// lane 4 elements of each), fp16 rounding, quantisation into the B
+// fragments of every group; clears the cross-warp partial sums.
+// kind: 0 = layer input, 1 = layer input + O accumulator, 2 = final residual.
+__device__ void norm_prologue(Ctx& c, int kind, uint32_t l, uint32_t tok, const float* nw) {
+  const D1Args& a = *c.a;
+  const uint32_t GH = a.g.GH, H = a.g.H;
+  float v[2][4];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint32_t gg = c.warp + 16 * i;
+    if (gg < GH) {
+      const uint32_t k = gg * 128 + 4 * c.lane;
+      if (kind == 2) {
+        const float4 r = __ldcg(reinterpret_cast<const float4*>(a.R + (size_t)(l & 1) * H + k));
+        v[i][0] = r.x; v[i][1] = r.y; v[i][2] = r.z; v[i][3] = r.w;
+      } else {
+        layer_in4(a, l, tok, k, v[i]);
+        if (kind == 1) {
+          const float4 z = __ldcg(reinterpret_cast<const float4*>(a.Z + (size_t)(l & 1) * H + k));
+          v[i][0] += z.x; v[i][1] += z.y; v[i][2] += z.z; v[i][3] += z.w;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) ss = fmaf(v[i][e], v[i][e], ss);
+    }
+  }
+  ss = warp_sum(ss);
+  float* red = reinterpret_cast<float*>(c.sm + OFF_RED);
+  if (c.lane == 0) red[c.warp] = ss;
+  // clear part[][] (16 x kD1MaxRb x 16 floats = 4 per thread)
+  reinterpret_cast<float4*>(c.sm + OFF_PART)[threadIdx.x] = make_float4(0.f, 0.f, 0.f, 0.f);
+  named_sync();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kD1Warps; ++w) tot += red[w];
+  const float r = 1.0f / sqrtf(tot / (float)H + a.eps);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint32_t gg = c.warp + 16 * i;
+    if (gg < GH) {
+      const uint32_t k = gg * 128 + 4 * c.lane;
+      const float4 w4 = __ldg(reinterpret_cast<const float4*>(nw + k));
+      const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+      float x[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[e] = __half2float(__float2half_rn(v[i][e] * r * wv[e]));
+      quant_group(x, gg, c.lane, c.sm);
+    }
+  }
+  named_sync();
+}
+
+// ---- attention ------------------------------------------------------------------------------
+struct AttGeo {
+  uint32_t j, s, t0, t1, nblk;
+  bool own_new;
+};
+
+__device__ __forceinline__ AttGeo att_geo(const D1Args& a, uint32_t c, int pos) {
+  AttGeo g{};
+  const uint32_t S = a.g.S, n = (uint32_t)pos + 1;
+  g.j = c / S;
+  g.s = c % S;
+  g.t0 = (uint32_t)(((uint64_t)g.s * n) / S);
+  g.t1 = (uint32_t)(((uint64_t)(g.s + 1) * n) / S);
+  g.nblk = (g.t1 - g.t0 + kD1KvBlk - 1) / kD1KvBlk;
+  g.own_new = g.t1 == n && g.t1 > g.t0;
+  return g;
+}
+
+// Thread 0: bulk-copy block `blk` of the split's cached K/V (positions < pos)
+// into stage (kvseq + blk) & 1.  Nothing is issued once the launch aborted.
+__device__ void att_issue(Ctx& c, const AttGeo& g, uint32_t l, int pos, uint32_t blk) {
+  const D1Args& a = *c.a;
+  if (c.failed || ld_relaxed_u32(&a.bar[2])) return;
+  const uint32_t seq = c.kvseq + blk, st = seq & 1u;
+  const uint32_t tb = g.t0 + blk * kD1KvBlk;
+  uint32_t te = tb + kD1KvBlk;
+  te = te < g.t1 ? te : g.t1;
+  te = te < (uint32_t)pos ? te : (uint32_t)pos;
+  const uint32_t n = te > tb ? te - tb : 0;
+  uint64_t* bar = kvbar(c.sm, st);
+  mbar_arrive_expect_tx(bar, 2 * n * 256);
+  if (n) {
+    const size_t off = (size_t)l * a.kv_layer + ((size_t)g.j * a.g.max_ctx + tb) * 128;
+    uint8_t* kd = c.sm + OFF_KV + st * 2 * KV_BLKB;
+    bulk_g2s(kd, a.kc + off, n * 256, bar);
+    bulk_g2s(kd + KV_BLKB, a.vc + off, n * 256, bar);
+  }
+  c.kv_hi = seq + 1;
+}
+
+// RMSNorm (f32) + RoPE of one 128-wide head held as 4 consecutive elements
+// per lane; the source is fp16 written in this launch (read through L2).
+__device__ __forceinline__ void norm_rope(const __half* src, const float* nw, const float2* cs, float eps,
+                                          int style, int lane, float (&v)[4]) {
+  const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(src) + lane);
+  const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+  const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+  v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+  float ss = v[0] * v[0];
+  ss = fmaf(v[1], v[1], ss);
+  ss = fmaf(v[2], v[2], ss);
+  ss = fmaf(v[3], v[3], ss);
+  ss = warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss / 128.f + eps);
+  const float4 w4 = __ldg(reinterpret_cast<const float4*>(nw) + lane);
+  v[0] = v[0] * r * w4.x; v[1] = v[1] * r * w4.y; v[2] = v[2] * r * w4.z; v[3] = v[3] * r * w4.w;
+  if (style == 0) {   // pairwise (2i, 2i+1)
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      const float2 q = __ldg(cs + (lane * 4 + e) / 2);
+      const float x0 = v[e], x1 = v[e + 1];
+      v[e] = x0 * q.x - x1 * q.y;
+      v[e + 1] = x0 * q.y + x1 * q.x;
+    }
+  } else {            // half split (i, i + 64)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float partner = __shfl_xor_sync(kFull, v[e], 16);
+      const float2 q = __ldg(cs + (lane & 15) * 4 + e);
+      v[e] = lane < 16 ? v[e] * q.x - partner * q.y : partner * q.y + v[e] * q.x;
+    }
+  }
+}
+
+__device__ void att_phase(Ctx& c, uint32_t l, int pos, uint32_t epoch_tok) {
+  const D1Args& a = *c.a;
+  const uint32_t G = a.g.G, S = a.g.S;
+  const AttGeo g = att_geo(a, c.c, pos);
+  uint8_t* sm = c.sm;
+  float* qs = reinterpret_cast<float*>(sm + OFF_QS);
+  float* sc = reinterpret_cast<float*>(sm + OFF_SC);
+  __half* knew = reinterpret_cast<__half*>(sm + OFF_KNEW);
+  __half* vnew = reinterpret_cast<__half*>(sm + OFF_VNEW);
+  float* mst = reinterpret_cast<float*>(sm + OFF_STAT);
+  float* lst = mst + kD1MaxG;
+  float* alp = lst + kD1MaxG;
+  const int warp = c.warp, lane = c.lane;
+
+  if (threadIdx.x == 0)
+    wait_count(a.cnt + (size_t)l * a.g.nkv + g.j, (epoch_tok + 1) * (G + 2) * 8, a);
+  named_sync();
+  const D1Layer& LW = a.layers[l];
+  const float2* cs = a.rope_tab + (size_t)pos * 64;
+  if ((uint32_t)warp < G) {
+    float v[4];
+    norm_rope(a.qkv + (size_t)(g.j * G + warp) * 128, LW.q_norm, cs, a.eps, a.rope_style, lane, v);
+    *reinterpret_cast<float4*>(qs + warp * 128 + 4 * lane) = make_float4(v[0], v[1], v[2], v[3]);
+  } else if ((uint32_t)warp == G && g.own_new) {
+    float v[4];
+    norm_rope(a.qkv + (size_t)(a.g.nq + g.j) * 128, LW.k_norm, cs, a.eps, a.rope_style, lane, v);
+    const __half2 k01 = __floats2half2_rn(v[0], v[1]), k23 = __floats2half2_rn(v[2], v[3]);
+    uint2 kk;
+    kk.x = *reinterpret_cast<const uint32_t*>(&k01);
+    kk.y = *reinterpret_cast<const uint32_t*>(&k23);
+    const uint2 vv = __ldcg(reinterpret_cast<const uint2*>(a.qkv + (size_t)(a.g.nq + a.g.nkv + g.j) * 128) + lane);
+    reinterpret_cast<uint2*>(knew)[lane] = kk;
+    reinterpret_cast<uint2*>(vnew)[lane] = vv;
+    const size_t off = (size_t)l * a.kv_layer + ((size_t)g.j * a.g.max_ctx + (uint32_t)pos) * 128;
+    reinterpret_cast<uint2*>(a.kc + off)[lane] = kk;
+    reinterpret_cast<uint2*>(a.vc + off)[lane] = vv;
+  }
+  if (threadIdx.x < kD1MaxG) {
+    mst[threadIdx.x] = -INFINITY;
+    lst[threadIdx.x] = 0.f;
+  }
+  named_sync();
+
+  // PV thread mapping: d = tid % 128, head gq % G, position partition gq / G
+  const uint32_t d = threadIdx.x & 127u, gq = threadIdx.x >> 7, gh = gq % G, part = gq / G, NP = 4 / G;
+  float accv = 0.f;
+  float qv[kD1MaxG][4];
+#pragma unroll
+  for (int h = 0; h < kD1MaxG; ++h) {
+    if ((uint32_t)h < G) {
+      const float4 q4 = *reinterpret_cast<const float4*>(qs + h * 128 + 4 * lane);
+      qv[h][0] = q4.x; qv[h][1] = q4.y; qv[h][2] = q4.z; qv[h][3] = q4.w;
+    }
+  }
+  const float inv = 1.0f / sqrtf(128.f);
+  for (uint32_t blk = 0; blk < g.nblk; ++blk) {
+    const uint32_t tb = g.t0 + blk * kD1KvBlk;
+    const uint32_t nb = min((uint32_t)kD1KvBlk, g.t1 - tb);
+    const uint32_t st = (c.kvseq + blk) & 1u;
+    if (!c.failed) c.failed = !wait_mbar(kvbar(sm, st), ((c.kvseq + blk) >> 1) & 1u, a);
+    const __half* kb = reinterpret_cast<const __half*>(sm + OFF_KV + st * 2 * KV_BLKB);
+    const __half* vb = reinterpret_cast<const __half*>(sm + OFF_KV + st * 2 * KV_BLKB + KV_BLKB);
+    for (uint32_t i = warp; i < nb; i += kD1Warps) {
+      const __half* kr = (tb + i == (uint32_t)pos) ? knew : kb + i * 128;
+      const uint2 raw = *reinterpret_cast<const uint2*>(kr + 4 * lane);
+      const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+      const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+#pragma unroll
+      for (int h = 0; h < kD1MaxG; ++h) {
+        if ((uint32_t)h < G) {
+          float dot = qv[h][0] * k0.x;
+          dot = fmaf(qv[h][1], k0.y, dot);
+          dot = fmaf(qv[h][2], k1.x, dot);
+          dot = fmaf(qv[h][3], k1.y, dot);
+          dot = warp_sum(dot);
+          if (lane == 0) sc[h * kD1KvBlk + i] = dot * inv;
+        }
+      }
+    }
+    named_sync();
+    if ((uint32_t)warp < G) {
+      const float sv = (uint32_t)lane < nb ? sc[warp * kD1KvBlk + lane] : -INFINITY;
+      const float mb = warp_max(sv);
+      const float mo = mst[warp], mn = fmaxf(mo, mb);
+      const float p = (uint32_t)lane < nb ? expf(sv - mn) : 0.f;
+      if ((uint32_t)lane < nb) sc[warp * kD1KvBlk + lane] = p;
+      const float ls = warp_sum(p);
+      if (lane == 0) {
+        const float al = mo == -INFINITY ? 0.f : expf(mo - mn);
+        alp[warp] = al;
+        lst[warp] = lst[warp] * al + ls;
+        mst[warp] = mn;
+      }
+    }
+    named_sync();
+    accv *= alp[gh];
+    for (uint32_t i = part; i < nb; i += NP) {
+      const __half* vr = (tb + i == (uint32_t)pos) ? vnew : vb + i * 128;
+      accv = fmaf(sc[gh * kD1KvBlk + i], __half2float(vr[d]), accv);
+    }
+    named_sync();
+    if (threadIdx.x == 0 && blk + 2 < g.nblk) att_issue(c, g, l, pos, blk + 2);
+  }
+  c.kvseq += g.nblk;
+  float* comb = reinterpret_cast<float*>(sm + OFF_COMB);
+  comb[gq * 128 + d] = accv;
+  named_sync();
+  if (threadIdx.x < G * 128) {
+    float o = 0.f;
+    for (uint32_t p = 0; p < NP; ++p) o += comb[(p * G + gh) * 128 + d];
+    float* rec = a.att + ((size_t)(g.j * S + g.s) * G + gh) * kD1AttRec;
+    rec[4 + d] = o;
+    if (d == 0) {
+      rec[0] = mst[gh];
+      rec[1] = lst[gh];
+    }
+  }
+  named_sync();
+  if (threadIdx.x == 0) red_release_u32(a.cnt + (size_t)(a.g.L + l) * a.g.nkv + g.j, 1u);
+}
+
+// ---- O projection -----------------------------------------------------------------------------
+__device__ void o_phase(Ctx& c, uint32_t l, uint32_t Kb, uint32_t epoch_tok) {
+  const D1Args& a = *c.a;
+  const D1Geom& G_ = a.g;
+  const uint32_t h = c.c / G_.nrr, r = c.c % G_.nrr;
+  const uint32_t rb0 = d1_lo(r, G_.nrb_h, G_.nrr), rb1 = d1_lo(r + 1, G_.nrb_h, G_.nrr);
+  const uint32_t j = h / G_.G, gq = h % G_.G, S = G_.S;
+  uint8_t* sm = c.sm;
+  if (threadIdx.x == 0) wait_count(a.cnt + (size_t)(G_.L + l) * G_.nkv + j, (epoch_tok + 1) * S, a);
+  named_sync();
+  // merge the head's splits: thread (part, d) folds splits part, part + 4, ...
+  const uint32_t d = threadIdx.x & 127u, part = threadIdx.x >> 7;
+  float M = -INFINITY, Ls = 0.f, O = 0.f;
+  for (uint32_t s0 = part; s0 < S; s0 += 16) {
+    float mv[4], lv[4], ov[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t s = s0 + 4 * q;
+      if (s < S) {
+        const float* rec = a.att + ((size_t)(j * S + s) * G_.G + gq) * kD1AttRec;
+        mv[q] = __ldcg(rec);
+        lv[q] = __ldcg(rec + 1);
+        ov[q] = __ldcg(rec + 4 + d);
+      } else {
+        mv[q] = -INFINITY; lv[q] = 0.f; ov[q] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (mv[q] == -INFINITY) continue;
+      const float nm = fmaxf(M, mv[q]);
+      const float a1 = M == -INFINITY ? 0.f : expf(M - nm), a2 = expf(mv[q] - nm);
+      Ls = Ls * a1 + lv[q] * a2;
+      O = O * a1 + ov[q] * a2;
+      M = nm;
+    }
+  }
+  float* mer = reinterpret_cast<float*>(sm + OFF_MER);
+  mer[part * kD1AttRec + 4 + d] = O;
+  if (d == 0) {
+    mer[part * kD1AttRec] = M;
+    mer[part * kD1AttRec + 1] = Ls;
+  }
+  named_sync();
+  float* xo = reinterpret_cast<float*>(sm + OFF_XO);
+  if (threadIdx.x < 128) {
+    float Mt = -INFINITY;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) Mt = fmaxf(Mt, mer[p * kD1AttRec]);
+    float Lt = 0.f, Ot = 0.f;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const float mp = mer[p * kD1AttRec];
+      const float f = mp == -INFINITY ? 0.f : expf(mp - Mt);
+      Lt = fmaf(f, mer[p * kD1AttRec + 1], Lt);
+      Ot = fmaf(f, mer[p * kD1AttRec + 4 + d], Ot);
+    }
+    xo[d] = __half2float(__float2half_rn(Ot / Lt));
+  }
+  named_sync();
+  if (c.warp == 0) {
+    const float4 x4 = *reinterpret_cast<const float4*>(xo + 4 * c.lane);
+    const float x[4] = {x4.x, x4.y, x4.z, x4.w};
+    quant_group(x, 0, c.lane, sm);
+  }
+  named_sync();
+  const uint2* xb = reinterpret_cast<const uint2*>(sm + OFF_XB);
+  const float ef = reinterpret_cast<const float*>(sm + OFF_GEF)[0];
+  const int sq = reinterpret_cast<const int*>(sm + OFF_GSQ)[0];
+  float* Zl = a.Z + (size_t)(l & 1) * G_.H;
+  const int r0 = c.lane >> 2;
+  for (uint32_t rb = rb0 + c.warp; rb < rb1; rb += kD1Warps) {
+    const uint32_t u = rb - rb0;
+    const uint8_t* unit = ring_get(c, Kb + u / 32) + (u % 32) * kD1Unit;
+    int acc[4];
+    unit_mma(unit, xb, c.lane, acc);
+    const uint16_t* scl = reinterpret_cast<const uint16_t*>(unit + 256);
+    float y0 = 0.f, y1 = 0.f;
+    unit_epi(acc, h2f(scl[r0]) * ef, h2f(scl[r0 + 8]) * ef, sq, y0, y1, c.lane);
+    red_rows16(Zl + rb * 16, y0, y1, c.lane);
+  }
+}
+
+// ---- gate/up + SiLU + down ---------------------------------------------------------------------
+__device__ void gudn_phase(Ctx& c, uint32_t l, uint32_t Kg, uint32_t tok) {
+  const D1Args& a = *c.a;
+  const D1Geom& g = a.g;
+  uint8_t* sm = c.sm;
+  const uint32_t i0 = d1_lo(c.c, g.nrb_i, g.P), nb = d1_lo(c.c + 1, g.nrb_i, g.P) - i0;
+  const uint32_t Kd = Kg + g.cg;
+  float* Rn = a.R + (size_t)((l + 1) & 1) * g.H;
+  if (nb) {
+    norm_prologue(c, 1, l, tok, a.layers[l].ffn_norm);
+    mv_group_split(c, Kg, 2 * nb * g.GH);
+    named_sync();
+    float* rows = reinterpret_cast<float*>(sm + OFF_ROWS);
+    if (threadIdx.x < nb * 16) {
+      const uint32_t p = threadIdx.x / 16, rr = threadIdx.x % 16;
+      const float* part = reinterpret_cast<const float*>(sm + OFF_PART);
+      float gv = 0.f, uv = 0.f;
+#pragma unroll
+      for (int w = 0; w < kD1Warps; ++w) {
+        gv += part[(w * kD1MaxRb + 2 * p) * 16 + rr];
+        uv += part[(w * kD1MaxRb + 2 * p + 1) * 16 + rr];
+      }
+      rows[threadIdx.x] = __half2float(__float2half_rn(gv / (1.0f + expf(-gv)) * uv));
+    }
+    named_sync();
+    if (c.warp == 0) {
+      const uint32_t p = c.lane >> 2;
+      const bool act = p < nb;
+      float x[4] = {0.f, 0.f, 0.f, 0.f};
+      if (act) {
+        const float4 x4 = *reinterpret_cast<const float4*>(rows + p * 16 + 4 * (c.lane & 3));
+        x[0] = x4.x; x[1] = x4.y; x[2] = x4.z; x[3] = x4.w;
+      }
+      quant_chunk16(x, p, c.lane, act, sm);
+    }
+    ring_release_upto(c, Kd);
+    named_sync();
+    // down projection: all H rows (row block R per warp step) x this CTA's nb k16 chunks
+    const uint32_t* xb16 = reinterpret_cast<const uint32_t*>(sm + OFF_XB16);
+    const float* ef16 = reinterpret_cast<const float*>(sm + OFF_EF16);
+    const int* sq16 = reinterpret_cast<const int*>(sm + OFF_SQ16);
+    const uint32_t soff = al16(nb * 32), gbase = (16 * i0) / 128;
+    const int lane = c.lane, r0 = lane >> 2;
+    uint32_t curk = 0xffffffffu;
+    const uint8_t* ch = nullptr;
+    for (uint32_t R = c.warp; R < g.nrb_h; R += kD1Warps) {
+      if (Kd + R / g.dupc != curk) {
+        curk = Kd + R / g.dupc;
+        ch = ring_get(c, curk);
+      }
+      const uint8_t* unit = ch + (R % g.dupc) * g.dub;
+      const uint16_t* scl = reinterpret_cast<const uint16_t*>(unit + soff);
+      float y0 = 0.f, y1 = 0.f;
+      for (uint32_t p = 0; p < nb; ++p) {
+        const uint32_t byte = unit[p * 32 + lane];
+        const uint32_t b = lane < 12 ? xb16[p * 12 + lane] : 0u;
+        int acc[4] = {0, 0, 0, 0};
+        mma_u8s8_k16(acc, spread4(byte & 0xFu), spread4(byte >> 4), b);
+        const uint32_t gl = (16 * (i0 + p)) / 128 - gbase;
+        const float ef = ef16[p];
+        unit_epi(acc, h2f(scl[gl * 16 + r0]) * ef, h2f(scl[gl * 16 + r0 + 8]) * ef, sq16[p], y0, y1, lane);
+      }
+      red_rows16(Rn + R * 16, y0, y1, lane);
+    }
+  }
+  ring_release_upto(c, Kd + g.cd);
+  // carry this CTA's slice of (layer input + O accumulator) into the next residual
+  const uint32_t e0 = d1_lo(c.c, g.H / 4, g.P) * 4, e1 = d1_lo(c.c + 1, g.H / 4, g.P) * 4;
+  if (threadIdx.x * 4 < e1 - e0) {
+    const uint32_t k = e0 + threadIdx.x * 4;
+    float v[4];
+    layer_in4(a, l, tok, k, v);
+    const float4 z = __ldcg(reinterpret_cast<const float4*>(a.Z + (size_t)(l & 1) * g.H + k));
+    red_add_v4(Rn + k, v[0] + z.x, v[1] + z.y, v[2] + z.z, v[3] + z.w);
+  }
+}
+
+// ---- QKV ----------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t kv_head_of_rb(const D1Geom& g, uint32_t rb) {
+  const uint32_t row = rb * 16, qd = g.nq * 128, kvd = g.nkv * 128;
+  if (row < qd) return row / (g.G * 128);
+  if (row < qd + kvd) return (row - qd) / 128;
+  return (row - qd - kvd) / 128;
+}
+
+__device__ void qkv_phase(Ctx& c, uint32_t l, uint32_t Kq, uint32_t tok) {
+  const D1Args& a = *c.a;
+  const D1Geom& g = a.g;
+  const uint32_t rb0 = d1_lo(c.c, g.nrb_qkv, g.P), rb1 = d1_lo(c.c + 1, g.nrb_qkv, g.P), nrb = rb1 - rb0;
+  // clear this CTA's slices of the next residual and the next O accumulator
+  {
+    const uint32_t e0 = d1_lo(c.c, g.H / 4, g.P) * 4, e1 = d1_lo(c.c + 1, g.H / 4, g.P) * 4;
+    if (threadIdx.x * 4 < e1 - e0) {
+      const uint32_t k = e0 + threadIdx.x * 4;
+      *reinterpret_cast<float4*>(a.R + (size_t)((l + 1) & 1) * g.H + k) = make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(a.Z + (size_t)((l + 1) & 1) * g.H + k) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  if (nrb) {
+    norm_prologue(c, 0, l, tok, a.layers[l].attn_norm);
+    mv_group_split(c, Kq, nrb * g.GH);
+    named_sync();
+    if (threadIdx.x < nrb * 16) {
+      const float* part = reinterpret_cast<const float*>(c.sm + OFF_PART);
+      const uint32_t rbl = threadIdx.x / 16, rr = threadIdx.x % 16;
+      float y = 0.f;
+#pragma unroll
+      for (int w = 0; w < kD1Warps; ++w) y += part[(w * kD1MaxRb + rbl) * 16 + rr];
+      a.qkv[rb0 * 16 + threadIdx.x] = __float2half_rn(y);
+    }
+  }
+  ring_release_upto(c, Kq + g.cq);
+  named_sync();
+  if (threadIdx.x == 0 && nrb) {
+    uint32_t rb = rb0;
+    while (rb < rb1) {
+      const uint32_t j = kv_head_of_rb(g, rb);
+      uint32_t n = 0;
+      while (rb < rb1 && kv_head_of_rb(g, rb) == j) { ++rb; ++n; }
+      red_release_u32(a.cnt + (size_t)l * g.nkv + j, n);
+    }
+  }
+}
+
+// ---- LM head --------------------------------------------------------------------------------------
+__device__ void lm_phase(Ctx& c, uint32_t Kl) {
+  const D1Args& a = *c.a;
+  const D1Geom& g = a.g;
+  uint8_t* sm = c.sm;
+  const uint32_t rb0 = d1_lo(c.c, g.nrb_v, g.P), rb1 = d1_lo(c.c + 1, g.nrb_v, g.P);
+  // the O accumulator of the last layer is free now: clear this CTA's slice
+  {
+    const uint32_t e0 = d1_lo(c.c, g.H / 4, g.P) * 4, e1 = d1_lo(c.c + 1, g.H / 4, g.P) * 4;
+    if (threadIdx.x * 4 < e1 - e0)
+      *reinterpret_cast<float4*>(a.Z + (size_t)((g.L - 1) & 1) * g.H + e0 + threadIdx.x * 4) =
+          make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  unsigned long long best = 0ull;
+  if (rb1 > rb0) {
+    norm_prologue(c, 2, g.L, 0, a.fnorm);
+    const uint2* xb = reinterpret_cast<const uint2*>(sm + OFF_XB);
+    const float* gef = reinterpret_cast<const float*>(sm + OFF_GEF);
+    const int* gsq = reinterpret_cast<const int*>(sm + OFF_GSQ);
+    const int lane = c.lane, r0 = lane >> 2;
+    uint32_t curk = 0xffffffffu;
+    const uint8_t* ch = nullptr;
+    for (uint32_t rb = rb0 + c.warp; rb < rb1; rb += kD1Warps) {
+      float y0 = 0.f, y1 = 0.f;
+      for (uint32_t gg = 0; gg < g.GH; ++gg) {
+        const uint32_t u = (rb - rb0) * g.GH + gg;
+        if (Kl + u / 32 != curk) {
+          curk = Kl + u / 32;
+          ch = ring_get(c, curk);
+        }
+        const uint8_t* unit = ch + (u % 32) * kD1Unit;
+        int acc[4];
+        unit_mma(unit, xb + gg * 48, lane, acc);
+        const uint16_t* scl = reinterpret_cast<const uint16_t*>(unit + 256);
+        const float ef = gef[gg];
+        unit_epi(acc, h2f(scl[r0]) * ef, h2f(scl[r0 + 8]) * ef, gsq[gg], y0, y1, lane);
+      }
+      if ((lane & 3) == 0) {
+        const uint32_t ra = rb * 16 + r0, rbb = ra + 8;
+        if (ra < g.V) {
+          if (a.logits) a.logits[ra] = y0;
+          const unsigned long long k = argmax_pack(y0, ra);
+          best = k > best ? k : best;
+        }
+        if (rbb < g.V) {
+          if (a.logits) a.logits[rbb] = y1;
+          const unsigned long long k = argmax_pack(y1, rbb);
+          best = k > best ? k : best;
+        }
+      }
+    }
+  }
+  ring_release_upto(c, Kl + g.clm);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(kFull, best, o);
+    best = other > best ? other : best;
+  }
+  unsigned long long* am = reinterpret_cast<unsigned long long*>(sm + OFF_AMAX);
+  if (c.lane == 0) am[c.warp] = best;
+  named_sync();
+  if (threadIdx.x == 0) {
+    unsigned long long b = 0ull;
+#pragma unroll
+    for (int w = 0; w < kD1Warps; ++w) b = am[w] > b ? am[w] : b;
+    if (b) atomicMax(&a.st->argmax[0], b);
+  }
+}
+
+// ---- producer warp ----------------------------------------------------------------------------------
+__device__ void producer(const D1Args& a, uint8_t* sm) {
+  const uint32_t c = blockIdx.x, nck = a.g.nck, total = a.ntok * nck;
+  const uint8_t* base = a.stream + (size_t)c * nck * kD1Chunk;
+  const uint32_t* cb = a.chunk_bytes + (size_t)c * nck;
+  uint32_t issued = 0;
+  for (uint32_t K = 0; K < total; ++K) {
+    const uint32_t s = K % kD1Slots, k = K % nck;
+    if (K >= (uint32_t)kD1Slots && !wait_mbar(emptyb(sm, s), ((K / kD1Slots) - 1) & 1u, a)) break;
+    if (ld_relaxed_u32(&a.bar[2])) break;
+    const uint32_t bytes = __ldg(cb + k);
+    mbar_arrive_expect_tx(fullb(sm, s), bytes);
+    if (bytes) bulk_g2s(sm + OFF_RING + s * kD1Chunk, base + (size_t)k * kD1Chunk, bytes, fullb(sm, s));
+    issued = K + 1;
+  }
+  // drain: the last copy issued into every slot has landed before the CTA exits
+  const uint32_t from = issued > (uint32_t)kD1Slots ? issued - kD1Slots : 0;
+  for (uint32_t K = from; K < issued; ++K) drain_mbar(fullb(sm, K % kD1Slots), (K / kD1Slots) & 1u);
+}
+
+__global__ void __launch_bounds__(kD1Threads, 1) d1_kernel(const __grid_constant__ D1Args a) {
+  extern __shared__ __align__(1024) uint8_t sm[];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kD1Slots; ++s) {
+      mbar_init(fullb(sm, s), 1);
+      mbar_init(emptyb(sm, s), kD1Warps);
+    }
+    mbar_init(kvbar(sm, 0), 1);
+    mbar_init(kvbar(sm, 1), 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == kD1Warps) {
+    if (lane == 0) producer(a, sm);
+    return;
+  }
+  Ctx c{};
+  c.a = &a;
+  c.sm = sm;
+  c.c = blockIdx.x;
+  c.warp = warp;
+  c.lane = lane;
+  c.bar_target = a.bar_base;
+  const D1Geom& g = a.g;
+  const bool att_cta = c.c < g.nkv * g.S;
+  const bool o_cta = c.c < g.nq * g.nrr;
+  uint32_t* tokp = reinterpret_cast<uint32_t*>(sm + OFF_TOK);
+  const bool stamps = a.prof && c.c == 0 && threadIdx.x == 0;
+  if (a.tstamp && c.c == 0 && threadIdx.x == 0) a.tstamp[0] = gtimer();
+  int pos = 0;
+  for (uint32_t t = 0; t < a.ntok; ++t) {
+    const uint32_t ep = a.epoch + t;
+    if (threadIdx.x == 0) {
+      int adv;
+      unsigned long long am;
+      uint32_t t0;
+      if (t == 0) {
+        adv = a.st->advance;
+        am = a.st->argmax[0];
+        pos = a.st->pos[0];
+        t0 = a.st->token[0];
+      } else {
+        adv = 1;
+        am = __ldcg(&a.st->argmax[0]);
+        t0 = 0;
+      }
+      uint32_t tok = adv ? argmax_index(am) : t0;
+      if (adv) ++pos;
+      int bad = 0;
+      if (tok >= g.V) { bad |= ERR_BAD_TOKEN; tok = 0; }
+      if (pos < 0 || (uint32_t)pos >= g.max_ctx) { bad |= ERR_BAD_POS; pos = pos < 0 ? 0 : (int)g.max_ctx - 1; }
+      if (bad && c.c == 0) atomicOr(a.err, bad);
+      tokp[0] = tok;
+      tokp[1] = (uint32_t)pos;
+      tokp[2] = (uint32_t)adv;
+    }
+    named_sync();
+    const uint32_t tok = tokp[0];
+    pos = (int)tokp[1];
+    const int adv = (int)tokp[2];
+    const uint32_t Kt = t * g.nck;
+    AttGeo ag{};
+    if (att_cta) ag = att_geo(a, c.c, pos);
+    for (uint32_t l = 0; l < g.L; ++l) {
+      const uint32_t Kl = Kt + l * g.cpl;
+      const bool st_l = stamps && t == 0 && l == 1;
+      if (l > 0) grid_bar(c);
+      if (st_l) a.prof[0] = gtimer();
+      if (att_cta && threadIdx.x == 0) {
+        // the cache rows were written by generic stores (earlier layers / tokens)
+        fence_proxy_async();
+        for (uint32_t b = 0; b < 2 && b < ag.nblk; ++b) att_issue(c, ag, l, pos, b);
+      }
+      qkv_phase(c, l, Kl, tok);
+      if (st_l) a.prof[1] = gtimer();
+      if (att_cta) att_phase(c, l, pos, ep);
+      if (st_l) a.prof[2] = gtimer();
+      if (o_cta) o_phase(c, l, Kl + g.cq, ep);
+      ring_release_upto(c, Kl + g.cq + g.co);
+      if (st_l) a.prof[3] = gtimer();
+      grid_bar(c);
+      if (st_l) a.prof[4] = gtimer();
+      if (l == 0 && c.c == 0 && threadIdx.x == 0) {
+        // every CTA has read the decode state of this token by now
+        a.st->pos[0] = pos;
+        a.st->token[0] = tok;
+        if (adv && a.seq && (uint32_t)pos < a.seq_len) a.seq[pos] = tok;
+        a.st->argmax[0] = 0ull;
+      }
+      gudn_phase(c, l, Kl + g.cq + g.co, tok);
+      if (st_l) a.prof[5] = gtimer();
+    }
+    grid_bar(c);
+    if (stamps && t == 0) a.prof[6] = gtimer();
+    lm_phase(c, Kt + g.L * g.cpl);
+    if (stamps && t == 0) a.prof[7] = gtimer();
+    grid_bar(c);
+    if (a.tstamp && c.c == 0 && threadIdx.x == 0) a.tstamp[t + 1] = gtimer();
+  }
+  // drain K/V copies that a failed wait skipped (the last one issued per stage)
+  if (threadIdx.x == 0 && c.kv_hi > c.kvseq) {
+    for (uint32_t s = c.kv_hi > 2 ? c.kv_hi - 2 : 0; s < c.kv_hi; ++s) drain_mbar(kvbar(sm, s & 1u), (s >> 1) & 1u);
+  }
+}
+
+// ---- host packing helpers -----------------------------------------------------------------------------
+inline uint32_t bit_at(const uint8_t* bits, uint32_t M, uint32_t K, uint32_t row, uint32_t k) {
+  if (row >= M) return 0;
+  const uint64_t f = (uint64_t)row * K + k;
+  return (bits[f >> 3] >> (f & 7)) & 1u;
+}
+inline uint16_t scale_at(const uint16_t* s, uint32_t M, uint32_t K, uint32_t row, uint32_t grp) {
+  if (row >= M) return 0;
+  return s[(uint64_t)row * (K / 128) + grp];
+}
+
+// 16 rows from row0, group gg (128 k) of an M x K matrix -> one 288-byte unit.
+void put_unit(uint8_t* dst, const uint8_t* bits, const uint16_t* s, uint32_t M, uint32_t K, uint32_t row0,
+              uint32_t gg) {
+  uint8_t tile[16][16];
+  for (uint32_t rr = 0; rr < 16; ++rr) {
+    const uint32_t row = row0 + rr;
+    if (row < M) memcpy(tile[rr], bits + ((uint64_t)row * K + gg * 128) / 8, 16);
+    else memset(tile[rr], 0, 16);
+  }
+  for (uint32_t lane = 0; lane < 32; ++lane) {
+    for (uint32_t w = 0; w < 2; ++w) {
+      uint32_t W = 0;
+      for (uint32_t b = 0; b < 32; ++b) {
+        const uint32_t s8 = b % 8, i = b / 8, j = 2 * w + s8 / 4, r = s8 % 4;
+        const uint32_t rr = lane / 4 + (r & 1) * 8;
+        const uint32_t k = j * 32 + (r >> 1) * 16 + (lane % 4) * 4 + i;
+        W |= ((uint32_t)(tile[rr][k >> 3] >> (k & 7)) & 1u) << b;
+      }
+      memcpy(dst + lane * 8 + w * 4, &W, 4);
+    }
+  }
+  for (uint32_t rr = 0; rr < 16; ++rr) {
+    const uint16_t v = scale_at(s, M, K, row0 + rr, gg);
+    memcpy(dst + 256 + rr * 2, &v, 2);
+  }
+}
+
+// Down-projection unit: row block R of the H x I matrix, K slice [16 i0, 16 (i0 + nb)).
+void put_dn_unit(uint8_t* dst, const D1Geom& g, const uint8_t* bits, const uint16_t* s, uint32_t R, uint32_t i0,
+                 uint32_t nb) {
+  const uint32_t M = g.H, K = g.I;
+  for (uint32_t p = 0; p < nb; ++p)
+    for (uint32_t lane = 0; lane < 32; ++lane) {
+      uint32_t byte = 0;
+      for (uint32_t r = 0; r < 2; ++r)
+        for (uint32_t i = 0; i < 4; ++i) {
+          const uint32_t row = R * 16 + lane / 4 + 8 * r, k = 16 * (i0 + p) + (lane % 4) * 4 + i;
+          byte |= bit_at(bits, M, K, row, k) << (r * 4 + i);
+        }
+      dst[p * 32 + lane] = (uint8_t)byte;
+    }
+  const uint32_t soff = al16(nb * 32), ng = d1_dn_groups(i0, nb), gb = (16 * i0) / 128;
+  for (uint32_t gl = 0; gl < ng; ++gl)
+    for (uint32_t rr = 0; rr < 16; ++rr) {
+      const uint16_t v = scale_at(s, M, K, R * 16 + rr, gb + gl);
+      memcpy(dst + soff + gl * 32 + rr * 2, &v, 2);
+    }
+}
+
+}  // namespace
+
+uint32_t d1_smem_bytes() { return SMEM_TOTAL; }
+
+bool d1_fits(int device, uint32_t P) {
+  int nsm = 0, coop = 0, per = 0;
+  if (cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (!coop || (uint32_t)nsm < P) return false;
+  if (cudaFuncSetAttribute(d1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_TOTAL) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, d1_kernel, kD1Threads, SMEM_TOTAL) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return per >= 1;
+}
+
+cudaError_t d1_launch(const D1Args& a, cudaStream_t st) {
+  void* args[] = {const_cast<D1Args*>(&a)};
+  return cudaLaunchCooperativeKernel((const void*)d1_kernel, dim3(a.g.P), dim3(kD1Threads), args, SMEM_TOTAL, st);
+}
+
+void d1_chunk_bytes(const D1Geom& g, std::vector<uint32_t>& out) {
+  out.assign((size_t)g.P * g.nck, 0u);
+  auto fill = [](uint32_t* dst, uint32_t nchunks, uint32_t units, uint32_t per, uint32_t ubytes) {
+    for (uint32_t q = 0; q < nchunks; ++q) {
+      const uint32_t n = units > q * per ? (units - q * per < per ? units - q * per : per) : 0;
+      dst[q] = n * ubytes;
+    }
+  };
+  for (uint32_t c = 0; c < g.P; ++c) {
+    uint32_t* row = out.data() + (size_t)c * g.nck;
+    const uint32_t nq_rb = d1_lo(c + 1, g.nrb_qkv, g.P) - d1_lo(c, g.nrb_qkv, g.P);
+    const uint32_t nb = d1_lo(c + 1, g.nrb_i, g.P) - d1_lo(c, g.nrb_i, g.P);
+    uint32_t o_rb = 0;
+    if (c < g.nq * g.nrr) {
+      const uint32_t r = c % g.nrr;
+      o_rb = d1_lo(r + 1, g.nrb_h, g.nrr) - d1_lo(r, g.nrb_h, g.nrr);
+    }
+    for (uint32_t l = 0; l < g.L; ++l) {
+      uint32_t* L0 = row + (size_t)l * g.cpl;
+      fill(L0, g.cq, nq_rb * g.GH, 32, kD1Unit);
+      fill(L0 + g.cq, g.co, o_rb, 32, kD1Unit);
+      fill(L0 + g.cq + g.co, g.cg, 2 * nb * g.GH, 32, kD1Unit);
+      fill(L0 + g.cq + g.co + g.cg, g.cd, nb ? g.nrb_h : 0, g.dupc, g.dub);
+    }
+    const uint32_t lm_rb = d1_lo(c + 1, g.nrb_v, g.P) - d1_lo(c, g.nrb_v, g.P);
+    fill(row + (size_t)g.L * g.cpl, g.clm, lm_rb * g.GH, 32, kD1Unit);
+  }
+}
+
+void d1_pack_layer(const D1Geom& g, const uint8_t* qkv_w, const uint16_t* qkv_s, const uint8_t* o_w,
+                   const uint16_t* o_s, const uint8_t* gate_w, const uint16_t* gate_s, const uint8_t* up_w,
+                   const uint16_t* up_s, const uint8_t* dn_w, const uint16_t* dn_s, uint8_t* dst) {
+  const size_t stride = (size_t)g.cpl * kD1Chunk;
+  for (uint32_t c = 0; c < g.P; ++c) {
+    uint8_t* base = dst + (size_t)c * stride;
+    memset(base, 0, stride);
+    // QKV: units (rb, group) rb-major
+    {
+      const uint32_t rb0 = d1_lo(c, g.nrb_qkv, g.P), rb1 = d1_lo(c + 1, g.nrb_qkv, g.P);
+      uint32_t u = 0;
+      for (uint32_t rb = rb0; rb < rb1; ++rb)
+        for (uint32_t gg = 0; gg < g.GH; ++gg, ++u)
+          put_unit(base + (u / 32) * kD1Chunk + (u % 32) * kD1Unit, qkv_w, qkv_s, g.qkv_rows, g.H, rb * 16, gg);
+    }
+    // O: (head h, row range r): rbs of the range, group h of K = nq * 128
+    if (c < g.nq * g.nrr) {
+      const uint32_t h = c / g.nrr, r = c % g.nrr;
+      const uint32_t rb0 = d1_lo(r, g.nrb_h, g.nrr), rb1 = d1_lo(r + 1, g.nrb_h, g.nrr);
+      uint8_t* ob = base + (size_t)g.cq * kD1Chunk;
+      for (uint32_t rb = rb0; rb < rb1; ++rb) {
+        const uint32_t u = rb - rb0;
+        put_unit(ob + (u / 32) * kD1Chunk + (u % 32) * kD1Unit, o_w, o_s, g.H, g.nq * 128, rb * 16, h);
+      }
+    }
+    const uint32_t i0 = d1_lo(c, g.nrb_i, g.P), nb = d1_lo(c + 1, g.nrb_i, g.P) - i0;
+    // gate/up: pair p -> gate rb (GH units), up rb (GH units)
+    {
+      uint8_t* gb = base + (size_t)(g.cq + g.co) * kD1Chunk;
+      uint32_t u = 0;
+      for (uint32_t p = 0; p < nb; ++p)
+        for (uint32_t half = 0; half < 2; ++half)
+          for (uint32_t gg = 0; gg < g.GH; ++gg, ++u)
+            put_unit(gb + (u / 32) * kD1Chunk + (u % 32) * kD1Unit, half ? up_w : gate_w, half ? up_s : gate_s,
+                     g.I, g.H, (i0 + p) * 16, gg);
+    }
+    if (nb) {
+      uint8_t* db = base + (size_t)(g.cq + g.co + g.cg) * kD1Chunk;
+      for (uint32_t R = 0; R < g.nrb_h; ++R)
+        put_dn_unit(db + (R / g.dupc) * kD1Chunk + (R % g.dupc) * g.dub, g, dn_w, dn_s, R, i0, nb);
+    }
+  }
+}
+
+void d1_pack_lm(const D1Geom& g, const uint8_t* w, const uint16_t* s, uint8_t* dst) {
+  const size_t stride = (size_t)g.clm * kD1Chunk;
+  for (uint32_t c = 0; c < g.P; ++c) {
+    uint8_t* base = dst + (size_t)c * stride;
+    memset(base, 0, stride);
+    const uint32_t rb0 = d1_lo(c, g.nrb_v, g.P), rb1 = d1_lo(c + 1, g.nrb_v, g.P);
+    uint32_t u = 0;
+    for (uint32_t rb = rb0; rb < rb1; ++rb)
+      for (uint32_t gg = 0; gg < g.GH; ++gg, ++u)
+        put_unit(base + (u / 32) * kD1Chunk + (u % 32) * kD1Unit, w, s, g.V, g.H, rb * 16, gg);
+  }
+}
+
+}  // namespace nnz

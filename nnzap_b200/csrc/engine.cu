@@ -23,6 +23,7 @@
 
 #include "../../include/nnz_b200.h"
 #include "attn.cuh"
+#include "decode1.cuh"
 #include "gemm.cuh"
 #include "mega.cuh"
 #include "misc.cuh"
@@ -247,6 +248,12 @@ struct nnz_model {
   struct MegaPlan { MegaArgs a; uint32_t grid, smem; bool ok; };
   std::map<uint32_t, MegaPlan> mplans;
   std::vector<cudaEvent_t> events;
+  // single-row Q1 decode kernel (decode1.cu)
+  bool d1_ok = false;
+  D1Args d1{};
+  unsigned long long d1_bar_count = 0;   // grid-barrier arrivals so far
+  uint32_t d1_epoch = 0;                 // tokens decoded since the counters were cleared
+  size_t d1_cnt_words = 0;
 };
 
 namespace {
@@ -607,6 +614,13 @@ int sync_check(nnz_model* m) {
     cudaMemset(m->err, 0, 4);
     if (m->mbar) cudaMemset(m->mbar, 0, 64);   // clear a persistent-kernel abort
     m->mbar_count = 0;
+    if (m->d1_ok) {   // single-row kernel: clear counters, barrier and accumulators
+      cudaMemset(m->d1.bar, 0, 64);
+      cudaMemset(m->d1.cnt, 0, m->d1_cnt_words * 4);
+      cudaMemset(m->d1.R, 0, 4 * (size_t)m->c.hidden_size * 4);
+      m->d1_bar_count = 0;
+      m->d1_epoch = 0;
+    }
     return fail(flags & (ERR_MBAR_TIMEOUT | ERR_SPIN_TIMEOUT) ? NNZ_ETIMEDOUT : NNZ_EDEVICE,
                 err_text(flags));
   }
@@ -672,7 +686,26 @@ const nnz_model::MegaPlan* mega_plan_for(nnz_model* m, uint32_t rows) {
 
 // One decode step for `rows` rows from the device decode state: the
 // persistent kernel when it applies, else the captured multi-kernel graph.
+// `ntok` greedy steps of the single-row kernel in one launch (token and
+// position advance on the device exactly as `ntok` separate steps would).
+int d1_run(nnz_model* m, uint32_t ntok, bool want_logits) {
+  if (m->d1_epoch + ntok > (1u << 24)) {   // keep the per-layer counters far from wrapping
+    NNZ_CK(cudaMemsetAsync(m->d1.cnt, 0, m->d1_cnt_words * 4, m->st));
+    m->d1_epoch = 0;
+  }
+  D1Args a = m->d1;
+  a.ntok = ntok;
+  a.logits = want_logits ? m->logits : nullptr;
+  a.bar_base = m->d1_bar_count;
+  a.epoch = m->d1_epoch;
+  NNZ_CK(d1_launch(a, m->st));
+  m->d1_bar_count += (unsigned long long)a.g.P * ntok * d1_barriers_per_token(a.g);
+  m->d1_epoch += ntok;
+  return NNZ_OK;
+}
+
 int run_step(nnz_model* m, uint32_t rows, bool want_logits) {
+  if (rows == 1 && m->d1_ok) return d1_run(m, 1, want_logits);
   if (const nnz_model::MegaPlan* P = mega_plan_for(m, rows)) {
     MegaArgs a = P->a;
     a.logits = want_logits ? m->logits : nullptr;
@@ -1000,6 +1033,29 @@ static int model_finalize_impl(nnz_model* m) {
   m->arena_bytes = off;
   int rc;
   if ((rc = dalloc(m, (void**)&m->arena, m->arena_bytes))) return rc;
+  // single-row decode kernel: Q1 g128, head_dim 128, one GPU, every SM
+  D1Geom d1g{};
+  std::vector<uint8_t> d1buf;
+  uint8_t* d1_stream = nullptr;
+  {
+    const char* path = getenv("NNZ_DECODE_PATH");
+    const bool off = path && (strcmp(path, "graph") == 0 || strcmp(path, "mega") == 0);
+    m->d1_ok = !off && fmt == NNZ_Q1 && gs == 128 && c.head_dim == 128 && m->tp == 1 && !m->bf16r &&
+               d1_geom(d1g, (uint32_t)m->num_sms, H, I, c.num_query_heads, c.num_kv_heads, c.num_layers,
+                       m->lm_rows, c.max_context_length) &&
+               d1_fits(m->device, d1g.P);
+    if (m->d1_ok) {
+      if ((rc = dalloc(m, (void**)&d1_stream, (size_t)d1g.P * d1g.nck * kD1Chunk))) return rc;
+      d1buf.resize((size_t)d1g.P * std::max(d1g.cpl, d1g.clm) * kD1Chunk);
+    }
+  }
+  auto d1_upload = [&](size_t chunk0, uint32_t nchunks) -> int {
+    NNZ_CK(cudaMemcpy2D(d1_stream + chunk0 * kD1Chunk, (size_t)d1g.nck * kD1Chunk, d1buf.data(),
+                        (size_t)nchunks * kD1Chunk, (size_t)nchunks * kD1Chunk, d1g.P, cudaMemcpyHostToDevice));
+    return NNZ_OK;
+  };
+  std::vector<uint8_t> d1qw, d1ow, d1gw, d1uw;
+  std::vector<uint16_t> d1qs, d1os, d1gs, d1us;
   std::vector<uint8_t> buf;
   std::vector<uint8_t> w;
   std::vector<uint16_t> s, b;
@@ -1019,6 +1075,7 @@ static int model_finalize_impl(nnz_model* m) {
         bc.insert(bc.end(), b.begin(), b.end());
       }
       if (m->gemm_prefill && (rc = upload_flat(m, wc, sc, bc, &m->L[l].fqkv))) return rc;
+      if (m->d1_ok) { d1qw = wc; d1qs = sc; }
       buf.assign(b_qkv, 0);
       pack_host(fmt, wc.data(), sc.data(), bc.empty() ? nullptr : bc.data(), m->qkv_rows, H, gs, 1, 0,
                 buf.data(), 0);
@@ -1026,19 +1083,27 @@ static int model_finalize_impl(nnz_model* m) {
     }
     if ((rc = get_proj_tp(m, pre + "self_attn.o_proj", H, m->qd, 1, w, s, b))) return rc;
     if (m->gemm_prefill && (rc = upload_flat(m, w, s, b, &m->L[l].fo))) return rc;
+    if (m->d1_ok) { d1ow = w; d1os = s; }
     buf.assign(b_o, 0);
     pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), H, m->qd, gs, 1, 0, buf.data(), 0);
     NNZ_CK(cudaMemcpy(m->arena + lo[l].o, buf.data(), b_o, cudaMemcpyHostToDevice));
     buf.assign(b_gu, 0);
     if ((rc = get_proj_tp(m, pre + "mlp.gate_proj", I, H, 0, w, s, b))) return rc;
     if (m->gemm_prefill && (rc = upload_flat(m, w, s, b, &m->L[l].fgate))) return rc;
+    if (m->d1_ok) { d1gw = w; d1gs = s; }
     pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), I, H, gs, 2, 0, buf.data(), 0);
     if ((rc = get_proj_tp(m, pre + "mlp.up_proj", I, H, 0, w, s, b))) return rc;
     if (m->gemm_prefill && (rc = upload_flat(m, w, s, b, &m->L[l].fup))) return rc;
+    if (m->d1_ok) { d1uw = w; d1us = s; }
     pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), I, H, gs, 2, 1, buf.data(), 0);
     NNZ_CK(cudaMemcpy(m->arena + lo[l].gu, buf.data(), b_gu, cudaMemcpyHostToDevice));
     if ((rc = get_proj_tp(m, pre + "mlp.down_proj", H, I, 1, w, s, b))) return rc;
     if (m->gemm_prefill && (rc = upload_flat(m, w, s, b, &m->L[l].fdown))) return rc;
+    if (m->d1_ok) {
+      d1_pack_layer(d1g, d1qw.data(), d1qs.data(), d1ow.data(), d1os.data(), d1gw.data(), d1gs.data(),
+                    d1uw.data(), d1us.data(), w.data(), s.data(), d1buf.data());
+      if ((rc = d1_upload((size_t)l * d1g.cpl, d1g.cpl))) return rc;
+    }
     buf.assign(b_dn, 0);
     pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), H, I, gs, 1, 0, buf.data(), 0);
     NNZ_CK(cudaMemcpy(m->arena + lo[l].dn, buf.data(), b_dn, cudaMemcpyHostToDevice));
@@ -1079,6 +1144,11 @@ static int model_finalize_impl(nnz_model* m) {
     m->flm.w = m->arena + o_embw;
     m->flm.s = reinterpret_cast<const uint16_t*>(m->arena + o_embs);
     m->flm.b = fmt == NNZ_Q4 ? reinterpret_cast<const uint16_t*>(m->arena + o_embb) : nullptr;
+  }
+  if (m->d1_ok) {
+    d1_pack_lm(d1g, w.data(), s.data(), d1buf.data());
+    if ((rc = d1_upload((size_t)c.num_layers * d1g.cpl, d1g.clm))) return rc;
+    std::vector<uint8_t>().swap(d1buf);
   }
   buf.assign(b_lm, 0);
   pack_host(fmt, w.data(), s.data(), b.empty() ? nullptr : b.data(), m->lm_rows, H, gs, 1, 0,
@@ -1195,6 +1265,53 @@ static int model_finalize_impl(nnz_model* m) {
         ml[l] = MegaLayer{W.qkv, W.o, W.gu, W.down, W.attn_norm, W.ffn_norm, W.q_norm, W.k_norm};
       }
       NNZ_CK(cudaMemcpy(m->mlayers, ml.data(), sizeof(MegaLayer) * ml.size(), cudaMemcpyHostToDevice));
+    }
+  }
+  if (m->d1_ok) {
+    D1Args& a = m->d1;
+    a.g = d1g;
+    a.eps = c.eps;
+    a.rope_style = c.rope_style;
+    a.rope_tab = m->rope_tab;
+    a.stream = d1_stream;
+    std::vector<uint32_t> cb;
+    d1_chunk_bytes(d1g, cb);
+    uint32_t* dcb = nullptr;
+    if ((rc = dalloc(m, (void**)&dcb, cb.size() * 4))) return rc;
+    NNZ_CK(cudaMemcpy(dcb, cb.data(), cb.size() * 4, cudaMemcpyHostToDevice));
+    a.chunk_bytes = dcb;
+    std::vector<D1Layer> dl(c.num_layers);
+    for (uint32_t l = 0; l < c.num_layers; ++l)
+      dl[l] = D1Layer{m->L[l].attn_norm, m->L[l].ffn_norm, m->L[l].q_norm, m->L[l].k_norm};
+    D1Layer* ddl = nullptr;
+    if ((rc = dalloc(m, (void**)&ddl, dl.size() * sizeof(D1Layer)))) return rc;
+    NNZ_CK(cudaMemcpy(ddl, dl.data(), dl.size() * sizeof(D1Layer), cudaMemcpyHostToDevice));
+    a.layers = ddl;
+    a.fnorm = m->fnorm;
+    a.emb_w = m->emb_w;
+    a.emb_s = m->emb_s;
+    a.kc = m->kc;
+    a.vc = m->vc;
+    a.kv_layer = m->kv_layer;
+    if ((rc = dalloc(m, (void**)&a.R, 4 * (size_t)H * 4))) return rc;
+    a.Z = a.R + 2 * H;
+    NNZ_CK(cudaMemset(a.R, 0, 4 * (size_t)H * 4));
+    if ((rc = dalloc(m, (void**)&a.qkv, (size_t)d1g.qkv_rows * 2))) return rc;
+    if ((rc = dalloc(m, (void**)&a.att, (size_t)c.num_kv_heads * d1g.S * d1g.G * kD1AttRec * 4))) return rc;
+    m->d1_cnt_words = (size_t)2 * c.num_layers * c.num_kv_heads;
+    if ((rc = dalloc(m, (void**)&a.cnt, m->d1_cnt_words * 4))) return rc;
+    NNZ_CK(cudaMemset(a.cnt, 0, m->d1_cnt_words * 4));
+    if ((rc = dalloc(m, (void**)&a.bar, 64))) return rc;
+    NNZ_CK(cudaMemset(a.bar, 0, 64));
+    a.st = m->state;
+    a.seq = m->seq;
+    a.seq_len = c.max_context_length;
+    a.err = m->err;
+    if ((rc = dalloc(m, (void**)&a.tstamp, ((size_t)c.max_context_length + 1) * 8))) return rc;
+    const char* prof = getenv("NNZ_D1_PROFILE");
+    if (prof && prof[0] == '1') {
+      if ((rc = dalloc(m, (void**)&a.prof, 64 * 8))) return rc;
+      NNZ_CK(cudaMemset(a.prof, 0, 64 * 8));
     }
   }
   NNZ_CK(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking));
@@ -1376,7 +1493,12 @@ int nnz_generate(nnz_model* m, const nnz_generate_opts* o, nnz_generate_result* 
   NNZ_CK(cudaMemcpyAsync(m->state->pos, &p, 4, cudaMemcpyHostToDevice, m->st));
   if ((rc = set_advance(m, 1))) return rc;
   NNZ_CK(cudaEventRecord(m->events[1], m->st));
-  for (uint32_t i = 0; i < steps; ++i) {
+  const bool one_launch = m->d1_ok && !sample;
+  if (one_launch) {
+    if ((rc = d1_run(m, steps, false))) return rc;
+    NNZ_CK(cudaEventRecord(m->events[2], m->st));
+  }
+  for (uint32_t i = 0; i < steps && !one_launch; ++i) {
     if ((rc = run_step(m, 1, sample))) return rc;
     if (sample && i + 1 < steps)
       NNZ_CK(sample_launch(m->logits, 1, m->lm_rows, m->lm_rows, o->temperature, o->top_k, o->top_p,
@@ -1385,6 +1507,9 @@ int nnz_generate(nnz_model* m, const nnz_generate_opts* o, nnz_generate_result* 
   }
   std::vector<uint32_t> toks(steps);
   NNZ_CK(cudaMemcpyAsync(toks.data(), m->seq + n, (size_t)steps * 4, cudaMemcpyDeviceToHost, m->st));
+  std::vector<unsigned long long> stamps(one_launch ? steps + 1 : 0);
+  if (one_launch)
+    NNZ_CK(cudaMemcpyAsync(stamps.data(), m->d1.tstamp, stamps.size() * 8, cudaMemcpyDeviceToHost, m->st));
   if ((rc = set_advance(m, 0))) return rc;
   if ((rc = sync_check(m))) return rc;
   float ms = 0.f;
@@ -1397,8 +1522,20 @@ int nnz_generate(nnz_model* m, const nnz_generate_opts* o, nnz_generate_result* 
     for (uint32_t k = 0; k < o->n_eos; ++k) eos |= (o->eos_ids && toks[i] == o->eos_ids[k]);
     if (eos) break;
     o->output_tokens[count] = toks[i];
-    NNZ_CK(cudaEventElapsedTime(&ms, m->events[1 + i], m->events[2 + i]));
-    const uint64_t ns = (uint64_t)((double)ms * 1e6);
+    uint64_t ns;
+    if (one_launch) {
+      // per-token device time from the kernel's %globaltimer stamps; the
+      // launch latency (event time minus stamped time) goes to the first token
+      ns = stamps[i + 1] - stamps[i];
+      if (i == 0) {
+        NNZ_CK(cudaEventElapsedTime(&ms, m->events[1], m->events[2]));
+        const double total = (double)ms * 1e6, stamped = (double)(stamps[steps] - stamps[0]);
+        if (total > stamped) ns += (uint64_t)(total - stamped);
+      }
+    } else {
+      NNZ_CK(cudaEventElapsedTime(&ms, m->events[1 + i], m->events[2 + i]));
+      ns = (uint64_t)((double)ms * 1e6);
+    }
     if (o->per_token_ns) o->per_token_ns[count] = ns;
     decode_ns += ns;
     ++count;
@@ -1697,6 +1834,16 @@ int nnz_attn_decode(const void* qkv, const float* q_norm, const float* k_norm, v
 int nnz_debug_gemm_profile(uint64_t* out) {
   if (!out) return fail(NNZ_EINVAL, "null");
   NNZ_CK(gemm_debug_profile(reinterpret_cast<unsigned long long*>(out)));
+  return NNZ_OK;
+}
+
+// Development aid (not part of the documented ABI): %globaltimer stamps of
+// the single-row decode kernel's CTA 0 (layer 1 phases of the first token of
+// the last launch) when the model was finalized with NNZ_D1_PROFILE=1.
+int nnz_debug_decode1_profile(nnz_model* m, uint64_t* out, uint32_t n) {
+  if (!m || !out || !m->d1_ok || !m->d1.prof) return fail(NNZ_ESTATE, "profiling not enabled");
+  NNZ_CK(cudaStreamSynchronize(m->st));
+  NNZ_CK(cudaMemcpy(out, m->d1.prof, 8 * std::min<uint32_t>(n, 64), cudaMemcpyDeviceToHost));
   return NNZ_OK;
 }
 
