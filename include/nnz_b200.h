@@ -208,7 +208,18 @@ int nnz_tp_init(nnz_model* m, const void* unique_id, size_t len);
 
 /* ---- per-kernel entry points on device pointers --------------------- */
 /* All asynchronous on `stream` (a cudaStream_t, NULL = default stream).
- * They share a per-device workspace allocated on first use. */
+ * They share a per-device workspace allocated on first use, except
+ * nnz_qmv_noalloc, which allocates nothing (see its comment).  Errors the
+ * kernels detect on the device are reported by nnz_stream_check. */
+
+/* Waits for `stream` and returns the device-side errors raised since the
+ * last check by the per-kernel entry points' launches on the current
+ * device: NNZ_ETIMEDOUT when a bounded wait inside a kernel gave up (its
+ * output is then invalid), NNZ_EDEVICE for an out-of-range position or
+ * token id; the flags are cleared.  Allocates nothing.  No counterpart in
+ * the reference (its kernels have no device-side error reporting: Metal
+ * command buffers, nnmetal/src/metal.zig:1325-1352). */
+int nnz_stream_check(void* stream);
 
 /* nnz_qmv without any device allocation, for callers that cannot allocate
  * device memory once running (a host that gave the whole device memory
@@ -221,7 +232,8 @@ int nnz_tp_init(nnz_model* m, const void* unique_id, size_t len);
  * share that array: calls that overlap on the GPU race, so issue them on one
  * stream.  The first call on a device does one-time set-up (device
  * addresses of the array, kernel attributes); make it before any stream
- * capture starts on that device. */
+ * capture starts on that device.  A bounded wait that gives up inside the
+ * kernel is reported by nnz_stream_check, not by the call itself. */
 int nnz_qmv_noalloc(int fmt, int scale_dtype, int bf16_round, const void* packed, uint32_t M,
                     uint32_t K, uint32_t gs, const void* x, uint32_t x_stride, uint32_t batch,
                     void* out, uint32_t out_stride, int out_kind, void* stream);

@@ -96,6 +96,7 @@ SIGNATURES = [
     ("nnz_unpack_weights", I32, [I32, P, U32, U32, U32, U32, U32, P, P, P]),
     ("nnz_dequant", I32, [I32, I32, P, U32, U32, U32, U32, U32, P, P]),
     ("nnz_qmv", I32, [I32, I32, I32, P, U32, U32, U32, P, U32, U32, P, U32, I32, P]),
+    ("nnz_stream_check", I32, [P]),
     ("nnz_qmv_noalloc", I32, [I32, I32, I32, P, U32, U32, U32, P, U32, U32, P, U32, I32, P]),
     ("nnz_qmv_norm", I32, [I32, I32, I32, P, U32, U32, U32, P, P, F32, U32, P, U32, I32, P]),
     ("nnz_lm_head_argmax", I32, [I32, I32, I32, P, U32, U32, U32, P, P, F32, U32, P, P, P]),

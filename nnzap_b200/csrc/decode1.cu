@@ -132,7 +132,10 @@ struct Ctx {
   unsigned long long bar_target; // thread 0: grid-barrier arrival target
   uint32_t kvseq;                // K/V blocks consumed by this CTA so far
   uint32_t kv_hi;                // thread 0: K/V block sequence numbers issued so far
+  unsigned long long* pf;        // profiling: non-null on the one thread that records stamps
 };
+// Profiling stamp (NNZ_D1_PROFILE=1): thread 0 of CTA 0, layer 1 of the first token.
+#define D1_STAMP(c, i) do { if ((c).pf) (c).pf[i] = gtimer(); } while (0)
 
 __device__ __forceinline__ uint64_t* fullb(uint8_t* sm, uint32_t s) { return reinterpret_cast<uint64_t*>(sm + OFF_BAR) + s; }
 __device__ __forceinline__ uint64_t* emptyb(uint8_t* sm, uint32_t s) {
@@ -556,6 +559,7 @@ __device__ void att_phase(Ctx& c, uint32_t l, int pos, uint32_t epoch_tok) {
   if (threadIdx.x == 0)
     wait_count(a.cnt + (size_t)l * a.g.nkv + g.j, (epoch_tok + 1) * (G + 2) * 8, a);
   named_sync();
+  D1_STAMP(c, 12);
   const D1Layer& LW = a.layers[l];
   const float2* cs = a.rope_tab + (size_t)pos * 64;
   if ((uint32_t)warp < G) {
@@ -582,6 +586,7 @@ __device__ void att_phase(Ctx& c, uint32_t l, int pos, uint32_t epoch_tok) {
   }
   named_sync();
 
+  D1_STAMP(c, 13);
   // PV thread mapping: d = tid % 128, head gq % G, position partition gq / G
   const uint32_t d = threadIdx.x & 127u, gq = threadIdx.x >> 7, gh = gq % G, part = gq / G, NP = 4 / G;
   float accv = 0.f;
@@ -643,6 +648,7 @@ __device__ void att_phase(Ctx& c, uint32_t l, int pos, uint32_t epoch_tok) {
     if (threadIdx.x == 0 && blk + 2 < g.nblk) att_issue(c, g, l, pos, blk + 2);
   }
   c.kvseq += g.nblk;
+  D1_STAMP(c, 14);
   float* comb = reinterpret_cast<float*>(sm + OFF_COMB);
   comb[gq * 128 + d] = accv;
   named_sync();
@@ -670,6 +676,7 @@ __device__ void o_phase(Ctx& c, uint32_t l, uint32_t Kb, uint32_t epoch_tok) {
   uint8_t* sm = c.sm;
   if (threadIdx.x == 0) wait_count(a.cnt + (size_t)(G_.L + l) * G_.nkv + j, (epoch_tok + 1) * S, a);
   named_sync();
+  D1_STAMP(c, 15);
   // merge the head's splits: thread (part, d) folds splits part, part + 4, ...
   const uint32_t d = threadIdx.x & 127u, part = threadIdx.x >> 7;
   float M = -INFINITY, Ls = 0.f, O = 0.f;
@@ -726,6 +733,7 @@ __device__ void o_phase(Ctx& c, uint32_t l, uint32_t Kb, uint32_t epoch_tok) {
     quant_group(x, 0, c.lane, sm);
   }
   named_sync();
+  D1_STAMP(c, 16);
   const uint2* xb = reinterpret_cast<const uint2*>(sm + OFF_XB);
   const float ef = reinterpret_cast<const float*>(sm + OFF_GEF)[0];
   const int sq = reinterpret_cast<const int*>(sm + OFF_GSQ)[0];
@@ -753,7 +761,9 @@ __device__ void gudn_phase(Ctx& c, uint32_t l, uint32_t Kg, uint32_t tok) {
   float* Rn = a.R + (size_t)((l + 1) & 1) * g.H;
   if (nb) {
     norm_prologue(c, 1, l, tok, a.layers[l].ffn_norm);
+    D1_STAMP(c, 17);
     mv_group_split(c, Kg, 2 * nb * g.GH);
+    D1_STAMP(c, 18);
     named_sync();
     float* rows = reinterpret_cast<float*>(sm + OFF_ROWS);
     if (threadIdx.x < nb * 16) {
@@ -780,6 +790,7 @@ __device__ void gudn_phase(Ctx& c, uint32_t l, uint32_t Kg, uint32_t tok) {
     }
     ring_release_upto(c, Kd);
     named_sync();
+    D1_STAMP(c, 19);
     // down projection: all H rows (row block R per warp step) x this CTA's nb k16 chunks
     const uint32_t* xb16 = reinterpret_cast<const uint32_t*>(sm + OFF_XB16);
     const float* ef16 = reinterpret_cast<const float*>(sm + OFF_EF16);
@@ -807,6 +818,7 @@ __device__ void gudn_phase(Ctx& c, uint32_t l, uint32_t Kg, uint32_t tok) {
       }
       red_rows16(Rn + R * 16, y0, y1, lane);
     }
+    D1_STAMP(c, 20);
   }
   ring_release_upto(c, Kd + g.cd);
   // carry this CTA's slice of (layer input + O accumulator) into the next residual
@@ -842,8 +854,11 @@ __device__ void qkv_phase(Ctx& c, uint32_t l, uint32_t Kq, uint32_t tok) {
     }
   }
   if (nrb) {
+    D1_STAMP(c, 8);
     norm_prologue(c, 0, l, tok, a.layers[l].attn_norm);
+    D1_STAMP(c, 9);
     mv_group_split(c, Kq, nrb * g.GH);
+    D1_STAMP(c, 10);
     named_sync();
     if (threadIdx.x < nrb * 16) {
       const float* part = reinterpret_cast<const float*>(c.sm + OFF_PART);
@@ -856,6 +871,7 @@ __device__ void qkv_phase(Ctx& c, uint32_t l, uint32_t Kq, uint32_t tok) {
   }
   ring_release_upto(c, Kq + g.cq);
   named_sync();
+  D1_STAMP(c, 11);
   if (threadIdx.x == 0 && nrb) {
     uint32_t rb = rb0;
     while (rb < rb1) {
@@ -883,6 +899,7 @@ __device__ void lm_phase(Ctx& c, uint32_t Kl) {
   unsigned long long best = 0ull;
   if (rb1 > rb0) {
     norm_prologue(c, 2, g.L, 0, a.fnorm);
+    D1_STAMP(c, 21);
     const uint2* xb = reinterpret_cast<const uint2*>(sm + OFF_XB);
     const float* gef = reinterpret_cast<const float*>(sm + OFF_GEF);
     const int* gsq = reinterpret_cast<const int*>(sm + OFF_GSQ);
@@ -1023,6 +1040,7 @@ __global__ void __launch_bounds__(kD1Threads, 1) d1_kernel(const __grid_constant
     for (uint32_t l = 0; l < g.L; ++l) {
       const uint32_t Kl = Kt + l * g.cpl;
       const bool st_l = stamps && t == 0 && l == 1;
+      c.pf = st_l ? a.prof : nullptr;
       if (l > 0) grid_bar(c);
       if (st_l) a.prof[0] = gtimer();
       if (att_cta && threadIdx.x == 0) {
@@ -1049,10 +1067,13 @@ __global__ void __launch_bounds__(kD1Threads, 1) d1_kernel(const __grid_constant
       gudn_phase(c, l, Kl + g.cq + g.co, tok);
       if (st_l) a.prof[5] = gtimer();
     }
+    c.pf = nullptr;
     grid_bar(c);
     if (stamps && t == 0) a.prof[6] = gtimer();
+    c.pf = (stamps && t == 0) ? a.prof : nullptr;
     lm_phase(c, Kt + g.L * g.cpl);
     if (stamps && t == 0) a.prof[7] = gtimer();
+    c.pf = nullptr;
     grid_bar(c);
     if (a.tstamp && c.c == 0 && threadIdx.x == 0) a.tstamp[t + 1] = gtimer();
   }

@@ -178,6 +178,7 @@ std::string err_text(int flags) {
 }  // namespace
 
 namespace nnz {
+int noalloc_take_error(int dev, int* flags);   // noalloc.cu
 // Lets other translation units of the library set nnz_last_error()'s text.
 void set_last_error(const std::string& msg) { g_err = msg; }
 }  // namespace nnz
@@ -1827,6 +1828,34 @@ int nnz_attn_decode(const void* qkv, const float* q_norm, const float* k_norm, v
     return fail(NNZ_EINVAL, "nnz_attn_decode: problem too large for the shared workspace");
   NNZ_CK(attn_decode_launch(a, (int)head_dim, 0, (cudaStream_t)stream));
   return NNZ_OK;
+}
+
+// Waits for `stream`, then reports (and clears) the device error flags that
+// the per-kernel entry points' launches on the current device raised: a
+// bounded wait that gave up (NNZ_ETIMEDOUT) or an out-of-range position /
+// token (NNZ_EDEVICE).  Allocates nothing.
+int nnz_stream_check(void* stream) {
+  return host_guard([&]() -> int {
+    NNZ_CK(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+    int dev = 0;
+    NNZ_CK(cudaGetDevice(&dev));
+    int flags = 0;
+    {
+      std::lock_guard<std::mutex> lk(g_ws_mu);
+      auto it = g_ws.find(dev);
+      if (it != g_ws.end() && it->second.err) {
+        NNZ_CK(cudaMemcpy(&flags, it->second.err, sizeof(int), cudaMemcpyDeviceToHost));
+        if (flags) NNZ_CK(cudaMemset(it->second.err, 0, sizeof(int)));
+      }
+    }
+    int na = 0;
+    const int rc = noalloc_take_error(dev, &na);
+    if (rc) return rc;
+    flags |= na;
+    if (flags)
+      return fail(flags & (ERR_MBAR_TIMEOUT | ERR_SPIN_TIMEOUT) ? NNZ_ETIMEDOUT : NNZ_EDEVICE, err_text(flags));
+    return NNZ_OK;
+  });
 }
 
 // Development aid (not part of the documented ABI): clock64() stamps of CTA

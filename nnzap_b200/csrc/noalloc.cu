@@ -16,12 +16,16 @@
 //  * all calls share the arrays, so calls that overlap on the GPU (different
 //    streams, or different host threads on one device) race -- serialise
 //    them on one stream;
-//  * the first call on a device resolves the arrays' device addresses and
-//    raises the kernels' shared-memory limit: make that first call before
-//    any stream capture starts on the device.
+//  * the first call on a device resolves the arrays' device addresses,
+//    clears the error word and raises the kernels' shared-memory limit:
+//    make that first call before any stream capture starts on the device;
+//  * a bounded wait that gives up inside the kernel sets the error word;
+//    nnz_stream_check() reads and clears it (the call itself returns as
+//    soon as the work is queued).
 #include <cuda_runtime.h>
 
 #include <mutex>
+#include <new>
 #include <string>
 
 #include "../../include/nnz_b200.h"
@@ -64,6 +68,7 @@ int setup(int dev, NoAllocDev** out) {
       e = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.counters), g_noalloc_counters);
     if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.err), g_noalloc_err);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess) e = cudaMemset(d.err, 0, sizeof(int));
     if (e == cudaSuccess) e = qmv_prepare();
     if (e != cudaSuccess) {
       set_last_error(std::string("nnz_qmv_noalloc set-up: ") + cudaGetErrorString(e));
@@ -76,11 +81,30 @@ int setup(int dev, NoAllocDev** out) {
 }
 
 }  // namespace
+
+// Device error flags raised by no-alloc launches on device `dev` since the
+// last call (read with a copy from the symbol, cleared; no allocation).
+int noalloc_take_error(int dev, int* flags) {
+  *flags = 0;
+  if (dev < 0 || dev >= kMaxDevices) return NNZ_OK;
+  int* p = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_dev[dev].ready) return NNZ_OK;
+    p = g_dev[dev].err;
+  }
+  if (cudaMemcpy(flags, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess ||
+      (*flags && cudaMemset(p, 0, sizeof(int)) != cudaSuccess)) {
+    set_last_error(std::string("nnz_stream_check: ") + cudaGetErrorString(cudaGetLastError()));
+    return NNZ_ECUDA;
+  }
+  return NNZ_OK;
+}
 }  // namespace nnz
 
 using namespace nnz;
 
-extern "C" int nnz_qmv_noalloc(int fmt, int scale_dtype, int bf16_round, const void* packed,
+static int qmv_noalloc_impl(int fmt, int scale_dtype, int bf16_round, const void* packed,
                                uint32_t M, uint32_t K, uint32_t gs, const void* x,
                                uint32_t x_stride, uint32_t batch, void* out, uint32_t out_stride,
                                int out_kind, void* stream) {
@@ -111,10 +135,10 @@ extern "C" int nnz_qmv_noalloc(int fmt, int scale_dtype, int bf16_round, const v
     return NNZ_EINVAL;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // counters and the error word must start at zero; the partial sums are
-  // fully overwritten before they are read
+  // the counters must start at zero (the error word accumulates until
+  // nnz_stream_check clears it); the partial sums are fully overwritten
+  // before they are read
   cudaError_t e = cudaMemsetAsync(d->counters, 0, need_ctr * sizeof(uint32_t), st);
-  if (e == cudaSuccess) e = cudaMemsetAsync(d->err, 0, sizeof(int), st);
   if (e == cudaSuccess) {
     QmvLaunch L{fmt, 1, PRO_F16, epi, fmt == NNZ_Q4 && scale_dtype == NNZ_SCALE_BF16, 0};
     QmvArgs a{};
@@ -130,4 +154,20 @@ extern "C" int nnz_qmv_noalloc(int fmt, int scale_dtype, int bf16_round, const v
     return NNZ_ECUDA;
   }
   return NNZ_OK;
+}
+
+// No C++ exception crosses the C ABI: the error-message building above can
+// throw std::bad_alloc and the set-up mutex std::system_error.
+extern "C" int nnz_qmv_noalloc(int fmt, int scale_dtype, int bf16_round, const void* packed,
+                               uint32_t M, uint32_t K, uint32_t gs, const void* x,
+                               uint32_t x_stride, uint32_t batch, void* out, uint32_t out_stride,
+                               int out_kind, void* stream) {
+  try {
+    return qmv_noalloc_impl(fmt, scale_dtype, bf16_round, packed, M, K, gs, x, x_stride, batch, out,
+                            out_stride, out_kind, stream);
+  } catch (const std::bad_alloc&) {
+    return NNZ_ENOMEM;
+  } catch (...) {
+    return NNZ_EINVAL;
+  }
 }

@@ -134,8 +134,13 @@ struct nnz_safetensors {
         if (d.kind != JVal::INT || d.i < 0 || d.i > 0xFFFFFFFFll)
           return fail(NNZ_EINVAL, "InvalidShape: '" + name + "'");
         t.dims[i] = (uint32_t)d.i;
+        // checked product: a wrapped element count must not pass the size check
+        if (t.dims[i] && count > UINT64_MAX / t.dims[i])
+          return fail(NNZ_EINVAL, "InvalidShape: '" + name + "' element count overflows");
         count *= t.dims[i];
       }
+      if (esize && count > UINT64_MAX / esize)
+        return fail(NNZ_EINVAL, "InvalidShape: '" + name + "' byte size overflows");
       const JVal* off = v.get("data_offsets");
       if (!off) return fail(NNZ_EINVAL, "MissingDataOffsets: '" + name + "'");
       if (off->kind != JVal::ARR || off->arr.size() != 2 || off->arr[0].kind != JVal::INT ||

@@ -19,6 +19,7 @@ finalize) and the model is finalized.
 from __future__ import annotations
 
 import json
+import math
 import mmap
 import struct
 from dataclasses import dataclass
@@ -131,7 +132,9 @@ class SafetensorsFile:
             if off[1] > len(data):
                 raise SafetensorsError(f"DataOffsetOutOfBounds: '{name}' ends at {off[1]} of {len(data)}")
             npdt, size = DTYPES[dt]
-            count = int(np.prod(shape)) if shape else 1
+            count = math.prod(int(d) for d in shape)   # Python ints: no silent wrap-around
+            if count * size >= 1 << 64:
+                raise SafetensorsError(f"InvalidShape: '{name}' element count overflows")
             if off[1] - off[0] != count * size:
                 raise SafetensorsError(f"InvalidDataOffsets: '{name}' holds {off[1] - off[0]} bytes, "
                                        f"shape needs {count * size}")

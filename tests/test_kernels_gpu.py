@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 from gpu_helpers import R, check, cfg_for, close, lib, pack, ptr, to_dev
-from nnzap_b200 import synth
+from nnzap_b200 import _capi, synth
 
 pytestmark = pytest.mark.gpu
 
@@ -233,3 +233,23 @@ def _attention_case(cuda, hd, n_q, n_kv, pos_list, splits, style, seed):
         close(kd[r][:, p].astype(np.float32), k.astype(np.float32), 2e-3, 2e-3, "k cache")
         # untouched history
         np.testing.assert_array_equal(kd[r][:, :p], kc[r][:, :p])
+
+
+def test_stream_check_reports_bad_position(cuda, built_lib):
+    """A device-side error of a per-kernel entry point (here a position past
+    max_context_length, which the attention kernel clamps and flags) reaches
+    the host through nnz_stream_check as NNZ_EDEVICE, once: the check clears it."""
+    torch = cuda
+    hd, n_q, n_kv, max_ctx = 128, 2, 1, 64
+    assert lib().nnz_stream_check(None) == _capi.NNZ_OK
+    qkv = to_dev(torch, np.ones((1, (n_q + 2 * n_kv) * hd), np.float16))
+    qn = to_dev(torch, np.ones(hd, np.float32))
+    kd = torch.zeros((n_kv, max_ctx, hd), dtype=torch.float16, device="cuda")
+    vd = torch.zeros_like(kd)
+    pos = to_dev(torch, np.array([max_ctx + 5], np.int32))
+    out = torch.empty((1, n_q * hd), dtype=torch.float16, device="cuda")
+    check(lib().nnz_attn_decode(ptr(qkv), ptr(qn), ptr(qn), ptr(kd), ptr(vd), max_ctx, ptr(pos), 1, n_q,
+                                n_kv, hd, 1e-6, 1e6, 0, 1, ptr(out), None))
+    assert lib().nnz_stream_check(None) == _capi.NNZ_EDEVICE
+    assert b"position" in lib().nnz_last_error()
+    assert lib().nnz_stream_check(None) == _capi.NNZ_OK

@@ -157,6 +157,9 @@ MALFORMED = [
     ({"t": {"dtype": "F32", "shape": [2], "data_offsets": [0, 8]}}, b"\0" * 4, "DataOffsetOutOfBounds"),
     ({"t": {"dtype": "F32", "shape": [3], "data_offsets": [0, 8]}}, b"\0" * 8, "InvalidDataOffsets"),
     ({"t": {"dtype": "F32", "shape": [-1], "data_offsets": [0, 4]}}, b"\0" * 4, "InvalidShape"),
+    # 2^64 elements: a wrapping product would equal the 0-byte range
+    ({"t": {"dtype": "U8", "shape": [65536, 65536, 65536, 65536], "data_offsets": [0, 0]}}, b"", "InvalidShape"),
+    ({"t": {"dtype": "F32", "shape": [4294967295, 4294967295, 4], "data_offsets": [0, 0]}}, b"", "InvalidShape"),
     ({"t": [1, 2]}, b"", "InvalidTensorEntry"),
     ({"x" * 257: {"dtype": "U8", "shape": [1], "data_offsets": [0, 1]}}, b"\0", "InvalidTensorEntry"),
     ([1, 2], b"", "InvalidJson"),

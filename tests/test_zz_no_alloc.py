@@ -47,6 +47,8 @@ def test_noalloc_matches_qmv_twice(cuda, built_lib, fmt, M, K, gs, batch, out_ki
             want = want + base.float().cpu().numpy()
         close(got.float().cpu().numpy(), want, *((2e-3, 2e-3) if out_kind == 0 else (1e-3, 1e-4)),
               f"oracle call {call}")
+        # no bounded wait gave up inside either call
+        assert lib().nnz_stream_check(None) == _capi.NNZ_OK
 
 
 def test_noalloc_rejects_oversized(cuda, built_lib):
@@ -59,3 +61,17 @@ def test_noalloc_rejects_oversized(cuda, built_lib):
                                1, None)
     assert rc == _capi.NNZ_EINVAL
     assert b"fixed limits" in lib().nnz_last_error()
+
+
+def test_noalloc_rejects_oversized_scratch(cuda, built_lib):
+    """The branch that protects the fixed split-K scratch: a batch-8 matvec
+    with K = 524288 (group 256) needs 16 counters but ~11 MB of split-K
+    partials, more than the 8 MiB array, and is refused before any launch."""
+    torch = cuda
+    M, K, gs, batch = 2048, 524288, 256, 8
+    dummy = torch.zeros(16, dtype=torch.uint8, device="cuda")   # never touched
+    rc = lib().nnz_qmv_noalloc(0, 0, 0, ptr(dummy), M, K, gs, ptr(dummy), K, batch, ptr(dummy), M,
+                               1, None)
+    assert rc == _capi.NNZ_EINVAL
+    err = lib().nnz_last_error()
+    assert b"fixed limits" in err and b"split-K scratch" in err
