@@ -68,7 +68,7 @@ class NnzGenerateResult(C.Structure):
 
 # (name, restype, argtypes) for every exported symbol of include/nnz_b200.h
 P, U32, I32, SZ, F32 = C.c_void_p, C.c_uint32, C.c_int, C.c_size_t, C.c_float
-DEBUG_SIGNATURES = [("nnz_debug_gemm_profile", I32, [P]), ("nnz_debug_decode1_profile", I32, [P, P, U32])]
+DEBUG_SIGNATURES = [("nnz_debug_gemm_profile", I32, [P]), ("nnz_debug_decode1_profile", I32, [P, P, U32]), ("nnz_debug_decode_path", I32, [P])]
 SIGNATURES = [
     ("nnz_last_error", C.c_char_p, []),
     ("nnz_version", I32, []),

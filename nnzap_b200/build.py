@@ -69,7 +69,8 @@ def build(verbose: bool = False, force: bool = False) -> Path:
                 cmd = ["g++", "-O3", "-std=c++20", "-fPIC", "-pthread", "-I", str(CSRC),
                        "-I", str(ROOT / "include"), "-c", str(src), "-o", str(obj)]
             else:
-                cmd = [nvcc, *ARCH, *NVCC_FLAGS, *_nccl_include(), "-c", str(src), "-o", str(obj)]
+                extra = os.environ.get("NNZ_NVCC_EXTRA", "").split()   # experiments only
+                cmd = [nvcc, *ARCH, *NVCC_FLAGS, *extra, *_nccl_include(), "-c", str(src), "-o", str(obj)]
             jobs.append(cmd)
     with cf.ThreadPoolExecutor(max_workers=max(1, os.cpu_count() or 1)) as ex:
         for cmd, res in zip(jobs, ex.map(lambda c: subprocess.run(c, capture_output=True, text=True), jobs)):

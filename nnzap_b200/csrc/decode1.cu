@@ -18,9 +18,10 @@
 //           red.add into the O accumulator Z;
 //     --- grid barrier ---
 //     GU    fused RMSNorm (ffn_norm) of residual + Z, gate and up rows of
-//           this CTA's intermediate slice, h = fp16(SiLU(g) * u);
-//     DN    down_proj columns of that slice for all H rows, red.add into the
-//           next residual (plus this CTA's slice of residual + Z);
+//           this CTA's intermediate slice, h = fp16(SiLU(g) * u) to L2;
+//     --- grid barrier ---
+//     DN    down_proj of this CTA's output rows over all of h; next
+//           residual = residual + Z + down (plain stores);
 //     --- grid barrier ---
 //   LM      fused final RMSNorm + this CTA's LM-head rows, f32 logits
 //           (optional) and a packed first-max argmax (atomicMax);
@@ -35,6 +36,8 @@
 // NNZ_ETIMEDOUT.  The red.add accumulations make the f32 sums' order (and so
 // their last bits) vary from run to run.
 #include <cuda_runtime.h>
+#include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "decode1.cuh"
@@ -44,6 +47,17 @@ namespace nnz {
 namespace {
 
 constexpr uint32_t kD1Spin = 1u << 22;
+
+// Inlining of the kernel's pieces (instruction footprint vs call overhead).
+#ifndef D1_PHASE
+#define D1_PHASE __forceinline__
+#endif
+#ifndef D1_MV
+#define D1_MV __forceinline__
+#endif
+#ifndef D1_SMALL
+#define D1_SMALL __forceinline__
+#endif
 constexpr unsigned kFull = 0xffffffffu;
 
 // ---- shared-memory layout ----------------------------------------------------
@@ -54,10 +68,7 @@ constexpr uint32_t OFF_KV = OFF_RING + kD1Slots * kD1Chunk;            // [2 sta
 constexpr uint32_t OFF_XB = OFF_KV + 4 * KV_BLKB;                      // [group][4 k32 chunks][12 lanes] uint2
 constexpr uint32_t OFF_GEF = OFF_XB + kD1MaxGroups * 4 * 12 * 8;       // [group] 2^(E-22)
 constexpr uint32_t OFF_GSQ = OFF_GEF + kD1MaxGroups * 4;               // [group] sum of q
-constexpr uint32_t OFF_XB16 = OFF_GSQ + kD1MaxGroups * 4;              // [k16 chunk][12 lanes] u32
-constexpr uint32_t OFF_EF16 = al16(OFF_XB16 + kD1MaxNb * 12 * 4);
-constexpr uint32_t OFF_SQ16 = OFF_EF16 + kD1MaxNb * 4;
-constexpr uint32_t OFF_PART = al16(OFF_SQ16 + kD1MaxNb * 4);           // [warp][rb][16] f32
+constexpr uint32_t OFF_PART = al16(OFF_GSQ + kD1MaxGroups * 4);        // [warp][rb][16] f32
 constexpr uint32_t OFF_ROWS = OFF_PART + kD1Warps * kD1MaxRb * 16 * 4; // [rb * 16] f32
 constexpr uint32_t OFF_RED = OFF_ROWS + kD1MaxRb * 16 * 4;             // [16] f32
 constexpr uint32_t OFF_AMAX = OFF_RED + 16 * 4;                        // [16] u64
@@ -70,8 +81,13 @@ constexpr uint32_t OFF_COMB = al16(OFF_STAT + 3 * kD1MaxG * 4);        // [4][12
 constexpr uint32_t OFF_MER = OFF_COMB + 4 * 128 * 4;                   // [4][132] f32
 constexpr uint32_t OFF_XO = OFF_MER + 4 * kD1AttRec * 4;               // [128] f32
 constexpr uint32_t OFF_TOK = OFF_XO + 128 * 4;                         // tok, pos, adv
-constexpr uint32_t OFF_BAR = al16(OFF_TOK + 16);                       // full[S], empty[S], kv[2]
-constexpr uint32_t SMEM_TOTAL = OFF_BAR + (2 * kD1Slots + 2) * 8;
+constexpr uint32_t kD1CbMax = 1024;                                    // chunk sizes cached in smem
+constexpr uint32_t OFF_CB = al16(OFF_TOK + 16);                        // [kD1CbMax] chunk bytes
+constexpr uint32_t OFF_RELC = OFF_CB + kD1CbMax * 4;                   // [S] releases of the slot's chunk
+constexpr uint32_t OFF_ISS = OFF_RELC + kD1Slots * 4;                  // [S] last chunk issued into the slot
+constexpr uint32_t OFF_LAY = al16(OFF_ISS + kD1Slots * 4);             // [L] D1Layer (norm pointers)
+constexpr uint32_t OFF_BAR = al16(OFF_LAY + kD1MaxLayers * sizeof(D1Layer)); // full[S], kv[2]
+constexpr uint32_t SMEM_TOTAL = OFF_BAR + (kD1Slots + 2) * 8;
 static_assert(SMEM_TOTAL <= 227 * 1024, "decode1 shared memory");
 static_assert(OFF_KV % 128 == 0 && OFF_XB % 16 == 0, "alignment");
 
@@ -105,20 +121,15 @@ __device__ __forceinline__ void mbar_arrive1(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async;" ::: "memory"); }
+// Prefetch [p, p + bytes) into L2 (bulk, no shared memory involved).
+__device__ __forceinline__ void l2_prefetch(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// D(16x8 s32) += A(16x16 u8) * B(16x8 s8)
-__device__ __forceinline__ void mma_u8s8_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-  asm("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
-      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-      : "r"(a0), "r"(a1), "r"(b0));
-}
-// four bits -> four bytes in {0, 1}
-__device__ __forceinline__ uint32_t spread4(uint32_t nib) { return (nib * 0x00204081u) & 0x01010101u; }
-
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
 // ---- per-warp state --------------------------------------------------------------
@@ -133,16 +144,27 @@ struct Ctx {
   uint32_t kvseq;                // K/V blocks consumed by this CTA so far
   uint32_t kv_hi;                // thread 0: K/V block sequence numbers issued so far
   unsigned long long* pf;        // profiling: non-null on the one thread that records stamps
+  bool probe;                    // profiling: layer 1 of the first token
+  uint32_t nbar;                 // profiling: grid barriers seen while probing
 };
 // Profiling stamp (NNZ_D1_PROFILE=1): thread 0 of CTA 0, layer 1 of the first token.
 #define D1_STAMP(c, i) do { if ((c).pf) (c).pf[i] = gtimer(); } while (0)
 
 __device__ __forceinline__ uint64_t* fullb(uint8_t* sm, uint32_t s) { return reinterpret_cast<uint64_t*>(sm + OFF_BAR) + s; }
-__device__ __forceinline__ uint64_t* emptyb(uint8_t* sm, uint32_t s) {
+__device__ __forceinline__ uint64_t* kvbar(uint8_t* sm, uint32_t s) {
   return reinterpret_cast<uint64_t*>(sm + OFF_BAR) + kD1Slots + s;
 }
-__device__ __forceinline__ uint64_t* kvbar(uint8_t* sm, uint32_t s) {
-  return reinterpret_cast<uint64_t*>(sm + OFF_BAR) + 2 * kD1Slots + s;
+
+// Issue chunk K (global index over the launch's tokens) of this CTA's weight
+// stream into its ring slot.
+__device__ __forceinline__ void ring_issue(const D1Args& a, uint8_t* sm, uint32_t K) {
+  const uint32_t nck = a.g.nck, k = K % nck, s = K % kD1Slots;
+  const uint32_t bytes = k < kD1CbMax ? reinterpret_cast<const uint32_t*>(sm + OFF_CB)[k]
+                                      : __ldg(a.chunk_bytes + (size_t)blockIdx.x * nck + k);
+  mbar_arrive_expect_tx(fullb(sm, s), bytes);
+  if (bytes)
+    bulk_g2s(sm + OFF_RING + s * kD1Chunk, a.stream + ((size_t)blockIdx.x * nck + k) * kD1Chunk, bytes, fullb(sm, s));
+  reinterpret_cast<uint32_t*>(sm + OFF_ISS)[s] = K;
 }
 
 __device__ __noinline__ void raise_abort(const D1Args& a, int code) {
@@ -187,10 +209,11 @@ __device__ __forceinline__ void wait_count(const unsigned int* ctr, unsigned int
 // Grid barrier over the compute warps of every CTA (co-resident by
 // cooperative launch): one release-add per CTA on a 64-bit counter that only
 // grows, acquire polls until it reaches this barrier's target.
-__device__ __forceinline__ void grid_bar(Ctx& c) {
+__device__ D1_SMALL void grid_bar(Ctx& c) {
   named_sync();
   if (threadIdx.x == 0) {
     const D1Args& a = *c.a;
+    if (c.probe && c.nbar < 4) a.prof[64 + c.c * 8 + 2 * c.nbar] = gtimer();
     unsigned long long* cnt = reinterpret_cast<unsigned long long*>(a.bar + 4);
     c.bar_target += a.g.P;
     asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(cnt) : "memory");
@@ -204,19 +227,30 @@ __device__ __forceinline__ void grid_bar(Ctx& c) {
         }
       }
     }
+    if (c.probe && c.nbar < 4) a.prof[64 + c.c * 8 + 2 * c.nbar + 1] = gtimer();
+    if (c.probe) ++c.nbar;
   }
   named_sync();
 }
 
-// ---- weight ring (consumer side) ----------------------------------------------------
-// A warp may arrive on a chunk's `empty` barrier only after that chunk's
-// `full` barrier completed (otherwise the arrival could count toward the
-// slot's previous use), so releasing a chunk waits for it first.
-__device__ __forceinline__ void ring_release_one(Ctx& c) {
+// ---- weight ring ---------------------------------------------------------------------
+// Every warp releases every chunk, in order.  A release waits for the chunk
+// to have landed first (so it can never count toward the slot's previous
+// chunk); the warp whose release is the slot's 16th issues the copy of the
+// chunk kD1Slots ahead into it.  Nothing is issued once the launch aborted.
+__device__ D1_SMALL void ring_release_one(Ctx& c) {
   const uint32_t K = c.rel;
   if (!c.failed) c.failed = !wait_mbar(fullb(c.sm, K % kD1Slots), (K / kD1Slots) & 1u, *c.a);
   __syncwarp();
-  if (c.lane == 0) mbar_arrive1(emptyb(c.sm, K % kD1Slots));
+  if (c.lane == 0) {
+    uint32_t* relc = reinterpret_cast<uint32_t*>(c.sm + OFF_RELC) + K % kD1Slots;
+    if (atomicAdd(relc, 1u) == (uint32_t)kD1Warps - 1) {
+      atomicExch(relc, 0u);
+      const uint32_t Kn = K + kD1Slots;
+      if (Kn < c.a->ntok * c.a->g.nck && !c.failed) ring_issue(*c.a, c.sm, Kn);
+    }
+  }
+  __syncwarp();
   ++c.rel;
 }
 __device__ __forceinline__ void ring_release_upto(Ctx& c, uint32_t K) {
@@ -224,6 +258,8 @@ __device__ __forceinline__ void ring_release_upto(Ctx& c, uint32_t K) {
 }
 __device__ __forceinline__ const uint8_t* ring_get(Ctx& c, uint32_t K) {
   ring_release_upto(c, K);
+  if (c.probe && c.c == 0 && c.lane == 0 && !mbar_try_wait(fullb(c.sm, K % kD1Slots), (K / kD1Slots) & 1u))
+    atomicAdd(reinterpret_cast<unsigned int*>(c.sm + OFF_TOK) + 3, 1u);
   if (!c.failed) c.failed = !wait_mbar(fullb(c.sm, K % kD1Slots), (K / kD1Slots) & 1u, *c.a);
   return c.sm + OFF_RING + (K % kD1Slots) * kD1Chunk;
 }
@@ -234,6 +270,17 @@ __device__ __forceinline__ const uint8_t* ring_get(Ctx& c, uint32_t K) {
 // the maximum; q = hi * 65536 + mid * 256 + lo with balanced signed bytes.
 // B fragment of m16n8k32 (.s8): lane n*4 + t holds column n, k = 4t..4t+3
 // (reg 0) and 16 + 4t.. (reg 1); columns 0, 1, 2 = hi, mid, lo.
+// For a group maximum am >= 0: E with 2^E > am (0 for am == 0 or a
+// subnormal), returned as the two exact powers of two 2^(22-E) (to scale
+// into the fixed-point grid) and 2^(E-22) (back), built from the exponent
+// bits: frexpf/ldexpf are long branchy sequences on the critical path.
+__device__ __forceinline__ void group_scales(float am, float& up, float& down) {
+  const int be = (int)((__float_as_uint(am) >> 23) & 0xFFu);   // biased exponent of am
+  const int E = be ? be - 126 : 0;                              // am < 2^(be-126)
+  up = __uint_as_float((uint32_t)(127 + 22 - E) << 23);
+  down = __uint_as_float((uint32_t)(127 - 22 + E) << 23);
+}
+
 __device__ __forceinline__ void digits(int q, uint32_t& hi, uint32_t& mid, uint32_t& lo) {
   const int l = ((q + 128) & 255) - 128;
   const int r1 = (q - l) >> 8;
@@ -244,12 +291,11 @@ __device__ __forceinline__ void digits(int q, uint32_t& hi, uint32_t& mid, uint3
   lo = (uint32_t)(l & 255);
 }
 
-__device__ __forceinline__ void quant_group(const float (&x)[4], uint32_t gg, int lane, uint8_t* sm) {
+__device__ D1_SMALL void quant_group(const float (&x)[4], uint32_t gg, int lane, uint8_t* sm) {
   float am = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
   am = warp_max(am);
-  int E = 0;
-  if (am > 0.f) frexpf(am, &E);
-  const float up = ldexpf(1.f, 22 - E);
+  float up, down;
+  group_scales(am, up, down);
   uint32_t w0 = 0, w1 = 0, w2 = 0;
   int sum = 0;
 #pragma unroll
@@ -269,44 +315,8 @@ __device__ __forceinline__ void quant_group(const float (&x)[4], uint32_t gg, in
   xb[(1 * 4 + t) * 2 + reg] = w1;
   xb[(2 * 4 + t) * 2 + reg] = w2;
   if (lane == 0) {
-    reinterpret_cast<float*>(sm + OFF_GEF)[gg] = ldexpf(1.f, E - 22);
+    reinterpret_cast<float*>(sm + OFF_GEF)[gg] = down;
     reinterpret_cast<int*>(sm + OFF_GSQ)[gg] = sum;
-  }
-}
-
-// k16 chunk p of the SiLU*up slice: lanes 4p .. 4p+3 of warp 0, lane holds
-// elements 4t .. 4t+3 of the chunk (t = lane & 3).
-__device__ __forceinline__ void quant_chunk16(const float (&x)[4], uint32_t p, int lane, bool active, uint8_t* sm) {
-  float am = active ? fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3]))) : 0.f;
-  am = fmaxf(am, __shfl_xor_sync(kFull, am, 1));
-  am = fmaxf(am, __shfl_xor_sync(kFull, am, 2));
-  int E = 0;
-  if (am > 0.f) frexpf(am, &E);
-  const float up = ldexpf(1.f, 22 - E);
-  uint32_t w0 = 0, w1 = 0, w2 = 0;
-  int sum = 0;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int q = active ? __float2int_rn(x[i] * up) : 0;
-    sum += q;
-    uint32_t h, m, l;
-    digits(q, h, m, l);
-    w0 |= h << (8 * i);
-    w1 |= m << (8 * i);
-    w2 |= l << (8 * i);
-  }
-  sum += __shfl_xor_sync(kFull, sum, 1);
-  sum += __shfl_xor_sync(kFull, sum, 2);
-  if (active) {
-    uint32_t* xb = reinterpret_cast<uint32_t*>(sm + OFF_XB16) + p * 12;
-    const int t = lane & 3;
-    xb[0 * 4 + t] = w0;
-    xb[1 * 4 + t] = w1;
-    xb[2 * 4 + t] = w2;
-    if (t == 0) {
-      reinterpret_cast<float*>(sm + OFF_EF16)[p] = ldexpf(1.f, E - 22);
-      reinterpret_cast<int*>(sm + OFF_SQ16)[p] = sum;
-    }
   }
 }
 
@@ -314,19 +324,6 @@ __device__ __forceinline__ void quant_chunk16(const float (&x)[4], uint32_t p, i
 // One 16-row x 128-k unit: 4 int8 MMAs.  Lane's 8 bytes: word w covers MMAs
 // 2w, 2w+1; bit (s + 8i) of a word, s = 4 j' + r, is byte i of A register r
 // of MMA 2w + j'.
-__device__ __forceinline__ void unit_mma(const uint8_t* unit, const uint2* xbg, int lane, int (&acc)[4]) {
-  const uint2 wb = *reinterpret_cast<const uint2*>(unit + lane * 8);
-  acc[0] = acc[1] = acc[2] = acc[3] = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t W = (j < 2) ? wb.x : wb.y;
-    const int s = (j & 1) * 4;
-    const uint2 b = lane < 12 ? xbg[j * 12 + lane] : make_uint2(0u, 0u);
-    mma_u8s8(acc, (W >> s) & 0x01010101u, (W >> (s + 1)) & 0x01010101u, (W >> (s + 2)) & 0x01010101u,
-             (W >> (s + 3)) & 0x01010101u, b.x, b.y);
-  }
-}
-
 // Accumulator digits -> scaled f32 row sums (lanes with lane % 4 == 0 hold rows
 // lane / 4 and lane / 4 + 8).  sum(sign * q) = 2 sum(bit * q) - sum(q), exact.
 __device__ __forceinline__ void unit_epi(const int (&acc)[4], float s0, float s1, int sq, float& y0, float& y1,
@@ -355,44 +352,87 @@ __device__ __forceinline__ void red_rows16(float* dst, float y0, float y1, int l
   if (lane < 4) red_add_v4(dst + 4 * lane, v[0], v[1], v[2], v[3]);
 }
 
-// Units [0, U) of a phase starting at ring chunk Kb, unit u = (row block
-// u / GH, group u % GH); warp w takes u = w, w + 16, ...  Per row block the
-// warp's partial sums go to part[warp][rb] (zeroed by the prologue).
-__device__ __forceinline__ void mv_group_split(Ctx& c, uint32_t Kb, uint32_t U) {
-  const uint32_t GH = c.a->g.GH;
+// The one matvec loop of the kernel (kept out of line: every phase shares
+// this copy of the instructions).  Units (row block rbl, group gg) of a
+// phase start at ring chunk Kb, unit index rbl * GH + gg.
+//   mode 0: group split -- warp w takes groups w, w + 16, ... of every row
+//           block and writes its partial row sums to part[w][rbl] (every
+//           entry written, zero when the warp had no group);
+//   mode 1: row split -- warp w takes row blocks w, w + 16, ... whole and
+//           red.adds the rows into dst[(rb_base + rbl) * 16 ..];
+//   mode 2: row split LM head -- f32 logits (dst, optional) and the packed
+//           first-max argmax of rows < V, returned.
+__device__ D1_MV unsigned long long mv_units(Ctx& c, uint32_t Kb, uint32_t nrb, uint32_t GH, int mode,
+                                                    float* dst, uint32_t rb_base, uint32_t V) {
   const int lane = c.lane, r0 = lane >> 2;
   const uint2* xb = reinterpret_cast<const uint2*>(c.sm + OFF_XB);
   const float* gef = reinterpret_cast<const float*>(c.sm + OFF_GEF);
   const int* gsq = reinterpret_cast<const int*>(c.sm + OFF_GSQ);
   float* part = reinterpret_cast<float*>(c.sm + OFF_PART) + c.warp * kD1MaxRb * 16;
-  float y0 = 0.f, y1 = 0.f;
-  uint32_t cur = 0xffffffffu, curk = 0xffffffffu;
+  const bool rows = mode != 0;
+  const uint32_t rstart = rows ? c.warp : 0, rstep = rows ? kD1Warps : 1;
+  const uint32_t gstart = rows ? 0 : c.warp, gstep = rows ? 1 : kD1Warps;
+  unsigned long long best = 0ull;
+  uint32_t curk = 0xffffffffu, curg = 0xffffffffu;
   const uint8_t* ch = nullptr;
-  for (uint32_t u = c.warp; u < U; u += kD1Warps) {
-    const uint32_t rbl = u / GH, gg = u % GH;
-    if (rbl != cur) {
-      if (cur != 0xffffffffu && (lane & 3) == 0) {
-        part[cur * 16 + r0] = y0;
-        part[cur * 16 + r0 + 8] = y1;
+  uint2 bq[4] = {};
+  float ef = 0.f;
+  int sq = 0;
+  if (mode == 0) D1_STAMP(c, 52);
+  for (uint32_t rbl = rstart; rbl < nrb; rbl += rstep) {
+    float y0 = 0.f, y1 = 0.f;
+    for (uint32_t gg = gstart; gg < GH; gg += gstep) {
+      const uint32_t u = rbl * GH + gg;
+      if (Kb + (u >> 5) != curk) {
+        curk = Kb + (u >> 5);
+        ch = ring_get(c, curk);
       }
-      cur = rbl;
-      y0 = y1 = 0.f;
+      if (gg != curg) {
+        curg = gg;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) bq[j] = lane < 12 ? xb[gg * 48 + j * 12 + lane] : make_uint2(0u, 0u);
+        ef = gef[gg];
+        sq = gsq[gg];
+      }
+      if (mode == 0 && rbl == 0) D1_STAMP(c, 53);
+      const uint8_t* unit = ch + (u & 31u) * kD1Unit;
+      const uint2 wb = *reinterpret_cast<const uint2*>(unit + lane * 8);
+      int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t W = (j < 2) ? wb.x : wb.y;
+        const int sh = (j & 1) * 4;
+        mma_u8s8(acc, (W >> sh) & 0x01010101u, (W >> (sh + 1)) & 0x01010101u, (W >> (sh + 2)) & 0x01010101u,
+                 (W >> (sh + 3)) & 0x01010101u, bq[j].x, bq[j].y);
+      }
+      const uint32_t s01 = *reinterpret_cast<const uint16_t*>(unit + 256 + r0 * 2) |
+                           ((uint32_t)*reinterpret_cast<const uint16_t*>(unit + 256 + (r0 + 8) * 2) << 16);
+      const float2 sf = __half22float2(*reinterpret_cast<const __half2*>(&s01));
+      unit_epi(acc, sf.x * ef, sf.y * ef, sq, y0, y1, lane);
     }
-    if (Kb + u / 32 != curk) {
-      curk = Kb + u / 32;
-      ch = ring_get(c, curk);
+    if (mode == 0) {
+      if (rbl == 0) D1_STAMP(c, 54);
+      if ((lane & 3) == 0) {
+        part[rbl * 16 + r0] = y0;
+        part[rbl * 16 + r0 + 8] = y1;
+      }
+    } else if (mode == 1) {
+      red_rows16(dst + (rb_base + rbl) * 16, y0, y1, lane);
+    } else if ((lane & 3) == 0) {
+      const uint32_t ra = (rb_base + rbl) * 16 + r0, rbb = ra + 8;
+      if (ra < V) {
+        if (dst) dst[ra] = y0;
+        const unsigned long long k = argmax_pack(y0, ra);
+        best = k > best ? k : best;
+      }
+      if (rbb < V) {
+        if (dst) dst[rbb] = y1;
+        const unsigned long long k = argmax_pack(y1, rbb);
+        best = k > best ? k : best;
+      }
     }
-    const uint8_t* unit = ch + (u % 32) * kD1Unit;
-    int acc[4];
-    unit_mma(unit, xb + gg * 48, lane, acc);
-    const uint16_t* sc = reinterpret_cast<const uint16_t*>(unit + 256);
-    const float ef = gef[gg];
-    unit_epi(acc, h2f(sc[r0]) * ef, h2f(sc[r0 + 8]) * ef, gsq[gg], y0, y1, lane);
   }
-  if (cur != 0xffffffffu && (lane & 3) == 0) {
-    part[cur * 16 + r0] = y0;
-    part[cur * 16 + r0 + 8] = y1;
-  }
+  return best;
 }
 
 // ---- residual sources --------------------------------------------------------------
@@ -416,13 +456,20 @@ __device__ __forceinline__ void layer_in4(const D1Args& a, uint32_t l, uint32_t 
 
 // RMSNorm of the input vector (H elements; warp w owns groups w and w + 16,
 // lane 4 elements of each), fp16 rounding, quantisation into the B
-// fragments of every group; clears the cross-warp partial sums.
+// fragments of every group.
 // kind: 0 = layer input, 1 = layer input + O accumulator, 2 = final residual.
-__device__ void norm_prologue(Ctx& c, int kind, uint32_t l, uint32_t tok, const float* nw) {
+__device__ D1_SMALL void norm_prologue(Ctx& c, int kind, uint32_t l, uint32_t tok, const float* nw) {
   const D1Args& a = *c.a;
   const uint32_t GH = a.g.GH, H = a.g.H;
   float v[2][4];
+  float4 w4[2];
   float ss = 0.f;
+  // the norm weights first: their load overlaps the residual's
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint32_t gg = c.warp + 16 * i;
+    if (gg < GH) w4[i] = __ldg(reinterpret_cast<const float4*>(nw + gg * 128 + 4 * c.lane));
+  }
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const uint32_t gg = c.warp + 16 * i;
@@ -442,29 +489,29 @@ __device__ void norm_prologue(Ctx& c, int kind, uint32_t l, uint32_t tok, const 
       for (int e = 0; e < 4; ++e) ss = fmaf(v[i][e], v[i][e], ss);
     }
   }
+  D1_STAMP(c, 40 + 4 * kind);
   ss = warp_sum(ss);
   float* red = reinterpret_cast<float*>(c.sm + OFF_RED);
   if (c.lane == 0) red[c.warp] = ss;
-  // clear part[][] (16 x kD1MaxRb x 16 floats = 4 per thread)
-  reinterpret_cast<float4*>(c.sm + OFF_PART)[threadIdx.x] = make_float4(0.f, 0.f, 0.f, 0.f);
   named_sync();
-  float tot = 0.f;
-#pragma unroll
-  for (int w = 0; w < kD1Warps; ++w) tot += red[w];
-  const float r = 1.0f / sqrtf(tot / (float)H + a.eps);
+  D1_STAMP(c, 41 + 4 * kind);
+  const float4* r4 = reinterpret_cast<const float4*>(red);
+  const float4 q0 = r4[0], q1 = r4[1], q2 = r4[2], q3 = r4[3];
+  const float tot = ((q0.x + q0.y) + (q0.z + q0.w)) + ((q1.x + q1.y) + (q1.z + q1.w)) +
+                    (((q2.x + q2.y) + (q2.z + q2.w)) + ((q3.x + q3.y) + (q3.z + q3.w)));
+  const float r = rsqrtf(tot / (float)H + a.eps);
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const uint32_t gg = c.warp + 16 * i;
     if (gg < GH) {
-      const uint32_t k = gg * 128 + 4 * c.lane;
-      const float4 w4 = __ldg(reinterpret_cast<const float4*>(nw + k));
-      const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+      const float wv[4] = {w4[i].x, w4[i].y, w4[i].z, w4[i].w};
       float x[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) x[e] = __half2float(__float2half_rn(v[i][e] * r * wv[e]));
       quant_group(x, gg, c.lane, c.sm);
     }
   }
+  D1_STAMP(c, 42 + 4 * kind);
   named_sync();
 }
 
@@ -479,8 +526,8 @@ __device__ __forceinline__ AttGeo att_geo(const D1Args& a, uint32_t c, int pos) 
   const uint32_t S = a.g.S, n = (uint32_t)pos + 1;
   g.j = c / S;
   g.s = c % S;
-  g.t0 = (uint32_t)(((uint64_t)g.s * n) / S);
-  g.t1 = (uint32_t)(((uint64_t)(g.s + 1) * n) / S);
+  g.t0 = (g.s * n) / S;          // S * max_ctx fits 32 bits (d1_geom)
+  g.t1 = ((g.s + 1) * n) / S;
   g.nblk = (g.t1 - g.t0 + kD1KvBlk - 1) / kD1KvBlk;
   g.own_new = g.t1 == n && g.t1 > g.t0;
   return g;
@@ -490,7 +537,7 @@ __device__ __forceinline__ AttGeo att_geo(const D1Args& a, uint32_t c, int pos) 
 // into stage (kvseq + blk) & 1.  Nothing is issued once the launch aborted.
 __device__ void att_issue(Ctx& c, const AttGeo& g, uint32_t l, int pos, uint32_t blk) {
   const D1Args& a = *c.a;
-  if (c.failed || ld_relaxed_u32(&a.bar[2])) return;
+  if (c.failed) return;
   const uint32_t seq = c.kvseq + blk, st = seq & 1u;
   const uint32_t tb = g.t0 + blk * kD1KvBlk;
   uint32_t te = tb + kD1KvBlk;
@@ -542,25 +589,26 @@ __device__ __forceinline__ void norm_rope(const __half* src, const float* nw, co
   }
 }
 
-__device__ void att_phase(Ctx& c, uint32_t l, int pos, uint32_t epoch_tok) {
+template <int GT>
+__device__ D1_PHASE void att_phase(Ctx& c, uint32_t l, int pos, uint32_t epoch_tok) {
   const D1Args& a = *c.a;
-  const uint32_t G = a.g.G, S = a.g.S;
+  constexpr uint32_t G = GT;
+  const uint32_t S = a.g.S;
   const AttGeo g = att_geo(a, c.c, pos);
   uint8_t* sm = c.sm;
   float* qs = reinterpret_cast<float*>(sm + OFF_QS);
-  float* sc = reinterpret_cast<float*>(sm + OFF_SC);
+  float* wst = reinterpret_cast<float*>(sm + OFF_SC);       // [warp][G] partial maxima
+  float* acc = reinterpret_cast<float*>(sm + OFF_COMB);     // [G][128] merged outputs
+  float* lsum = reinterpret_cast<float*>(sm + OFF_STAT);    // [G] merged sums
   __half* knew = reinterpret_cast<__half*>(sm + OFF_KNEW);
   __half* vnew = reinterpret_cast<__half*>(sm + OFF_VNEW);
-  float* mst = reinterpret_cast<float*>(sm + OFF_STAT);
-  float* lst = mst + kD1MaxG;
-  float* alp = lst + kD1MaxG;
   const int warp = c.warp, lane = c.lane;
 
   if (threadIdx.x == 0)
     wait_count(a.cnt + (size_t)l * a.g.nkv + g.j, (epoch_tok + 1) * (G + 2) * 8, a);
   named_sync();
   D1_STAMP(c, 12);
-  const D1Layer& LW = a.layers[l];
+  const D1Layer& LW = reinterpret_cast<const D1Layer*>(sm + OFF_LAY)[l];
   const float2* cs = a.rope_tab + (size_t)pos * 64;
   if ((uint32_t)warp < G) {
     float v[4];
@@ -580,192 +628,209 @@ __device__ void att_phase(Ctx& c, uint32_t l, int pos, uint32_t epoch_tok) {
     reinterpret_cast<uint2*>(a.kc + off)[lane] = kk;
     reinterpret_cast<uint2*>(a.vc + off)[lane] = vv;
   }
-  if (threadIdx.x < kD1MaxG) {
-    mst[threadIdx.x] = -INFINITY;
-    lst[threadIdx.x] = 0.f;
-  }
   named_sync();
-
   D1_STAMP(c, 13);
-  // PV thread mapping: d = tid % 128, head gq % G, position partition gq / G
-  const uint32_t d = threadIdx.x & 127u, gq = threadIdx.x >> 7, gh = gq % G, part = gq / G, NP = 4 / G;
-  float accv = 0.f;
-  float qv[kD1MaxG][4];
+
+  // Each warp runs its own online softmax over positions t0 + warp, + 16, ...
+  // (lane: head dims 4 lane .. 4 lane + 3 of every head); K/V blocks arrive
+  // two at a time, so splits longer than 64 positions refill between rounds.
+  float qv[GT][4], m[GT], ls[GT], o[GT][4];
 #pragma unroll
-  for (int h = 0; h < kD1MaxG; ++h) {
+  for (int h = 0; h < GT; ++h) {
+    m[h] = -INFINITY;
+    ls[h] = 0.f;
+    o[h][0] = o[h][1] = o[h][2] = o[h][3] = 0.f;
     if ((uint32_t)h < G) {
       const float4 q4 = *reinterpret_cast<const float4*>(qs + h * 128 + 4 * lane);
       qv[h][0] = q4.x; qv[h][1] = q4.y; qv[h][2] = q4.z; qv[h][3] = q4.w;
     }
   }
   const float inv = 1.0f / sqrtf(128.f);
-  for (uint32_t blk = 0; blk < g.nblk; ++blk) {
-    const uint32_t tb = g.t0 + blk * kD1KvBlk;
-    const uint32_t nb = min((uint32_t)kD1KvBlk, g.t1 - tb);
-    const uint32_t st = (c.kvseq + blk) & 1u;
-    if (!c.failed) c.failed = !wait_mbar(kvbar(sm, st), ((c.kvseq + blk) >> 1) & 1u, a);
-    const __half* kb = reinterpret_cast<const __half*>(sm + OFF_KV + st * 2 * KV_BLKB);
-    const __half* vb = reinterpret_cast<const __half*>(sm + OFF_KV + st * 2 * KV_BLKB + KV_BLKB);
-    for (uint32_t i = warp; i < nb; i += kD1Warps) {
-      const __half* kr = (tb + i == (uint32_t)pos) ? knew : kb + i * 128;
-      const uint2 raw = *reinterpret_cast<const uint2*>(kr + 4 * lane);
-      const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-      const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+  for (uint32_t b0 = 0; b0 < g.nblk; b0 += 2) {
+    for (uint32_t blk = b0; blk < b0 + 2 && blk < g.nblk; ++blk) {
+      const uint32_t tb = g.t0 + blk * kD1KvBlk;
+      const uint32_t nb = min((uint32_t)kD1KvBlk, g.t1 - tb);
+      if ((uint32_t)warp >= nb) continue;
+      const uint32_t st = (c.kvseq + blk) & 1u;
+      if (!c.failed) c.failed = !wait_mbar(kvbar(sm, st), ((c.kvseq + blk) >> 1) & 1u, a);
+      const __half* kb = reinterpret_cast<const __half*>(sm + OFF_KV + st * 2 * KV_BLKB);
+      const __half* vb = kb + KV_BLKB / 2;
+      for (uint32_t i = warp; i < nb; i += kD1Warps) {
+        const bool nw = tb + i == (uint32_t)pos;
+        const uint2 kr = *reinterpret_cast<const uint2*>((nw ? knew : kb + i * 128) + 4 * lane);
+        const uint2 vr = *reinterpret_cast<const uint2*>((nw ? vnew : vb + i * 128) + 4 * lane);
+        const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&kr.x));
+        const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&kr.y));
+        const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&vr.x));
+        const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&vr.y));
 #pragma unroll
-      for (int h = 0; h < kD1MaxG; ++h) {
-        if ((uint32_t)h < G) {
-          float dot = qv[h][0] * k0.x;
-          dot = fmaf(qv[h][1], k0.y, dot);
-          dot = fmaf(qv[h][2], k1.x, dot);
-          dot = fmaf(qv[h][3], k1.y, dot);
-          dot = warp_sum(dot);
-          if (lane == 0) sc[h * kD1KvBlk + i] = dot * inv;
+        for (int h = 0; h < GT; ++h) {
+          {
+            float dot = qv[h][0] * k0.x;
+            dot = fmaf(qv[h][1], k0.y, dot);
+            dot = fmaf(qv[h][2], k1.x, dot);
+            dot = fmaf(qv[h][3], k1.y, dot);
+            const float s = warp_sum(dot) * inv;
+            const float mn = fmaxf(m[h], s);
+            const float al = expf(m[h] - mn), p = expf(s - mn);
+            ls[h] = fmaf(ls[h], al, p);
+            o[h][0] = fmaf(o[h][0], al, p * v0.x);
+            o[h][1] = fmaf(o[h][1], al, p * v0.y);
+            o[h][2] = fmaf(o[h][2], al, p * v1.x);
+            o[h][3] = fmaf(o[h][3], al, p * v1.y);
+            m[h] = mn;
+          }
         }
       }
     }
-    named_sync();
-    if ((uint32_t)warp < G) {
-      const float sv = (uint32_t)lane < nb ? sc[warp * kD1KvBlk + lane] : -INFINITY;
-      const float mb = warp_max(sv);
-      const float mo = mst[warp], mn = fmaxf(mo, mb);
-      const float p = (uint32_t)lane < nb ? expf(sv - mn) : 0.f;
-      if ((uint32_t)lane < nb) sc[warp * kD1KvBlk + lane] = p;
-      const float ls = warp_sum(p);
-      if (lane == 0) {
-        const float al = mo == -INFINITY ? 0.f : expf(mo - mn);
-        alp[warp] = al;
-        lst[warp] = lst[warp] * al + ls;
-        mst[warp] = mn;
-      }
+    if (b0 + 2 < g.nblk) {
+      named_sync();
+      if (threadIdx.x == 0)
+        for (uint32_t blk = b0 + 2; blk < b0 + 4 && blk < g.nblk; ++blk) att_issue(c, g, l, pos, blk);
     }
-    named_sync();
-    accv *= alp[gh];
-    for (uint32_t i = part; i < nb; i += NP) {
-      const __half* vr = (tb + i == (uint32_t)pos) ? vnew : vb + i * 128;
-      accv = fmaf(sc[gh * kD1KvBlk + i], __half2float(vr[d]), accv);
-    }
-    named_sync();
-    if (threadIdx.x == 0 && blk + 2 < g.nblk) att_issue(c, g, l, pos, blk + 2);
   }
   c.kvseq += g.nblk;
   D1_STAMP(c, 14);
-  float* comb = reinterpret_cast<float*>(sm + OFF_COMB);
-  comb[gq * 128 + d] = accv;
-  named_sync();
-  if (threadIdx.x < G * 128) {
-    float o = 0.f;
-    for (uint32_t p = 0; p < NP; ++p) o += comb[(p * G + gh) * 128 + d];
-    float* rec = a.att + ((size_t)(g.j * S + g.s) * G + gh) * kD1AttRec;
-    rec[4 + d] = o;
-    if (d == 0) {
-      rec[0] = mst[gh];
-      rec[1] = lst[gh];
+  // merge the 16 warps' partials (the K/V stages are idle now): per-warp
+  // (max, sum) and output rows to shared memory, the G x 16 rescale factors
+  // once, then every (head, dim) sums its 16 rescaled rows
+  float* po = reinterpret_cast<float*>(sm + OFF_KV);          // [warp][G][128]
+  float* fw = reinterpret_cast<float*>(sm + OFF_SC) + kD1Warps * kD1MaxG;   // [G][16] factors
+  named_sync();   // every warp is done reading the K/V stages
+#pragma unroll
+  for (int h = 0; h < GT; ++h)
+    *reinterpret_cast<float4*>(po + (warp * GT + h) * 128 + 4 * lane) = make_float4(o[h][0], o[h][1], o[h][2], o[h][3]);
+  if (lane == 0)
+#pragma unroll
+    for (int h = 0; h < GT; ++h) {
+      wst[warp * kD1MaxG + h] = m[h];
+      acc[warp * kD1MaxG + h] = ls[h];
     }
+  named_sync();
+  if (threadIdx.x < GT * kD1Warps) {
+    const uint32_t h = threadIdx.x / kD1Warps, w = threadIdx.x % kD1Warps;
+    float M = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < kD1Warps; ++q) M = fmaxf(M, wst[q * kD1MaxG + h]);
+    const float mw = wst[w * kD1MaxG + h];
+    fw[h * kD1Warps + w] = mw == -INFINITY ? 0.f : expf(mw - M);
+    if (w == 0) lsum[h] = M;
   }
   named_sync();
-  if (threadIdx.x == 0) red_release_u32(a.cnt + (size_t)(a.g.L + l) * a.g.nkv + g.j, 1u);
+  if (threadIdx.x < G * 128) {
+    const uint32_t h = threadIdx.x >> 7, d = threadIdx.x & 127u;
+    float ov = 0.f, lv = 0.f;
+#pragma unroll
+    for (int w = 0; w < kD1Warps; ++w) {
+      const float f = fw[h * kD1Warps + w];
+      ov = fmaf(f, po[(w * GT + h) * 128 + d], ov);
+      lv = fmaf(f, acc[w * kD1MaxG + h], lv);
+    }
+    float* rec = a.att + ((size_t)(g.j * S + g.s) * G + h) * kD1AttRec;
+    rec[4 + d] = ov;
+    if (d == 0) {
+      rec[0] = lsum[h];
+      rec[1] = lv;
+    }
+    __syncwarp();
+    if (lane == 0) red_release_u32(a.cnt + (size_t)(a.g.L + l) * a.g.nkv + g.j, 1u);
+  }
+}
+
+// Thread 0 of an attention CTA: prefetch the first two K/V blocks of layer l.
+__device__ __forceinline__ void att_prefetch(Ctx& c, const AttGeo& g, uint32_t l, int pos) {
+  for (uint32_t b = 0; b < 2 && b < g.nblk; ++b) att_issue(c, g, l, pos, b);
 }
 
 // ---- O projection -----------------------------------------------------------------------------
-__device__ void o_phase(Ctx& c, uint32_t l, uint32_t Kb, uint32_t epoch_tok) {
+__device__ D1_PHASE void o_phase(Ctx& c, uint32_t l, uint32_t Kb, uint32_t epoch_tok) {
   const D1Args& a = *c.a;
   const D1Geom& G_ = a.g;
   const uint32_t h = c.c / G_.nrr, r = c.c % G_.nrr;
   const uint32_t rb0 = d1_lo(r, G_.nrb_h, G_.nrr), rb1 = d1_lo(r + 1, G_.nrb_h, G_.nrr);
   const uint32_t j = h / G_.G, gq = h % G_.G, S = G_.S;
   uint8_t* sm = c.sm;
-  if (threadIdx.x == 0) wait_count(a.cnt + (size_t)(G_.L + l) * G_.nkv + j, (epoch_tok + 1) * S, a);
+  float* mer = reinterpret_cast<float*>(sm + OFF_MER);      // [4 warps][132]
+  if (threadIdx.x == 0) wait_count(a.cnt + (size_t)(G_.L + l) * G_.nkv + j, (epoch_tok + 1) * S * G_.G * 4, a);
   named_sync();
   D1_STAMP(c, 15);
-  // merge the head's splits: thread (part, d) folds splits part, part + 4, ...
-  const uint32_t d = threadIdx.x & 127u, part = threadIdx.x >> 7;
-  float M = -INFINITY, Ls = 0.f, O = 0.f;
-  for (uint32_t s0 = part; s0 < S; s0 += 16) {
-    float mv[4], lv[4], ov[4];
+  // warps 0..3 fold splits s = warp, warp + 4, ... (lane: dims 4 lane .. + 3)
+  if (c.warp < 4) {
+    float M = -INFINITY, Ls = 0.f, O[4] = {0.f, 0.f, 0.f, 0.f};
+    for (uint32_t s0 = c.warp; s0 < S; s0 += 32) {
+      float mv[8], lv[8];
+      float4 ov[8];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t s = s0 + 4 * q;
-      if (s < S) {
-        const float* rec = a.att + ((size_t)(j * S + s) * G_.G + gq) * kD1AttRec;
-        mv[q] = __ldcg(rec);
-        lv[q] = __ldcg(rec + 1);
-        ov[q] = __ldcg(rec + 4 + d);
-      } else {
-        mv[q] = -INFINITY; lv[q] = 0.f; ov[q] = 0.f;
+      for (int q = 0; q < 8; ++q) {
+        const uint32_t s = s0 + 4 * q;
+        if (s < S) {
+          const float* rec = a.att + ((size_t)(j * S + s) * G_.G + gq) * kD1AttRec;
+          mv[q] = __ldcg(rec);
+          lv[q] = __ldcg(rec + 1);
+          ov[q] = __ldcg(reinterpret_cast<const float4*>(rec + 4) + c.lane);
+        } else {
+          mv[q] = -INFINITY; lv[q] = 0.f; ov[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      float nm = M;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) nm = fmaxf(nm, mv[q]);
+      if (nm != -INFINITY) {
+        const float al = M == -INFINITY ? 0.f : expf(M - nm);
+        Ls *= al; O[0] *= al; O[1] *= al; O[2] *= al; O[3] *= al;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float f = mv[q] == -INFINITY ? 0.f : expf(mv[q] - nm);
+          Ls = fmaf(f, lv[q], Ls);
+          O[0] = fmaf(f, ov[q].x, O[0]); O[1] = fmaf(f, ov[q].y, O[1]);
+          O[2] = fmaf(f, ov[q].z, O[2]); O[3] = fmaf(f, ov[q].w, O[3]);
+        }
+        M = nm;
       }
     }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      if (mv[q] == -INFINITY) continue;
-      const float nm = fmaxf(M, mv[q]);
-      const float a1 = M == -INFINITY ? 0.f : expf(M - nm), a2 = expf(mv[q] - nm);
-      Ls = Ls * a1 + lv[q] * a2;
-      O = O * a1 + ov[q] * a2;
-      M = nm;
+    reinterpret_cast<float4*>(mer + c.warp * kD1AttRec + 4)[c.lane] = make_float4(O[0], O[1], O[2], O[3]);
+    if (c.lane == 0) {
+      mer[c.warp * kD1AttRec] = M;
+      mer[c.warp * kD1AttRec + 1] = Ls;
     }
   }
-  float* mer = reinterpret_cast<float*>(sm + OFF_MER);
-  mer[part * kD1AttRec + 4 + d] = O;
-  if (d == 0) {
-    mer[part * kD1AttRec] = M;
-    mer[part * kD1AttRec + 1] = Ls;
-  }
   named_sync();
-  float* xo = reinterpret_cast<float*>(sm + OFF_XO);
-  if (threadIdx.x < 128) {
+  if (c.warp == 0) {
     float Mt = -INFINITY;
 #pragma unroll
     for (int p = 0; p < 4; ++p) Mt = fmaxf(Mt, mer[p * kD1AttRec]);
-    float Lt = 0.f, Ot = 0.f;
+    float Lt = 0.f, Ot[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
       const float mp = mer[p * kD1AttRec];
       const float f = mp == -INFINITY ? 0.f : expf(mp - Mt);
       Lt = fmaf(f, mer[p * kD1AttRec + 1], Lt);
-      Ot = fmaf(f, mer[p * kD1AttRec + 4 + d], Ot);
+      const float4 op = reinterpret_cast<const float4*>(mer + p * kD1AttRec + 4)[c.lane];
+      Ot[0] = fmaf(f, op.x, Ot[0]); Ot[1] = fmaf(f, op.y, Ot[1]);
+      Ot[2] = fmaf(f, op.z, Ot[2]); Ot[3] = fmaf(f, op.w, Ot[3]);
     }
-    xo[d] = __half2float(__float2half_rn(Ot / Lt));
-  }
-  named_sync();
-  if (c.warp == 0) {
-    const float4 x4 = *reinterpret_cast<const float4*>(xo + 4 * c.lane);
-    const float x[4] = {x4.x, x4.y, x4.z, x4.w};
+    float x[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) x[e] = __half2float(__float2half_rn(Ot[e] / Lt));
     quant_group(x, 0, c.lane, sm);
   }
   named_sync();
   D1_STAMP(c, 16);
-  const uint2* xb = reinterpret_cast<const uint2*>(sm + OFF_XB);
-  const float ef = reinterpret_cast<const float*>(sm + OFF_GEF)[0];
-  const int sq = reinterpret_cast<const int*>(sm + OFF_GSQ)[0];
-  float* Zl = a.Z + (size_t)(l & 1) * G_.H;
-  const int r0 = c.lane >> 2;
-  for (uint32_t rb = rb0 + c.warp; rb < rb1; rb += kD1Warps) {
-    const uint32_t u = rb - rb0;
-    const uint8_t* unit = ring_get(c, Kb + u / 32) + (u % 32) * kD1Unit;
-    int acc[4];
-    unit_mma(unit, xb, c.lane, acc);
-    const uint16_t* scl = reinterpret_cast<const uint16_t*>(unit + 256);
-    float y0 = 0.f, y1 = 0.f;
-    unit_epi(acc, h2f(scl[r0]) * ef, h2f(scl[r0 + 8]) * ef, sq, y0, y1, c.lane);
-    red_rows16(Zl + rb * 16, y0, y1, c.lane);
-  }
+  mv_units(c, Kb, rb1 - rb0, 1, 1, a.Z + (size_t)(l & 1) * G_.H, rb0, 0);
 }
 
-// ---- gate/up + SiLU + down ---------------------------------------------------------------------
-__device__ void gudn_phase(Ctx& c, uint32_t l, uint32_t Kg, uint32_t tok) {
+// ---- gate/up + SiLU*up --------------------------------------------------------------------------
+__device__ D1_PHASE void gu_phase(Ctx& c, uint32_t l, uint32_t Kg, uint32_t tok) {
   const D1Args& a = *c.a;
   const D1Geom& g = a.g;
   uint8_t* sm = c.sm;
   const uint32_t i0 = d1_lo(c.c, g.nrb_i, g.P), nb = d1_lo(c.c + 1, g.nrb_i, g.P) - i0;
-  const uint32_t Kd = Kg + g.cg;
-  float* Rn = a.R + (size_t)((l + 1) & 1) * g.H;
   if (nb) {
-    norm_prologue(c, 1, l, tok, a.layers[l].ffn_norm);
+    norm_prologue(c, 1, l, tok, reinterpret_cast<const D1Layer*>(sm + OFF_LAY)[l].ffn_norm);
     D1_STAMP(c, 17);
-    mv_group_split(c, Kg, 2 * nb * g.GH);
+    mv_units(c, Kg, 2 * nb, g.GH, 0, nullptr, 0, 0);
     D1_STAMP(c, 18);
     named_sync();
-    float* rows = reinterpret_cast<float*>(sm + OFF_ROWS);
     if (threadIdx.x < nb * 16) {
       const uint32_t p = threadIdx.x / 16, rr = threadIdx.x % 16;
       const float* part = reinterpret_cast<const float*>(sm + OFF_PART);
@@ -775,61 +840,52 @@ __device__ void gudn_phase(Ctx& c, uint32_t l, uint32_t Kg, uint32_t tok) {
         gv += part[(w * kD1MaxRb + 2 * p) * 16 + rr];
         uv += part[(w * kD1MaxRb + 2 * p + 1) * 16 + rr];
       }
-      rows[threadIdx.x] = __half2float(__float2half_rn(gv / (1.0f + expf(-gv)) * uv));
+      a.h[(size_t)i0 * 16 + threadIdx.x] = __float2half_rn(gv / (1.0f + expf(-gv)) * uv);
     }
-    named_sync();
-    if (c.warp == 0) {
-      const uint32_t p = c.lane >> 2;
-      const bool act = p < nb;
-      float x[4] = {0.f, 0.f, 0.f, 0.f};
-      if (act) {
-        const float4 x4 = *reinterpret_cast<const float4*>(rows + p * 16 + 4 * (c.lane & 3));
-        x[0] = x4.x; x[1] = x4.y; x[2] = x4.z; x[3] = x4.w;
-      }
-      quant_chunk16(x, p, c.lane, act, sm);
+  }
+  ring_release_upto(c, Kg + g.cg);
+}
+
+// ---- down projection: whole output rows, K = I ------------------------------------------------------
+__device__ D1_PHASE void dn_phase(Ctx& c, uint32_t l, uint32_t Kd, uint32_t tok) {
+  const D1Args& a = *c.a;
+  const D1Geom& g = a.g;
+  uint8_t* sm = c.sm;
+  const uint32_t rb0 = d1_lo(c.c, g.nrb_h, g.P), rb1 = d1_lo(c.c + 1, g.nrb_h, g.P), nrb = rb1 - rb0;
+  if (nrb) {
+    // h (fp16, written before the barrier) -> B fragments of every group
+    for (uint32_t gg = c.warp; gg < g.GI; gg += kD1Warps) {
+      const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(a.h + (size_t)gg * 128) + c.lane);
+      const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+      const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+      const float x[4] = {f0.x, f0.y, f1.x, f1.y};
+      quant_group(x, gg, c.lane, sm);
     }
-    ring_release_upto(c, Kd);
     named_sync();
     D1_STAMP(c, 19);
-    // down projection: all H rows (row block R per warp step) x this CTA's nb k16 chunks
-    const uint32_t* xb16 = reinterpret_cast<const uint32_t*>(sm + OFF_XB16);
-    const float* ef16 = reinterpret_cast<const float*>(sm + OFF_EF16);
-    const int* sq16 = reinterpret_cast<const int*>(sm + OFF_SQ16);
-    const uint32_t soff = al16(nb * 32), gbase = (16 * i0) / 128;
-    const int lane = c.lane, r0 = lane >> 2;
-    uint32_t curk = 0xffffffffu;
-    const uint8_t* ch = nullptr;
-    for (uint32_t R = c.warp; R < g.nrb_h; R += kD1Warps) {
-      if (Kd + R / g.dupc != curk) {
-        curk = Kd + R / g.dupc;
-        ch = ring_get(c, curk);
+    mv_units(c, Kd, nrb, g.GI, 0, nullptr, 0, 0);
+    named_sync();
+    // next residual = layer input + O accumulator + down projection (plain stores)
+    if (threadIdx.x < nrb * 16) {
+      const uint32_t rbl = threadIdx.x / 16, rr = threadIdx.x % 16, row = rb0 * 16 + threadIdx.x;
+      const float* pp = reinterpret_cast<const float*>(sm + OFF_PART);
+      float y = 0.f;
+#pragma unroll
+      for (int w = 0; w < kD1Warps; ++w) y += pp[(w * kD1MaxRb + rbl) * 16 + rr];
+      float x;
+      if (l == 0) {
+        const uint64_t f = (uint64_t)tok * g.H + row;
+        x = ((__ldg(a.emb_w + (f >> 3)) >> (f & 7)) & 1u) ? h2f(__ldg(a.emb_s + f / 128))
+                                                          : -h2f(__ldg(a.emb_s + f / 128));
+      } else {
+        x = __ldcg(a.R + (size_t)(l & 1) * g.H + row);
       }
-      const uint8_t* unit = ch + (R % g.dupc) * g.dub;
-      const uint16_t* scl = reinterpret_cast<const uint16_t*>(unit + soff);
-      float y0 = 0.f, y1 = 0.f;
-      for (uint32_t p = 0; p < nb; ++p) {
-        const uint32_t byte = unit[p * 32 + lane];
-        const uint32_t b = lane < 12 ? xb16[p * 12 + lane] : 0u;
-        int acc[4] = {0, 0, 0, 0};
-        mma_u8s8_k16(acc, spread4(byte & 0xFu), spread4(byte >> 4), b);
-        const uint32_t gl = (16 * (i0 + p)) / 128 - gbase;
-        const float ef = ef16[p];
-        unit_epi(acc, h2f(scl[gl * 16 + r0]) * ef, h2f(scl[gl * 16 + r0 + 8]) * ef, sq16[p], y0, y1, lane);
-      }
-      red_rows16(Rn + R * 16, y0, y1, lane);
+      x += __ldcg(a.Z + (size_t)(l & 1) * g.H + row);
+      a.R[(size_t)((l + 1) & 1) * g.H + row] = x + y;
     }
     D1_STAMP(c, 20);
   }
   ring_release_upto(c, Kd + g.cd);
-  // carry this CTA's slice of (layer input + O accumulator) into the next residual
-  const uint32_t e0 = d1_lo(c.c, g.H / 4, g.P) * 4, e1 = d1_lo(c.c + 1, g.H / 4, g.P) * 4;
-  if (threadIdx.x * 4 < e1 - e0) {
-    const uint32_t k = e0 + threadIdx.x * 4;
-    float v[4];
-    layer_in4(a, l, tok, k, v);
-    const float4 z = __ldcg(reinterpret_cast<const float4*>(a.Z + (size_t)(l & 1) * g.H + k));
-    red_add_v4(Rn + k, v[0] + z.x, v[1] + z.y, v[2] + z.z, v[3] + z.w);
-  }
 }
 
 // ---- QKV ----------------------------------------------------------------------------------------
@@ -840,51 +896,44 @@ __device__ __forceinline__ uint32_t kv_head_of_rb(const D1Geom& g, uint32_t rb) 
   return (row - qd - kvd) / 128;
 }
 
-__device__ void qkv_phase(Ctx& c, uint32_t l, uint32_t Kq, uint32_t tok) {
+__device__ D1_PHASE void qkv_phase(Ctx& c, uint32_t l, uint32_t Kq, uint32_t tok) {
   const D1Args& a = *c.a;
   const D1Geom& g = a.g;
   const uint32_t rb0 = d1_lo(c.c, g.nrb_qkv, g.P), rb1 = d1_lo(c.c + 1, g.nrb_qkv, g.P), nrb = rb1 - rb0;
-  // clear this CTA's slices of the next residual and the next O accumulator
+  // clear this CTA's slice of the next layer's O accumulator
   {
     const uint32_t e0 = d1_lo(c.c, g.H / 4, g.P) * 4, e1 = d1_lo(c.c + 1, g.H / 4, g.P) * 4;
-    if (threadIdx.x * 4 < e1 - e0) {
-      const uint32_t k = e0 + threadIdx.x * 4;
-      *reinterpret_cast<float4*>(a.R + (size_t)((l + 1) & 1) * g.H + k) = make_float4(0.f, 0.f, 0.f, 0.f);
-      *reinterpret_cast<float4*>(a.Z + (size_t)((l + 1) & 1) * g.H + k) = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    if (threadIdx.x * 4 < e1 - e0)
+      *reinterpret_cast<float4*>(a.Z + (size_t)((l + 1) & 1) * g.H + e0 + threadIdx.x * 4) =
+          make_float4(0.f, 0.f, 0.f, 0.f);
   }
   if (nrb) {
     D1_STAMP(c, 8);
-    norm_prologue(c, 0, l, tok, a.layers[l].attn_norm);
+    norm_prologue(c, 0, l, tok, reinterpret_cast<const D1Layer*>(c.sm + OFF_LAY)[l].attn_norm);
     D1_STAMP(c, 9);
-    mv_group_split(c, Kq, nrb * g.GH);
+    mv_units(c, Kq, nrb, g.GH, 0, nullptr, 0, 0);
     D1_STAMP(c, 10);
     named_sync();
-    if (threadIdx.x < nrb * 16) {
-      const float* part = reinterpret_cast<const float*>(c.sm + OFF_PART);
+    if (threadIdx.x < ((nrb * 16 + 31) & ~31u)) {   // whole warps
       const uint32_t rbl = threadIdx.x / 16, rr = threadIdx.x % 16;
-      float y = 0.f;
+      if (rbl < nrb) {
+        const float* part = reinterpret_cast<const float*>(c.sm + OFF_PART);
+        float y = 0.f;
 #pragma unroll
-      for (int w = 0; w < kD1Warps; ++w) y += part[(w * kD1MaxRb + rbl) * 16 + rr];
-      a.qkv[rb0 * 16 + threadIdx.x] = __float2half_rn(y);
+        for (int w = 0; w < kD1Warps; ++w) y += part[(w * kD1MaxRb + rbl) * 16 + rr];
+        a.qkv[rb0 * 16 + threadIdx.x] = __float2half_rn(y);
+      }
+      // publish per row block: the warp syncs, one lane per block releases
+      __syncwarp();
+      if (rr == 0 && rbl < nrb) red_release_u32(a.cnt + (size_t)l * g.nkv + kv_head_of_rb(g, rb0 + rbl), 1u);
     }
   }
-  ring_release_upto(c, Kq + g.cq);
-  named_sync();
   D1_STAMP(c, 11);
-  if (threadIdx.x == 0 && nrb) {
-    uint32_t rb = rb0;
-    while (rb < rb1) {
-      const uint32_t j = kv_head_of_rb(g, rb);
-      uint32_t n = 0;
-      while (rb < rb1 && kv_head_of_rb(g, rb) == j) { ++rb; ++n; }
-      red_release_u32(a.cnt + (size_t)l * g.nkv + j, n);
-    }
-  }
+  ring_release_upto(c, Kq + g.cq);
 }
 
 // ---- LM head --------------------------------------------------------------------------------------
-__device__ void lm_phase(Ctx& c, uint32_t Kl) {
+__device__ D1_PHASE void lm_phase(Ctx& c, uint32_t Kl) {
   const D1Args& a = *c.a;
   const D1Geom& g = a.g;
   uint8_t* sm = c.sm;
@@ -900,41 +949,7 @@ __device__ void lm_phase(Ctx& c, uint32_t Kl) {
   if (rb1 > rb0) {
     norm_prologue(c, 2, g.L, 0, a.fnorm);
     D1_STAMP(c, 21);
-    const uint2* xb = reinterpret_cast<const uint2*>(sm + OFF_XB);
-    const float* gef = reinterpret_cast<const float*>(sm + OFF_GEF);
-    const int* gsq = reinterpret_cast<const int*>(sm + OFF_GSQ);
-    const int lane = c.lane, r0 = lane >> 2;
-    uint32_t curk = 0xffffffffu;
-    const uint8_t* ch = nullptr;
-    for (uint32_t rb = rb0 + c.warp; rb < rb1; rb += kD1Warps) {
-      float y0 = 0.f, y1 = 0.f;
-      for (uint32_t gg = 0; gg < g.GH; ++gg) {
-        const uint32_t u = (rb - rb0) * g.GH + gg;
-        if (Kl + u / 32 != curk) {
-          curk = Kl + u / 32;
-          ch = ring_get(c, curk);
-        }
-        const uint8_t* unit = ch + (u % 32) * kD1Unit;
-        int acc[4];
-        unit_mma(unit, xb + gg * 48, lane, acc);
-        const uint16_t* scl = reinterpret_cast<const uint16_t*>(unit + 256);
-        const float ef = gef[gg];
-        unit_epi(acc, h2f(scl[r0]) * ef, h2f(scl[r0 + 8]) * ef, gsq[gg], y0, y1, lane);
-      }
-      if ((lane & 3) == 0) {
-        const uint32_t ra = rb * 16 + r0, rbb = ra + 8;
-        if (ra < g.V) {
-          if (a.logits) a.logits[ra] = y0;
-          const unsigned long long k = argmax_pack(y0, ra);
-          best = k > best ? k : best;
-        }
-        if (rbb < g.V) {
-          if (a.logits) a.logits[rbb] = y1;
-          const unsigned long long k = argmax_pack(y1, rbb);
-          best = k > best ? k : best;
-        }
-      }
-    }
+    best = mv_units(c, Kl, rb1 - rb0, g.GH, 2, a.logits, rb0, g.V);
   }
   ring_release_upto(c, Kl + g.clm);
 #pragma unroll
@@ -953,42 +968,33 @@ __device__ void lm_phase(Ctx& c, uint32_t Kl) {
   }
 }
 
-// ---- producer warp ----------------------------------------------------------------------------------
-__device__ void producer(const D1Args& a, uint8_t* sm) {
-  const uint32_t c = blockIdx.x, nck = a.g.nck, total = a.ntok * nck;
-  const uint8_t* base = a.stream + (size_t)c * nck * kD1Chunk;
-  const uint32_t* cb = a.chunk_bytes + (size_t)c * nck;
-  uint32_t issued = 0;
-  for (uint32_t K = 0; K < total; ++K) {
-    const uint32_t s = K % kD1Slots, k = K % nck;
-    if (K >= (uint32_t)kD1Slots && !wait_mbar(emptyb(sm, s), ((K / kD1Slots) - 1) & 1u, a)) break;
-    if (ld_relaxed_u32(&a.bar[2])) break;
-    const uint32_t bytes = __ldg(cb + k);
-    mbar_arrive_expect_tx(fullb(sm, s), bytes);
-    if (bytes) bulk_g2s(sm + OFF_RING + s * kD1Chunk, base + (size_t)k * kD1Chunk, bytes, fullb(sm, s));
-    issued = K + 1;
-  }
-  // drain: the last copy issued into every slot has landed before the CTA exits
-  const uint32_t from = issued > (uint32_t)kD1Slots ? issued - kD1Slots : 0;
-  for (uint32_t K = from; K < issued; ++K) drain_mbar(fullb(sm, K % kD1Slots), (K / kD1Slots) & 1u);
-}
-
 __global__ void __launch_bounds__(kD1Threads, 1) d1_kernel(const __grid_constant__ D1Args a) {
   extern __shared__ __align__(1024) uint8_t sm[];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  {
+    uint32_t* cbs = reinterpret_cast<uint32_t*>(sm + OFF_CB);
+    const uint32_t n = a.g.nck < kD1CbMax ? a.g.nck : kD1CbMax;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) cbs[i] = __ldg(a.chunk_bytes + (size_t)blockIdx.x * a.g.nck + i);
+    if (threadIdx.x < (uint32_t)kD1Slots) reinterpret_cast<uint32_t*>(sm + OFF_RELC)[threadIdx.x] = 0u;
+    for (uint32_t i = threadIdx.x; i < a.g.L; i += blockDim.x)
+      reinterpret_cast<D1Layer*>(sm + OFF_LAY)[i] = a.layers[i];
+  }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kD1Slots; ++s) {
-      mbar_init(fullb(sm, s), 1);
-      mbar_init(emptyb(sm, s), kD1Warps);
-    }
+    for (int s = 0; s < kD1Slots; ++s) mbar_init(fullb(sm, s), 1);
     mbar_init(kvbar(sm, 0), 1);
     mbar_init(kvbar(sm, 1), 1);
     fence_barrier_init();
   }
   __syncthreads();
-  if (warp == kD1Warps) {
-    if (lane == 0) producer(a, sm);
-    return;
+  if (threadIdx.x == 0) {
+    const uint32_t total = a.ntok * a.g.nck;
+    for (uint32_t K = 0; K < (uint32_t)kD1Slots && K < total; ++K) ring_issue(a, sm, K);
+  } else if (threadIdx.x == 32) {
+    const D1Layer* lt = reinterpret_cast<const D1Layer*>(sm + OFF_LAY);
+    l2_prefetch(lt[0].attn_norm, a.g.H * 4);
+    l2_prefetch(lt[0].ffn_norm, a.g.H * 4);
+    l2_prefetch(lt[0].q_norm, 512);
+    l2_prefetch(lt[0].k_norm, 512);
   }
   Ctx c{};
   c.a = &a;
@@ -1041,16 +1047,43 @@ __global__ void __launch_bounds__(kD1Threads, 1) d1_kernel(const __grid_constant
       const uint32_t Kl = Kt + l * g.cpl;
       const bool st_l = stamps && t == 0 && l == 1;
       c.pf = st_l ? a.prof : nullptr;
+      c.probe = a.prof && t == 0 && l == 1;
+      if (c.probe && threadIdx.x == 0) tokp[3] = 0u;
+      c.nbar = 0;
       if (l > 0) grid_bar(c);
       if (st_l) a.prof[0] = gtimer();
-      if (att_cta && threadIdx.x == 0) {
-        // the cache rows were written by generic stores (earlier layers / tokens)
+      if (threadIdx.x == 32) {
+        // the next layer's (or the final) norm vectors: L2 misses on the
+        // critical path otherwise (the streamed weights evict them)
+        const D1Layer* lt = reinterpret_cast<const D1Layer*>(sm + OFF_LAY);
+        if (l + 1 < g.L) {
+          l2_prefetch(lt[l + 1].attn_norm, g.H * 4);
+          l2_prefetch(lt[l + 1].ffn_norm, g.H * 4);
+          l2_prefetch(lt[l + 1].q_norm, 512);
+          l2_prefetch(lt[l + 1].k_norm, 512);
+        } else {
+          l2_prefetch(a.fnorm, g.H * 4);
+          l2_prefetch(lt[0].attn_norm, g.H * 4);
+          l2_prefetch(lt[0].ffn_norm, g.H * 4);
+          l2_prefetch(lt[0].q_norm, 512);
+          l2_prefetch(lt[0].k_norm, 512);
+        }
+      }
+      if (l == 0 && att_cta && threadIdx.x == 0) {
+        // every cache row the bulk copies of this token read was written by
+        // generic stores in earlier tokens, ordered before this point by the
+        // grid barriers; one proxy fence orders them before the async reads
         fence_proxy_async();
-        for (uint32_t b = 0; b < 2 && b < ag.nblk; ++b) att_issue(c, ag, l, pos, b);
+        att_prefetch(c, ag, 0, pos);
       }
       qkv_phase(c, l, Kl, tok);
       if (st_l) a.prof[1] = gtimer();
-      if (att_cta) att_phase(c, l, pos, ep);
+      if (att_cta) {
+        if (g.G == 1) att_phase<1>(c, l, pos, ep);
+        else if (g.G == 2) att_phase<2>(c, l, pos, ep);
+        else att_phase<4>(c, l, pos, ep);
+        if (threadIdx.x == 0 && l + 1 < g.L) att_prefetch(c, ag, l + 1, pos);
+      }
       if (st_l) a.prof[2] = gtimer();
       if (o_cta) o_phase(c, l, Kl + g.cq, ep);
       ring_release_upto(c, Kl + g.cq + g.co);
@@ -1064,8 +1097,15 @@ __global__ void __launch_bounds__(kD1Threads, 1) d1_kernel(const __grid_constant
         if (adv && a.seq && (uint32_t)pos < a.seq_len) a.seq[pos] = tok;
         a.st->argmax[0] = 0ull;
       }
-      gudn_phase(c, l, Kl + g.cq + g.co, tok);
+      gu_phase(c, l, Kl + g.cq + g.co, tok);
+      grid_bar(c);
+      if (st_l) a.prof[22] = gtimer();
+      dn_phase(c, l, Kl + g.cq + g.co + g.cg, tok);
       if (st_l) a.prof[5] = gtimer();
+      if (c.probe) {
+        named_sync();
+        if (threadIdx.x == 0 && c.c == 0) a.prof[30] = tokp[3];
+      }
     }
     c.pf = nullptr;
     grid_bar(c);
@@ -1077,7 +1117,16 @@ __global__ void __launch_bounds__(kD1Threads, 1) d1_kernel(const __grid_constant
     grid_bar(c);
     if (a.tstamp && c.c == 0 && threadIdx.x == 0) a.tstamp[t + 1] = gtimer();
   }
-  // drain K/V copies that a failed wait skipped (the last one issued per stage)
+  // drain copies that failed waits skipped: the last one issued into every
+  // ring slot and K/V stage has landed before the CTA exits
+  named_sync();
+  if (threadIdx.x == 0 && (c.failed || ld_relaxed_u32(&a.bar[2]))) {
+    const uint32_t total = a.ntok * g.nck;
+    for (uint32_t s = 0; s < (uint32_t)kD1Slots && s < total; ++s) {
+      const uint32_t K = reinterpret_cast<const uint32_t*>(sm + OFF_ISS)[s];
+      drain_mbar(fullb(sm, s), (K / kD1Slots) & 1u);
+    }
+  }
   if (threadIdx.x == 0 && c.kv_hi > c.kvseq) {
     for (uint32_t s = c.kv_hi > 2 ? c.kv_hi - 2 : 0; s < c.kv_hi; ++s) drain_mbar(kvbar(sm, s & 1u), (s >> 1) & 1u);
   }
@@ -1121,28 +1170,6 @@ void put_unit(uint8_t* dst, const uint8_t* bits, const uint16_t* s, uint32_t M, 
   }
 }
 
-// Down-projection unit: row block R of the H x I matrix, K slice [16 i0, 16 (i0 + nb)).
-void put_dn_unit(uint8_t* dst, const D1Geom& g, const uint8_t* bits, const uint16_t* s, uint32_t R, uint32_t i0,
-                 uint32_t nb) {
-  const uint32_t M = g.H, K = g.I;
-  for (uint32_t p = 0; p < nb; ++p)
-    for (uint32_t lane = 0; lane < 32; ++lane) {
-      uint32_t byte = 0;
-      for (uint32_t r = 0; r < 2; ++r)
-        for (uint32_t i = 0; i < 4; ++i) {
-          const uint32_t row = R * 16 + lane / 4 + 8 * r, k = 16 * (i0 + p) + (lane % 4) * 4 + i;
-          byte |= bit_at(bits, M, K, row, k) << (r * 4 + i);
-        }
-      dst[p * 32 + lane] = (uint8_t)byte;
-    }
-  const uint32_t soff = al16(nb * 32), ng = d1_dn_groups(i0, nb), gb = (16 * i0) / 128;
-  for (uint32_t gl = 0; gl < ng; ++gl)
-    for (uint32_t rr = 0; rr < 16; ++rr) {
-      const uint16_t v = scale_at(s, M, K, R * 16 + rr, gb + gl);
-      memcpy(dst + soff + gl * 32 + rr * 2, &v, 2);
-    }
-}
-
 }  // namespace
 
 uint32_t d1_smem_bytes() { return SMEM_TOTAL; }
@@ -1155,8 +1182,12 @@ bool d1_fits(int device, uint32_t P) {
     return false;
   }
   if (!coop || (uint32_t)nsm < P) return false;
-  if (cudaFuncSetAttribute(d1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_TOTAL) != cudaSuccess ||
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, d1_kernel, kD1Threads, SMEM_TOTAL) != cudaSuccess) {
+  cudaError_t e = cudaFuncSetAttribute(d1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_TOTAL);
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, d1_kernel, kD1Threads, SMEM_TOTAL);
+  const char* dbg = getenv("NNZ_D1_DEBUG");
+  if (dbg && dbg[0] == '1')
+    fprintf(stderr, "decode1: smem %u B, blocks/SM %d, %s\n", SMEM_TOTAL, per, cudaGetErrorString(e));
+  if (e != cudaSuccess) {
     cudaGetLastError();
     return false;
   }
@@ -1179,6 +1210,7 @@ void d1_chunk_bytes(const D1Geom& g, std::vector<uint32_t>& out) {
   for (uint32_t c = 0; c < g.P; ++c) {
     uint32_t* row = out.data() + (size_t)c * g.nck;
     const uint32_t nq_rb = d1_lo(c + 1, g.nrb_qkv, g.P) - d1_lo(c, g.nrb_qkv, g.P);
+    const uint32_t dn_rb = d1_lo(c + 1, g.nrb_h, g.P) - d1_lo(c, g.nrb_h, g.P);
     const uint32_t nb = d1_lo(c + 1, g.nrb_i, g.P) - d1_lo(c, g.nrb_i, g.P);
     uint32_t o_rb = 0;
     if (c < g.nq * g.nrr) {
@@ -1190,7 +1222,7 @@ void d1_chunk_bytes(const D1Geom& g, std::vector<uint32_t>& out) {
       fill(L0, g.cq, nq_rb * g.GH, 32, kD1Unit);
       fill(L0 + g.cq, g.co, o_rb, 32, kD1Unit);
       fill(L0 + g.cq + g.co, g.cg, 2 * nb * g.GH, 32, kD1Unit);
-      fill(L0 + g.cq + g.co + g.cg, g.cd, nb ? g.nrb_h : 0, g.dupc, g.dub);
+      fill(L0 + g.cq + g.co + g.cg, g.cd, dn_rb * g.GI, 32, kD1Unit);
     }
     const uint32_t lm_rb = d1_lo(c + 1, g.nrb_v, g.P) - d1_lo(c, g.nrb_v, g.P);
     fill(row + (size_t)g.L * g.cpl, g.clm, lm_rb * g.GH, 32, kD1Unit);
@@ -1233,10 +1265,14 @@ void d1_pack_layer(const D1Geom& g, const uint8_t* qkv_w, const uint16_t* qkv_s,
             put_unit(gb + (u / 32) * kD1Chunk + (u % 32) * kD1Unit, half ? up_w : gate_w, half ? up_s : gate_s,
                      g.I, g.H, (i0 + p) * 16, gg);
     }
-    if (nb) {
+    // down: units (rb, group) rb-major over this CTA's output row blocks, K = I
+    {
       uint8_t* db = base + (size_t)(g.cq + g.co + g.cg) * kD1Chunk;
-      for (uint32_t R = 0; R < g.nrb_h; ++R)
-        put_dn_unit(db + (R / g.dupc) * kD1Chunk + (R % g.dupc) * g.dub, g, dn_w, dn_s, R, i0, nb);
+      const uint32_t rb0 = d1_lo(c, g.nrb_h, g.P), rb1 = d1_lo(c + 1, g.nrb_h, g.P);
+      uint32_t u = 0;
+      for (uint32_t rb = rb0; rb < rb1; ++rb)
+        for (uint32_t gg = 0; gg < g.GI; ++gg, ++u)
+          put_unit(db + (u / 32) * kD1Chunk + (u % 32) * kD1Unit, dn_w, dn_s, g.H, g.I, rb * 16, gg);
     }
   }
 }

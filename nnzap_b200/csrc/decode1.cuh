@@ -9,10 +9,11 @@
 // Design (B200, 148 SMs, one CTA per SM):
 //  * Weights are re-laid out at load time into one contiguous byte stream per
 //    CTA, in the exact order that CTA consumes them (QKV, O, gate/up, down of
-//    every layer, then its LM-head rows).  A producer warp copies the stream
-//    into a 16-slot shared-memory ring with 9 KiB bulk copies (TMA engine, no
-//    multicast), running up to two layers ahead of the compute warps, and
-//    across token boundaries when a launch decodes several tokens.
+//    every layer, then its LM-head rows), copied into a 16-slot shared-memory
+//    ring with 9 KiB bulk copies (TMA engine, no multicast).  The warp that
+//    makes the last release of a slot issues the copy of the chunk 16
+//    ahead into it, so the stream runs up to two layers ahead of the
+//    compute, across token boundaries when a launch decodes several tokens.
 //  * The matvec core is the int8 tensor-core MMA (m16n8k32 / m16n8k16):
 //    1-bit weights become u8 {0,1} operands with one shift+AND per four
 //    weights, and each activation group is an exact fixed-point integer
@@ -22,9 +23,8 @@
 //    (every fp16 value representable relative to that maximum); smaller
 //    elements carry at most 2^(E-23) absolute error.
 //  * Per layer the critical path is QKV -> attention -> O (dataflow counters
-//    per kv head) -> grid barrier -> gate/up fused with down (each CTA applies
-//    the down projection to its own SiLU*up slice and red.adds the partial
-//    into the next residual) -> grid barrier.
+//    per kv head) -> grid barrier -> gate/up + SiLU*up -> grid barrier ->
+//    down projection (each CTA owns whole output rows) -> grid barrier.
 #pragma once
 #include "common.cuh"
 #include "misc.cuh"
@@ -33,15 +33,15 @@
 namespace nnz {
 
 constexpr int kD1Warps = 16;                        // compute warps
-constexpr int kD1Threads = (kD1Warps + 1) * 32;     // + one producer warp
+constexpr int kD1Threads = kD1Warps * 32;
 constexpr uint32_t kD1Unit = 288;                   // 16 rows x 128 k: 256 B bits + 32 B scales
 constexpr uint32_t kD1Chunk = 9216;                 // one ring slot = 32 units
 constexpr int kD1Slots = 16;
 constexpr int kD1KvBlk = 32;                        // attention positions per K/V block
 constexpr int kD1MaxG = 4;                          // query heads per kv head
-constexpr uint32_t kD1MaxGroups = 32;               // hidden <= 4096
+constexpr uint32_t kD1MaxGroups = 64;               // scale groups of the widest input (hidden, intermediate <= 8192)
 constexpr uint32_t kD1MaxRb = 8;                    // QKV row blocks / gate+up row blocks per CTA
-constexpr uint32_t kD1MaxNb = 4;                    // SiLU*up k16 chunks per CTA (down K slice)
+constexpr uint32_t kD1MaxLayers = 64;
 constexpr uint32_t kD1AttRec = 132;                 // m, l, 2 pad, o[128] (floats)
 
 // Work assignment shared by the host packer and the kernel.  Everything is a
@@ -49,57 +49,48 @@ constexpr uint32_t kD1AttRec = 132;                 // m, l, 2 pad, o[128] (floa
 struct D1Geom {
   uint32_t P, H, I, nq, nkv, L, V, max_ctx;
   uint32_t G;          // query heads per kv head
-  uint32_t GH;         // scale groups along H (H / 128)
+  uint32_t GH;         // scale groups along H (H / 128, a power of two)
+  uint32_t lgh;        // log2(GH)
   uint32_t qkv_rows, nrb_qkv, nrb_h, nrb_i, nrb_v;
+  uint32_t GI;         // scale groups along I (I / 128)
   uint32_t S;          // attention splits per kv head (nkv * S <= P)
   uint32_t nrr;        // O-projection row ranges per head (nq * nrr <= P)
-  uint32_t dub;        // bytes per down-projection unit (one 16-row block of the CTA's K slice)
-  uint32_t dupc;       // down units per chunk
   uint32_t cq, co, cg, cd, cpl, clm, nck;   // chunks: per phase, per layer, LM head, per token
 };
 
-__host__ __device__ inline uint32_t d1_lo(uint32_t c, uint32_t n, uint32_t P) {
-  return (uint32_t)(((uint64_t)c * n) / P);
-}
-
-// Down-projection groups touched by the K slice [16 i0, 16 (i0 + nb)).
-__host__ __device__ inline uint32_t d1_dn_groups(uint32_t i0, uint32_t nb) {
-  if (nb == 0) return 0;
-  return (16 * (i0 + nb) - 1) / 128 - (16 * i0) / 128 + 1;
-}
+// First item of part c when n items are cut into P near-equal parts.  32-bit
+// arithmetic (d1_geom checks that P * n fits): the kernel calls it in every
+// phase and a 64-bit division is a long software sequence on the GPU.
+__host__ __device__ inline uint32_t d1_lo(uint32_t c, uint32_t n, uint32_t P) { return (c * n) / P; }
 
 inline bool d1_geom(D1Geom& g, uint32_t P, uint32_t H, uint32_t I, uint32_t nq, uint32_t nkv,
                     uint32_t L, uint32_t V, uint32_t max_ctx) {
   g = D1Geom{};
   g.P = P; g.H = H; g.I = I; g.nq = nq; g.nkv = nkv; g.L = L; g.V = V; g.max_ctx = max_ctx;
-  if (!nkv || nq % nkv || H % 128 || H > 128 * kD1MaxGroups || I % 16 || !L || !V) return false;
+  if (!nkv || nq % nkv || H % 128 || H > 128 * 32 || I % 128 || I > 128 * kD1MaxGroups || !L || L > kD1MaxLayers || !V)
+    return false;
   g.G = nq / nkv;
   g.GH = H / 128;
+  g.GI = I / 128;
   if (g.G > (uint32_t)kD1MaxG || 4 % g.G || 32 % g.GH) return false;
+  while ((1u << g.lgh) < g.GH) ++g.lgh;
   g.qkv_rows = (nq + 2 * nkv) * 128;
   g.nrb_qkv = g.qkv_rows / 16;
   g.nrb_h = H / 16;
   g.nrb_i = I / 16;
   g.nrb_v = (V + 15) / 16;
   if (P < nkv || P < nq) return false;
+  const uint32_t nmax = g.nrb_v > I ? (g.nrb_v > max_ctx ? g.nrb_v : max_ctx) : (I > max_ctx ? I : max_ctx);
+  if ((uint64_t)(P + 1) * (nmax + 1) >= (1ull << 32)) return false;
   g.S = P / nkv;
   g.nrr = P / nq;
-  const uint32_t qrb = (g.nrb_qkv + P - 1) / P, nb = (g.nrb_i + P - 1) / P;
-  if (qrb > kD1MaxRb || 2 * nb > kD1MaxRb || nb > kD1MaxNb) return false;
-  // widest down unit over the CTAs (the stream uses one unit size)
-  uint32_t ngm = 0;
-  for (uint32_t c = 0; c < P; ++c) {
-    const uint32_t i0 = d1_lo(c, g.nrb_i, P), i1 = d1_lo(c + 1, g.nrb_i, P);
-    const uint32_t ng = d1_dn_groups(i0, i1 - i0);
-    ngm = ng > ngm ? ng : ngm;
-  }
-  g.dub = ((nb * 32 + 15) / 16) * 16 + ngm * 32;
-  g.dupc = kD1Chunk / g.dub;
+  const uint32_t qrb = (g.nrb_qkv + P - 1) / P, nb = (g.nrb_i + P - 1) / P, drb = (g.nrb_h + P - 1) / P;
+  if (qrb > kD1MaxRb || 2 * nb > kD1MaxRb || drb > kD1MaxRb) return false;
   const uint32_t orb = (g.nrb_h + g.nrr - 1) / g.nrr;
   g.cq = (qrb * g.GH + 31) / 32;
   g.co = (orb + 31) / 32;
   g.cg = (2 * nb * g.GH + 31) / 32;
-  g.cd = nb ? (g.nrb_h + g.dupc - 1) / g.dupc : 0;
+  g.cd = (drb * g.GI + 31) / 32;
   g.cpl = g.cq + g.co + g.cg + g.cd;
   const uint32_t lrb = (g.nrb_v + P - 1) / P;
   g.clm = (lrb * g.GH + 31) / 32;
@@ -128,6 +119,7 @@ struct D1Args {
   float* R;                        // [2][H] residual versions
   float* Z;                        // [2][H] O-projection accumulators
   __half* qkv;                     // [qkv_rows]
+  __half* h;                       // [I] SiLU(gate) * up
   float* att;                      // [nkv * S * G][kD1AttRec]
   unsigned int* cnt;               // [L][nkv] QKV row blocks done, then [L][nkv] attention splits done
   unsigned int* bar;               // [2] abort flag, [4..5] u64 grid-barrier arrivals
@@ -143,9 +135,9 @@ struct D1Args {
   unsigned long long* prof;        // optional per-phase stamps (CTA 0)
 };
 
-// Grid barriers per decoded token: one after each layer's O projection, one
-// before each next layer / the LM head, one after the LM head.
-inline uint32_t d1_barriers_per_token(const D1Geom& g) { return 2 * g.L + 1; }
+// Grid barriers per decoded token: per layer one after the O projection, one
+// after gate/up and one after the down projection; one after the LM head.
+inline uint32_t d1_barriers_per_token(const D1Geom& g) { return 3 * g.L + 1; }
 
 // Shared-memory bytes of the kernel.
 uint32_t d1_smem_bytes();

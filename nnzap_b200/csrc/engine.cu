@@ -1298,6 +1298,7 @@ static int model_finalize_impl(nnz_model* m) {
     a.Z = a.R + 2 * H;
     NNZ_CK(cudaMemset(a.R, 0, 4 * (size_t)H * 4));
     if ((rc = dalloc(m, (void**)&a.qkv, (size_t)d1g.qkv_rows * 2))) return rc;
+    if ((rc = dalloc(m, (void**)&a.h, (size_t)I * 2))) return rc;
     if ((rc = dalloc(m, (void**)&a.att, (size_t)c.num_kv_heads * d1g.S * d1g.G * kD1AttRec * 4))) return rc;
     m->d1_cnt_words = (size_t)2 * c.num_layers * c.num_kv_heads;
     if ((rc = dalloc(m, (void**)&a.cnt, m->d1_cnt_words * 4))) return rc;
@@ -1311,8 +1312,8 @@ static int model_finalize_impl(nnz_model* m) {
     if ((rc = dalloc(m, (void**)&a.tstamp, ((size_t)c.max_context_length + 1) * 8))) return rc;
     const char* prof = getenv("NNZ_D1_PROFILE");
     if (prof && prof[0] == '1') {
-      if ((rc = dalloc(m, (void**)&a.prof, 64 * 8))) return rc;
-      NNZ_CK(cudaMemset(a.prof, 0, 64 * 8));
+      if ((rc = dalloc(m, (void**)&a.prof, (64 + 8 * (size_t)d1g.P) * 8))) return rc;
+      NNZ_CK(cudaMemset(a.prof, 0, (64 + 8 * (size_t)d1g.P) * 8));
     }
   }
   NNZ_CK(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking));
@@ -1866,13 +1867,22 @@ int nnz_debug_gemm_profile(uint64_t* out) {
   return NNZ_OK;
 }
 
+// Development aid (not part of the documented ABI): which kernel runs a
+// batch-1 decode step: 1 = single-row kernel (decode1.cu), 2 = persistent
+// multi-row kernel (mega.cu), 0 = captured multi-kernel graph.
+int nnz_debug_decode_path(nnz_model* m) {
+  if (!m || !m->finalized) return fail(NNZ_ESTATE, "model not finalized");
+  if (m->d1_ok) return 1;
+  return mega_plan_for(m, 1) ? 2 : 0;
+}
+
 // Development aid (not part of the documented ABI): %globaltimer stamps of
 // the single-row decode kernel's CTA 0 (layer 1 phases of the first token of
 // the last launch) when the model was finalized with NNZ_D1_PROFILE=1.
 int nnz_debug_decode1_profile(nnz_model* m, uint64_t* out, uint32_t n) {
   if (!m || !out || !m->d1_ok || !m->d1.prof) return fail(NNZ_ESTATE, "profiling not enabled");
   NNZ_CK(cudaStreamSynchronize(m->st));
-  NNZ_CK(cudaMemcpy(out, m->d1.prof, 8 * std::min<uint32_t>(n, 64), cudaMemcpyDeviceToHost));
+  NNZ_CK(cudaMemcpy(out, m->d1.prof, 8 * std::min<uint32_t>(n, 64 + 8 * m->d1.g.P), cudaMemcpyDeviceToHost));
   return NNZ_OK;
 }
 
