@@ -32,8 +32,10 @@ def oracle_cfg(d):
 
 
 def build(d, seed=0, max_ctx=256, max_batch=4, path="persistent"):
-    """path: "persistent" (one cooperative kernel per decode step, the default)
-    or "graph" (the captured multi-kernel CUDA graph)."""
+    """path: "persistent" (the default: the single-row kernel for Q1 batch-1
+    steps, else the persistent multi-row kernel), "mega" (the multi-row
+    persistent kernel for every batch <= 8) or "graph" (the captured
+    multi-kernel CUDA graph)."""
     import os
     W = synth.make_model(d, seed=seed)
     old = os.environ.get("NNZ_DECODE_PATH")
@@ -59,7 +61,7 @@ def greedy_ok(cfg, W, prompt, toks, tol=2e-2):
     return exact
 
 
-@pytest.mark.parametrize("path", ["persistent", "graph"])
+@pytest.mark.parametrize("path", ["persistent", "mega", "graph"])
 @pytest.mark.parametrize("d", [SMALL_Q1, SMALL_Q4, SMALL_Q4_ENGINE, SMALL_HALF],
                          ids=["q1", "q4", "q4_engine_bf16", "q1_half_split_hd64"])
 def test_forward_decode_logits(cuda, built_lib, d, path):
@@ -98,7 +100,7 @@ def test_prefill_matches_decode_and_oracle(cuda, built_lib, d):
     m.free()
 
 
-@pytest.mark.parametrize("path", ["persistent", "graph"])
+@pytest.mark.parametrize("path", ["persistent", "mega", "graph"])
 @pytest.mark.parametrize("d", [SMALL_Q1, SMALL_Q4], ids=["q1", "q4"])
 def test_generate_greedy(cuda, built_lib, d, path):
     m, W = build(d, path=path)
@@ -125,7 +127,11 @@ def test_batched_decode_rows_independent(cuda, built_lib, path):
     am, lg = m.forward_decode(toks, pos, want_logits=True)
     for r in range(6):
         am1, lg1 = m.forward_decode([toks[r]], [0], want_logits=True)
-        np.testing.assert_allclose(lg1[0], lg[r], atol=1e-4)
+        # a single row runs the single-row kernel (exact 22-bit activation
+        # split) and a batch of 6 the multi-row one (15-bit split): the same
+        # row agrees to the multi-row kernel's rounding, not bit for bit
+        tol = 1e-4 if path != "persistent" else 2e-3
+        np.testing.assert_allclose(lg1[0], lg[r], atol=tol)
     out = m.decode_steps(toks, pos + 1, steps=5)
     assert out.shape == (5, 6)
     m.free()
