@@ -13,6 +13,14 @@ host->device, tokens device->host, prefill included).  Multi-GPU runs are
 independent replicas (batch-1 decode does not shard), so ``value`` sums the
 ranks' tokens over the slowest rank's time.
 
+The line also carries the reference bench's own keys (decode_tok_per_sec,
+prefill_tok_per_sec, decode_p50_us, decode_p99_us; see
+nnzap_b200/bonsai_bench.py for the drop-in entry point), a parity check of
+the benchmarked run itself (every generated token against the CPU oracle's
+teacher-forced logits), and ``tp_config4``: benchmark configuration 4
+(batch 64, KV 4096) decoded tensor-parallel over the job's N GPUs, with a
+TP-N vs TP-1 logits check at N > 1 and the 4-bit variant at N = 1.
+
 ``--impl reference`` times the CPU oracle's token-at-a-time decode on a
 bounded sample (the reference engine itself needs Apple Metal + Zig).
 """
@@ -34,6 +42,9 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 PROMPT, GEN = 512, 256
+# ncu (dram__bytes_read.sum + dram__bytes_write.sum) of one decode launch of
+# the config-3 model at context TRAFFIC_CTX (profiling command in DESIGN.md)
+TRAFFIC_BYTES, TRAFFIC_CTX = 338.3e6, 516
 METRIC = "decode_tok_per_sec"
 UNIT = "tok/s"
 
@@ -115,12 +126,13 @@ def launches_per_step(d, prompt, gen, chunk=512):
     """Our kernels launched per generate(): GEMM prefill per 512-row chunk
     (embed, 9 per layer: norm, QKV GEMM, K/V write, attention + split
     combine, O GEMM, norm, gate/up GEMM, down GEMM; LM head on the last
-    chunk) plus one persistent kernel per decode token (or, on the CUDA-graph
-    path, embed + 7 per layer: QKV, 3 attention kernels, O, gate/up, down +
-    LM head)."""
+    chunk) plus the decode: one single-row kernel launch for all greedy
+    tokens (NNZ_DECODE_PATH=mega: one persistent kernel per token; =graph:
+    embed + 7 per layer + LM head per token)."""
     chunks = -(-prompt // chunk)
-    per_tok = (1 + d.layers * 7 + 1) if os.environ.get("NNZ_DECODE_PATH") == "graph" else 1
-    return chunks * (1 + d.layers * 9) + 1 + gen * per_tok
+    path = os.environ.get("NNZ_DECODE_PATH")
+    decode = gen * (1 + d.layers * 7 + 1) if path == "graph" else gen if path == "mega" else 1
+    return chunks * (1 + d.layers * 9) + 1 + decode
 
 
 def oracle_cfg(d):
@@ -129,9 +141,12 @@ def oracle_cfg(d):
                  n_kv=d.n_kv, head_dim=d.head_dim, gs=d.gs, quant=d.quant)
 
 
-def cpu_decode_sample(d, W, n_prompt=24, n_decode=3):
-    """Token-at-a-time CPU decode with the oracle (all host cores via BLAS)."""
+def cpu_decode_sample(d, W, n_prompt=8, n_decode=16):
+    """Token-at-a-time CPU decode with the oracle (all host cores via BLAS),
+    every weight matrix dequantized once and kept (the first prompt token
+    pays for that)."""
     from oracle import qwen3_ref as R
+    R.set_dequant_cache(True)
     cfg = oracle_cfg(d)
     prompt = np.random.default_rng(0).integers(0, d.vocab, n_prompt)
     kv = []
@@ -146,6 +161,7 @@ def cpu_decode_sample(d, W, n_prompt=24, n_decode=3):
         lg = R.decode_one(cfg, W, kv, tok, n_prompt + i)
         tok = int(np.argmax(lg))
         times.append(time.perf_counter() - a)
+    R.set_dequant_cache(False)
     return {"decode_tok_per_sec": n_decode / sum(times), "prefill_tok_per_sec": n_prompt / (t1 - t0),
             "decode_s": sum(times), "prefill_s": t1 - t0, "n_prompt": n_prompt, "n_decode": n_decode}
 
@@ -159,6 +175,7 @@ def run_reference(args):
     d = synth.BONSAI_1_7B_Q1
     W = synth.make_model(d, seed=0)
     cfg = oracle_cfg(d)
+    R.set_dequant_cache(True)     # dequantize once, like a real CPU engine keeps its weights
     n_prompt = 8
     kv = []
     for p, tok in enumerate(np.random.default_rng(0).integers(0, d.vocab, n_prompt)):
@@ -175,7 +192,8 @@ def run_reference(args):
     v = args.steps / dt
     cores = os.cpu_count()
     sample = (f"oracle token-at-a-time decode of {args.steps} tokens (after an {n_prompt}-token "
-              f"prompt and {args.warmup} warm-up tokens) on the full config-3 model, numpy/BLAS")
+              f"prompt and {args.warmup} warm-up tokens) on the full config-3 model, numpy/BLAS, "
+              "weights dequantized once to f32")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1000 / args.steps,
@@ -225,20 +243,59 @@ def qmv_config0(torch, iters=200):
 C4_BATCH, C4_CTX = 64, 4096
 
 
-def run_config4(args):
-    """Benchmark configuration 4: 64 sequences decoded together with a 4096-position
-    KV cache, tensor-parallel over the job's GPUs (tp = N: heads, gate/up
-    rows and vocabulary split, NCCL all-reduce after o/down inside the decode
-    graph).  A step = one decode step of all 64 rows; positions start at
-    4096 - steps - warmup so the last step attends over 4095 positions."""
-    import torch
-    rank, world, local = rank_env()
-    torch.cuda.set_device(local)
+def _barrier(torch, world):
+    torch.cuda.synchronize()
     if world > 1:
-        import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+
+def _gpu_uuid(torch, local):
+    try:
+        u = str(torch.cuda.get_device_properties(local).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return None
+
+
+def tp_parity(torch, model, d, W, rank, world, local, rows=C4_BATCH, pos=16):
+    """TP-N logits vs a TP-1 model of the same weights on the same inputs
+    (fresh caches, one decode step of `rows` rows at position `pos`): the
+    vocabulary shards are gathered on rank 0, which builds the TP-1 model.
+    Returns {"max_abs": ..., "argmax_equal": ..., "near_ties": ...} on rank 0."""
+    from nnzap_b200 import Model, config_from_dims
+    tok = np.random.default_rng(1).integers(0, d.vocab, rows).astype(np.uint32)
+    _, lg = model.forward_decode(tok, np.full(rows, pos, np.uint32), want_logits=True)
+    shard = torch.from_numpy(np.ascontiguousarray(lg)).cuda()
+    parts = [torch.empty_like(shard) for _ in range(world)]
+    torch.distributed.all_gather(parts, shard)
+    if rank != 0:
+        _barrier(torch, world)
+        return None
+    full = torch.cat(parts, dim=1).cpu().numpy()
+    ref = Model(config_from_dims(d, max_context_length=pos + 8, max_batch=rows), device=local)
+    ref.load_weights(__import__("nnzap_b200").synth.iter_named_tensors(W))
+    _, want = ref.forward_decode(tok, np.full(rows, pos, np.uint32), want_logits=True)
+    ref.free()
+    _barrier(torch, world)
+    am_n, am_1 = full.argmax(1), want.argmax(1)
+    top2 = np.sort(want, axis=1)[:, -2:]
+    near = (top2[:, 1] - top2[:, 0]) < 2e-2
+    return {"rows": rows, "position": pos, "max_abs": float(np.abs(full - want).max()),
+            "argmax_equal": int((am_n == am_1).sum()), "near_ties": int(near.sum()),
+            "ok": bool(np.abs(full - want).max() <= 2e-2 and ((am_n == am_1) | near).all())}
+
+
+def config4_measure(torch, rank, world, local, quant, steps, warmup, parity=False):
+    """Benchmark configuration 4: 64 sequences decoded together with a
+    4096-position KV cache, tensor-parallel over the job's GPUs (tp = N:
+    heads, gate/up rows and vocabulary split, all-reduce after o/down inside
+    the decode graph).  A step = one decode step of all 64 rows; positions
+    start at 4096 - steps - warmup so the last step attends over 4095
+    positions.  Collective over the job's ranks; returns the result dict on
+    rank 0 (None elsewhere)."""
     from nnzap_b200 import Model, config_from_dims, synth, tp_unique_id
-    d = synth.BONSAI_1_7B_Q1 if args.quant == "q1" else synth.BONSAI_1_7B_Q4
+    d = synth.BONSAI_1_7B_Q1 if quant == "q1" else synth.BONSAI_1_7B_Q4
     t0 = time.perf_counter()
     W = synth.make_model(d, seed=0)
     uid = None
@@ -250,73 +307,77 @@ def run_config4(args):
         tp_rank=rank, tp_size=world)
     model = Model(cfg, device=local, tp_unique_id=uid)
     model.load_weights(synth.iter_named_tensors(W))
-    del W
     load_ms = (time.perf_counter() - t0) * 1000
+    par = tp_parity(torch, model, d, W, rank, world, local) if (parity and world > 1) else None
+    del W
     tok = np.random.default_rng(0).integers(0, d.vocab, C4_BATCH).astype(np.uint32)
-    p0 = C4_CTX - args.steps - args.warmup - 1
-    model.decode_steps(tok, np.full(C4_BATCH, p0, np.uint32), args.warmup)
-
-    def barrier():
-        torch.cuda.synchronize()
-        if world > 1:
-            torch.distributed.barrier()
-            torch.cuda.synchronize()
-
-    uuid = None
-    try:
-        uuid = str(torch.cuda.get_device_properties(local).uuid)
-        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
-    except Exception:
-        pass
-    clocks = ClockSampler(uuid)
+    p0 = C4_CTX - steps - warmup - 1
+    model.decode_steps(tok, np.full(C4_BATCH, p0, np.uint32), warmup)
+    clocks = ClockSampler(_gpu_uuid(torch, local))
     clocks.start()
-    barrier()
+    _barrier(torch, world)
     w0 = time.perf_counter()
-    out, ns = model.decode_steps(tok, np.full(C4_BATCH, p0 + args.warmup, np.uint32), args.steps,
-                                 timings=True)
+    out, ns = model.decode_steps(tok, np.full(C4_BATCH, p0 + warmup, np.uint32), steps, timings=True)
     wall = time.perf_counter() - w0
-    barrier()
+    _barrier(torch, world)
     clk = clocks.stop()
+    model.free()
     stats = torch.tensor([float(ns.sum()) / 1e9, wall], dtype=torch.float64, device="cuda")
     if world > 1:
         torch.distributed.all_reduce(stats, op=torch.distributed.ReduceOp.MAX)
     dev_s, wall_s = stats.tolist()
     if rank != 0:
-        if world > 1:
-            torch.distributed.barrier()
-        return
+        return None
     hbm, peak_kind = measured_peaks()
-    mean_ctx = p0 + args.warmup + (args.steps + 1) / 2
+    mean_ctx = p0 + warmup + (steps + 1) / 2
     per_param = (1 / 8 + 2 / d.gs) if d.quant == "q1" else (1 / 2 + 4 / d.gs)
     qd, kvd = d.n_q * d.head_dim, d.n_kv * d.head_dim
     wbytes = (d.layers * (d.hidden * (qd + 2 * kvd) + qd * d.hidden + 3 * d.hidden * d.inter)
               + d.vocab * d.hidden) * per_param
     kvbytes = C4_BATCH * d.layers * 2 * kvd * mean_ctx * 2
     step_bytes_gpu = (wbytes + kvbytes) / world
-    achieved = step_bytes_gpu / (dev_s / args.steps) / 1e9
+    achieved = step_bytes_gpu / (dev_s / steps) / 1e9
     per_step_launches = 1 + d.layers * 9 + 4 + (4 * d.layers + 1 if world > 1 else 0)
+    return {"quant": d.quant, "tp": world, "batch": C4_BATCH, "kv": C4_CTX, "steps": steps, "warmup": warmup,
+            "value": C4_BATCH * steps / dev_s, "unit": "tok/s", "ms_per_step": dev_s / steps * 1000,
+            "load_ms": load_ms, "wall_s": wall_s, "mean_ctx": mean_ctx,
+            "roofline": {"bound": "hbm", "kernel": "decode step (CUDA graph: attn_tc_kernel dominant)",
+                         "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "peak_kind": peak_kind, "traffic": None,
+                         "algorithmic_bytes_per_step_per_gpu": step_bytes_gpu},
+            "gpu_launches": per_step_launches * steps, "clocks": clk, "parity_vs_tp1": par,
+            "sample_tokens": out[-1][:8].tolist()}
+
+
+def run_config4(args):
+    """`--workload config4`: the configuration-4 measurement as the line itself."""
+    import torch
+    rank, world, local = rank_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    r = config4_measure(torch, rank, world, local, args.quant, args.steps, args.warmup, parity=True)
+    if rank != 0:
+        if world > 1:
+            torch.distributed.barrier()
+        return
     print(json.dumps({
-        "metric": "decode_tok_per_sec", "value": C4_BATCH * args.steps / dev_s, "unit": "tok/s",
+        "metric": "decode_tok_per_sec", "value": r["value"], "unit": "tok/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": dev_s / args.steps * 1000, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": f"{d.quant} weights; fp16 KV, f32 accumulate", "data": "synthetic",
-        "config": {"workload": f"config 4: batch {C4_BATCH}, KV {C4_CTX}, Bonsai-1.7B-shaped {d.quant} "
+        "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": f"{r['quant']} weights; fp16 KV, f32 accumulate", "data": "synthetic",
+        "config": {"workload": f"config 4: batch {C4_BATCH}, KV {C4_CTX}, Bonsai-1.7B-shaped {r['quant']} "
                                "random-init, greedy decode steps",
                    "model": "Qwen3-1.7B architecture (28 layers, vocab 151936)", "global_batch": C4_BATCH,
                    "seq_len": C4_CTX, "parallelism": f"tp{world}",
                    "l2": "inputs larger than L2: 30 GB of KV cache read per step",
                    "kv_contents": "zero-initialised cache (attention time does not depend on values)"},
-        "load_ms": load_ms,
-        "roofline": {"bound": "hbm", "kernel": "decode step (CUDA graph: attn_tc_kernel dominant)",
-                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": peak_kind, "traffic": None,
-                     "algorithmic_bytes_per_step_per_gpu": step_bytes_gpu},
-        "cpu_baseline": None,
-        "e2e": {"value": C4_BATCH * args.steps / wall_s, "unit": "tok/s (nnz_decode_steps wall time)",
-                "h2d_bytes_per_step": C4_BATCH * 8 / args.steps,
-                "d2h_bytes_per_step": C4_BATCH * 4},
-        "gpu_launches": per_step_launches * args.steps, "clocks": clk,
-        "sample_tokens": out[-1][:8].tolist()}), flush=True)
+        "load_ms": r["load_ms"], "roofline": r["roofline"], "cpu_baseline": None,
+        "e2e": {"value": C4_BATCH * args.steps / r["wall_s"], "unit": "tok/s (nnz_decode_steps wall time)",
+                "h2d_bytes_per_step": C4_BATCH * 8 / args.steps, "d2h_bytes_per_step": C4_BATCH * 4},
+        "gpu_launches": r["gpu_launches"], "clocks": r["clocks"], "parity_vs_tp1": r["parity_vs_tp1"],
+        "sample_tokens": r["sample_tokens"]}), flush=True)
     if world > 1:
         torch.distributed.barrier()
 
@@ -432,6 +493,8 @@ def main():
                          "decode at KV 4096, tensor-parallel over the N GPUs; tokenizer: host BPE "
                          "encode throughput")
     ap.add_argument("--quant", default="q1", choices=["q1", "q4"], help="config4 weights")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the benchmarked tokens")
+    ap.add_argument("--no-tp", action="store_true", help="skip the appended tensor-parallel config-4 run")
     args = ap.parse_args()
     if args.workload == "tokenizer":
         run_tokenizer(args)
@@ -491,6 +554,15 @@ def main():
     barrier()
     clk = clocks.stop()
 
+    # configuration 4 tensor parallel over the same GPUs (collective: every rank)
+    tp4 = None
+    if not args.no_tp:
+        tp4 = config4_measure(torch, rank, world, local, "q1", 8, 3, parity=True)
+        if world == 1:
+            q4 = config4_measure(torch, rank, world, local, "q4", 8, 3)
+            tp4 = {"q1": tp4, "q4_g64": q4}
+        else:
+            tp4 = {"q1": tp4} if rank == 0 else None
     stats = torch.tensor([decode_ns / 1e9, prefill_ns / 1e9, sum(walls)], dtype=torch.float64,
                          device="cuda")
     if world > 1:
@@ -512,6 +584,19 @@ def main():
     us_tok = dec_s / (GEN * args.steps) * 1e6
     achieved = bytes_tok / (us_tok * 1e-6) / 1e9
     q0_us, q0_gbs, q0_bytes = qmv_config0(torch)
+    parity = None
+    if not args.no_parity:
+        # the benchmarked run itself: every generated token against the oracle's
+        # teacher-forced logits over prompt + generated (ids identical unless the
+        # oracle has a near tie; the reference's own check is exact ids,
+        # nnmetal/examples/bonsai_golden.zig:304-357)
+        from oracle import qwen3_ref as R
+        R.set_dequant_cache(True)
+        t_par = time.perf_counter()
+        exact, worst, _ = R.greedy_check(oracle_cfg(d), W, prompt, tokens)
+        R.set_dequant_cache(False)
+        parity = {"checked_tokens": len(tokens), "exact": exact, "worst_gap": worst,
+                  "tolerance": 2e-2, "ok": worst <= 2e-2, "oracle_s": time.perf_counter() - t_par}
     cpu = None
     if not args.no_cpu_baseline:
         c = cpu_decode_sample(d, W)
@@ -531,17 +616,18 @@ def main():
                    "model": "Qwen3-1.7B architecture (28 layers, vocab 151936)", "global_batch": world,
                    "seq_len": PROMPT + GEN, "parallelism": f"replicas x{world}",
                    "l2": "inputs larger than L2: 242 MB of weights streamed per token"},
-        "prefill_tok_per_sec": prefill_tps, "decode_p50_us": p50, "decode_p99_us": p99,
+        "decode_tok_per_sec": GEN * args.steps / dec_s, "prefill_tok_per_sec": prefill_tps,
+        "decode_p50_us": p50, "decode_p99_us": p99,
         "load_ms": load_ms, "prompt_tokens": PROMPT, "measured_tokens": GEN * args.steps,
         "roofline": {"bound": "hbm",
                      "kernel": ("decode step: CUDA graph" if os.environ.get("NNZ_DECODE_PATH") == "graph"
-                                else "decode step: persistent cooperative kernel mega_kernel"),
+                                else "decode step: single-row cooperative kernel d1_kernel"),
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": peak_kind,
-                     # ncu dram__bytes of one persistent decode launch at ctx 66
-                     # (profiles/decode_persistent_bonsai_q1.md), scaled to the
-                     # mean context by the KV bytes it adds
-                     "traffic": 260e6 + d.layers * 2 * d.n_kv * (mean_ctx - 66) * d.head_dim * 2,
+                     # DRAM bytes (read + write) of one single-token decode launch
+                     # measured by ncu at context TRAFFIC_CTX, moved to the mean
+                     # context by the K/V bytes a position adds
+                     "traffic": TRAFFIC_BYTES + d.layers * 2 * d.n_kv * (mean_ctx - TRAFFIC_CTX) * d.head_dim * 2,
                      "algorithmic_bytes_per_token": bytes_tok},
         "qmv_config0": {"us": q0_us, "achieved_gbs": q0_gbs, "frac": q0_gbs / hbm,
                         "algorithmic_bytes": q0_bytes},
@@ -552,6 +638,8 @@ def main():
         "gpu_launches": launches_per_step(d, PROMPT, GEN) * args.steps,
         "clocks": clk,
         "sample_tokens": tokens[:8],
+        "parity": parity,
+        "tp_config4": tp4,
     }
     print(json.dumps(out), flush=True)
     if world > 1:

@@ -1,5 +1,6 @@
-"""Kernel-level timing drivers (the commands the ncu summaries in profiles/
-were taken with).  Each prints one line of CUDA-event timings.
+"""Kernel-level timing drivers: each runs one kernel family on a small,
+seeded case and prints one line of CUDA-event timings (small enough to
+capture a single launch under a profiler).
 
   python -m nnzap_b200.microbench attn --rows 16 --ctx 4032
       tensor-core decode attention (nnz_attn_decode) over a random fp16 KV

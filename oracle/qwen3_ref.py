@@ -290,9 +290,27 @@ def _to_f16(cfg: Cfg, y: np.ndarray) -> np.ndarray:
     return _round_out(cfg, y).astype(F16).astype(F32)
 
 
+_DQ_CACHE = None
+
+
+def set_dequant_cache(on: bool) -> None:
+    """Keep every dequantized matrix (f32) after its first use, so repeated
+    decode steps stop re-expanding the packed weights (the timed CPU baseline
+    and the parity checks of long runs; ~7 GB for the 1.7B model)."""
+    global _DQ_CACHE
+    _DQ_CACHE = {} if on else None
+
+
 def qmv(cfg: Cfg, t: dict, M: int, K: int, x: np.ndarray, row_chunk: int = 8192) -> np.ndarray:
     """y[T, M] = x[T, K] @ W^T with f32 accumulation; W dequantized exactly."""
     x = x.astype(np.float32)
+    if _DQ_CACHE is not None:
+        key = (id(t["weight"]), M, K)
+        hit = _DQ_CACHE.get(key)
+        if hit is None:
+            hit = (t["weight"], dequant_tensor(cfg, t, M, K))   # the array ref keeps the id valid
+            _DQ_CACHE[key] = hit
+        return x @ hit[1].T
     if M <= row_chunk:
         return x @ dequant_tensor(cfg, t, M, K).T
     out = np.empty((x.shape[0], M), dtype=np.float32)
