@@ -644,6 +644,7 @@ def main():
     print(json.dumps(out), flush=True)
     if world > 1:
         torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
 
 
 if __name__ == "__main__":

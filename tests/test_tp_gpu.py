@@ -1,10 +1,10 @@
-"""Tensor-parallel decode on 2 GPUs (one process per GPU, NCCL inside the
-decode graph) against the single-device oracle.
+"""Tensor-parallel decode on 2, 4 and 8 GPUs (one process per GPU, the
+reduction inside the decode graph) against the single-device oracle.
 
-Each rank holds half the heads / intermediate rows and half the
+Each rank holds 1/tp of the heads / intermediate rows and of the
 vocabulary; argmax ids must be the oracle's (teacher-forced, near ties
 excepted) and each rank's logits shard must match the oracle's slice within
-2e-2.  Skipped with fewer than 2 GPUs.
+2e-2.  Skipped when the box has fewer GPUs than the case needs.
 """
 import numpy as np
 import pytest
@@ -16,9 +16,12 @@ pytestmark = pytest.mark.gpu
 
 DIMS = synth.ModelDims(vocab=1000, hidden=256, inter=768, layers=2, n_q=4, n_kv=2,
                        head_dim=128, gs=128, quant="q1")
+# 8 kv heads (the Bonsai layout): splits whole kv heads up to tp = 8
+DIMS8 = synth.ModelDims(vocab=1024, hidden=512, inter=1024, layers=2, n_q=16, n_kv=8,
+                        head_dim=128, gs=128, quant="q1")
 
 
-def _rank(rank, world, uid, q, rows):
+def _rank(rank, world, uid, q, rows, DIMS):
     from nnzap_b200 import GenerateOpts, Model, config_from_dims, generate
     W = synth.make_model(DIMS, seed=5)
     cfg = config_from_dims(DIMS, max_context_length=64, max_batch=max(rows, 1)).replace(
@@ -33,21 +36,22 @@ def _rank(rank, world, uid, q, rows):
     m.free()
 
 
-@pytest.mark.parametrize("rows", [3, 20])
-def test_tp2_decode_matches_oracle(cuda, built_lib, rows):
+@pytest.mark.parametrize("world,rows", [(2, 3), (2, 20), (4, 20), (8, 20)])
+def test_tp_decode_matches_oracle(cuda, built_lib, world, rows):
     torch = cuda
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    DIMS = DIMS8 if world > 2 else globals()["DIMS"]
     import torch.multiprocessing as mp
     from nnzap_b200 import tp_unique_id
     uid = tp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, uid, q, rows)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, world, uid, q, rows, DIMS)) for r in range(world)]
     for p in procs:
         p.start()
     out = {}
-    for _ in range(2):
+    for _ in range(world):
         r, *vals = q.get(timeout=300)
         out[r] = vals
     for p in procs:
@@ -58,14 +62,14 @@ def test_tp2_decode_matches_oracle(cuda, built_lib, rows):
                 n_q=DIMS.n_q, n_kv=DIMS.n_kv, head_dim=DIMS.head_dim, gs=DIMS.gs, quant="q1",
                 rope_theta=DIMS.rope_theta, eps=DIMS.eps)
     toks, am, _, am2, _, gen = out[0]
-    per = DIMS.vocab // 2
-    for r in range(2):   # every rank reports the same global argmax ids
+    per = DIMS.vocab // world
+    for r in range(world):   # every rank reports the same global argmax ids
         np.testing.assert_array_equal(out[r][1], am)
         np.testing.assert_array_equal(out[r][3], am2)
     for b in range(0, rows, 7):
         want = R.forward_tokens(cfg, W, [int(toks[b]), int(am[b])])
         for step, lgi, amv in ((0, 2, am), (1, 4, am2)):
-            for r in range(2):
+            for r in range(world):
                 np.testing.assert_allclose(out[r][lgi][b], want[step][r * per:(r + 1) * per], atol=2e-2,
                                            rtol=0)
             row = want[step]
