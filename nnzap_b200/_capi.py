@@ -68,7 +68,7 @@ class NnzGenerateResult(C.Structure):
 
 # (name, restype, argtypes) for every exported symbol of include/nnz_b200.h
 P, U32, I32, SZ, F32 = C.c_void_p, C.c_uint32, C.c_int, C.c_size_t, C.c_float
-DEBUG_SIGNATURES = [("nnz_debug_gemm_profile", I32, [P]), ("nnz_debug_decode1_profile", I32, [P, P, U32]), ("nnz_debug_decode_path", I32, [P])]
+DEBUG_SIGNATURES = [("nnz_debug_gemm_profile", I32, [P]), ("nnz_debug_decode1_profile", I32, [P, P, U32]), ("nnz_debug_decode_path", I32, [P]), ("nnz_debug_tp_wait_timeout", I32, [U32, P])]
 SIGNATURES = [
     ("nnz_last_error", C.c_char_p, []),
     ("nnz_version", I32, []),
@@ -134,7 +134,7 @@ def lib() -> C.CDLL:
                 f"{LIB_PATH} is missing: build it with `python -m nnzap_b200.build` "
                 "(no CPU fallback exists)")
         L = C.CDLL(str(LIB_PATH))
-        for name, res, args in SIGNATURES:
+        for name, res, args in SIGNATURES + DEBUG_SIGNATURES:
             fn = getattr(L, name)
             fn.restype = res
             fn.argtypes = args

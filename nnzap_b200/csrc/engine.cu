@@ -1867,6 +1867,53 @@ int nnz_debug_gemm_profile(uint64_t* out) {
   return NNZ_OK;
 }
 
+// Development aid (not part of the documented ABI), for the failure tests:
+// the peer-memory all-reduce kernel on the current device as rank 0 of a
+// 2-rank group whose "peer" is a local stand-in that never arrives, with a
+// wait limit of `spin_limit` polls.  The bounded wait must give up: returns
+// NNZ_ETIMEDOUT with the raised device flags in *flags_out, and the CUDA
+// context stays usable.  Nothing waits on another GPU.
+int nnz_debug_tp_wait_timeout(uint32_t spin_limit, int* flags_out) {
+  if (!flags_out) return fail(NNZ_EINVAL, "null argument");
+  return host_guard([&]() -> int {
+    const size_t n = 4096;
+    const size_t nflag = tp_allreduce_flag_words(n, 2);
+    float *res = nullptr, *part = nullptr, *slots = nullptr;
+    uint32_t* flags = nullptr;
+    int* err = nullptr;
+    void* tabs = nullptr;
+    auto cleanup = [&] {
+      cudaFree(res); cudaFree(part); cudaFree(slots); cudaFree(flags); cudaFree(err); cudaFree(tabs);
+    };
+    if (cudaMalloc(&res, n * 4) || cudaMalloc(&part, n * 4) || cudaMalloc(&slots, 2 * 2 * n * 4) ||
+        cudaMalloc(&flags, 2 * nflag * 4) || cudaMalloc(&err, 4) || cudaMalloc(&tabs, 4 * sizeof(void*))) {
+      cudaGetLastError();
+      cleanup();
+      return fail(NNZ_ENOMEM, "nnz_debug_tp_wait_timeout: allocation failed");
+    }
+    cudaMemset(res, 0, n * 4);
+    cudaMemset(part, 0, n * 4);
+    cudaMemset(flags, 0, 2 * nflag * 4);
+    cudaMemset(err, 0, 4);
+    // slot arrays and flag arrays of "GPU 0" (this one) and the stand-in "GPU 1"
+    float* slot_tab[2] = {slots, slots + 2 * n};
+    uint32_t* flag_tab[2] = {flags, flags + nflag};
+    cudaMemcpy(tabs, slot_tab, sizeof(slot_tab), cudaMemcpyHostToDevice);
+    cudaMemcpy(static_cast<char*>(tabs) + sizeof(slot_tab), flag_tab, sizeof(flag_tab), cudaMemcpyHostToDevice);
+    cudaError_t e = tp_allreduce_launch(res, part, static_cast<float* const*>(tabs), flags,
+                                        reinterpret_cast<uint32_t* const*>(static_cast<char*>(tabs) + sizeof(slot_tab)),
+                                        n, 0, 2, err, nullptr, spin_limit);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    int flags_host = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&flags_host, err, 4, cudaMemcpyDeviceToHost);
+    cleanup();
+    if (e != cudaSuccess) return fail(NNZ_ECUDA, std::string("nnz_debug_tp_wait_timeout: ") + cudaGetErrorString(e));
+    *flags_out = flags_host;
+    if (flags_host & (ERR_SPIN_TIMEOUT | ERR_MBAR_TIMEOUT)) return fail(NNZ_ETIMEDOUT, err_text(flags_host));
+    return NNZ_OK;
+  });
+}
+
 // Development aid (not part of the documented ABI): which kernel runs a
 // batch-1 decode step: 1 = single-row kernel (decode1.cu), 2 = persistent
 // multi-row kernel (mega.cu), 0 = captured multi-kernel graph.

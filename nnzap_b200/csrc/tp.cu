@@ -49,7 +49,7 @@ constexpr size_t kArSlice = kArThreads * 8;   // floats per CTA (two float4 per 
 __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(float* residual, float* part,
                                                                   float* const* peer_slots, uint32_t* flags,
                                                                   uint32_t* const* peer_flags, size_t n, int rank,
-                                                                  int T, int* err) {
+                                                                  int T, int* err, uint32_t spin_limit) {
   const size_t c = blockIdx.x, base = c * kArSlice;
   const size_t stride = (size_t)(T + 1);
   float4 v[2];
@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(float* residua
       for (;;) {
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(flags + c * stride + j) : "memory");
         if ((int)(f - cnt) >= 0) break;
-        if (++it > kTpSpinLimit) {
+        if (++it > spin_limit) {
           atomicOr(err, ERR_SPIN_TIMEOUT);
           break;
         }
@@ -124,10 +124,11 @@ size_t tp_allreduce_flag_words(size_t n_max, int T) {
 
 cudaError_t tp_allreduce_launch(float* residual, float* part, float* const* peer_slots, uint32_t* flags,
                                 uint32_t* const* peer_flags, size_t n, int rank, int T, int* err,
-                                cudaStream_t st) {
+                                cudaStream_t st, uint32_t spin_limit) {
   if (n % 4) return cudaErrorInvalidValue;
   const unsigned grid = (unsigned)((n + kArSlice - 1) / kArSlice);
-  tp_allreduce_kernel<<<grid, kArThreads, 0, st>>>(residual, part, peer_slots, flags, peer_flags, n, rank, T, err);
+  tp_allreduce_kernel<<<grid, kArThreads, 0, st>>>(residual, part, peer_slots, flags, peer_flags, n, rank, T, err,
+                                                   spin_limit ? spin_limit : kTpSpinLimit);
   return cudaGetLastError();
 }
 

@@ -49,9 +49,10 @@ cudaError_t argmax_shift_launch(unsigned long long* argmax, uint32_t rows, uint3
 // into this process (entry `rank` = this GPU's own).  Flags are
 // [nslice][T + 1] u32: arrival counts per source, then this GPU's own call
 // count for the slice.
+// spin_limit: polls of a peer flag before giving up (0 = the library default).
 cudaError_t tp_allreduce_launch(float* residual, float* part, float* const* peer_slots,
                                 uint32_t* flags, uint32_t* const* peer_flags, size_t n, int rank, int T,
-                                int* err, cudaStream_t st);
+                                int* err, cudaStream_t st, uint32_t spin_limit = 0);
 // Flag words tp_allreduce_launch needs for n floats at T ranks.
 size_t tp_allreduce_flag_words(size_t n_max, int T);
 
