@@ -29,6 +29,7 @@
 #include "misc.cuh"
 #include "packing.h"
 #include "qmv.cuh"
+#include "qmvf.cuh"
 #include "tp.cuh"
 
 using namespace nnz;
@@ -138,6 +139,7 @@ int prepare_device(int dev) {
   std::lock_guard<std::mutex> lk(mu);
   if (g_prepared[dev]) return NNZ_OK;
   NNZ_CK(qmv_prepare());
+  NNZ_CK(qmvf_prepare());
   NNZ_CK(attn_prepare());
   g_prepared[dev] = true;
   return NNZ_OK;
@@ -1697,6 +1699,14 @@ static int qmv_common(int fmt, int scale_dtype, int bf16_round, const void* pack
   if (qmv_ws_floats(M, K, gs, fmt, 1, batch, w->num_sms) > w->ws_floats ||
       (size_t)((batch + 7) / 8) * num_tiles(M) > w->n_counters)
     return fail(NNZ_EINVAL, "qmv: problem too large for the shared workspace");
+  if (pro == PRO_F16 && !logits && !am && qmvf_applies(fmt, M, K, gs, batch, epi, w->num_sms)) {
+    // one activation row: the cluster kernel (no workspace, no split-K pass)
+    QmvfArgs f{};
+    f.w = (const uint8_t*)packed; f.M = M; f.K = K; f.gs = gs; f.x = (const __half*)x; f.out = out;
+    f.epi = epi; f.bf16_round = (fmt == NNZ_Q4 && bf16_round) ? 1u : 0u; f.err = w->err;
+    NNZ_CK(qmvf_launch(fmt, fmt == NNZ_Q4 && scale_dtype == NNZ_SCALE_BF16, f, w->num_sms, (cudaStream_t)stream));
+    return NNZ_OK;
+  }
   QmvLaunch L{fmt, 1, pro, epi, fmt == NNZ_Q4 && scale_dtype == NNZ_SCALE_BF16, 0};
   QmvArgs a{};
   a.w = (const uint8_t*)packed; a.M = M; a.K = K; a.gs = gs;
