@@ -11,6 +11,14 @@ capture a single launch under a profiler).
       full Bonsai-1.7B-shaped Q1 model: prompt prefill through nnz_prefill
   python -m nnzap_b200.microbench decode --batch 64 --ctx 256 --steps 2
       full model: batched greedy decode steps (nnz_decode_steps)
+  python -m nnzap_b200.microbench decode1 --ctx 512 --steps 4
+      full model: single-row decode launches (one token each) after a prefill
+  python -m nnzap_b200.microbench qmv
+      BASELINE configuration 0 (Q4 6144x2048 g64 matvec, fp16 in/out)
+  python -m nnzap_b200.microbench attn --hd 64 --heads 8 --kv-heads 2
+      CUDA-core decode attention (head_dim 64)
+  python -m nnzap_b200.microbench sample --rows 4
+      top-k / top-p sampling over the full vocabulary
 """
 from __future__ import annotations
 
@@ -26,7 +34,7 @@ def _events(torch):
 def attn(args):
     import torch
     from ._capi import check, lib
-    n_q, n_kv, hd, max_ctx = 16, 8, 128, 4096
+    n_q, n_kv, hd, max_ctx = args.heads, args.kv_heads, args.hd, 4096
     rows, ctx = args.rows, args.ctx
     L = lib()
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -114,11 +122,63 @@ def decode(args):
     print(f"decode batch {args.batch} ctx {args.ctx}: per-step ms {np.round(ns / 1e6, 3).tolist()}")
 
 
+def decode1(args):
+    d, m = _model(1, args.ctx + args.steps + 8)
+    prompt = np.random.default_rng(0).integers(0, d.vocab, args.ctx)
+    nxt, _ = m.prefill(prompt)
+    import time
+    ts = []
+    for i in range(args.steps):
+        t0 = time.perf_counter()
+        am, _ = m.forward_decode([nxt], [args.ctx + i])
+        ts.append(time.perf_counter() - t0)
+        nxt = int(am[0])
+    print(f"single-row decode at ctx {args.ctx}: host ms per token {np.round(np.array(ts) * 1e3, 3).tolist()}")
+
+
+def qmv(args):
+    import torch
+    from . import synth
+    from ._capi import check, lib, ptr
+    M, K, gs = 6144, 2048, 64
+    L = lib()
+    t = synth.rand_q4(np.random.default_rng(0), M, K, gs)
+    packed = np.zeros(L.nnz_packed_bytes(1, M, K, gs, 1), dtype=np.uint8)
+    check(L.nnz_pack_weights(1, ptr(t["weight"]), ptr(t["scales"]), ptr(t["biases"]), M, K, gs, 1, 0,
+                             ptr(packed)))
+    w = torch.from_numpy(packed).cuda()
+    x = torch.randn(K, device="cuda").half()
+    y = torch.empty(M, device="cuda", dtype=torch.float16)
+    st = torch.cuda.current_stream().cuda_stream
+    for _ in range(args.iters):
+        check(L.nnz_qmv(1, 0, 0, w.data_ptr(), M, K, gs, ptr(x), K, 1, ptr(y), M, 0, st))
+    torch.cuda.synchronize()
+    print(f"qmv config 0: {args.iters} calls done")
+
+
+def sample(args):
+    import torch
+    from ._capi import check, lib
+    V = 151936
+    g = torch.Generator(device="cuda").manual_seed(0)
+    lg = torch.randn(args.rows, V, device="cuda", generator=g) * 3
+    u = torch.rand(args.rows, device="cuda", generator=g)
+    out = torch.empty(args.rows, dtype=torch.int32, device="cuda")
+    for _ in range(args.iters):
+        check(lib().nnz_sample(lg.data_ptr(), args.rows, V, V, 0.8, 40, 0.9, u.data_ptr(), out.data_ptr(),
+                               torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    print(f"sample rows {args.rows}: tokens {out.tolist()}")
+
+
 def main():
     ap = argparse.ArgumentParser(prog="python -m nnzap_b200.microbench")
     sub = ap.add_subparsers(dest="cmd", required=True)
     p = sub.add_parser("attn")
     p.add_argument("--rows", type=int, default=16)
+    p.add_argument("--hd", type=int, default=128)
+    p.add_argument("--heads", type=int, default=16)
+    p.add_argument("--kv-heads", type=int, default=8)
     p.add_argument("--ctx", type=int, default=4032)
     p.add_argument("--iters", type=int, default=20)
     p = sub.add_parser("gemm")
@@ -133,8 +193,17 @@ def main():
     p.add_argument("--batch", type=int, default=64)
     p.add_argument("--ctx", type=int, default=256)
     p.add_argument("--steps", type=int, default=2)
+    p = sub.add_parser("decode1")
+    p.add_argument("--ctx", type=int, default=512)
+    p.add_argument("--steps", type=int, default=4)
+    p = sub.add_parser("qmv")
+    p.add_argument("--iters", type=int, default=20)
+    p = sub.add_parser("sample")
+    p.add_argument("--rows", type=int, default=4)
+    p.add_argument("--iters", type=int, default=3)
     args = ap.parse_args()
-    {"attn": attn, "gemm": gemm, "prefill": prefill, "decode": decode}[args.cmd](args)
+    {"attn": attn, "gemm": gemm, "prefill": prefill, "decode": decode, "decode1": decode1, "qmv": qmv,
+     "sample": sample}[args.cmd](args)
 
 
 if __name__ == "__main__":
