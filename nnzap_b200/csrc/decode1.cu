@@ -146,6 +146,7 @@ struct Ctx {
   unsigned long long* pf;        // profiling: non-null on the one thread that records stamps
   bool probe;                    // profiling: layer 1 of the first token
   uint32_t nbar;                 // profiling: grid barriers seen while probing
+  unsigned long long* pf2;       // profiling: per-warp LM stamps (CTA 0, first token)
 };
 // Profiling stamp (NNZ_D1_PROFILE=1): thread 0 of CTA 0, layer 1 of the first token.
 #define D1_STAMP(c, i) do { if ((c).pf) (c).pf[i] = gtimer(); } while (0)
@@ -324,20 +325,6 @@ __device__ D1_SMALL void quant_group(const float (&x)[4], uint32_t gg, int lane,
 // One 16-row x 128-k unit: 4 int8 MMAs.  Lane's 8 bytes: word w covers MMAs
 // 2w, 2w+1; bit (s + 8i) of a word, s = 4 j' + r, is byte i of A register r
 // of MMA 2w + j'.
-// Accumulator digits -> scaled f32 row sums (lanes with lane % 4 == 0 hold rows
-// lane / 4 and lane / 4 + 8).  sum(sign * q) = 2 sum(bit * q) - sum(q), exact.
-__device__ __forceinline__ void unit_epi(const int (&acc)[4], float s0, float s1, int sq, float& y0, float& y1,
-                                         int lane) {
-  const int lo0 = __shfl_down_sync(kFull, acc[0], 1);
-  const int lo1 = __shfl_down_sync(kFull, acc[2], 1);
-  if ((lane & 3) == 0) {
-    const int v0 = acc[0] * 65536 + acc[1] * 256 + lo0;
-    const int v1 = acc[2] * 65536 + acc[3] * 256 + lo1;
-    y0 = fmaf(s0, (float)(2 * v0 - sq), y0);
-    y1 = fmaf(s1, (float)(2 * v1 - sq), y1);
-  }
-}
-
 // Row sums of 16 rows (lanes 4r hold rows r and r + 8) into lanes 0..3 as
 // float4 of rows 4q..4q+3, then one vector red.add per lane.
 __device__ __forceinline__ void red_rows16(float* dst, float y0, float y1, int lane) {
@@ -352,71 +339,130 @@ __device__ __forceinline__ void red_rows16(float* dst, float y0, float y1, int l
   if (lane < 4) red_add_v4(dst + 4 * lane, v[0], v[1], v[2], v[3]);
 }
 
-// The one matvec loop of the kernel (kept out of line: every phase shares
-// this copy of the instructions).  Units (row block rbl, group gg) of a
+// Per-lane digit weights of the accumulator columns: lane t = 0 holds the
+// (hi, mid) columns, lane t = 1 the lo column, lanes 2 and 3 zero columns.
+// Each lane folds its columns to 2 * (column value) in f32 (minus sum(q)
+// on lane 0), so sum over the lane pair (t = 0, 1) of a unit's terms is
+// 2 * sum(bit * q) - sum(q) = sum(sign * q): the group dot product.  The
+// pair is added once per row block instead of two shuffles per unit.
+struct DigitW {
+  float w0, w1, sqs;
+};
+// Exact int -> f32 for |i| < 2^22 with two full-rate instructions (the
+// conversion unit runs at a quarter of the ALU rate): the integer is placed
+// in the mantissa of 1.5 * 2^23, whose value is then subtracted.  The MMA
+// column sums of one unit are below 2^15 in magnitude.
+__device__ __forceinline__ float i2f_small(int i) {
+  return __int_as_float(0x4B400000 + i) - 12582912.0f;
+}
+
+__device__ __forceinline__ DigitW digit_w(int lane) {
+  const int t = lane & 3;
+  DigitW d;
+  d.w0 = t == 0 ? 131072.f : t == 1 ? 2.f : 0.f;
+  d.w1 = t == 0 ? 512.f : 0.f;
+  d.sqs = t == 0 ? 1.f : 0.f;
+  return d;
+}
+
+// One unit: 4 int8 MMAs, then this lane's f32 share of the two rows
+// (rows lane / 4 and lane / 4 + 8) added into y0, y1.
+__device__ __forceinline__ void unit_acc(const uint8_t* unit, uint2 wb, const uint2 (&bq)[4], float ef, int sq,
+                                         const DigitW& dw, int r0, float& y0, float& y1) {
+  int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t W = (j < 2) ? wb.x : wb.y;
+    const int sh = (j & 1) * 4;
+    mma_u8s8(acc, (W >> sh) & 0x01010101u, (W >> (sh + 1)) & 0x01010101u, (W >> (sh + 2)) & 0x01010101u,
+             (W >> (sh + 3)) & 0x01010101u, bq[j].x, bq[j].y);
+  }
+  // scales of rows r0 and r0 + 8 packed in one word (see put_unit)
+  const float2 sf = __half22float2(*reinterpret_cast<const __half2*>(unit + 256 + r0 * 4));
+  const float nsq = -(float)sq * dw.sqs;
+  y0 = fmaf(sf.x * ef, fmaf(i2f_small(acc[0]), dw.w0, fmaf(i2f_small(acc[1]), dw.w1, nsq)), y0);
+  y1 = fmaf(sf.y * ef, fmaf(i2f_small(acc[2]), dw.w0, fmaf(i2f_small(acc[3]), dw.w1, nsq)), y1);
+}
+
+__device__ __forceinline__ void load_b(const uint8_t* sm, uint32_t gg, int lane, uint2 (&bq)[4]) {
+  const uint2* xb = reinterpret_cast<const uint2*>(sm + OFF_XB) + gg * 48;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) bq[j] = lane < 12 ? xb[j * 12 + lane] : make_uint2(0u, 0u);
+}
+
+// Address of chunk K in the ring, after waiting for it to have landed (no
+// release: the phase releases its chunks when it ends).
+__device__ __forceinline__ const uint8_t* ring_peek(Ctx& c, uint32_t K) {
+  if (!c.failed) c.failed = !wait_mbar(fullb(c.sm, K % kD1Slots), (K / kD1Slots) & 1u, *c.a);
+  return c.sm + OFF_RING + (K % kD1Slots) * kD1Chunk;
+}
+
+// The matvec loop of every phase.  Units (row block rbl, group gg) of a
 // phase start at ring chunk Kb, unit index rbl * GH + gg.
 //   mode 0: group split -- warp w takes groups w, w + 16, ... of every row
-//           block and writes its partial row sums to part[w][rbl] (every
-//           entry written, zero when the warp had no group);
+//           block (all of the phase's chunks are resident: a phase uses at
+//           most 3) and writes its partial row sums to part[w][rbl];
 //   mode 1: row split -- warp w takes row blocks w, w + 16, ... whole and
 //           red.adds the rows into dst[(rb_base + rbl) * 16 ..];
 //   mode 2: row split LM head -- f32 logits (dst, optional) and the packed
 //           first-max argmax of rows < V, returned.
 __device__ D1_MV unsigned long long mv_units(Ctx& c, uint32_t Kb, uint32_t nrb, uint32_t GH, int mode,
-                                                    float* dst, uint32_t rb_base, uint32_t V) {
+                                             float* dst, uint32_t rb_base, uint32_t V) {
   const int lane = c.lane, r0 = lane >> 2;
-  const uint2* xb = reinterpret_cast<const uint2*>(c.sm + OFF_XB);
   const float* gef = reinterpret_cast<const float*>(c.sm + OFF_GEF);
   const int* gsq = reinterpret_cast<const int*>(c.sm + OFF_GSQ);
-  float* part = reinterpret_cast<float*>(c.sm + OFF_PART) + c.warp * kD1MaxRb * 16;
-  const bool rows = mode != 0;
-  const uint32_t rstart = rows ? c.warp : 0, rstep = rows ? kD1Warps : 1;
-  const uint32_t gstart = rows ? 0 : c.warp, gstep = rows ? 1 : kD1Warps;
+  const DigitW dw = digit_w(lane);
   unsigned long long best = 0ull;
-  uint32_t curk = 0xffffffffu, curg = 0xffffffffu;
-  const uint8_t* ch = nullptr;
-  uint2 bq[4] = {};
-  float ef = 0.f;
-  int sq = 0;
-  if (mode == 0) D1_STAMP(c, 52);
-  for (uint32_t rbl = rstart; rbl < nrb; rbl += rstep) {
-    float y0 = 0.f, y1 = 0.f;
-    for (uint32_t gg = gstart; gg < GH; gg += gstep) {
-      const uint32_t u = rbl * GH + gg;
-      if (Kb + (u >> 5) != curk) {
-        curk = Kb + (u >> 5);
-        ch = ring_get(c, curk);
+  if (mode == 0) {
+    float* part = reinterpret_cast<float*>(c.sm + OFF_PART) + c.warp * kD1MaxRb * 16;
+    const uint32_t nch = (nrb * GH + 31) / 32;
+    for (uint32_t k = 0; k < nch; ++k) ring_peek(c, Kb + k);
+    uint32_t curg = 0xffffffffu;
+    uint2 bq[4] = {};
+    float ef = 0.f;
+    int sq = 0;
+    for (uint32_t rbl = 0; rbl < nrb; ++rbl) {
+      float y0 = 0.f, y1 = 0.f;
+      for (uint32_t gg = c.warp; gg < GH; gg += kD1Warps) {
+        if (gg != curg) {   // once per phase when the group count divides 16
+          curg = gg;
+          load_b(c.sm, gg, lane, bq);
+          ef = gef[gg];
+          sq = gsq[gg];
+        }
+        const uint32_t u = rbl * GH + gg;
+        const uint8_t* unit = c.sm + OFF_RING + ((Kb + (u >> 5)) % kD1Slots) * kD1Chunk + (u & 31u) * kD1Unit;
+        unit_acc(unit, *reinterpret_cast<const uint2*>(unit + lane * 8), bq, ef, sq, dw, r0, y0, y1);
       }
-      if (gg != curg) {
-        curg = gg;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) bq[j] = lane < 12 ? xb[gg * 48 + j * 12 + lane] : make_uint2(0u, 0u);
-        ef = gef[gg];
-        sq = gsq[gg];
-      }
-      if (mode == 0 && rbl == 0) D1_STAMP(c, 53);
-      const uint8_t* unit = ch + (u & 31u) * kD1Unit;
-      const uint2 wb = *reinterpret_cast<const uint2*>(unit + lane * 8);
-      int acc[4] = {0, 0, 0, 0};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t W = (j < 2) ? wb.x : wb.y;
-        const int sh = (j & 1) * 4;
-        mma_u8s8(acc, (W >> sh) & 0x01010101u, (W >> (sh + 1)) & 0x01010101u, (W >> (sh + 2)) & 0x01010101u,
-                 (W >> (sh + 3)) & 0x01010101u, bq[j].x, bq[j].y);
-      }
-      const uint32_t s01 = *reinterpret_cast<const uint16_t*>(unit + 256 + r0 * 2) |
-                           ((uint32_t)*reinterpret_cast<const uint16_t*>(unit + 256 + (r0 + 8) * 2) << 16);
-      const float2 sf = __half22float2(*reinterpret_cast<const __half2*>(&s01));
-      unit_epi(acc, sf.x * ef, sf.y * ef, sq, y0, y1, lane);
-    }
-    if (mode == 0) {
-      if (rbl == 0) D1_STAMP(c, 54);
+      y0 += __shfl_xor_sync(kFull, y0, 1);
+      y1 += __shfl_xor_sync(kFull, y1, 1);
       if ((lane & 3) == 0) {
         part[rbl * 16 + r0] = y0;
         part[rbl * 16 + r0 + 8] = y1;
       }
-    } else if (mode == 1) {
+    }
+    return 0ull;
+  }
+  // row split: the GH units of a row block are contiguous in one ring chunk
+  // (GH divides 32): one chunk lookup per row block, the next unit's weight
+  // word loaded while the current unit's MMAs run
+  for (uint32_t rbl = c.warp; rbl < nrb; rbl += kD1Warps) {
+    const uint32_t u0 = rbl * GH;
+    const uint8_t* base = ring_get(c, Kb + (u0 >> 5)) + (u0 & 31u) * kD1Unit;
+    float y0 = 0.f, y1 = 0.f;
+    uint2 wn = *reinterpret_cast<const uint2*>(base + lane * 8);
+#pragma unroll 2
+    for (uint32_t gg = 0; gg < GH; ++gg) {
+      const uint8_t* unit = base + gg * kD1Unit;
+      const uint2 wb = wn;
+      if (gg + 1 < GH) wn = *reinterpret_cast<const uint2*>(unit + kD1Unit + lane * 8);
+      uint2 bq[4];
+      load_b(c.sm, gg, lane, bq);
+      unit_acc(unit, wb, bq, gef[gg], gsq[gg], dw, r0, y0, y1);
+    }
+    y0 += __shfl_xor_sync(kFull, y0, 1);
+    y1 += __shfl_xor_sync(kFull, y1, 1);
+    if (mode == 1) {
       red_rows16(dst + (rb_base + rbl) * 16, y0, y1, lane);
     } else if ((lane & 3) == 0) {
       const uint32_t ra = (rb_base + rbl) * 16 + r0, rbb = ra + 8;
@@ -949,7 +995,9 @@ __device__ D1_PHASE void lm_phase(Ctx& c, uint32_t Kl) {
   if (rb1 > rb0) {
     norm_prologue(c, 2, g.L, 0, a.fnorm);
     D1_STAMP(c, 21);
+    if (c.pf2 && c.lane == 0) c.pf2[c.warp * 2] = gtimer();
     best = mv_units(c, Kl, rb1 - rb0, g.GH, 2, a.logits, rb0, g.V);
+    if (c.pf2 && c.lane == 0) c.pf2[c.warp * 2 + 1] = gtimer();
   }
   ring_release_upto(c, Kl + g.clm);
 #pragma unroll
@@ -1111,6 +1159,7 @@ __global__ void __launch_bounds__(kD1Threads, 1) d1_kernel(const __grid_constant
     grid_bar(c);
     if (stamps && t == 0) a.prof[6] = gtimer();
     c.pf = (stamps && t == 0) ? a.prof : nullptr;
+    c.pf2 = (a.prof && c.c == 0 && t == 0) ? a.prof + 64 + 8 * g.P : nullptr;
     lm_phase(c, Kt + g.L * g.cpl);
     if (stamps && t == 0) a.prof[7] = gtimer();
     c.pf = nullptr;
@@ -1164,9 +1213,10 @@ void put_unit(uint8_t* dst, const uint8_t* bits, const uint16_t* s, uint32_t M, 
       memcpy(dst + lane * 8 + w * 4, &W, 4);
     }
   }
+  // scales: word r (r < 8) = (row r, row r + 8), the two rows of lane 4 r
   for (uint32_t rr = 0; rr < 16; ++rr) {
     const uint16_t v = scale_at(s, M, K, row0 + rr, gg);
-    memcpy(dst + 256 + rr * 2, &v, 2);
+    memcpy(dst + 256 + (rr % 8) * 4 + (rr / 8) * 2, &v, 2);
   }
 }
 

@@ -1314,8 +1314,8 @@ static int model_finalize_impl(nnz_model* m) {
     if ((rc = dalloc(m, (void**)&a.tstamp, ((size_t)c.max_context_length + 1) * 8))) return rc;
     const char* prof = getenv("NNZ_D1_PROFILE");
     if (prof && prof[0] == '1') {
-      if ((rc = dalloc(m, (void**)&a.prof, (64 + 8 * (size_t)d1g.P) * 8))) return rc;
-      NNZ_CK(cudaMemset(a.prof, 0, (64 + 8 * (size_t)d1g.P) * 8));
+      if ((rc = dalloc(m, (void**)&a.prof, (64 + 8 * (size_t)d1g.P + 64) * 8))) return rc;
+      NNZ_CK(cudaMemset(a.prof, 0, (64 + 8 * (size_t)d1g.P + 64) * 8));
     }
   }
   NNZ_CK(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking));
@@ -1939,7 +1939,7 @@ int nnz_debug_decode_path(nnz_model* m) {
 int nnz_debug_decode1_profile(nnz_model* m, uint64_t* out, uint32_t n) {
   if (!m || !out || !m->d1_ok || !m->d1.prof) return fail(NNZ_ESTATE, "profiling not enabled");
   NNZ_CK(cudaStreamSynchronize(m->st));
-  NNZ_CK(cudaMemcpy(out, m->d1.prof, 8 * std::min<uint32_t>(n, 64 + 8 * m->d1.g.P), cudaMemcpyDeviceToHost));
+  NNZ_CK(cudaMemcpy(out, m->d1.prof, 8 * std::min<uint32_t>(n, 64 + 8 * m->d1.g.P + 64), cudaMemcpyDeviceToHost));
   return NNZ_OK;
 }
 
