@@ -9,9 +9,18 @@
 namespace nnz {
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kBK = 64, kStages = 4;
-constexpr uint32_t kTileBytes = kBM * kBK * 2;          // 16 KB per operand per stage
-constexpr uint32_t kTmemCols = 128;
+constexpr int kBM = 128, kBN = 128, kBK = 64;
+constexpr uint32_t kTileBytes = kBM * kBK * 2;          // 16 KB per operand tile per stage
+// MT 128-row M tiles per CTA share each dequantized weight tile: MT TMEM
+// accumulators of 128 columns; ring stages of MT activation tiles + one
+// weight tile, as many as fit (4 for MT <= 2, 2 for MT = 4).  (Per-tile
+// activation slots with their own barriers, committed after each tile's
+// MMAs, measured slower: 44 -> 69 us on a 512 x 2048 x 12288 GEMM.)
+template <int MT> struct GemmShape {
+  static constexpr int kStages = MT >= 4 ? 2 : 4;
+  static constexpr uint32_t kTmemCols = 128 * MT;
+  static constexpr uint32_t kSmemBytes = kStages * (MT + 1) * kTileBytes + 1024 + 256;
+};
 constexpr int kGroups = 2;        // dequantizing groups of 4 warps, K steps dealt round robin
 constexpr int kThreads = 128 + 128 * kGroups;
 constexpr int kProducerWarps = 4;   // full-barrier arrivals per stage: one per warp of the filling group
@@ -140,8 +149,8 @@ __device__ __forceinline__ void write_row(uint32_t stage, uint32_t r, const Raw&
                  : "memory");
 }
 
-// Warp roles (128 + 128 kGroups threads): warp 0 lane 0 streams X tiles
-// with TMA up to kStages ahead; warp 1 lane 0 issues the MMAs; the warps
+// Warp roles (128 + 128 kGroups threads): warp 0 lane 0 streams the MT
+// X tiles of each K step with TMA up to kStages ahead; warp 1 lane 0 issues the MMAs; the warps
 // from 4 on dequantize the weights into the B stages in kGroups groups of
 // four -- group g takes K steps g, g + kGroups, ..., one weight row per
 // thread, raw weights prefetched kPf of the group's steps ahead in
@@ -149,8 +158,10 @@ __device__ __forceinline__ void write_row(uint32_t stage, uint32_t r, const Raw&
 // others' dequantization.  Groups 0 and 1 (warps 4-11) run the epilogue
 // (TMEM lane quarter = warp % 4, the two groups taking alternate column
 // halves).
-// Split-K over gridDim.z is allowed only for the residual-add epilogue,
-// whose partial sums are accumulated with atomicAdd.
+// warp 1 issues the MT MMA chains of a K step back to back on the one
+// dequantized weight tile.
+// Split-K over gridDim.z (MT = 1 only) accumulates the residual-add
+// epilogue's partial sums with atomicAdd, the others' in the f32 accumulator.
 // Development aid: NNZ_GEMM_PROFILE=1 makes CTA (0,0,0) record clock64()
 // stamps of its pipeline (read back with nnz_debug_gemm_profile).
 __device__ unsigned long long g_gemm_prof[128];
@@ -158,20 +169,24 @@ __device__ __forceinline__ void gstamp(const GemmArgs& a, int i) {
   if (a.prof && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && i < 128) g_gemm_prof[i] = clock64();
 }
 
-template <int FMT>
+template <int FMT, int MT>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmX, GemmArgs a) {
+  constexpr int kStages = GemmShape<MT>::kStages;
+  constexpr uint32_t kTmemCols = GemmShape<MT>::kTmemCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* As = sm;
-  uint8_t* Bs = sm + kStages * kTileBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + 2 * kStages * kTileBytes);
+  uint8_t* As = sm;                                     // [stage][MT][16 KB]
+  uint8_t* Bs = sm + kStages * MT * kTileBytes;         // [stage][16 KB]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kStages * (MT + 1) * kTileBytes);
   uint64_t* empty = full + kStages;
   uint64_t* done = empty + kStages;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) gstamp(a, 0);
-  const uint32_t m0 = blockIdx.y * kBM;
+  const uint32_t m0 = blockIdx.y * kBM * MT;
+  // M tiles of this CTA inside the matrix (the TMA, MMAs and epilogue skip the rest)
+  const uint32_t nv = (a.M - m0 + kBM - 1) / kBM < (uint32_t)MT ? (a.M - m0 + kBM - 1) / kBM : (uint32_t)MT;
   const bool silu = a.epi == GEPI_SILU;
   const uint32_t ncols = silu ? kBN / 2 : kBN;           // output columns per tile
   const uint32_t n0 = blockIdx.x * ncols;
@@ -207,8 +222,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       for (uint32_t i = 0; i < nk; ++i) {
         const uint32_t s = i % kStages;
         if (i >= (uint32_t)kStages && !failed) failed = !mbar_wait(&empty[s], ((i / kStages) - 1) & 1u, a.err);
-        mbar_arrive_expect_tx(&full[s], kTileBytes);
-        tma_load_2d(As + s * kTileBytes, &tmX, (int)((ks0 + i) * kBK), (int)m0, &full[s]);
+        mbar_arrive_expect_tx(&full[s], nv * kTileBytes);
+        for (uint32_t mt = 0; mt < nv; ++mt)
+          tma_load_2d(As + (s * MT + mt) * kTileBytes, &tmX, (int)((ks0 + i) * kBK), (int)(m0 + mt * kBM), &full[s]);
       }
     }
   } else if (warp == 1) {
@@ -219,11 +235,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (!failed) failed = !mbar_wait(&full[s], (i / kStages) & 1u, a.err);
         if (i < 32) gstamp(a, 66 + (int)i);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint64_t da = smem_desc_sw128(As + s * kTileBytes);
         const uint64_t db = smem_desc_sw128(Bs + s * kTileBytes);
+        for (uint32_t mt = 0; mt < nv; ++mt) {
+          const uint64_t da = smem_desc_sw128(As + (s * MT + mt) * kTileBytes);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk)   // +32 B per 16-element K step inside the swizzle atom
-          umma_f16(tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (i | kk) != 0);
+          for (int kk = 0; kk < kBK / 16; ++kk)   // +32 B per 16-element K step inside the swizzle atom
+            umma_f16(tmem + mt * kBN, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (i | kk) != 0);
+        }
         umma_commit(&empty[s]);
       }
       umma_commit(done);
@@ -259,86 +277,89 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       }
     }
   }
-  // ---- epilogue (warps 4-11): TMEM lanes 32q..32q+31 = rows m0 + 32q + lane;
-  // warps 4-7 take column chunks 0-1, warps 8-11 chunks 2-3 ----
+  // ---- epilogue (warps 4-11), per M tile mt (TMEM columns 128 mt ..):
+  // TMEM lanes 32q..32q+31 = rows m0 + 128 mt + 32q + lane; warps 4-7 take
+  // column chunks 0-1, warps 8-11 chunks 2-3 ----
   if (warp >= 4 && warp < 12) {
     if (!failed) failed = !mbar_wait(done, 0, a.err);
     if (tid == 128) gstamp(a, 98);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const int q = warp & 3, part = (warp - 4) >> 2;
-    const uint32_t m = m0 + 32 * q + lane;
-    const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16);
     const bool rb = a.bf16r != 0;
-    if (gridDim.z > 1 && a.epi != GEPI_RESADD) {
-      // split K: f32 partials into the accumulator (gate | up halves for SILU)
-      for (int cc = 2 * part; cc < 2 * part + 2; ++cc) {
-        uint32_t v[32];
-        tmem_ld32(tbase + cc * 32, v);
-        if (m >= a.M) continue;
-        const uint32_t half = silu ? (uint32_t)(cc * 32) / (kBN / 2) : 0;
-        const uint32_t nb = n0 + (silu ? (uint32_t)(cc * 32) % (kBN / 2) : (uint32_t)(cc * 32));
-        float* o = a.acc + (size_t)m * (silu ? 2 * a.N : a.N) + half * a.N + nb;
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (nb + j < a.N) atomicAdd(&o[j], __uint_as_float(v[j]));
-      }
-    } else if (silu) {
-      for (int cc = part; cc < part + 1; ++cc) {
-        uint32_t g[32], u[32];
-        tmem_ld32(tbase + cc * 32, g);
-        tmem_ld32(tbase + 64 + cc * 32, u);
-        if (m < a.M) {
-          __half* o = static_cast<__half*>(a.out) + (size_t)m * a.ldo + n0 + cc * 32;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const uint32_t n = n0 + cc * 32 + j;
-            const float gv = __uint_as_float(g[j]), uv = __uint_as_float(u[j]);
-            float h = gv / (1.0f + expf(-gv)) * uv;
-            if (rb) h = bf16_trunc(h);
-            if (n < a.N) o[j] = __float2half_rn(h);
+    for (uint32_t mt = 0; mt < nv; ++mt) {
+      const uint32_t m = m0 + mt * kBM + 32 * q + lane;
+      const uint32_t tbase = tmem + mt * kBN + ((uint32_t)(32 * q) << 16);
+      if (gridDim.z > 1 && a.epi != GEPI_RESADD) {
+        // split K: f32 partials into the accumulator (gate | up halves for SILU)
+        for (int cc = 2 * part; cc < 2 * part + 2; ++cc) {
+          uint32_t v[32];
+          tmem_ld32(tbase + cc * 32, v);
+          if (m >= a.M) continue;
+          const uint32_t half = silu ? (uint32_t)(cc * 32) / (kBN / 2) : 0;
+          const uint32_t nb = n0 + (silu ? (uint32_t)(cc * 32) % (kBN / 2) : (uint32_t)(cc * 32));
+          float* o = a.acc + (size_t)m * (silu ? 2 * a.N : a.N) + half * a.N + nb;
+  #pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (nb + j < a.N) atomicAdd(&o[j], __uint_as_float(v[j]));
+        }
+      } else if (silu) {
+        for (int cc = part; cc < part + 1; ++cc) {
+          uint32_t g[32], u[32];
+          tmem_ld32(tbase + cc * 32, g);
+          tmem_ld32(tbase + 64 + cc * 32, u);
+          if (m < a.M) {
+            __half* o = static_cast<__half*>(a.out) + (size_t)m * a.ldo + n0 + cc * 32;
+  #pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const uint32_t n = n0 + cc * 32 + j;
+              const float gv = __uint_as_float(g[j]), uv = __uint_as_float(u[j]);
+              float h = gv / (1.0f + expf(-gv)) * uv;
+              if (rb) h = bf16_trunc(h);
+              if (n < a.N) o[j] = __float2half_rn(h);
+            }
           }
         }
-      }
-    } else {
-      for (int cc = 2 * part; cc < 2 * part + 2; ++cc) {
-        uint32_t v[32];
-        tmem_ld32(tbase + cc * 32, v);
-        if (m >= a.M) continue;
-        const uint32_t nb = n0 + cc * 32;
-        if (a.epi == GEPI_F16) {
-          __half* o = static_cast<__half*>(a.out) + (size_t)m * a.ldo + nb;
-          if (nb + 32 <= a.N && (a.ldo & 7) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0) {
-            // 16-byte stores
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              uint32_t pk[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                float x0 = __uint_as_float(v[j + 2 * e]), x1 = __uint_as_float(v[j + 2 * e + 1]);
-                if (rb) { x0 = bf16_trunc(x0); x1 = bf16_trunc(x1); }
-                const __half2 h2 = __floats2half2_rn(x0, x1);
-                pk[e] = *reinterpret_cast<const uint32_t*>(&h2);
+      } else {
+        for (int cc = 2 * part; cc < 2 * part + 2; ++cc) {
+          uint32_t v[32];
+          tmem_ld32(tbase + cc * 32, v);
+          if (m >= a.M) continue;
+          const uint32_t nb = n0 + cc * 32;
+          if (a.epi == GEPI_F16) {
+            __half* o = static_cast<__half*>(a.out) + (size_t)m * a.ldo + nb;
+            if (nb + 32 <= a.N && (a.ldo & 7) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0) {
+              // 16-byte stores
+  #pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                uint32_t pk[4];
+  #pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  float x0 = __uint_as_float(v[j + 2 * e]), x1 = __uint_as_float(v[j + 2 * e + 1]);
+                  if (rb) { x0 = bf16_trunc(x0); x1 = bf16_trunc(x1); }
+                  const __half2 h2 = __floats2half2_rn(x0, x1);
+                  pk[e] = *reinterpret_cast<const uint32_t*>(&h2);
+                }
+                *reinterpret_cast<uint4*>(o + j) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
               }
-              *reinterpret_cast<uint4*>(o + j) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            } else {
+  #pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                float x = __uint_as_float(v[j]);
+                if (rb) x = bf16_trunc(x);
+                if (nb + j < a.N) o[j] = __float2half_rn(x);
+              }
             }
           } else {
-#pragma unroll
+            float* o = static_cast<float*>(a.out) + (size_t)m * a.ldo + nb;
+  #pragma unroll
             for (int j = 0; j < 32; ++j) {
               float x = __uint_as_float(v[j]);
               if (rb) x = bf16_trunc(x);
-              if (nb + j < a.N) o[j] = __float2half_rn(x);
-            }
-          }
-        } else {
-          float* o = static_cast<float*>(a.out) + (size_t)m * a.ldo + nb;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float x = __uint_as_float(v[j]);
-            if (rb) x = bf16_trunc(x);
-            if (nb + j < a.N) {
-              if (a.epi == GEPI_F32) o[j] = x;
-              else if (gridDim.z > 1) atomicAdd(&o[j], x);
-              else o[j] += x;
+              if (nb + j < a.N) {
+                if (a.epi == GEPI_F32) o[j] = x;
+                else if (gridDim.z > 1) atomicAdd(&o[j], x);
+                else o[j] += x;
+              }
             }
           }
         }
@@ -444,7 +465,6 @@ EncodeFn get_encode() {
   return fn;
 }
 
-constexpr uint32_t kSmemBytes = 2 * kStages * kTileBytes + 1024 + 256;
 
 }  // namespace
 
@@ -487,16 +507,28 @@ cudaError_t gemm_launch(const GemmArgs& a_in, const __half* x, cudaStream_t st) 
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
   const uint32_t ncols = a.epi == GEPI_SILU ? kBN / 2 : kBN;
-  dim3 grid((a.N + ncols - 1) / ncols, (a.M + kBM - 1) / kBM);
+  int sms = 148, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // M tiles per CTA: the most that still gives at least 60 % of the SMs a
+  // CTA (each weight tile is dequantized once per CTA and its MMAs run back
+  // to back, so MT = 4 does a quarter of the dequantization of MT = 1 on a
+  // 512-row chunk; fewer CTAs than that lose more to idle SMs)
+  const uint32_t ntn = (a.N + ncols - 1) / ncols, ntm = (a.M + kBM - 1) / kBM;
+  static const int mt_max = [] {   // NNZ_GEMM_MT caps it (1, 2 or 4; for measurements)
+    const char* e = getenv("NNZ_GEMM_MT");
+    return e ? atoi(e) : 4;
+  }();
+  int mt = 1;
+  if (mt_max >= 4 && ntm >= 3 && ntn * ((ntm + 3) / 4) * 5 >= (uint32_t)sms * 3) mt = 4;
+  else if (mt_max >= 2 && ntm >= 2 && ntn * ((ntm + 1) / 2) * 5 >= (uint32_t)sms * 3) mt = 2;
+  dim3 grid(ntn, (ntm + mt - 1) / mt);
   // GEMMs with fewer tiles than SMs split K: residual adds accumulate their
   // partials atomically in place, the other epilogues in the f32
   // accumulator (when given one that fits), finished by gemm_finalize_kernel
   const size_t acc_need = (size_t)a.M * a.N * (a.epi == GEPI_SILU ? 2 : 1);
   const bool can_split = a.epi == GEPI_RESADD ? a.bf16r == 0 : (a.acc && acc_need <= a.acc_floats);
-  if (can_split) {
-    int sms = 148, dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (can_split && mt == 1) {
     uint32_t ks = (uint32_t)sms / (grid.x * grid.y);
     const uint32_t nk = a.K / kBK;
     if (ks > nk / 4) ks = nk / 4;            // >= 4 K steps per CTA
@@ -505,28 +537,30 @@ cudaError_t gemm_launch(const GemmArgs& a_in, const __half* x, cudaStream_t st) 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = st;
   cfg.numAttrs = 0;
-  if (a.fmt == FMT_Q1) {
-    static bool attr = false;
+  cudaError_t e = cudaSuccess;
+  auto go = [&](auto kern, uint32_t smem, bool& attr) {
     if (!attr) {
-      cudaError_t e = cudaFuncSetAttribute(&gemm_kernel<FMT_Q1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-      if (e != cudaSuccess) return e;
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return;
       attr = true;
     }
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, &gemm_kernel<FMT_Q1>, tm, a);
-    if (e != cudaSuccess || grid.z == 1 || a.epi == GEPI_RESADD) return e;
+    cfg.dynamicSmemBytes = smem;
+    e = cudaLaunchKernelEx(&cfg, kern, tm, a);
+  };
+  static bool at[2][3] = {};
+  const int fi = a.fmt == FMT_Q1 ? 0 : 1, mi = mt == 4 ? 2 : mt - 1;
+  if (a.fmt == FMT_Q1) {
+    if (mt == 4) go(&gemm_kernel<FMT_Q1, 4>, GemmShape<4>::kSmemBytes, at[fi][mi]);
+    else if (mt == 2) go(&gemm_kernel<FMT_Q1, 2>, GemmShape<2>::kSmemBytes, at[fi][mi]);
+    else go(&gemm_kernel<FMT_Q1, 1>, GemmShape<1>::kSmemBytes, at[fi][mi]);
   } else {
-    static bool attr4 = false;
-    if (!attr4) {
-      cudaError_t e = cudaFuncSetAttribute(&gemm_kernel<FMT_Q4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-      if (e != cudaSuccess) return e;
-      attr4 = true;
-    }
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, &gemm_kernel<FMT_Q4>, tm, a);
-    if (e != cudaSuccess || grid.z == 1 || a.epi == GEPI_RESADD) return e;
+    if (mt == 4) go(&gemm_kernel<FMT_Q4, 4>, GemmShape<4>::kSmemBytes, at[fi][mi]);
+    else if (mt == 2) go(&gemm_kernel<FMT_Q4, 2>, GemmShape<2>::kSmemBytes, at[fi][mi]);
+    else go(&gemm_kernel<FMT_Q4, 1>, GemmShape<1>::kSmemBytes, at[fi][mi]);
   }
+  if (e != cudaSuccess || grid.z == 1 || a.epi == GEPI_RESADD) return e;
   const size_t n = (size_t)a.M * a.N;
   gemm_finalize_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a);
   return cudaGetLastError();

@@ -250,9 +250,11 @@ __device__ __forceinline__ void stage_f16(const __half* xh, uint32_t stride, uin
   }
 }
 
-// Per (row, group): exact fixed-point split of the staged fp16 x into int8
+// Per (row, group): 15-bit fixed-point split of the staged fp16 x into int8
 // hi/lo B fragments (xf), the group scale 2^(E-14) (gsx), sum(x) (gsum) and
-// sum(q) (gsq).  Zeroes xf/gsx/gsum/gsq itself.  Syncs at start and end.
+// sum(q) (gsq).  q = round(x * 2^(14-E)) with amax = m * 2^E: elements within
+// 1/16 of the group maximum are exact (fp16 has 11 significant bits), smaller
+// ones carry at most 2^(E-15) absolute error.  Zeroes xf/gsx/gsum/gsq itself.  Syncs at start and end.
 // With zero = false the caller guarantees xf/gsx/gsum/gsq were zeroed once
 // and only ever rewritten at the same (row < bc) positions.
 template <int NT>

@@ -15,8 +15,11 @@ NcclApi g_api;
 bool g_ok = false;
 std::string g_err;
 
+// NNZ_NCCL_LIB, when set, is the only library tried (so a deployment can
+// pin one, and a missing one is reported rather than silently replaced).
 void load() {
-  const char* cands[] = {getenv("NNZ_NCCL_LIB"), "libnccl.so.2", "libnccl.so"};
+  const char* pinned = getenv("NNZ_NCCL_LIB");
+  const char* cands[] = {pinned, pinned ? nullptr : "libnccl.so.2", pinned ? nullptr : "libnccl.so"};
   void* h = nullptr;
   for (const char* c : cands) {
     if (!c) continue;
@@ -25,7 +28,8 @@ void load() {
     if (h) break;
   }
   if (!h) {
-    g_err = "NCCL not found (libnccl.so.2; set NNZ_NCCL_LIB)";
+    g_err = pinned ? std::string("NCCL not found at NNZ_NCCL_LIB=") + pinned
+                   : std::string("NCCL not found (libnccl.so.2; set NNZ_NCCL_LIB)");
     return;
   }
   g_api.get_unique_id = reinterpret_cast<decltype(g_api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));

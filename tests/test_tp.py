@@ -118,3 +118,61 @@ def test_tp_algebra_two_gloo_ranks(built_lib):
     err, tok, want = q.get(timeout=5)
     assert err < 1e-3
     assert tok == want
+
+
+def _init_rank_main(rank, world, port, nccl_lib, q):
+    """One gloo rank of the tensor-parallel set-up handshake: rank 0 asks the
+    library for the NCCL unique id and broadcasts it (or its failure) over
+    the host channel; every rank reports what it saw."""
+    import torch.distributed as dist
+    if nccl_lib is not None:
+        os.environ["NNZ_NCCL_LIB"] = nccl_lib
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from nnzap_b200 import tp_unique_id
+        from nnzap_b200._capi import NnzError
+        msg = [None]
+        if rank == 0:
+            try:
+                msg[0] = ("ok", tp_unique_id())
+            except NnzError as e:
+                msg[0] = ("err", (e.code, str(e)))
+        dist.broadcast_object_list(msg, src=0)
+        q.put((rank, msg[0]))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_init(nccl_lib):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_init_rank_main, args=(r, 2, port, nccl_lib, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    return dict(q.get(timeout=5) for _ in procs)
+
+
+def test_tp_init_nccl_missing_two_gloo_ranks(built_lib):
+    """Host-injected failure: the NCCL library the deployment pins is absent.
+    Rank 0's unique-id request fails with NNZ_ENCCL (no device touched, no
+    hang) and every rank learns it over the host channel before any model
+    or collective exists."""
+    from nnzap_b200._capi import NNZ_ENCCL
+    seen = _run_init("/nonexistent/libnccl.so.2")
+    for rank in (0, 1):
+        kind, (code, text) = seen[rank]
+        assert kind == "err" and code == NNZ_ENCCL and "NNZ_NCCL_LIB" in text
+
+
+def test_tp_init_unique_id_two_gloo_ranks(built_lib):
+    """The same handshake with the real library: every rank receives the same
+    128-byte id (ncclGetUniqueId needs no GPU)."""
+    seen = _run_init(None)
+    assert seen[0] == seen[1] and seen[0][0] == "ok" and len(seen[0][1]) == 128
