@@ -44,7 +44,7 @@ sys.path.insert(0, str(ROOT))
 PROMPT, GEN = 512, 256
 # ncu (dram__bytes_read.sum + dram__bytes_write.sum) of one decode launch of
 # the config-3 model at context TRAFFIC_CTX (profiling command in DESIGN.md)
-TRAFFIC_BYTES, TRAFFIC_CTX = 338.3e6, 516
+TRAFFIC_BYTES, TRAFFIC_CTX = 310.53e6, 515
 METRIC = "decode_tok_per_sec"
 UNIT = "tok/s"
 
