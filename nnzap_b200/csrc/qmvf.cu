@@ -19,6 +19,7 @@
 //    global workspace, no atomics, no second kernel.
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
+#include <stdlib.h>
 
 #include "qmv.cuh"
 #include "qmvf.cuh"
@@ -49,7 +50,7 @@ __host__ __device__ inline QfLayout qf_layout(int fmt, uint32_t K, uint32_t gs, 
   L.gsum = o; o += ng * kBatchChunk * 4;
   L.gsq = o; o += ng * kBatchChunk * 4;
   L.red = o; o += kQmvWarps * kTileRows * 4;
-  L.yt = o; o += 8 * kTileRows * 4;      // [cluster rank][128] partial tiles (leader's copy)
+  L.yt = o; o += 16 * kTileRows * 4;     // [cluster rank][128] partial tiles (leader's copy)
   L.bar = o; o += 16;                     // weights landed, peers' partials landed
   L.total = o;
   return L;
@@ -75,8 +76,10 @@ __global__ void __launch_bounds__(kQmvThreads) qmvf_kernel(QmvfArgs a) {
     if (bytes) bulk_g2s(sm + L.w, a.w + ((size_t)tile * groups + g0) * seg, bytes, bar);
   }
   // the leader's "partials" barrier must be initialised before any peer
-  // arrives on it
-  cl.sync();
+  // arrives on it: arrive on the cluster barrier now (release), wait on it
+  // only before the partial tiles are exchanged, so its latency overlaps
+  // the staging and the MMAs
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   // programmatic dependent launch: the weights are constant, so their copy
   // above may overlap the previous kernel; x (and the output) may not
   pdl_wait();
@@ -105,6 +108,7 @@ __global__ void __launch_bounds__(kQmvThreads) qmvf_kernel(QmvfArgs a) {
     for (int v = 0; v < 16; ++v) red[warp * kTileRows + y_row<FMT>(v, lane >> 2)] = y[0][0][v];
   }
   __syncthreads();
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
   float* yt = reinterpret_cast<float*>(sm + L.yt);
   const uint32_t r = threadIdx.x;   // kQmvThreads == kTileRows
   float part = 0.f;
@@ -162,10 +166,17 @@ cudaError_t launch_t(const QmvfArgs& a, uint32_t grid, uint32_t smem, cudaStream
 
 uint32_t qmvf_pick_ks(int fmt, uint32_t M, uint32_t K, uint32_t gs, int num_sms) {
   const uint32_t tiles = num_tiles(M), groups = K / gs;
-  uint32_t ks = tiles >= 2u * (uint32_t)num_sms ? 1 : 2u * (uint32_t)num_sms / tiles;
-  ks = ks > 8 ? 8 : ks;
+  // about 4 CTAs per SM (measured on config 0: 1 per SM 4.95 us, 2: 4.38,
+  // 3-4 (cluster size capped at 8): 3.65); NNZ_QMVF_KS_MAX (8 or 16) is a
+  // measurement aid for non-portable cluster sizes
+  static const uint32_t ks_max = [] {
+    const char* e = getenv("NNZ_QMVF_KS_MAX");
+    return e && atoi(e) == 16 ? 16u : 8u;
+  }();
+  uint32_t ks = tiles >= 4u * (uint32_t)num_sms ? 1 : 4u * (uint32_t)num_sms / tiles;
+  ks = ks > ks_max ? ks_max : ks;
   ks = ks > groups ? groups : ks;
-  while (ks < groups && ks < 8 && qf_layout(fmt, K, gs, ks).total > kQfMaxSmem) ++ks;
+  while (ks < groups && ks < ks_max && qf_layout(fmt, K, gs, ks).total > kQfMaxSmem) ++ks;
   return ks ? ks : 1;
 }
 
@@ -181,6 +192,7 @@ cudaError_t qmvf_prepare() {
   cudaError_t e = cudaSuccess;
   auto raise = [&](const void* f) {
     if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kQfMaxSmem);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   };
   raise((const void*)qmvf_kernel<FMT_Q1, false>);
   raise((const void*)qmvf_kernel<FMT_Q4, false>);
