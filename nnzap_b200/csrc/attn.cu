@@ -498,7 +498,14 @@ __global__ void __launch_bounds__(kPfThreads) attn_prefill_kernel(AttnArgs a) {
 }  // namespace
 
 cudaError_t attn_prefill_launch(const AttnArgs& a, int head_dim, int pdl, cudaStream_t st) {
-  if (attn_tc_applies(a.n_q, a.n_kv, head_dim) && a.ws && !use_legacy_attn()) return attn_prefill_tc_launch(a, pdl, st);
+  if (attn_tc_applies(a.n_q, a.n_kv, head_dim) && !use_legacy_attn()) {
+    static const bool mma = [] {
+      const char* e = getenv("NNZ_PREFILL_ATTN");
+      return e && strcmp(e, "mma") == 0;
+    }();
+    if (!mma && attn_pf_umma_applies(a.n_q, a.n_kv)) return attn_pf_umma_launch(a, pdl, st);
+    if (a.ws) return attn_prefill_tc_launch(a, pdl, st);
+  }
   const uint32_t G = a.n_q / a.n_kv;
   if (a.rows == 0 || a.n_kv == 0 || a.n_q % a.n_kv || 4 * G > (uint32_t)kPfThreads) return cudaErrorInvalidValue;
   const uint32_t rpc = kPfThreads / (4 * G);

@@ -74,6 +74,12 @@ cudaError_t attn_tc_launch(const AttnArgs& a, int pdl, cudaStream_t st);
 // attn_prefill_launch; head_dim 128, G in {1, 2, 4}).
 // Uses a.ws (attn_prefill_tc_ws_floats) for the key splits' partials.
 cudaError_t attn_prefill_tc_launch(const AttnArgs& a, int pdl, cudaStream_t st);
+// Causal prefill attention on tcgen05 / TMEM (attn_pf.cu): one CTA per
+// (kv head, 128 / G query positions), no workspace; a.slots must be the
+// number of cache slots (the K/V tensor maps cover exactly those).  The default for head_dim
+// 128; NNZ_PREFILL_ATTN=mma selects attn_prefill_tc_launch instead.
+bool attn_pf_umma_applies(uint32_t n_q, uint32_t n_kv);
+cudaError_t attn_pf_umma_launch(const AttnArgs& a, int pdl, cudaStream_t st);
 size_t attn_prefill_tc_ws_floats(uint32_t rows, uint32_t n_q);
 
 // Writes normed+roped k and v of `rows` query rows at their positions

@@ -751,7 +751,7 @@ int enqueue_layer_gemm(nnz_model* m, uint32_t l, uint32_t rows, const int* pos) 
     AttnArgs aa{};
     aa.qkv = m->qkv; aa.qkv_stride = m->qkv_rows; aa.q_norm = W.q_norm; aa.k_norm = W.k_norm;
     aa.kc = m->kc + m->kv_layer * l; aa.vc = m->vc + m->kv_layer * l; aa.max_ctx = c.max_context_length;
-    aa.pos = pos; aa.slot = m->zeros; aa.rows = rows; aa.n_q = c.num_query_heads; aa.n_kv = c.num_kv_heads;
+    aa.pos = pos; aa.slot = m->zeros; aa.slots = m->slots; aa.rows = rows; aa.n_q = c.num_query_heads; aa.n_kv = c.num_kv_heads;
     aa.eps = c.eps; aa.theta = c.rope_theta; aa.rope_style = c.rope_style; aa.out = m->attn;
     aa.out_stride = m->qd; aa.err = m->err; aa.rope_tab = m->rope_tab; aa.ws = m->ws;
     NNZ_CK(attn_prefill_launch(aa, (int)c.head_dim, 0, m->st));

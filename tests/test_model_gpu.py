@@ -232,3 +232,25 @@ def test_generate_sampled_matches_oracle(cuda, built_lib):
             # logits differ from the oracle by < 2e-2, so the CDF may shift a little
             assert abs(float(cum[min(t, want)]) - float(u[i])) < 2e-2, (i, t, want)
     m.free()
+
+
+@pytest.mark.parametrize("n_q,n_kv,style,plen", [(4, 4, "pairwise", 300), (4, 2, "pairwise", 700),
+                                                 (8, 2, "half_split", 300), (8, 2, "pairwise", 129)],
+                         ids=["G1", "G2_two_chunks", "G4_half_split", "G4_tile_edge"])
+def test_prefill_attention_tiles(cuda, built_lib, n_q, n_kv, style, plen):
+    """The tcgen05 prefill attention over several 128-key tiles, every GQA
+    group size, both RoPE pairings, a prompt that spans two prefill chunks
+    (the second chunk's queries start past the first's keys) and one that
+    ends one key into a tile: last-row logits against the oracle, then the
+    greedy continuation decoded from the cache the prefill wrote."""
+    d = synth.ModelDims(vocab=800, hidden=256, inter=512, layers=2, n_q=n_q, n_kv=n_kv, head_dim=128,
+                        gs=128, quant="q1", rope_style=style)
+    m, W = build(d, max_ctx=1024)
+    cfg = oracle_cfg(d)
+    prompt = np.random.default_rng(plen).integers(0, d.vocab, plen)
+    nxt, lg = m.prefill(prompt, want_logits=True)
+    want = R.forward_tokens(cfg, W, prompt, logits_rows=[plen - 1])[0]
+    assert np.abs(lg - want).max() <= 2e-2, float(np.abs(lg - want).max())
+    res = generate(m, GenerateOpts(prompt_ids=list(prompt), max_new=6))
+    assert greedy_ok(cfg, W, list(prompt), res.tokens) >= 0
+    m.free()
