@@ -178,8 +178,15 @@ __global__ void __launch_bounds__(512, 1) attn_pf_umma_kernel(const __grid_const
   {
     const float tot = (red[r] + red[128 + r]) + (red[256 + r] + red[384 + r]);
     const float rr = rsqrtf(tot / (float)kHd + a.eps);
+    const float4* qn4 = reinterpret_cast<const float4*>(a.q_norm + 32 * c);
 #pragma unroll
-    for (int e = 0; e < 32; ++e) v[e] = v[e] * rr * __ldg(a.q_norm + 32 * c + e);
+    for (int i = 0; i < 8; ++i) {
+      const float4 w = __ldg(qn4 + i);
+      v[4 * i] = v[4 * i] * rr * w.x;
+      v[4 * i + 1] = v[4 * i + 1] * rr * w.y;
+      v[4 * i + 2] = v[4 * i + 2] * rr * w.z;
+      v[4 * i + 3] = v[4 * i + 3] * rr * w.w;
+    }
   }
   const int pp = pos < 0 ? 0 : pos;
   const float2* tab = a.rope_tab ? a.rope_tab + (size_t)pp * (kHd / 2) : nullptr;
@@ -216,7 +223,7 @@ __global__ void __launch_bounds__(512, 1) attn_pf_umma_kernel(const __grid_const
   PF_STAMP(1);
 
   const uint32_t idesc = idesc_f16(128, 128);
-  const uint32_t idesc_pv = idesc_f16(128, 64) | (1u << 16);   // N = 64, B MN-major
+  const uint32_t idesc_pv = idesc_f16(128, 128) | (1u << 16);  // B MN-major
   // scores scaled by 1 / sqrt(128) and log2(e): the softmax runs on exp2
   const float sl2 = rsqrtf((float)kHd) * 1.4426950408889634f;
   const uint32_t tq = tmem + ((32 * (warp & 3)) << 16);   // this warp's TMEM lane quarter
@@ -307,20 +314,19 @@ __global__ void __launch_bounds__(512, 1) attn_pf_umma_kernel(const __grid_const
     if (tid == 0) {
       pf_wait(mbv, (uint32_t)j & 1u, a.err, failed);
       tc_fence_after();
-      // O += P_hi V + P_lo V: V as loaded ([key][d], MN-major B), one MMA
-      // per 64-column half of d; K steps of 16 keys = 2048 bytes of V rows
+      // O += P_hi V + P_lo V: V as loaded ([key][d], MN-major B: the two
+      // 64-wide d halves are the two TMA boxes, 16 KB apart); K steps of 16
+      // keys = 2048 bytes of V rows
 #pragma unroll
       for (int part = 0; part < 2; ++part)
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb) {
           const uint64_t da = smem_desc_sw128(sm + (part ? OFF_PL : OFF_PH) + kb * kBlk);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-            for (int hb = 0; hb < 2; ++hb) {
-              const uint64_t db = smem_desc_sw128_mn(sm + OFF_VT + hb * kBlk + (kb * 64 + kk * 16) * 128);
-              umma_f16(tmem + 128 + hb * 64, da + (uint64_t)(kk * 2), db, idesc_pv, (j | part | kb | kk) != 0);
-            }
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t db = smem_desc_sw128_mn(sm + OFF_VT + (kb * 64 + kk * 16) * 128);
+            umma_f16(tmem + 128, da + (uint64_t)(kk * 2), db, idesc_pv, (j | part | kb | kk) != 0);
+          }
         }
       umma_commit(mb);
     }

@@ -23,16 +23,15 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
   return d;
 }
 
-// MN-major (the N index contiguous), 128B-swizzled operand as a 2-D TMA
-// copy of box {64 N, rows K} with 128-byte swizzle lays it out: 8-row (K)
-// groups of 128-byte rows 1024 bytes apart (stride byte offset); used only
-// with N = 64, one swizzle atom wide, so the leading byte offset (the step
-// to the next 64 N) is never followed.
+// MN-major (the N index contiguous), 128B-swizzled operand as 2-D TMA
+// copies of box {64 N, rows K} with 128-byte swizzle lay it out: 8-row (K)
+// groups of 128-byte rows 1024 bytes apart (stride byte offset), the next
+// 64 N in the next box, 16 KB on (leading byte offset: boxes of 128 K rows).
 __device__ __forceinline__ uint64_t smem_desc_sw128_mn(const void* p) {
   const uint64_t addr = smem_u32(p);
   uint64_t d = 0;
   d |= (addr >> 4) & 0x3FFFull;
-  d |= (uint64_t)(16384 >> 4) << 16;            // leading byte offset (next 64 N; not reached at N = 64)
+  d |= (uint64_t)(16384 >> 4) << 16;            // leading byte offset: the next 64 N
   d |= (uint64_t)(1024 >> 4) << 32;             // stride byte offset: 8 K rows x 128 B
   d |= (uint64_t)1 << 46;
   d |= (uint64_t)2 << 61;
