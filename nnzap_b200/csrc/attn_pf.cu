@@ -13,15 +13,16 @@
 // meet in shared memory), write it as fp16 hi + lo into shared memory, run
 // the row's online softmax straight out of TMEM (one shared-memory max
 // exchange per tile) and write the output row.
-// Per 128-key tile (the next tile's K/V rows are loaded into registers
-// while the current one is computed):
-//   K tile -> shared memory (K-major, 128B swizzle), V tile transposed ->
-//   shared memory (d rows, K-major over keys);
-//   S = Q_hi K^T + Q_lo K^T            (16 MMAs 128x128x16, f32 in TMEM cols 0-127)
+// Per 128-key tile j:
+//   S(j) = Q_hi K^T + Q_lo K^T (16 MMAs 128x128x16, f32 in one of two TMEM
+//   buffers, columns 0-127 / 128-255) -- issued together with the previous
+//   tile's P V, so it is ready when the softmax comes round;
 //   P = exp(S / sqrt(128) - m) per row (computed as exp2 of log2(e)-scaled
-//   scores), fp16 hi + lo into shared memory; the O accumulator (TMEM cols
-//   128-255) rescaled by exp(m_old - m_new);
-//   O += P_hi V + P_lo V                (16 MMAs)
+//   scores), fp16 hi + lo into shared memory; the O accumulator (TMEM
+//   columns 256-383) rescaled by exp(m_old - m_new);
+//   O += P_hi V + P_lo V (16 MMAs; V as stored, [key][d], an MN-major B).
+// K and V tiles arrive by TMA one tile ahead (K as soon as the S that read
+// the buffer has completed, V as soon as the P V has).
 // q and the probabilities keep ~22 significant bits through the hi/lo
 // split, products are exact and accumulate in f32: the f32 semantics of the
 // reference's scores and softmax, with the fp16 K/V cache it stores.
@@ -47,7 +48,7 @@ constexpr uint32_t OFF_QH = 0, OFF_QL = 2 * kBlk, OFF_K = 4 * kBlk, OFF_VT = 6 *
                    OFF_PL = 10 * kBlk, OFF_MISC = 12 * kBlk;
 constexpr uint32_t OFF_RED = OFF_MISC + 64;            // [4 chunks][128 rows] f32 partial reductions
 constexpr uint32_t kPfSmem = OFF_RED + 4 * 128 * 4 + 1024;   // + alignment slack
-constexpr uint32_t kTmemCols = 256;                  // S: 0-127, O: 128-255
+constexpr uint32_t kTmemCols = 512;                  // S: two buffers 0-127 / 128-255, O: 256-383
 
 // 16-byte chunk c (8 fp16 along K) of row r in a two-block K-major tile.
 __device__ __forceinline__ uint32_t tile_off(uint32_t r, uint32_t c) {
@@ -232,37 +233,44 @@ __global__ void __launch_bounds__(512, 1) attn_pf_umma_kernel(const __grid_const
   uint32_t ph = 0;   // commit phases consumed
   const int ntile = kmax / kKeys + 1;
   const uint32_t pbh = smem_u32(sm + OFF_PH), pbl = smem_u32(sm + OFF_PL);
+  // S of tile j into TMEM columns 128 (j % 2) (thread 0)
+  auto issue_s = [&](int j) {
+    pf_wait(mbk, (uint32_t)j & 1u, a.err, failed);
+    tc_fence_after();
+#pragma unroll
+    for (int part = 0; part < 2; ++part)            // S = Q_hi K^T + Q_lo K^T
+#pragma unroll
+      for (int kb = 0; kb < 2; ++kb) {
+        const uint64_t da = smem_desc_sw128(sm + (part ? OFF_QL : OFF_QH) + kb * kBlk);
+        const uint64_t db = smem_desc_sw128(sm + OFF_K + kb * kBlk);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16(tmem + (uint32_t)(j & 1) * 128, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc,
+                   (part | kb | kk) != 0);
+      }
+  };
+  // the query tiles were written by every thread
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 0) {
+    issue_s(0);
+    umma_commit(mb);
+  }
+  pf_wait(mb, ph & 1u, a.err, failed);
+  ++ph;
+  tc_fence_after();
+  if (tid == 0 && ntile > 1) issue_k(1);
+  // Per tile: softmax of S(j) -> P; then one commit covers S(j + 1) (the
+  // other TMEM buffer, its K tile loaded meanwhile) and O += P V(j), so the
+  // next tile's scores are ready when the softmax loop comes round.
   for (int j = 0; j < ntile; ++j) {
     PF_STAMP(2 + 6 * j);
-    PF_STAMP(3 + 6 * j);
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      pf_wait(mbk, (uint32_t)j & 1u, a.err, failed);
-      tc_fence_after();
-#pragma unroll
-      for (int part = 0; part < 2; ++part)          // S = Q_hi K^T + Q_lo K^T
-#pragma unroll
-        for (int kb = 0; kb < 2; ++kb) {
-          const uint64_t da = smem_desc_sw128(sm + (part ? OFF_QL : OFF_QH) + kb * kBlk);
-          const uint64_t db = smem_desc_sw128(sm + OFF_K + kb * kBlk);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_f16(tmem, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (part | kb | kk) != 0);
-        }
-      umma_commit(mb);
-    }
-    pf_wait(mb, ph & 1u, a.err, failed);
-    ++ph;
-    tc_fence_after();
-    PF_STAMP(4 + 6 * j);
-    if (tid == 0 && j + 1 < ntile) issue_k(j + 1);   // the K tile is free once S is
     // online softmax: this thread's 32 scores of row r
     float sv[32];
     {
       uint32_t u[32];
-      tmem_ld32(tq + 32 * c, u);
+      tmem_ld32(tq + (uint32_t)(j & 1) * 128 + 32 * c, u);
       float mx = -INFINITY;
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
@@ -291,10 +299,10 @@ __global__ void __launch_bounds__(512, 1) attn_pf_umma_kernel(const __grid_const
     if (j > 0) {   // O *= alpha (the previous tile's P V has completed)
       uint32_t u[32];
       tc_fence_after();
-      tmem_ld32(tq + 128 + 32 * c, u);
+      tmem_ld32(tq + 256 + 32 * c, u);
 #pragma unroll
       for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
-      tmem_st32(tq + 128 + 32 * c, u);
+      tmem_st32(tq + 256 + 32 * c, u);
     }
     PF_STAMP(6 + 6 * j);
     if (j == ntile - 1) {
@@ -310,8 +318,9 @@ __global__ void __launch_bounds__(512, 1) attn_pf_umma_kernel(const __grid_const
     }
     fence_async_smem();
     tc_fence_before();
-    __syncthreads();   // also: every thread has read red[] before the next tile rewrites it
+    __syncthreads();   // also: every thread has read red[] and S(j) before they are rewritten
     if (tid == 0) {
+      if (j + 1 < ntile) issue_s(j + 1);
       pf_wait(mbv, (uint32_t)j & 1u, a.err, failed);
       tc_fence_after();
       // O += P_hi V + P_lo V: V as loaded ([key][d], MN-major B: the two
@@ -325,7 +334,7 @@ __global__ void __launch_bounds__(512, 1) attn_pf_umma_kernel(const __grid_const
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t db = smem_desc_sw128_mn(sm + OFF_VT + (kb * 64 + kk * 16) * 128);
-            umma_f16(tmem + 128, da + (uint64_t)(kk * 2), db, idesc_pv, (j | part | kb | kk) != 0);
+            umma_f16(tmem + 256, da + (uint64_t)(kk * 2), db, idesc_pv, (j | part | kb | kk) != 0);
           }
         }
       umma_commit(mb);
@@ -333,7 +342,10 @@ __global__ void __launch_bounds__(512, 1) attn_pf_umma_kernel(const __grid_const
     pf_wait(mb, ph & 1u, a.err, failed);
     ++ph;
     tc_fence_after();
-    if (tid == 0 && j + 1 < ntile) issue_v(j + 1);   // the V tile is free once P V is
+    if (tid == 0) {   // K and V tiles are free again
+      if (j + 2 < ntile) issue_k(j + 2);
+      if (j + 1 < ntile) issue_v(j + 1);
+    }
   }
   PF_STAMP(60);
   // ---- output row r, columns [32c, 32c + 32): O / l, fp16 ----
@@ -342,7 +354,7 @@ __global__ void __launch_bounds__(512, 1) attn_pf_umma_kernel(const __grid_const
   {
     const float il = 1.0f / ((red[r] + red[128 + r]) + (red[256 + r] + red[384 + r]));
     uint32_t u[32];
-    tmem_ld32(tq + 128 + 32 * c, u);
+    tmem_ld32(tq + 256 + 32 * c, u);
     if (valid) {
       __half* dst = a.out + (size_t)qi * a.out_stride + (size_t)h * kHd + 32 * c;
 #pragma unroll
