@@ -236,12 +236,27 @@ __device__ D1_SMALL void grid_bar(Ctx& c) {
 
 // ---- weight ring ---------------------------------------------------------------------
 // Every warp releases every chunk, in order.  A release waits for the chunk
-// to have landed first (so it can never count toward the slot's previous
-// chunk); the warp whose release is the slot's 16th issues the copy of the
-// chunk kD1Slots ahead into it.  Nothing is issued once the launch aborted.
+// to have been issued (the slot's issue record; so it can never count toward
+// the slot's previous chunk); the warp whose release is the slot's 16th
+// issues the copy of the chunk kD1Slots ahead into it.  A warp that reads a
+// chunk waits for it to land before it reads and so before it releases, so
+// the 16th release of a chunk always follows its landing.  Nothing is issued
+// once the launch aborted.
 __device__ D1_SMALL void ring_release_one(Ctx& c) {
   const uint32_t K = c.rel;
-  if (!c.failed) c.failed = !wait_mbar(fullb(c.sm, K % kD1Slots), (K / kD1Slots) & 1u, *c.a);
+  if (!c.failed) {
+    const volatile uint32_t* iss = reinterpret_cast<const volatile uint32_t*>(c.sm + OFF_ISS) + K % kD1Slots;
+    for (uint32_t i = 0; *iss != K; ++i) {
+      if ((i & 63u) == 63u) {
+        if (ld_relaxed_u32(&c.a->bar[2])) { c.failed = true; break; }
+        if (i > kD1Spin) {
+          raise_abort(*c.a, ERR_SPIN_TIMEOUT);
+          c.failed = true;
+          break;
+        }
+      }
+    }
+  }
   __syncwarp();
   if (c.lane == 0) {
     uint32_t* relc = reinterpret_cast<uint32_t*>(c.sm + OFF_RELC) + K % kD1Slots;
@@ -1023,7 +1038,10 @@ __global__ void __launch_bounds__(kD1Threads, 1) d1_kernel(const __grid_constant
     uint32_t* cbs = reinterpret_cast<uint32_t*>(sm + OFF_CB);
     const uint32_t n = a.g.nck < kD1CbMax ? a.g.nck : kD1CbMax;
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) cbs[i] = __ldg(a.chunk_bytes + (size_t)blockIdx.x * a.g.nck + i);
-    if (threadIdx.x < (uint32_t)kD1Slots) reinterpret_cast<uint32_t*>(sm + OFF_RELC)[threadIdx.x] = 0u;
+    if (threadIdx.x < (uint32_t)kD1Slots) {
+      reinterpret_cast<uint32_t*>(sm + OFF_RELC)[threadIdx.x] = 0u;
+      reinterpret_cast<uint32_t*>(sm + OFF_ISS)[threadIdx.x] = 0xffffffffu;   // nothing issued yet
+    }
     for (uint32_t i = threadIdx.x; i < a.g.L; i += blockDim.x)
       reinterpret_cast<D1Layer*>(sm + OFF_LAY)[i] = a.layers[i];
   }
