@@ -309,7 +309,8 @@ __device__ __forceinline__ void digits(int q, uint32_t& hi, uint32_t& mid, uint3
 
 __device__ D1_SMALL void quant_group(const float (&x)[4], uint32_t gg, int lane, uint8_t* sm) {
   float am = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
-  am = warp_max(am);
+  // |x| >= 0 orders like its bit pattern: one redux instead of a shuffle tree
+  am = __uint_as_float(__reduce_max_sync(kFull, __float_as_uint(am)));
   float up, down;
   group_scales(am, up, down);
   uint32_t w0 = 0, w1 = 0, w2 = 0;
@@ -324,7 +325,7 @@ __device__ D1_SMALL void quant_group(const float (&x)[4], uint32_t gg, int lane,
     w1 |= m << (8 * i);
     w2 |= l << (8 * i);
   }
-  sum = warp_sum_int(sum);
+  sum = __reduce_add_sync(kFull, sum);
   uint32_t* xb = reinterpret_cast<uint32_t*>(sm + OFF_XB) + ((size_t)gg * 4 + (lane >> 3)) * 24;
   const int t = lane & 3, reg = (lane >> 2) & 1;
   xb[(0 * 4 + t) * 2 + reg] = w0;

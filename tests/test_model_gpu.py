@@ -254,3 +254,18 @@ def test_prefill_attention_tiles(cuda, built_lib, n_q, n_kv, style, plen):
     res = generate(m, GenerateOpts(prompt_ids=list(prompt), max_new=6))
     assert greedy_ok(cfg, W, list(prompt), res.tokens) >= 0
     m.free()
+
+
+def test_prefill_attention_mma_fallback(cuda, built_lib, tmp_path):
+    """NNZ_PREFILL_ATTN=mma (read once per process) still selects the
+    mma.sync prefill attention: run the tile test's G2 two-chunk case in a
+    child process with it set."""
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ, NNZ_PREFILL_ATTN="mma")
+    here = os.path.dirname(os.path.abspath(__file__))
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider",
+                        os.path.join(here, "test_model_gpu.py"), "-k", "test_prefill_attention_tiles and G2_two_chunks"],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
