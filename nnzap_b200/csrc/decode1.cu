@@ -617,11 +617,32 @@ __device__ void att_issue(Ctx& c, const AttGeo& g, uint32_t l, int pos, uint32_t
   c.kv_hi = seq + 1;
 }
 
+// Lane's 4 tagged QKV words of a 128-wide row written in this launch: polls
+// (relaxed, bounded) until all four carry `tag`, i.e. the producer's store of
+// this layer step; the fp16 halves of the value words are returned.  The
+// data is its own flag: no counter, no release / acquire pair.
+__device__ __forceinline__ uint2 load_tagged(const uint32_t* row, uint32_t tag, int lane, const D1Args& a) {
+  const uint32_t* p = row + 4 * lane;
+  uint4 w;
+  for (uint32_t i = 0;; ++i) {
+    asm volatile("ld.relaxed.gpu.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w) : "l"(p) : "memory");
+    if ((w.x >> 16) == tag && (w.y >> 16) == tag && (w.z >> 16) == tag && (w.w >> 16) == tag) break;
+    if ((i & 63u) == 63u) {
+      if (ld_relaxed_u32(&a.bar[2])) break;
+      if (i > kD1Spin) {
+        raise_abort(a, ERR_SPIN_TIMEOUT);
+        break;
+      }
+    }
+  }
+  return make_uint2((w.x & 0xffffu) | (w.y << 16), (w.z & 0xffffu) | (w.w << 16));
+}
+
 // RMSNorm (f32) + RoPE of one 128-wide head held as 4 consecutive elements
-// per lane; the source is fp16 written in this launch (read through L2).
-__device__ __forceinline__ void norm_rope(const __half* src, const float* nw, const float2* cs, float eps,
+// per lane (raw: the lane's 4 fp16 values).
+__device__ __forceinline__ void norm_rope(uint2 raw, const float* nw, const float2* cs, float eps,
                                           int style, int lane, float (&v)[4]) {
-  const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(src) + lane);
   const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
   const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
   v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
@@ -666,24 +687,25 @@ __device__ D1_PHASE void att_phase(Ctx& c, uint32_t l, int pos, uint32_t epoch_t
   __half* vnew = reinterpret_cast<__half*>(sm + OFF_VNEW);
   const int warp = c.warp, lane = c.lane;
 
-  if (threadIdx.x == 0)
-    wait_count(a.cnt + (size_t)l * a.g.nkv + g.j, (epoch_tok + 1) * (G + 2) * 8, a);
-  named_sync();
+  // the q / k / v rows of this kv head, polled as tagged words (QKV phase)
+  const uint32_t tag = d1_tag(epoch_tok * a.g.L + l);
   D1_STAMP(c, 12);
   const D1Layer& LW = reinterpret_cast<const D1Layer*>(sm + OFF_LAY)[l];
   const float2* cs = a.rope_tab + (size_t)pos * 64;
   if ((uint32_t)warp < G) {
     float v[4];
-    norm_rope(a.qkv + (size_t)(g.j * G + warp) * 128, LW.q_norm, cs, a.eps, a.rope_style, lane, v);
+    norm_rope(load_tagged(a.qkv + (size_t)(g.j * G + warp) * 128, tag, lane, a), LW.q_norm, cs, a.eps,
+              a.rope_style, lane, v);
     *reinterpret_cast<float4*>(qs + warp * 128 + 4 * lane) = make_float4(v[0], v[1], v[2], v[3]);
   } else if ((uint32_t)warp == G && g.own_new) {
     float v[4];
-    norm_rope(a.qkv + (size_t)(a.g.nq + g.j) * 128, LW.k_norm, cs, a.eps, a.rope_style, lane, v);
+    norm_rope(load_tagged(a.qkv + (size_t)(a.g.nq + g.j) * 128, tag, lane, a), LW.k_norm, cs, a.eps,
+              a.rope_style, lane, v);
     const __half2 k01 = __floats2half2_rn(v[0], v[1]), k23 = __floats2half2_rn(v[2], v[3]);
     uint2 kk;
     kk.x = *reinterpret_cast<const uint32_t*>(&k01);
     kk.y = *reinterpret_cast<const uint32_t*>(&k23);
-    const uint2 vv = __ldcg(reinterpret_cast<const uint2*>(a.qkv + (size_t)(a.g.nq + a.g.nkv + g.j) * 128) + lane);
+    const uint2 vv = load_tagged(a.qkv + (size_t)(a.g.nq + a.g.nkv + g.j) * 128, tag, lane, a);
     reinterpret_cast<uint2*>(knew)[lane] = kk;
     reinterpret_cast<uint2*>(vnew)[lane] = vv;
     const size_t off = (size_t)l * a.kv_layer + ((size_t)g.j * a.g.max_ctx + (uint32_t)pos) * 128;
@@ -951,14 +973,7 @@ __device__ D1_PHASE void dn_phase(Ctx& c, uint32_t l, uint32_t Kd, uint32_t tok)
 }
 
 // ---- QKV ----------------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t kv_head_of_rb(const D1Geom& g, uint32_t rb) {
-  const uint32_t row = rb * 16, qd = g.nq * 128, kvd = g.nkv * 128;
-  if (row < qd) return row / (g.G * 128);
-  if (row < qd + kvd) return (row - qd) / 128;
-  return (row - qd - kvd) / 128;
-}
-
-__device__ D1_PHASE void qkv_phase(Ctx& c, uint32_t l, uint32_t Kq, uint32_t tok) {
+__device__ D1_PHASE void qkv_phase(Ctx& c, uint32_t l, uint32_t Kq, uint32_t tok, uint32_t tag) {
   const D1Args& a = *c.a;
   const D1Geom& g = a.g;
   const uint32_t rb0 = d1_lo(c.c, g.nrb_qkv, g.P), rb1 = d1_lo(c.c + 1, g.nrb_qkv, g.P), nrb = rb1 - rb0;
@@ -983,11 +998,11 @@ __device__ D1_PHASE void qkv_phase(Ctx& c, uint32_t l, uint32_t Kq, uint32_t tok
         float y = 0.f;
 #pragma unroll
         for (int w = 0; w < kD1Warps; ++w) y += part[(w * kD1MaxRb + rbl) * 16 + rr];
-        a.qkv[rb0 * 16 + threadIdx.x] = __float2half_rn(y);
+        // fp16 value and this layer step's tag in one word: the attention
+        // CTAs poll the words themselves (no flag, no release fence)
+        const uint32_t w = (uint32_t)__half_as_ushort(__float2half_rn(y)) | (tag << 16);
+        asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(a.qkv + rb0 * 16 + threadIdx.x), "r"(w) : "memory");
       }
-      // publish per row block: the warp syncs, one lane per block releases
-      __syncwarp();
-      if (rr == 0 && rbl < nrb) red_release_u32(a.cnt + (size_t)l * g.nkv + kv_head_of_rb(g, rb0 + rbl), 1u);
     }
   }
   D1_STAMP(c, 11);
@@ -1143,7 +1158,7 @@ __global__ void __launch_bounds__(kD1Threads, 1) d1_kernel(const __grid_constant
         fence_proxy_async();
         att_prefetch(c, ag, 0, pos);
       }
-      qkv_phase(c, l, Kl, tok);
+      qkv_phase(c, l, Kl, tok, d1_tag(ep * g.L + l));
       if (st_l) a.prof[1] = gtimer();
       if (att_cta) {
         if (g.G == 1) att_phase<1>(c, l, pos, ep);

@@ -118,7 +118,7 @@ struct D1Args {
   size_t kv_layer;                 // elements per layer per cache
   float* R;                        // [2][H] residual versions
   float* Z;                        // [2][H] O-projection accumulators
-  __half* qkv;                     // [qkv_rows]
+  uint32_t* qkv;                   // [qkv_rows] fp16 value | layer tag << 16 (see d1_tag)
   __half* h;                       // [I] SiLU(gate) * up
   float* att;                      // [nkv * S * G][kD1AttRec]
   unsigned int* cnt;               // [L][nkv] QKV row blocks done, then [L][nkv] attention splits done
@@ -134,6 +134,11 @@ struct D1Args {
   unsigned long long* tstamp;      // optional [ntok + 1] %globaltimer at token boundaries
   unsigned long long* prof;        // optional per-phase stamps (CTA 0)
 };
+
+// Tag of the layer step n = token * L + layer in the tagged QKV words: 15
+// bits, never 0, so a word from the previous step (or the zeroed buffer)
+// never matches; every step rewrites every word before the next one reads.
+__host__ __device__ inline uint32_t d1_tag(uint32_t n) { return (n & 0x7fffu) | 0x8000u; }
 
 // Grid barriers per decoded token: per layer one after the O projection, one
 // after gate/up and one after the down projection; one after the LM head.

@@ -621,6 +621,7 @@ int sync_check(nnz_model* m) {
       cudaMemset(m->d1.bar, 0, 64);
       cudaMemset(m->d1.cnt, 0, m->d1_cnt_words * 4);
       cudaMemset(m->d1.R, 0, 4 * (size_t)m->c.hidden_size * 4);
+      cudaMemset(m->d1.qkv, 0, (size_t)m->d1.g.qkv_rows * 4);   // no stale layer tags
       m->d1_bar_count = 0;
       m->d1_epoch = 0;
     }
@@ -694,6 +695,8 @@ const nnz_model::MegaPlan* mega_plan_for(nnz_model* m, uint32_t rows) {
 int d1_run(nnz_model* m, uint32_t ntok, bool want_logits) {
   if (m->d1_epoch + ntok > (1u << 24)) {   // keep the per-layer counters far from wrapping
     NNZ_CK(cudaMemsetAsync(m->d1.cnt, 0, m->d1_cnt_words * 4, m->st));
+    // the layer tags restart with the epoch: clear the words they mark
+    NNZ_CK(cudaMemsetAsync(m->d1.qkv, 0, (size_t)m->d1.g.qkv_rows * 4, m->st));
     m->d1_epoch = 0;
   }
   D1Args a = m->d1;
@@ -1299,7 +1302,8 @@ static int model_finalize_impl(nnz_model* m) {
     if ((rc = dalloc(m, (void**)&a.R, 4 * (size_t)H * 4))) return rc;
     a.Z = a.R + 2 * H;
     NNZ_CK(cudaMemset(a.R, 0, 4 * (size_t)H * 4));
-    if ((rc = dalloc(m, (void**)&a.qkv, (size_t)d1g.qkv_rows * 2))) return rc;
+    if ((rc = dalloc(m, (void**)&a.qkv, (size_t)d1g.qkv_rows * 4))) return rc;
+    NNZ_CK(cudaMemset(a.qkv, 0, (size_t)d1g.qkv_rows * 4));
     if ((rc = dalloc(m, (void**)&a.h, (size_t)I * 2))) return rc;
     if ((rc = dalloc(m, (void**)&a.att, (size_t)c.num_kv_heads * d1g.S * d1g.G * kD1AttRec * 4))) return rc;
     m->d1_cnt_words = (size_t)2 * c.num_layers * c.num_kv_heads;
