@@ -522,11 +522,11 @@ int enqueue_layer(nnz_model* m, uint32_t l, uint32_t rows, const int* pos, const
   if (!prefill && m->gemm_prefill && rows >= kGemmDecodeRows) {
     // large decode batches: the projections as tcgen05 GEMMs over the rows
     const uint32_t H = c.hidden_size, I = c.intermediate_size;
-    NNZ_CK(rmsnorm_f16_launch(m->residual, W.attn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st));
+    NNZ_CK(rmsnorm_f16_launch(m->residual, W.attn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st, 1));
     if ((rc = gemm(m, W.fqkv, nullptr, m->qkv_rows, H, m->xn, rows, GEPI_F16, m->qkv, m->qkv_rows))) return rc;
-    if ((rc = attn(m, l, rows, pos, slot, 1, 0))) return rc;
+    if ((rc = attn(m, l, rows, pos, slot, 1, 1))) return rc;
     if ((rc = gemm_resadd_tp(m, W.fo, m->qd, m->attn, rows))) return rc;
-    NNZ_CK(rmsnorm_f16_launch(m->residual, W.ffn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st));
+    NNZ_CK(rmsnorm_f16_launch(m->residual, W.ffn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st, 1));
     if ((rc = gemm(m, W.fgate, &W.fup, I, H, m->xn, rows, GEPI_SILU, m->h, I))) return rc;
     return gemm_resadd_tp(m, W.fdown, I, m->h, rows);
   }
@@ -574,7 +574,7 @@ int enqueue_decode(nnz_model* m, uint32_t rows, bool want_logits, int pdl) {
   if (m->gemm_prefill && rows >= kGemmDecodeRows) {
     // final norm -> LM-head GEMM into the logits buffer -> argmax per row
     const nnz_config& c = m->c;
-    NNZ_CK(rmsnorm_f16_launch(m->residual, m->fnorm, c.eps, rows, c.hidden_size, m->bf16r, m->xn, m->st));
+    NNZ_CK(rmsnorm_f16_launch(m->residual, m->fnorm, c.eps, rows, c.hidden_size, m->bf16r, m->xn, m->st, 1));
     if ((rc = gemm(m, m->flm, nullptr, m->lm_rows, c.hidden_size, m->xn, rows, GEPI_F32, m->logits,
                    m->lm_rows)))
       return rc;
@@ -735,6 +735,7 @@ int gemm(nnz_model* m, const FlatW& W, const FlatW* W2, uint32_t N, uint32_t K, 
   if (W2) { g.w2 = W2->w; g.s2 = W2->s; g.b2 = W2->b; }
   g.epi = epi; g.out = out; g.ldo = ldo; g.err = m->err;
   g.acc = m->gacc; g.acc_floats = m->gacc_floats;
+  g.pdl = 1;
   NNZ_CK(gemm_launch(g, x, m->st));
   return NNZ_OK;
 }
@@ -747,7 +748,7 @@ int enqueue_layer_gemm(nnz_model* m, uint32_t l, uint32_t rows, const int* pos) 
   const LayerW& W = m->L[l];
   const uint32_t H = c.hidden_size, I = c.intermediate_size;
   int rc;
-  NNZ_CK(rmsnorm_f16_launch(m->residual, W.attn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st));
+  NNZ_CK(rmsnorm_f16_launch(m->residual, W.attn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st, 1));
   if ((rc = gemm(m, W.fqkv, nullptr, m->qkv_rows, H, m->xn, rows, GEPI_F16, m->qkv, m->qkv_rows))) return rc;
   if ((rc = kv_write(m, l, rows, pos, m->zeros, 0))) return rc;
   {
@@ -760,7 +761,7 @@ int enqueue_layer_gemm(nnz_model* m, uint32_t l, uint32_t rows, const int* pos) 
     NNZ_CK(attn_prefill_launch(aa, (int)c.head_dim, 0, m->st));
   }
   if ((rc = gemm_resadd_tp(m, W.fo, m->qd, m->attn, rows))) return rc;
-  NNZ_CK(rmsnorm_f16_launch(m->residual, W.ffn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st));
+  NNZ_CK(rmsnorm_f16_launch(m->residual, W.ffn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st, 1));
   if ((rc = gemm(m, W.fgate, &W.fup, I, H, m->xn, rows, GEPI_SILU, m->h, I))) return rc;
   return gemm_resadd_tp(m, W.fdown, I, m->h, rows);
 }

@@ -18,14 +18,27 @@ constexpr uint32_t kTileBytes = kBM * kBK * 2;          // 16 KB per operand til
 // activation slots with their own barriers, committed after each tile's
 // MMAs, measured slower: 44 -> 69 us on a 512 x 2048 x 12288 GEMM.)
 template <int MT> struct GemmShape {
-  static constexpr int kStages = MT >= 4 ? 2 : 4;
+  static constexpr int kStages = MT >= 4 ? 2 : (MT == 2 ? 4 : 6);
   static constexpr uint32_t kTmemCols = 128 * MT;
   static constexpr uint32_t kSmemBytes = kStages * (MT + 1) * kTileBytes + 1024 + 256;
 };
 constexpr int kGroups = 2;        // dequantizing groups of 4 warps, K steps dealt round robin
+// Every stage must always be filled by the same group (stage = step %
+// kStages, group = step % kGroups): a group that fills stages of several
+// groups can run a whole phase ahead on a stage's empty barrier, where a
+// parity wait cannot tell the pending phase from the completed one.
+static_assert(GemmShape<1>::kStages % kGroups == 0 && GemmShape<2>::kStages % kGroups == 0 &&
+                  GemmShape<4>::kStages % kGroups == 0,
+              "ring stages must be a multiple of the dequantizing groups");
 constexpr int kThreads = 128 + 128 * kGroups;
 constexpr int kProducerWarps = 4;   // full-barrier arrivals per stage: one per warp of the filling group
 constexpr int kPf = 4;            // raw-weight prefetch depth (steps of a producer group)
+
+// Vector f32 reduction into global memory (16-byte aligned address).
+__device__ __forceinline__ void red_add_f32x4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -164,6 +177,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tslot;
+  // dequantizing warps: weight row of the tile, K-step residue, and the
+  // first kPf raw steps, loaded before the grid-dependency wait (the
+  // weights are constant, so the HBM latency overlaps the previous kernel)
+  const uint32_t r = (tid - 128) & (kBN - 1);
+  const uint32_t grp = (tid - 128) / kBN;
+  const uint8_t* w = a.w;
+  const uint16_t* sc = a.s;
+  const uint16_t* bi = a.b;
+  uint32_t row = n0 + r;
+  if (silu && r >= kBN / 2) { w = a.w2; sc = a.s2; bi = a.b2; row = n0 + r - kBN / 2; }
+  const bool rok = warp >= 4 && row < a.N;
+  Raw raw[kPf];
+#pragma unroll
+  for (int d = 0; d < kPf; ++d)
+    raw[d] = load_raw<FMT>(a, w, sc, bi, row, rok && grp + kGroups * d < nk, ks0 + grp + kGroups * d);
   pdl_wait();
   pdl_launch();
   if (tid == 0) gstamp(a, 1);
@@ -199,18 +227,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       umma_commit(done);
     }
   } else if (warp >= 4) {
-    const uint32_t r = (tid - 128) & (kBN - 1);   // weight row of the tile
-    const uint32_t grp = (tid - 128) / kBN;       // K steps grp, grp + kGroups, ...
-    const uint8_t* w = a.w;
-    const uint16_t* sc = a.s;
-    const uint16_t* bi = a.b;
-    uint32_t row = n0 + r;
-    if (silu && r >= kBN / 2) { w = a.w2; sc = a.s2; bi = a.b2; row = n0 + r - kBN / 2; }
-    const bool rok = row < a.N;
-    Raw raw[kPf];
-#pragma unroll
-    for (int d = 0; d < kPf; ++d)
-      raw[d] = load_raw<FMT>(a, w, sc, bi, row, rok && grp + kGroups * d < nk, ks0 + grp + kGroups * d);
     for (uint32_t i0 = grp; i0 < nk; i0 += kGroups * kPf) {
 #pragma unroll
       for (int d = 0; d < kPf; ++d) {
@@ -223,6 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           if (tid == 128 && i < 32) gstamp(a, 34 + (int)i);
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
+          if (tid == 128 && i < 28) gstamp(a, 100 + (int)i);
           if (lane == 0) mbar_arrive(&full[s]);
           raw[d] = load_raw<FMT>(a, w, sc, bi, row, rok && i + kGroups * kPf < nk, ks0 + i + kGroups * kPf);
         }
@@ -250,9 +267,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           const uint32_t half = silu ? (uint32_t)(cc * 32) / (kBN / 2) : 0;
           const uint32_t nb = n0 + (silu ? (uint32_t)(cc * 32) % (kBN / 2) : (uint32_t)(cc * 32));
           float* o = a.acc + (size_t)m * (silu ? 2 * a.N : a.N) + half * a.N + nb;
+          if (nb + 32 <= a.N && (a.N & 3) == 0 && (reinterpret_cast<uintptr_t>(a.acc) & 15) == 0) {
   #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (nb + j < a.N) atomicAdd(&o[j], __uint_as_float(v[j]));
+            for (int j = 0; j < 32; j += 4)
+              red_add_f32x4(o + j, __uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                            __uint_as_float(v[j + 3]));
+          } else {
+  #pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < a.N) atomicAdd(&o[j], __uint_as_float(v[j]));
+          }
         }
       } else if (silu) {
         for (int cc = part; cc < part + 1; ++cc) {
@@ -303,6 +327,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             }
           } else {
             float* o = static_cast<float*>(a.out) + (size_t)m * a.ldo + nb;
+            if (a.epi == GEPI_RESADD && gridDim.z > 1 && !rb && nb + 32 <= a.N && (a.ldo & 3) == 0 &&
+                (reinterpret_cast<uintptr_t>(a.out) & 15) == 0) {
+  #pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                red_add_f32x4(o + j, __uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                              __uint_as_float(v[j + 3]));
+              continue;
+            }
   #pragma unroll
             for (int j = 0; j < 32; ++j) {
               float x = __uint_as_float(v[j]);
@@ -332,6 +364,8 @@ __global__ void __launch_bounds__(256) rmsnorm_f16_kernel(const float* res, cons
   constexpr int kU = 4;
   __shared__ float red[32];
   const uint32_t row = blockIdx.x, K4 = K / 4;
+  pdl_wait();
+  pdl_launch();
   const float4* x = reinterpret_cast<const float4*>(res + (size_t)row * K);
   float ss = 0.f;
   for (uint32_t k0 = threadIdx.x; k0 < K4; k0 += kU * blockDim.x) {
@@ -379,6 +413,8 @@ __global__ void __launch_bounds__(256) rmsnorm_f16_kernel(const float* res, cons
 // Split-K finalize: the accumulated f32 tile -> the epilogue's output, and
 // the accumulator back to zero for its next use.
 __global__ void __launch_bounds__(256) gemm_finalize_kernel(GemmArgs a) {
+  pdl_wait();
+  pdl_launch();
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (size_t)a.M * a.N) return;
   const uint32_t m = (uint32_t)(i / a.N), n = (uint32_t)(i % a.N);
@@ -486,11 +522,15 @@ cudaError_t gemm_launch(const GemmArgs& a_in, const __half* x, cudaStream_t st) 
     if (ks > nk / 4) ks = nk / 4;            // >= 4 K steps per CTA
     grid.z = ks < 1 ? 1 : ks;
   }
+  cudaLaunchAttribute la[1];
+  la[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  la[0].val.programmaticStreamSerializationAllowed = a.pdl ? 1 : 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);
   cfg.stream = st;
-  cfg.numAttrs = 0;
+  cfg.attrs = la;
+  cfg.numAttrs = 1;
   cudaError_t e = cudaSuccess;
   auto go = [&](auto kern, uint32_t smem, bool& attr) {
     if (!attr) {
@@ -514,15 +554,28 @@ cudaError_t gemm_launch(const GemmArgs& a_in, const __half* x, cudaStream_t st) 
   }
   if (e != cudaSuccess || grid.z == 1 || a.epi == GEPI_RESADD) return e;
   const size_t n = (size_t)a.M * a.N;
-  gemm_finalize_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t fc = {};
+  fc.gridDim = dim3((unsigned)((n + 255) / 256));
+  fc.blockDim = dim3(256);
+  fc.stream = st;
+  fc.attrs = la;
+  fc.numAttrs = 1;
+  return cudaLaunchKernelEx(&fc, &gemm_finalize_kernel, a);
 }
 
 cudaError_t rmsnorm_f16_launch(const float* res, const float* w, float eps, uint32_t rows, uint32_t K, int bf16r,
-                               __half* out, cudaStream_t st) {
+                               __half* out, cudaStream_t st, int pdl) {
   if (K % 4) return cudaErrorInvalidValue;
-  rmsnorm_f16_kernel<<<rows, 256, 0, st>>>(res, w, eps, K, bf16r, out);
-  return cudaGetLastError();
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(rows);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, &rmsnorm_f16_kernel, res, w, eps, K, bf16r, out);
 }
 
 }  // namespace nnz

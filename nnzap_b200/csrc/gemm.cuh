@@ -43,6 +43,7 @@ struct GemmArgs {
   uint32_t ldo;
   int* err;
   int prof;                      // set by gemm_launch from NNZ_GEMM_PROFILE
+  int pdl;                       // launch with programmatic dependent launch (GEMM and finalize)
 };
 
 // Builds the TMA descriptor for X [M][K] fp16 (row stride K) and launches.
@@ -56,6 +57,6 @@ bool tensor_map_f16_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64
 cudaError_t gemm_debug_profile(unsigned long long* out);
 // RMSNorm rows of an f32 residual into fp16 (the prefill GEMM's X operand).
 cudaError_t rmsnorm_f16_launch(const float* res, const float* w, float eps, uint32_t rows, uint32_t K,
-                               int bf16r, __half* out, cudaStream_t st);
+                               int bf16r, __half* out, cudaStream_t st, int pdl = 0);
 
 }  // namespace nnz
