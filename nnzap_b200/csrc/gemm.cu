@@ -50,22 +50,39 @@ struct Raw {
   uint16_t s, b;
 };
 
+// Row base pointers of one weight row (bits / nibbles, scales, biases).
+struct RowPtr {
+  const uint8_t* w;
+  const uint16_t* s;
+  const uint16_t* b;
+};
+
 template <int FMT>
-__device__ __forceinline__ Raw load_raw(const GemmArgs& a, const uint8_t* w, const uint16_t* s, const uint16_t* b,
-                                        uint32_t row, bool ok, uint32_t step) {
+__device__ __forceinline__ RowPtr row_ptr(const GemmArgs& a, const uint8_t* w, const uint16_t* s, const uint16_t* b,
+                                          uint32_t row) {
+  RowPtr p;
+  const size_t groups = (size_t)row * (a.K / (uint32_t)a.gs);
+  p.w = w + (size_t)row * a.K / (FMT == FMT_Q1 ? 8 : 2);
+  p.s = s + groups;
+  p.b = b ? b + groups : nullptr;
+  return p;
+}
+
+template <int FMT>
+__device__ __forceinline__ Raw load_raw(const RowPtr& p, uint32_t gs, bool ok, uint32_t step) {
   Raw r{};
   if (!ok) return r;
   const uint32_t k0 = step * kBK;
-  const size_t g = (size_t)row * (a.K / a.gs) + k0 / a.gs;
+  const uint32_t g = k0 / gs;
   if constexpr (FMT == FMT_Q1) {
-    const uint2 v = *reinterpret_cast<const uint2*>(w + ((size_t)row * a.K + k0) / 8);
+    const uint2 v = *reinterpret_cast<const uint2*>(p.w + k0 / 8);
     r.q0.x = v.x; r.q0.y = v.y;
   } else {
-    const uint4* p = reinterpret_cast<const uint4*>(w + ((size_t)row * a.K + k0) / 2);
-    r.q0 = p[0]; r.q1 = p[1];
-    r.b = b[g];
+    const uint4* q = reinterpret_cast<const uint4*>(p.w + k0 / 2);
+    r.q0 = q[0]; r.q1 = q[1];
+    r.b = p.b[g];
   }
-  r.s = s[g];
+  r.s = p.s[g];
   return r;
 }
 
@@ -73,24 +90,28 @@ __device__ __forceinline__ float u16f(uint16_t v, int bf16s) {
   return bf16s ? __uint_as_float((uint32_t)v << 16) : __half2float(__ushort_as_half(v));
 }
 
-// Dequantize one row's 64 weights into the 128B-swizzled K-major stage.
-// Dequantize one row's 64 weights into the 128B-swizzled K-major stage
-// (.shared addresses).
+// One row's 64 weights of a K step as 32 fp16 pairs: word w holds K
+// elements 2w (low half) and 2w + 1 (Q1: +-scale, exact in fp16; Q4:
+// scale * q + bias rounded to fp16).
 template <int FMT>
-__device__ __forceinline__ void write_row(uint32_t stage, uint32_t r, const Raw& raw, int bf16s) {
-  const uint32_t rowp = stage + (r >> 3) * 1024 + (r & 7) * 128;
-  uint32_t h[8][4];
+__device__ __forceinline__ void dequant_words(const Raw& raw, int bf16s, uint32_t (&h)[32]) {
   if constexpr (FMT == FMT_Q1) {
-    // bit 2j / 2j+1 of byte c -> sign of half 0 / 1 of word j: +s for 1, -s for 0
-    const uint32_t sp = raw.s, sn = raw.s ^ 0x8000u;
+    // bits 2w / 2w + 1 -> halves 0 / 1 of word w: +s for a 1 bit, -s for a 0
+    // bit.  The two cleared bits of pair p, (~q) & (3 << 2p), times
+    // 2^(15-2p) + 2^(30-2p) land on bits 15/16 and 30/31 without carries;
+    // bits 15 and 31 are the two sign flips, applied to s | s << 16 by xor
+    // (three integer operations per word; pairs 8-15 of a 32-bit half use
+    // the half shifted down by 16 bits).
+    const uint32_t s2 = (uint32_t)raw.s | ((uint32_t)raw.s << 16);
 #pragma unroll
-    for (uint32_t c = 0; c < 8; ++c) {
-      const uint32_t bits = (c < 4 ? raw.q0.x : raw.q0.y) >> (8 * (c & 3));
+    for (int hw = 0; hw < 4; ++hw) {
+      const uint32_t q = hw < 2 ? raw.q0.x : raw.q0.y;
+      const uint32_t t = (hw & 1) ? (q >> 16) : q;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t lo = ((bits >> (2 * j)) & 1u) ? sp : sn;
-        const uint32_t hi = ((bits >> (2 * j + 1)) & 1u) ? sp : sn;
-        h[c][j] = lo | (hi << 16);
+      for (int p = 0; p < 8; ++p) {
+        const uint32_t m = ~t & (3u << (2 * p));
+        const uint32_t f = m * (0x40008000u >> (2 * p));
+        h[8 * hw + p] = (f & 0x80008000u) ^ s2;
       }
     }
   } else {
@@ -103,14 +124,23 @@ __device__ __forceinline__ void write_row(uint32_t stage, uint32_t r, const Raw&
         const float f0 = __fadd_rn(__fmul_rn(sc, (float)((word >> (8 * j)) & 0xFu)), bi);
         const float f1 = __fadd_rn(__fmul_rn(sc, (float)((word >> (8 * j + 4)) & 0xFu)), bi);
         const __half2 v = __floats2half2_rn(f0, f1);
-        h[c][j] = *reinterpret_cast<const uint32_t*>(&v);
+        h[4 * c + j] = *reinterpret_cast<const uint32_t*>(&v);
       }
     }
   }
+}
+
+// Dequantize one row's 64 weights into the 128B-swizzled K-major stage
+// (.shared addresses).
+template <int FMT>
+__device__ __forceinline__ void write_row(uint32_t stage, uint32_t r, const Raw& raw, int bf16s) {
+  const uint32_t rowp = stage + (r >> 3) * 1024 + (r & 7) * 128;
+  uint32_t h[32];
+  dequant_words<FMT>(raw, bf16s, h);
 #pragma unroll
   for (uint32_t c = 0; c < 8; ++c)
-    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(rowp + ((c ^ (r & 7)) << 4)), "r"(h[c][0]),
-                 "r"(h[c][1]), "r"(h[c][2]), "r"(h[c][3])
+    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(rowp + ((c ^ (r & 7)) << 4)), "r"(h[4 * c]),
+                 "r"(h[4 * c + 1]), "r"(h[4 * c + 2]), "r"(h[4 * c + 3])
                  : "memory");
 }
 
@@ -188,10 +218,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   uint32_t row = n0 + r;
   if (silu && r >= kBN / 2) { w = a.w2; sc = a.s2; bi = a.b2; row = n0 + r - kBN / 2; }
   const bool rok = warp >= 4 && row < a.N;
+  const RowPtr rp = row_ptr<FMT>(a, w, sc, bi, rok ? row : 0);
+  const uint32_t gs = (uint32_t)a.gs;
   Raw raw[kPf];
 #pragma unroll
   for (int d = 0; d < kPf; ++d)
-    raw[d] = load_raw<FMT>(a, w, sc, bi, row, rok && grp + kGroups * d < nk, ks0 + grp + kGroups * d);
+    raw[d] = load_raw<FMT>(rp, gs, rok && grp + kGroups * d < nk, ks0 + grp + kGroups * d);
   pdl_wait();
   pdl_launch();
   if (tid == 0) gstamp(a, 1);
@@ -241,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           __syncwarp();
           if (tid == 128 && i < 28) gstamp(a, 100 + (int)i);
           if (lane == 0) mbar_arrive(&full[s]);
-          raw[d] = load_raw<FMT>(a, w, sc, bi, row, rok && i + kGroups * kPf < nk, ks0 + i + kGroups * kPf);
+          raw[d] = load_raw<FMT>(rp, gs, rok && i + kGroups * kPf < nk, ks0 + i + kGroups * kPf);
         }
       }
     }
@@ -355,6 +387,217 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   __syncthreads();
   if (warp == 2)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Decode-batch variant (M <= 128 rows): the dequantized weight tile is the A
+// operand and lives in TMEM, the activations are the B operand (N = NT
+// token columns).  Each dequantizing thread owns one TMEM lane (one weight
+// row) and writes its 64 fp16 weights of a K step with one tcgen05.st, so
+// the weights never pass through shared memory; per K step shared memory
+// only holds the NT x 64 activation tile the TMA brings in (the MMA reads it
+// once).  TMEM: the f32 accumulator (128 weight rows x NT tokens) in columns
+// [0, NT), then kTsStages A stages of 32 columns (64 fp16 of K per lane).
+// SILU tiles interleave the weight rows: lane 2i is gate row n0 + i, lane
+// 2i + 1 the matching up row, so the epilogue pairs them with one shuffle.
+// ---------------------------------------------------------------------------
+template <int NT> struct TsShape {
+  static constexpr int kStages = NT <= 64 ? 6 : 4;
+  static constexpr uint32_t kXBytes = NT * kBK * 2;        // activation tile per stage
+  static constexpr uint32_t kTmemCols = 256;               // NT + 32 * kStages <= 256
+  static constexpr uint32_t kSmemBytes = kStages * kXBytes + 1024 + 256;
+  static_assert(NT + 32 * kStages <= (int)kTmemCols, "TMEM budget");
+  static_assert(kStages % kGroups == 0, "ring stages must be a multiple of the dequantizing groups");
+};
+constexpr int kTsThreads = 128 + 128 * kGroups;
+
+// D(tmem) (+)= A(tmem) * B(smem descriptor)^T, kind::f16.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+template <int FMT, int NT>
+__global__ void __launch_bounds__(kTsThreads, 1) gemm_ts_kernel(const __grid_constant__ CUtensorMap tmX, GemmArgs a) {
+  using S = TsShape<NT>;
+  constexpr int kStages = S::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* Xs = sm;                                             // [stage][NT rows x 128 B]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kStages * S::kXBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* done = empty + kStages;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool silu = a.epi == GEPI_SILU;
+  const uint32_t ncols = silu ? kBN / 2 : kBN;
+  const uint32_t n0 = blockIdx.x * ncols;
+  const uint32_t nk_all = a.K / kBK;
+  const uint32_t ks0 = nk_all * blockIdx.z / gridDim.z, ks1 = nk_all * (blockIdx.z + 1) / gridDim.z;
+  const uint32_t nk = ks1 - ks0;
+
+  if (tid == 0) {
+    for (int st = 0; st < kStages; ++st) {
+      mbar_init(&full[st], kProducerWarps + 1);
+      mbar_init(&empty[st], 1);
+    }
+    mbar_init(done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
+                 "r"(S::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tslot;
+  // dequantizing warps: TMEM lane r = weight row of the tile
+  const uint32_t r = (tid - 128) & (kBN - 1);
+  const uint32_t grp = (tid - 128) / kBN;
+  const uint8_t* w = a.w;
+  const uint16_t* sc = a.s;
+  const uint16_t* bi = a.b;
+  uint32_t row = n0 + r;
+  if (silu) {
+    row = n0 + (r >> 1);
+    if (r & 1) { w = a.w2; sc = a.s2; bi = a.b2; }
+  }
+  const bool rok = warp >= 4 && row < a.N;
+  const RowPtr rp = row_ptr<FMT>(a, w, sc, bi, rok ? row : 0);
+  const uint32_t gs = (uint32_t)a.gs;
+  Raw raw[kPf];
+#pragma unroll
+  for (int d = 0; d < kPf; ++d)
+    raw[d] = load_raw<FMT>(rp, gs, rok && grp + kGroups * d < nk, ks0 + grp + kGroups * d);
+  pdl_wait();
+  pdl_launch();
+  bool failed = false;
+  const uint32_t tA = tmem + NT;                                // A stages: 32 columns each
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (uint32_t i = 0; i < nk; ++i) {
+        const uint32_t st = i % kStages;
+        if (i >= (uint32_t)kStages && !failed) failed = !mbar_wait(&empty[st], ((i / kStages) - 1) & 1u, a.err);
+        mbar_arrive_expect_tx(&full[st], S::kXBytes);
+        tma_load_2d(Xs + st * S::kXBytes, &tmX, (int)((ks0 + i) * kBK), 0, &full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(kBM, NT);
+      for (uint32_t i = 0; i < nk; ++i) {
+        const uint32_t st = i % kStages;
+        if (!failed) failed = !mbar_wait(&full[st], (i / kStages) & 1u, a.err);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint64_t db = smem_desc_sw128(Xs + st * S::kXBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)   // 8 TMEM columns / +32 B per 16-element K step
+          umma_f16_ts(tmem, tA + st * 32 + kk * 8, db + (uint64_t)(kk * 2), idesc, (i | kk) != 0);
+        umma_commit(&empty[st]);
+      }
+      umma_commit(done);
+    }
+  } else if (warp >= 4) {
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    for (uint32_t i0 = grp; i0 < nk; i0 += kGroups * kPf) {
+#pragma unroll
+      for (int d = 0; d < kPf; ++d) {
+        const uint32_t i = i0 + kGroups * d;
+        if (i < nk) {
+          const uint32_t st = i % kStages;
+          if (i >= (uint32_t)kStages && !failed) failed = !mbar_wait(&empty[st], ((i / kStages) - 1) & 1u, a.err);
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          uint32_t h[32];
+          dequant_words<FMT>(raw[d], a.bf16s, h);
+          tmem_st32(tA + lane_base + st * 32, h);
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full[st]);
+          raw[d] = load_raw<FMT>(rp, gs, rok && i + kGroups * kPf < nk, ks0 + i + kGroups * kPf);
+        }
+      }
+    }
+  }
+  // ---- epilogue: warps 4-11; TMEM lane quarter q = warp % 4 (weight rows
+  // 32q + lane), part p = (warp - 4) / 4 takes token columns [p NT/2, (p+1) NT/2) ----
+  if (warp >= 4 && warp < 12) {
+    if (!failed) failed = !mbar_wait(done, 0, a.err);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int q = warp & 3, part = (warp - 4) >> 2;
+    const bool rb = a.bf16r != 0;
+    const uint32_t rr = 32 * q + lane;                            // weight row of the tile
+    const bool split = gridDim.z > 1;
+#pragma unroll
+    for (int cc = 0; cc < NT / 64; ++cc) {
+      const uint32_t c0 = (uint32_t)part * (NT / 2) + cc * 32;   // first token column
+      uint32_t v[32];
+      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + c0, v);
+      if (c0 >= a.M) continue;
+      if (silu) {
+        const uint32_t n = n0 + (rr >> 1);
+        if (split) {
+          // f32 partials: gate | up halves of acc [M][2][N]
+          if (n < a.N) {
+            float* o = a.acc + (size_t)(rr & 1) * a.N + n;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (c0 + j < a.M) atomicAdd(o + (size_t)(c0 + j) * 2 * a.N, __uint_as_float(v[j]));
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float mine = __uint_as_float(v[j]);
+            const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+            if ((lane & 1) == 0 && n < a.N && c0 + j < a.M) {
+              float hv = mine / (1.0f + expf(-mine)) * other;
+              if (rb) hv = bf16_trunc(hv);
+              static_cast<__half*>(a.out)[(size_t)(c0 + j) * a.ldo + n] = __float2half_rn(hv);
+            }
+          }
+        }
+        continue;
+      }
+      const uint32_t n = n0 + rr;
+      if (n >= a.N) {
+      } else if (split) {
+        float* o = (a.epi == GEPI_RESADD ? static_cast<float*>(a.out) : a.acc) + n;
+        const size_t ld = a.epi == GEPI_RESADD ? a.ldo : a.N;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < a.M) atomicAdd(o + (size_t)(c0 + j) * ld, __uint_as_float(v[j]));
+      } else if (a.epi == GEPI_F16) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float x = __uint_as_float(v[j]);
+          if (rb) x = bf16_trunc(x);
+          if (c0 + j < a.M) static_cast<__half*>(a.out)[(size_t)(c0 + j) * a.ldo + n] = __float2half_rn(x);
+        }
+      } else {
+        float* o = static_cast<float*>(a.out) + n;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float x = __uint_as_float(v[j]);
+          if (rb) x = bf16_trunc(x);
+          if (c0 + j < a.M) {
+            if (a.epi == GEPI_F32) o[(size_t)(c0 + j) * a.ldo] = x;
+            else o[(size_t)(c0 + j) * a.ldo] += x;
+          }
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 2)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S::kTmemCols) : "memory");
 }
 
 // One CTA per row; K % 4 == 0.  Every thread's float4 loads of a pass are
@@ -532,6 +775,39 @@ cudaError_t gemm_launch(const GemmArgs& a_in, const __half* x, cudaStream_t st) 
   cfg.attrs = la;
   cfg.numAttrs = 1;
   cudaError_t e = cudaSuccess;
+  // up to 128 rows: the weights-in-TMEM variant (NNZ_GEMM_TS=0 turns it off, for measurements)
+  static const bool ts_on = [] {
+    const char* v = getenv("NNZ_GEMM_TS");
+    return !(v && v[0] == '0');
+  }();
+  if (ts_on && a.M <= 128) {
+    const uint32_t nt = a.M <= 64 ? 64 : 128;
+    CUtensorMap tx;
+    const cuuint32_t boxt[2] = {kBK, nt};
+    if (enc(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x), dims, strides, boxt, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+    cfg.blockDim = dim3(kTsThreads);
+    static bool ats[2][2] = {};
+    auto gots = [&](auto kern, uint32_t smem, bool& attr) {
+      if (!attr) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return;
+        attr = true;
+      }
+      cfg.dynamicSmemBytes = smem;
+      e = cudaLaunchKernelEx(&cfg, kern, tx, a);
+    };
+    const int fi = a.fmt == FMT_Q1 ? 0 : 1, ni = nt == 64 ? 0 : 1;
+    if (a.fmt == FMT_Q1) {
+      if (nt == 64) gots(&gemm_ts_kernel<FMT_Q1, 64>, TsShape<64>::kSmemBytes, ats[fi][ni]);
+      else gots(&gemm_ts_kernel<FMT_Q1, 128>, TsShape<128>::kSmemBytes, ats[fi][ni]);
+    } else {
+      if (nt == 64) gots(&gemm_ts_kernel<FMT_Q4, 64>, TsShape<64>::kSmemBytes, ats[fi][ni]);
+      else gots(&gemm_ts_kernel<FMT_Q4, 128>, TsShape<128>::kSmemBytes, ats[fi][ni]);
+    }
+  } else {
   auto go = [&](auto kern, uint32_t smem, bool& attr) {
     if (!attr) {
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -551,6 +827,7 @@ cudaError_t gemm_launch(const GemmArgs& a_in, const __half* x, cudaStream_t st) 
     if (mt == 4) go(&gemm_kernel<FMT_Q4, 4>, GemmShape<4>::kSmemBytes, at[fi][mi]);
     else if (mt == 2) go(&gemm_kernel<FMT_Q4, 2>, GemmShape<2>::kSmemBytes, at[fi][mi]);
     else go(&gemm_kernel<FMT_Q4, 1>, GemmShape<1>::kSmemBytes, at[fi][mi]);
+  }
   }
   if (e != cudaSuccess || grid.z == 1 || a.epi == GEPI_RESADD) return e;
   const size_t n = (size_t)a.M * a.N;

@@ -19,7 +19,10 @@ pytestmark = pytest.mark.gpu
     (0, 128, 128, 128, 128), (0, 512, 2048, 4096, 128), (0, 77, 2048, 300, 128),
     (0, 200, 6144, 2048, 128), (1, 512, 2048, 2048, 64), (1, 33, 512, 130, 64),
     # 4 and 2 M tiles per CTA (wide N), with a ragged last M tile
-    (0, 400, 2048, 12288, 128), (1, 300, 1024, 6144, 64)])
+    (0, 400, 2048, 12288, 128), (1, 300, 1024, 6144, 64),
+    # decode batches (<= 128 rows: weights in TMEM), split K and whole K
+    (0, 64, 2048, 4096, 128), (0, 64, 6144, 2048, 128), (1, 64, 2048, 2048, 64),
+    (0, 100, 2048, 12288, 128), (1, 16, 2048, 12288, 64)])
 def test_prefill_gemm_vs_oracle(cuda, built_lib, fmt, M, K, N, gs):
     torch = cuda
     rng = np.random.default_rng(M + K + N)
