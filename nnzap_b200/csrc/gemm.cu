@@ -68,15 +68,20 @@ __device__ __forceinline__ RowPtr row_ptr(const GemmArgs& a, const uint8_t* w, c
   return p;
 }
 
+// Raw weights of K step `step` (the caller clamps it into the matrix).  The
+// loads are unconditional: a zero default selected on a predicate would make
+// the select wait for the load, i.e. stall the thread for the whole memory
+// latency at the prefetch instead of at the (much later) use.
 template <int FMT>
-__device__ __forceinline__ Raw load_raw(const RowPtr& p, uint32_t gs, bool ok, uint32_t step) {
-  Raw r{};
-  if (!ok) return r;
+__device__ __forceinline__ Raw load_raw(const RowPtr& p, uint32_t gs, uint32_t step) {
+  Raw r;
   const uint32_t k0 = step * kBK;
   const uint32_t g = k0 / gs;
   if constexpr (FMT == FMT_Q1) {
     const uint2 v = *reinterpret_cast<const uint2*>(p.w + k0 / 8);
-    r.q0.x = v.x; r.q0.y = v.y;
+    r.q0 = make_uint4(v.x, v.y, 0u, 0u);
+    r.q1 = make_uint4(0u, 0u, 0u, 0u);
+    r.b = 0;
   } else {
     const uint4* q = reinterpret_cast<const uint4*>(p.w + k0 / 2);
     r.q0 = q[0]; r.q1 = q[1];
@@ -217,13 +222,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   const uint16_t* bi = a.b;
   uint32_t row = n0 + r;
   if (silu && r >= kBN / 2) { w = a.w2; sc = a.s2; bi = a.b2; row = n0 + r - kBN / 2; }
-  const bool rok = warp >= 4 && row < a.N;
-  const RowPtr rp = row_ptr<FMT>(a, w, sc, bi, rok ? row : 0);
+  const RowPtr rp = row_ptr<FMT>(a, w, sc, bi, row < a.N ? row : a.N - 1);
+  const uint32_t klast = nk_all - 1;   // prefetches past the split read its last step (unused)
   const uint32_t gs = (uint32_t)a.gs;
   Raw raw[kPf];
 #pragma unroll
   for (int d = 0; d < kPf; ++d)
-    raw[d] = load_raw<FMT>(rp, gs, rok && grp + kGroups * d < nk, ks0 + grp + kGroups * d);
+    raw[d] = load_raw<FMT>(rp, gs, min(ks0 + grp + kGroups * d, klast));
   pdl_wait();
   pdl_launch();
   if (tid == 0) gstamp(a, 1);
@@ -273,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           __syncwarp();
           if (tid == 128 && i < 28) gstamp(a, 100 + (int)i);
           if (lane == 0) mbar_arrive(&full[s]);
-          raw[d] = load_raw<FMT>(rp, gs, rok && i + kGroups * kPf < nk, ks0 + i + kGroups * kPf);
+          raw[d] = load_raw<FMT>(rp, gs, min(ks0 + i + kGroups * kPf, klast));
         }
       }
     }
@@ -403,13 +408,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 // ---------------------------------------------------------------------------
 template <int NT> struct TsShape {
   static constexpr int kStages = NT <= 64 ? 6 : 4;
+  // accumulators the MMAs of a K step rotate over (the epilogue adds them);
+  // measured: 4 at NT = 64 were no faster than one
+  static constexpr int kAcc = 1;
   static constexpr uint32_t kXBytes = NT * kBK * 2;        // activation tile per stage
-  static constexpr uint32_t kTmemCols = 256;               // NT + 32 * kStages <= 256
+  static constexpr uint32_t kTmemCols = 256;
   static constexpr uint32_t kSmemBytes = kStages * kXBytes + 1024 + 256;
-  static_assert(NT + 32 * kStages <= (int)kTmemCols, "TMEM budget");
+  static_assert(kAcc * NT + 32 * kStages <= (int)kTmemCols, "TMEM budget");
   static_assert(kStages % kGroups == 0, "ring stages must be a multiple of the dequantizing groups");
 };
 constexpr int kTsThreads = 128 + 128 * kGroups;
+constexpr int kTsPf = 4;          // raw-weight prefetch depth (steps of a producer group)
 
 // D(tmem) (+)= A(tmem) * B(smem descriptor)^T, kind::f16.
 __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
@@ -469,17 +478,17 @@ __global__ void __launch_bounds__(kTsThreads, 1) gemm_ts_kernel(const __grid_con
     row = n0 + (r >> 1);
     if (r & 1) { w = a.w2; sc = a.s2; bi = a.b2; }
   }
-  const bool rok = warp >= 4 && row < a.N;
-  const RowPtr rp = row_ptr<FMT>(a, w, sc, bi, rok ? row : 0);
+  const RowPtr rp = row_ptr<FMT>(a, w, sc, bi, row < a.N ? row : a.N - 1);
+  const uint32_t klast = nk_all - 1;   // prefetches past the split read its last step (unused)
   const uint32_t gs = (uint32_t)a.gs;
-  Raw raw[kPf];
+  Raw raw[kTsPf];
 #pragma unroll
-  for (int d = 0; d < kPf; ++d)
-    raw[d] = load_raw<FMT>(rp, gs, rok && grp + kGroups * d < nk, ks0 + grp + kGroups * d);
+  for (int d = 0; d < kTsPf; ++d)
+    raw[d] = load_raw<FMT>(rp, gs, min(ks0 + grp + kGroups * d, klast));
   pdl_wait();
   pdl_launch();
   bool failed = false;
-  const uint32_t tA = tmem + NT;                                // A stages: 32 columns each
+  const uint32_t tA = tmem + S::kAcc * NT;                      // A stages: 32 columns each
 
   if (warp == 0) {
     if (lane == 0) {
@@ -500,16 +509,17 @@ __global__ void __launch_bounds__(kTsThreads, 1) gemm_ts_kernel(const __grid_con
         const uint64_t db = smem_desc_sw128(Xs + st * S::kXBytes);
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)   // 8 TMEM columns / +32 B per 16-element K step
-          umma_f16_ts(tmem, tA + st * 32 + kk * 8, db + (uint64_t)(kk * 2), idesc, (i | kk) != 0);
+          umma_f16_ts(tmem + (kk % S::kAcc) * NT, tA + st * 32 + kk * 8, db + (uint64_t)(kk * 2), idesc,
+                      (i | (uint32_t)(kk / S::kAcc)) != 0);
         umma_commit(&empty[st]);
       }
       umma_commit(done);
     }
   } else if (warp >= 4) {
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-    for (uint32_t i0 = grp; i0 < nk; i0 += kGroups * kPf) {
+    for (uint32_t i0 = grp; i0 < nk; i0 += kGroups * kTsPf) {
 #pragma unroll
-      for (int d = 0; d < kPf; ++d) {
+      for (int d = 0; d < kTsPf; ++d) {
         const uint32_t i = i0 + kGroups * d;
         if (i < nk) {
           const uint32_t st = i % kStages;
@@ -521,7 +531,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) gemm_ts_kernel(const __grid_con
           asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
           __syncwarp();
           if (lane == 0) mbar_arrive(&full[st]);
-          raw[d] = load_raw<FMT>(rp, gs, rok && i + kGroups * kPf < nk, ks0 + i + kGroups * kPf);
+          raw[d] = load_raw<FMT>(rp, gs, min(ks0 + i + kGroups * kTsPf, klast));
         }
       }
     }
@@ -540,6 +550,13 @@ __global__ void __launch_bounds__(kTsThreads, 1) gemm_ts_kernel(const __grid_con
       const uint32_t c0 = (uint32_t)part * (NT / 2) + cc * 32;   // first token column
       uint32_t v[32];
       tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + c0, v);
+#pragma unroll
+      for (int ac = 1; ac < S::kAcc; ++ac) {
+        uint32_t u[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + ac * NT + c0, u);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(u[j]));
+      }
       if (c0 >= a.M) continue;
       if (silu) {
         const uint32_t n = n0 + (rr >> 1);
