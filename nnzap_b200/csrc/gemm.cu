@@ -517,23 +517,22 @@ __global__ void __launch_bounds__(kTsThreads, 1) gemm_ts_kernel(const __grid_con
     }
   } else if (warp >= 4) {
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-    for (uint32_t i0 = grp; i0 < nk; i0 += kGroups * kTsPf) {
+    // one rolled step (a short loop body stays in the instruction cache);
+    // the kTsPf prefetched steps rotate through registers
+#pragma unroll 1
+    for (uint32_t i = grp; i < nk; i += kGroups) {
+      const uint32_t st = i % kStages;
+      if (i >= (uint32_t)kStages && !failed) failed = !mbar_wait(&empty[st], ((i / kStages) - 1) & 1u, a.err);
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      uint32_t h[32];
+      dequant_words<FMT>(raw[0], a.bf16s, h);
+      tmem_st32(tA + lane_base + st * 32, h);
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[st]);
 #pragma unroll
-      for (int d = 0; d < kTsPf; ++d) {
-        const uint32_t i = i0 + kGroups * d;
-        if (i < nk) {
-          const uint32_t st = i % kStages;
-          if (i >= (uint32_t)kStages && !failed) failed = !mbar_wait(&empty[st], ((i / kStages) - 1) & 1u, a.err);
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          uint32_t h[32];
-          dequant_words<FMT>(raw[d], a.bf16s, h);
-          tmem_st32(tA + lane_base + st * 32, h);
-          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&full[st]);
-          raw[d] = load_raw<FMT>(rp, gs, min(ks0 + i + kGroups * kTsPf, klast));
-        }
-      }
+      for (int d = 0; d + 1 < kTsPf; ++d) raw[d] = raw[d + 1];
+      raw[kTsPf - 1] = load_raw<FMT>(rp, gs, min(ks0 + i + kGroups * kTsPf, klast));
     }
   }
   // ---- epilogue: warps 4-11; TMEM lane quarter q = warp % 4 (weight rows
