@@ -192,6 +192,9 @@ struct nnz_model {
   ncclComm_t comm = nullptr;
   // fused GEMM + peer-memory all-reduce (decode / prefill GEMM path)
   bool tp_fused = false;
+  // the last peer-memory reduction also wrote xn (the RMSNorm the next GEMM
+  // needs), so the caller skips its own RMSNorm launch
+  bool xn_from_tp = false;
   float* tp_racc = nullptr;            // [2][rows_max][H] f32 local partials, zero at rest
   float* tp_slots = nullptr;           // [2][tp][rows_max * H] f32 peers' partials
   int tp_parity = 0;                   // which half the next reduction uses
@@ -478,16 +481,24 @@ int nccl_fail(ncclResult_t r) {
 // runs ahead writes into the half its slower peers are not reading.
 // Otherwise: zero-start + NCCL all-reduce.
 int tp_post_add(nnz_model* m, uint32_t rows);
-int gemm_resadd_tp(nnz_model* m, const FlatW& W, uint32_t K, const __half* x, uint32_t rows) {
+// next_norm (optional): the RMSNorm weights of the norm that follows; with
+// the peer-memory reduction and hidden size 2048 the reduction kernel
+// applies it and writes xn itself (m->xn_from_tp).
+int gemm_resadd_tp(nnz_model* m, const FlatW& W, uint32_t K, const __half* x, uint32_t rows,
+                   const float* next_norm = nullptr) {
   const uint32_t H = m->c.hidden_size;
   int rc;
+  m->xn_from_tp = false;
   if (m->tp_fused) {
     const int par = m->tp_parity;
     m->tp_parity ^= 1;
     float* racc = m->tp_racc + (size_t)par * m->rows_max * H;
     if ((rc = gemm(m, W, nullptr, H, K, x, rows, GEPI_RESADD, racc, H))) return rc;
+    const bool fuse = next_norm && H == kTpNormRow;
     NNZ_CK(tp_allreduce_launch(m->residual, racc, m->d_peer_slots + (size_t)par * m->tp, m->tp_flags,
-                               m->d_peer_flags, (size_t)rows * H, m->tp_rank, m->tp, m->err, m->st));
+                               m->d_peer_flags, (size_t)rows * H, m->tp_rank, m->tp, m->err, m->st, 0,
+                               fuse ? next_norm : nullptr, m->c.eps, m->xn, m->bf16r, 1));
+    m->xn_from_tp = fuse;
     return NNZ_OK;
   }
   if ((rc = tp_pre_add(m, rows))) return rc;
@@ -522,13 +533,16 @@ int enqueue_layer(nnz_model* m, uint32_t l, uint32_t rows, const int* pos, const
   if (!prefill && m->gemm_prefill && rows >= kGemmDecodeRows) {
     // large decode batches: the projections as tcgen05 GEMMs over the rows
     const uint32_t H = c.hidden_size, I = c.intermediate_size;
-    NNZ_CK(rmsnorm_f16_launch(m->residual, W.attn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st, 1));
+    const float* next_norm = l + 1 < c.num_layers ? m->L[l + 1].attn_norm : m->fnorm;
+    if (!(l > 0 && m->xn_from_tp))
+      NNZ_CK(rmsnorm_f16_launch(m->residual, W.attn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st, 1));
     if ((rc = gemm(m, W.fqkv, nullptr, m->qkv_rows, H, m->xn, rows, GEPI_F16, m->qkv, m->qkv_rows))) return rc;
     if ((rc = attn(m, l, rows, pos, slot, 1, 1))) return rc;
-    if ((rc = gemm_resadd_tp(m, W.fo, m->qd, m->attn, rows))) return rc;
-    NNZ_CK(rmsnorm_f16_launch(m->residual, W.ffn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st, 1));
+    if ((rc = gemm_resadd_tp(m, W.fo, m->qd, m->attn, rows, W.ffn_norm))) return rc;
+    if (!m->xn_from_tp)
+      NNZ_CK(rmsnorm_f16_launch(m->residual, W.ffn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st, 1));
     if ((rc = gemm(m, W.fgate, &W.fup, I, H, m->xn, rows, GEPI_SILU, m->h, I))) return rc;
-    return gemm_resadd_tp(m, W.fdown, I, m->h, rows);
+    return gemm_resadd_tp(m, W.fdown, I, m->h, rows, next_norm);
   }
   if ((rc = qmv(m, 1, PRO_NORM, EPI_F16, W.qkv, m->qkv_rows, c.hidden_size, m->residual,
                 c.hidden_size, W.attn_norm, rows, m->qkv, m->qkv_rows, nullptr, nullptr, pdl)))
@@ -574,7 +588,8 @@ int enqueue_decode(nnz_model* m, uint32_t rows, bool want_logits, int pdl) {
   if (m->gemm_prefill && rows >= kGemmDecodeRows) {
     // final norm -> LM-head GEMM into the logits buffer -> argmax per row
     const nnz_config& c = m->c;
-    NNZ_CK(rmsnorm_f16_launch(m->residual, m->fnorm, c.eps, rows, c.hidden_size, m->bf16r, m->xn, m->st, 1));
+    if (!m->xn_from_tp)
+      NNZ_CK(rmsnorm_f16_launch(m->residual, m->fnorm, c.eps, rows, c.hidden_size, m->bf16r, m->xn, m->st, 1));
     if ((rc = gemm(m, m->flm, nullptr, m->lm_rows, c.hidden_size, m->xn, rows, GEPI_F32, m->logits,
                    m->lm_rows)))
       return rc;
@@ -748,7 +763,8 @@ int enqueue_layer_gemm(nnz_model* m, uint32_t l, uint32_t rows, const int* pos) 
   const LayerW& W = m->L[l];
   const uint32_t H = c.hidden_size, I = c.intermediate_size;
   int rc;
-  NNZ_CK(rmsnorm_f16_launch(m->residual, W.attn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st, 1));
+  if (!(l > 0 && m->xn_from_tp))
+    NNZ_CK(rmsnorm_f16_launch(m->residual, W.attn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st, 1));
   if ((rc = gemm(m, W.fqkv, nullptr, m->qkv_rows, H, m->xn, rows, GEPI_F16, m->qkv, m->qkv_rows))) return rc;
   if ((rc = kv_write(m, l, rows, pos, m->zeros, 0))) return rc;
   {
@@ -760,10 +776,13 @@ int enqueue_layer_gemm(nnz_model* m, uint32_t l, uint32_t rows, const int* pos) 
     aa.out_stride = m->qd; aa.err = m->err; aa.rope_tab = m->rope_tab; aa.ws = m->ws;
     NNZ_CK(attn_prefill_launch(aa, (int)c.head_dim, 0, m->st));
   }
-  if ((rc = gemm_resadd_tp(m, W.fo, m->qd, m->attn, rows))) return rc;
-  NNZ_CK(rmsnorm_f16_launch(m->residual, W.ffn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st, 1));
+  if ((rc = gemm_resadd_tp(m, W.fo, m->qd, m->attn, rows, W.ffn_norm))) return rc;
+  if (!m->xn_from_tp)
+    NNZ_CK(rmsnorm_f16_launch(m->residual, W.ffn_norm, c.eps, rows, H, m->bf16r, m->xn, m->st, 1));
   if ((rc = gemm(m, W.fgate, &W.fup, I, H, m->xn, rows, GEPI_SILU, m->h, I))) return rc;
-  return gemm_resadd_tp(m, W.fdown, I, m->h, rows);
+  // the next layer's attention norm (the final norm is not needed here: the
+  // prefill's LM head normalises the last row itself)
+  return gemm_resadd_tp(m, W.fdown, I, m->h, rows, l + 1 < c.num_layers ? m->L[l + 1].attn_norm : nullptr);
 }
 
 int enqueue_prefill(nnz_model* m, uint32_t n, bool want_logits) {

@@ -53,9 +53,13 @@ constexpr size_t kArSlice = kArThreads * 8;   // floats per CTA (two float4 per 
 __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(float* residual, float* part,
                                                                   float* const* peer_slots, uint32_t* flags,
                                                                   uint32_t* const* peer_flags, size_t n, int rank,
-                                                                  int T, int* err, uint32_t spin_limit) {
+                                                                  int T, int* err, uint32_t spin_limit,
+                                                                  const float* norm_w, float eps, __half* xn,
+                                                                  int bf16r) {
   const size_t c = blockIdx.x, base = c * kArSlice;
   const size_t stride = (size_t)(T + 1);
+  pdl_wait();
+  pdl_launch();
   float4 v[2];
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
@@ -113,6 +117,31 @@ __global__ void __launch_bounds__(kArThreads) tp_allreduce_kernel(float* residua
     r.x += acc.x; r.y += acc.y; r.z += acc.z; r.w += acc.w;
     *reinterpret_cast<float4*>(residual + i) = r;
     *reinterpret_cast<float4*>(part + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+    v[u] = r;
+  }
+  if (!norm_w) return;
+  // 5. fused RMSNorm of the new residual row (slice c = row c, fully inside n)
+  __shared__ float red[kArThreads / 32];
+  float ss = 0.f;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < kArThreads / 32; ++w) t += red[w];
+  const float rs = rsqrtf(t / (float)kArSlice + eps);
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const uint32_t k = (threadIdx.x + u * kArThreads) * 4;
+    const float4 g = *reinterpret_cast<const float4*>(norm_w + k);
+    float o[4] = {v[u].x * rs * g.x, v[u].y * rs * g.y, v[u].z * rs * g.z, v[u].w * rs * g.w};
+    if (bf16r)
+      for (int e = 0; e < 4; ++e) o[e] = bf16_trunc(o[e]);
+    __half2* dst = reinterpret_cast<__half2*>(xn + base + k);
+    dst[0] = __floats2half2_rn(o[0], o[1]);
+    dst[1] = __floats2half2_rn(o[2], o[3]);
   }
 }
 
@@ -128,12 +157,22 @@ size_t tp_allreduce_flag_words(size_t n_max, int T) {
 
 cudaError_t tp_allreduce_launch(float* residual, float* part, float* const* peer_slots, uint32_t* flags,
                                 uint32_t* const* peer_flags, size_t n, int rank, int T, int* err,
-                                cudaStream_t st, uint32_t spin_limit) {
-  if (n % 4) return cudaErrorInvalidValue;
+                                cudaStream_t st, uint32_t spin_limit, const float* norm_w, float eps, __half* xn,
+                                int bf16r, int pdl) {
+  static_assert(kArSlice == kTpNormRow, "fused RMSNorm: one slice per residual row");
+  if (n % 4 || (norm_w && (n % kArSlice || !xn))) return cudaErrorInvalidValue;
   const unsigned grid = (unsigned)((n + kArSlice - 1) / kArSlice);
-  tp_allreduce_kernel<<<grid, kArThreads, 0, st>>>(residual, part, peer_slots, flags, peer_flags, n, rank, T, err,
-                                                   spin_limit ? spin_limit : kTpSpinLimit);
-  return cudaGetLastError();
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kArThreads);
+  cfg.stream = st;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, &tp_allreduce_kernel, residual, part, peer_slots, flags, peer_flags, n, rank, T,
+                            err, spin_limit ? spin_limit : kTpSpinLimit, norm_w, eps, xn, bf16r);
 }
 
 const NcclApi* nccl_api(std::string* err) {

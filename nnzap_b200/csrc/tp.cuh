@@ -6,6 +6,7 @@
 // points below.  Every rank of a tensor-parallel group is one process
 // driving one GPU.
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <nccl.h>
 
@@ -50,9 +51,17 @@ cudaError_t argmax_shift_launch(unsigned long long* argmax, uint32_t rows, uint3
 // [nslice][T + 1] u32: arrival counts per source, then this GPU's own call
 // count for the slice.
 // spin_limit: polls of a peer flag before giving up (0 = the library default).
+// Optional fused RMSNorm (norm_w non-null; needs n = rows x 2048, i.e. one
+// slice per residual row): the CTA also writes xn[row] = fp16(RMSNorm(new
+// residual row) * norm_w) (BF16-truncated first when bf16r), the next
+// GEMM's input.  pdl: launched with programmatic dependent launch.
 cudaError_t tp_allreduce_launch(float* residual, float* part, float* const* peer_slots,
                                 uint32_t* flags, uint32_t* const* peer_flags, size_t n, int rank, int T,
-                                int* err, cudaStream_t st, uint32_t spin_limit = 0);
+                                int* err, cudaStream_t st, uint32_t spin_limit = 0,
+                                const float* norm_w = nullptr, float eps = 0.f, __half* xn = nullptr,
+                                int bf16r = 0, int pdl = 0);
+// Residual row length the fused RMSNorm of tp_allreduce_launch handles.
+constexpr uint32_t kTpNormRow = 2048;
 // Flag words tp_allreduce_launch needs for n floats at T ranks.
 size_t tp_allreduce_flag_words(size_t n_max, int T);
 
