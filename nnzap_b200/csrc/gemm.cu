@@ -407,12 +407,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 // 2i + 1 the matching up row, so the epilogue pairs them with one shuffle.
 // ---------------------------------------------------------------------------
 template <int NT> struct TsShape {
-  static constexpr int kStages = NT <= 64 ? 6 : 4;
+  static constexpr int kStages = NT <= 64 ? 6 : 4;   // NT = 256: 4 x 32 KB of activations
   // accumulators the MMAs of a K step rotate over (the epilogue adds them);
   // measured: 4 at NT = 64 were no faster than one
   static constexpr int kAcc = 1;
   static constexpr uint32_t kXBytes = NT * kBK * 2;        // activation tile per stage
-  static constexpr uint32_t kTmemCols = 256;
+  static constexpr uint32_t kTmemCols = kAcc * NT + 32 * kStages <= 256 ? 256 : 512;
   static constexpr uint32_t kSmemBytes = kStages * kXBytes + 1024 + 256;
   static_assert(kAcc * NT + 32 * kStages <= (int)kTmemCols, "TMEM budget");
   static_assert(kStages % kGroups == 0, "ring stages must be a multiple of the dequantizing groups");
@@ -445,6 +445,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) gemm_ts_kernel(const __grid_con
   const bool silu = a.epi == GEPI_SILU;
   const uint32_t ncols = silu ? kBN / 2 : kBN;
   const uint32_t n0 = blockIdx.x * ncols;
+  const uint32_t m0 = blockIdx.y * NT;                          // first token row of the tile
   const uint32_t nk_all = a.K / kBK;
   const uint32_t ks0 = nk_all * blockIdx.z / gridDim.z, ks1 = nk_all * (blockIdx.z + 1) / gridDim.z;
   const uint32_t nk = ks1 - ks0;
@@ -496,7 +497,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) gemm_ts_kernel(const __grid_con
         const uint32_t st = i % kStages;
         if (i >= (uint32_t)kStages && !failed) failed = !mbar_wait(&empty[st], ((i / kStages) - 1) & 1u, a.err);
         mbar_arrive_expect_tx(&full[st], S::kXBytes);
-        tma_load_2d(Xs + st * S::kXBytes, &tmX, (int)((ks0 + i) * kBK), 0, &full[st]);
+        tma_load_2d(Xs + st * S::kXBytes, &tmX, (int)((ks0 + i) * kBK), (int)m0, &full[st]);
       }
     }
   } else if (warp == 1) {
@@ -546,13 +547,14 @@ __global__ void __launch_bounds__(kTsThreads, 1) gemm_ts_kernel(const __grid_con
     const bool split = gridDim.z > 1;
 #pragma unroll
     for (int cc = 0; cc < NT / 64; ++cc) {
-      const uint32_t c0 = (uint32_t)part * (NT / 2) + cc * 32;   // first token column
+      const uint32_t tc = (uint32_t)part * (NT / 2) + cc * 32;   // first TMEM column
+      const uint32_t c0 = m0 + tc;                               // its token row
       uint32_t v[32];
-      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + c0, v);
+      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + tc, v);
 #pragma unroll
       for (int ac = 1; ac < S::kAcc; ++ac) {
         uint32_t u[32];
-        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + ac * NT + c0, u);
+        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + ac * NT + tc, u);
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(u[j]));
       }
@@ -796,8 +798,20 @@ cudaError_t gemm_launch(const GemmArgs& a_in, const __half* x, cudaStream_t st) 
     const char* v = getenv("NNZ_GEMM_TS");
     return !(v && v[0] == '0');
   }();
-  if (ts_on && a.M <= 128) {
-    const uint32_t nt = a.M <= 64 ? 64 : 128;
+  if (ts_on) {
+    // token tiles of NT rows: 64 / 128 for decode batches, 256 for prompts
+    // (tensor-bound: 64 KB of shared-memory traffic per 4.2 MFLOP K step,
+    // against 208 KB per 8.4 MFLOP for four 128-row tiles sharing a
+    // shared-memory weight tile)
+    const uint32_t nt = a.M <= 64 ? 64 : (a.M <= 128 ? 128 : 256);
+    grid = dim3(ntn, (a.M + nt - 1) / nt, 1);
+    if (can_split) {
+      uint32_t ks = (uint32_t)sms / (grid.x * grid.y);
+      const uint32_t nk = a.K / kBK;
+      if (ks > nk / 4) ks = nk / 4;
+      grid.z = ks < 1 ? 1 : ks;
+    }
+    cfg.gridDim = grid;
     CUtensorMap tx;
     const cuuint32_t boxt[2] = {kBK, nt};
     if (enc(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x), dims, strides, boxt, estr,
@@ -805,7 +819,7 @@ cudaError_t gemm_launch(const GemmArgs& a_in, const __half* x, cudaStream_t st) 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
     cfg.blockDim = dim3(kTsThreads);
-    static bool ats[2][2] = {};
+    static bool ats[2][3] = {};
     auto gots = [&](auto kern, uint32_t smem, bool& attr) {
       if (!attr) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -815,13 +829,15 @@ cudaError_t gemm_launch(const GemmArgs& a_in, const __half* x, cudaStream_t st) 
       cfg.dynamicSmemBytes = smem;
       e = cudaLaunchKernelEx(&cfg, kern, tx, a);
     };
-    const int fi = a.fmt == FMT_Q1 ? 0 : 1, ni = nt == 64 ? 0 : 1;
+    const int fi = a.fmt == FMT_Q1 ? 0 : 1, ni = nt == 64 ? 0 : (nt == 128 ? 1 : 2);
     if (a.fmt == FMT_Q1) {
       if (nt == 64) gots(&gemm_ts_kernel<FMT_Q1, 64>, TsShape<64>::kSmemBytes, ats[fi][ni]);
-      else gots(&gemm_ts_kernel<FMT_Q1, 128>, TsShape<128>::kSmemBytes, ats[fi][ni]);
+      else if (nt == 128) gots(&gemm_ts_kernel<FMT_Q1, 128>, TsShape<128>::kSmemBytes, ats[fi][ni]);
+      else gots(&gemm_ts_kernel<FMT_Q1, 256>, TsShape<256>::kSmemBytes, ats[fi][ni]);
     } else {
       if (nt == 64) gots(&gemm_ts_kernel<FMT_Q4, 64>, TsShape<64>::kSmemBytes, ats[fi][ni]);
-      else gots(&gemm_ts_kernel<FMT_Q4, 128>, TsShape<128>::kSmemBytes, ats[fi][ni]);
+      else if (nt == 128) gots(&gemm_ts_kernel<FMT_Q4, 128>, TsShape<128>::kSmemBytes, ats[fi][ni]);
+      else gots(&gemm_ts_kernel<FMT_Q4, 256>, TsShape<256>::kSmemBytes, ats[fi][ni]);
     }
   } else {
   auto go = [&](auto kern, uint32_t smem, bool& attr) {
