@@ -676,26 +676,38 @@ __global__ void __launch_bounds__(256) rmsnorm_f16_kernel(const float* res, cons
 __global__ void __launch_bounds__(256) gemm_finalize_kernel(GemmArgs a) {
   pdl_wait();
   pdl_launch();
-  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (size_t)a.M * a.N) return;
-  const uint32_t m = (uint32_t)(i / a.N), n = (uint32_t)(i % a.N);
+  // row m = blockIdx.y; four consecutive columns per thread (N % 4 == 0)
+  const uint32_t m = blockIdx.y, n = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (n >= a.N) return;
   const bool rb = a.bf16r != 0;
+  float o[4];
   if (a.epi == GEPI_SILU) {
-    float* g = a.acc + (size_t)m * 2 * a.N + n;
-    const float gv = *g, uv = g[a.N];
-    *g = 0.f;
-    g[a.N] = 0.f;
-    float h = gv / (1.0f + expf(-gv)) * uv;
-    if (rb) h = bf16_trunc(h);
-    static_cast<__half*>(a.out)[(size_t)m * a.ldo + n] = __float2half_rn(h);
-    return;
+    float4* g = reinterpret_cast<float4*>(a.acc + (size_t)m * 2 * a.N + n);
+    float4* u = reinterpret_cast<float4*>(a.acc + (size_t)m * 2 * a.N + a.N + n);
+    const float4 gv = *g, uv = *u;
+    *g = make_float4(0.f, 0.f, 0.f, 0.f);
+    *u = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float gs[4] = {gv.x, gv.y, gv.z, gv.w}, us[4] = {uv.x, uv.y, uv.z, uv.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] = gs[e] / (1.0f + expf(-gs[e])) * us[e];
+  } else {
+    float4* p = reinterpret_cast<float4*>(a.acc + (size_t)m * a.N + n);
+    const float4 v = *p;
+    *p = make_float4(0.f, 0.f, 0.f, 0.f);
+    o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
   }
-  float* p = a.acc + i;
-  float x = *p;
-  *p = 0.f;
-  if (rb) x = bf16_trunc(x);
-  if (a.epi == GEPI_F16) static_cast<__half*>(a.out)[(size_t)m * a.ldo + n] = __float2half_rn(x);
-  else static_cast<float*>(a.out)[(size_t)m * a.ldo + n] = x;
+  if (rb)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] = bf16_trunc(o[e]);
+  if (a.epi == GEPI_F32) {
+    float* d = static_cast<float*>(a.out) + (size_t)m * a.ldo + n;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) d[e] = o[e];
+  } else {
+    __half* d = static_cast<__half*>(a.out) + (size_t)m * a.ldo + n;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) d[e] = __float2half_rn(o[e]);
+  }
 }
 
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -776,7 +788,10 @@ cudaError_t gemm_launch(const GemmArgs& a_in, const __half* x, cudaStream_t st) 
   // partials atomically in place, the other epilogues in the f32
   // accumulator (when given one that fits), finished by gemm_finalize_kernel
   const size_t acc_need = (size_t)a.M * a.N * (a.epi == GEPI_SILU ? 2 : 1);
-  const bool can_split = a.epi == GEPI_RESADD ? a.bf16r == 0 : (a.acc && acc_need <= a.acc_floats);
+  // (the finalize kernel takes four columns per thread: N % 4 == 0)
+  const bool can_split = a.epi == GEPI_RESADD ? a.bf16r == 0
+                                              : (a.acc && acc_need <= a.acc_floats && a.N % 4 == 0 &&
+                                                 (reinterpret_cast<uintptr_t>(a.acc) & 15) == 0);
   if (can_split && mt == 1) {
     uint32_t ks = (uint32_t)sms / (grid.x * grid.y);
     const uint32_t nk = a.K / kBK;
@@ -862,9 +877,8 @@ cudaError_t gemm_launch(const GemmArgs& a_in, const __half* x, cudaStream_t st) 
   }
   }
   if (e != cudaSuccess || grid.z == 1 || a.epi == GEPI_RESADD) return e;
-  const size_t n = (size_t)a.M * a.N;
   cudaLaunchConfig_t fc = {};
-  fc.gridDim = dim3((unsigned)((n + 255) / 256));
+  fc.gridDim = dim3((a.N / 4 + 255) / 256, a.M);
   fc.blockDim = dim3(256);
   fc.stream = st;
   fc.attrs = la;
