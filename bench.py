@@ -43,7 +43,9 @@ sys.path.insert(0, str(ROOT))
 
 PROMPT, GEN = 512, 256
 # ncu (dram__bytes_read.sum + dram__bytes_write.sum) of one decode launch of
-# the config-3 model at context TRAFFIC_CTX (profiling command in DESIGN.md)
+# the config-3 model at context TRAFFIC_CTX, captured with
+# `python -m nnzap_b200.microbench decode1 --ctx 512 --steps 4` under
+# `ncu --clock-control none -k regex:d1_kernel -s 2 -c 1`
 TRAFFIC_BYTES, TRAFFIC_CTX = 310.53e6, 515
 METRIC = "decode_tok_per_sec"
 UNIT = "tok/s"
