@@ -191,22 +191,23 @@ def test_full_bonsai_q1_generate(cuda, built_lib, path):
 
 
 @pytest.mark.parametrize("d", [SMALL_Q1, SMALL_Q4], ids=["q1", "q4"])
-def test_batched_decode_gemm_rows(cuda, built_lib, d):
-    """Decode batches of >= 16 rows run the projections as tcgen05 GEMMs:
-    every row's logits match the oracle's token-at-a-time decode."""
-    rows = 20
+@pytest.mark.parametrize("rows", [20, 64, 100])
+def test_batched_decode_gemm_rows(cuda, built_lib, d, rows):
+    """Decode batches of >= 16 rows run the projections as tcgen05 GEMMs
+    (weights as the TMEM operand; 64 token columns up to 64 rows, 128 above):
+    every sampled row's logits match the oracle's token-at-a-time decode."""
     m, W = build(d, max_ctx=64, max_batch=rows, path="graph")
     cfg = oracle_cfg(d)
     rng = np.random.default_rng(11)
     toks = rng.integers(0, d.vocab, rows)
     am, lg = m.forward_decode(toks, np.zeros(rows, dtype=np.uint32), want_logits=True)
-    for r in range(0, rows, 7):
+    for r in list(range(0, rows, 7)) + [rows - 1]:
         want = R.forward_tokens(cfg, W, [int(toks[r])])[-1]
         np.testing.assert_allclose(lg[r], want, atol=2e-2, rtol=0)
     # a second step at position 1 attends over the cache the first wrote
     nxt = am.astype(np.uint32)
     am2, lg2 = m.forward_decode(nxt, np.ones(rows, dtype=np.uint32), want_logits=True)
-    for r in range(0, rows, 7):
+    for r in list(range(0, rows, 7)) + [rows - 1]:
         want = R.forward_tokens(cfg, W, [int(toks[r]), int(nxt[r])])[-1]
         np.testing.assert_allclose(lg2[r], want, atol=2e-2, rtol=0)
     m.free()
